@@ -1,0 +1,421 @@
+"""Benchmark of the quantized decode-GEMV path (driver contract: one JSON line).
+
+Workload (the mixed-format GEMVs at Q4_K_M decode shapes):
+  (a) Q4_K 4096 -> 12288, (b) Q6_K 12288 -> 4096, (c) Q8_0 4096 -> 4096,
+  (d) Q6_K LM head 4096 -> 151936 + greedy argmax.
+One step = one pass of (a)-(d) on seeded synthetic weights and x ~ N(0,1).
+The weights of one step (598 MB) exceed the 126 MB L2, so every step streams
+them from HBM; no separate flush is needed.
+
+Arithmetic: the K-quant GEMVs run MODE_Q8K_EXACT (bit-identical to the
+reference's gemv_quant_q8k, its production path); Q8_0 has no Q8_K path in the
+reference and runs MODE_F32X. The F32X rate of the whole mix is reported too.
+
+N > 1 GPUs (torchrun): the projections are sharded as in a tensor-parallel
+decode: (a) and (c) column-split (rows), (b) row-split on its inputs followed
+by an NCCL all-reduce of y, (d) vocab-split with a cross-GPU argmax
+(all-reduce MAX of a packed 64-bit key). Total work is fixed: strong scaling.
+
+--impl reference times the reference's CPU implementation of the same step
+(the oracle restatement of quants.rs: gemv_quant_q8k single-threaded per
+projection as the reference runs them, the LM head row-parallel over all
+host cores as min_forward.rs:245-264 does) on rank 0.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import sys
+import threading
+import time
+
+REPO = os.path.dirname(os.path.abspath(__file__))
+sys.path[:0] = [os.path.join(REPO, "unltd-inference_b200"), os.path.join(REPO, "oracle")]
+
+import numpy as np  # noqa: E402
+
+import synth  # noqa: E402
+
+METRIC = "Q4_K/Q6_K GEMV GB/s vs B200 HBM peak; 9B-class decode tok/s at 1/2/4/8 GPUs"
+UNIT = "GB/s"
+Q4K, Q6K, Q8_0 = synth.Q4K, synth.Q6K, synth.Q8_0
+# (name, dtype, dim_in, dim_out, split): split = "rows" (column-parallel) | "cols" (row-parallel)
+MIX = [
+    ("a_q4k_gate_up", Q4K, 4096, 12288, "rows"),
+    ("b_q6k_down", Q6K, 12288, 4096, "cols"),
+    ("c_q8_0", Q8_0, 4096, 4096, "rows"),
+    ("d_q6k_lm_head", Q6K, 4096, 151936, "rows"),
+]
+SEEDS = {n: 1000 + i for i, (n, *_rest) in enumerate(MIX)}
+
+
+def algorithmic_bytes(dtype, dim_in, dim_out, argmax=False):
+    """Packed weights + x read once + y written (+ the 4-byte token)."""
+    return synth.row_bytes(dtype, dim_in) * dim_out + 4 * dim_in + 4 * dim_out + (4 if argmax else 0)
+
+
+STEP_BYTES = sum(algorithmic_bytes(dt, di, do, n.startswith("d_")) for n, dt, di, do, _ in MIX)
+
+
+def _peaks():
+    p = os.path.join(REPO, "MEASURED_PEAKS.json")
+    if os.path.exists(p):
+        with open(p) as f:
+            d = json.load(f)
+        return float(d["hbm_gbs"]), "measured"
+    return 6650.0, "fallback"
+
+
+def _traffic():
+    p = os.path.join(REPO, "profiles", "traffic.json")
+    if os.path.exists(p):
+        with open(p) as f:
+            return json.load(f)
+    return {}
+
+
+class ClockSampler:
+    """Samples SM clock and throttle reasons through NVML while running."""
+
+    def __init__(self, device: int):
+        self.samples, self.reasons = [], set()
+        self.max_mhz = None
+        self._stop = threading.Event()
+        try:
+            import pynvml
+
+            pynvml.nvmlInit()
+            self.nv = pynvml
+            self.h = pynvml.nvmlDeviceGetHandleByIndex(device)
+            self.max_mhz = pynvml.nvmlDeviceGetMaxClockInfo(self.h, pynvml.NVML_CLOCK_SM)
+        except Exception:
+            self.nv = None
+
+    def _run(self):
+        names = {
+            0x8: "hw_slowdown", 0x40: "hw_thermal_slowdown", 0x20: "sw_thermal_slowdown",
+            0x4: "sw_power_cap", 0x80: "hw_power_brake_slowdown",
+        }
+        while not self._stop.is_set():
+            try:
+                self.samples.append(self.nv.nvmlDeviceGetClockInfo(self.h, self.nv.NVML_CLOCK_SM))
+                r = self.nv.nvmlDeviceGetCurrentClocksEventReasons(self.h)
+                for bit, name in names.items():
+                    if r & bit:
+                        self.reasons.add(name)
+            except Exception:
+                pass
+            time.sleep(0.02)
+
+    def __enter__(self):
+        if self.nv:
+            self.t = threading.Thread(target=self._run, daemon=True)
+            self.t.start()
+        return self
+
+    def __exit__(self, *a):
+        self._stop.set()
+        if self.nv:
+            self.t.join()
+
+    def summary(self):
+        return {
+            "sm_mhz": statistics.median(self.samples) if self.samples else None,
+            "sm_max_mhz": self.max_mhz,
+            "reasons": sorted(self.reasons),
+            "samples": len(self.samples),
+        }
+
+
+def _dist_env():
+    rank = int(os.environ.get("RANK", "0"))
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    return rank, world, local
+
+
+def shard_weights(wb, dtype, dim_in, dim_out, split, rank, world):
+    """Host-side shard of a packed tensor: rows [r0, r1) or input blocks [b0, b1)."""
+    rb = synth.row_bytes(dtype, dim_in)
+    if world == 1:
+        return wb, dim_in, dim_out, 0
+    if split == "rows":
+        per = -(-dim_out // world)
+        r0, r1 = rank * per, min(dim_out, (rank + 1) * per)
+        return wb[r0 * rb:r1 * rb], dim_in, r1 - r0, r0
+    be = synth.BLOCK_ELEMS[dtype]
+    nblk = dim_in // be
+    per = -(-nblk // world)
+    b0, b1 = rank * per, min(nblk, (rank + 1) * per)
+    bb = synth.BLOCK_BYTES[dtype]
+    m = wb.reshape(dim_out, rb)[:, b0 * bb:b1 * bb]
+    return np.ascontiguousarray(m).reshape(-1), (b1 - b0) * be, dim_out, b0 * be
+
+
+def cpu_baseline(steps=3):
+    """The oracle (reference restatement) on one full config-1 step, median of `steps`."""
+    import oracle
+
+    ncores = os.cpu_count() or 1
+    data = []
+    for n, dt, di, do, _ in MIX:
+        data.append((n, dt, di, do, synth.quant_weights(dt, di, do, SEEDS[n]), synth.activations(di, SEEDS[n] + 1)))
+    times = []
+    for _ in range(steps):
+        t0 = time.perf_counter()
+        for n, dt, di, do, wb, x in data:
+            if n.startswith("d_"):
+                y = oracle.gemv_quant_q8k(x, wb, di, do, dt, ncores)
+                oracle.argmax(y)
+            elif dt == Q8_0:
+                oracle.gemv_quant(x, wb, di, do, dt, 1)
+            else:
+                oracle.gemv_quant_q8k(x, wb, di, do, dt, 1)
+        times.append(time.perf_counter() - t0)
+    t = statistics.median(times)
+    return {
+        "value": round(STEP_BYTES / t / 1e9, 4),
+        "unit": UNIT,
+        "cores": ncores,
+        "kind": "port",
+        "sample": f"{steps} full config-1 steps (median {t:.3f} s/step): projections single-threaded, "
+                  f"LM head row-parallel on {ncores} threads, as the reference runs them",
+    }
+
+
+def run_reference(args):
+    rank, world, _ = _dist_env()
+    if rank != 0:
+        return
+    import oracle
+
+    ncores = os.cpu_count() or 1
+    data = []
+    for n, dt, di, do, _ in MIX:
+        data.append((n, dt, di, do, synth.quant_weights(dt, di, do, SEEDS[n]), synth.activations(di, SEEDS[n] + 1)))
+
+    def step():
+        for n, dt, di, do, wb, x in data:
+            if n.startswith("d_"):
+                oracle.argmax(oracle.gemv_quant_q8k(x, wb, di, do, dt, ncores))
+            elif dt == Q8_0:
+                oracle.gemv_quant(x, wb, di, do, dt, 1)
+            else:
+                oracle.gemv_quant_q8k(x, wb, di, do, dt, 1)
+
+    for _ in range(args.warmup):
+        step()
+    t0 = time.perf_counter()
+    for _ in range(args.steps):
+        step()
+    dt_s = (time.perf_counter() - t0) / max(args.steps, 1)
+    v = STEP_BYTES / dt_s / 1e9
+    line = {
+        "impl": "reference", "metric": METRIC, "value": round(v, 4), "unit": UNIT, "n_gpus": world,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(dt_s * 1e3, 3),
+        "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "int8xint8->int32,f32",
+        "data": "synthetic (seeded, BASELINE config 1 shapes)",
+        "config": {"workload": "config1_mixed_gemv_decode", "gemvs": [m[0] for m in MIX],
+                   "step_bytes": STEP_BYTES},
+        "cpu_baseline": {"value": round(v, 4), "unit": UNIT, "cores": ncores, "kind": "port",
+                         "sample": f"full config-1 steps; projections single-threaded, LM head on {ncores} threads"},
+        "e2e": {"value": round(v, 4), "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=50)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    args = ap.parse_args()
+    if args.impl == "reference":
+        return run_reference(args)
+
+    import torch
+
+    import unltd_gpu as ug
+
+    rank, world, local = _dist_env()
+    torch.cuda.set_device(local)
+    dist = None
+    if world > 1:
+        import datetime
+
+        import torch.distributed as dist
+
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=torch.device("cuda", local))
+    torch.cuda.set_stream(torch.cuda.Stream())
+    stream = torch.cuda.current_stream()
+    ctx = ug.Context(local, stream=stream.cuda_stream)
+
+    # ---- workload ----
+    items = []
+    for n, dt, di, do, split in MIX:
+        wb = synth.quant_weights(dt, di, do, SEEDS[n])
+        x = synth.activations(di, SEEDS[n] + 1)
+        swb, sdi, sdo, off = shard_weights(wb, dt, di, do, split, rank, world)
+        w = ctx.upload(swb, dt, sdi, sdo)
+        xs = x[off:off + sdi] if split == "cols" else x
+        items.append({
+            "name": n, "dtype": dt, "dim_in": di, "dim_out": do, "split": split, "w": w, "off": off,
+            "x_host": x, "x": torch.from_numpy(np.ascontiguousarray(xs)).cuda(),
+            "y": torch.empty(sdo, device="cuda"), "mode": ug.MODE_F32X if dt == Q8_0 else ug.MODE_Q8K,
+            "bytes": algorithmic_bytes(dt, di, do, n.startswith("d_")),
+            "local_bytes": algorithmic_bytes(dt, sdi, sdo, n.startswith("d_")),
+        })
+    tok = torch.zeros(1, dtype=torch.int32, device="cuda")
+    key = torch.zeros(1, dtype=torch.int64, device="cuda")
+    del wb
+
+    def run_item(it, mode=None):
+        m = it["mode"] if mode is None else (ug.MODE_F32X if it["dtype"] == Q8_0 else mode)
+        if it["name"].startswith("d_"):
+            ctx.gemv_argmax(it["w"], it["x"], tok, logits=it["y"], mode=m)
+            if world > 1:
+                # local index -> global key (orderable(logit) << 32 | ~global_idx), then MAX
+                li = tok.to(torch.int64)
+                v = it["y"][li.clamp_max(it["y"].numel() - 1)]
+                b = v.view(torch.int32).to(torch.int64) & 0xFFFFFFFF
+                ordv = torch.where(b >= 0x80000000, (~b) & 0xFFFFFFFF, b | 0x80000000)
+                key.copy_((ordv << 32) | (0xFFFFFFFF - (li + it["off"])))
+                dist.all_reduce(key, op=dist.ReduceOp.MAX)
+        else:
+            ctx.gemv(it["w"], it["x"], it["y"], m)
+            if world > 1 and it["split"] == "cols":
+                dist.all_reduce(it["y"])
+
+    def step(mode=None, events=None):
+        for i, it in enumerate(items):
+            if events is not None:
+                events[i][0].record(stream)
+            run_item(it, mode)
+            if events is not None:
+                events[i][1].record(stream)
+
+    for _ in range(max(args.warmup, 3)):
+        step()
+    torch.cuda.synchronize()
+
+    # ---- timed: device-resident inputs ----
+    K = args.steps
+    ev = [[(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in items]
+          for _ in range(K)]
+    t_start, t_end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    sampler = ClockSampler(local)
+    n0 = ctx.launch_count()
+    with sampler:
+        if dist:
+            dist.barrier()
+        torch.cuda.synchronize()
+        t_start.record(stream)
+        for k in range(K):
+            step(events=ev[k])
+        t_end.record(stream)
+        torch.cuda.synchronize()
+    launches = ctx.launch_count() - n0
+    ms = t_start.elapsed_time(t_end)
+    if dist:
+        tt = torch.tensor([ms], device="cuda")
+        dist.all_reduce(tt, op=dist.ReduceOp.MAX)
+        ms = float(tt.item())
+    ms_step = ms / K
+    value = STEP_BYTES / (ms_step * 1e-3) / 1e9
+    per_item_ms = [statistics.mean(ev[k][i][0].elapsed_time(ev[k][i][1]) for k in range(K)) for i in range(len(items))]
+
+    # ---- F32X rate of the same mix ----
+    for _ in range(2):
+        step(mode=ug.MODE_F32X)
+    torch.cuda.synchronize()
+    t_start.record(stream)
+    for _ in range(K):
+        step(mode=ug.MODE_F32X)
+    t_end.record(stream)
+    torch.cuda.synchronize()
+    ms_f32x = t_start.elapsed_time(t_end) / K
+    if dist:
+        tt = torch.tensor([ms_f32x], device="cuda")
+        dist.all_reduce(tt, op=dist.ReduceOp.MAX)
+        ms_f32x = float(tt.item())
+
+    # ---- e2e through the reference-signature C ABI, host buffers ----
+    e2e = None
+    if world == 1:
+        host = []
+        for n, dt, di, do, _s in MIX:
+            wb = synth.quant_weights(dt, di, do, SEEDS[n])
+            xp = torch.from_numpy(synth.activations(di, SEEDS[n] + 1)).pin_memory()
+            yp = torch.empty(do, dtype=torch.float32).pin_memory()
+            host.append((n, dt, di, do, wb, xp.numpy(), yp.numpy()))
+
+        def e2e_step():
+            for n, dt, di, do, wb, xh, yh in host:
+                if dt == Q8_0:
+                    ug.gemv_quant(yh, xh, wb, di, do, dt)
+                else:
+                    ug.gemv_quant_q8k(yh, xh, wb, di, do, dt)
+                if n.startswith("d_"):
+                    int(np.argmax(yh))  # greedy.rs argmax on the host, as the reference does
+
+        for _ in range(2):
+            e2e_step()
+        t0 = time.perf_counter()
+        for _ in range(K):
+            e2e_step()
+        e2e_s = (time.perf_counter() - t0) / K
+        e2e = {
+            "value": round(STEP_BYTES / e2e_s / 1e9, 2), "unit": UNIT,
+            "h2d_bytes_per_step": int(sum(4 * di for _, _, di, _, _ in MIX)),
+            "d2h_bytes_per_step": int(sum(4 * do for _, _, _, do, _ in MIX)),
+            "ms_per_step": round(e2e_s * 1e3, 4),
+            "path": "unltd_gemv_quant_q8k / unltd_gemv_quant (host buffers, pinned; weights cached after first call)",
+        }
+        ug.forget_host_weights()
+
+    peak, peak_kind = _peaks()
+    dom = 3  # LM head: the dominant kernel (85% of the step's bytes)
+    dom_bytes = items[dom]["local_bytes"]
+    achieved = dom_bytes / (per_item_ms[dom] * 1e-3) / 1e9
+    traffic = _traffic().get("gemv_q6k_q8k_lm_head_per_launch")
+    line = {
+        "metric": METRIC, "value": round(value, 2), "unit": UNIT, "n_gpus": world, "steps": K,
+        "warmup": args.warmup, "ms_per_step": round(ms_step, 4), "higher_is_better": True,
+        "scaling": "strong", "vs_baseline": None, "dtype": "int8xint8->int32,f32 (Q8K_EXACT); Q8_0: F32X",
+        "data": "synthetic (seeded weights and x ~ N(0,1), BASELINE config 1 shapes)",
+        "config": {
+            "workload": "config1_mixed_gemv_decode", "gemvs": [m[0] for m in MIX], "step_bytes": STEP_BYTES,
+            "parallelism": f"tp{world}" if world > 1 else "single", "l2": "inputs larger than L2 (598 MB/step)",
+            "mode": "Q8K_EXACT (Q8_0 in F32X)",
+        },
+        "per_gemv": {it["name"]: {"ms": round(per_item_ms[i], 4),
+                                  "gbs": round(it["local_bytes"] / (per_item_ms[i] * 1e-3) / 1e9, 1)}
+                     for i, it in enumerate(items)},
+        "f32x_mode": {"value": round(STEP_BYTES / (ms_f32x * 1e-3) / 1e9, 2), "unit": UNIT,
+                      "ms_per_step": round(ms_f32x, 4)},
+        "roofline": {"bound": "hbm", "kernel": "gemv Q6_K Q8K_EXACT + fused argmax (LM head, prep+gemv)",
+                     "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
+                     "frac": round(achieved / peak, 4), "peak_kind": peak_kind,
+                     "traffic": traffic},
+        "gpu_launches": int(launches),
+        "clocks": sampler.summary(),
+        "e2e": e2e,
+    }
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        line["cpu_baseline"] = cpu_baseline()
+    if rank == 0:
+        print(json.dumps(line), flush=True)
+    for it in items:
+        it["w"].free()
+    ctx.close()
+    if dist:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

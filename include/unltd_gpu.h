@@ -1,0 +1,160 @@
+/*
+ * unltd_gpu.h — C ABI of the B200 (sm_100a) quantized matrix-product path.
+ *
+ * This library replaces, for CUDA devices, the quantized matvec operators of
+ * the reference crate `unltd-tensor` (crates/unltd-tensor/src/quants.rs).
+ * Every function returns an int32 status (UNLTD_OK = 0) and never aborts;
+ * `unltd_last_error()` gives a message for the calling thread. Argument
+ * checks mirror the reference's `assert!`s one for one, so a call the
+ * reference would panic on returns an error status here instead.
+ *
+ * Two layers:
+ *  1. Handle API (device pointers, asynchronous on the context's stream):
+ *     contexts, weight upload from a host view (an mmap'd GGUF tensor) with a
+ *     lossless on-device repack, GEMV/argmax/GEMM/dequant launches, NCCL.
+ *  2. Reference-signature API (host buffers, synchronous): the exact argument
+ *     lists of `gemv_quant`, `gemv_quant_q8k` and `dequantize_q4_k`. The
+ *     weight bytes are uploaded on first use and cached by host address, so a
+ *     caller holding mmap views can switch without changing call sites.
+ *
+ * Conventions (quants.rs:414-417): W has `dim_out` rows of `dim_in` packed
+ * elements, as GGUF writes it, so y = W.x; Y = X.W^T for the batched GEMM.
+ * Thread safety: a context may be used from one host thread at a time;
+ * separate contexts are independent. The reference-signature API uses one
+ * default context per process (device selectable by unltd_set_default_device).
+ */
+#ifndef UNLTD_GPU_H
+#define UNLTD_GPU_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+#if defined(__GNUC__)
+#pragma GCC visibility push(default)
+#endif
+
+#define UNLTD_ABI_VERSION 1
+
+/* Element types, same ordinals as the reference enum DType
+ * (crates/unltd-tensor/src/lib.rs:19-31). Only F32 inputs and the packed
+ * Q4_K / Q6_K / Q8_0 weights are accepted by the compute entry points. */
+typedef enum {
+    UNLTD_DTYPE_F32 = 0,
+    UNLTD_DTYPE_F16 = 1,
+    UNLTD_DTYPE_BF16 = 2,
+    UNLTD_DTYPE_I8 = 3,
+    UNLTD_DTYPE_U8 = 4,
+    UNLTD_DTYPE_Q4K = 5,
+    UNLTD_DTYPE_Q6K = 6,
+    UNLTD_DTYPE_Q8_0 = 7
+} unltd_dtype;
+
+typedef enum {
+    UNLTD_OK = 0,
+    UNLTD_ERR_INVALID_ARG = 1,   /* null pointer, bad enum, bad handle */
+    UNLTD_ERR_LENGTH = 2,        /* a buffer length that a reference assert rejects */
+    UNLTD_ERR_DIM = 3,           /* dim_in not a multiple of the block size */
+    UNLTD_ERR_UNSUPPORTED = 4,   /* dtype/mode pair with no kernel (the reference panics too) */
+    UNLTD_ERR_CUDA = 5,          /* a CUDA runtime error; see unltd_last_error */
+    UNLTD_ERR_OUT_OF_MEMORY = 6,
+    UNLTD_ERR_NO_DEVICE = 7,
+    UNLTD_ERR_NCCL = 8,
+    UNLTD_ERR_TIMEOUT = 9
+} unltd_status;
+
+/* GEMV arithmetic modes.
+ * F32X      — f32 activations, exact integer products over the packed weights
+ *             with x held as 24-bit fixed point per 256-element block; within
+ *             1e-4 max-rel of the f64-accumulated `gemv_quant`
+ *             (quants.rs:422-466). Q4_K, Q6_K and Q8_0.
+ * Q8K_EXACT — bit-identical to `gemv_quant_q8k` (quants.rs:474-515): x is
+ *             quantized to Q8_K exactly as `quantize_q8_k` does, the integer
+ *             lane sums are exact, and the per-block f32 epilogue runs in the
+ *             reference's order without FMA. Q4_K and Q6_K only. */
+typedef enum { UNLTD_MODE_F32X = 0, UNLTD_MODE_Q8K_EXACT = 1 } unltd_mode;
+
+typedef struct unltd_ctx_s *unltd_ctx;
+typedef struct unltd_weight_s *unltd_weight;
+
+/* ---- errors and library info ---------------------------------------- */
+const char *unltd_last_error(void);
+int32_t unltd_abi_version(void);
+/* Bytes of one packed row (min_forward.rs:52-80); 0 if dim_in is not a
+ * multiple of the dtype's block or the dtype is not packed/F32. */
+size_t unltd_row_bytes(int32_t dtype, size_t dim_in);
+
+/* ---- contexts --------------------------------------------------------- */
+/* A context owns a CUDA stream on `device`, its scratch memory and (after
+ * unltd_comm_init) an NCCL communicator. */
+int32_t unltd_ctx_create(int32_t device, unltd_ctx *out);
+int32_t unltd_ctx_destroy(unltd_ctx ctx);
+/* The cudaStream_t the context launches on, as void*. */
+int32_t unltd_ctx_stream(unltd_ctx ctx, void **stream_out);
+/* Launch on a caller-owned stream instead (NULL restores the own stream). */
+int32_t unltd_ctx_set_stream(unltd_ctx ctx, void *stream);
+int32_t unltd_ctx_synchronize(unltd_ctx ctx);
+/* Number of kernels this context has launched so far. */
+int64_t unltd_ctx_launch_count(unltd_ctx ctx);
+
+/* ---- weights ------------------------------------------------------------ */
+/* Copy a packed weight view (GGUF bytes, `dim_out` rows of `dim_in`
+ * elements, `nbytes` = dim_out * row_bytes) to the device and repack it
+ * losslessly into the kernels' row layout. Replaces the zero-copy `&[u8]`
+ * view the reference passes to every call (weights.rs:55-61): the upload
+ * happens once. Validates like gemv_quant (quants.rs:430-452). */
+int32_t unltd_weight_upload(unltd_ctx ctx, const void *host_bytes, size_t nbytes, int32_t dtype,
+                            size_t dim_in, size_t dim_out, unltd_weight *out);
+/* Same, for a row range [row0, row0 + rows) of a host view whose full shape
+ * is dim_out x dim_in (tensor-parallel column shards of a projection). */
+int32_t unltd_weight_upload_rows(unltd_ctx ctx, const void *host_bytes, size_t nbytes, int32_t dtype,
+                                 size_t dim_in, size_t dim_out, size_t row0, size_t rows,
+                                 unltd_weight *out);
+int32_t unltd_weight_free(unltd_weight w);
+int32_t unltd_weight_info(unltd_weight w, int32_t *dtype, size_t *dim_in, size_t *dim_out,
+                          size_t *device_bytes);
+
+/* ---- compute (device pointers, async on the context stream) ------------- */
+/* y[dim_out] = W . x[dim_in]; f32 in and out. Replaces gemv_quant
+ * (quants.rs:422) for mode F32X and gemv_quant_q8k (quants.rs:474) for
+ * mode Q8K_EXACT. */
+int32_t unltd_gemv(unltd_ctx ctx, unltd_weight w, const float *x_dev, float *y_dev, int32_t mode);
+
+/* LM head: logits = W . x, then the first index of the maximum
+ * (min_forward.rs:210-266 followed by greedy.rs:18-27), fused. `logits_dev`
+ * may be NULL. `token_dev` receives the index as uint32. A NaN logit never
+ * wins except at index 0, as in the reference's strict '>' scan. */
+int32_t unltd_gemv_argmax(unltd_ctx ctx, unltd_weight w, const float *x_dev, float *logits_dev,
+                          uint32_t *token_dev, int32_t mode);
+
+/* Dequantize all rows to f32, row-major [dim_out][dim_in]. Bit-exact with
+ * dequantize_q4_k (quants.rs:534-567) for Q4_K and with the exact element
+ * values of dot_q6_k (quants.rs:171-200) and of the Q8_0 format. */
+int32_t unltd_dequant(unltd_ctx ctx, unltd_weight w, float *out_dev);
+
+/* ---- reference-signature API (host buffers, synchronous) ---------------- */
+/* quants.rs:422  pub fn gemv_quant(out, x, w, dim_in, dim_out, dtype) */
+int32_t unltd_gemv_quant(float *out, size_t out_len, const float *x, size_t x_len, const uint8_t *w,
+                         size_t w_len, size_t dim_in, size_t dim_out, int32_t dtype);
+/* quants.rs:474  pub fn gemv_quant_q8k(out, x, w, dim_in, dim_out, dtype) */
+int32_t unltd_gemv_quant_q8k(float *out, size_t out_len, const float *x, size_t x_len,
+                             const uint8_t *w, size_t w_len, size_t dim_in, size_t dim_out,
+                             int32_t dtype);
+/* quants.rs:534  pub fn dequantize_q4_k(out, w) */
+int32_t unltd_dequantize_q4_k(float *out, size_t out_len, const uint8_t *w, size_t w_len);
+/* Device used by the reference-signature API (default 0). Must be called
+ * before the first such call. */
+int32_t unltd_set_default_device(int32_t device);
+/* Drop every cached weight upload of the reference-signature API (call when
+ * the mmap behind the cached host addresses goes away). */
+int32_t unltd_forget_host_weights(void);
+
+#if defined(__GNUC__)
+#pragma GCC visibility pop
+#endif
+#ifdef __cplusplus
+}
+#endif
+#endif /* UNLTD_GPU_H */

@@ -1,0 +1,196 @@
+"""Numpy model of the GEMV kernels' index arithmetic (test infrastructure).
+
+Restates, element by element, what gemv.cu / weights.cu do with the device
+row layout: the within-block permutations of the repack, the x-image
+positions, the words each lane loads, the DP4A products and the lane
+reductions. Tests compare this model with the oracle on CPU, so a wrong
+permutation or lane mapping is caught before anything runs on a GPU.
+"""
+from __future__ import annotations
+
+import numpy as np
+
+
+def q4_xpos(e):
+    e = np.asarray(e)
+    p, half, r = e >> 6, (e >> 5) & 1, e & 31
+    return 64 * p + 32 * half + 4 * (r & 7) + (r >> 3)
+
+
+def q6_pic(ipos):
+    ipos = np.asarray(ipos)
+    return 4 * ((ipos & 7) >> 1) + 2 * (ipos & 1) + (ipos >> 3)
+
+
+def q6_xpos(e):
+    e = np.asarray(e)
+    h, pos = e >> 7, e & 127
+    hi, c = pos >> 6, pos & 63
+    u = c >> 4
+    return 32 * (4 * h + u) + 16 * hi + q6_pic(c & 15)
+
+
+# ---- repack of one GGUF block (weights.cu repack_q4k / repack_q6k) ----------
+
+def repack_q4k_block(blk: np.ndarray):
+    hdr = blk[:16].copy()
+    qs = np.zeros(128, np.uint8)
+    o = np.arange(128)
+    p, rr = o >> 5, o & 31
+    qs[32 * p + 4 * (rr & 7) + (rr >> 3)] = blk[16 + o]
+    return hdr, qs
+
+
+def repack_q6k_block(blk: np.ndarray):
+    ql = np.zeros(128, np.uint8)
+    qh = np.zeros(64, np.uint8)
+    o = np.arange(128)
+    ql[16 * (o >> 4) + q6_pic(o & 15)] = blk[o]
+    o = np.arange(64)
+    qh[16 * (o >> 4) + q6_pic(o & 15)] = blk[128 + o]
+    return ql, qh, blk[192:208].view(np.int8).astype(np.int64), blk[208:210].view(np.float16)[0]
+
+
+def _bytes(words_u8: np.ndarray) -> np.ndarray:
+    return words_u8.astype(np.int64)
+
+
+def q4_scales(hdr: np.ndarray, p: int):
+    s = hdr[4:16].astype(np.int64)
+    out = []
+    for g in (2 * p, 2 * p + 1):
+        if g < 4:
+            out.append((s[g] & 63, s[g + 4] & 63))
+        else:
+            out.append(((s[g + 4] & 0xF) | ((s[g - 4] >> 6) << 4), (s[g + 4] >> 4) | ((s[g] >> 6) << 4)))
+    return out  # [(sc_lo, m_lo), (sc_hi, m_hi)]
+
+
+# ---- Q8_K exact: per-block integer lane sums -------------------------------------
+
+def q4k_block_sumi_model(blk: np.ndarray, q8: np.ndarray):
+    """Per-class sums sumi[k] and minsum of one block, via the kernel's lanes."""
+    hdr, qs = repack_q4k_block(blk)
+    img = np.zeros(256, np.int64)
+    img[q4_xpos(np.arange(256))] = q8
+    sumi = np.zeros(8, np.int64)
+    msum = 0
+    for j in range(8):
+        p, kh = j >> 1, j & 1
+        (sc_lo, m_lo), (sc_hi, m_hi) = q4_scales(hdr, p)
+        w = _bytes(qs[32 * p + 16 * kh: 32 * p + 16 * kh + 16]).reshape(4, 4)
+        qa = img[64 * p + 16 * kh: 64 * p + 16 * kh + 16].reshape(4, 4)
+        qb = img[64 * p + 32 + 16 * kh: 64 * p + 32 + 16 * kh + 16].reshape(4, 4)
+        for t in range(4):
+            lo, hi = w[t] & 0xF, w[t] >> 4
+            sumi[4 * kh + t] += sc_lo * int((lo * qa[t]).sum()) + sc_hi * int((hi * qb[t]).sum())
+        bs_lo = int(q8[(64 * p + np.arange(32))[((np.arange(32) & 7) >> 2) == kh]].sum())
+        bs_hi = int(q8[(64 * p + 32 + np.arange(32))[((np.arange(32) & 7) >> 2) == kh]].sum())
+        msum += m_lo * bs_lo + m_hi * bs_hi
+    return sumi, msum
+
+
+def q4k_block_sumi_reference(blk: np.ndarray, q8: np.ndarray):
+    """quants.rs:328-351 directly."""
+    s = blk[4:16].astype(np.int64)
+    sc, m = [], []
+    for g in range(8):
+        if g < 4:
+            sc.append(s[g] & 63)
+            m.append(s[g + 4] & 63)
+        else:
+            sc.append((s[g + 4] & 0xF) | ((s[g - 4] >> 6) << 4))
+            m.append((s[g + 4] >> 4) | ((s[g] >> 6) << 4))
+    qs = blk[16:].astype(np.int64)
+    sumi = np.zeros(8, np.int64)
+    for e in range(256):
+        pos = e % 64
+        byte = qs[32 * (e // 64) + pos % 32]
+        a = byte & 0xF if pos < 32 else byte >> 4
+        sumi[e % 8] += sc[e // 32] * a * int(q8[e])
+    bsums = q8.astype(np.int64).reshape(16, 16).sum(1)
+    minsum = int(sum(bsums[g] * m[g // 2] for g in range(16)))
+    return sumi, minsum
+
+
+def q6k_block_sumi_model(blk: np.ndarray, q8: np.ndarray):
+    ql, qh, sc, _ = repack_q6k_block(blk)
+    # x image: masked A/B words per (lane, half, word)
+    A = np.zeros((8, 2, 4, 4), np.int64)
+    B = np.zeros((8, 2, 4, 4), np.int64)
+    for e in range(256):
+        h, pos = e >> 7, e & 127
+        hh, c = pos >> 6, pos & 63
+        u, ipos = c >> 4, c & 15
+        j = 4 * h + u
+        pic = int(q6_pic(ipos))
+        w, bpos = pic >> 2, pic & 3
+        (A if bpos < 2 else B)[j, hh, w, bpos] = int(q8[e])
+    P = np.zeros((8, 8), np.int64)  # [lane, class] partial 4*sumi
+    for j in range(8):
+        h, u = j >> 2, j & 3
+        sl = 2 * (u >> 1)
+        wl = _bytes(ql[16 * j: 16 * j + 16]).reshape(4, 4)
+        wh = _bytes(qh[16 * (2 * h + (u & 1)): 16 * (2 * h + (u & 1)) + 16]).reshape(4, 4)
+        sc_lo, sc_hi = sc[8 * h + u], sc[8 * h + 4 + u]
+        for t in range(4):
+            raw_lo = (wl[t] & 0xF) | (((wh[t] >> sl) & 3) << 4)
+            raw_hi = (wl[t] >> 4) | (((wh[t] >> (sl + 4)) & 3) << 4)
+            a_lo, a_hi = 4 * (raw_lo - 32), 4 * (raw_hi - 32)
+            P[j, 2 * t] += sc_lo * int((a_lo * A[j, 0, t]).sum()) + sc_hi * int((a_hi * A[j, 1, t]).sum())
+            P[j, 2 * t + 1] += sc_lo * int((a_lo * B[j, 0, t]).sum()) + sc_hi * int((a_hi * B[j, 1, t]).sum())
+    tot = P.sum(0)
+    assert np.all(tot % 4 == 0)
+    return tot >> 2
+
+
+def q6k_block_sumi_reference(blk: np.ndarray, q8: np.ndarray):
+    ql, qh = blk[:128].astype(np.int64), blk[128:192].astype(np.int64)
+    sc = blk[192:208].view(np.int8).astype(np.int64)
+    sumi = np.zeros(8, np.int64)
+    for e in range(256):
+        pos = e % 128
+        byte = ql[64 * (e // 128) + pos % 64]
+        nib = byte & 0xF if pos < 64 else byte >> 4
+        hi2 = (qh[32 * (e // 128) + pos % 32] >> (2 * (pos // 32))) & 3
+        a = (nib | (hi2 << 4)) - 32
+        sumi[e % 8] += sc[e // 16] * a * int(q8[e])
+    return sumi
+
+
+# ---- F32X: 22-bit fixed-point limbs, exact integer dots ---------------------------
+
+def f32x_limbs(x: np.ndarray):
+    """prep_f32x for one 256-span: (xint, xs) with x ~= xint * xs."""
+    amax = float(np.max(np.abs(x)))
+    if amax == 0.0:
+        return np.zeros(256, np.int64), 0.0
+    _, ex = np.frexp(np.float32(amax))
+    xi = np.rint(np.ldexp(x.astype(np.float64), 22 - int(ex))).astype(np.int64)
+    return xi, float(np.ldexp(1.0, int(ex) - 22))
+
+
+def q4k_block_f32x_model(blk: np.ndarray, x: np.ndarray) -> float:
+    """F32X block contribution via lanes: exact ints, combined in float64 here."""
+    hdr, qs = repack_q4k_block(blk)
+    xi, xs = f32x_limbs(x)
+    img = np.zeros(256, np.int64)
+    img[q4_xpos(np.arange(256))] = xi
+    hi_l, mid_l, lo_l = img >> 16, (img >> 8) & 255, img & 255
+    assert np.all(hi_l * 65536 + mid_l * 256 + lo_l == img) and np.all(np.abs(hi_l) <= 64)
+    d = float(hdr[0:2].view(np.float16)[0])
+    dmin = float(hdr[2:4].view(np.float16)[0])
+    tot = 0.0
+    for j in range(8):
+        p, kh = j >> 1, j & 1
+        (sc_lo, m_lo), (sc_hi, m_hi) = q4_scales(hdr, p)
+        w = _bytes(qs[32 * p + 16 * kh: 32 * p + 16 * kh + 16])
+        o_lo, o_hi = 64 * p + 16 * kh, 64 * p + 32 + 16 * kh
+        lo, hi = w & 0xF, w >> 4
+        A = [sc_lo * int((lo * L[o_lo:o_lo + 16]).sum()) + sc_hi * int((hi * L[o_hi:o_hi + 16]).sum())
+             for L in (hi_l, mid_l, lo_l)]
+        F = A[0] * 65536.0 + A[1] * 256.0 + A[2]
+        xsl = float(img[o_lo:o_lo + 16].sum()) * xs
+        xsh = float(img[o_hi:o_hi + 16].sum()) * xs
+        tot += d * xs * F - dmin * (m_lo * xsl + m_hi * xsh)
+    return tot

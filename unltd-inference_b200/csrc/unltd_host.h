@@ -1,0 +1,61 @@
+// Host-side internal interfaces of libunltd_gpu (not part of the C ABI).
+#pragma once
+
+#include <cuda_runtime.h>
+#include <stddef.h>
+#include <stdint.h>
+
+#include <atomic>
+#include <string>
+
+#include "../../include/unltd_gpu.h"
+
+struct unltd_ctx_s {
+  int device = 0;
+  int num_sms = 0;
+  cudaStream_t own_stream = nullptr;
+  cudaStream_t stream = nullptr;
+  // Scratch for per-call x images (grown on demand, never shrunk).
+  uint8_t *scratch = nullptr;
+  size_t scratch_bytes = 0;
+  // Argmax reduction state: a 64-bit key and a CTA-completion counter.
+  unsigned long long *argmax_key = nullptr;
+  unsigned int *argmax_done = nullptr;
+  std::atomic<int64_t> launches{0};
+  void *comm = nullptr;  // ncclComm_t once unltd_comm_init ran
+};
+
+struct unltd_weight_s {
+  unltd_ctx ctx = nullptr;
+  int dtype = 0;
+  size_t dim_in = 0, dim_out = 0;
+  size_t nb = 0;          // blocks per row (256 elems for K-quants, 32 for Q8_0)
+  size_t row_bytes = 0;   // GGUF bytes per row
+  size_t row_stride = 0;  // device bytes per row (row_bytes rounded up to 16)
+  uint8_t *dev = nullptr;
+};
+
+namespace unltd {
+
+// Thread-local error message behind unltd_last_error().
+int32_t set_error(int32_t status, const std::string &msg);
+int32_t cuda_error(cudaError_t e, const char *what);
+
+// weights.cu
+cudaError_t launch_repack(const unltd_weight_s &w, const uint8_t *raw_dev, size_t row0_local,
+                          size_t rows, cudaStream_t s);
+cudaError_t launch_dequant(const unltd_weight_s &w, float *out, cudaStream_t s);
+
+// gemv.cu
+struct GemvArgs {
+  const unltd_weight_s *w;
+  const float *x;
+  float *y;
+  int mode;
+  unsigned long long *argmax_key;  // non-null: fused argmax
+  unsigned int *argmax_done;
+  uint32_t *token;
+};
+int32_t gemv_launch(unltd_ctx ctx, const GemvArgs &a);
+
+}  // namespace unltd

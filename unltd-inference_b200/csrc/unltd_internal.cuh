@@ -1,0 +1,135 @@
+// Internal definitions shared by the CUDA translation units of libunltd_gpu.
+//
+// Device weight layout ("row planes"). Every uploaded row keeps its GGUF byte
+// count (row_bytes, min_forward.rs:52-80); rows are padded to a 16-byte
+// stride so each lane can use 128-bit loads. Inside a row the bytes of each
+// block are regrouped into planes and permuted *within* a block, losslessly:
+//
+//   Q4_K  [hdr  nb x 16 B: d f16 | dmin f16 | scales[12] (unchanged)]
+//         [qs   nb x 128 B, permuted: old qs[32p + k + 8i] -> new 32p + 4k + i]
+//   Q6_K  [ql   nb x 128 B, permuted within each 16-byte chunk by PIC6]
+//         [qh   nb x 64 B,  permuted within each 16-byte chunk by PIC6]
+//         [sc   nb x 16 B  (int8 scales, unchanged)]
+//         [d    nb x 2 B   (f16)]
+//   Q8_0  [qs   nb x 32 B][d nb x 2 B]          (nb = dim_in / 32 here)
+//
+// The permutations put, into each 32-bit word a lane loads, four elements
+// that share both their scale group and their Q8_K lane class e % 8 (Q4_K)
+// or two pairs of such elements (Q6_K). That is what lets one DP4A produce a
+// term of the reference's per-lane integer sums exactly
+// (quants.rs:337-342, 390-401) and, in F32X mode, a chain of DP4As share one
+// scale.
+#pragma once
+
+#include <cuda_fp16.h>
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+namespace unltd {
+
+constexpr int kQK = 256;          // K-quant super-block
+constexpr int kQ4Bytes = 144;
+constexpr int kQ6Bytes = 210;
+constexpr int kQ80Bytes = 34;
+constexpr int kQ80Elems = 32;
+
+enum Dtype : int { F32 = 0, F16 = 1, BF16 = 2, I8 = 3, U8 = 4, Q4K = 5, Q6K = 6, Q8_0 = 7 };
+enum Mode : int { MODE_F32X = 0, MODE_Q8K = 1 };
+
+// ---- x images: per 256-element span, what one GEMV call prepares once ----
+// F32X (all formats): limb planes hi (s8) | mid (u8) | lo (u8), 256 B each,
+// element order = the format's lane order; then xs (f32 scale 2^(e-22)),
+// then 16 f32 lane-half sums (Q4_K min term).
+constexpr int kImgF32X = 848;
+constexpr int kImgF32X_XS = 768;
+constexpr int kImgF32X_XSUM = 784;
+// Q8K for Q4_K: q8 (256 B, Q4_K lane order) | d f32 | pad | 16 x i32 lane-half sums
+constexpr int kImgQ8K4 = 336;
+constexpr int kImgQ8K4_D = 256;
+constexpr int kImgQ8K4_BS = 272;
+// Q8K for Q6_K: for lane j, half h, word t: two masked q8 words (A: bytes
+// 0,1; B: bytes 2,3) -> 8*2*4*2 words = 512 B | d f32 | pad
+constexpr int kImgQ8K6 = 528;
+constexpr int kImgQ8K6_D = 512;
+
+__host__ __device__ inline int img_stride(int dtype, int mode) {
+  return mode == MODE_F32X ? kImgF32X : (dtype == Q4K ? kImgQ8K4 : kImgQ8K6);
+}
+
+// Element e (0..255) of a span -> byte index in the lane-ordered 256-byte
+// plane of an x image, and the same permutation of the weights.
+//  Q4_K: p = e/64 (qs segment), half = (e%64)/32 (low/high nibble group),
+//        r = e%32, k = r%8, i = r/8   ->  64p + 32*half + 4k + i
+__host__ __device__ inline int q4_xpos(int e) {
+  int p = e >> 6, half = (e >> 5) & 1, r = e & 31;
+  return 64 * p + 32 * half + 4 * (r & 7) + (r >> 3);
+}
+// In-chunk position of run position ipos (0..15) for Q6_K: word t holds run
+// positions (2t, 2t+8, 2t+1, 2t+9), i.e. Q8_K lane classes 2t and 2t+1.
+__host__ __device__ inline int q6_pic(int ipos) {
+  return 4 * ((ipos & 7) >> 1) + 2 * (ipos & 1) + (ipos >> 3);
+}
+//  Q6_K: h = e/128, pos = e%128, hi = pos/64, c = pos%64, u = c/16,
+//        lane j = 4h + u  ->  32j + 16*hi + pic(c%16)
+__host__ __device__ inline int q6_xpos(int e) {
+  int h = e >> 7, pos = e & 127, hi = pos >> 6, c = pos & 63, u = c >> 4;
+  return 32 * (4 * h + u) + 16 * hi + q6_pic(c & 15);
+}
+
+__host__ __device__ inline size_t round_up(size_t v, size_t a) { return (v + a - 1) / a * a; }
+
+// GGUF bytes of one row (min_forward.rs:52-80); 0 when not a whole number of blocks.
+__host__ __device__ inline size_t gguf_row_bytes(int dtype, size_t dim_in) {
+  switch (dtype) {
+    case F32: return dim_in * 4;
+    case Q4K: return dim_in % kQK ? 0 : dim_in / kQK * kQ4Bytes;
+    case Q6K: return dim_in % kQK ? 0 : dim_in / kQK * kQ6Bytes;
+    case Q8_0: return dim_in % kQ80Elems ? 0 : dim_in / kQ80Elems * kQ80Bytes;
+    default: return 0;
+  }
+}
+
+// ---- small device helpers ---------------------------------------------
+__device__ __forceinline__ int dp4a_uu(unsigned a, unsigned b, int c) {
+  int r;
+  asm("dp4a.u32.u32 %0, %1, %2, %3;" : "=r"(r) : "r"(a), "r"(b), "r"(c));
+  return r;
+}
+__device__ __forceinline__ int dp4a_us(unsigned a, unsigned b, int c) {  // a unsigned, b signed
+  int r;
+  asm("dp4a.u32.s32 %0, %1, %2, %3;" : "=r"(r) : "r"(a), "r"(b), "r"(c));
+  return r;
+}
+__device__ __forceinline__ int dp4a_ss(unsigned a, unsigned b, int c) {
+  int r;
+  asm("dp4a.s32.s32 %0, %1, %2, %3;" : "=r"(r) : "r"(a), "r"(b), "r"(c));
+  return r;
+}
+__device__ __forceinline__ int dp4a_su(unsigned a, unsigned b, int c) {  // a signed, b unsigned
+  int r;
+  asm("dp4a.s32.u32 %0, %1, %2, %3;" : "=r"(r) : "r"(a), "r"(b), "r"(c));
+  return r;
+}
+
+__device__ __forceinline__ uint4 ldg_stream(const void *p) {
+  uint4 v;
+  asm volatile("ld.global.nc.L1::no_allocate.v4.u32 {%0,%1,%2,%3}, [%4];"
+               : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
+               : "l"(p));
+  return v;
+}
+
+__device__ __forceinline__ float h2f_bits(uint32_t bits16) {
+  return __half2float(__ushort_as_half((unsigned short)bits16));
+}
+
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void pdl_trigger() { asm volatile("griddepcontrol.launch_dependents;"); }
+
+// f32 -> order-preserving u32 (larger float -> larger key).
+__device__ __forceinline__ uint32_t orderable(float v) {
+  uint32_t b = __float_as_uint(v);
+  return (b & 0x80000000u) ? ~b : (b | 0x80000000u);
+}
+
+}  // namespace unltd

@@ -1,0 +1,208 @@
+"""ctypes binding of libunltd_gpu (include/unltd_gpu.h).
+
+Mirrors the reference crate's operator names (crates/unltd-tensor/src/
+quants.rs): ``gemv_quant``, ``gemv_quant_q8k``, ``dequantize_q4_k`` take host
+numpy arrays exactly like the Rust functions take slices; the handle API
+(``Context``, ``Weight``) takes device pointers (e.g. ``torch.Tensor.data_ptr()``).
+
+There is no CPU fallback: importing works without a GPU (so the library can
+be inspected), but every compute call goes through the CUDA library and
+raises ``UnltdError`` when it fails or when no device is present.
+"""
+from __future__ import annotations
+
+import ctypes
+import os
+
+import numpy as np
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+LIB_PATH = os.path.join(HERE, "lib", "libunltd_gpu.so")
+
+# DType ordinals (crates/unltd-tensor/src/lib.rs:19-31)
+F32, F16, BF16, I8, U8, Q4K, Q6K, Q8_0 = range(8)
+MODE_F32X, MODE_Q8K = 0, 1
+STATUS = {
+    0: "OK", 1: "INVALID_ARG", 2: "LENGTH", 3: "DIM", 4: "UNSUPPORTED", 5: "CUDA",
+    6: "OUT_OF_MEMORY", 7: "NO_DEVICE", 8: "NCCL", 9: "TIMEOUT",
+}
+
+# Every symbol include/unltd_gpu.h declares: (name, restype, argtypes)
+_P, _S, _I, _I64 = ctypes.c_void_p, ctypes.c_size_t, ctypes.c_int32, ctypes.c_int64
+SIGNATURES = [
+    ("unltd_last_error", ctypes.c_char_p, []),
+    ("unltd_abi_version", _I, []),
+    ("unltd_row_bytes", _S, [_I, _S]),
+    ("unltd_ctx_create", _I, [_I, ctypes.POINTER(_P)]),
+    ("unltd_ctx_destroy", _I, [_P]),
+    ("unltd_ctx_stream", _I, [_P, ctypes.POINTER(_P)]),
+    ("unltd_ctx_set_stream", _I, [_P, _P]),
+    ("unltd_ctx_synchronize", _I, [_P]),
+    ("unltd_ctx_launch_count", _I64, [_P]),
+    ("unltd_weight_upload", _I, [_P, _P, _S, _I, _S, _S, ctypes.POINTER(_P)]),
+    ("unltd_weight_upload_rows", _I, [_P, _P, _S, _I, _S, _S, _S, _S, ctypes.POINTER(_P)]),
+    ("unltd_weight_free", _I, [_P]),
+    ("unltd_weight_info", _I, [_P, ctypes.POINTER(_I), ctypes.POINTER(_S), ctypes.POINTER(_S), ctypes.POINTER(_S)]),
+    ("unltd_gemv", _I, [_P, _P, _P, _P, _I]),
+    ("unltd_gemv_argmax", _I, [_P, _P, _P, _P, _P, _I]),
+    ("unltd_dequant", _I, [_P, _P, _P]),
+    ("unltd_gemv_quant", _I, [_P, _S, _P, _S, _P, _S, _S, _S, _I]),
+    ("unltd_gemv_quant_q8k", _I, [_P, _S, _P, _S, _P, _S, _S, _S, _I]),
+    ("unltd_dequantize_q4_k", _I, [_P, _S, _P, _S]),
+    ("unltd_set_default_device", _I, [_I]),
+    ("unltd_forget_host_weights", _I, []),
+]
+
+
+class UnltdError(RuntimeError):
+    def __init__(self, status: int, msg: str):
+        super().__init__(f"{STATUS.get(status, status)}: {msg}")
+        self.status = status
+
+
+_lib = None
+
+
+def lib():
+    """Load the in-tree CUDA library (raises if it was not built)."""
+    global _lib
+    if _lib is None:
+        if not os.path.exists(LIB_PATH):
+            raise ImportError(
+                f"{LIB_PATH} is missing: build it with `python unltd-inference_b200/build.py` "
+                "(there is no CPU fallback)"
+            )
+        L = ctypes.CDLL(LIB_PATH)
+        for name, res, args in SIGNATURES:
+            f = getattr(L, name)
+            f.restype = res
+            f.argtypes = args
+        _lib = L
+    return _lib
+
+
+def _check(rc: int):
+    if rc != 0:
+        raise UnltdError(rc, lib().unltd_last_error().decode(errors="replace"))
+
+
+def last_error() -> str:
+    return lib().unltd_last_error().decode(errors="replace")
+
+
+def row_bytes(dtype: int, dim_in: int) -> int:
+    return int(lib().unltd_row_bytes(dtype, dim_in))
+
+
+def _ptr(a) -> int:
+    if isinstance(a, int):
+        return a
+    if hasattr(a, "data_ptr"):
+        return a.data_ptr()
+    return a.ctypes.data
+
+
+class Context:
+    """A CUDA stream + scratch on one device (unltd_ctx_create)."""
+
+    def __init__(self, device: int = 0, stream: int | None = None):
+        h = ctypes.c_void_p()
+        _check(lib().unltd_ctx_create(device, ctypes.byref(h)))
+        self.h = h
+        self.device = device
+        if stream is not None:
+            self.set_stream(stream)
+
+    def set_stream(self, stream: int | None):
+        """Launch on `stream` (a cudaStream_t as int). 0 is the legacy default
+        stream (torch's default), passed as cudaStreamLegacy; None restores
+        the context's own stream."""
+        if stream is None:
+            _check(lib().unltd_ctx_set_stream(self.h, None))
+        else:
+            _check(lib().unltd_ctx_set_stream(self.h, ctypes.c_void_p(stream if stream else 0x1)))
+
+    def stream(self) -> int:
+        s = ctypes.c_void_p()
+        _check(lib().unltd_ctx_stream(self.h, ctypes.byref(s)))
+        return s.value or 0
+
+    def synchronize(self):
+        _check(lib().unltd_ctx_synchronize(self.h))
+
+    def launch_count(self) -> int:
+        return int(lib().unltd_ctx_launch_count(self.h))
+
+    def upload(self, w: np.ndarray, dtype: int, dim_in: int, dim_out: int, row0: int = 0, rows: int | None = None):
+        w = np.ascontiguousarray(w, dtype=np.uint8)
+        rows = dim_out - row0 if rows is None else rows
+        h = ctypes.c_void_p()
+        _check(lib().unltd_weight_upload_rows(self.h, w.ctypes.data, w.nbytes, dtype, dim_in, dim_out, row0, rows,
+                                              ctypes.byref(h)))
+        return Weight(self, h, dtype, dim_in, rows)
+
+    def gemv(self, w: "Weight", x, y, mode: int = MODE_F32X):
+        _check(lib().unltd_gemv(self.h, w.h, _ptr(x), _ptr(y), mode))
+
+    def gemv_argmax(self, w: "Weight", x, token, logits=None, mode: int = MODE_Q8K):
+        _check(lib().unltd_gemv_argmax(self.h, w.h, _ptr(x), _ptr(logits) if logits is not None else None,
+                                       _ptr(token), mode))
+
+    def dequant(self, w: "Weight", out):
+        _check(lib().unltd_dequant(self.h, w.h, _ptr(out)))
+
+    def close(self):
+        if getattr(self, "h", None):
+            lib().unltd_ctx_destroy(self.h)
+            self.h = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+
+class Weight:
+    def __init__(self, ctx: Context, h, dtype, dim_in, dim_out):
+        self.ctx, self.h, self.dtype, self.dim_in, self.dim_out = ctx, h, dtype, dim_in, dim_out
+
+    def info(self):
+        dt, di, do, nb = _I(), _S(), _S(), _S()
+        _check(lib().unltd_weight_info(self.h, ctypes.byref(dt), ctypes.byref(di), ctypes.byref(do), ctypes.byref(nb)))
+        return dt.value, di.value, do.value, nb.value
+
+    def free(self):
+        if getattr(self, "h", None):
+            lib().unltd_weight_free(self.h)
+            self.h = None
+
+    def __del__(self):
+        try:
+            if self.ctx.h:
+                self.free()
+        except Exception:
+            pass
+
+
+# ---- reference-signature API (host numpy buffers) ------------------------------
+
+def gemv_quant(out: np.ndarray, x: np.ndarray, w: np.ndarray, dim_in: int, dim_out: int, dtype: int):
+    """quants.rs:422 ``gemv_quant(out, x, w, dim_in, dim_out, dtype)`` on the GPU."""
+    _check(lib().unltd_gemv_quant(out.ctypes.data, out.size, x.ctypes.data, x.size, w.ctypes.data, w.nbytes,
+                                  dim_in, dim_out, dtype))
+
+
+def gemv_quant_q8k(out: np.ndarray, x: np.ndarray, w: np.ndarray, dim_in: int, dim_out: int, dtype: int):
+    """quants.rs:474 ``gemv_quant_q8k(out, x, w, dim_in, dim_out, dtype)`` on the GPU."""
+    _check(lib().unltd_gemv_quant_q8k(out.ctypes.data, out.size, x.ctypes.data, x.size, w.ctypes.data, w.nbytes,
+                                      dim_in, dim_out, dtype))
+
+
+def dequantize_q4_k(out: np.ndarray, w: np.ndarray):
+    """quants.rs:534 ``dequantize_q4_k(out, w)`` on the GPU."""
+    _check(lib().unltd_dequantize_q4_k(out.ctypes.data, out.size, w.ctypes.data, w.nbytes))
+
+
+def forget_host_weights():
+    _check(lib().unltd_forget_host_weights())
