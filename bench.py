@@ -233,6 +233,9 @@ def main():
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--only", default=None, help="comma-separated subset of the mix (profiling)")
+    ap.add_argument("--mode", default="q8k", choices=["q8k", "f32x"], help="arithmetic of the K-quant GEMVs")
     args = ap.parse_args()
     if args.impl == "reference":
         return run_reference(args)
@@ -256,7 +259,9 @@ def main():
 
     # ---- workload ----
     items = []
-    for n, dt, di, do, split in MIX:
+    mix = [m for m in MIX if args.only is None or m[0] in args.only.split(",")]
+    head_mode = ug.MODE_Q8K if args.mode == "q8k" else ug.MODE_F32X
+    for n, dt, di, do, split in mix:
         wb = synth.quant_weights(dt, di, do, SEEDS[n])
         x = synth.activations(di, SEEDS[n] + 1)
         swb, sdi, sdo, off = shard_weights(wb, dt, di, do, split, rank, world)
@@ -265,7 +270,7 @@ def main():
         items.append({
             "name": n, "dtype": dt, "dim_in": di, "dim_out": do, "split": split, "w": w, "off": off,
             "x_host": x, "x": torch.from_numpy(np.ascontiguousarray(xs)).cuda(),
-            "y": torch.empty(sdo, device="cuda"), "mode": ug.MODE_F32X if dt == Q8_0 else ug.MODE_Q8K,
+            "y": torch.empty(sdo, device="cuda"), "mode": ug.MODE_F32X if dt == Q8_0 else head_mode,
             "bytes": algorithmic_bytes(dt, di, do, n.startswith("d_")),
             "local_bytes": algorithmic_bytes(dt, sdi, sdo, n.startswith("d_")),
         })
@@ -345,7 +350,7 @@ def main():
 
     # ---- e2e through the reference-signature C ABI, host buffers ----
     e2e = None
-    if world == 1:
+    if world == 1 and not args.no_e2e and args.only is None:
         host = []
         for n, dt, di, do, _s in MIX:
             wb = synth.quant_weights(dt, di, do, SEEDS[n])
@@ -378,7 +383,9 @@ def main():
         ug.forget_host_weights()
 
     peak, peak_kind = _peaks()
-    dom = 3  # LM head: the dominant kernel (85% of the step's bytes)
+    step_bytes = sum(it["bytes"] for it in items)
+    value = step_bytes / (ms_step * 1e-3) / 1e9
+    dom = max(range(len(items)), key=lambda i: items[i]["bytes"])  # LM head: 85% of the step's bytes
     dom_bytes = items[dom]["local_bytes"]
     achieved = dom_bytes / (per_item_ms[dom] * 1e-3) / 1e9
     traffic = _traffic().get("gemv_q6k_q8k_lm_head_per_launch")
@@ -388,14 +395,14 @@ def main():
         "scaling": "strong", "vs_baseline": None, "dtype": "int8xint8->int32,f32 (Q8K_EXACT); Q8_0: F32X",
         "data": "synthetic (seeded weights and x ~ N(0,1), BASELINE config 1 shapes)",
         "config": {
-            "workload": "config1_mixed_gemv_decode", "gemvs": [m[0] for m in MIX], "step_bytes": STEP_BYTES,
+            "workload": "config1_mixed_gemv_decode", "gemvs": [it["name"] for it in items], "step_bytes": step_bytes,
             "parallelism": f"tp{world}" if world > 1 else "single", "l2": "inputs larger than L2 (598 MB/step)",
             "mode": "Q8K_EXACT (Q8_0 in F32X)",
         },
         "per_gemv": {it["name"]: {"ms": round(per_item_ms[i], 4),
                                   "gbs": round(it["local_bytes"] / (per_item_ms[i] * 1e-3) / 1e9, 1)}
                      for i, it in enumerate(items)},
-        "f32x_mode": {"value": round(STEP_BYTES / (ms_f32x * 1e-3) / 1e9, 2), "unit": UNIT,
+        "f32x_mode": {"value": round(step_bytes / (ms_f32x * 1e-3) / 1e9, 2), "unit": UNIT,
                       "ms_per_step": round(ms_f32x, 4)},
         "roofline": {"bound": "hbm", "kernel": "gemv Q6_K Q8K_EXACT + fused argmax (LM head, prep+gemv)",
                      "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
@@ -405,7 +412,7 @@ def main():
         "clocks": sampler.summary(),
         "e2e": e2e,
     }
-    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+    if rank == 0 and world == 1 and not args.no_cpu_baseline and args.only is None:
         line["cpu_baseline"] = cpu_baseline()
     if rank == 0:
         print(json.dumps(line), flush=True)

@@ -14,7 +14,7 @@ import numpy as np
 def q4_xpos(e):
     e = np.asarray(e)
     p, half, r = e >> 6, (e >> 5) & 1, e & 31
-    return 64 * p + 32 * half + 4 * (r & 7) + (r >> 3)
+    return 128 * half + 32 * p + 4 * (r & 7) + (r >> 3)
 
 
 def q6_pic(ipos):
@@ -27,7 +27,7 @@ def q6_xpos(e):
     h, pos = e >> 7, e & 127
     hi, c = pos >> 6, pos & 63
     u = c >> 4
-    return 32 * (4 * h + u) + 16 * hi + q6_pic(c & 15)
+    return 128 * hi + 16 * (4 * h + u) + q6_pic(c & 15)
 
 
 # ---- repack of one GGUF block (weights.cu repack_q4k / repack_q6k) ----------
@@ -79,8 +79,8 @@ def q4k_block_sumi_model(blk: np.ndarray, q8: np.ndarray):
         p, kh = j >> 1, j & 1
         (sc_lo, m_lo), (sc_hi, m_hi) = q4_scales(hdr, p)
         w = _bytes(qs[32 * p + 16 * kh: 32 * p + 16 * kh + 16]).reshape(4, 4)
-        qa = img[64 * p + 16 * kh: 64 * p + 16 * kh + 16].reshape(4, 4)
-        qb = img[64 * p + 32 + 16 * kh: 64 * p + 32 + 16 * kh + 16].reshape(4, 4)
+        qa = img[16 * j: 16 * j + 16].reshape(4, 4)
+        qb = img[128 + 16 * j: 128 + 16 * j + 16].reshape(4, 4)
         for t in range(4):
             lo, hi = w[t] & 0xF, w[t] >> 4
             sumi[4 * kh + t] += sc_lo * int((lo * qa[t]).sum()) + sc_hi * int((hi * qb[t]).sum())
@@ -185,7 +185,7 @@ def q4k_block_f32x_model(blk: np.ndarray, x: np.ndarray) -> float:
         p, kh = j >> 1, j & 1
         (sc_lo, m_lo), (sc_hi, m_hi) = q4_scales(hdr, p)
         w = _bytes(qs[32 * p + 16 * kh: 32 * p + 16 * kh + 16])
-        o_lo, o_hi = 64 * p + 16 * kh, 64 * p + 32 + 16 * kh
+        o_lo, o_hi = 16 * j, 128 + 16 * j
         lo, hi = w & 0xF, w >> 4
         A = [sc_lo * int((lo * L[o_lo:o_lo + 16]).sum()) + sc_hi * int((hi * L[o_hi:o_hi + 16]).sum())
              for L in (hi_l, mid_l, lo_l)]

@@ -80,6 +80,20 @@ struct CtxGuard {
 
 }  // namespace
 
+namespace unltd {
+
+// Reads and clears the context's device error word (bounded-wait timeouts).
+int32_t check_device_error(unltd_ctx c, const char *who) {
+  int v = 0;
+  cudaError_t e = cudaMemcpy(&v, c->err, sizeof(int), cudaMemcpyDeviceToHost);
+  if (e != cudaSuccess) return cuda_error(e, who);
+  if (v == 0) return UNLTD_OK;
+  cudaMemset(c->err, 0, sizeof(int));
+  return set_error(UNLTD_ERR_TIMEOUT, std::string(who) + ": a kernel gave up waiting on a pipeline barrier");
+}
+
+}  // namespace unltd
+
 extern "C" {
 
 const char *unltd_last_error(void) { return g_err.c_str(); }
@@ -107,6 +121,7 @@ int32_t unltd_ctx_create(int32_t device, unltd_ctx *out) {
   if (e == cudaSuccess) e = cudaMalloc(&c->argmax_key, 64);
   if (e == cudaSuccess) {
     c->argmax_done = reinterpret_cast<unsigned *>(reinterpret_cast<uint8_t *>(c->argmax_key) + 8);
+    c->err = reinterpret_cast<int *>(reinterpret_cast<uint8_t *>(c->argmax_key) + 12);
     e = cudaMemset(c->argmax_key, 0, 64);
   }
   if (e == cudaSuccess) {
@@ -151,7 +166,9 @@ int32_t unltd_ctx_set_stream(unltd_ctx c, void *s) {
 int32_t unltd_ctx_synchronize(unltd_ctx c) {
   if (!c) return set_error(UNLTD_ERR_INVALID_ARG, "ctx_synchronize: NULL ctx");
   CtxGuard g(c->device);
-  return cuda_error(cudaStreamSynchronize(c->stream), "ctx_synchronize");
+  int32_t rc = cuda_error(cudaStreamSynchronize(c->stream), "ctx_synchronize");
+  if (rc) return rc;
+  return check_device_error(c, "ctx_synchronize");
 }
 
 int64_t unltd_ctx_launch_count(unltd_ctx c) { return c ? c->launches.load() : -1; }
@@ -333,7 +350,8 @@ int32_t host_gemv(float *out, size_t out_len, const float *x, size_t x_len, cons
   if ((rc = gemv_launch(s.ctx, a))) return rc;
   e = cudaMemcpyAsync(out, s.ybuf, dim_out * sizeof(float), cudaMemcpyDeviceToHost, st);
   if (e == cudaSuccess) e = cudaStreamSynchronize(st);
-  return cuda_error(e, who);
+  if ((rc = cuda_error(e, who))) return rc;
+  return check_device_error(s.ctx, who);
 }
 
 }  // namespace

@@ -7,16 +7,27 @@
 //     22-bit fixed-point integer per span split into three byte limbs (s8
 //     hi, u8 mid, u8 lo) with a power-of-two scale; mode Q8K_EXACT stores
 //     quantize_q8_k's output (quants.rs:250-290) bit for bit.
-//  2. gemv: each warp owns R output rows; its four 8-lane subgroups walk
-//     consecutive blocks of those rows, one 16-byte chunk of packed quants
-//     per lane per row, and form exact integer dot products with DP4A
-//     against the image held in shared memory. F32X combines the integer
-//     limb sums in f32 per block; Q8K_EXACT reproduces the reference's
-//     per-lane (e % 8) integer sums and then its sequential f32 epilogue
-//     (quants.rs:343-358, 402-411) without FMA, block by block in order.
-// The gemv kernel is launched with programmatic dependent launch so its
-// CTAs become resident while prep runs; it waits (griddepcontrol.wait)
-// before reading the image.
+//  2. gemv: a persistent kernel, one CTA per SM over a contiguous range of
+//     rows. A producer warp streams tiles of T rows (one contiguous chunk of
+//     global memory each) into a ring of shared-memory stages with 1-D bulk
+//     copies (TMA) completing on mbarriers; eight consumer warps process each
+//     tile in two phases:
+//       integer phase — each 8-lane subgroup takes (R rows, block) items; a
+//         lane handles one 16-byte chunk of the block's packed quants and
+//         forms exact integer dot products with DP4A against the x image;
+//         F32X writes one f32 partial per (row, block), Q8K_EXACT writes the
+//         reference's per-block products d * sumi[k] for its eight lane
+//         classes k = e % 8 (quants.rs:337-346, 390-404) and dmin * minsum;
+//       chain phase — per row, the sequential per-block epilogue in block
+//         order: F32X sums its partials; Q8K_EXACT runs
+//         sums[k] += ..., sumf -= ... and s = sumf + sums[0] + ... + sums[7]
+//         without FMA (quants.rs:343-358, 402-411), bit for bit.
+//     The weight stage is released right after the integer phase, so the
+//     producer refills it while the chain phase runs.
+// The gemv kernel is launched with programmatic dependent launch: its
+// producer starts streaming weights while prep still runs; the consumers wait
+// (griddepcontrol.wait) before reading the image. Every mbarrier wait is
+// bounded in time and reports a timeout through the context error word.
 #include <algorithm>
 #include <cstdio>
 #include <mutex>
@@ -29,11 +40,15 @@
 namespace unltd {
 namespace {
 
-constexpr int kThreads = 256;
+constexpr int kThreads = 256;  // prep kernels
+constexpr int kConsumerWarps = 8;
+constexpr int kConsumers = kConsumerWarps * 32;
+constexpr int kGemvThreads = kConsumers + 32;  // + one producer warp
+constexpr int kMaxStages = 8;
+constexpr int kBarBytes = 128;
 
 // ---------------------------------------------------------------- prep ----
 
-// Block-wide reductions for the 256-thread prep kernels.
 __device__ __forceinline__ float block_max(float v, float *red) {
   for (int o = 16; o; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
   int w = threadIdx.x >> 5;
@@ -43,6 +58,13 @@ __device__ __forceinline__ float block_max(float v, float *red) {
   for (int i = 1; i < 8; i++) r = fmaxf(r, red[i]);
   __syncthreads();
   return r;
+}
+
+template <int FMT>
+__device__ __forceinline__ int f32x_pos(int t) {
+  if constexpr (FMT == Q4K) return q4_xpos(t);
+  else if constexpr (FMT == Q6K) return q6_xpos(t);
+  else return q80_xpos(t);
 }
 
 template <int FMT>
@@ -75,16 +97,13 @@ __global__ void __launch_bounds__(kThreads) prep_f32x(const float *__restrict__ 
     xs = ldexpf(1.0f, ex - 22);
   }
   if (bad_s) xs = __int_as_float(0x7fc00000);  // non-finite x: outputs become NaN
-  int pos;
-  if constexpr (FMT == Q4K) pos = q4_xpos(t);
-  else if constexpr (FMT == Q6K) pos = q6_xpos(t);
-  else pos = t;
+  const int pos = f32x_pos<FMT>(t);
   uint8_t *im = img + span * kImgF32X;
   im[pos] = (uint8_t)(xi >> 16);
   im[256 + pos] = (uint8_t)((xi >> 8) & 0xFF);
   im[512 + pos] = (uint8_t)(xi & 0xFF);
   if constexpr (FMT == Q4K) {
-    // lane-half sums for the Q4_K min term: lane j = 2p + (k>=4), half = nibble group
+    // lane-half sums for the Q4_K min term: lane j = 2p + (k >= 4), half = nibble group
     int p = t >> 6, half = (t >> 5) & 1, k = t & 7;
     atomicAdd(&hsum[2 * (2 * p + (k >> 2)) + half], xi);
   }
@@ -95,7 +114,7 @@ __global__ void __launch_bounds__(kThreads) prep_f32x(const float *__restrict__ 
   }
 }
 
-// Exact restatement of quantize_q8_k (quants.rs:250-290) for one span per CTA.
+// Exact restatement of quantize_q8_k (quants.rs:250-290), one span per CTA.
 template <int FMT>
 __global__ void __launch_bounds__(kThreads) prep_q8k(const float *__restrict__ x, size_t dim_in,
                                                      uint8_t *__restrict__ img,
@@ -167,10 +186,9 @@ __global__ void __launch_bounds__(kThreads) prep_q8k(const float *__restrict__ x
     int j = 4 * h + u;
     int pic = q6_pic(ipos);
     int w = pic >> 2, bpos = pic & 3;
-    int base = (((j * 2 + hh) * 4 + w) * 2) * 4;  // byte offset of word A
-    int own = bpos < 2 ? 0 : 4;
-    im[base + own + bpos] = (uint8_t)(int8_t)q;
-    im[base + (4 - own) + bpos] = 0;
+    int own = bpos < 2 ? 0 : 1;
+    im[q6_q8k_byte(j, hh, w, own, bpos)] = (uint8_t)(int8_t)q;
+    im[q6_q8k_byte(j, hh, w, 1 - own, bpos)] = 0;
     if (t == 0) *reinterpret_cast<float *>(im + kImgQ8K6_D) = d;
   }
 }
@@ -179,21 +197,25 @@ __global__ void __launch_bounds__(kThreads) prep_q8k(const float *__restrict__ x
 
 struct Params {
   const uint8_t *W;
-  size_t stride;
-  int nb;       // blocks per row (Q8_0: 32-element blocks)
-  int nspans;   // 256-element spans
+  size_t stride;   // device bytes per row
+  int nb;          // blocks per row (Q8_0: 32-element blocks)
+  int nbu;         // work units per row: 256-element blocks (K-quants) or spans (Q8_0)
   int rows;
   const uint8_t *img;
+  int img_bytes;
   float *y;
   unsigned long long *key;
   unsigned *done;
   uint32_t *token;
+  int *err;
+  int T;           // rows per tile
+  int S;           // stages
+  int stage_bytes; // bytes per stage buffer (>= T * stride, multiple of 128)
+  int rs;          // chain-buffer row stride in floats
+  int cbuf_bytes;  // one chain buffer
 };
 
-__device__ __forceinline__ float warp_sum(float v) {
-  for (int o = 16; o; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
-  return v;
-}
+__device__ __forceinline__ uint4 lds128(const uint8_t *p) { return *reinterpret_cast<const uint4 *>(p); }
 
 __device__ __forceinline__ unsigned long long argmax_key(float v, int row) {
   if (isnan(v)) return row == 0 ? ~0ull : 0ull;
@@ -212,15 +234,15 @@ __device__ __forceinline__ void q4_scales(const uint4 &hq, int p, int &sc_lo, in
     SC = (hq.w & 0x0F0F0F0Fu) | ((hq.y >> 2) & 0x30303030u);
     MM = ((hq.w >> 4) & 0x0F0F0F0Fu) | ((hq.z >> 2) & 0x30303030u);
   }
-  int sh = (p & 1) * 16;
+  const int sh = (p & 1) * 16;
   sc_lo = (SC >> sh) & 0xFF;
   sc_hi = (SC >> (sh + 8)) & 0xFF;
   m_lo = (MM >> sh) & 0xFF;
   m_hi = (MM >> (sh + 8)) & 0xFF;
 }
 
-// Q6_K: four words of 4*(raw6 - 32) as s8 from ql/qh words (shift of the
-// 2-bit field in qh: s for the low-nibble half, s+4 for the high half).
+// Q6_K: a word of 4*(raw6 - 32) as s8 from ql/qh words (2-bit field of qh at
+// shift sl for the low-nibble half, sl + 4 for the high half).
 __device__ __forceinline__ uint32_t q6_a4_lo(uint32_t ql, uint32_t qh, int sl) {
   return (((ql << 2) & 0x3C3C3C3Cu) | ((qh << (6 - sl)) & 0xC0C0C0C0u)) ^ 0x80808080u;
 }
@@ -228,335 +250,347 @@ __device__ __forceinline__ uint32_t q6_a4_hi(uint32_t ql, uint32_t qh, int sl) {
   return (((ql >> 2) & 0x3C3C3C3Cu) | ((qh << (2 - sl)) & 0xC0C0C0C0u)) ^ 0x80808080u;
 }
 
+__device__ __forceinline__ float sub_sum(float v, unsigned m) {
+  v += __shfl_xor_sync(m, v, 4);
+  v += __shfl_xor_sync(m, v, 2);
+  v += __shfl_xor_sync(m, v, 1);
+  return v;
+}
+
+// One (R rows, block b) item of the integer phase for an 8-lane subgroup.
+// rowp[r]: the rows in shared memory; im: the x image of block/span b.
+// F32X: writes cb[r * rs + b]. Q8K: writes cb[r * rs + 8b + k] (d * sumi per
+// class) and cm[r * rs/8 + b] (dmin * minsum). cb/cm point at the item's first row.
+template <int FMT, int MODE, int R>
+__device__ __forceinline__ void integer_item(const uint8_t *const (&rowp)[R], const bool (&rv)[R], int b,
+                                             const uint8_t *im, const Params &P, float *cb, float *cm, int j,
+                                             unsigned m) {
+  const int nb = P.nb;
+  if constexpr (MODE == MODE_F32X) {
+    float acc[R];
+    if constexpr (FMT == Q4K) {
+      const int p = j >> 1, kh = j & 1;
+      const uint4 xh0 = lds128(im + 16 * j), xh1 = lds128(im + 128 + 16 * j);
+      const uint4 xm0 = lds128(im + 256 + 16 * j), xm1 = lds128(im + 384 + 16 * j);
+      const uint4 xl0 = lds128(im + 512 + 16 * j), xl1 = lds128(im + 640 + 16 * j);
+      const float xs = *reinterpret_cast<const float *>(im + kImgF32X_XS);
+      const float xsl = reinterpret_cast<const float *>(im + kImgF32X_XSUM)[2 * j];
+      const float xsh = reinterpret_cast<const float *>(im + kImgF32X_XSUM)[2 * j + 1];
+      const uint32_t xh_lo[4] = {xh0.x, xh0.y, xh0.z, xh0.w}, xh_hi[4] = {xh1.x, xh1.y, xh1.z, xh1.w};
+      const uint32_t xm_lo[4] = {xm0.x, xm0.y, xm0.z, xm0.w}, xm_hi[4] = {xm1.x, xm1.y, xm1.z, xm1.w};
+      const uint32_t xl_lo[4] = {xl0.x, xl0.y, xl0.z, xl0.w}, xl_hi[4] = {xl1.x, xl1.y, xl1.z, xl1.w};
+#pragma unroll
+      for (int r = 0; r < R; r++) {
+        const uint4 hq = lds128(rowp[r] + b * 16);
+        const uint4 q = lds128(rowp[r] + nb * 16 + b * 128 + 32 * p + 16 * kh);
+        int sc_lo, sc_hi, m_lo, m_hi;
+        q4_scales(hq, p, sc_lo, sc_hi, m_lo, m_hi);
+        const uint32_t w[4] = {q.x, q.y, q.z, q.w};
+        int shl = 0, sml = 0, sll = 0, shh = 0, smh = 0, slh = 0;
+#pragma unroll
+        for (int t = 0; t < 4; t++) {
+          const uint32_t lo = w[t] & 0x0F0F0F0Fu, hi = (w[t] >> 4) & 0x0F0F0F0Fu;
+          shl = dp4a_us(lo, xh_lo[t], shl);
+          sml = dp4a_uu(lo, xm_lo[t], sml);
+          sll = dp4a_uu(lo, xl_lo[t], sll);
+          shh = dp4a_us(hi, xh_hi[t], shh);
+          smh = dp4a_uu(hi, xm_hi[t], smh);
+          slh = dp4a_uu(hi, xl_hi[t], slh);
+        }
+        const int ah = sc_lo * shl + sc_hi * shh;
+        const int am = sc_lo * sml + sc_hi * smh;
+        const int al = sc_lo * sll + sc_hi * slh;
+        const float F = fmaf((float)ah, 65536.0f, fmaf((float)am, 256.0f, (float)al));
+        const float d = h2f_bits(hq.x & 0xFFFFu), dmin = h2f_bits(hq.x >> 16);
+        const float M = fmaf((float)m_lo, xsl, (float)m_hi * xsh);
+        acc[r] = fmaf(d * xs, F, -dmin * M);
+      }
+    } else if constexpr (FMT == Q6K) {
+      const int h = j >> 2, u = j & 3, sl = 2 * (u >> 1);
+      const uint4 xh0 = lds128(im + 16 * j), xh1 = lds128(im + 128 + 16 * j);
+      const uint4 xm0 = lds128(im + 256 + 16 * j), xm1 = lds128(im + 384 + 16 * j);
+      const uint4 xl0 = lds128(im + 512 + 16 * j), xl1 = lds128(im + 640 + 16 * j);
+      const float xs = *reinterpret_cast<const float *>(im + kImgF32X_XS);
+      const uint32_t xh_lo[4] = {xh0.x, xh0.y, xh0.z, xh0.w}, xh_hi[4] = {xh1.x, xh1.y, xh1.z, xh1.w};
+      const uint32_t xm_lo[4] = {xm0.x, xm0.y, xm0.z, xm0.w}, xm_hi[4] = {xm1.x, xm1.y, xm1.z, xm1.w};
+      const uint32_t xl_lo[4] = {xl0.x, xl0.y, xl0.z, xl0.w}, xl_hi[4] = {xl1.x, xl1.y, xl1.z, xl1.w};
+#pragma unroll
+      for (int r = 0; r < R; r++) {
+        const uint8_t *row = rowp[r];
+        const uint4 ql = lds128(row + b * 128 + 16 * j);
+        const uint4 qh = lds128(row + nb * 128 + b * 64 + 16 * (2 * h + (u & 1)));
+        const int8_t *scp = reinterpret_cast<const int8_t *>(row + nb * 192 + b * 16);
+        const int sc_lo = scp[8 * h + u], sc_hi = scp[8 * h + 4 + u];
+        const float d = h2f_bits(*reinterpret_cast<const unsigned short *>(row + nb * 208 + b * 2));
+        const uint32_t wl[4] = {ql.x, ql.y, ql.z, ql.w}, wh[4] = {qh.x, qh.y, qh.z, qh.w};
+        int shl = 0, sml = 0, sll = 0, shh = 0, smh = 0, slh = 0;
+#pragma unroll
+        for (int t = 0; t < 4; t++) {
+          const uint32_t lo = q6_a4_lo(wl[t], wh[t], sl), hi = q6_a4_hi(wl[t], wh[t], sl);
+          shl = dp4a_ss(lo, xh_lo[t], shl);
+          sml = dp4a_su(lo, xm_lo[t], sml);
+          sll = dp4a_su(lo, xl_lo[t], sll);
+          shh = dp4a_ss(hi, xh_hi[t], shh);
+          smh = dp4a_su(hi, xm_hi[t], smh);
+          slh = dp4a_su(hi, xl_hi[t], slh);
+        }
+        const int ah = sc_lo * shl + sc_hi * shh;
+        const int am = sc_lo * sml + sc_hi * smh;
+        const int al = sc_lo * sll + sc_hi * slh;
+        const float F = fmaf((float)ah, 65536.0f, fmaf((float)am, 256.0f, (float)al));
+        acc[r] = d * xs * 0.25f * F;
+      }
+    } else {  // Q8_0: lane j owns 32-element block 8b + j of span b
+      const int b32 = 8 * b + j;
+      const bool ok = b32 < nb;
+      const uint4 xh0 = lds128(im + 16 * j), xh1 = lds128(im + 128 + 16 * j);
+      const uint4 xm0 = lds128(im + 256 + 16 * j), xm1 = lds128(im + 384 + 16 * j);
+      const uint4 xl0 = lds128(im + 512 + 16 * j), xl1 = lds128(im + 640 + 16 * j);
+      const float xs = *reinterpret_cast<const float *>(im + kImgF32X_XS);
+      const uint32_t xh[8] = {xh0.x, xh0.y, xh0.z, xh0.w, xh1.x, xh1.y, xh1.z, xh1.w};
+      const uint32_t xm[8] = {xm0.x, xm0.y, xm0.z, xm0.w, xm1.x, xm1.y, xm1.z, xm1.w};
+      const uint32_t xl[8] = {xl0.x, xl0.y, xl0.z, xl0.w, xl1.x, xl1.y, xl1.z, xl1.w};
+      const int bb = ok ? b32 : 0;
+#pragma unroll
+      for (int r = 0; r < R; r++) {
+        const uint4 q0 = lds128(rowp[r] + bb * 32), q1 = lds128(rowp[r] + bb * 32 + 16);
+        const float d = h2f_bits(*reinterpret_cast<const unsigned short *>(rowp[r] + nb * 32 + bb * 2));
+        const uint32_t w[8] = {q0.x, q0.y, q0.z, q0.w, q1.x, q1.y, q1.z, q1.w};
+        int sh = 0, sm = 0, sll = 0;
+#pragma unroll
+        for (int t = 0; t < 8; t++) {
+          sh = dp4a_ss(w[t], xh[t], sh);
+          sm = dp4a_su(w[t], xm[t], sm);
+          sll = dp4a_su(w[t], xl[t], sll);
+        }
+        const float F = fmaf((float)sh, 65536.0f, fmaf((float)sm, 256.0f, (float)sll));
+        acc[r] = ok ? d * xs * F : 0.0f;
+      }
+    }
+#pragma unroll
+    for (int r = 0; r < R; r++) {
+      const float v = sub_sum(acc[r], m);
+      if (j == 0 && rv[r]) cb[r * P.rs + b] = v;
+    }
+  } else {  // MODE_Q8K
+    float *tk = cb;  // rows of rs floats: 8 per block
+    float *tm = cm;  // rows of rs/8 floats: 1 per block
+    const int rs2 = P.rs / 8;
+    const float xd = *reinterpret_cast<const float *>(im + (FMT == Q4K ? kImgQ8K4_D : kImgQ8K6_D));
+    if constexpr (FMT == Q4K) {
+      const int p = j >> 1, kh = j & 1;
+      const uint4 q80 = lds128(im + 16 * j), q81 = lds128(im + 128 + 16 * j);
+      const int bs_lo = reinterpret_cast<const int *>(im + kImgQ8K4_BS)[2 * j];
+      const int bs_hi = reinterpret_cast<const int *>(im + kImgQ8K4_BS)[2 * j + 1];
+      const uint32_t qa[4] = {q80.x, q80.y, q80.z, q80.w}, qb[4] = {q81.x, q81.y, q81.z, q81.w};
+      const bool b2 = (j >> 2) & 1, b1 = (j >> 1) & 1;
+      const int kj = 4 * kh + 2 * b2 + b1;  // class held after the reduction
+#pragma unroll
+      for (int r = 0; r < R; r++) {
+        const uint4 hq = lds128(rowp[r] + b * 16);
+        const uint4 q = lds128(rowp[r] + nb * 16 + b * 128 + 32 * p + 16 * kh);
+        int sc_lo, sc_hi, m_lo, m_hi;
+        q4_scales(hq, p, sc_lo, sc_hi, m_lo, m_hi);
+        const uint32_t w[4] = {q.x, q.y, q.z, q.w};
+        int P4[4];
+#pragma unroll
+        for (int t = 0; t < 4; t++) {
+          const uint32_t lo = w[t] & 0x0F0F0F0Fu, hi = (w[t] >> 4) & 0x0F0F0F0Fu;
+          P4[t] = sc_lo * dp4a_us(lo, qa[t], 0) + sc_hi * dp4a_us(hi, qb[t], 0);
+        }
+        int msum = m_lo * bs_lo + m_hi * bs_hi;
+        // reduce over the four lanes sharing kh (lane bits 1, 2): recursive halving
+        int k0 = b2 ? P4[2] : P4[0], k1 = b2 ? P4[3] : P4[1];
+        const int s0 = b2 ? P4[0] : P4[2], s1 = b2 ? P4[1] : P4[3];
+        k0 += __shfl_xor_sync(m, s0, 4);
+        k1 += __shfl_xor_sync(m, s1, 4);
+        int keep = b1 ? k1 : k0;
+        const int send = b1 ? k0 : k1;
+        keep += __shfl_xor_sync(m, send, 2);
+        msum += __shfl_xor_sync(m, msum, 4);
+        msum += __shfl_xor_sync(m, msum, 2);
+        msum += __shfl_xor_sync(m, msum, 1);
+        const float d = __fmul_rn(xd, h2f_bits(hq.x & 0xFFFFu));   // q8.d * f16(d)
+        const float dm = __fmul_rn(h2f_bits(hq.x >> 16), xd);      // f16(dmin) * q8.d
+        if (rv[r]) {
+          tk[r * P.rs + 8 * b + kj] = __fmul_rn(d, (float)keep);
+          if (j == 0) tm[r * rs2 + b] = __fmul_rn(dm, (float)msum);
+        }
+      }
+    } else {  // Q6_K
+      const int h = j >> 2, u = j & 3, sl = 2 * (u >> 1);
+      const uint4 c0 = lds128(im + 16 * j), c1 = lds128(im + 128 + 16 * j);
+      const uint4 c2 = lds128(im + 256 + 16 * j), c3 = lds128(im + 384 + 16 * j);
+      const uint32_t qA_lo[4] = {c0.x, c0.z, c1.x, c1.z}, qB_lo[4] = {c0.y, c0.w, c1.y, c1.w};
+      const uint32_t qA_hi[4] = {c2.x, c2.z, c3.x, c3.z}, qB_hi[4] = {c2.y, c2.w, c3.y, c3.w};
+      const bool b2 = (j >> 2) & 1, b1 = (j >> 1) & 1, b0 = j & 1;
+#pragma unroll
+      for (int r = 0; r < R; r++) {
+        const uint8_t *row = rowp[r];
+        const uint4 ql = lds128(row + b * 128 + 16 * j);
+        const uint4 qh = lds128(row + nb * 128 + b * 64 + 16 * (2 * h + (u & 1)));
+        const int8_t *scp = reinterpret_cast<const int8_t *>(row + nb * 192 + b * 16);
+        const int sc_lo = scp[8 * h + u], sc_hi = scp[8 * h + 4 + u];
+        const uint32_t dbits = *reinterpret_cast<const unsigned short *>(row + nb * 208 + b * 2);
+        const uint32_t wl[4] = {ql.x, ql.y, ql.z, ql.w}, wh[4] = {qh.x, qh.y, qh.z, qh.w};
+        int P4[8];
+#pragma unroll
+        for (int t = 0; t < 4; t++) {
+          const uint32_t lo = q6_a4_lo(wl[t], wh[t], sl), hi = q6_a4_hi(wl[t], wh[t], sl);
+          P4[2 * t] = sc_lo * dp4a_ss(lo, qA_lo[t], 0) + sc_hi * dp4a_ss(hi, qA_hi[t], 0);
+          P4[2 * t + 1] = sc_lo * dp4a_ss(lo, qB_lo[t], 0) + sc_hi * dp4a_ss(hi, qB_hi[t], 0);
+        }
+        // reduce-scatter over the 8 lanes: lane j ends with class k = j
+        int v4[4];
+#pragma unroll
+        for (int i = 0; i < 4; i++) {
+          const int keepv = b2 ? P4[4 + i] : P4[i];
+          const int sendv = b2 ? P4[i] : P4[4 + i];
+          v4[i] = keepv + __shfl_xor_sync(m, sendv, 4);
+        }
+        int v2[2];
+#pragma unroll
+        for (int i = 0; i < 2; i++) {
+          const int keepv = b1 ? v4[2 + i] : v4[i];
+          const int sendv = b1 ? v4[i] : v4[2 + i];
+          v2[i] = keepv + __shfl_xor_sync(m, sendv, 2);
+        }
+        const int keepv = b0 ? v2[1] : v2[0];
+        const int sendv = b0 ? v2[0] : v2[1];
+        const int sumi = (keepv + __shfl_xor_sync(m, sendv, 1)) >> 2;
+        const float d = __fmul_rn(xd, h2f_bits(dbits));
+        if (rv[r]) tk[r * P.rs + 8 * b + j] = __fmul_rn(d, (float)sumi);
+      }
+    }
+  }
+}
+
 template <int FMT, int MODE, int R, bool ARGMAX>
-__global__ void __launch_bounds__(kThreads) gemv_kernel(Params P) {
-  extern __shared__ uint4 smem4[];
-  const uint8_t *simg = reinterpret_cast<const uint8_t *>(smem4);
-  constexpr int ISTR = (MODE == MODE_F32X) ? kImgF32X : (FMT == Q4K ? kImgQ8K4 : kImgQ8K6);
+__global__ void __launch_bounds__(kGemvThreads, 1) gemv_kernel(Params P) {
+  extern __shared__ __align__(128) uint8_t smem[];
+  uint64_t *full = reinterpret_cast<uint64_t *>(smem);
+  uint64_t *empty = full + kMaxStages;
+  uint8_t *ximg = smem + kBarBytes;
+  float *cbuf0 = reinterpret_cast<float *>(ximg + P.img_bytes);
+  uint8_t *stages = reinterpret_cast<uint8_t *>(cbuf0) + 2 * P.cbuf_bytes;
 
-  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-  const int s = lane >> 3, j = lane & 7;
-  const int ntasks = (P.rows + R - 1) / R;
-  const int gw = blockIdx.x * (kThreads / 32) + warp, nw = gridDim.x * (kThreads / 32);
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int G = gridDim.x;
+  const int rb = (int)((long long)P.rows * blockIdx.x / G);
+  const int re = (int)((long long)P.rows * (blockIdx.x + 1) / G);
+  const int ntiles = (re - rb + P.T - 1) / P.T;
 
-  pdl_wait();
-  {
-    const uint4 *src = reinterpret_cast<const uint4 *>(P.img);
-    uint4 *dst = smem4;
-    const int n16 = P.nspans * ISTR / 16;
-    for (int i = threadIdx.x; i < n16; i += kThreads) dst[i] = src[i];
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < P.S; s++) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], kConsumerWarps);
+    }
+    fence_mbar_init();
   }
   __syncthreads();
 
+  if (warp == kConsumerWarps) {
+    // ---------------- producer: one thread streams row tiles -------------
+    if (lane == 0) {
+      int issued = 0;
+      bool ok = true;
+      for (int i = 0; i < ntiles && ok; i++) {
+        const int s = i % P.S;
+        if (i >= P.S) ok = mbar_wait_bounded(&empty[s], ((i / P.S) - 1) & 1, P.err);
+        if (!ok) break;
+        const int r0 = rb + i * P.T;
+        const int nr = min(P.T, re - r0);
+        const uint32_t bytes = (uint32_t)(nr * P.stride);
+        mbar_expect_tx(&full[s], bytes);
+        bulk_g2s(stages + (size_t)s * P.stage_bytes, P.W + (size_t)r0 * P.stride, bytes, &full[s]);
+        issued = i + 1;
+      }
+      // never leave with copies in flight: wait (bounded) for the last copy of each stage
+      for (int i = max(0, issued - P.S); i < issued; i++)
+        mbar_wait_bounded(&full[i % P.S], (i / P.S) & 1, P.err);
+    }
+    return;
+  }
+
+  // ---------------- consumers ---------------------------------------------
+  pdl_wait();
+  {
+    const uint4 *src = reinterpret_cast<const uint4 *>(P.img);
+    uint4 *dst = reinterpret_cast<uint4 *>(ximg);
+    for (int i = threadIdx.x; i < P.img_bytes / 16; i += kConsumers) dst[i] = src[i];
+  }
+  named_bar_sync(1, kConsumers);
+
+  const int s_in = lane >> 3, j = lane & 7;
+  const unsigned subm = 0xFFu << (lane & 24);
+  const int sg = warp * 4 + s_in;  // subgroup id 0..31
   unsigned long long best = 0ull;
-  const int nsteps = (FMT == Q8_0) ? (P.nspans + 3) / 4 : (P.nb + 3) / 4;
+  const int istr = MODE == MODE_F32X ? kImgF32X : (FMT == Q4K ? kImgQ8K4 : kImgQ8K6);
 
-  for (int task = gw; task < ntasks; task += nw) {
-    const int row0 = task * R;
-    const uint8_t *Wr[R];
+  for (int i = 0; i < ntiles; i++) {
+    const int s = i % P.S;
+    const int r0 = rb + i * P.T;
+    const int nr = min(P.T, re - r0);
+    const bool got = mbar_wait_bounded(&full[s], (i / P.S) & 1, P.err);
+    if (!named_bar_red_and(1, kConsumers, got)) break;  // uniform: every consumer leaves together
+    const uint8_t *tile = stages + (size_t)s * P.stage_bytes;
+    float *cb = reinterpret_cast<float *>(reinterpret_cast<uint8_t *>(cbuf0) + (i & 1) * P.cbuf_bytes);
+
+    // integer phase
+    const int ngroups = (nr + R - 1) / R;
+    const int nitems = ngroups * P.nbu;
+    for (int it = sg; it < nitems; it += 32) {
+      const int g = it / P.nbu, b = it - g * P.nbu;
+      const uint8_t *rowp[R];
+      bool rv[R];
 #pragma unroll
-    for (int r = 0; r < R; r++) Wr[r] = P.W + (size_t)min(row0 + r, P.rows - 1) * P.stride;
+      for (int r = 0; r < R; r++) {
+        const int lr = g * R + r;
+        rv[r] = lr < nr;
+        rowp[r] = tile + (size_t)(rv[r] ? lr : 0) * P.stride;
+      }
+      float *cbr = cb + g * R * P.rs;                       // this group's first chain row
+      float *cmr = cb + P.T * P.rs + g * R * (P.rs / 8);    // Q8K: its dmin*minsum row
+      integer_item<FMT, MODE, R>(rowp, rv, b, ximg + (size_t)b * istr, P, cbr, cmr, j, subm);
+    }
+    __syncwarp();
+    if (lane == 0) mbar_arrive(&empty[s]);  // this warp is done with the weight stage
+    named_bar_sync(1, kConsumers);
 
+    // chain phase
     if constexpr (MODE == MODE_F32X) {
-      float acc[R];
-#pragma unroll
-      for (int r = 0; r < R; r++) acc[r] = 0.0f;
-      for (int st = 0; st < nsteps; st++) {
-        if constexpr (FMT == Q4K) {
-          const int b = 4 * st + s;
-          if (b < P.nb) {
-            const int p = j >> 1, kh = j & 1;
-            const uint8_t *im = simg + b * kImgF32X;
-            const int o_lo = 64 * p + 16 * kh, o_hi = o_lo + 32;
-            const uint4 xh0 = *reinterpret_cast<const uint4 *>(im + o_lo);
-            const uint4 xh1 = *reinterpret_cast<const uint4 *>(im + o_hi);
-            const uint4 xm0 = *reinterpret_cast<const uint4 *>(im + 256 + o_lo);
-            const uint4 xm1 = *reinterpret_cast<const uint4 *>(im + 256 + o_hi);
-            const uint4 xl0 = *reinterpret_cast<const uint4 *>(im + 512 + o_lo);
-            const uint4 xl1 = *reinterpret_cast<const uint4 *>(im + 512 + o_hi);
-            const float xs = *reinterpret_cast<const float *>(im + kImgF32X_XS);
-            const float xsl = reinterpret_cast<const float *>(im + kImgF32X_XSUM)[2 * j];
-            const float xsh = reinterpret_cast<const float *>(im + kImgF32X_XSUM)[2 * j + 1];
-            uint4 hq[R], q[R];
-#pragma unroll
-            for (int r = 0; r < R; r++) {
-              hq[r] = __ldg(reinterpret_cast<const uint4 *>(Wr[r] + b * 16));
-              q[r] = ldg_stream(Wr[r] + (size_t)P.nb * 16 + b * 128 + 32 * p + 16 * kh);
-            }
-#pragma unroll
-            for (int r = 0; r < R; r++) {
-              int sc_lo, sc_hi, m_lo, m_hi;
-              q4_scales(hq[r], p, sc_lo, sc_hi, m_lo, m_hi);
-              const uint32_t w[4] = {q[r].x, q[r].y, q[r].z, q[r].w};
-              const uint32_t xh_lo[4] = {xh0.x, xh0.y, xh0.z, xh0.w}, xh_hi[4] = {xh1.x, xh1.y, xh1.z, xh1.w};
-              const uint32_t xm_lo[4] = {xm0.x, xm0.y, xm0.z, xm0.w}, xm_hi[4] = {xm1.x, xm1.y, xm1.z, xm1.w};
-              const uint32_t xl_lo[4] = {xl0.x, xl0.y, xl0.z, xl0.w}, xl_hi[4] = {xl1.x, xl1.y, xl1.z, xl1.w};
-              int shl = 0, sml = 0, sll = 0, shh = 0, smh = 0, slh = 0;
-#pragma unroll
-              for (int t = 0; t < 4; t++) {
-                const uint32_t lo = w[t] & 0x0F0F0F0Fu, hi = (w[t] >> 4) & 0x0F0F0F0Fu;
-                shl = dp4a_us(lo, xh_lo[t], shl);
-                sml = dp4a_uu(lo, xm_lo[t], sml);
-                sll = dp4a_uu(lo, xl_lo[t], sll);
-                shh = dp4a_us(hi, xh_hi[t], shh);
-                smh = dp4a_uu(hi, xm_hi[t], smh);
-                slh = dp4a_uu(hi, xl_hi[t], slh);
-              }
-              const int ah = sc_lo * shl + sc_hi * shh;
-              const int am = sc_lo * sml + sc_hi * smh;
-              const int al = sc_lo * sll + sc_hi * slh;
-              const float F = fmaf((float)ah, 65536.0f, fmaf((float)am, 256.0f, (float)al));
-              const float d = h2f_bits(hq[r].x & 0xFFFFu), dmin = h2f_bits(hq[r].x >> 16);
-              const float M = fmaf((float)m_lo, xsl, (float)m_hi * xsh);
-              acc[r] = fmaf(d * xs, F, acc[r]);
-              acc[r] = fmaf(-dmin, M, acc[r]);
-            }
-          }
-        } else if constexpr (FMT == Q6K) {
-          const int b = 4 * st + s;
-          if (b < P.nb) {
-            const int h = j >> 2, u = j & 3, sl = 2 * (u >> 1);
-            const uint8_t *im = simg + b * kImgF32X;
-            const int o_lo = 32 * j, o_hi = o_lo + 16;
-            const uint4 xh0 = *reinterpret_cast<const uint4 *>(im + o_lo);
-            const uint4 xh1 = *reinterpret_cast<const uint4 *>(im + o_hi);
-            const uint4 xm0 = *reinterpret_cast<const uint4 *>(im + 256 + o_lo);
-            const uint4 xm1 = *reinterpret_cast<const uint4 *>(im + 256 + o_hi);
-            const uint4 xl0 = *reinterpret_cast<const uint4 *>(im + 512 + o_lo);
-            const uint4 xl1 = *reinterpret_cast<const uint4 *>(im + 512 + o_hi);
-            const float xs = *reinterpret_cast<const float *>(im + kImgF32X_XS);
-            uint4 ql[R], qh[R];
-            int sc_lo[R], sc_hi[R];
-            uint32_t dbits[R];
-#pragma unroll
-            for (int r = 0; r < R; r++) {
-              ql[r] = ldg_stream(Wr[r] + b * 128 + 16 * j);
-              qh[r] = ldg_stream(Wr[r] + (size_t)P.nb * 128 + b * 64 + 16 * (2 * h + (u & 1)));
-              const int8_t *scp = reinterpret_cast<const int8_t *>(Wr[r] + (size_t)P.nb * 192 + b * 16);
-              sc_lo[r] = __ldg(scp + 8 * h + u);
-              sc_hi[r] = __ldg(scp + 8 * h + 4 + u);
-              dbits[r] = __ldg(reinterpret_cast<const unsigned short *>(Wr[r] + (size_t)P.nb * 208 + b * 2));
-            }
-#pragma unroll
-            for (int r = 0; r < R; r++) {
-              const uint32_t wl[4] = {ql[r].x, ql[r].y, ql[r].z, ql[r].w};
-              const uint32_t wh[4] = {qh[r].x, qh[r].y, qh[r].z, qh[r].w};
-              const uint32_t xh_lo[4] = {xh0.x, xh0.y, xh0.z, xh0.w}, xh_hi[4] = {xh1.x, xh1.y, xh1.z, xh1.w};
-              const uint32_t xm_lo[4] = {xm0.x, xm0.y, xm0.z, xm0.w}, xm_hi[4] = {xm1.x, xm1.y, xm1.z, xm1.w};
-              const uint32_t xl_lo[4] = {xl0.x, xl0.y, xl0.z, xl0.w}, xl_hi[4] = {xl1.x, xl1.y, xl1.z, xl1.w};
-              int shl = 0, sml = 0, sll = 0, shh = 0, smh = 0, slh = 0;
-#pragma unroll
-              for (int t = 0; t < 4; t++) {
-                const uint32_t lo = q6_a4_lo(wl[t], wh[t], sl), hi = q6_a4_hi(wl[t], wh[t], sl);
-                shl = dp4a_ss(lo, xh_lo[t], shl);
-                sml = dp4a_su(lo, xm_lo[t], sml);
-                sll = dp4a_su(lo, xl_lo[t], sll);
-                shh = dp4a_ss(hi, xh_hi[t], shh);
-                smh = dp4a_su(hi, xm_hi[t], smh);
-                slh = dp4a_su(hi, xl_hi[t], slh);
-              }
-              const int ah = sc_lo[r] * shl + sc_hi[r] * shh;
-              const int am = sc_lo[r] * sml + sc_hi[r] * smh;
-              const int al = sc_lo[r] * sll + sc_hi[r] * slh;
-              const float F = fmaf((float)ah, 65536.0f, fmaf((float)am, 256.0f, (float)al));
-              const float d = h2f_bits(dbits[r]);
-              acc[r] = fmaf(d * xs * 0.25f, F, acc[r]);
-            }
-          }
-        } else {  // Q8_0: 8 lanes = 8 blocks of 32 in a 256-span
-          const int span = 4 * st + s;
-          const int b32 = 8 * span + j;
-          if (b32 < P.nb) {
-            const uint8_t *im = simg + span * kImgF32X;
-            const int o = 32 * j;
-            const uint4 xh0 = *reinterpret_cast<const uint4 *>(im + o);
-            const uint4 xh1 = *reinterpret_cast<const uint4 *>(im + o + 16);
-            const uint4 xm0 = *reinterpret_cast<const uint4 *>(im + 256 + o);
-            const uint4 xm1 = *reinterpret_cast<const uint4 *>(im + 256 + o + 16);
-            const uint4 xl0 = *reinterpret_cast<const uint4 *>(im + 512 + o);
-            const uint4 xl1 = *reinterpret_cast<const uint4 *>(im + 512 + o + 16);
-            const float xs = *reinterpret_cast<const float *>(im + kImgF32X_XS);
-            uint4 q0[R], q1[R];
-            uint32_t dbits[R];
-#pragma unroll
-            for (int r = 0; r < R; r++) {
-              q0[r] = ldg_stream(Wr[r] + (size_t)b32 * 32);
-              q1[r] = ldg_stream(Wr[r] + (size_t)b32 * 32 + 16);
-              dbits[r] = __ldg(reinterpret_cast<const unsigned short *>(Wr[r] + (size_t)P.nb * 32 + b32 * 2));
-            }
-#pragma unroll
-            for (int r = 0; r < R; r++) {
-              const uint32_t w[8] = {q0[r].x, q0[r].y, q0[r].z, q0[r].w, q1[r].x, q1[r].y, q1[r].z, q1[r].w};
-              const uint32_t xh[8] = {xh0.x, xh0.y, xh0.z, xh0.w, xh1.x, xh1.y, xh1.z, xh1.w};
-              const uint32_t xm[8] = {xm0.x, xm0.y, xm0.z, xm0.w, xm1.x, xm1.y, xm1.z, xm1.w};
-              const uint32_t xl[8] = {xl0.x, xl0.y, xl0.z, xl0.w, xl1.x, xl1.y, xl1.z, xl1.w};
-              int sh = 0, sm = 0, sll = 0;
-#pragma unroll
-              for (int t = 0; t < 8; t++) {
-                sh = dp4a_ss(w[t], xh[t], sh);
-                sm = dp4a_su(w[t], xm[t], sm);
-                sll = dp4a_su(w[t], xl[t], sll);
-              }
-              const float F = fmaf((float)sh, 65536.0f, fmaf((float)sm, 256.0f, (float)sll));
-              acc[r] = fmaf(h2f_bits(dbits[r]) * xs, F, acc[r]);
-            }
-          }
+      const int t = threadIdx.x;
+      if (t < nr) {
+        const float *fr = cb + t * P.rs;
+        float v = 0.0f;
+        for (int b = 0; b < P.nbu; b++) v += fr[b];
+        const int row = r0 + t;
+        if (P.y) P.y[row] = v;
+        if (ARGMAX) {
+          const unsigned long long kk = argmax_key(v, row);
+          best = kk > best ? kk : best;
         }
       }
+    } else {
+      const int t = threadIdx.x, lr = t >> 3, k = t & 7;
+      if (lr < nr) {
+        const float *tk = cb + lr * P.rs + k;
+        const float *tm = cb + P.T * P.rs + lr * (P.rs / 8);
+        float sums = 0.0f, sumf = 0.0f;
+        for (int b = 0; b < P.nbu; b++) {
+          sums = __fadd_rn(sums, tk[8 * b]);
+          if (FMT == Q4K) sumf = __fsub_rn(sumf, tm[b]);
+        }
+        const unsigned gm = 0xFFu << (lane & 24);
+        float acc = sumf;  // Q6_K: sumf = 0, s = 0 + sums[0] + ...
 #pragma unroll
-      for (int r = 0; r < R; r++) {
-        const float v = warp_sum(acc[r]);
-        const int row = row0 + r;
-        if (row < P.rows) {
-          if (lane == 0 && P.y) P.y[row] = v;
+        for (int kk = 0; kk < 8; kk++) acc = __fadd_rn(acc, __shfl_sync(gm, sums, (lane & 24) + kk));
+        const int row = r0 + lr;
+        if (k == 0) {
+          if (P.y) P.y[row] = acc;
           if (ARGMAX) {
-            const unsigned long long k = argmax_key(v, row);
-            best = k > best ? k : best;
-          }
-        }
-      }
-    } else {  // MODE_Q8K: bit-exact with gemv_quant_q8k
-      float sums[R], sumf[R];
-#pragma unroll
-      for (int r = 0; r < R; r++) {
-        sums[r] = 0.0f;
-        sumf[r] = 0.0f;
-      }
-      for (int st = 0; st < nsteps; st++) {
-        const int b = 4 * st + s;
-        const bool valid = b < P.nb;
-        const int bb = valid ? b : P.nb - 1;  // clamp loads; results masked below
-        const uint8_t *im = simg + bb * ISTR;
-        const float xd = *reinterpret_cast<const float *>(im + (FMT == Q4K ? kImgQ8K4_D : kImgQ8K6_D));
-        float tk[R], tm[R];
-        if constexpr (FMT == Q4K) {
-          const int p = j >> 1, kh = j & 1;
-          const uint4 q80 = *reinterpret_cast<const uint4 *>(im + 64 * p + 16 * kh);
-          const uint4 q81 = *reinterpret_cast<const uint4 *>(im + 64 * p + 32 + 16 * kh);
-          const int bs_lo = reinterpret_cast<const int *>(im + kImgQ8K4_BS)[2 * j];
-          const int bs_hi = reinterpret_cast<const int *>(im + kImgQ8K4_BS)[2 * j + 1];
-          uint4 hq[R], q[R];
-#pragma unroll
-          for (int r = 0; r < R; r++) {
-            hq[r] = __ldg(reinterpret_cast<const uint4 *>(Wr[r] + bb * 16));
-            q[r] = ldg_stream(Wr[r] + (size_t)P.nb * 16 + bb * 128 + 32 * p + 16 * kh);
-          }
-#pragma unroll
-          for (int r = 0; r < R; r++) {
-            int sc_lo, sc_hi, m_lo, m_hi;
-            q4_scales(hq[r], p, sc_lo, sc_hi, m_lo, m_hi);
-            const uint32_t w[4] = {q[r].x, q[r].y, q[r].z, q[r].w};
-            const uint32_t qa[4] = {q80.x, q80.y, q80.z, q80.w}, qb[4] = {q81.x, q81.y, q81.z, q81.w};
-            int P4[4];
-#pragma unroll
-            for (int t = 0; t < 4; t++) {
-              const uint32_t lo = w[t] & 0x0F0F0F0Fu, hi = (w[t] >> 4) & 0x0F0F0F0Fu;
-              P4[t] = sc_lo * dp4a_us(lo, qa[t], 0) + sc_hi * dp4a_us(hi, qb[t], 0);
-            }
-            int msum = m_lo * bs_lo + m_hi * bs_hi;
-            // reduce over the four lanes sharing kh (lane bits 1, 2): recursive halving
-            const bool b2 = (j >> 2) & 1, b1 = (j >> 1) & 1;
-            int k0 = b2 ? P4[2] : P4[0], k1 = b2 ? P4[3] : P4[1];
-            const int s0 = b2 ? P4[0] : P4[2], s1 = b2 ? P4[1] : P4[3];
-            k0 += __shfl_xor_sync(0xffffffffu, s0, 4);
-            k1 += __shfl_xor_sync(0xffffffffu, s1, 4);
-            int keep = b1 ? k1 : k0;
-            const int send = b1 ? k0 : k1;
-            keep += __shfl_xor_sync(0xffffffffu, send, 2);
-            msum += __shfl_xor_sync(0xffffffffu, msum, 4);
-            msum += __shfl_xor_sync(0xffffffffu, msum, 2);
-            msum += __shfl_xor_sync(0xffffffffu, msum, 1);
-            const float d = __fmul_rn(xd, h2f_bits(hq[r].x & 0xFFFFu));   // q8.d * f16(d)
-            const float dm = __fmul_rn(h2f_bits(hq[r].x >> 16), xd);      // f16(dmin) * q8.d
-            tk[r] = __fmul_rn(d, (float)keep);
-            tm[r] = __fmul_rn(dm, (float)msum);
-          }
-        } else {  // Q6K
-          const int h = j >> 2, u = j & 3, sl = 2 * (u >> 1);
-          const uint4 *qw = reinterpret_cast<const uint4 *>(im + j * 64);
-          const uint4 A0 = qw[0], A1 = qw[1], B0 = qw[2], B1 = qw[3];  // (A,B) word pairs, halves 0/1
-          const uint32_t qA_lo[4] = {A0.x, A0.z, A1.x, A1.z}, qB_lo[4] = {A0.y, A0.w, A1.y, A1.w};
-          const uint32_t qA_hi[4] = {B0.x, B0.z, B1.x, B1.z}, qB_hi[4] = {B0.y, B0.w, B1.y, B1.w};
-          uint4 ql[R], qh[R];
-          int sc_lo[R], sc_hi[R];
-          uint32_t dbits[R];
-#pragma unroll
-          for (int r = 0; r < R; r++) {
-            ql[r] = ldg_stream(Wr[r] + bb * 128 + 16 * j);
-            qh[r] = ldg_stream(Wr[r] + (size_t)P.nb * 128 + bb * 64 + 16 * (2 * h + (u & 1)));
-            const int8_t *scp = reinterpret_cast<const int8_t *>(Wr[r] + (size_t)P.nb * 192 + bb * 16);
-            sc_lo[r] = __ldg(scp + 8 * h + u);
-            sc_hi[r] = __ldg(scp + 8 * h + 4 + u);
-            dbits[r] = __ldg(reinterpret_cast<const unsigned short *>(Wr[r] + (size_t)P.nb * 208 + bb * 2));
-          }
-#pragma unroll
-          for (int r = 0; r < R; r++) {
-            const uint32_t wl[4] = {ql[r].x, ql[r].y, ql[r].z, ql[r].w};
-            const uint32_t wh[4] = {qh[r].x, qh[r].y, qh[r].z, qh[r].w};
-            int P4[8];
-#pragma unroll
-            for (int t = 0; t < 4; t++) {
-              const uint32_t lo = q6_a4_lo(wl[t], wh[t], sl), hi = q6_a4_hi(wl[t], wh[t], sl);
-              P4[2 * t] = sc_lo[r] * dp4a_ss(lo, qA_lo[t], 0) + sc_hi[r] * dp4a_ss(hi, qA_hi[t], 0);
-              P4[2 * t + 1] = sc_lo[r] * dp4a_ss(lo, qB_lo[t], 0) + sc_hi[r] * dp4a_ss(hi, qB_hi[t], 0);
-            }
-            // reduce-scatter over the 8 lanes: lane j ends with class k = j
-            const bool b2 = (j >> 2) & 1, b1 = (j >> 1) & 1, b0 = j & 1;
-            int v4[4];
-#pragma unroll
-            for (int i = 0; i < 4; i++) {
-              const int keepv = b2 ? P4[4 + i] : P4[i];
-              const int sendv = b2 ? P4[i] : P4[4 + i];
-              v4[i] = keepv + __shfl_xor_sync(0xffffffffu, sendv, 4);
-            }
-            int v2[2];
-#pragma unroll
-            for (int i = 0; i < 2; i++) {
-              const int keepv = b1 ? v4[2 + i] : v4[i];
-              const int sendv = b1 ? v4[i] : v4[2 + i];
-              v2[i] = keepv + __shfl_xor_sync(0xffffffffu, sendv, 2);
-            }
-            const int keepv = b0 ? v2[1] : v2[0];
-            const int sendv = b0 ? v2[0] : v2[1];
-            const int sumi = (keepv + __shfl_xor_sync(0xffffffffu, sendv, 1)) >> 2;
-            const float d = __fmul_rn(xd, h2f_bits(dbits[r]));
-            tk[r] = __fmul_rn(d, (float)sumi);
-            tm[r] = 0.0f;
-          }
-        }
-        // sequential per-block epilogue, blocks 4*st .. 4*st+3 in order
-#pragma unroll
-        for (int sp = 0; sp < 4; sp++) {
-          const bool ok = 4 * st + sp < P.nb;
-#pragma unroll
-          for (int r = 0; r < R; r++) {
-            const float a = __shfl_sync(0xffffffffu, tk[r], 8 * sp + j);
-            const float m = __shfl_sync(0xffffffffu, tm[r], 8 * sp + j);
-            if (ok) {
-              sums[r] = __fadd_rn(sums[r], a);
-              if (FMT == Q4K) sumf[r] = __fsub_rn(sumf[r], m);
-            }
-          }
-        }
-        (void)valid;
-      }
-      // s = sumf + sums[0] + ... + sums[7] (Q6_K: sumf = 0)
-#pragma unroll
-      for (int r = 0; r < R; r++) {
-        float acc = sumf[r];
-#pragma unroll
-        for (int k = 0; k < 8; k++) {
-          int src;
-          if (FMT == Q4K) src = ((k >> 2) & 1) + 4 * ((k >> 1) & 1) + 2 * (k & 1);
-          else src = k;
-          acc = __fadd_rn(acc, __shfl_sync(0xffffffffu, sums[r], src));
-        }
-        const int row = row0 + r;
-        if (row < P.rows) {
-          if (lane == 0 && P.y) P.y[row] = acc;
-          if (ARGMAX) {
-            const unsigned long long k = argmax_key(acc, row);
-            best = k > best ? k : best;
+            const unsigned long long kk = argmax_key(acc, row);
+            best = kk > best ? kk : best;
           }
         }
       }
@@ -564,12 +598,16 @@ __global__ void __launch_bounds__(kThreads) gemv_kernel(Params P) {
   }
 
   if constexpr (ARGMAX) {
-    __shared__ unsigned long long cta_best[kThreads / 32];
+    __shared__ unsigned long long cta_best[kConsumerWarps];
+    for (int o = 16; o; o >>= 1) {
+      const unsigned long long other = __shfl_xor_sync(0xffffffffu, best, o);
+      best = other > best ? other : best;
+    }
     if (lane == 0) cta_best[warp] = best;
-    __syncthreads();
+    named_bar_sync(1, kConsumers);
     if (threadIdx.x == 0) {
       unsigned long long b = cta_best[0];
-      for (int i = 1; i < kThreads / 32; i++) b = cta_best[i] > b ? cta_best[i] : b;
+      for (int i = 1; i < kConsumerWarps; i++) b = cta_best[i] > b ? cta_best[i] : b;
       atomicMax(P.key, b);
       __threadfence();
       const unsigned prev = atomicAdd(P.done, 1u);
@@ -587,20 +625,16 @@ __global__ void __launch_bounds__(kThreads) gemv_kernel(Params P) {
 // Plain f32 weights (gemv_quant's F32 case): one warp per row, f32 FMA.
 __global__ void __launch_bounds__(kThreads) gemv_f32_kernel(const uint8_t *__restrict__ W, size_t stride,
                                                             int dim_in, int rows, const float *__restrict__ x,
-                                                            float *__restrict__ y,
-                                                            unsigned long long *key, unsigned *done,
-                                                            uint32_t *token) {
+                                                            float *__restrict__ y, unsigned long long *key,
+                                                            unsigned *done, uint32_t *token) {
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   const int gw = blockIdx.x * (kThreads / 32) + warp, nw = gridDim.x * (kThreads / 32);
   unsigned long long best = 0ull;
-  if (key && blockIdx.x == 0 && threadIdx.x == 0) {
-    // reset is done by the host memset before launch
-  }
   for (int row = gw; row < rows; row += nw) {
     const float *wr = reinterpret_cast<const float *>(W + (size_t)row * stride);
     float acc = 0.0f;
     for (int i = lane; i < dim_in; i += 32) acc = fmaf(wr[i], x[i], acc);
-    acc = warp_sum(acc);
+    for (int o = 16; o; o >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, o);
     if (lane == 0 && y) y[row] = acc;
     if (key) {
       const unsigned long long k = argmax_key(acc, row);
@@ -634,11 +668,7 @@ using GemvFn = void (*)(Params);
 
 template <int FMT, int MODE, bool AM>
 GemvFn pick_r(int R) {
-  switch (R) {
-    case 1: return gemv_kernel<FMT, MODE, 1, AM>;
-    case 2: return gemv_kernel<FMT, MODE, 2, AM>;
-    default: return gemv_kernel<FMT, MODE, 4, AM>;
-  }
+  return R == 1 ? gemv_kernel<FMT, MODE, 1, AM> : gemv_kernel<FMT, MODE, 2, AM>;
 }
 
 template <bool AM>
@@ -652,29 +682,26 @@ GemvFn pick(int fmt, int mode, int R) {
   return pick_r<Q6K, MODE_Q8K, AM>(R);
 }
 
-int choose_r(int rows) {
-  if (rows >= 32768) return 4;
-  if (rows >= 8192) return 2;
-  return 1;
-}
-
-struct OccKey {
-  GemvFn fn;
-  int smem;
-  bool operator==(const OccKey &o) const { return fn == o.fn && smem == o.smem; }
-};
-
-int blocks_per_sm(GemvFn fn, int smem) {
+int max_smem_optin(int device) {
   static std::mutex mu;
-  static std::vector<std::pair<OccKey, int>> cache;
+  static std::vector<std::pair<int, int>> cache;
   std::lock_guard<std::mutex> lk(mu);
   for (auto &e : cache)
-    if (e.first == OccKey{fn, smem}) return e.second;
-  if (smem > 48 * 1024) cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
-  int n = 0;
-  if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, fn, kThreads, smem) != cudaSuccess || n < 1) n = 1;
-  cache.push_back({OccKey{fn, smem}, n});
-  return n;
+    if (e.first == device) return e.second;
+  int v = 0;
+  cudaDeviceGetAttribute(&v, cudaDevAttrMaxSharedMemoryPerBlockOptin, device);
+  cache.push_back({device, v});
+  return v;
+}
+
+void ensure_smem_attr(GemvFn fn, int smem) {
+  static std::mutex mu;
+  static std::vector<std::pair<GemvFn, int>> done;
+  std::lock_guard<std::mutex> lk(mu);
+  for (auto &e : done)
+    if (e.first == fn && e.second >= smem) return;
+  cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+  done.push_back({fn, smem});
 }
 
 }  // namespace
@@ -701,11 +728,10 @@ int32_t gemv_launch(unltd_ctx ctx, const GemvArgs &a) {
 
   const int fmt = w.dtype, mode = a.mode;
   const int nspans = fmt == Q8_0 ? (int)((w.nb + 7) / 8) : (int)w.nb;
+  const int nbu = nspans;
   const int istr = img_stride(fmt, mode);
-  const size_t img_bytes = (size_t)nspans * istr;
-  if (img_bytes > 200 * 1024)
-    return set_error(UNLTD_ERR_UNSUPPORTED, "gemv: dim_in too large for the shared-memory x image (max 61440 for F32X)");
-  if (ctx->scratch_bytes < img_bytes) {
+  const int img_bytes = nspans * istr;
+  if (ctx->scratch_bytes < (size_t)img_bytes) {
     if (ctx->scratch) cudaFree(ctx->scratch);
     ctx->scratch = nullptr;
     ctx->scratch_bytes = 0;
@@ -713,6 +739,30 @@ int32_t gemv_launch(unltd_ctx ctx, const GemvArgs &a) {
     if (e != cudaSuccess) return cuda_error(e, "scratch alloc");
     ctx->scratch_bytes = img_bytes;
   }
+
+  // ---- tiling: rows per tile T, stages S, shared-memory plan ----
+  const int rows = (int)w.dim_out;
+  const int stride = (int)w.row_stride;
+  const int smem_max = max_smem_optin(ctx->device) - 1024;
+  const int rs = mode == MODE_F32X ? (nbu | 1) : 8 * (nbu | 1);  // floats per chain row
+  auto cbuf_for = [&](int T) {
+    int f = mode == MODE_F32X ? T * rs : T * rs + T * (rs / 8);
+    return (int)round_up((size_t)f * 4, 128);
+  };
+  int R = 2, T = 0, S = 0, stage_bytes = 0, cbuf = 0;
+  for (int target = 32 * 1024; target >= 4 * 1024 && S < 2; target /= 2) {
+    T = std::max(1, std::min(32, target / stride));
+    R = T >= 2 ? 2 : 1;
+    T = std::max(R, T / R * R);
+    stage_bytes = (int)round_up((size_t)T * stride, 128);
+    cbuf = cbuf_for(T);
+    const int fixed = kBarBytes + img_bytes + 2 * cbuf;
+    S = std::min(kMaxStages, (smem_max - fixed) / stage_bytes);
+  }
+  if (S < 2)
+    return set_error(UNLTD_ERR_UNSUPPORTED, "gemv: row too long for the shared-memory pipeline (dim_in too large)");
+  const int smem = kBarBytes + img_bytes + 2 * cbuf + S * stage_bytes;
+  const int grid = std::max(1, std::min(ctx->num_sms, (rows + T - 1) / T));
 
   // 1) prep
   unsigned long long *key = am ? a.argmax_key : nullptr;
@@ -730,29 +780,31 @@ int32_t gemv_launch(unltd_ctx ctx, const GemvArgs &a) {
   ctx->launches += 1;
 
   // 2) gemv, programmatic dependent launch
-  const int rows = (int)w.dim_out;
-  const int R = choose_r(rows);
   GemvFn fn = am ? pick<true>(fmt, mode, R) : pick<false>(fmt, mode, R);
-  const int smem = (int)img_bytes;
-  const int bps = blocks_per_sm(fn, smem);
-  const int tasks = (rows + R - 1) / R;
-  const int grid = std::max(1, std::min((tasks + 7) / 8, ctx->num_sms * bps));
+  ensure_smem_attr(fn, smem);
 
   Params P;
   P.W = w.dev;
   P.stride = w.row_stride;
   P.nb = (int)w.nb;
-  P.nspans = nspans;
+  P.nbu = nbu;
   P.rows = rows;
   P.img = ctx->scratch;
+  P.img_bytes = img_bytes;
   P.y = a.y;
   P.key = a.argmax_key;
   P.done = a.argmax_done;
   P.token = a.token;
+  P.err = ctx->err;
+  P.T = T;
+  P.S = S;
+  P.stage_bytes = stage_bytes;
+  P.rs = rs;
+  P.cbuf_bytes = cbuf;
 
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(grid);
-  cfg.blockDim = dim3(kThreads);
+  cfg.blockDim = dim3(kGemvThreads);
   cfg.dynamicSmemBytes = smem;
   cfg.stream = st;
   cudaLaunchAttribute attr[1];

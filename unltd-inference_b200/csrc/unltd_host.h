@@ -21,6 +21,8 @@ struct unltd_ctx_s {
   // Argmax reduction state: a 64-bit key and a CTA-completion counter.
   unsigned long long *argmax_key = nullptr;
   unsigned int *argmax_done = nullptr;
+  // Device error word: kernels write a nonzero code on a bounded-wait timeout.
+  int *err = nullptr;
   std::atomic<int64_t> launches{0};
   void *comm = nullptr;  // ncclComm_t once unltd_comm_init ran
 };
@@ -40,6 +42,7 @@ namespace unltd {
 // Thread-local error message behind unltd_last_error().
 int32_t set_error(int32_t status, const std::string &msg);
 int32_t cuda_error(cudaError_t e, const char *what);
+int32_t check_device_error(unltd_ctx c, const char *who);
 
 // weights.cu
 cudaError_t launch_repack(const unltd_weight_s &w, const uint8_t *raw_dev, size_t row0_local,

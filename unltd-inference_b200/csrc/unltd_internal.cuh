@@ -56,13 +56,17 @@ __host__ __device__ inline int img_stride(int dtype, int mode) {
   return mode == MODE_F32X ? kImgF32X : (dtype == Q4K ? kImgQ8K4 : kImgQ8K6);
 }
 
-// Element e (0..255) of a span -> byte index in the lane-ordered 256-byte
-// plane of an x image, and the same permutation of the weights.
+// Element e (0..255) of a span -> byte index in a lane-ordered 256-byte
+// plane of an x image. Lane j of an 8-lane subgroup reads its low-nibble
+// (or first-half) words at 16j and its high-nibble words at 128 + 16j, so
+// the eight lanes of a quarter-warp touch 128 contiguous bytes (no bank
+// conflicts). The same in-word order as the weights' permutation:
 //  Q4_K: p = e/64 (qs segment), half = (e%64)/32 (low/high nibble group),
-//        r = e%32, k = r%8, i = r/8   ->  64p + 32*half + 4k + i
+//        r = e%32, k = r%8, i = r/8, lane j = 2p + k/4
+//        -> 128*half + 32p + 4k + i
 __host__ __device__ inline int q4_xpos(int e) {
   int p = e >> 6, half = (e >> 5) & 1, r = e & 31;
-  return 64 * p + 32 * half + 4 * (r & 7) + (r >> 3);
+  return 128 * half + 32 * p + 4 * (r & 7) + (r >> 3);
 }
 // In-chunk position of run position ipos (0..15) for Q6_K: word t holds run
 // positions (2t, 2t+8, 2t+1, 2t+9), i.e. Q8_K lane classes 2t and 2t+1.
@@ -70,10 +74,22 @@ __host__ __device__ inline int q6_pic(int ipos) {
   return 4 * ((ipos & 7) >> 1) + 2 * (ipos & 1) + (ipos >> 3);
 }
 //  Q6_K: h = e/128, pos = e%128, hi = pos/64, c = pos%64, u = c/16,
-//        lane j = 4h + u  ->  32j + 16*hi + pic(c%16)
+//        lane j = 4h + u  ->  128*hi + 16j + pic(c%16)
 __host__ __device__ inline int q6_xpos(int e) {
   int h = e >> 7, pos = e & 127, hi = pos >> 6, c = pos & 63, u = c >> 4;
-  return 32 * (4 * h + u) + 16 * hi + q6_pic(c & 15);
+  return 128 * hi + 16 * (4 * h + u) + q6_pic(c & 15);
+}
+//  Q8_0 (a span is 8 blocks of 32): lane j = e/32 owns block j; its first 16
+//  elements at 16j, the next 16 at 128 + 16j.
+__host__ __device__ inline int q80_xpos(int e) {
+  return 128 * ((e >> 4) & 1) + 16 * (e >> 5) + (e & 15);
+}
+// Q8K image of Q6_K: lane j's four 16-byte chunks q = 0..3 at 128q + 16j.
+// Chunk q = 2*hh + (w >> 1) holds, for half hh and words w, w+1 of the lane,
+// the masked q8 words (A: run positions 2w, 2w+8 in bytes 0,1; B: 2w+1,
+// 2w+9 in bytes 2,3) as A_w, B_w, A_{w+1}, B_{w+1}.
+__host__ __device__ inline int q6_q8k_byte(int j, int hh, int w, int ab, int bpos) {
+  return 128 * (2 * hh + (w >> 1)) + 16 * j + 4 * (2 * (w & 1) + ab) + bpos;
 }
 
 __host__ __device__ inline size_t round_up(size_t v, size_t a) { return (v + a - 1) / a * a; }
@@ -125,6 +141,74 @@ __device__ __forceinline__ float h2f_bits(uint32_t bits16) {
 
 __device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
 __device__ __forceinline__ void pdl_trigger() { asm volatile("griddepcontrol.launch_dependents;"); }
+
+// ---- mbarrier + bulk-copy (TMA, non-tensor) helpers ----------------------
+__device__ __forceinline__ uint32_t smem_u32(const void *p) {
+  return (uint32_t)__cvta_generic_to_shared(p);
+}
+__device__ __forceinline__ void mbar_init(uint64_t *bar, uint32_t count) {
+  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(bar)), "r"(count) : "memory");
+}
+__device__ __forceinline__ void fence_mbar_init() {
+  asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+}
+__device__ __forceinline__ void mbar_expect_tx(uint64_t *bar, uint32_t bytes) {
+  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(bar)), "r"(bytes)
+               : "memory");
+}
+__device__ __forceinline__ void mbar_arrive(uint64_t *bar) {
+  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
+}
+__device__ __forceinline__ bool mbar_try_wait(uint64_t *bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n selp.u32 %0, 1, 0, p;\n}"
+      : "=r"(ok)
+      : "r"(smem_u32(bar)), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+__device__ __forceinline__ uint64_t global_ns() {
+  uint64_t t;
+  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+  return t;
+}
+// Wait for the phase of `parity` to complete, for at most ~2 s of wall time;
+// on timeout record code 1 in *err and return false (never spins forever).
+__device__ __forceinline__ bool mbar_wait_bounded(uint64_t *bar, uint32_t parity, int *err) {
+  if (mbar_try_wait(bar, parity)) return true;
+  const uint64_t t0 = global_ns();
+  for (uint32_t it = 1;; ++it) {
+    if (mbar_try_wait(bar, parity)) return true;
+    if ((it & 255u) == 0 && global_ns() - t0 > 2000000000ull) {
+      atomicExch(err, 1);
+      return false;
+    }
+  }
+}
+// 1-D bulk copy global -> shared, completing `bytes` of transaction on `bar`.
+// Addresses 16-byte aligned, bytes a multiple of 16.
+__device__ __forceinline__ void bulk_g2s(void *dst, const void *src, uint32_t bytes, uint64_t *bar) {
+  asm volatile(
+      "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+          smem_u32(dst)),
+      "l"(src), "r"(bytes), "r"(smem_u32(bar))
+      : "memory");
+}
+__device__ __forceinline__ void named_bar_sync(int id, int nthreads) {
+  asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(nthreads) : "memory");
+}
+
+// bar.red.and over a named barrier: true iff `pred` holds in every participant.
+__device__ __forceinline__ bool named_bar_red_and(int id, int nthreads, bool pred) {
+  uint32_t r;
+  asm volatile(
+      "{\n .reg .pred p, q;\n setp.ne.u32 p, %1, 0;\n bar.red.and.pred q, %2, %3, p;\n selp.u32 %0, 1, 0, q;\n}"
+      : "=r"(r)
+      : "r"((uint32_t)pred), "r"(id), "r"(nthreads)
+      : "memory");
+  return r != 0;
+}
 
 // f32 -> order-preserving u32 (larger float -> larger key).
 __device__ __forceinline__ uint32_t orderable(float v) {

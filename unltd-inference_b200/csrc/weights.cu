@@ -112,7 +112,9 @@ __global__ void dequant_q6k(const uint8_t *__restrict__ dev, float *__restrict__
   int sc = (int8_t)row[nb * 192 + b * 16 + (el >> 4)];
   const uint8_t *dp = row + nb * 208 + b * 2;
   float d = h2f_bits(dp[0] | (dp[1] << 8));
-  out[t] = __fmul_rn(d, (float)(sc * q));
+  // f32 product, not an integer one: keeps the sign of a zero weight
+  // (a negative scale times q = 0 is -0.0 in the reference's f64 decode).
+  out[t] = __fmul_rn(d, __fmul_rn((float)sc, (float)q));
 }
 
 __global__ void dequant_q80(const uint8_t *__restrict__ dev, float *__restrict__ out, size_t rows,
