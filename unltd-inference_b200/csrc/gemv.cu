@@ -41,7 +41,7 @@ namespace unltd {
 namespace {
 
 constexpr int kThreads = 256;  // prep kernels
-constexpr int kConsumerWarps = 8;
+constexpr int kConsumerWarps = 16;
 constexpr int kConsumers = kConsumerWarps * 32;
 constexpr int kGemvThreads = kConsumers + 32;  // + one producer warp
 constexpr int kMaxStages = 8;
@@ -523,23 +523,27 @@ __global__ void __launch_bounds__(kGemvThreads, 1) gemv_kernel(Params P) {
 
   const int s_in = lane >> 3, j = lane & 7;
   const unsigned subm = 0xFFu << (lane & 24);
-  const int sg = warp * 4 + s_in;  // subgroup id 0..31
+  const int sg = warp * 4 + s_in;  // subgroup id
+  constexpr int kSubgroups = kConsumerWarps * 4;
   unsigned long long best = 0ull;
   const int istr = MODE == MODE_F32X ? kImgF32X : (FMT == Q4K ? kImgQ8K4 : kImgQ8K6);
 
+  // One named barrier per tile, between the phases. The chain phase of tile i
+  // (a few warps) overlaps the integer phase of tile i+1 (the others); the
+  // two chain buffers alternate, and barrier i+1 orders chain(i) before
+  // anyone writes that buffer again at tile i+2.
   for (int i = 0; i < ntiles; i++) {
     const int s = i % P.S;
     const int r0 = rb + i * P.T;
     const int nr = min(P.T, re - r0);
     const bool got = mbar_wait_bounded(&full[s], (i / P.S) & 1, P.err);
-    if (!named_bar_red_and(1, kConsumers, got)) break;  // uniform: every consumer leaves together
     const uint8_t *tile = stages + (size_t)s * P.stage_bytes;
     float *cb = reinterpret_cast<float *>(reinterpret_cast<uint8_t *>(cbuf0) + (i & 1) * P.cbuf_bytes);
 
     // integer phase
     const int ngroups = (nr + R - 1) / R;
-    const int nitems = ngroups * P.nbu;
-    for (int it = sg; it < nitems; it += 32) {
+    const int nitems = got ? ngroups * P.nbu : 0;
+    for (int it = sg; it < nitems; it += kSubgroups) {
       const int g = it / P.nbu, b = it - g * P.nbu;
       const uint8_t *rowp[R];
       bool rv[R];
@@ -555,15 +559,22 @@ __global__ void __launch_bounds__(kGemvThreads, 1) gemv_kernel(Params P) {
     }
     __syncwarp();
     if (lane == 0) mbar_arrive(&empty[s]);  // this warp is done with the weight stage
-    named_bar_sync(1, kConsumers);
+    // uniform exit if any consumer timed out waiting for this tile
+    if (!named_bar_red_and(1, kConsumers, got)) break;
 
-    // chain phase
+    // chain phase: loads hoisted ahead of the dependent adds, 8 at a time
     if constexpr (MODE == MODE_F32X) {
       const int t = threadIdx.x;
       if (t < nr) {
         const float *fr = cb + t * P.rs;
         float v = 0.0f;
-        for (int b = 0; b < P.nbu; b++) v += fr[b];
+        for (int b = 0; b < P.nbu; b += 8) {
+          float f[8];
+#pragma unroll
+          for (int q = 0; q < 8; q++) f[q] = b + q < P.nbu ? fr[b + q] : 0.0f;
+#pragma unroll
+          for (int q = 0; q < 8; q++) v += f[q];
+        }
         const int row = r0 + t;
         if (P.y) P.y[row] = v;
         if (ARGMAX) {
@@ -577,9 +588,21 @@ __global__ void __launch_bounds__(kGemvThreads, 1) gemv_kernel(Params P) {
         const float *tk = cb + lr * P.rs + k;
         const float *tm = cb + P.T * P.rs + lr * (P.rs / 8);
         float sums = 0.0f, sumf = 0.0f;
-        for (int b = 0; b < P.nbu; b++) {
-          sums = __fadd_rn(sums, tk[8 * b]);
-          if (FMT == Q4K) sumf = __fsub_rn(sumf, tm[b]);
+        for (int b = 0; b < P.nbu; b += 8) {
+          float a[8], mm[8];
+#pragma unroll
+          for (int q = 0; q < 8; q++) {
+            const bool in = b + q < P.nbu;
+            a[q] = in ? tk[8 * (b + q)] : 0.0f;
+            if (FMT == Q4K) mm[q] = in ? tm[b + q] : 0.0f;
+          }
+#pragma unroll
+          for (int q = 0; q < 8; q++) {
+            if (b + q < P.nbu) {
+              sums = __fadd_rn(sums, a[q]);
+              if (FMT == Q4K) sumf = __fsub_rn(sumf, mm[q]);
+            }
+          }
         }
         const unsigned gm = 0xFFu << (lane & 24);
         float acc = sumf;  // Q6_K: sumf = 0, s = 0 + sums[0] + ...
@@ -749,15 +772,32 @@ int32_t gemv_launch(unltd_ctx ctx, const GemvArgs &a) {
     int f = mode == MODE_F32X ? T * rs : T * rs + T * (rs / 8);
     return (int)round_up((size_t)f * 4, 128);
   };
-  int R = 2, T = 0, S = 0, stage_bytes = 0, cbuf = 0;
-  for (int target = 32 * 1024; target >= 4 * 1024 && S < 2; target /= 2) {
-    T = std::max(1, std::min(32, target / stride));
-    R = T >= 2 ? 2 : 1;
-    T = std::max(R, T / R * R);
-    stage_bytes = (int)round_up((size_t)T * stride, 128);
-    cbuf = cbuf_for(T);
-    const int fixed = kBarBytes + img_bytes + 2 * cbuf;
-    S = std::min(kMaxStages, (smem_max - fixed) / stage_bytes);
+  // Pick rows per tile T: stages of at most 56 KB, at least 2 (preferably 3+)
+  // stages in flight, and (T/R) * nbu items a multiple of the 64 subgroups so
+  // the integer phase is balanced; then the largest such T.
+  int R = 1, T = 0, S = 0, stage_bytes = 0, cbuf = 0;
+  double best_score = -1.0;
+  const int nsub = kConsumerWarps * 4;
+  for (int t = 1; t <= 32; t++) {
+    const int r = t >= 2 ? 2 : 1;
+    if (t % r) continue;
+    const int sb = (int)round_up((size_t)t * stride, 128);
+    if (sb > 56 * 1024 && t > 1) continue;
+    const int cb = cbuf_for(t);
+    const int fixed = kBarBytes + img_bytes + 2 * cb;
+    const int s = std::min(kMaxStages, (smem_max - fixed) / sb);
+    if (s < 2) continue;
+    const int items = (t / r) * nbu;
+    const double score = (s >= 3 ? 4.0 : 0.0) + (items % nsub == 0 ? 2.0 : 0.0) + (items >= nsub ? 1.0 : 0.0) +
+                         t / 64.0;
+    if (score > best_score) {
+      best_score = score;
+      T = t;
+      R = r;
+      S = s;
+      stage_bytes = sb;
+      cbuf = cb;
+    }
   }
   if (S < 2)
     return set_error(UNLTD_ERR_UNSUPPORTED, "gemv: row too long for the shared-memory pipeline (dim_in too large)");
