@@ -134,6 +134,19 @@ int32_t unltd_gemv_argmax(unltd_ctx ctx, unltd_weight w, const float *x_dev, flo
  * values of dot_q6_k (quants.rs:171-200) and of the Q8_0 format. */
 int32_t unltd_dequant(unltd_ctx ctx, unltd_weight w, float *out_dev);
 
+/* Same result as unltd_gemv (no counterpart in the reference), for callers
+ * that cannot allocate GPU memory: code inside an allocator or memory pool,
+ * hosts that reserve all device memory up front, or code that must not hit
+ * the implicit synchronisation of cudaMalloc/cudaFree. Its scratch is a
+ * fixed 64 KiB device array inside the library (held on every GPU that loads
+ * the library until exit), so a call allocates nothing. Limits: dim_in <=
+ * 16384 (larger is rejected with UNLTD_ERR_UNSUPPORTED); Q4_K, Q6_K, Q8_0.
+ * All calls on a device share the array: calls whose kernels overlap on the
+ * GPU race; order them on one stream. `stream` is a cudaStream_t (NULL = the
+ * legacy default stream). The first call on a device sets up that device
+ * (symbol address, kernel attributes); make it before any stream capture. */
+int32_t unltd_gemv_noalloc(unltd_weight w, const float *x_dev, float *y_dev, int32_t mode, void *stream);
+
 /* ---- reference-signature API (host buffers, synchronous) ---------------- */
 /* quants.rs:422  pub fn gemv_quant(out, x, w, dim_in, dim_out, dtype) */
 int32_t unltd_gemv_quant(float *out, size_t out_len, const float *x, size_t x_len, const uint8_t *w,

@@ -729,6 +729,22 @@ void ensure_smem_attr(GemvFn fn, int smem) {
 
 }  // namespace
 
+// Sets the dynamic shared-memory limit of every quantized GEMV kernel to the
+// largest plan gemv_launch can choose on `device`, so later launches find
+// their attribute already set (no host-side cache growth on the hot path).
+void gemv_prewarm(int device) {
+  const int m = max_smem_optin(device) - 1024;
+  const int fmts[3] = {Q4K, Q6K, Q8_0};
+  for (int fmt : fmts)
+    for (int mode = MODE_F32X; mode <= MODE_Q8K; mode++) {
+      if (mode == MODE_Q8K && fmt == Q8_0) continue;
+      for (int r = 1; r <= 2; r++) {
+        ensure_smem_attr(pick<false>(fmt, mode, r), m);
+        ensure_smem_attr(pick<true>(fmt, mode, r), m);
+      }
+    }
+}
+
 int32_t gemv_launch(unltd_ctx ctx, const GemvArgs &a) {
   const unltd_weight_s &w = *a.w;
   cudaStream_t st = ctx->stream;

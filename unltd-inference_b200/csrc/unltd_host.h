@@ -60,5 +60,6 @@ struct GemvArgs {
   uint32_t *token;
 };
 int32_t gemv_launch(unltd_ctx ctx, const GemvArgs &a);
+void gemv_prewarm(int device);
 
 }  // namespace unltd

@@ -46,6 +46,7 @@ SIGNATURES = [
     ("unltd_gemv", _I, [_P, _P, _P, _P, _I]),
     ("unltd_gemv_argmax", _I, [_P, _P, _P, _P, _P, _I]),
     ("unltd_dequant", _I, [_P, _P, _P]),
+    ("unltd_gemv_noalloc", _I, [_P, _P, _P, _I, _P]),
     ("unltd_gemv_quant", _I, [_P, _S, _P, _S, _P, _S, _S, _S, _I]),
     ("unltd_gemv_quant_q8k", _I, [_P, _S, _P, _S, _P, _S, _S, _S, _I]),
     ("unltd_dequantize_q4_k", _I, [_P, _S, _P, _S]),
