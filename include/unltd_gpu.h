@@ -129,6 +129,15 @@ int32_t unltd_gemv(unltd_ctx ctx, unltd_weight w, const float *x_dev, float *y_d
 int32_t unltd_gemv_argmax(unltd_ctx ctx, unltd_weight w, const float *x_dev, float *logits_dev,
                           uint32_t *token_dev, int32_t mode);
 
+/* Batched prefill: Y[m][n] = sum_k X[m][k] * W[n][k] for m < m_tokens, X f32
+ * row-major [m_tokens][dim_in], Y f32 row-major [m_tokens][dim_out]. This is
+ * gemv_quant (quants.rs:422) applied to every token at once; the reference
+ * runs prefill token by token (qwen35_forward.rs:8-12, greedy.rs:55-65).
+ * Q4_K weights; tcgen05 tensor cores with bf16 operands (X and the
+ * dequantized W rounded once to bf16) and f32 accumulation, so
+ * |Y - exact| <= 2^-7 * sum_k |X W| per element. */
+int32_t unltd_gemm(unltd_ctx ctx, unltd_weight w, const float *X_dev, float *Y_dev, size_t m_tokens);
+
 /* Dequantize all rows to f32, row-major [dim_out][dim_in]. Bit-exact with
  * dequantize_q4_k (quants.rs:534-567) for Q4_K and with the exact element
  * values of dot_q6_k (quants.rs:171-200) and of the Q8_0 format. */

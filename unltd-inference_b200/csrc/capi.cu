@@ -145,6 +145,7 @@ int32_t unltd_ctx_destroy(unltd_ctx c) {
   CtxGuard g(c->device);
   cudaStreamSynchronize(c->stream);
   if (c->scratch) cudaFree(c->scratch);
+  if (c->gemm_scratch) cudaFree(c->gemm_scratch);
   if (c->argmax_key) cudaFree(c->argmax_key);
   if (c->own_stream) cudaStreamDestroy(c->own_stream);
   delete c;
@@ -273,6 +274,14 @@ int32_t unltd_gemv_argmax(unltd_ctx c, unltd_weight w, const float *x, float *lo
   CtxGuard g(c->device);
   GemvArgs a{w, x, logits, mode, c->argmax_key, c->argmax_done, token};
   return gemv_launch(c, a);
+}
+
+int32_t unltd_gemm(unltd_ctx c, unltd_weight w, const float *X, float *Y, size_t m_tokens) {
+  if (!c || !w || !X || !Y) return set_error(UNLTD_ERR_INVALID_ARG, "gemm: NULL argument");
+  if (w->ctx != c) return set_error(UNLTD_ERR_INVALID_ARG, "gemm: weight belongs to another context");
+  if (m_tokens > (size_t)1 << 24) return set_error(UNLTD_ERR_LENGTH, "gemm: m_tokens too large");
+  CtxGuard g(c->device);
+  return gemm_launch(c, *w, X, Y, m_tokens);
 }
 
 int32_t unltd_dequant(unltd_ctx c, unltd_weight w, float *out) {

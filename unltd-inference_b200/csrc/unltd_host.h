@@ -23,6 +23,9 @@ struct unltd_ctx_s {
   unsigned int *argmax_done = nullptr;
   // Device error word: kernels write a nonzero code on a bounded-wait timeout.
   int *err = nullptr;
+  // Scratch of the prefill GEMM (bf16 copy of X), grown on demand.
+  uint8_t *gemm_scratch = nullptr;
+  size_t gemm_scratch_bytes = 0;
   std::atomic<int64_t> launches{0};
   void *comm = nullptr;  // ncclComm_t once unltd_comm_init ran
 };
@@ -61,5 +64,8 @@ struct GemvArgs {
 };
 int32_t gemv_launch(unltd_ctx ctx, const GemvArgs &a);
 void gemv_prewarm(int device);
+
+// gemm_tc.cu
+int32_t gemm_launch(unltd_ctx ctx, const unltd_weight_s &w, const float *X, float *Y, size_t M);
 
 }  // namespace unltd

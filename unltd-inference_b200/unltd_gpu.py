@@ -47,6 +47,7 @@ SIGNATURES = [
     ("unltd_gemv_argmax", _I, [_P, _P, _P, _P, _P, _I]),
     ("unltd_dequant", _I, [_P, _P, _P]),
     ("unltd_gemv_noalloc", _I, [_P, _P, _P, _I, _P]),
+    ("unltd_gemm", _I, [_P, _P, _P, _P, _S]),
     ("unltd_gemv_quant", _I, [_P, _S, _P, _S, _P, _S, _S, _S, _I]),
     ("unltd_gemv_quant_q8k", _I, [_P, _S, _P, _S, _P, _S, _S, _S, _I]),
     ("unltd_dequantize_q4_k", _I, [_P, _S, _P, _S]),
@@ -148,6 +149,10 @@ class Context:
     def gemv_argmax(self, w: "Weight", x, token, logits=None, mode: int = MODE_Q8K):
         _check(lib().unltd_gemv_argmax(self.h, w.h, _ptr(x), _ptr(logits) if logits is not None else None,
                                        _ptr(token), mode))
+
+    def gemm(self, w: "Weight", X, Y, m_tokens: int):
+        """Y[m][n] = sum_k X[m][k] W[n][k] on the tensor cores (bf16 operands, f32 accumulate)."""
+        _check(lib().unltd_gemm(self.h, w.h, _ptr(X), _ptr(Y), m_tokens))
 
     def dequant(self, w: "Weight", out):
         _check(lib().unltd_dequant(self.h, w.h, _ptr(out)))
