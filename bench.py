@@ -68,6 +68,14 @@ def _peaks():
     return 6650.0, "fallback"
 
 
+def _bf16_peak():
+    p = os.path.join(REPO, "MEASURED_PEAKS.json")
+    if os.path.exists(p):
+        with open(p) as f:
+            return float(json.load(f)["bf16_tflops"]), "measured (burst)"
+    return 1590.0, "fallback"
+
+
 def _traffic():
     p = os.path.join(REPO, "profiles", "traffic.json")
     if os.path.exists(p):
@@ -234,6 +242,7 @@ def main():
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--no-gemm", action="store_true")
     ap.add_argument("--only", default=None, help="comma-separated subset of the mix (profiling)")
     ap.add_argument("--mode", default="q8k", choices=["q8k", "f32x"], help="arithmetic of the K-quant GEMVs")
     args = ap.parse_args()
@@ -382,6 +391,35 @@ def main():
         }
         ug.forget_host_weights()
 
+    # ---- batched prefill GEMM on the tensor cores ----
+    gemm = None
+    if world == 1 and args.only is None and not args.no_gemm:
+        GM, GN, GK = 512, 12288, 4096
+        gw = ctx.upload(synth.quant_weights(Q4K, GK, GN, 2024), Q4K, GK, GN)
+        GX = torch.from_numpy(synth.activations(GK, 2025, rows=GM)).cuda()
+        GY = torch.empty((GM, GN), device="cuda")
+        for _ in range(3):
+            ctx.gemm(gw, GX, GY, GM)
+        torch.cuda.synchronize()
+        g0, g1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        n_it = max(K, 10)
+        g0.record(stream)
+        for _ in range(n_it):
+            ctx.gemm(gw, GX, GY, GM)
+        g1.record(stream)
+        torch.cuda.synchronize()
+        gms = g0.elapsed_time(g1) / n_it
+        flops = 2.0 * GM * GN * GK
+        peak_tf, peak_tf_kind = _bf16_peak()
+        gemm = {
+            "workload": "config2_prefill_gemm_q4k_512x4096x12288", "ms": round(gms, 4),
+            "tflops": round(flops / (gms * 1e-3) / 1e12, 1), "peak_tflops": peak_tf, "peak_kind": peak_tf_kind,
+            "frac": round(flops / (gms * 1e-3) / 1e12 / peak_tf, 4),
+            "note": "includes the X f32->bf16 conversion kernel; bf16 operands, f32 accumulation",
+        }
+        gw.free()
+        del GX, GY
+
     peak, peak_kind = _peaks()
     step_bytes = sum(it["bytes"] for it in items)
     value = step_bytes / (ms_step * 1e-3) / 1e9
@@ -411,6 +449,7 @@ def main():
         "gpu_launches": int(launches),
         "clocks": sampler.summary(),
         "e2e": e2e,
+        "gemm_prefill": gemm,
     }
     if rank == 0 and world == 1 and not args.no_cpu_baseline and args.only is None:
         line["cpu_baseline"] = cpu_baseline()

@@ -133,9 +133,10 @@ int32_t unltd_gemv_argmax(unltd_ctx ctx, unltd_weight w, const float *x_dev, flo
  * row-major [m_tokens][dim_in], Y f32 row-major [m_tokens][dim_out]. This is
  * gemv_quant (quants.rs:422) applied to every token at once; the reference
  * runs prefill token by token (qwen35_forward.rs:8-12, greedy.rs:55-65).
- * Q4_K weights; tcgen05 tensor cores with bf16 operands (X and the
- * dequantized W rounded once to bf16) and f32 accumulation, so
- * |Y - exact| <= 2^-7 * sum_k |X W| per element. */
+ * Q4_K weights; tcgen05 tensor cores with fp16 operands (X rounded once to
+ * fp16, |X| < 65504; W = q*fp16(d*sc) - fp16(dmin*m) in one fp16 FMA) and f32
+ * accumulation: |Y - exact| <= 2^-9 * sum_k |X| (|W| + |d sc q| + |dmin m|)
+ * per element. */
 int32_t unltd_gemm(unltd_ctx ctx, unltd_weight w, const float *X_dev, float *Y_dev, size_t m_tokens);
 
 /* Dequantize all rows to f32, row-major [dim_out][dim_in]. Bit-exact with

@@ -4,21 +4,22 @@
 // prefill token by token, qwen35_forward.rs:8-12).
 //
 // Design (one CTA per SM, persistent over 256-token x 192-row output tiles):
-//  * X is converted once per call to bf16, with the columns of every
-//    64-element segment permuted exactly like the Q4_K quants of the weight
-//    repack, so the K order of A and B agree without any byte transpose.
+//  * X is converted once per call to fp16, with the columns of every
+//    64-element segment permuted to the K order in which the dequant writes
+//    the weight tile, so A and B agree without any byte transpose.
 //  * warp 0 (one thread): TMA producer. Per 64-wide K step it loads the two
-//    128x64 bf16 A tiles (SWIZZLE_128B tensor map) and, for the 192 weight
+//    128x64 fp16 A tiles (SWIZZLE_128B tensor map) and, for the 192 weight
 //    rows of the tile, the 32-byte quant segment and 16-byte block header
 //    (2-D tensor maps over the repacked rows) into a 3-stage ring.
-//  * warps 2-7 (192 threads, one per weight row): dequantize the segment to
-//    bf16, d*sc*q - dmin*m in f32 rounded once to bf16, and store it into the
+//  * warps 2-13 (384 threads, two per weight row, one per nibble group):
+//    dequantize to fp16 — nibble -> exact fp16 (the 1024 + q bias trick),
+//    then q * fp16(d*sc) - fp16(dmin*m) in one fp16 FMA — and store into the
 //    B tile in the canonical K-major SWIZZLE_128B layout.
-//  * warp 1 (one thread): issues tcgen05.mma kind::f16 (bf16 x bf16 -> f32),
+//  * warp 1 (one thread): issues tcgen05.mma kind::f16 (fp16 x fp16 -> f32),
 //    M=128 N=192 K=16, for both 128-token halves, accumulating in TMEM
 //    (columns [0,192) and [256,448)); tcgen05.commit frees each stage and,
 //    after the last step, signals the epilogue.
-//  * warps 8-11: tcgen05.ld the accumulators (32x32b) and store Y in f32.
+//  * warps 14-17: tcgen05.ld the accumulators (32x32b) and store Y in f32.
 // Every mbarrier wait is bounded (2 s) and records a timeout in the context
 // error word; on any timeout all roles leave their loops, in-flight copies and
 // MMAs are waited for (bounded), and TMEM is freed before the CTA exits.
@@ -40,8 +41,8 @@ constexpr int kTileM = 256;   // tokens per tile (two MMAs of M = 128)
 constexpr int kTileN = 192;   // weight rows per tile (MMA N)
 constexpr int kStepK = 64;    // K per stage: one Q4_K quant segment
 constexpr int kStages = 3;
-constexpr int kThreadsG = 384;
-constexpr int kDequantWarps = 6;  // warps 2..7, one thread per weight row
+constexpr int kDequantWarps = 12;  // warps 2..13: two threads per weight row
+constexpr int kThreadsG = (2 + kDequantWarps + 4) * 32;  // + producer, MMA, 4 epilogue warps
 constexpr uint32_t kABytes = 2 * 128 * kStepK * 2;          // 32 KB
 constexpr uint32_t kBBytes = kTileN * kStepK * 2;            // 24 KB
 constexpr uint32_t kWqBytes = kTileN * 32;                   // 6 KB
@@ -63,7 +64,7 @@ __device__ __forceinline__ void tmem_relinquish() {
 __device__ __forceinline__ void tmem_dealloc(uint32_t taddr, uint32_t ncols) {
   asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(taddr), "r"(ncols) : "memory");
 }
-__device__ __forceinline__ void umma_bf16(uint32_t d_tmem, uint64_t adesc, uint64_t bdesc, uint32_t idesc,
+__device__ __forceinline__ void umma_f16(uint32_t d_tmem, uint64_t adesc, uint64_t bdesc, uint32_t idesc,
                                           uint32_t accumulate) {
   asm volatile(
       "{\n .reg .pred p;\n setp.ne.b32 p, %4, 0;\n"
@@ -111,8 +112,8 @@ __device__ __forceinline__ uint64_t sw128_desc(uint32_t saddr) {
   return d;
 }
 
-// Instruction descriptor: D f32, A/B bf16, both K-major, M=128, N=kTileN.
-constexpr uint32_t kIdesc = (1u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(kTileN >> 3) << 17) |
+// Instruction descriptor: D f32, A/B f16, both K-major, M=128, N=kTileN.
+constexpr uint32_t kIdesc = (1u << 4) | (0u << 7) | (0u << 10) | ((uint32_t)(kTileN >> 3) << 17) |
                             ((uint32_t)(128 >> 4) << 24);
 
 struct GemmParams {
@@ -209,7 +210,7 @@ __global__ void __launch_bounds__(kThreadsG, 1)
           for (int h = 0; h < 2; h++)
 #pragma unroll
             for (int kk = 0; kk < kStepK / 16; kk++)
-              umma_bf16(tbase + (uint32_t)(h * 256), sw128_desc(a0 + h * (kABytes / 2) + kk * 32),
+              umma_f16(tbase + (uint32_t)(h * 256), sw128_desc(a0 + h * (kABytes / 2) + kk * 32),
                         sw128_desc(b0 + kk * 32), kIdesc, (ks > 0 || kk > 0) ? 1u : 0u);
           umma_commit(&empty[s]);
           last = &empty[s];
@@ -224,8 +225,11 @@ __global__ void __launch_bounds__(kThreadsG, 1)
       if (last) mbar_wait_bounded(last, last_par, P.err);  // MMAs retired before TMEM is freed
     }
   } else if (warp < 2 + kDequantWarps) {
-    // ---------------- dequantize Q4_K -> bf16 B tile ----------------
-    const int r = threadIdx.x - 64;  // weight row within the tile, 0..191
+    // ---------------- dequantize Q4_K -> fp16 B tile ----------------
+    // Thread (r, hf): weight row r of the tile, nibble half hf (group 2p or
+    // 2p+1 of the current 64-element segment p).
+    const int dt = threadIdx.x - 64;
+    const int r = dt % kTileN, hf = dt / kTileN;
     long g = 0;
     bool ok = true;
     for (int t = blockIdx.x; t < P.ntiles && ok; t += gridDim.x) {
@@ -235,8 +239,12 @@ __global__ void __launch_bounds__(kThreadsG, 1)
         ok = mbar_wait_bounded(&full[s], par, P.err);
         if (ok) {
           const uint4 hq = *reinterpret_cast<const uint4 *>(stWh(s) + r * 16);
-          const uint4 q0 = *reinterpret_cast<const uint4 *>(stWq(s) + r * 32);
-          const uint4 q1 = *reinterpret_cast<const uint4 *>(stWq(s) + r * 32 + 16);
+          // the two 16-byte halves of the row's 32 quant bytes, read in an
+          // order that keeps the 8 lanes of each quarter-warp on distinct banks
+          const int f = (r >> 2) & 1;
+          const uint4 qa = *reinterpret_cast<const uint4 *>(stWq(s) + r * 32 + 16 * f);
+          const uint4 qb = *reinterpret_cast<const uint4 *>(stWq(s) + r * 32 + 16 * (1 - f));
+          const uint4 q0 = f ? qb : qa, q1 = f ? qa : qb;
           const int p = ks & 3;
           uint32_t SC, MM;
           if (p < 2) {
@@ -246,33 +254,30 @@ __global__ void __launch_bounds__(kThreadsG, 1)
             SC = (hq.w & 0x0F0F0F0Fu) | ((hq.y >> 2) & 0x30303030u);
             MM = ((hq.w >> 4) & 0x0F0F0F0Fu) | ((hq.z >> 2) & 0x30303030u);
           }
-          const int sh = (p & 1) * 16;
+          const int sh = (p & 1) * 16 + hf * 8;
           const float d = h2f_bits(hq.x & 0xFFFFu), dmin = h2f_bits(hq.x >> 16);
-          const float d1[2] = {__fmul_rn(d, (float)((SC >> sh) & 0xFF)), __fmul_rn(d, (float)((SC >> (sh + 8)) & 0xFF))};
-          const float m1[2] = {__fmul_rn(dmin, (float)((MM >> sh) & 0xFF)),
-                               __fmul_rn(dmin, (float)((MM >> (sh + 8)) & 0xFF))};
+          const __half2 d1 = __float2half2_rn(__fmul_rn(d, (float)((SC >> sh) & 0xFF)));
+          const __half2 nm1 = __float2half2_rn(-__fmul_rn(dmin, (float)((MM >> sh) & 0xFF)));
+          const __half2 k1024 = __float2half2_rn(1024.0f);
           const uint32_t w[8] = {q0.x, q0.y, q0.z, q0.w, q1.x, q1.y, q1.z, q1.w};
           uint8_t *brow = stB(s) + (r >> 3) * 1024 + (r & 7) * 128;
 #pragma unroll
-          for (int c = 0; c < 8; c++) {
-            const int half = c >> 2;  // 0: low nibbles (group 2p), 1: high nibbles (group 2p+1)
+          for (int c = 0; c < 4; c++) {
             uint32_t outw[4];
 #pragma unroll
             for (int ww = 0; ww < 2; ww++) {
-              const uint32_t word = w[2 * (c & 3) + ww];
-              const uint32_t nib = half ? ((word >> 4) & 0x0F0F0F0Fu) : (word & 0x0F0F0F0Fu);
-              float v[4];
-#pragma unroll
-              for (int i = 0; i < 4; i++) {
-                const float qf = __uint_as_float(__byte_perm(nib, 0x4B000000u, 0x7540u | i)) - 8388608.0f;
-                v[i] = fmaf(d1[half], qf, -m1[half]);
-              }
-              __nv_bfloat162 p01 = __floats2bfloat162_rn(v[0], v[1]);
-              __nv_bfloat162 p23 = __floats2bfloat162_rn(v[2], v[3]);
-              outw[2 * ww] = *reinterpret_cast<uint32_t *>(&p01);
-              outw[2 * ww + 1] = *reinterpret_cast<uint32_t *>(&p23);
+              const uint32_t nib = hf ? ((w[2 * c + ww] >> 4) & 0x0F0F0F0Fu) : (w[2 * c + ww] & 0x0F0F0F0Fu);
+              // bytes (0,2) and (1,3) as fp16 pairs 1024 + q, exact
+              uint32_t a = (nib & 0x000F000Fu) | 0x64006400u;
+              uint32_t b = ((nib >> 8) & 0x000F000Fu) | 0x64006400u;
+              __half2 qa2 = __hsub2(*reinterpret_cast<__half2 *>(&a), k1024);
+              __half2 qb2 = __hsub2(*reinterpret_cast<__half2 *>(&b), k1024);
+              __half2 va = __hfma2(qa2, d1, nm1), vb = __hfma2(qb2, d1, nm1);
+              outw[2 * ww] = *reinterpret_cast<uint32_t *>(&va);
+              outw[2 * ww + 1] = *reinterpret_cast<uint32_t *>(&vb);
             }
-            *reinterpret_cast<uint4 *>(brow + ((c ^ (r & 7)) << 4)) = make_uint4(outw[0], outw[1], outw[2], outw[3]);
+            const int chunk = 4 * hf + c;
+            *reinterpret_cast<uint4 *>(brow + ((chunk ^ (r & 7)) << 4)) = make_uint4(outw[0], outw[1], outw[2], outw[3]);
           }
           fence_proxy_async();  // generic-proxy stores -> visible to the tensor core
           mbar_arrive(&bready[s]);
@@ -324,16 +329,19 @@ __global__ void __launch_bounds__(kThreadsG, 1)
   }
 }
 
-// X f32 [M][K] -> bf16 with each 64-element segment's columns permuted like
-// the Q4_K quants of the weight repack (32*half + r -> 32*half + 4*(r%8) + r/8).
-__global__ void x_to_bf16_q4perm(const float *__restrict__ X, __nv_bfloat16 *__restrict__ Xb, size_t M, int K) {
+// X f32 [M][K] -> fp16 with each 64-element segment's columns permuted to the
+// K order in which the dequant warps write the weight tile.
+__global__ void x_to_f16_q4perm(const float *__restrict__ X, __half *__restrict__ Xb, size_t M, int K) {
   const size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x;
   if (i >= M * (size_t)K) return;
   const size_t m = i / K;
   const int k = (int)(i % K);
   const int seg = k >> 6, half = (k >> 5) & 1, r = k & 31;
-  const int kp = (seg << 6) + 32 * half + 4 * (r & 7) + (r >> 3);
-  Xb[m * K + kp] = __float2bfloat16_rn(X[i]);
+  // element r of the half sits in repacked quant word r%8, byte r/8; the
+  // dequant writes each word's bytes in the order (0, 2, 1, 3)
+  const int byte = r >> 3;
+  const int kp = (seg << 6) + 32 * half + 4 * (r & 7) + ((byte & 1) << 1) + (byte >> 1);
+  Xb[m * K + kp] = __float2half_rn(X[i]);
 }
 
 using EncodeTiledFn = CUresult (*)(CUtensorMap *, CUtensorMapDataType, cuuint32_t, void *, const cuuint64_t *,
@@ -373,7 +381,7 @@ int32_t gemm_launch(unltd_ctx ctx, const unltd_weight_s &w, const float *X, floa
   if (M == 0 || w.dim_out == 0) return UNLTD_OK;
   const int K = (int)w.dim_in;
   cudaStream_t st = ctx->stream;
-  // bf16 copy of X with the permuted segment columns
+  // fp16 copy of X with the permuted segment columns
   const size_t xb_bytes = M * (size_t)K * 2;
   if (ctx->gemm_scratch_bytes < xb_bytes) {
     if (ctx->gemm_scratch) cudaFree(ctx->gemm_scratch);
@@ -383,16 +391,16 @@ int32_t gemm_launch(unltd_ctx ctx, const unltd_weight_s &w, const float *X, floa
     if (e != cudaSuccess) return cuda_error(e, "gemm scratch");
     ctx->gemm_scratch_bytes = xb_bytes;
   }
-  __nv_bfloat16 *Xb = reinterpret_cast<__nv_bfloat16 *>(ctx->gemm_scratch);
+  __half *Xb = reinterpret_cast<__half *>(ctx->gemm_scratch);
   {
     const size_t n = M * (size_t)K;
-    x_to_bf16_q4perm<<<(unsigned)((n + 255) / 256), 256, 0, st>>>(X, Xb, M, K);
+    x_to_f16_q4perm<<<(unsigned)((n + 255) / 256), 256, 0, st>>>(X, Xb, M, K);
     cudaError_t e = cudaGetLastError();
     if (e != cudaSuccess) return cuda_error(e, "gemm x convert");
     ctx->launches += 1;
   }
   CUtensorMap tmA, tmWq, tmWh;
-  if (!make_map_2d(&tmA, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, Xb, (uint64_t)K, M, (uint64_t)K * 2, kStepK, 128,
+  if (!make_map_2d(&tmA, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, Xb, (uint64_t)K, M, (uint64_t)K * 2, kStepK, 128,
                    CU_TENSOR_MAP_SWIZZLE_128B) ||
       !make_map_2d(&tmWq, CU_TENSOR_MAP_DATA_TYPE_UINT8, w.dev, w.row_stride, w.dim_out, w.row_stride, 32, kTileN,
                    CU_TENSOR_MAP_SWIZZLE_NONE) ||
