@@ -7,11 +7,14 @@
 //  * X is converted once per call to fp16, with the columns of every
 //    64-element segment permuted to the K order in which the dequant writes
 //    the weight tile, so A and B agree without any byte transpose.
-//  * warp 0 (one thread): TMA producer. Per 64-wide K step it loads the two
+//  * warps 0 and 2 (one thread each): TMA producers. Per 64-wide K step they load the two
 //    128x64 fp16 A tiles (SWIZZLE_128B tensor map) and, for the 192 weight
 //    rows of the tile, the 32-byte quant segment and 16-byte block header
-//    (2-D tensor maps over the repacked rows) into a 3-stage ring.
-//  * warps 2-13 (384 threads, two per weight row, one per nibble group):
+//    (2-D tensor maps over the repacked rows). Three rings decouple the
+//    latencies: packed weights (8 small stages, freed by the dequant, so they
+//    stream far ahead from HBM), X tiles (3 stages) and fp16 weight tiles (2
+//    stages), both freed by the MMAs' tcgen05.commit.
+//  * warps 3-14 (384 threads, two per weight row, one per nibble group):
 //    dequantize to fp16 — nibble -> exact fp16 (the 1024 + q bias trick),
 //    then q * fp16(d*sc) - fp16(dmin*m) in one fp16 FMA — and store into the
 //    B tile in the canonical K-major SWIZZLE_128B layout.
@@ -19,7 +22,7 @@
 //    M=128 N=192 K=16, for both 128-token halves, accumulating in TMEM
 //    (columns [0,192) and [256,448)); tcgen05.commit frees each stage and,
 //    after the last step, signals the epilogue.
-//  * warps 14-17: tcgen05.ld the accumulators (32x32b) and store Y in f32.
+//  * warps 15-18: tcgen05.ld the accumulators (32x32b) and store Y in f32.
 // Every mbarrier wait is bounded (2 s) and records a timeout in the context
 // error word; on any timeout all roles leave their loops, in-flight copies and
 // MMAs are waited for (bounded), and TMEM is freed before the CTA exits.
@@ -40,17 +43,19 @@ namespace {
 constexpr int kTileM = 256;   // tokens per tile (two MMAs of M = 128)
 constexpr int kTileN = 192;   // weight rows per tile (MMA N)
 constexpr int kStepK = 64;    // K per stage: one Q4_K quant segment
-constexpr int kStages = 3;
-constexpr int kDequantWarps = 12;  // warps 2..13: two threads per weight row
-constexpr int kThreadsG = (2 + kDequantWarps + 4) * 32;  // + producer, MMA, 4 epilogue warps
+constexpr int kStagesA = 3;   // X tiles, released by the MMAs
+constexpr int kStagesB = 2;   // dequantized weight tiles, released by the MMAs
+constexpr int kStagesW = 8;   // packed weight segments, released by the dequant
+constexpr int kDequantWarps = 12;  // warps 3..14: two threads per weight row
+constexpr int kThreadsG = (3 + kDequantWarps + 4) * 32;  // + 2 producers, MMA, 4 epilogue warps
 constexpr uint32_t kABytes = 2 * 128 * kStepK * 2;          // 32 KB
 constexpr uint32_t kBBytes = kTileN * kStepK * 2;            // 24 KB
 constexpr uint32_t kWqBytes = kTileN * 32;                   // 6 KB
 constexpr uint32_t kWhBytes = kTileN * 16;                   // 3 KB
-constexpr uint32_t kStageBytes = kABytes + kBBytes + kWqBytes + kWhBytes;
-constexpr uint32_t kTxBytes = kABytes + kWqBytes + kWhBytes;
+constexpr uint32_t kWBytes = kWqBytes + kWhBytes;            // 9 KB
 constexpr uint32_t kTmemCols = 512;
-constexpr int kSmemBytes = kStages * kStageBytes + 1024 /*align*/ + 256 /*barriers*/;
+constexpr int kSmemBytes =
+    kStagesA * kABytes + kStagesB * kBBytes + kStagesW * kWBytes + 1024 /*align*/ + 256 /*barriers*/;
 
 // ---- tcgen05 / TMA wrappers (inline PTX, sm_100a) --------------------------
 __device__ __forceinline__ void tmem_alloc(uint32_t *slot, uint32_t ncols) {
@@ -130,20 +135,32 @@ __global__ void __launch_bounds__(kThreadsG, 1)
   const uint32_t raw = smem_u32(smem_raw);
   const uint32_t pad = ((raw + 1023u) & ~1023u) - raw;
   uint8_t *base = smem_raw + pad;
-  uint8_t *stage0 = base;
-  uint64_t *bars = reinterpret_cast<uint64_t *>(base + kStages * kStageBytes);
-  uint64_t *full = bars, *bready = bars + kStages, *empty = bars + 2 * kStages;
-  uint64_t *acc_full = bars + 3 * kStages, *acc_empty = acc_full + 1;
+  uint8_t *ringA = base;
+  uint8_t *ringB = ringA + kStagesA * kABytes;
+  uint8_t *ringW = ringB + kStagesB * kBBytes;
+  uint64_t *bars = reinterpret_cast<uint64_t *>(ringW + kStagesW * kWBytes);
+  uint64_t *afull = bars, *aempty = afull + kStagesA;
+  uint64_t *bfull = aempty + kStagesA, *bempty = bfull + kStagesB;
+  uint64_t *wfull = bempty + kStagesB, *wempty = wfull + kStagesW;
+  uint64_t *acc_full = wempty + kStagesW, *acc_empty = acc_full + 1;
   uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(acc_empty + 1);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int ksteps = P.K / kStepK;
+  constexpr int kDequantThreads = kDequantWarps * 32;
 
   if (threadIdx.x == 0) {
-    for (int s = 0; s < kStages; s++) {
-      mbar_init(&full[s], 1);
-      mbar_init(&bready[s], kDequantWarps * 32);
-      mbar_init(&empty[s], 1);
+    for (int s = 0; s < kStagesA; s++) {
+      mbar_init(&afull[s], 1);
+      mbar_init(&aempty[s], 1);
+    }
+    for (int s = 0; s < kStagesB; s++) {
+      mbar_init(&bfull[s], kDequantThreads);
+      mbar_init(&bempty[s], 1);
+    }
+    for (int s = 0; s < kStagesW; s++) {
+      mbar_init(&wfull[s], 1);
+      mbar_init(&wempty[s], kDequantThreads);
     }
     mbar_init(acc_full, 1);
     mbar_init(acc_empty, 4);
@@ -158,34 +175,38 @@ __global__ void __launch_bounds__(kThreadsG, 1)
   tc_fence_after();
   const uint32_t tbase = *tmem_slot;
 
-  auto stA = [&](int s) { return stage0 + (size_t)s * kStageBytes; };
-  auto stB = [&](int s) { return stage0 + (size_t)s * kStageBytes + kABytes; };
-  auto stWq = [&](int s) { return stage0 + (size_t)s * kStageBytes + kABytes + kBBytes; };
-  auto stWh = [&](int s) { return stage0 + (size_t)s * kStageBytes + kABytes + kBBytes + kWqBytes; };
-
-  if (warp == 0) {
-    // ---------------- TMA producer ----------------
+  if (warp == 0 || warp == 2) {
+    // ---------------- TMA producers: warp 0 the X tiles, warp 2 the weight segments ----
     if (lane == 0) {
+      const bool isA = warp == 0;
+      const int S = isA ? kStagesA : kStagesW;
+      uint64_t *fullb = isA ? afull : wfull;
+      uint64_t *emptyb = isA ? aempty : wempty;
       long g = 0;
       bool ok = true;
       for (int t = blockIdx.x; t < P.ntiles && ok; t += gridDim.x) {
         const int tm = t / P.tiles_n, tn = t % P.tiles_n;
         for (int ks = 0; ks < ksteps && ok; ks++, g++) {
-          const int s = (int)(g % kStages);
-          const long round = g / kStages;
-          if (round > 0) ok = mbar_wait_bounded(&empty[s], (uint32_t)((round - 1) & 1), P.err);
+          const int s = (int)(g % S);
+          const long round = g / S;
+          if (round > 0) ok = mbar_wait_bounded(&emptyb[s], (uint32_t)((round - 1) & 1), P.err);
           if (!ok) break;
-          mbar_expect_tx(&full[s], kTxBytes);
-          tma_load_2d(stA(s), &tmA, ks * kStepK, tm * kTileM, &full[s]);
-          tma_load_2d(stA(s) + kABytes / 2, &tmA, ks * kStepK, tm * kTileM + 128, &full[s]);
-          const int b = ks >> 2, p = ks & 3;
-          tma_load_2d(stWq(s), &tmWq, P.nb * 16 + b * 128 + 32 * p, tn * kTileN, &full[s]);
-          tma_load_2d(stWh(s), &tmWh, b * 16, tn * kTileN, &full[s]);
+          if (isA) {
+            uint8_t *dst = ringA + (size_t)s * kABytes;
+            mbar_expect_tx(&fullb[s], kABytes);
+            tma_load_2d(dst, &tmA, ks * kStepK, tm * kTileM, &fullb[s]);
+            tma_load_2d(dst + kABytes / 2, &tmA, ks * kStepK, tm * kTileM + 128, &fullb[s]);
+          } else {
+            uint8_t *dst = ringW + (size_t)s * kWBytes;
+            const int b = ks >> 2, p = ks & 3;
+            mbar_expect_tx(&fullb[s], kWBytes);
+            tma_load_2d(dst, &tmWq, P.nb * 16 + b * 128 + 32 * p, tn * kTileN, &fullb[s]);
+            tma_load_2d(dst + kWqBytes, &tmWh, b * 16, tn * kTileN, &fullb[s]);
+          }
         }
       }
       // leave no copy in flight: wait for the last fill of every stage
-      for (long i = g - kStages < 0 ? 0 : g - kStages; i < g; i++)
-        mbar_wait_bounded(&full[i % kStages], (uint32_t)((i / kStages) & 1), P.err);
+      for (long i = g - S < 0 ? 0 : g - S; i < g; i++) mbar_wait_bounded(&fullb[i % S], (uint32_t)((i / S) & 1), P.err);
     }
   } else if (warp == 1) {
     // ---------------- MMA issuer ----------------
@@ -200,21 +221,22 @@ __global__ void __launch_bounds__(kThreadsG, 1)
         if (!ok) break;
         tc_fence_after();
         for (int ks = 0; ks < ksteps && ok; ks++, g++) {
-          const int s = (int)(g % kStages);
-          const uint32_t par = (uint32_t)((g / kStages) & 1);
-          ok = mbar_wait_bounded(&full[s], par, P.err) && mbar_wait_bounded(&bready[s], par, P.err);
+          const int sa = (int)(g % kStagesA), sb = (int)(g % kStagesB);
+          ok = mbar_wait_bounded(&afull[sa], (uint32_t)((g / kStagesA) & 1), P.err) &&
+               mbar_wait_bounded(&bfull[sb], (uint32_t)((g / kStagesB) & 1), P.err);
           if (!ok) break;
           tc_fence_after();
-          const uint32_t a0 = smem_u32(stA(s)), b0 = smem_u32(stB(s));
+          const uint32_t a0 = smem_u32(ringA + (size_t)sa * kABytes), b0 = smem_u32(ringB + (size_t)sb * kBBytes);
 #pragma unroll
           for (int h = 0; h < 2; h++)
 #pragma unroll
             for (int kk = 0; kk < kStepK / 16; kk++)
               umma_f16(tbase + (uint32_t)(h * 256), sw128_desc(a0 + h * (kABytes / 2) + kk * 32),
-                        sw128_desc(b0 + kk * 32), kIdesc, (ks > 0 || kk > 0) ? 1u : 0u);
-          umma_commit(&empty[s]);
-          last = &empty[s];
-          last_par = par;
+                       sw128_desc(b0 + kk * 32), kIdesc, (ks > 0 || kk > 0) ? 1u : 0u);
+          umma_commit(&aempty[sa]);
+          umma_commit(&bempty[sb]);
+          last = &bempty[sb];
+          last_par = (uint32_t)((g / kStagesB) & 1);
         }
         if (ok) {
           umma_commit(acc_full);
@@ -224,64 +246,65 @@ __global__ void __launch_bounds__(kThreadsG, 1)
       }
       if (last) mbar_wait_bounded(last, last_par, P.err);  // MMAs retired before TMEM is freed
     }
-  } else if (warp < 2 + kDequantWarps) {
+  } else if (warp < 3 + kDequantWarps) {
     // ---------------- dequantize Q4_K -> fp16 B tile ----------------
     // Thread (r, hf): weight row r of the tile, nibble half hf (group 2p or
     // 2p+1 of the current 64-element segment p).
-    const int dt = threadIdx.x - 64;
+    const int dt = threadIdx.x - 96;
     const int r = dt % kTileN, hf = dt / kTileN;
     long g = 0;
     bool ok = true;
     for (int t = blockIdx.x; t < P.ntiles && ok; t += gridDim.x) {
       for (int ks = 0; ks < ksteps && ok; ks++, g++) {
-        const int s = (int)(g % kStages);
-        const uint32_t par = (uint32_t)((g / kStages) & 1);
-        ok = mbar_wait_bounded(&full[s], par, P.err);
-        if (ok) {
-          const uint4 hq = *reinterpret_cast<const uint4 *>(stWh(s) + r * 16);
-          // the two 16-byte halves of the row's 32 quant bytes, read in an
-          // order that keeps the 8 lanes of each quarter-warp on distinct banks
-          const int f = (r >> 2) & 1;
-          const uint4 qa = *reinterpret_cast<const uint4 *>(stWq(s) + r * 32 + 16 * f);
-          const uint4 qb = *reinterpret_cast<const uint4 *>(stWq(s) + r * 32 + 16 * (1 - f));
-          const uint4 q0 = f ? qb : qa, q1 = f ? qa : qb;
-          const int p = ks & 3;
-          uint32_t SC, MM;
-          if (p < 2) {
-            SC = hq.y & 0x3F3F3F3Fu;
-            MM = hq.z & 0x3F3F3F3Fu;
-          } else {
-            SC = (hq.w & 0x0F0F0F0Fu) | ((hq.y >> 2) & 0x30303030u);
-            MM = ((hq.w >> 4) & 0x0F0F0F0Fu) | ((hq.z >> 2) & 0x30303030u);
-          }
-          const int sh = (p & 1) * 16 + hf * 8;
-          const float d = h2f_bits(hq.x & 0xFFFFu), dmin = h2f_bits(hq.x >> 16);
-          const __half2 d1 = __float2half2_rn(__fmul_rn(d, (float)((SC >> sh) & 0xFF)));
-          const __half2 nm1 = __float2half2_rn(-__fmul_rn(dmin, (float)((MM >> sh) & 0xFF)));
-          const __half2 k1024 = __float2half2_rn(1024.0f);
-          const uint32_t w[8] = {q0.x, q0.y, q0.z, q0.w, q1.x, q1.y, q1.z, q1.w};
-          uint8_t *brow = stB(s) + (r >> 3) * 1024 + (r & 7) * 128;
-#pragma unroll
-          for (int c = 0; c < 4; c++) {
-            uint32_t outw[4];
-#pragma unroll
-            for (int ww = 0; ww < 2; ww++) {
-              const uint32_t nib = hf ? ((w[2 * c + ww] >> 4) & 0x0F0F0F0Fu) : (w[2 * c + ww] & 0x0F0F0F0Fu);
-              // bytes (0,2) and (1,3) as fp16 pairs 1024 + q, exact
-              uint32_t a = (nib & 0x000F000Fu) | 0x64006400u;
-              uint32_t b = ((nib >> 8) & 0x000F000Fu) | 0x64006400u;
-              __half2 qa2 = __hsub2(*reinterpret_cast<__half2 *>(&a), k1024);
-              __half2 qb2 = __hsub2(*reinterpret_cast<__half2 *>(&b), k1024);
-              __half2 va = __hfma2(qa2, d1, nm1), vb = __hfma2(qb2, d1, nm1);
-              outw[2 * ww] = *reinterpret_cast<uint32_t *>(&va);
-              outw[2 * ww + 1] = *reinterpret_cast<uint32_t *>(&vb);
-            }
-            const int chunk = 4 * hf + c;
-            *reinterpret_cast<uint4 *>(brow + ((chunk ^ (r & 7)) << 4)) = make_uint4(outw[0], outw[1], outw[2], outw[3]);
-          }
-          fence_proxy_async();  // generic-proxy stores -> visible to the tensor core
-          mbar_arrive(&bready[s]);
+        const int sw = (int)(g % kStagesW), sb = (int)(g % kStagesB);
+        ok = mbar_wait_bounded(&wfull[sw], (uint32_t)((g / kStagesW) & 1), P.err);
+        if (ok && g >= kStagesB) ok = mbar_wait_bounded(&bempty[sb], (uint32_t)((g / kStagesB - 1) & 1), P.err);
+        if (!ok) break;
+        const uint8_t *wst = ringW + (size_t)sw * kWBytes;
+        const uint4 hq = *reinterpret_cast<const uint4 *>(wst + kWqBytes + r * 16);
+        // the two 16-byte halves of the row's 32 quant bytes, read in an
+        // order that keeps the 8 lanes of each quarter-warp on distinct banks
+        const int f = (r >> 2) & 1;
+        const uint4 qa = *reinterpret_cast<const uint4 *>(wst + r * 32 + 16 * f);
+        const uint4 qb = *reinterpret_cast<const uint4 *>(wst + r * 32 + 16 * (1 - f));
+        mbar_arrive(&wempty[sw]);  // the weight stage is in registers now
+        const uint4 q0 = f ? qb : qa, q1 = f ? qa : qb;
+        const int p = ks & 3;
+        uint32_t SC, MM;
+        if (p < 2) {
+          SC = hq.y & 0x3F3F3F3Fu;
+          MM = hq.z & 0x3F3F3F3Fu;
+        } else {
+          SC = (hq.w & 0x0F0F0F0Fu) | ((hq.y >> 2) & 0x30303030u);
+          MM = ((hq.w >> 4) & 0x0F0F0F0Fu) | ((hq.z >> 2) & 0x30303030u);
         }
+        const int sh = (p & 1) * 16 + hf * 8;
+        const float d = h2f_bits(hq.x & 0xFFFFu), dmin = h2f_bits(hq.x >> 16);
+        const __half2 d1 = __float2half2_rn(__fmul_rn(d, (float)((SC >> sh) & 0xFF)));
+        const __half2 nm1 = __float2half2_rn(-__fmul_rn(dmin, (float)((MM >> sh) & 0xFF)));
+        const __half2 k1024 = __float2half2_rn(1024.0f);
+        const uint32_t w[8] = {q0.x, q0.y, q0.z, q0.w, q1.x, q1.y, q1.z, q1.w};
+        uint8_t *brow = ringB + (size_t)sb * kBBytes + (r >> 3) * 1024 + (r & 7) * 128;
+#pragma unroll
+        for (int c = 0; c < 4; c++) {
+          uint32_t outw[4];
+#pragma unroll
+          for (int ww = 0; ww < 2; ww++) {
+            const uint32_t nib = hf ? ((w[2 * c + ww] >> 4) & 0x0F0F0F0Fu) : (w[2 * c + ww] & 0x0F0F0F0Fu);
+            // bytes (0,2) and (1,3) as fp16 pairs 1024 + q, exact
+            uint32_t a = (nib & 0x000F000Fu) | 0x64006400u;
+            uint32_t b = ((nib >> 8) & 0x000F000Fu) | 0x64006400u;
+            __half2 qa2 = __hsub2(*reinterpret_cast<__half2 *>(&a), k1024);
+            __half2 qb2 = __hsub2(*reinterpret_cast<__half2 *>(&b), k1024);
+            __half2 va = __hfma2(qa2, d1, nm1), vb = __hfma2(qb2, d1, nm1);
+            outw[2 * ww] = *reinterpret_cast<uint32_t *>(&va);
+            outw[2 * ww + 1] = *reinterpret_cast<uint32_t *>(&vb);
+          }
+          const int chunk = 4 * hf + c;
+          *reinterpret_cast<uint4 *>(brow + ((chunk ^ (r & 7)) << 4)) = make_uint4(outw[0], outw[1], outw[2], outw[3]);
+        }
+        fence_proxy_async();  // generic-proxy stores -> visible to the tensor core
+        mbar_arrive(&bfull[sb]);
       }
     }
   } else {
