@@ -44,8 +44,8 @@ constexpr int kTileM = 256;   // tokens per tile (two MMAs of M = 128)
 constexpr int kTileN = 192;   // weight rows per tile (MMA N)
 constexpr int kStepK = 64;    // K per stage: one Q4_K quant segment
 constexpr int kStagesA = 3;   // X tiles, released by the MMAs
-constexpr int kStagesB = 2;   // dequantized weight tiles, released by the MMAs
-constexpr int kStagesW = 8;   // packed weight segments, released by the dequant
+constexpr int kStagesB = 3;   // dequantized weight tiles, released by the MMAs
+constexpr int kStagesW = 5;   // packed weight segments, released by the dequant
 constexpr int kDequantWarps = 12;  // warps 3..14: two threads per weight row
 constexpr int kThreadsG = (3 + kDequantWarps + 4) * 32;  // + 2 producers, MMA, 4 epilogue warps
 constexpr uint32_t kABytes = 2 * 128 * kStepK * 2;          // 32 KB
