@@ -157,6 +157,56 @@ int32_t unltd_dequant(unltd_ctx ctx, unltd_weight w, float *out_dev);
  * (symbol address, kernel attributes); make it before any stream capture. */
 int32_t unltd_gemv_noalloc(unltd_weight w, const float *x_dev, float *y_dev, int32_t mode, void *stream);
 
+/* ---- Qwen3.5-style hybrid decode step ------------------------------------
+ * Replaces Qwen35Forward (crates/unltd-generation/src/qwen35_forward.rs):
+ * open (139-232: every tensor checked for shape and dtype), new_session
+ * (235-257), step (295-330) and, fused on the device, output_norm + the LM
+ * head (min_forward.rs:210-266) + greedy argmax (greedy.rs:18-27). One CUDA
+ * graph per token; the greedy token is fed back on the device. Every
+ * projection is gemv_quant_q8k-exact and the f32 kernels between them keep
+ * the reference's operation order, so hidden states and logits equal the
+ * reference's (f32 exp/log correctly rounded). Kernel limits: linear head dim
+ * 128, attention head_dim 128 or 256, d_inner == n_embd, ctx <= 16384. */
+typedef struct {
+    int32_t n_layer, n_embd, n_ff, n_head, n_head_kv, head_dim, head_dim_v, n_rot;
+    int32_t conv_kernel, state_size, group_count, time_step_rank, d_inner, full_attn_interval, vocab;
+    float freq_base, rms_eps;
+} unltd_qwen35_config; /* qwen35.rs:46-80 */
+
+typedef struct unltd_qwen35_s *unltd_qwen35;
+typedef struct unltd_qwen35_session_s *unltd_qwen35_session;
+
+int32_t unltd_qwen35_create(unltd_ctx ctx, const unltd_qwen35_config *cfg, unltd_qwen35 *out);
+/* Upload one GGUF tensor by its name ("blk.3.attn_q.weight", "output.weight",
+ * ...): packed bytes or F32 values, checked against the configuration. */
+int32_t unltd_qwen35_set_tensor(unltd_qwen35 m, const char *name, const void *host, size_t nbytes, int32_t dtype);
+/* Check that every tensor is present and merge same-input projections
+ * (qkv|z|beta|alpha, q|k|v, gate|up) into single GEMVs. */
+int32_t unltd_qwen35_finalize(unltd_qwen35 m);
+int32_t unltd_qwen35_destroy(unltd_qwen35 m);
+/* A session: conv windows, GDN states and K/V cache for ctx_len positions,
+ * all zero, position 0 (new_session). Has its own stream. */
+int32_t unltd_qwen35_session_create(unltd_qwen35 m, int32_t ctx_len, unltd_qwen35_session *out);
+int32_t unltd_qwen35_session_destroy(unltd_qwen35_session s);
+/* Load a state at `position`: per recurrent layer (in layer order) the conv
+ * window ((conv_kernel-1) x 2*d_inner, oldest row first) and the GDN
+ * matrices (n_v x 128 x 128); per attention layer the first `position` rows
+ * of K and V (n_head_kv*head_dim each). NULL arrays or entries mean zeros. */
+int32_t unltd_qwen35_session_set_state(unltd_qwen35_session s, int32_t position, const float *const *conv,
+                                       const float *const *gdn, const float *const *kcache,
+                                       const float *const *vcache);
+/* Teacher-forced steps over a prompt; *next_token (nullable) = the greedy
+ * token after the last one. */
+int32_t unltd_qwen35_feed(unltd_qwen35_session s, const uint32_t *tokens, int32_t n, uint32_t *next_token);
+/* Greedy decode of n_steps tokens: step 0 consumes `token`, step i consumes
+ * tokens_out[i-1]; tokens_out[i] = argmax of step i's logits. */
+int32_t unltd_qwen35_decode(unltd_qwen35_session s, uint32_t token, int32_t n_steps, uint32_t *tokens_out);
+/* Position, the session's cudaStream_t, kernels launched per step. */
+int32_t unltd_qwen35_session_info(unltd_qwen35_session s, int32_t *position, void **stream,
+                                  int64_t *launches_per_step);
+/* Last step's logits (vocab) and hidden state (l_out of the last layer). */
+int32_t unltd_qwen35_session_read(unltd_qwen35_session s, float *logits, float *hidden);
+
 /* ---- reference-signature API (host buffers, synchronous) ---------------- */
 /* quants.rs:422  pub fn gemv_quant(out, x, w, dim_in, dim_out, dtype) */
 int32_t unltd_gemv_quant(float *out, size_t out_len, const float *x, size_t x_len, const uint8_t *w,

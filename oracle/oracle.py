@@ -42,7 +42,7 @@ def lib():
     global _lib
     if _lib is None:
         if not os.path.exists(LIB_PATH) or os.path.getmtime(LIB_PATH) < max(
-            os.path.getmtime(os.path.join(HERE, f)) for f in ("quants_ref.c", "quants_ref.h")
+            os.path.getmtime(os.path.join(HERE, f)) for f in ("quants_ref.c", "quants_ref.h", "forward_ref.c", "forward_ref.h")
         ):
             build()
         L = ctypes.CDLL(LIB_PATH)
@@ -199,3 +199,187 @@ def argmax(v) -> int:
 
 def row_bytes(dtype, dim_in) -> int:
     return int(lib().ora_row_bytes(dtype, dim_in))
+
+
+# ---- Qwen3.5-style hybrid decode step (forward_ref.c) -----------------------
+
+class _OraCfg(ctypes.Structure):
+    _fields_ = [(n, ctypes.c_int) for n in (
+        "n_layer", "n_embd", "n_ff", "n_head", "n_head_kv", "head_dim", "n_rot", "conv_kernel", "group_count",
+        "d_inner", "full_attn_interval", "vocab", "ctx")] + [("rms_eps", ctypes.c_float), ("theta_scale", ctypes.c_double)]
+
+
+# Per-layer tensor slots, in the order of the ORA_* enum of forward_ref.h.
+LAYER_KINDS = [
+    "attn_norm.weight", "post_attention_norm.weight", "ffn_gate.weight", "ffn_up.weight", "ffn_down.weight",
+    "attn_q.weight", "attn_q_norm.weight", "attn_k.weight", "attn_k_norm.weight", "attn_v.weight",
+    "attn_output.weight", "attn_qkv.weight", "attn_gate.weight", "ssm_conv1d.weight", "ssm_dt.bias", "ssm_a",
+    "ssm_beta.weight", "ssm_alpha.weight", "ssm_norm.weight", "ssm_out.weight",
+]
+GLOBAL_KINDS = ["token_embd.weight", "output_norm.weight", "output.weight"]
+
+
+class Qwen35Oracle:
+    """CPU decode step (ora_decode_token) over a model given as name ->
+    (dtype, array), with its own copy of the session state."""
+
+    def __init__(self, cfg: dict, tensors: dict, ctx: int, state: dict | None = None, position: int = 0,
+                 theta_scale: float | None = None):
+        L = lib()
+        if not hasattr(L, "_fwd_ready"):
+            L.ora_decode_token.argtypes = [ctypes.c_void_p] * 6 + [ctypes.c_void_p, ctypes.c_int, ctypes.c_uint32,
+                                                                    ctypes.c_void_p, ctypes.c_void_p, ctypes.c_int]
+            L.ora_decode_token.restype = ctypes.c_int
+            L._fwd_ready = True
+        if theta_scale is None:
+            theta_scale = float(np.float32(np.float32(cfg["freq_base"]) ** (np.float32(-2.0) / np.float32(cfg["n_rot"]))))
+        self.cfg = cfg
+        self.c = _OraCfg(cfg["n_layer"], cfg["n_embd"], cfg["n_ff"], cfg["n_head"], cfg["n_head_kv"], cfg["head_dim"],
+                         cfg["n_rot"], cfg["conv_kernel"], cfg["group_count"], cfg["d_inner"],
+                         cfg["full_attn_interval"], cfg["vocab"], ctx, cfg["rms_eps"], theta_scale)
+        nslots = len(GLOBAL_KINDS) + len(LAYER_KINDS) * cfg["n_layer"]
+        self._keep = []
+        ptrs = (ctypes.c_void_p * nslots)()
+        dts = (ctypes.c_int * nslots)()
+        names = list(GLOBAL_KINDS) + [f"blk.{il}.{k}" for il in range(cfg["n_layer"]) for k in LAYER_KINDS]
+        for i, nm in enumerate(names):
+            if nm in tensors:
+                dt, arr = tensors[nm]
+                arr = np.ascontiguousarray(arr)
+                self._keep.append(arr)
+                ptrs[i] = arr.ctypes.data
+                dts[i] = dt
+        self.ptrs, self.dts = ptrs, dts
+        hd = cfg["d_inner"] // (2 * cfg["group_count"])
+        nv, dconv, kvlen = cfg["d_inner"] // hd, 2 * cfg["d_inner"], cfg["n_head_kv"] * cfg["head_dim"]
+        attn = [(il + 1) % cfg["full_attn_interval"] == 0 for il in range(cfg["n_layer"])]
+        nr, na = attn.count(False), attn.count(True)
+        st = state or {}
+        self.conv = [np.array(st["conv"][i], np.float32) if st.get("conv") else
+                     np.zeros((cfg["conv_kernel"] - 1, dconv), np.float32) for i in range(nr)]
+        self.gdn = [np.array(st["gdn"][i], np.float32) if st.get("gdn") else np.zeros((nv, hd, hd), np.float32)
+                    for i in range(nr)]
+        self.k = [np.zeros((ctx, kvlen), np.float32) for _ in range(na)]
+        self.v = [np.zeros((ctx, kvlen), np.float32) for _ in range(na)]
+        for i in range(na):
+            if st.get("k"):
+                self.k[i][:position] = st["k"][i][:position]
+                self.v[i][:position] = st["v"][i][:position]
+        self.position = position
+
+        def arr(xs):
+            a = (ctypes.c_void_p * max(1, len(xs)))()
+            for i, x in enumerate(xs):
+                a[i] = x.ctypes.data
+            return a
+
+        self._conv_p, self._gdn_p, self._k_p, self._v_p = arr(self.conv), arr(self.gdn), arr(self.k), arr(self.v)
+
+    def step(self, token: int, nthreads: int = 8):
+        """One token; returns (logits, hidden) and advances the position."""
+        logits = np.empty(self.cfg["vocab"], np.float32)
+        hidden = np.empty(self.cfg["n_embd"], np.float32)
+        rc = lib().ora_decode_token(ctypes.byref(self.c), self.ptrs, self.dts, self._conv_p, self._gdn_p, self._k_p,
+                                    self._v_p, self.position, token, logits.ctypes.data, hidden.ctypes.data, nthreads)
+        if rc != 0:
+            raise ValueError(f"ora_decode_token failed ({rc})")
+        self.position += 1
+        return logits, hidden
+
+    def greedy(self, token: int, n_steps: int, nthreads: int = 8):
+        """greedy.rs: step, argmax (first index of the max), feed back."""
+        out, logits, hidden = [], None, None
+        for _ in range(n_steps):
+            logits, hidden = self.step(token, nthreads)
+            token = argmax(logits)
+            out.append(token)
+        return out, logits, hidden
+
+
+# ---- f32 kernels of the decode step (forward_ref.c, kernels.rs) --------------
+
+def _fwd_lib():
+    L = lib()
+    if not hasattr(L, "_fwd_k_ready"):
+        P, I, F, D = ctypes.c_void_p, ctypes.c_int, ctypes.c_float, ctypes.c_double
+        L.ora_rmsnorm.argtypes = [P, P, P, I, F]
+        L.ora_l2_norm_rows.argtypes = [P, I, I, F]
+        L.ora_gdn_step.argtypes = [P, P, P, P, P, F, F, F, I]
+        L.ora_rope_imrope.argtypes = [P, I, D, I]
+        L.ora_softmax.argtypes = [P, P, I, F]
+        for nm in ("ora_sigmoid", "ora_silu", "ora_softplus"):
+            getattr(L, nm).argtypes = [P, P, I]
+        L.ora_swiglu.argtypes = [P, P, P, I]
+        L.ora_ssm_conv.argtypes = [P, P, I, P, I, I]
+        L.ora_expf.argtypes = [F]
+        L.ora_expf.restype = F
+        L._fwd_k_ready = True
+    return L
+
+
+def rmsnorm(x, w, eps):
+    x, w = _f32(x), _f32(w)
+    out = np.zeros_like(x)
+    _fwd_lib().ora_rmsnorm(_p(out), _p(x), _p(w), x.size, eps)
+    return out
+
+
+def l2_norm_rows(x, dim, eps):
+    x = _f32(x).copy()
+    _fwd_lib().ora_l2_norm_rows(_p(x), x.size // dim, dim, eps)
+    return x
+
+
+def gdn_step(state, q, k, v, gate, beta, scale):
+    state = _f32(state).copy()
+    q, k, v = _f32(q), _f32(k), _f32(v)
+    out = np.zeros(q.size, np.float32)
+    _fwd_lib().ora_gdn_step(_p(state), _p(out), _p(q), _p(k), _p(v), gate, beta, scale, q.size)
+    return state, out
+
+
+def rope_imrope(x, n_rot, theta_scale, pos):
+    x = _f32(x).copy()
+    _fwd_lib().ora_rope_imrope(_p(x), n_rot, theta_scale, pos)
+    return x
+
+
+def softmax(x, scale):
+    x = _f32(x)
+    out = np.zeros_like(x)
+    _fwd_lib().ora_softmax(_p(out), _p(x), x.size, scale)
+    return out
+
+
+def _elementwise(name, x):
+    x = _f32(x)
+    out = np.zeros_like(x)
+    getattr(_fwd_lib(), name)(_p(out), _p(x), x.size)
+    return out
+
+
+def sigmoid(x):
+    return _elementwise("ora_sigmoid", x)
+
+
+def silu(x):
+    return _elementwise("ora_silu", x)
+
+
+def softplus(x):
+    return _elementwise("ora_softplus", x)
+
+
+def swiglu(g, u):
+    g, u = _f32(g), _f32(u)
+    out = np.zeros_like(g)
+    _fwd_lib().ora_swiglu(_p(out), _p(g), _p(u), g.size)
+    return out
+
+
+def ssm_conv(x, kernel, d_conv, channels):
+    x, kernel = _f32(x), _f32(kernel)
+    ncs = x.size // channels
+    out = np.zeros((ncs - (d_conv - 1)) * channels, np.float32)
+    _fwd_lib().ora_ssm_conv(_p(out), _p(x), ncs, _p(kernel), d_conv, channels)
+    return out

@@ -65,19 +65,6 @@ int32_t check_view(int dtype, size_t dim_in, size_t dim_out, size_t nbytes, cons
   return UNLTD_OK;
 }
 
-struct CtxGuard {
-  int prev = -1;
-  explicit CtxGuard(int dev) {
-    cudaGetDevice(&prev);
-    if (prev != dev) cudaSetDevice(dev);
-  }
-  ~CtxGuard() {
-    int cur = -1;
-    cudaGetDevice(&cur);
-    if (prev >= 0 && cur != prev) cudaSetDevice(prev);
-  }
-};
-
 }  // namespace
 
 namespace unltd {
@@ -89,6 +76,7 @@ int32_t check_device_error(unltd_ctx c, const char *who) {
   if (e != cudaSuccess) return cuda_error(e, who);
   if (v == 0) return UNLTD_OK;
   cudaMemset(c->err, 0, sizeof(int));
+  if (v == 2) return set_error(UNLTD_ERR_INVALID_ARG, std::string(who) + ": a token id outside the vocabulary reached the embedding");
   return set_error(UNLTD_ERR_TIMEOUT, std::string(who) + ": a kernel gave up waiting on a pipeline barrier");
 }
 

@@ -1,0 +1,1223 @@
+// Greedy decode step of the Qwen3.5-style hybrid model on one GPU: the f32
+// kernels between the quantized projections, and the model/session runner
+// that chains them with the Q8_K-exact GEMVs of gemv.cu into one CUDA graph
+// per token.
+//
+// Follows crates/unltd-generation/src/qwen35_forward.rs (step 295-330,
+// recr_layer 333-543, attn_layer 546-710, ffn 713-768), the LM head of
+// min_forward.rs:210-266 and greedy.rs:18-27. Every f32/f64 operation of the
+// reference is reproduced in the same order with explicit round-to-nearest
+// intrinsics (no contraction), so the hidden states match the reference's
+// bit for bit, with one stated exception: f32 exp/log are the correctly
+// rounded values (computed through double precision), where the reference
+// inherits its platform libm's last bit.
+//
+// Sequential f64 sums (rmsnorm, l2_norm_rows, the attention value sum) are
+// evaluated in parallel and resolved exactly: the reference's left-to-right
+// sum and the parallel sum both lie within (n-1)*2^-53*sum|t| of the exact
+// sum, so when every value within twice that bound rounds to the same f32
+// result, that result is the reference's; otherwise (rare: the interval
+// straddles an f32 rounding boundary) one thread recomputes the sum
+// left-to-right.
+#include <cmath>
+#include <cstring>
+#include <map>
+#include <string>
+#include <vector>
+
+#include "unltd_host.h"
+#include "unltd_internal.cuh"
+
+namespace unltd {
+namespace {
+
+constexpr int kErrTimeout = 1;
+constexpr int kErrToken = 2;
+
+// ---- scalar functions (kernels.rs:198-226, 174-182) ----------------------
+__device__ __forceinline__ float exp_cr(float x) { return (float)exp((double)x); }
+__device__ __forceinline__ float log_cr(float x) { return (float)log((double)x); }
+__device__ __forceinline__ float sigmoid_f(float x) { return __fdiv_rn(1.0f, __fadd_rn(1.0f, exp_cr(-x))); }
+__device__ __forceinline__ float silu_f(float x) { return __fdiv_rn(x, __fadd_rn(1.0f, exp_cr(-x))); }
+__device__ __forceinline__ float softplus_f(float x) {
+  return x > 20.0f ? x : log_cr(__fadd_rn(1.0f, exp_cr(x)));
+}
+
+// ---- reductions -----------------------------------------------------------
+// Sum of a and b over the block; every thread receives the same values.
+template <int NT>
+__device__ __forceinline__ void block_sum2(double &a, double &b, double *red) {
+#pragma unroll
+  for (int o = 16; o; o >>= 1) {
+    a += __shfl_xor_sync(~0u, a, o);
+    b += __shfl_xor_sync(~0u, b, o);
+  }
+  constexpr int NW = NT / 32;
+  if constexpr (NW > 1) {
+    const int w = threadIdx.x >> 5;
+    __syncthreads();
+    if ((threadIdx.x & 31) == 0) {
+      red[w] = a;
+      red[NW + w] = b;
+    }
+    __syncthreads();
+    a = 0.0;
+    b = 0.0;
+#pragma unroll
+    for (int i = 0; i < NW; i++) {
+      a += red[i];
+      b += red[NW + i];
+    }
+  }
+}
+
+template <int NT>
+__device__ __forceinline__ float block_max(float v, float *red) {
+#pragma unroll
+  for (int o = 16; o; o >>= 1) v = fmaxf(v, __shfl_xor_sync(~0u, v, o));
+  constexpr int NW = NT / 32;
+  if constexpr (NW > 1) {
+    __syncthreads();
+    if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = v;
+    __syncthreads();
+    v = red[0];
+#pragma unroll
+    for (int i = 1; i < NW; i++) v = fmaxf(v, red[i]);
+  }
+  return v;
+}
+
+// f(seq) for the reference's left-to-right f64 sum `seq` of n terms, given
+// the parallel sum S of the same terms and their absolute sum A, with f a
+// monotone non-decreasing map to f32. True when the bound decides it.
+template <class F>
+__device__ __forceinline__ bool resolve_sum(double S, double A, int n, F f, float *out) {
+  const double B = (double)(n + 8) * 0x1p-51 * A;
+  const float lo = f(S - B), hi = f(S + B);
+  *out = lo;
+  return lo == hi;
+}
+
+struct MeanOf {
+  int n;
+  __device__ float operator()(double s) const { return (float)(s / (double)n); }
+};
+struct ToF32 {
+  __device__ float operator()(double s) const { return (float)s; }
+};
+
+// ---- RMSNorm with an optional residual add (kernels.rs:61-78) ------------
+// r = a (+ b) elementwise; r_out = r when non-null; out = rmsnorm(r, w).
+template <int NT>
+__global__ void __launch_bounds__(NT) add_rmsnorm_kernel(const float *a, const float *b, float *r_out,
+                                                         const float *w, float *out, int n, float eps) {
+  __shared__ double red[2 * NT / 32];
+  __shared__ float s_mean;
+  double S = 0.0, A = 0.0;
+  for (int i = threadIdx.x; i < n; i += NT) {
+    const float r = b ? __fadd_rn(a[i], b[i]) : a[i];
+    if (r_out) r_out[i] = r;
+    S += (double)__fmul_rn(r, r);
+  }
+  block_sum2<NT>(S, A, red);
+  auto R = [&](int i) { return r_out ? r_out[i] : (b ? __fadd_rn(a[i], b[i]) : a[i]); };
+  float mean;
+  const MeanOf f{n};
+  if (!resolve_sum(S, S, n, f, &mean)) {
+    __syncthreads();  // r_out visible to thread 0
+    if (threadIdx.x == 0) {
+      double s = 0.0;
+#pragma unroll 1
+      for (int i = 0; i < n; i++) {
+        const float r = R(i);
+        s = __dadd_rn(s, (double)__fmul_rn(r, r));
+      }
+      s_mean = f(s);
+    }
+    __syncthreads();
+    mean = s_mean;
+  }
+  const float scale = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(mean, eps)));
+  for (int i = threadIdx.x; i < n; i += NT) {
+    const float r = r_out ? R(i) : (b ? __fadd_rn(a[i], b[i]) : a[i]);
+    out[i] = __fmul_rn(__fmul_rn(r, scale), w[i]);
+  }
+}
+
+// ---- token embedding: one Q4_K row, dequantized (min_forward.rs:160-184) --
+__global__ void embed_q4k_kernel(const uint8_t *table, size_t stride, size_t nb, const uint32_t *token,
+                                 uint32_t vocab, float *x, int n, int *err) {
+  uint32_t t = *token;
+  if (t >= vocab) {
+    if (blockIdx.x == 0 && threadIdx.x == 0) atomicExch(err, kErrToken);
+    t = 0;
+  }
+  const uint8_t *row = table + (size_t)t * stride;
+  for (int e = blockIdx.x * blockDim.x + threadIdx.x; e < n; e += gridDim.x * blockDim.x)
+    x[e] = q4k_row_elem(row, nb, (size_t)e);
+}
+
+// ---- SwiGLU (kernels.rs:174-182) -------------------------------------------
+__global__ void swiglu_kernel(const float *g, const float *u, float *out, int n) {
+  int i = blockIdx.x * blockDim.x + threadIdx.x;
+  if (i < n) {
+    const float t = g[i];
+    const float s = __fdiv_rn(t, __fadd_rn(1.0f, exp_cr(-t)));
+    out[i] = __fmul_rn(s, u[i]);
+  }
+}
+
+// ---- recurrent layer between the projections (qwen35_forward.rs:390-508) --
+struct RecrArgs {
+  const float *proj;    // [qkv (dconv) | z (nv*HD) | beta_raw (nv) | alpha (nv)]
+  float *ring;          // K slots x dconv; row tau of the window at slot (pos+tau) % K
+  const float *convw;   // ssm_conv1d.weight as stored, [channel][tau]
+  const float *dt_bias, *ssm_a, *ssm_norm;
+  float *state;         // nv x HD x HD, state[h][i][j]
+  float *y;             // nv*HD gated output
+  const int *pos;
+  int K, nqk, nv, dconv, z_off, beta_off, alpha_off;
+  float eps;
+};
+
+// One CTA per v-head h, one thread per channel j of the head. Thread j owns
+// column j of the head's GDN state (gdn_fused_step, kernels.rs:316-372,
+// touches column j only through the dots over i), kept in registers.
+template <int HD>
+__global__ void __launch_bounds__(HD) recr_mid_kernel(RecrArgs a) {
+  __shared__ float qs[HD], ks[HD], os[HD];
+  __shared__ double red[2 * HD / 32];
+  __shared__ float s_f[2];
+  const int h = blockIdx.x, j = threadIdx.x;
+  const int qk = h % a.nqk;  // periodic qk-head of v-head h (qwen35_forward.rs:464)
+  const int pos = *a.pos, K = a.K;
+  const int chq = qk * HD + j, chk = a.nqk * HD + qk * HD + j, chv = 2 * a.nqk * HD + h * HD + j;
+
+  // depthwise conv over [window rows, current qkv] (kernels.rs:265-310), silu
+  auto conv = [&](int ch) {
+    float s = 0.0f;
+    for (int tau = 0; tau < K; tau++) {
+      const float xv = tau < K - 1 ? a.ring[(size_t)((pos + tau) % K) * a.dconv + ch] : a.proj[ch];
+      s = __fadd_rn(s, __fmul_rn(xv, a.convw[(size_t)ch * K + tau]));
+    }
+    return s;
+  };
+  float q = silu_f(conv(chq)), k = silu_f(conv(chk));
+  const float v = silu_f(conv(chv));
+  // the current row enters the window: it becomes row K-2 of the next step
+  const size_t ws = (size_t)((pos + K - 1) % K) * a.dconv;
+  if (h < a.nqk) {
+    a.ring[ws + chq] = a.proj[chq];
+    a.ring[ws + chk] = a.proj[chk];
+  }
+  a.ring[ws + chv] = a.proj[chv];
+
+  // l2_norm_rows of q and k (kernels.rs:236-252)
+  qs[j] = q;
+  ks[j] = k;
+  double Sq = (double)__fmul_rn(q, q), Sk = (double)__fmul_rn(k, k);
+  block_sum2<HD>(Sq, Sk, red);
+  float fq, fk;
+  const bool okq = resolve_sum(Sq, Sq, HD, ToF32{}, &fq);
+  const bool okk = resolve_sum(Sk, Sk, HD, ToF32{}, &fk);
+  if (!okq || !okk) {
+    __syncthreads();
+    if (j < 2 && !(j == 0 ? okq : okk)) {
+      const float *src = j == 0 ? qs : ks;
+      double s = 0.0;
+#pragma unroll 1
+      for (int i = 0; i < HD; i++) s = __dadd_rn(s, (double)__fmul_rn(src[i], src[i]));
+      s_f[j] = (float)s;
+    }
+    __syncthreads();
+    if (!okq) fq = s_f[0];
+    if (!okk) fk = s_f[1];
+  }
+  q = __fmul_rn(q, __fdiv_rn(1.0f, fmaxf(__fsqrt_rn(fq), a.eps)));
+  k = __fmul_rn(k, __fdiv_rn(1.0f, fmaxf(__fsqrt_rn(fk), a.eps)));
+  __syncthreads();
+  qs[j] = q;
+  ks[j] = k;
+
+  // beta = sigmoid(beta_raw); gate = softplus(alpha + dt_bias) * ssm_a
+  const float beta = sigmoid_f(a.proj[a.beta_off + h]);
+  const float gate = __fmul_rn(softplus_f(__fadd_rn(a.proj[a.alpha_off + h], a.dt_bias[h])), a.ssm_a[h]);
+  __syncthreads();
+
+  // gdn_fused_step, column j
+  float st[HD];
+  float *S = a.state + (size_t)h * HD * HD;
+#pragma unroll
+  for (int i = 0; i < HD; i++) st[i] = S[(size_t)i * HD + j];
+  const float g = exp_cr(gate);
+  double acc = 0.0;
+#pragma unroll
+  for (int i = 0; i < HD; i++) {
+    st[i] = __fmul_rn(st[i], g);
+    acc = __dadd_rn(acc, (double)__fmul_rn(st[i], ks[i]));
+  }
+  const float d = __fmul_rn(__fsub_rn(v, (float)acc), beta);
+  acc = 0.0;
+#pragma unroll
+  for (int i = 0; i < HD; i++) {
+    st[i] = __fadd_rn(st[i], __fmul_rn(ks[i], d));
+    acc = __dadd_rn(acc, (double)__fmul_rn(st[i], qs[i]));
+  }
+#pragma unroll
+  for (int i = 0; i < HD; i++) S[(size_t)i * HD + j] = st[i];
+  const float o = __fmul_rn((float)acc, __fdiv_rn(1.0f, __fsqrt_rn((float)HD)));
+
+  // rmsnorm over the head with ssm_norm, times silu(z)
+  os[j] = o;
+  double So = (double)__fmul_rn(o, o), dummy = 0.0;
+  block_sum2<HD>(So, dummy, red);
+  float mean;
+  const MeanOf f{HD};
+  if (!resolve_sum(So, So, HD, f, &mean)) {
+    __syncthreads();
+    if (j == 0) {
+      double s = 0.0;
+#pragma unroll 1
+      for (int i = 0; i < HD; i++) s = __dadd_rn(s, (double)__fmul_rn(os[i], os[i]));
+      s_f[0] = f(s);
+    }
+    __syncthreads();
+    mean = s_f[0];
+  }
+  const float scale = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(mean, a.eps)));
+  const float yn = __fmul_rn(__fmul_rn(o, scale), a.ssm_norm[j]);
+  a.y[h * HD + j] = __fmul_rn(yn, silu_f(a.proj[a.z_off + h * HD + j]));
+}
+
+// ---- full-attention layer (qwen35_forward.rs:584-686) ----------------------
+struct AttnArgs {
+  const float *qk;      // [qfull (nh x 2HDV: q | gate per head) | k (nkv x HDV)]
+  const float *v;       // nkv x HDV
+  const float *q_norm, *k_norm;
+  const double2 *rope;  // [ctx][nrp] (cos, sin) of the rotated pairs
+  float *q;             // nh x HDV, normed and rotated
+  float *kcache, *vcache;  // ctx x (nkv*HDV)
+  float *scores;        // nh x ctx
+  float *gated;         // nh x HDV
+  const int *pos;
+  int nh, nkv, n_rot, nrp, ctx;
+  float eps, kq_scale;
+};
+
+// q/k head norms, IMROPE (kernels.rs:381-400) and the cache write. One CTA
+// per q head and per kv head.
+template <int HDV>
+__global__ void __launch_bounds__(HDV) attn_pre_kernel(AttnArgs a) {
+  __shared__ double red[2 * HDV / 32];
+  __shared__ float sx[HDV];
+  __shared__ float s_mean;
+  const int b = blockIdx.x, j = threadIdx.x;
+  const bool isq = b < a.nh;
+  const int hh = isq ? b : b - a.nh;
+  const int pos = *a.pos;
+  const float *src = isq ? a.qk + (size_t)hh * 2 * HDV : a.qk + (size_t)a.nh * 2 * HDV + (size_t)hh * HDV;
+  const float *wn = isq ? a.q_norm : a.k_norm;
+  const float x = src[j];
+  sx[j] = x;
+  double S = (double)__fmul_rn(x, x), dummy = 0.0;
+  block_sum2<HDV>(S, dummy, red);
+  float mean;
+  const MeanOf f{HDV};
+  if (!resolve_sum(S, S, HDV, f, &mean)) {
+    __syncthreads();
+    if (j == 0) {
+      double s = 0.0;
+#pragma unroll 1
+      for (int i = 0; i < HDV; i++) s = __dadd_rn(s, (double)__fmul_rn(sx[i], sx[i]));
+      s_mean = f(s);
+    }
+    __syncthreads();
+    mean = s_mean;
+  }
+  const float scale = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(mean, a.eps)));
+  const float xn = __fmul_rn(__fmul_rn(x, scale), wn[j]);
+  __syncthreads();
+  sx[j] = xn;
+  __syncthreads();
+  float out = xn;
+  const int half = a.n_rot / 2;
+  if (j < a.n_rot) {
+    const int ic = j < half ? j : j - half;
+    if (ic % 3 == 0) {
+      const double2 cs = a.rope[(size_t)pos * a.nrp + ic / 3];
+      const double x0 = sx[ic], x1 = sx[ic + half];
+      out = j < half ? (float)fma(cs.x, x0, -__dmul_rn(cs.y, x1)) : (float)fma(cs.y, x0, __dmul_rn(cs.x, x1));
+    }
+  }
+  const size_t kvlen = (size_t)a.nkv * HDV;
+  if (isq) {
+    a.q[(size_t)hh * HDV + j] = out;
+  } else {
+    a.kcache[(size_t)pos * kvlen + (size_t)hh * HDV + j] = out;
+    a.vcache[(size_t)pos * kvlen + (size_t)hh * HDV + j] = a.v[(size_t)hh * HDV + j];
+  }
+}
+
+// scores[h][p] = dot_f32(q_h, k_p) as f32 (quants.rs:106-114): exact f64
+// products summed by the pairwise tree, which for HDV = 32 * E (E a power of
+// two) is lane-local subtrees over E contiguous elements and then a butterfly.
+// One warp per position, all q heads of the kv group.
+template <int HDV>
+__global__ void __launch_bounds__(256) attn_scores_kernel(AttnArgs a) {
+  constexpr int E = HDV / 32;
+  extern __shared__ float qsm[];  // G x HDV
+  const int kvh = blockIdx.x, G = a.nh / a.nkv;
+  const int n_ctx = *a.pos + 1;
+  const int p0 = blockIdx.y * 32;
+  if (p0 >= n_ctx) return;
+  for (int i = threadIdx.x; i < G * HDV; i += 256) qsm[i] = a.q[(size_t)(kvh * G) * HDV + i];
+  __syncthreads();
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const size_t kvlen = (size_t)a.nkv * HDV;
+  for (int p = p0 + warp; p < min(p0 + 32, n_ctx); p += 8) {
+    const float *kr = a.kcache + (size_t)p * kvlen + (size_t)kvh * HDV + lane * E;
+    float kv[E];
+#pragma unroll
+    for (int t = 0; t < E; t += 4) {
+      float4 v4 = *reinterpret_cast<const float4 *>(kr + t);
+      kv[t] = v4.x, kv[t + 1] = v4.y, kv[t + 2] = v4.z, kv[t + 3] = v4.w;
+    }
+    for (int g = 0; g < G; g++) {
+      double pr[E];
+#pragma unroll
+      for (int t = 0; t < E; t++) pr[t] = __dmul_rn((double)qsm[g * HDV + lane * E + t], (double)kv[t]);
+#pragma unroll
+      for (int w = 1; w < E; w <<= 1)
+#pragma unroll
+        for (int t = 0; t < E; t += 2 * w) pr[t] = __dadd_rn(pr[t], pr[t + w]);
+      double s = pr[0];
+#pragma unroll
+      for (int o = 1; o < 32; o <<= 1) s = __dadd_rn(s, __shfl_xor_sync(~0u, s, o));
+      if (lane == 0) a.scores[(size_t)(kvh * G + g) * a.ctx + p] = (float)s;
+    }
+  }
+}
+
+// softmax (kernels.rs:157-168) of head h's scores, then the f64 value sum
+// over positions (qwen35_forward.rs:660-672) for 32 columns, times
+// sigmoid(gate). Grid (nh, HDV/32), 256 threads.
+template <int HDV>
+__global__ void __launch_bounds__(256) attn_out_kernel(AttnArgs a) {
+  extern __shared__ __align__(16) uint8_t sm[];
+  __shared__ float redf[8];
+  __shared__ double part[2][8][32];
+  const int h = blockIdx.x, tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int kvh = h / (a.nh / a.nkv);
+  const int n = *a.pos + 1;
+  float *e = reinterpret_cast<float *>(sm);
+  double *l0 = reinterpret_cast<double *>(sm + round_up((size_t)a.ctx * 4, 16));
+  double *l1 = l0 + (a.ctx + 1) / 2;
+  const float *sc = a.scores + (size_t)h * a.ctx;
+
+  float m = -INFINITY;
+  for (int p = tid; p < n; p += 256) m = fmaxf(m, sc[p]);
+  m = block_max<256>(m, redf);
+  for (int p = tid; p < n; p += 256) e[p] = exp_cr(__fmul_rn(__fsub_rn(sc[p], m), a.kq_scale));
+  __syncthreads();
+  // pairwise_sum_f64 (kernels.rs:24-38): pairs (2i, 2i+1) per level, odd tail carried
+  int len = (n + 1) / 2;
+  for (int i = tid; i < len; i += 256)
+    l0[i] = 2 * i + 1 < n ? __dadd_rn((double)e[2 * i], (double)e[2 * i + 1]) : (double)e[2 * i];
+  __syncthreads();
+  double *cur = l0, *nxt = l1;
+  while (len > 1) {
+    const int nl = (len + 1) / 2;
+    for (int i = tid; i < nl; i += 256) nxt[i] = 2 * i + 1 < len ? __dadd_rn(cur[2 * i], cur[2 * i + 1]) : cur[2 * i];
+    __syncthreads();
+    double *t = cur;
+    cur = nxt;
+    nxt = t;
+    len = nl;
+  }
+  const double sum = cur[0];
+  __syncthreads();
+  for (int p = tid; p < n; p += 256) e[p] = (float)__ddiv_rn((double)e[p], sum);
+  __syncthreads();
+
+  const int c = blockIdx.y * 32 + lane;
+  const size_t kvlen = (size_t)a.nkv * HDV;
+  const float *vcol = a.vcache + (size_t)kvh * HDV + c;
+  double S = 0.0, A = 0.0;
+  for (int p = warp; p < n; p += 8) {
+    const double t = __dmul_rn((double)e[p], (double)vcol[(size_t)p * kvlen]);
+    S += t;
+    A += fabs(t);
+  }
+  part[0][warp][lane] = S;
+  part[1][warp][lane] = A;
+  __syncthreads();
+  if (warp == 0) {
+    S = 0.0;
+    A = 0.0;
+#pragma unroll
+    for (int w = 0; w < 8; w++) {
+      S += part[0][w][lane];
+      A += part[1][w][lane];
+    }
+    float attn;
+    if (!resolve_sum(S, A, n, ToF32{}, &attn)) {
+      double s = 0.0;
+#pragma unroll 1
+      for (int p = 0; p < n; p++) s = __dadd_rn(s, __dmul_rn((double)e[p], (double)vcol[(size_t)p * kvlen]));
+      attn = (float)s;
+    }
+    const float gate = a.qk[(size_t)h * 2 * HDV + HDV + c];
+    a.gated[(size_t)h * HDV + c] = __fmul_rn(attn, sigmoid_f(gate));
+  }
+}
+
+// token bookkeeping at the end of a step
+__global__ void step_end_kernel(const uint32_t *cur, uint32_t *hist, int *counter, int *pos) {
+  hist[*counter] = *cur;
+  *counter += 1;
+  *pos += 1;
+}
+
+}  // namespace
+}  // namespace unltd
+
+// ===========================================================================
+// Host side: model (weights) and session (state + graph).
+// ===========================================================================
+using namespace unltd;
+
+namespace {
+
+struct Derived {
+  int n, nff, nh, nkv, hdv, n_rot, K, nqk, hd, nv, dconv, kvlen, vocab, n_layer, interval, nrp;
+  float eps, kq_scale;
+  double theta_scale;
+};
+
+struct Part {
+  std::string name;
+  size_t dim_in, dim_out;
+  std::vector<int> dtypes;  // allowed
+};
+
+// One projection: consecutive same-dtype parts merged into one weight each.
+struct Proj {
+  std::vector<unltd_weight_s *> w;
+  std::vector<size_t> off;  // output offset of each merged weight
+  size_t rows = 0;
+};
+
+struct Layer {
+  bool attn = false;
+  int slot = 0;  // index among layers of the same kind
+  float *attn_norm = nullptr, *post_norm = nullptr;
+  Proj in;        // recurrent: qkv|z|beta|alpha; attention: q|k|v
+  unltd_weight_s *out = nullptr;  // ssm_out / attn_output
+  Proj gate_up;
+  unltd_weight_s *down = nullptr;
+  float *convw = nullptr, *dt_bias = nullptr, *ssm_a = nullptr, *ssm_norm = nullptr;  // recurrent
+  float *q_norm = nullptr, *k_norm = nullptr;                                        // attention
+};
+
+struct Staged {
+  int dtype = 0;
+  unltd_weight_s *w = nullptr;
+  float *f = nullptr;
+};
+
+}  // namespace
+
+struct unltd_qwen35_s {
+  unltd_ctx ctx = nullptr;
+  unltd_qwen35_config cfg{};
+  Derived d{};
+  std::map<std::string, Staged> staged;
+  bool finalized = false;
+  std::vector<Layer> layers;
+  unltd_weight_s *embd = nullptr, *output = nullptr;
+  float *out_norm = nullptr;
+  std::vector<void *> f32_bufs;
+  int n_recr = 0, n_attn = 0;
+  size_t proj_rows = 0;
+};
+
+struct unltd_qwen35_session_s {
+  unltd_qwen35 m = nullptr;
+  unltd_ctx ctx = nullptr;  // own context: stream, GEMV scratch, argmax state
+  int ctx_len = 0;
+  int host_pos = 0;
+  // activations
+  float *X = nullptr, *XN = nullptr, *R = nullptr, *T = nullptr, *F = nullptr, *P = nullptr;
+  float *proj = nullptr, *Y = nullptr, *FF = nullptr, *SW = nullptr;
+  float *q = nullptr, *scores = nullptr, *gated = nullptr, *logits = nullptr;
+  double2 *rope = nullptr;
+  uint32_t *cur_token = nullptr, *hist = nullptr, *feed = nullptr;
+  int *counter = nullptr, *pos = nullptr;
+  std::vector<float *> ring, state, kc, vc;
+  std::vector<void *> bufs;
+  cudaGraphExec_t graph = nullptr;
+  bool graph_tried = false;
+  int64_t launches_per_step = 0;
+};
+
+namespace {
+
+int32_t derive(const unltd_qwen35_config &c, Derived *d) {
+  auto bad = [](const std::string &m) { return set_error(UNLTD_ERR_INVALID_ARG, "qwen35 config: " + m); };
+  auto unsup = [](const std::string &m) { return set_error(UNLTD_ERR_UNSUPPORTED, "qwen35 config: " + m); };
+  // qwen35.rs:174-252
+  if (c.n_layer < 1) return bad("block_count = 0");
+  if (c.n_embd <= 0 || c.n_ff <= 0) return bad("zero embedding/FFN dims");
+  if (c.n_head < 1) return bad("attention.head_count = 0");
+  if (c.n_head_kv < 1 || c.n_head % c.n_head_kv) return bad("invalid GQA");
+  if (c.n_head * c.head_dim != c.n_embd) return bad("head_count * key_length != n_embd");
+  if (c.head_dim != c.head_dim_v) return bad("key_length != value_length");
+  if (c.n_rot % 2 || c.n_rot > c.head_dim || c.n_rot < 0) return bad("n_rot must be even and <= head_dim");
+  if (!(c.freq_base > 0.0f)) return bad("rope.freq_base <= 0");
+  if (!(c.rms_eps > 0.0f)) return bad("layer_norm_rms_epsilon <= 0");
+  if (c.conv_kernel < 2) return bad("ssm.conv_kernel < 2");
+  if (c.group_count < 1) return bad("ssm.group_count = 0");
+  if (c.d_inner <= 0 || c.d_inner % (2 * c.group_count)) return bad("d_inner not a multiple of 2*group_count");
+  if (c.time_step_rank < 1) return bad("ssm.time_step_rank = 0");
+  const int hd = c.d_inner / (2 * c.group_count);
+  if (c.state_size != hd) return bad("state_size != linear head dim");
+  if (c.full_attn_interval < 1) return bad("full_attention_interval = 0");
+  if (c.vocab < 1) return bad("vocab = 0");
+  // what the kernels of this library cover
+  if (c.d_inner != c.n_embd) return unsup("d_inner != n_embd (the recurrent output feeds an n_embd x n_embd ssm_out)");
+  if (hd != 128) return unsup("linear head dim must be 128");
+  if (c.head_dim != 256 && c.head_dim != 128) return unsup("head_dim must be 128 or 256");
+  if (c.n_embd % 256 || c.n_ff % 256) return unsup("n_embd and n_ff must be multiples of 256");
+  if (c.conv_kernel > 16) return unsup("conv_kernel > 16");
+  d->n = c.n_embd;
+  d->nff = c.n_ff;
+  d->nh = c.n_head;
+  d->nkv = c.n_head_kv;
+  d->hdv = c.head_dim;
+  d->n_rot = c.n_rot;
+  d->K = c.conv_kernel;
+  d->nqk = c.group_count;
+  d->hd = hd;
+  d->nv = c.d_inner / hd;
+  d->dconv = 2 * c.d_inner;
+  d->kvlen = c.n_head_kv * c.head_dim;
+  d->vocab = c.vocab;
+  d->n_layer = c.n_layer;
+  d->interval = c.full_attn_interval;
+  d->nrp = (c.n_rot / 2 + 2) / 3;
+  d->eps = c.rms_eps;
+  d->kq_scale = 1.0f / std::sqrt((float)c.head_dim);
+  d->theta_scale = (double)std::pow(c.freq_base, -2.0f / (float)c.n_rot);
+  return UNLTD_OK;
+}
+
+bool is_attn(const Derived &d, int il) { return (il + 1) % d.interval == 0; }
+
+// Expected tensors (qwen35_forward.rs:139-221, min_forward.rs): name -> shape, dtypes.
+std::vector<Part> expected(const Derived &d) {
+  std::vector<Part> v;
+  const std::vector<int> f32{F32}, q4{Q4K}, q46{Q4K, Q6K};
+  v.push_back({"token_embd.weight", (size_t)d.n, (size_t)d.vocab, q4});
+  v.push_back({"output_norm.weight", (size_t)d.n, 1, f32});
+  v.push_back({"output.weight", (size_t)d.n, (size_t)d.vocab, q46});
+  for (int il = 0; il < d.n_layer; il++) {
+    const std::string p = "blk." + std::to_string(il) + ".";
+    v.push_back({p + "attn_norm.weight", (size_t)d.n, 1, f32});
+    v.push_back({p + "post_attention_norm.weight", (size_t)d.n, 1, f32});
+    v.push_back({p + "ffn_gate.weight", (size_t)d.n, (size_t)d.nff, q4});
+    v.push_back({p + "ffn_up.weight", (size_t)d.n, (size_t)d.nff, q4});
+    v.push_back({p + "ffn_down.weight", (size_t)d.nff, (size_t)d.n, q46});
+    if (is_attn(d, il)) {
+      v.push_back({p + "attn_q.weight", (size_t)d.n, (size_t)(2 * d.n), q4});
+      v.push_back({p + "attn_q_norm.weight", (size_t)d.hdv, 1, f32});
+      v.push_back({p + "attn_k.weight", (size_t)d.n, (size_t)d.kvlen, q4});
+      v.push_back({p + "attn_k_norm.weight", (size_t)d.hdv, 1, f32});
+      v.push_back({p + "attn_v.weight", (size_t)d.n, (size_t)d.kvlen, q46});
+      v.push_back({p + "attn_output.weight", (size_t)d.n, (size_t)d.n, q4});
+    } else {
+      v.push_back({p + "attn_qkv.weight", (size_t)d.n, (size_t)d.dconv, q46});
+      v.push_back({p + "attn_gate.weight", (size_t)d.n, (size_t)d.n, q4});
+      v.push_back({p + "ssm_conv1d.weight", (size_t)(d.K * d.dconv), 1, f32});
+      v.push_back({p + "ssm_dt.bias", (size_t)d.nv, 1, f32});
+      v.push_back({p + "ssm_a", (size_t)d.nv, 1, f32});
+      v.push_back({p + "ssm_beta.weight", (size_t)d.n, (size_t)d.nv, q4});
+      v.push_back({p + "ssm_alpha.weight", (size_t)d.n, (size_t)d.nv, q4});
+      v.push_back({p + "ssm_norm.weight", (size_t)d.hd, 1, f32});
+      v.push_back({p + "ssm_out.weight", (size_t)d.n, (size_t)d.n, q4});
+    }
+  }
+  return v;
+}
+
+const char *dtype_str(int t) {
+  switch (t) {
+    case F32: return "F32";
+    case Q4K: return "Q4_K";
+    case Q6K: return "Q6_K";
+    case Q8_0: return "Q8_0";
+    default: return "other";
+  }
+}
+
+// Merge row-concatenated weights of one dtype into one device allocation.
+int32_t merge(unltd_ctx ctx, const std::vector<unltd_weight_s *> &parts, unltd_weight_s **out) {
+  if (parts.size() == 1) {
+    *out = parts[0];
+    return UNLTD_OK;
+  }
+  unltd_weight_s *w = new unltd_weight_s(*parts[0]);
+  size_t rows = 0;
+  for (auto *p : parts) rows += p->dim_out;
+  w->dim_out = rows;
+  cudaError_t e = cudaMalloc(&w->dev, std::max<size_t>(rows * w->row_stride, 16));
+  if (e != cudaSuccess) {
+    delete w;
+    return cuda_error(e, "qwen35: merged weight alloc");
+  }
+  size_t r = 0;
+  for (auto *p : parts) {
+    e = cudaMemcpyAsync(w->dev + r * w->row_stride, p->dev, p->dim_out * p->row_stride, cudaMemcpyDeviceToDevice,
+                        ctx->stream);
+    if (e != cudaSuccess) break;
+    r += p->dim_out;
+  }
+  if (e == cudaSuccess) e = cudaStreamSynchronize(ctx->stream);
+  if (e != cudaSuccess) {
+    cudaFree(w->dev);
+    delete w;
+    return cuda_error(e, "qwen35: merge copy");
+  }
+  for (auto *p : parts) unltd_weight_free(p);
+  *out = w;
+  return UNLTD_OK;
+}
+
+int32_t build_proj(unltd_qwen35 m, const std::vector<std::string> &names, Proj *pr) {
+  std::vector<unltd_weight_s *> run;
+  size_t off = 0, run_off = 0;
+  auto flush = [&]() -> int32_t {
+    if (run.empty()) return UNLTD_OK;
+    unltd_weight_s *w = nullptr;
+    int32_t rc = merge(m->ctx, run, &w);
+    if (rc) return rc;
+    pr->w.push_back(w);
+    pr->off.push_back(run_off);
+    run.clear();
+    return UNLTD_OK;
+  };
+  for (const auto &nm : names) {
+    Staged &s = m->staged.at(nm);
+    if (!run.empty() && run.back()->dtype != s.w->dtype) {
+      if (int32_t rc = flush()) return rc;
+    }
+    if (run.empty()) run_off = off;
+    run.push_back(s.w);
+    off += s.w->dim_out;
+    s.w = nullptr;
+  }
+  if (int32_t rc = flush()) return rc;
+  pr->rows = off;
+  return UNLTD_OK;
+}
+
+template <class T>
+int32_t dalloc(std::vector<void *> &bufs, T **p, size_t n, const char *what) {
+  cudaError_t e = cudaMalloc(reinterpret_cast<void **>(p), std::max<size_t>(n * sizeof(T), 16));
+  if (e != cudaSuccess) return cuda_error(e, what);
+  bufs.push_back(*p);
+  return UNLTD_OK;
+}
+
+int64_t launch_gemv(unltd_ctx c, const unltd_weight_s *w, const float *x, float *y, int32_t *rc) {
+  GemvArgs g{w, x, y, MODE_Q8K, nullptr, nullptr, nullptr};
+  if (!*rc) *rc = gemv_launch(c, g);
+  return 2;
+}
+
+// Enqueue one decode step on the session's stream.
+int32_t enqueue_step(unltd_qwen35_session s) {
+  unltd_qwen35 m = s->m;
+  const Derived &d = m->d;
+  cudaStream_t st = s->ctx->stream;
+  int32_t rc = UNLTD_OK;
+  int64_t nl = 0;
+  auto chk = [&](const char *what) {
+    if (!rc) rc = cuda_error(cudaGetLastError(), what);
+    nl++;
+  };
+  auto proj = [&](const Proj &p, const float *x) {
+    for (size_t i = 0; i < p.w.size(); i++) nl += launch_gemv(s->ctx, p.w[i], x, s->proj + p.off[i], &rc);
+  };
+  embed_q4k_kernel<<<d.n / 256, 256, 0, st>>>(m->embd->dev, m->embd->row_stride, m->embd->nb, s->cur_token,
+                                                (uint32_t)d.vocab, s->X, d.n, s->ctx->err);
+  chk("embed");
+  for (int il = 0; il < d.n_layer; il++) {
+    const Layer &L = m->layers[il];
+    // layer input = l_out of the previous layer (residual + ffn), fused into the norm
+    if (il == 0) add_rmsnorm_kernel<1024><<<1, 1024, 0, st>>>(s->X, nullptr, nullptr, L.attn_norm, s->XN, d.n, d.eps);
+    else add_rmsnorm_kernel<1024><<<1, 1024, 0, st>>>(s->R, s->F, s->X, L.attn_norm, s->XN, d.n, d.eps);
+    chk("attn_norm");
+    proj(L.in, s->XN);
+    if (!L.attn) {
+      RecrArgs a;
+      a.proj = s->proj;
+      a.ring = s->ring[L.slot];
+      a.convw = L.convw;
+      a.dt_bias = L.dt_bias;
+      a.ssm_a = L.ssm_a;
+      a.ssm_norm = L.ssm_norm;
+      a.state = s->state[L.slot];
+      a.y = s->Y;
+      a.pos = s->pos;
+      a.K = d.K;
+      a.nqk = d.nqk;
+      a.nv = d.nv;
+      a.dconv = d.dconv;
+      a.z_off = d.dconv;
+      a.beta_off = d.dconv + d.n;
+      a.alpha_off = d.dconv + d.n + d.nv;
+      a.eps = d.eps;
+      recr_mid_kernel<128><<<d.nv, 128, 0, st>>>(a);
+      chk("recr_mid");
+      nl += launch_gemv(s->ctx, L.out, s->Y, s->T, &rc);
+    } else {
+      AttnArgs a;
+      a.qk = s->proj;
+      a.v = s->proj + 2 * d.n + d.kvlen;
+      a.q_norm = L.q_norm;
+      a.k_norm = L.k_norm;
+      a.rope = s->rope;
+      a.q = s->q;
+      a.kcache = s->kc[L.slot];
+      a.vcache = s->vc[L.slot];
+      a.scores = s->scores;
+      a.gated = s->gated;
+      a.pos = s->pos;
+      a.nh = d.nh;
+      a.nkv = d.nkv;
+      a.n_rot = d.n_rot;
+      a.nrp = d.nrp;
+      a.ctx = s->ctx_len;
+      a.eps = d.eps;
+      a.kq_scale = d.kq_scale;
+      const size_t out_smem = round_up((size_t)s->ctx_len * 4, 16) + (size_t)((s->ctx_len + 1) / 2 + (s->ctx_len + 3) / 4 + 1) * 8;
+      const dim3 sg(d.nkv, (s->ctx_len + 31) / 32), og(d.nh, d.hdv / 32);
+      const size_t q_smem = (size_t)(d.nh / d.nkv) * d.hdv * 4;
+      if (d.hdv == 256) {
+        attn_pre_kernel<256><<<d.nh + d.nkv, 256, 0, st>>>(a);
+        chk("attn_pre");
+        attn_scores_kernel<256><<<sg, 256, q_smem, st>>>(a);
+        chk("attn_scores");
+        attn_out_kernel<256><<<og, 256, out_smem, st>>>(a);
+        chk("attn_out");
+      } else {
+        attn_pre_kernel<128><<<d.nh + d.nkv, 128, 0, st>>>(a);
+        chk("attn_pre");
+        attn_scores_kernel<128><<<sg, 256, q_smem, st>>>(a);
+        chk("attn_scores");
+        attn_out_kernel<128><<<og, 256, out_smem, st>>>(a);
+        chk("attn_out");
+      }
+      nl += launch_gemv(s->ctx, L.out, s->gated, s->T, &rc);
+    }
+    // residual = x_in + attn_out; p = rmsnorm(residual, post_attention_norm)
+    add_rmsnorm_kernel<1024><<<1, 1024, 0, st>>>(s->X, s->T, s->R, L.post_norm, s->P, d.n, d.eps);
+    chk("post_norm");
+    for (size_t i = 0; i < L.gate_up.w.size(); i++)
+      nl += launch_gemv(s->ctx, L.gate_up.w[i], s->P, s->FF + L.gate_up.off[i], &rc);
+    swiglu_kernel<<<(d.nff + 255) / 256, 256, 0, st>>>(s->FF, s->FF + d.nff, s->SW, d.nff);
+    chk("swiglu");
+    nl += launch_gemv(s->ctx, L.down, s->SW, s->F, &rc);
+  }
+  // l_out of the last layer -> output norm -> LM head + greedy argmax
+  add_rmsnorm_kernel<1024><<<1, 1024, 0, st>>>(s->R, s->F, s->X, m->out_norm, s->XN, d.n, d.eps);
+  chk("output_norm");
+  {
+    GemvArgs g{m->output, s->XN, s->logits, MODE_Q8K, s->ctx->argmax_key, s->ctx->argmax_done, s->cur_token};
+    if (!rc) rc = gemv_launch(s->ctx, g);
+    nl += 2;
+  }
+  step_end_kernel<<<1, 1, 0, st>>>(s->cur_token, s->hist, s->counter, s->pos);
+  chk("step_end");
+  s->launches_per_step = nl;
+  return rc;
+}
+
+int32_t run_step(unltd_qwen35_session s) {
+  if (!s->graph_tried) {
+    s->graph_tried = true;
+    const char *env = getenv("UNLTD_NO_GRAPH");
+    if (!(env && env[0] == '1')) {
+      cudaStream_t st = s->ctx->stream;
+      cudaGraph_t g = nullptr;
+      cudaError_t e = cudaStreamBeginCapture(st, cudaStreamCaptureModeThreadLocal);
+      int32_t rc = UNLTD_OK;
+      if (e == cudaSuccess) {
+        rc = enqueue_step(s);
+        e = cudaStreamEndCapture(st, &g);
+      }
+      if (e == cudaSuccess && rc == UNLTD_OK) e = cudaGraphInstantiate(&s->graph, g, 0);
+      if (g) cudaGraphDestroy(g);
+      if (e != cudaSuccess || rc != UNLTD_OK) {
+        s->graph = nullptr;
+        cudaGetLastError();  // capture failure: run uncaptured launches instead
+      }
+    }
+  }
+  if (s->graph) {
+    s->ctx->launches += s->launches_per_step;
+    return cuda_error(cudaGraphLaunch(s->graph, s->ctx->stream), "qwen35: graph launch");
+  }
+  return enqueue_step(s);
+}
+
+}  // namespace
+
+extern "C" {
+
+int32_t unltd_qwen35_create(unltd_ctx ctx, const unltd_qwen35_config *cfg, unltd_qwen35 *out) {
+  if (!ctx || !cfg || !out) return set_error(UNLTD_ERR_INVALID_ARG, "qwen35_create: NULL argument");
+  *out = nullptr;
+  Derived d;
+  if (int32_t rc = derive(*cfg, &d)) return rc;
+  unltd_qwen35 m = new unltd_qwen35_s();
+  m->ctx = ctx;
+  m->cfg = *cfg;
+  m->d = d;
+  *out = m;
+  return UNLTD_OK;
+}
+
+int32_t unltd_qwen35_set_tensor(unltd_qwen35 m, const char *name, const void *host, size_t nbytes, int32_t dtype) {
+  if (!m || !name || !host) return set_error(UNLTD_ERR_INVALID_ARG, "qwen35_set_tensor: NULL argument");
+  if (m->finalized) return set_error(UNLTD_ERR_INVALID_ARG, "qwen35_set_tensor: model already finalized");
+  const std::vector<Part> parts = expected(m->d);
+  const Part *pt = nullptr;
+  for (const auto &p : parts)
+    if (p.name == name) pt = &p;
+  if (!pt) return set_error(UNLTD_ERR_INVALID_ARG, std::string("qwen35_set_tensor: unexpected tensor '") + name + "'");
+  bool ok = false;
+  for (int t : pt->dtypes) ok |= t == dtype;
+  if (!ok)
+    return set_error(UNLTD_ERR_UNSUPPORTED,
+                     std::string("tensor '") + name + "': dtype " + dtype_str(dtype) + " not accepted");
+  const size_t want = gguf_row_bytes(dtype, pt->dim_in) * pt->dim_out;
+  if (nbytes != want)
+    return set_error(UNLTD_ERR_LENGTH, std::string("tensor '") + name + "': " + std::to_string(nbytes) +
+                                           " bytes, expected " + std::to_string(want));
+  CtxGuard g(m->ctx->device);
+  Staged s;
+  s.dtype = dtype;
+  auto it = m->staged.find(name);
+  if (it != m->staged.end()) {
+    if (it->second.w) unltd_weight_free(it->second.w);
+    if (it->second.f) cudaFree(it->second.f);
+    m->staged.erase(it);
+  }
+  if (dtype == F32) {
+    cudaError_t e = cudaMalloc(&s.f, nbytes);
+    if (e == cudaSuccess) e = cudaMemcpy(s.f, host, nbytes, cudaMemcpyHostToDevice);
+    if (e != cudaSuccess) return cuda_error(e, "qwen35_set_tensor");
+  } else {
+    int32_t rc = unltd_weight_upload(m->ctx, host, nbytes, dtype, pt->dim_in, pt->dim_out, &s.w);
+    if (rc) return rc;
+  }
+  m->staged[name] = s;
+  return UNLTD_OK;
+}
+
+int32_t unltd_qwen35_finalize(unltd_qwen35 m) {
+  if (!m) return set_error(UNLTD_ERR_INVALID_ARG, "qwen35_finalize: NULL model");
+  if (m->finalized) return UNLTD_OK;
+  const Derived &d = m->d;
+  for (const auto &p : expected(d))
+    if (!m->staged.count(p.name)) return set_error(UNLTD_ERR_INVALID_ARG, "missing tensor '" + p.name + "'");
+  CtxGuard g(m->ctx->device);
+  auto take_f = [&](const std::string &nm) {
+    float *f = m->staged.at(nm).f;
+    m->staged.at(nm).f = nullptr;
+    m->f32_bufs.push_back(f);
+    return f;
+  };
+  auto take_w = [&](const std::string &nm) {
+    unltd_weight_s *w = m->staged.at(nm).w;
+    m->staged.at(nm).w = nullptr;
+    return w;
+  };
+  m->embd = take_w("token_embd.weight");
+  m->output = take_w("output.weight");
+  m->out_norm = take_f("output_norm.weight");
+  m->layers.resize(d.n_layer);
+  size_t proj_rows = 0;
+  for (int il = 0; il < d.n_layer; il++) {
+    Layer &L = m->layers[il];
+    const std::string p = "blk." + std::to_string(il) + ".";
+    L.attn = is_attn(d, il);
+    L.slot = L.attn ? m->n_attn++ : m->n_recr++;
+    L.attn_norm = take_f(p + "attn_norm.weight");
+    L.post_norm = take_f(p + "post_attention_norm.weight");
+    int32_t rc;
+    if (L.attn) {
+      rc = build_proj(m, {p + "attn_q.weight", p + "attn_k.weight", p + "attn_v.weight"}, &L.in);
+      L.q_norm = take_f(p + "attn_q_norm.weight");
+      L.k_norm = take_f(p + "attn_k_norm.weight");
+      L.out = take_w(p + "attn_output.weight");
+    } else {
+      rc = build_proj(m, {p + "attn_qkv.weight", p + "attn_gate.weight", p + "ssm_beta.weight", p + "ssm_alpha.weight"},
+                      &L.in);
+      L.convw = take_f(p + "ssm_conv1d.weight");
+      L.dt_bias = take_f(p + "ssm_dt.bias");
+      L.ssm_a = take_f(p + "ssm_a");
+      L.ssm_norm = take_f(p + "ssm_norm.weight");
+      L.out = take_w(p + "ssm_out.weight");
+    }
+    if (rc) return rc;
+    if ((rc = build_proj(m, {p + "ffn_gate.weight", p + "ffn_up.weight"}, &L.gate_up))) return rc;
+    L.down = take_w(p + "ffn_down.weight");
+    proj_rows = std::max(proj_rows, L.in.rows);
+  }
+  m->proj_rows = proj_rows;
+  m->staged.clear();
+  m->finalized = true;
+  return UNLTD_OK;
+}
+
+int32_t unltd_qwen35_destroy(unltd_qwen35 m) {
+  if (!m) return UNLTD_OK;
+  CtxGuard g(m->ctx->device);
+  cudaStreamSynchronize(m->ctx->stream);
+  for (auto &kv : m->staged) {
+    if (kv.second.w) unltd_weight_free(kv.second.w);
+    if (kv.second.f) cudaFree(kv.second.f);
+  }
+  for (auto &L : m->layers) {
+    for (auto *w : L.in.w) unltd_weight_free(w);
+    for (auto *w : L.gate_up.w) unltd_weight_free(w);
+    unltd_weight_free(L.out);
+    unltd_weight_free(L.down);
+  }
+  unltd_weight_free(m->embd);
+  unltd_weight_free(m->output);
+  for (void *p : m->f32_bufs) cudaFree(p);
+  delete m;
+  return UNLTD_OK;
+}
+
+int32_t unltd_qwen35_session_destroy(unltd_qwen35_session s);
+
+int32_t unltd_qwen35_session_create(unltd_qwen35 m, int32_t ctx_len, unltd_qwen35_session *out) {
+  if (!m || !out) return set_error(UNLTD_ERR_INVALID_ARG, "qwen35_session_create: NULL argument");
+  *out = nullptr;
+  if (!m->finalized) {
+    if (int32_t rc = unltd_qwen35_finalize(m)) return rc;
+  }
+  if (ctx_len < 1 || ctx_len > 16384)
+    return set_error(UNLTD_ERR_UNSUPPORTED, "qwen35_session_create: ctx must be in [1, 16384]");
+  const Derived &d = m->d;
+  unltd_qwen35_session s = new unltd_qwen35_session_s();
+  s->m = m;
+  s->ctx_len = ctx_len;
+  int32_t rc = unltd_ctx_create(m->ctx->device, &s->ctx);
+  if (rc) {
+    delete s;
+    return rc;
+  }
+  CtxGuard g(m->ctx->device);
+  auto &B = s->bufs;
+  const size_t n = d.n;
+  if (!rc) rc = dalloc(B, &s->X, n, "session");
+  if (!rc) rc = dalloc(B, &s->XN, n, "session");
+  if (!rc) rc = dalloc(B, &s->R, n, "session");
+  if (!rc) rc = dalloc(B, &s->T, n, "session");
+  if (!rc) rc = dalloc(B, &s->F, n, "session");
+  if (!rc) rc = dalloc(B, &s->P, n, "session");
+  if (!rc) rc = dalloc(B, &s->proj, m->proj_rows, "session");
+  if (!rc) rc = dalloc(B, &s->Y, n, "session");
+  if (!rc) rc = dalloc(B, &s->FF, 2 * (size_t)d.nff, "session");
+  if (!rc) rc = dalloc(B, &s->SW, (size_t)d.nff, "session");
+  if (!rc) rc = dalloc(B, &s->q, (size_t)d.nh * d.hdv, "session");
+  if (!rc) rc = dalloc(B, &s->scores, (size_t)d.nh * ctx_len, "session");
+  if (!rc) rc = dalloc(B, &s->gated, n, "session");
+  if (!rc) rc = dalloc(B, &s->logits, (size_t)d.vocab, "session");
+  if (!rc) rc = dalloc(B, &s->rope, (size_t)ctx_len * std::max(d.nrp, 1), "session");
+  if (!rc) rc = dalloc(B, &s->cur_token, 1, "session");
+  if (!rc) rc = dalloc(B, &s->hist, (size_t)ctx_len + 1, "session");
+  if (!rc) rc = dalloc(B, &s->feed, (size_t)ctx_len + 1, "session");
+  if (!rc) rc = dalloc(B, &s->counter, 1, "session");
+  if (!rc) rc = dalloc(B, &s->pos, 1, "session");
+  for (int i = 0; !rc && i < m->n_recr; i++) {
+    float *r = nullptr, *st = nullptr;
+    rc = dalloc(B, &r, (size_t)d.K * d.dconv, "session ring");
+    if (!rc) rc = dalloc(B, &st, (size_t)d.nv * d.hd * d.hd, "session state");
+    s->ring.push_back(r);
+    s->state.push_back(st);
+  }
+  for (int i = 0; !rc && i < m->n_attn; i++) {
+    float *k = nullptr, *v = nullptr;
+    rc = dalloc(B, &k, (size_t)ctx_len * d.kvlen, "session kv cache");
+    if (!rc) rc = dalloc(B, &v, (size_t)ctx_len * d.kvlen, "session kv cache");
+    s->kc.push_back(k);
+    s->vc.push_back(v);
+  }
+  // IMROPE angles (kernels.rs:381-400): angle = pos * theta^ic by repeated
+  // multiplication; (cos, sin) of the rotated pairs ic % 3 == 0, from libm.
+  if (!rc && d.nrp > 0) {
+    std::vector<double2> tab((size_t)ctx_len * d.nrp);
+    for (int p = 0; p < ctx_len; p++) {
+      double angle = (double)p;
+      for (int ic = 0; ic < d.n_rot / 2; ic++) {
+        if (ic % 3 == 0) tab[(size_t)p * d.nrp + ic / 3] = make_double2(std::cos(angle), std::sin(angle));
+        angle *= d.theta_scale;
+      }
+    }
+    rc = cuda_error(cudaMemcpy(s->rope, tab.data(), tab.size() * sizeof(double2), cudaMemcpyHostToDevice), "rope table");
+  }
+  for (void *p : B)
+    if (!rc) rc = cuda_error(cudaMemset(p, 0, 16), "session init");
+  for (int i = 0; !rc && i < m->n_recr; i++) {
+    rc = cuda_error(cudaMemset(s->ring[i], 0, (size_t)d.K * d.dconv * 4), "session init");
+    if (!rc) rc = cuda_error(cudaMemset(s->state[i], 0, (size_t)d.nv * d.hd * d.hd * 4), "session init");
+  }
+  // GEMV scratch sized for every projection before any graph capture
+  for (const auto &L : m->layers) {
+    for (auto *w : L.in.w)
+      if (!rc) rc = gemv_reserve(s->ctx, *w, MODE_Q8K);
+    for (auto *w : L.gate_up.w)
+      if (!rc) rc = gemv_reserve(s->ctx, *w, MODE_Q8K);
+    if (!rc) rc = gemv_reserve(s->ctx, *L.out, MODE_Q8K);
+    if (!rc) rc = gemv_reserve(s->ctx, *L.down, MODE_Q8K);
+  }
+  if (!rc) rc = gemv_reserve(s->ctx, *m->output, MODE_Q8K);
+  if (!rc) {
+    const size_t out_smem =
+        round_up((size_t)ctx_len * 4, 16) + (size_t)((ctx_len + 1) / 2 + (ctx_len + 3) / 4 + 1) * 8;
+    cudaError_t e = cudaFuncSetAttribute(attn_out_kernel<256>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)out_smem);
+    if (e == cudaSuccess)
+      e = cudaFuncSetAttribute(attn_out_kernel<128>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)out_smem);
+    rc = cuda_error(e, "attention smem");
+  }
+  if (!rc) rc = cuda_error(cudaDeviceSynchronize(), "session init");
+  if (rc) {
+    unltd_qwen35_session_destroy(s);
+    return rc;
+  }
+  *out = s;
+  return UNLTD_OK;
+}
+
+int32_t unltd_qwen35_session_destroy(unltd_qwen35_session s) {
+  if (!s) return UNLTD_OK;
+  CtxGuard g(s->m->ctx->device);
+  if (s->ctx) cudaStreamSynchronize(s->ctx->stream);
+  if (s->graph) cudaGraphExecDestroy(s->graph);
+  for (void *p : s->bufs) cudaFree(p);
+  if (s->ctx) unltd_ctx_destroy(s->ctx);
+  delete s;
+  return UNLTD_OK;
+}
+
+int32_t unltd_qwen35_session_set_state(unltd_qwen35_session s, int32_t position, const float *const *conv,
+                                       const float *const *gdn, const float *const *kcache,
+                                       const float *const *vcache) {
+  if (!s) return set_error(UNLTD_ERR_INVALID_ARG, "qwen35_set_state: NULL session");
+  if (position < 0 || position >= s->ctx_len)
+    return set_error(UNLTD_ERR_LENGTH, "qwen35_set_state: position outside the context");
+  const Derived &d = s->m->d;
+  CtxGuard g(s->m->ctx->device);
+  cudaStream_t st = s->ctx->stream;
+  cudaError_t e = cudaStreamSynchronize(st);
+  for (int i = 0; e == cudaSuccess && i < s->m->n_recr; i++) {
+    e = cudaMemset(s->ring[i], 0, (size_t)d.K * d.dconv * 4);
+    // row tau of the window (oldest first) lives in slot (position + tau) % K
+    for (int tau = 0; e == cudaSuccess && conv && conv[i] && tau < d.K - 1; tau++)
+      e = cudaMemcpy(s->ring[i] + (size_t)((position + tau) % d.K) * d.dconv, conv[i] + (size_t)tau * d.dconv,
+                     (size_t)d.dconv * 4, cudaMemcpyHostToDevice);
+    if (e == cudaSuccess) {
+      if (gdn && gdn[i]) e = cudaMemcpy(s->state[i], gdn[i], (size_t)d.nv * d.hd * d.hd * 4, cudaMemcpyHostToDevice);
+      else e = cudaMemset(s->state[i], 0, (size_t)d.nv * d.hd * d.hd * 4);
+    }
+  }
+  for (int i = 0; e == cudaSuccess && i < s->m->n_attn; i++) {
+    const size_t full = (size_t)s->ctx_len * d.kvlen * 4, part = (size_t)position * d.kvlen * 4;
+    e = cudaMemset(s->kc[i], 0, full);
+    if (e == cudaSuccess) e = cudaMemset(s->vc[i], 0, full);
+    if (e == cudaSuccess && part && kcache && kcache[i]) e = cudaMemcpy(s->kc[i], kcache[i], part, cudaMemcpyHostToDevice);
+    if (e == cudaSuccess && part && vcache && vcache[i]) e = cudaMemcpy(s->vc[i], vcache[i], part, cudaMemcpyHostToDevice);
+  }
+  if (e == cudaSuccess) e = cudaMemcpy(s->pos, &position, 4, cudaMemcpyHostToDevice);
+  if (e != cudaSuccess) return cuda_error(e, "qwen35_set_state");
+  s->host_pos = position;
+  return UNLTD_OK;
+}
+
+// Teacher-forced steps over `tokens` (a prompt); then *next_token = the
+// greedy token after the last one (may be NULL).
+int32_t unltd_qwen35_feed(unltd_qwen35_session s, const uint32_t *tokens, int32_t n, uint32_t *next_token) {
+  if (!s || (!tokens && n > 0)) return set_error(UNLTD_ERR_INVALID_ARG, "qwen35_feed: NULL argument");
+  if (n < 0 || n > s->ctx_len - s->host_pos)
+    return set_error(UNLTD_ERR_LENGTH, "qwen35_feed: context full (" + std::to_string(s->host_pos) + " of " +
+                                           std::to_string(s->ctx_len) + " positions used)");
+  for (int i = 0; i < n; i++)
+    if (tokens[i] >= (uint32_t)s->m->d.vocab)
+      return set_error(UNLTD_ERR_INVALID_ARG, "qwen35_feed: token " + std::to_string(tokens[i]) + " outside the vocab");
+  CtxGuard g(s->m->ctx->device);
+  cudaStream_t st = s->ctx->stream;
+  cudaError_t e = cudaSuccess;
+  if (n > 0) e = cudaMemcpyAsync(s->feed, tokens, (size_t)n * 4, cudaMemcpyHostToDevice, st);
+  if (e == cudaSuccess) e = cudaMemsetAsync(s->counter, 0, 4, st);
+  int32_t rc = cuda_error(e, "qwen35_feed");
+  for (int i = 0; !rc && i < n; i++) {
+    rc = cuda_error(cudaMemcpyAsync(s->cur_token, s->feed + i, 4, cudaMemcpyDeviceToDevice, st), "qwen35_feed");
+    if (!rc) rc = run_step(s);
+  }
+  if (!rc && next_token && n > 0) rc = cuda_error(cudaMemcpyAsync(next_token, s->cur_token, 4, cudaMemcpyDeviceToHost, st), "qwen35_feed");
+  if (!rc) rc = cuda_error(cudaStreamSynchronize(st), "qwen35_feed");
+  if (!rc) rc = check_device_error(s->ctx, "qwen35_feed");
+  if (!rc) s->host_pos += n;
+  return rc;
+}
+
+// Greedy decode: step 0 consumes `token`; step i > 0 consumes the token step
+// i-1 produced. tokens_out[i] = the greedy token of step i.
+int32_t unltd_qwen35_decode(unltd_qwen35_session s, uint32_t token, int32_t n_steps, uint32_t *tokens_out) {
+  if (!s || (!tokens_out && n_steps > 0)) return set_error(UNLTD_ERR_INVALID_ARG, "qwen35_decode: NULL argument");
+  if (n_steps < 0 || n_steps > s->ctx_len - s->host_pos)
+    return set_error(UNLTD_ERR_LENGTH, "qwen35_decode: context full (" + std::to_string(s->host_pos) + " of " +
+                                           std::to_string(s->ctx_len) + " positions used)");
+  if (token >= (uint32_t)s->m->d.vocab)
+    return set_error(UNLTD_ERR_INVALID_ARG, "qwen35_decode: token " + std::to_string(token) + " outside the vocab");
+  CtxGuard g(s->m->ctx->device);
+  cudaStream_t st = s->ctx->stream;
+  cudaError_t e = cudaMemcpyAsync(s->cur_token, &token, 4, cudaMemcpyHostToDevice, st);
+  if (e == cudaSuccess) e = cudaMemsetAsync(s->counter, 0, 4, st);
+  int32_t rc = cuda_error(e, "qwen35_decode");
+  for (int i = 0; !rc && i < n_steps; i++) rc = run_step(s);
+  if (!rc && n_steps > 0)
+    rc = cuda_error(cudaMemcpyAsync(tokens_out, s->hist, (size_t)n_steps * 4, cudaMemcpyDeviceToHost, st), "qwen35_decode");
+  if (!rc) rc = cuda_error(cudaStreamSynchronize(st), "qwen35_decode");
+  if (!rc) rc = check_device_error(s->ctx, "qwen35_decode");
+  if (!rc) s->host_pos += n_steps;
+  return rc;
+}
+
+int32_t unltd_qwen35_session_info(unltd_qwen35_session s, int32_t *position, void **stream, int64_t *launches_per_step) {
+  if (!s) return set_error(UNLTD_ERR_INVALID_ARG, "qwen35_session_info: NULL session");
+  if (position) *position = s->host_pos;
+  if (stream) *stream = s->ctx->stream;
+  if (launches_per_step) *launches_per_step = s->launches_per_step;
+  return UNLTD_OK;
+}
+
+// Copy the last step's logits (vocab floats) and/or hidden state (l_out of
+// the last layer, n_embd floats) to host buffers (NULL skips).
+int32_t unltd_qwen35_session_read(unltd_qwen35_session s, float *logits, float *hidden) {
+  if (!s) return set_error(UNLTD_ERR_INVALID_ARG, "qwen35_session_read: NULL session");
+  CtxGuard g(s->m->ctx->device);
+  cudaStream_t st = s->ctx->stream;
+  cudaError_t e = cudaStreamSynchronize(st);
+  if (e == cudaSuccess && logits) e = cudaMemcpy(logits, s->logits, (size_t)s->m->d.vocab * 4, cudaMemcpyDeviceToHost);
+  if (e == cudaSuccess && hidden) e = cudaMemcpy(hidden, s->X, (size_t)s->m->d.n * 4, cudaMemcpyDeviceToHost);
+  return cuda_error(e, "qwen35_session_read");
+}
+
+}  // extern "C"

@@ -745,6 +745,20 @@ void gemv_prewarm(int device) {
     }
 }
 
+int32_t gemv_reserve(unltd_ctx ctx, const unltd_weight_s &w, int mode) {
+  if (w.dtype == F32 || w.dim_out == 0) return UNLTD_OK;
+  const int nspans = w.dtype == Q8_0 ? (int)((w.nb + 7) / 8) : (int)w.nb;
+  const size_t img_bytes = (size_t)nspans * img_stride(w.dtype, mode);
+  if (ctx->scratch_bytes >= img_bytes) return UNLTD_OK;
+  if (ctx->scratch) cudaFree(ctx->scratch);
+  ctx->scratch = nullptr;
+  ctx->scratch_bytes = 0;
+  cudaError_t e = cudaMalloc(&ctx->scratch, img_bytes);
+  if (e != cudaSuccess) return cuda_error(e, "scratch alloc");
+  ctx->scratch_bytes = img_bytes;
+  return UNLTD_OK;
+}
+
 int32_t gemv_launch(unltd_ctx ctx, const GemvArgs &a) {
   const unltd_weight_s &w = *a.w;
   cudaStream_t st = ctx->stream;
@@ -768,16 +782,8 @@ int32_t gemv_launch(unltd_ctx ctx, const GemvArgs &a) {
   const int fmt = w.dtype, mode = a.mode;
   const int nspans = fmt == Q8_0 ? (int)((w.nb + 7) / 8) : (int)w.nb;
   const int nbu = nspans;
-  const int istr = img_stride(fmt, mode);
-  const int img_bytes = nspans * istr;
-  if (ctx->scratch_bytes < (size_t)img_bytes) {
-    if (ctx->scratch) cudaFree(ctx->scratch);
-    ctx->scratch = nullptr;
-    ctx->scratch_bytes = 0;
-    cudaError_t e = cudaMalloc(&ctx->scratch, img_bytes);
-    if (e != cudaSuccess) return cuda_error(e, "scratch alloc");
-    ctx->scratch_bytes = img_bytes;
-  }
+  const int img_bytes = nspans * img_stride(fmt, mode);
+  if (int32_t rc = gemv_reserve(ctx, w, mode)) return rc;
 
   // ---- tiling: rows per tile T, stages S, shared-memory plan ----
   const int rows = (int)w.dim_out;

@@ -42,6 +42,20 @@ struct unltd_weight_s {
 
 namespace unltd {
 
+// Makes `dev` the current device for a scope and restores the previous one.
+struct CtxGuard {
+  int prev = -1;
+  explicit CtxGuard(int dev) {
+    cudaGetDevice(&prev);
+    if (prev != dev) cudaSetDevice(dev);
+  }
+  ~CtxGuard() {
+    int cur = -1;
+    cudaGetDevice(&cur);
+    if (prev >= 0 && cur != prev) cudaSetDevice(prev);
+  }
+};
+
 // Thread-local error message behind unltd_last_error().
 int32_t set_error(int32_t status, const std::string &msg);
 int32_t cuda_error(cudaError_t e, const char *what);
@@ -63,6 +77,8 @@ struct GemvArgs {
   uint32_t *token;
 };
 int32_t gemv_launch(unltd_ctx ctx, const GemvArgs &a);
+// Grow the context's x-image scratch for w (call before stream capture).
+int32_t gemv_reserve(unltd_ctx ctx, const unltd_weight_s &w, int mode);
 void gemv_prewarm(int device);
 
 // gemm_tc.cu

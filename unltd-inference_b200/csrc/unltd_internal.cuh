@@ -216,4 +216,29 @@ __device__ __forceinline__ uint32_t orderable(float v) {
   return (b & 0x80000000u) ? ~b : (b | 0x80000000u);
 }
 
+// Element e of a repacked Q4_K row with nb blocks, with the f32 operations
+// of dequantize_q4_k (quants.rs:534-567): d1 = d*sc, m1 = dmin*m, y = d1*q - m1.
+__device__ __forceinline__ float q4k_row_elem(const uint8_t *row, size_t nb, size_t e) {
+  size_t b = e / kQK;
+  int el = (int)(e % kQK), g = el >> 5;
+  const uint8_t *hdr = row + b * 16;
+  const uint8_t *s = hdr + 4;
+  int sc, m;
+  if (g < 4) {
+    sc = s[g] & 63;
+    m = s[g + 4] & 63;
+  } else {
+    sc = (s[g + 4] & 0xF) | ((s[g - 4] >> 6) << 4);
+    m = (s[g + 4] >> 4) | ((s[g] >> 6) << 4);
+  }
+  float d = h2f_bits(hdr[0] | (hdr[1] << 8));
+  float dmin = h2f_bits(hdr[2] | (hdr[3] << 8));
+  int rr = el & 31, p = g >> 1;
+  uint8_t byte = row[nb * 16 + b * 128 + 32 * p + 4 * (rr & 7) + (rr >> 3)];
+  int q = (g & 1) ? (byte >> 4) : (byte & 0xF);
+  float d1 = __fmul_rn(d, (float)sc);
+  float m1 = __fmul_rn(dmin, (float)m);
+  return __fsub_rn(__fmul_rn(d1, (float)q), m1);
+}
+
 }  // namespace unltd

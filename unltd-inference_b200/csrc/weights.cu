@@ -70,27 +70,8 @@ __global__ void dequant_q4k(const uint8_t *__restrict__ dev, float *__restrict__
   size_t n = nb * kQK;
   size_t t = blockIdx.x * (size_t)blockDim.x + threadIdx.x;
   if (t >= rows * n) return;
-  size_t r = t / n, e = t % n, b = e / kQK;
-  int el = (int)(e % kQK), g = el >> 5;
-  const uint8_t *row = dev + r * stride;
-  const uint8_t *hdr = row + b * 16;
-  const uint8_t *s = hdr + 4;
-  int sc, m;
-  if (g < 4) {
-    sc = s[g] & 63;
-    m = s[g + 4] & 63;
-  } else {
-    sc = (s[g + 4] & 0xF) | ((s[g - 4] >> 6) << 4);
-    m = (s[g + 4] >> 4) | ((s[g] >> 6) << 4);
-  }
-  float d = h2f_bits(hdr[0] | (hdr[1] << 8));
-  float dmin = h2f_bits(hdr[2] | (hdr[3] << 8));
-  int rr = el & 31, p = g >> 1;
-  uint8_t byte = row[nb * 16 + b * 128 + 32 * p + 4 * (rr & 7) + (rr >> 3)];
-  int q = (g & 1) ? (byte >> 4) : (byte & 0xF);
-  float d1 = __fmul_rn(d, (float)sc);
-  float m1 = __fmul_rn(dmin, (float)m);
-  out[t] = __fsub_rn(__fmul_rn(d1, (float)q), m1);
+  size_t r = t / n, e = t % n;
+  out[t] = q4k_row_elem(dev + r * stride, nb, e);
 }
 
 __global__ void dequant_q6k(const uint8_t *__restrict__ dev, float *__restrict__ out, size_t rows,

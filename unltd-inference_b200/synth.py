@@ -55,3 +55,124 @@ def row_bytes(dtype: int, dim_in: int) -> int:
     if dtype == F32:
         return 4 * dim_in
     return dim_in // BLOCK_ELEMS[dtype] * BLOCK_BYTES[dtype]
+
+
+# ---- synthetic Qwen3.5-style hybrid model ------------------------------------
+# Shapes follow crates/unltd-generation/src/qwen35_forward.rs:139-221; the
+# dtypes follow the Q4_K_M mix (Q4_K for most projections and the embedding,
+# Q6_K for attn_v, ffn_down and the LM head). Quantized tensors use the block
+# distributions above. f32 tensors (the reference loads them from the GGUF):
+#   attn_norm / post_attention_norm / output_norm / ssm_norm ~ U[2e-4, 6e-4]
+#     (uniform Q4_K blocks are positively biased, so each projection adds a
+#     large common-mode term to the residual stream; small norm weights keep
+#     that term from swamping the token embedding, so the greedy stream
+#     depends on the tokens instead of settling on one vocab row),
+#   attn_q_norm / attn_k_norm ~ U[0.5, 1.5], ssm_conv1d ~ U[-0.5, 0.5],
+#   ssm_dt.bias ~ U[-1, 1], ssm_a ~ -U[0.1, 1].
+# The session state stands in for a prefilled context: K and V cache rows
+# ~ N(0, 1), conv windows ~ N(0, 1), GDN matrices ~ N(0, 0.05^2).
+
+import zlib
+
+QWEN35_9B = dict(
+    n_layer=32, n_embd=4096, n_ff=12288, n_head=16, n_head_kv=4, head_dim=256, head_dim_v=256, n_rot=64,
+    conv_kernel=4, state_size=128, group_count=16, time_step_rank=32, d_inner=4096, full_attn_interval=4,
+    vocab=151936, freq_base=1e7, rms_eps=1e-6,
+)
+
+# Small configuration with the same structure (3 recurrent + 1 attention layer).
+QWEN35_TINY = dict(
+    n_layer=4, n_embd=512, n_ff=1024, n_head=2, n_head_kv=1, head_dim=256, head_dim_v=256, n_rot=64,
+    conv_kernel=4, state_size=128, group_count=2, time_step_rank=4, d_inner=512, full_attn_interval=4,
+    vocab=1000, freq_base=1e7, rms_eps=1e-6,
+)
+
+
+def qwen35_dims(cfg: dict) -> dict:
+    """Derived dimensions (qwen35.rs:255-291)."""
+    hd = cfg["d_inner"] // (2 * cfg["group_count"])
+    theta = np.float32(cfg["freq_base"]) ** (np.float32(-2.0) / np.float32(cfg["n_rot"]))
+    return dict(
+        hd=hd, nv=cfg["d_inner"] // hd, nqk=cfg["group_count"], dconv=2 * cfg["d_inner"],
+        kvlen=cfg["n_head_kv"] * cfg["head_dim"],
+        attn=[(il + 1) % cfg["full_attn_interval"] == 0 for il in range(cfg["n_layer"])],
+        theta_scale=float(np.float32(theta)),
+    )
+
+
+def qwen35_tensor_list(cfg: dict) -> list:
+    """(name, dtype, dim_in, dim_out) of every tensor, Q4_K_M mix; F32 tensors
+    have dim_out = 1."""
+    d = qwen35_dims(cfg)
+    n, nff = cfg["n_embd"], cfg["n_ff"]
+    t = [("token_embd.weight", Q4K, n, cfg["vocab"]), ("output_norm.weight", F32, n, 1),
+         ("output.weight", Q6K, n, cfg["vocab"])]
+    for il in range(cfg["n_layer"]):
+        p = f"blk.{il}."
+        t += [(p + "attn_norm.weight", F32, n, 1), (p + "post_attention_norm.weight", F32, n, 1),
+              (p + "ffn_gate.weight", Q4K, n, nff), (p + "ffn_up.weight", Q4K, n, nff),
+              (p + "ffn_down.weight", Q6K, nff, n)]
+        if d["attn"][il]:
+            t += [(p + "attn_q.weight", Q4K, n, 2 * n), (p + "attn_q_norm.weight", F32, cfg["head_dim"], 1),
+                  (p + "attn_k.weight", Q4K, n, d["kvlen"]), (p + "attn_k_norm.weight", F32, cfg["head_dim"], 1),
+                  (p + "attn_v.weight", Q6K, n, d["kvlen"]), (p + "attn_output.weight", Q4K, n, n)]
+        else:
+            t += [(p + "attn_qkv.weight", Q4K, n, d["dconv"]), (p + "attn_gate.weight", Q4K, n, n),
+                  (p + "ssm_conv1d.weight", F32, cfg["conv_kernel"] * d["dconv"], 1),
+                  (p + "ssm_dt.bias", F32, d["nv"], 1), (p + "ssm_a", F32, d["nv"], 1),
+                  (p + "ssm_beta.weight", Q4K, n, d["nv"]), (p + "ssm_alpha.weight", Q4K, n, d["nv"]),
+                  (p + "ssm_norm.weight", F32, d["hd"], 1), (p + "ssm_out.weight", Q4K, n, n)]
+    return t
+
+
+def _tensor_seed(seed: int, name: str) -> int:
+    return (seed * 1000003 + zlib.crc32(name.encode())) & 0xFFFFFFFF
+
+
+def _f32_tensor(name: str, n: int, seed: int) -> np.ndarray:
+    rng = np.random.default_rng(_tensor_seed(seed, name))
+    if name.endswith(("attn_norm.weight", "post_attention_norm.weight", "ssm_norm.weight")) or name == "output_norm.weight":
+        lo, hi = 2e-4, 6e-4
+    elif name.endswith(("attn_q_norm.weight", "attn_k_norm.weight")):
+        lo, hi = 0.5, 1.5
+    elif name.endswith("ssm_conv1d.weight"):
+        lo, hi = -0.5, 0.5
+    elif name.endswith("ssm_dt.bias"):
+        lo, hi = -1.0, 1.0
+    elif name.endswith("ssm_a"):
+        return -rng.uniform(0.1, 1.0, n).astype(np.float32)
+    else:
+        raise KeyError(name)
+    return rng.uniform(lo, hi, n).astype(np.float32)
+
+
+def qwen35_tensor(cfg: dict, name: str, seed: int):
+    """(dtype, array) of one tensor: packed bytes (uint8) or f32 values."""
+    for nm, dt, di, do in qwen35_tensor_list(cfg):
+        if nm == name:
+            if dt == F32:
+                return dt, _f32_tensor(nm, di, seed)
+            return dt, quant_weights(dt, di, do, _tensor_seed(seed, nm))
+    raise KeyError(name)
+
+
+def qwen35_model(cfg: dict, seed: int) -> dict:
+    """name -> (dtype, array) for the whole model."""
+    return {nm: qwen35_tensor(cfg, nm, seed) for nm, _, _, _ in qwen35_tensor_list(cfg)}
+
+
+def qwen35_state(cfg: dict, position: int, seed: int) -> dict:
+    """Seeded session state at `position`: per recurrent layer the conv window
+    ((K-1) x d_conv, oldest row first) and GDN matrices (n_v x hd x hd); per
+    attention layer `position` rows of K and V."""
+    d = qwen35_dims(cfg)
+    rng = np.random.default_rng(seed)
+    st = {"conv": [], "gdn": [], "k": [], "v": []}
+    for il in range(cfg["n_layer"]):
+        if d["attn"][il]:
+            st["k"].append(rng.standard_normal((position, d["kvlen"]), dtype=np.float32))
+            st["v"].append(rng.standard_normal((position, d["kvlen"]), dtype=np.float32))
+        else:
+            st["conv"].append(rng.standard_normal((cfg["conv_kernel"] - 1, d["dconv"]), dtype=np.float32))
+            st["gdn"].append((0.05 * rng.standard_normal((d["nv"], d["hd"], d["hd"]), dtype=np.float32)).astype(np.float32))
+    return st

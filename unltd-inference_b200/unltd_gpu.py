@@ -53,6 +53,17 @@ SIGNATURES = [
     ("unltd_dequantize_q4_k", _I, [_P, _S, _P, _S]),
     ("unltd_set_default_device", _I, [_I]),
     ("unltd_forget_host_weights", _I, []),
+    ("unltd_qwen35_create", _I, [_P, _P, ctypes.POINTER(_P)]),
+    ("unltd_qwen35_set_tensor", _I, [_P, ctypes.c_char_p, _P, _S, _I]),
+    ("unltd_qwen35_finalize", _I, [_P]),
+    ("unltd_qwen35_destroy", _I, [_P]),
+    ("unltd_qwen35_session_create", _I, [_P, _I, ctypes.POINTER(_P)]),
+    ("unltd_qwen35_session_destroy", _I, [_P]),
+    ("unltd_qwen35_session_set_state", _I, [_P, _I, _P, _P, _P, _P]),
+    ("unltd_qwen35_feed", _I, [_P, _P, _I, _P]),
+    ("unltd_qwen35_decode", _I, [_P, ctypes.c_uint32, _I, _P]),
+    ("unltd_qwen35_session_info", _I, [_P, ctypes.POINTER(_I), ctypes.POINTER(_P), ctypes.POINTER(_I64)]),
+    ("unltd_qwen35_session_read", _I, [_P, _P, _P]),
 ]
 
 
@@ -151,7 +162,7 @@ class Context:
                                        _ptr(token), mode))
 
     def gemm(self, w: "Weight", X, Y, m_tokens: int):
-        """Y[m][n] = sum_k X[m][k] W[n][k] on the tensor cores (bf16 operands, f32 accumulate)."""
+        """Y[m][n] = sum_k X[m][k] W[n][k] on the tensor cores (fp16 operands, f32 accumulate)."""
         _check(lib().unltd_gemm(self.h, w.h, _ptr(X), _ptr(Y), m_tokens))
 
     def dequant(self, w: "Weight", out):
@@ -212,3 +223,107 @@ def dequantize_q4_k(out: np.ndarray, w: np.ndarray):
 
 def forget_host_weights():
     _check(lib().unltd_forget_host_weights())
+
+
+# ---- Qwen3.5-style hybrid decode (unltd_qwen35_*) ------------------------------
+
+class Qwen35Config(ctypes.Structure):
+    """unltd_qwen35_config (qwen35.rs:46-80)."""
+    _fields_ = [(n, ctypes.c_int32) for n in (
+        "n_layer", "n_embd", "n_ff", "n_head", "n_head_kv", "head_dim", "head_dim_v", "n_rot",
+        "conv_kernel", "state_size", "group_count", "time_step_rank", "d_inner", "full_attn_interval", "vocab")] + [
+        ("freq_base", ctypes.c_float), ("rms_eps", ctypes.c_float)]
+
+    @classmethod
+    def from_dict(cls, d: dict) -> "Qwen35Config":
+        return cls(**{k: d[k] for k, _ in cls._fields_})
+
+
+class Qwen35Model:
+    """Qwen35Forward::open on the device: tensors uploaded by GGUF name."""
+
+    def __init__(self, ctx: Context, cfg: dict):
+        self.ctx, self.cfg = ctx, dict(cfg)
+        self._c = Qwen35Config.from_dict(cfg)
+        h = ctypes.c_void_p()
+        _check(lib().unltd_qwen35_create(ctx.h, ctypes.byref(self._c), ctypes.byref(h)))
+        self.h = h
+
+    def set_tensor(self, name: str, data: np.ndarray, dtype: int):
+        data = np.ascontiguousarray(data)
+        _check(lib().unltd_qwen35_set_tensor(self.h, name.encode(), data.ctypes.data, data.nbytes, dtype))
+
+    def load(self, tensors: dict):
+        """tensors: name -> (dtype, array), as synth.qwen35_model returns."""
+        for name, (dt, arr) in tensors.items():
+            self.set_tensor(name, arr, dt)
+        _check(lib().unltd_qwen35_finalize(self.h))
+
+    def session(self, ctx_len: int) -> "Qwen35Session":
+        h = ctypes.c_void_p()
+        _check(lib().unltd_qwen35_session_create(self.h, ctx_len, ctypes.byref(h)))
+        return Qwen35Session(self, h, ctx_len)
+
+    def close(self):
+        if getattr(self, "h", None):
+            lib().unltd_qwen35_destroy(self.h)
+            self.h = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+
+def _ptr_array(arrs):
+    if arrs is None:
+        return None, None
+    keep = [None if a is None else np.ascontiguousarray(a, dtype=np.float32) for a in arrs]
+    arr = (ctypes.c_void_p * max(1, len(keep)))(*[None if a is None else a.ctypes.data for a in keep])
+    return arr, keep
+
+
+class Qwen35Session:
+    def __init__(self, model: Qwen35Model, h, ctx_len: int):
+        self.model, self.h, self.ctx_len = model, h, ctx_len
+
+    def set_state(self, position: int, conv=None, gdn=None, kcache=None, vcache=None):
+        ptrs = [_ptr_array(a) for a in (conv, gdn, kcache, vcache)]
+        _check(lib().unltd_qwen35_session_set_state(self.h, position, *[p[0] for p in ptrs]))
+
+    def feed(self, tokens) -> int:
+        t = np.ascontiguousarray(tokens, dtype=np.uint32)
+        nxt = np.zeros(1, np.uint32)
+        _check(lib().unltd_qwen35_feed(self.h, t.ctypes.data, t.size, nxt.ctypes.data))
+        return int(nxt[0])
+
+    def decode(self, token: int, n_steps: int, out: np.ndarray | None = None) -> np.ndarray:
+        out = np.zeros(n_steps, np.uint32) if out is None else out
+        _check(lib().unltd_qwen35_decode(self.h, token, n_steps, out.ctypes.data))
+        return out
+
+    def info(self):
+        pos, st, nl = _I(), _P(), _I64()
+        _check(lib().unltd_qwen35_session_info(self.h, ctypes.byref(pos), ctypes.byref(st), ctypes.byref(nl)))
+        return {"position": pos.value, "stream": st.value or 0, "launches_per_step": nl.value}
+
+    def read(self, logits: bool = True, hidden: bool = True):
+        cfg = self.model.cfg
+        lg = np.empty(cfg["vocab"], np.float32) if logits else None
+        hd = np.empty(cfg["n_embd"], np.float32) if hidden else None
+        _check(lib().unltd_qwen35_session_read(self.h, None if lg is None else lg.ctypes.data,
+                                               None if hd is None else hd.ctypes.data))
+        return lg, hd
+
+    def close(self):
+        if getattr(self, "h", None):
+            lib().unltd_qwen35_session_destroy(self.h)
+            self.h = None
+
+    def __del__(self):
+        try:
+            if self.model.h:
+                self.close()
+        except Exception:
+            pass
