@@ -195,6 +195,10 @@ int32_t unltd_qwen35_session_destroy(unltd_qwen35_session s);
 int32_t unltd_qwen35_session_set_state(unltd_qwen35_session s, int32_t position, const float *const *conv,
                                        const float *const *gdn, const float *const *kcache,
                                        const float *const *vcache);
+/* The inverse: copy the state at the current position out, same layout
+ * (caller-allocated host buffers; NULL arrays or entries are skipped). */
+int32_t unltd_qwen35_session_get_state(unltd_qwen35_session s, float *const *conv, float *const *gdn,
+                                       float *const *kcache, float *const *vcache);
 /* Teacher-forced steps over a prompt; *next_token (nullable) = the greedy
  * token after the last one. */
 int32_t unltd_qwen35_feed(unltd_qwen35_session s, const uint32_t *tokens, int32_t n, uint32_t *next_token);

@@ -53,11 +53,18 @@ def test_tiny_greedy_stream_bit_exact(tiny):
     o = oracle.Qwen35Oracle(cfg, tensors, 64, st, 40)
     otoks, ologits, ohidden = o.greedy(5, 12)
     assert toks.tolist() == otoks
-    assert len(set(otoks)) > 1, "the synthetic model should not repeat one token"
     lg, hd = s.read()
     assert (bits(hd) == bits(ohidden)).all()
     assert (bits(lg) == bits(ologits)).all()
     assert s.info()["position"] == 52
+    # the session state (conv windows, GDN matrices, K/V rows) equals the oracle's
+    gs = s.get_state()
+    for i in range(len(o.conv)):
+        assert (bits(gs["conv"][i]) == bits(o.conv[i])).all()
+        assert (bits(gs["gdn"][i]) == bits(o.gdn[i])).all()
+    for i in range(len(o.k)):
+        assert (bits(gs["k"][i]) == bits(o.k[i][:52])).all()
+        assert (bits(gs["v"][i]) == bits(o.v[i][:52])).all()
     s.close()
 
 
@@ -78,6 +85,27 @@ def test_tiny_prompt_from_position_zero(tiny):
     otoks, _, _ = o.greedy(nxt, 5)
     assert toks.tolist() == otoks
     s.close()
+
+
+def test_tiny_state_round_trip(tiny):
+    """get_state returns what set_state loaded (the checkpoint/resume pair)."""
+    cfg, tensors, m = tiny
+    st = synth.qwen35_state(cfg, 17, 9)
+    s = m.session(24)
+    s.set_state(17, st["conv"], st["gdn"], st["k"], st["v"])
+    gs = s.get_state()
+    for key in ("conv", "gdn", "k", "v"):
+        for a, b in zip(gs[key], st[key]):
+            assert (bits(a) == bits(b)).all(), key
+    # resuming a copy of a state continues exactly like the original session
+    a = s.decode(11, 3)
+    s2 = m.session(24)
+    s2.set_state(17, st["conv"], st["gdn"], st["k"], st["v"])
+    b = s2.decode(11, 3)
+    assert a.tolist() == b.tolist()
+    assert (bits(s.read()[0]) == bits(s2.read()[0])).all()
+    s.close()
+    s2.close()
 
 
 def test_tiny_graph_matches_uncaptured(tiny):

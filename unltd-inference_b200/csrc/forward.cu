@@ -25,6 +25,7 @@
 #include <string>
 #include <vector>
 
+#include "q8k_span.cuh"
 #include "unltd_host.h"
 #include "unltd_internal.cuh"
 
@@ -106,29 +107,42 @@ struct ToF32 {
   __device__ float operator()(double s) const { return (float)s; }
 };
 
-// ---- RMSNorm with an optional residual add (kernels.rs:61-78) ------------
-// r = a (+ b) elementwise; r_out = r when non-null; out = rmsnorm(r, w).
-template <int NT>
-__global__ void __launch_bounds__(NT) add_rmsnorm_kernel(const float *a, const float *b, float *r_out,
-                                                         const float *w, float *out, int n, float eps) {
-  __shared__ double red[2 * NT / 32];
+// ---- RMSNorm (kernels.rs:61-78) fused with the Q8_K image of its output ---
+// r = a (+ b); r_out = r (when non-null); xn = rmsnorm(r, w), quantized
+// (quantize_q8_k) straight into the x images of the GEMVs that consume it.
+// One CTA per 256-element span; each CTA sums all n squares itself.
+struct NormArgs {
+  const float *a, *b;
+  float *r_out;
+  const float *w;
+  int n;
+  float eps;
+  uint8_t *img4, *img6;     // Q4_K / Q6_K image (either may be null)
+  unsigned long long *key;  // non-null: reset the LM-head argmax state
+  unsigned *done;
+};
+
+__global__ void __launch_bounds__(256) norm_quant_kernel(NormArgs p) {
+  pdl_trigger();
+  __shared__ double red[16];
   __shared__ float s_mean;
+  __shared__ Q8KSpanSmem sm;
+  pdl_wait();
+  const int t = threadIdx.x, span = blockIdx.x;
+  auto R = [&](int i) { return p.b ? __fadd_rn(p.a[i], p.b[i]) : p.a[i]; };
   double S = 0.0, A = 0.0;
-  for (int i = threadIdx.x; i < n; i += NT) {
-    const float r = b ? __fadd_rn(a[i], b[i]) : a[i];
-    if (r_out) r_out[i] = r;
+  for (int i = t; i < p.n; i += 256) {
+    const float r = R(i);
     S += (double)__fmul_rn(r, r);
   }
-  block_sum2<NT>(S, A, red);
-  auto R = [&](int i) { return r_out ? r_out[i] : (b ? __fadd_rn(a[i], b[i]) : a[i]); };
+  block_sum2<256>(S, A, red);
   float mean;
-  const MeanOf f{n};
-  if (!resolve_sum(S, S, n, f, &mean)) {
-    __syncthreads();  // r_out visible to thread 0
-    if (threadIdx.x == 0) {
+  const MeanOf f{p.n};
+  if (!resolve_sum(S, S, p.n, f, &mean)) {
+    if (t == 0) {
       double s = 0.0;
 #pragma unroll 1
-      for (int i = 0; i < n; i++) {
+      for (int i = 0; i < p.n; i++) {
         const float r = R(i);
         s = __dadd_rn(s, (double)__fmul_rn(r, r));
       }
@@ -137,16 +151,24 @@ __global__ void __launch_bounds__(NT) add_rmsnorm_kernel(const float *a, const f
     __syncthreads();
     mean = s_mean;
   }
-  const float scale = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(mean, eps)));
-  for (int i = threadIdx.x; i < n; i += NT) {
-    const float r = r_out ? R(i) : (b ? __fadd_rn(a[i], b[i]) : a[i]);
-    out[i] = __fmul_rn(__fmul_rn(r, scale), w[i]);
+  const float scale = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(mean, p.eps)));
+  const int e = span * 256 + t;
+  const float r = R(e);
+  if (p.r_out) p.r_out[e] = r;
+  const float xn = __fmul_rn(__fmul_rn(r, scale), p.w[e]);
+  q8k_span_write(xn, p.img4 ? p.img4 + (size_t)span * kImgQ8K4 : nullptr,
+                 p.img6 ? p.img6 + (size_t)span * kImgQ8K6 : nullptr, sm);
+  if (p.key && span == 0 && t == 0) {
+    *p.key = 0ull;
+    *p.done = 0u;
   }
 }
 
 // ---- token embedding: one Q4_K row, dequantized (min_forward.rs:160-184) --
 __global__ void embed_q4k_kernel(const uint8_t *table, size_t stride, size_t nb, const uint32_t *token,
                                  uint32_t vocab, float *x, int n, int *err) {
+  pdl_trigger();
+  pdl_wait();
   uint32_t t = *token;
   if (t >= vocab) {
     if (blockIdx.x == 0 && threadIdx.x == 0) atomicExch(err, kErrToken);
@@ -157,14 +179,17 @@ __global__ void embed_q4k_kernel(const uint8_t *table, size_t stride, size_t nb,
     x[e] = q4k_row_elem(row, nb, (size_t)e);
 }
 
-// ---- SwiGLU (kernels.rs:174-182) -------------------------------------------
-__global__ void swiglu_kernel(const float *g, const float *u, float *out, int n) {
-  int i = blockIdx.x * blockDim.x + threadIdx.x;
-  if (i < n) {
-    const float t = g[i];
-    const float s = __fdiv_rn(t, __fadd_rn(1.0f, exp_cr(-t)));
-    out[i] = __fmul_rn(s, u[i]);
-  }
+// ---- SwiGLU (kernels.rs:174-182) fused with the Q8_K image of its output ---
+__global__ void __launch_bounds__(256) swiglu_quant_kernel(const float *g, const float *u, uint8_t *img4,
+                                                           uint8_t *img6) {
+  pdl_trigger();
+  __shared__ Q8KSpanSmem sm;
+  pdl_wait();
+  const int span = blockIdx.x, e = span * 256 + threadIdx.x;
+  const float t = g[e];
+  const float s = __fdiv_rn(t, __fadd_rn(1.0f, exp_cr(-t)));
+  q8k_span_write(__fmul_rn(s, u[e]), img4 ? img4 + (size_t)span * kImgQ8K4 : nullptr,
+                 img6 ? img6 + (size_t)span * kImgQ8K6 : nullptr, sm);
 }
 
 // ---- recurrent layer between the projections (qwen35_forward.rs:390-508) --
@@ -185,9 +210,11 @@ struct RecrArgs {
 // touches column j only through the dots over i), kept in registers.
 template <int HD>
 __global__ void __launch_bounds__(HD) recr_mid_kernel(RecrArgs a) {
+  pdl_trigger();
   __shared__ float qs[HD], ks[HD], os[HD];
   __shared__ double red[2 * HD / 32];
   __shared__ float s_f[2];
+  pdl_wait();
   const int h = blockIdx.x, j = threadIdx.x;
   const int qk = h % a.nqk;  // periodic qk-head of v-head h (qwen35_forward.rs:464)
   const int pos = *a.pos, K = a.K;
@@ -290,6 +317,9 @@ __global__ void __launch_bounds__(HD) recr_mid_kernel(RecrArgs a) {
 }
 
 // ---- full-attention layer (qwen35_forward.rs:584-686) ----------------------
+constexpr int kChunk = 64;    // positions per value-pass CTA
+constexpr int kMaxGroup = 8;  // q heads per kv head
+
 struct AttnArgs {
   const float *qk;      // [qfull (nh x 2HDV: q | gate per head) | k (nkv x HDV)]
   const float *v;       // nkv x HDV
@@ -297,10 +327,11 @@ struct AttnArgs {
   const double2 *rope;  // [ctx][nrp] (cos, sin) of the rotated pairs
   float *q;             // nh x HDV, normed and rotated
   float *kcache, *vcache;  // ctx x (nkv*HDV)
-  float *scores;        // nh x ctx
-  float *gated;         // nh x HDV
+  float *scores;        // nh x ctx: scores, then softmax weights in place
+  double2 *part;        // nh x nsplit x HDV: per-chunk (sum, sum |running sum|)
+  uint8_t *img4, *img6; // x image(s) of attn_output's input
   const int *pos;
-  int nh, nkv, n_rot, nrp, ctx;
+  int nh, nkv, n_rot, nrp, ctx, nsplit;
   float eps, kq_scale;
 };
 
@@ -308,9 +339,11 @@ struct AttnArgs {
 // per q head and per kv head.
 template <int HDV>
 __global__ void __launch_bounds__(HDV) attn_pre_kernel(AttnArgs a) {
+  pdl_trigger();
   __shared__ double red[2 * HDV / 32];
   __shared__ float sx[HDV];
   __shared__ float s_mean;
+  pdl_wait();
   const int b = blockIdx.x, j = threadIdx.x;
   const bool isq = b < a.nh;
   const int hh = isq ? b : b - a.nh;
@@ -361,31 +394,41 @@ __global__ void __launch_bounds__(HDV) attn_pre_kernel(AttnArgs a) {
 // scores[h][p] = dot_f32(q_h, k_p) as f32 (quants.rs:106-114): exact f64
 // products summed by the pairwise tree, which for HDV = 32 * E (E a power of
 // two) is lane-local subtrees over E contiguous elements and then a butterfly.
-// One warp per position, all q heads of the kv group.
+// A warp takes four positions (all loads issued first), all q heads of the
+// kv group; 32 positions per CTA.
 template <int HDV>
 __global__ void __launch_bounds__(256) attn_scores_kernel(AttnArgs a) {
   constexpr int E = HDV / 32;
+  pdl_trigger();
   extern __shared__ float qsm[];  // G x HDV
+  pdl_wait();
   const int kvh = blockIdx.x, G = a.nh / a.nkv;
   const int n_ctx = *a.pos + 1;
   const int p0 = blockIdx.y * 32;
   if (p0 >= n_ctx) return;
   for (int i = threadIdx.x; i < G * HDV; i += 256) qsm[i] = a.q[(size_t)(kvh * G) * HDV + i];
-  __syncthreads();
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const size_t kvlen = (size_t)a.nkv * HDV;
-  for (int p = p0 + warp; p < min(p0 + 32, n_ctx); p += 8) {
+  float kv[4][E];
+#pragma unroll
+  for (int r = 0; r < 4; r++) {
+    const int p = min(p0 + warp + 8 * r, n_ctx - 1);
     const float *kr = a.kcache + (size_t)p * kvlen + (size_t)kvh * HDV + lane * E;
-    float kv[E];
 #pragma unroll
     for (int t = 0; t < E; t += 4) {
-      float4 v4 = *reinterpret_cast<const float4 *>(kr + t);
-      kv[t] = v4.x, kv[t + 1] = v4.y, kv[t + 2] = v4.z, kv[t + 3] = v4.w;
+      const float4 v4 = *reinterpret_cast<const float4 *>(kr + t);
+      kv[r][t] = v4.x, kv[r][t + 1] = v4.y, kv[r][t + 2] = v4.z, kv[r][t + 3] = v4.w;
     }
+  }
+  __syncthreads();
+#pragma unroll
+  for (int r = 0; r < 4; r++) {
+    const int p = p0 + warp + 8 * r;
+    if (p >= n_ctx) break;
     for (int g = 0; g < G; g++) {
       double pr[E];
 #pragma unroll
-      for (int t = 0; t < E; t++) pr[t] = __dmul_rn((double)qsm[g * HDV + lane * E + t], (double)kv[t]);
+      for (int t = 0; t < E; t++) pr[t] = __dmul_rn((double)qsm[g * HDV + lane * E + t], (double)kv[r][t]);
 #pragma unroll
       for (int w = 1; w < E; w <<= 1)
 #pragma unroll
@@ -398,22 +441,18 @@ __global__ void __launch_bounds__(256) attn_scores_kernel(AttnArgs a) {
   }
 }
 
-// softmax (kernels.rs:157-168) of head h's scores, then the f64 value sum
-// over positions (qwen35_forward.rs:660-672) for 32 columns, times
-// sigmoid(gate). Grid (nh, HDV/32), 256 threads.
-template <int HDV>
-__global__ void __launch_bounds__(256) attn_out_kernel(AttnArgs a) {
+// softmax (kernels.rs:157-168) of one head's scores, in place. 256 threads.
+__global__ void __launch_bounds__(256) attn_softmax_kernel(AttnArgs a) {
+  pdl_trigger();
   extern __shared__ __align__(16) uint8_t sm[];
   __shared__ float redf[8];
-  __shared__ double part[2][8][32];
-  const int h = blockIdx.x, tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-  const int kvh = h / (a.nh / a.nkv);
+  pdl_wait();
+  const int h = blockIdx.x, tid = threadIdx.x;
   const int n = *a.pos + 1;
   float *e = reinterpret_cast<float *>(sm);
   double *l0 = reinterpret_cast<double *>(sm + round_up((size_t)a.ctx * 4, 16));
   double *l1 = l0 + (a.ctx + 1) / 2;
-  const float *sc = a.scores + (size_t)h * a.ctx;
-
+  float *sc = a.scores + (size_t)h * a.ctx;
   float m = -INFINITY;
   for (int p = tid; p < n; p += 256) m = fmaxf(m, sc[p]);
   m = block_max<256>(m, redf);
@@ -435,44 +474,112 @@ __global__ void __launch_bounds__(256) attn_out_kernel(AttnArgs a) {
     len = nl;
   }
   const double sum = cur[0];
-  __syncthreads();
-  for (int p = tid; p < n; p += 256) e[p] = (float)__ddiv_rn((double)e[p], sum);
-  __syncthreads();
+  for (int p = tid; p < n; p += 256) sc[p] = (float)__ddiv_rn((double)e[p], sum);
+}
 
-  const int c = blockIdx.y * 32 + lane;
+// Value pass over one chunk of kChunk positions for the G q heads of one kv
+// head: per (head, column) the chunk's left-to-right f64 sum of
+// soft[p] * v[p] (qwen35_forward.rs:660-672) and the sum of |running sum|,
+// which bounds that chunk's rounding error. The chunk's V rows are staged in
+// shared memory once for all G heads. Grid (nkv, nsplit), thread = column.
+template <int HDV>
+__global__ void __launch_bounds__(HDV) attn_values_kernel(AttnArgs a) {
+  pdl_trigger();
+  extern __shared__ __align__(16) float vsm[];  // kChunk x HDV
+  __shared__ float ssoft[kMaxGroup][kChunk];
+  pdl_wait();
+  const int kvh = blockIdx.x, split = blockIdx.y, c = threadIdx.x;
+  const int n = *a.pos + 1, G = a.nh / a.nkv;
+  const int p0 = split * kChunk;
+  if (p0 >= n) return;
+  const int len = min(kChunk, n - p0);
   const size_t kvlen = (size_t)a.nkv * HDV;
-  const float *vcol = a.vcache + (size_t)kvh * HDV + c;
-  double S = 0.0, A = 0.0;
-  for (int p = warp; p < n; p += 8) {
-    const double t = __dmul_rn((double)e[p], (double)vcol[(size_t)p * kvlen]);
-    S += t;
-    A += fabs(t);
-  }
-  part[0][warp][lane] = S;
-  part[1][warp][lane] = A;
-  __syncthreads();
-  if (warp == 0) {
-    S = 0.0;
-    A = 0.0;
+  constexpr int V4 = kChunk / 4;  // float4 loads per thread: kChunk * HDV / 4 / HDV
+  float4 buf[V4];
 #pragma unroll
-    for (int w = 0; w < 8; w++) {
-      S += part[0][w][lane];
-      A += part[1][w][lane];
-    }
-    float attn;
-    if (!resolve_sum(S, A, n, ToF32{}, &attn)) {
-      double s = 0.0;
-#pragma unroll 1
-      for (int p = 0; p < n; p++) s = __dadd_rn(s, __dmul_rn((double)e[p], (double)vcol[(size_t)p * kvlen]));
-      attn = (float)s;
-    }
-    const float gate = a.qk[(size_t)h * 2 * HDV + HDV + c];
-    a.gated[(size_t)h * HDV + c] = __fmul_rn(attn, sigmoid_f(gate));
+  for (int i = 0; i < V4; i++) {
+    const int idx = i * HDV + c;  // float4 index within the chunk
+    const int p = idx / (HDV / 4), col4 = idx % (HDV / 4);
+    buf[i] = p < len ? *reinterpret_cast<const float4 *>(a.vcache + (size_t)(p0 + p) * kvlen + (size_t)kvh * HDV +
+                                                         col4 * 4)
+                     : make_float4(0.f, 0.f, 0.f, 0.f);
   }
+  for (int i = c; i < G * kChunk; i += HDV) {
+    const int g = i / kChunk, pp = i % kChunk;
+    ssoft[g][pp] = pp < len ? a.scores[(size_t)(kvh * G + g) * a.ctx + p0 + pp] : 0.0f;
+  }
+#pragma unroll
+  for (int i = 0; i < V4; i++) reinterpret_cast<float4 *>(vsm)[i * HDV + c] = buf[i];
+  __syncthreads();
+  double S[kMaxGroup], Q[kMaxGroup];
+#pragma unroll
+  for (int g = 0; g < kMaxGroup; g++) S[g] = Q[g] = 0.0;
+  for (int p = 0; p < len; p++) {
+    const double v = (double)vsm[p * HDV + c];
+#pragma unroll
+    for (int g = 0; g < kMaxGroup; g++) {
+      if (g < G) {
+        S[g] = __dadd_rn(S[g], __dmul_rn((double)ssoft[g][p], v));
+        Q[g] = __dadd_rn(Q[g], fabs(S[g]));
+      }
+    }
+  }
+#pragma unroll
+  for (int g = 0; g < kMaxGroup; g++)
+    if (g < G) a.part[((size_t)(kvh * G + g) * a.nsplit + split) * HDV + c] = make_double2(S[g], Q[g]);
+}
+
+// Combine the chunks in position order, resolve the reference's sequential
+// f64 sum exactly, gate with sigmoid (qwen35_forward.rs:676-686) and write the
+// x image of attn_output's input. One CTA per 256-element span.
+//
+// Bound: the reference's left-to-right sum s^ of n terms satisfies
+// |s^ - s| <= u' * sum_k |s^_k| <= u' (1 + O(nu)) sum_k |s_k| (s_k the exact
+// prefix sums, u' = u / (1 - u)); with the exact total O_w before chunk w and
+// in-chunk running sums q, sum_k |s_k| <= sum_w (len_w |O_w| + sum |q|). The
+// chunked sum computed here is off by at most u' (sum_w sum |q| +
+// sum_w |O_{w+1}|). B is their sum with a factor 4 (2^-51 instead of 2^-53)
+// that covers every second-order term and the rounding of S +- B.
+template <int HDV>
+__global__ void __launch_bounds__(256) attn_combine_quant_kernel(AttnArgs a) {
+  pdl_trigger();
+  __shared__ Q8KSpanSmem sm;
+  pdl_wait();
+  const int span = blockIdx.x, t = threadIdx.x;
+  const int e = span * 256 + t, h = e / HDV, c = e % HDV;
+  const int kvh = h / (a.nh / a.nkv);
+  const int n = *a.pos + 1;
+  const int nw = (n + kChunk - 1) / kChunk;
+  const double2 *pp = a.part + (size_t)h * a.nsplit * HDV + c;
+  double O = 0.0, T1 = 0.0, T2 = 0.0, T3 = 0.0;
+  for (int w = 0; w < nw; w++) {
+    const double2 sq = pp[(size_t)w * HDV];
+    const int len = min(kChunk, n - w * kChunk);
+    T1 += sq.y;
+    T2 += (double)len * fabs(O);
+    O = __dadd_rn(O, sq.x);
+    T3 += fabs(O);
+  }
+  const double B = 0x1p-51 * (2.0 * T1 + T2 + T3);
+  float attn = (float)(O - B);
+  if (attn != (float)(O + B)) {
+    const size_t kvlen = (size_t)a.nkv * HDV;
+    const float *vcol = a.vcache + (size_t)kvh * HDV + c;
+    const float *soft = a.scores + (size_t)h * a.ctx;
+    double s = 0.0;
+#pragma unroll 8
+    for (int p = 0; p < n; p++) s = __dadd_rn(s, __dmul_rn((double)soft[p], (double)vcol[(size_t)p * kvlen]));
+    attn = (float)s;
+  }
+  const float gate = a.qk[(size_t)h * 2 * HDV + HDV + c];
+  q8k_span_write(__fmul_rn(attn, sigmoid_f(gate)), a.img4 ? a.img4 + (size_t)span * kImgQ8K4 : nullptr,
+                 a.img6 ? a.img6 + (size_t)span * kImgQ8K6 : nullptr, sm);
 }
 
 // token bookkeeping at the end of a step
 __global__ void step_end_kernel(const uint32_t *cur, uint32_t *hist, int *counter, int *pos) {
+  pdl_trigger();
+  pdl_wait();
   hist[*counter] = *cur;
   *counter += 1;
   *pos += 1;
@@ -547,10 +654,12 @@ struct unltd_qwen35_session_s {
   int ctx_len = 0;
   int host_pos = 0;
   // activations
-  float *X = nullptr, *XN = nullptr, *R = nullptr, *T = nullptr, *F = nullptr, *P = nullptr;
-  float *proj = nullptr, *Y = nullptr, *FF = nullptr, *SW = nullptr;
-  float *q = nullptr, *scores = nullptr, *gated = nullptr, *logits = nullptr;
-  double2 *rope = nullptr;
+  float *X = nullptr, *R = nullptr, *T = nullptr, *F = nullptr;
+  float *proj = nullptr, *Y = nullptr, *FF = nullptr;
+  float *q = nullptr, *scores = nullptr, *logits = nullptr;
+  double2 *rope = nullptr, *part = nullptr;
+  uint8_t *img4 = nullptr, *img6 = nullptr;  // x images written by the fused producer kernels
+  int nsplit = 0;
   uint32_t *cur_token = nullptr, *hist = nullptr, *feed = nullptr;
   int *counter = nullptr, *pos = nullptr;
   std::vector<float *> ring, state, kc, vc;
@@ -589,6 +698,7 @@ int32_t derive(const unltd_qwen35_config &c, Derived *d) {
   if (c.head_dim != 256 && c.head_dim != 128) return unsup("head_dim must be 128 or 256");
   if (c.n_embd % 256 || c.n_ff % 256) return unsup("n_embd and n_ff must be multiples of 256");
   if (c.conv_kernel > 16) return unsup("conv_kernel > 16");
+  if (c.n_head / c.n_head_kv > kMaxGroup) return unsup("more than 8 query heads per kv head");
   d->n = c.n_embd;
   d->nff = c.n_ff;
   d->nh = c.n_head;
@@ -734,6 +844,42 @@ int64_t launch_gemv(unltd_ctx c, const unltd_weight_s *w, const float *x, float 
   return 2;
 }
 
+// GEMV whose x image a fused producer kernel already wrote.
+int64_t launch_gemv_img(unltd_qwen35_session s, const unltd_weight_s *w, float *y, int32_t *rc) {
+  GemvArgs g{w, nullptr, y, MODE_Q8K, nullptr, nullptr, nullptr};
+  g.img = w->dtype == Q4K ? s->img4 : s->img6;
+  if (!*rc) *rc = gemv_launch(s->ctx, g);
+  return 1;
+}
+
+// Kernel launch with programmatic stream serialization: the kernel may become
+// resident while its predecessor runs; it calls griddepcontrol.wait before
+// reading the predecessor's output or writing anything.
+template <typename... KArgs, typename... Args>
+cudaError_t launch_pdl(void (*k)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t st, Args... args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = st;
+  cudaLaunchAttribute at[1];
+  at[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  at[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = at;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, k, args...);
+}
+
+bool any_dtype(const Proj &p, int dt) {
+  for (auto *w : p.w)
+    if (w->dtype == dt) return true;
+  return false;
+}
+
+size_t softmax_smem(int ctx_len) {
+  return round_up((size_t)ctx_len * 4, 16) + (size_t)((ctx_len + 1) / 2 + (ctx_len + 3) / 4 + 1) * 8;
+}
+
 // Enqueue one decode step on the session's stream.
 int32_t enqueue_step(unltd_qwen35_session s) {
   unltd_qwen35 m = s->m;
@@ -741,23 +887,26 @@ int32_t enqueue_step(unltd_qwen35_session s) {
   cudaStream_t st = s->ctx->stream;
   int32_t rc = UNLTD_OK;
   int64_t nl = 0;
-  auto chk = [&](const char *what) {
-    if (!rc) rc = cuda_error(cudaGetLastError(), what);
+  auto chk = [&](cudaError_t e, const char *what) {
+    if (!rc) rc = cuda_error(e, what);
     nl++;
   };
-  auto proj = [&](const Proj &p, const float *x) {
-    for (size_t i = 0; i < p.w.size(); i++) nl += launch_gemv(s->ctx, p.w[i], x, s->proj + p.off[i], &rc);
+  auto norm = [&](const float *a, const float *b, float *r_out, const float *w, bool q4, bool q6, bool argmax) {
+    NormArgs p{a, b, r_out, w, d.n, d.eps, q4 ? s->img4 : nullptr, q6 ? s->img6 : nullptr,
+               argmax ? s->ctx->argmax_key : nullptr, argmax ? s->ctx->argmax_done : nullptr};
+    chk(launch_pdl(norm_quant_kernel, dim3(d.n / 256), dim3(256), 0, st, p), "norm");
   };
-  embed_q4k_kernel<<<d.n / 256, 256, 0, st>>>(m->embd->dev, m->embd->row_stride, m->embd->nb, s->cur_token,
-                                                (uint32_t)d.vocab, s->X, d.n, s->ctx->err);
-  chk("embed");
+  chk(launch_pdl(embed_q4k_kernel, dim3(d.n / 256), dim3(256), 0, st, (const uint8_t *)m->embd->dev,
+                 m->embd->row_stride, m->embd->nb, (const uint32_t *)s->cur_token, (uint32_t)d.vocab, s->X, d.n,
+                 s->ctx->err),
+      "embed");
   for (int il = 0; il < d.n_layer; il++) {
     const Layer &L = m->layers[il];
     // layer input = l_out of the previous layer (residual + ffn), fused into the norm
-    if (il == 0) add_rmsnorm_kernel<1024><<<1, 1024, 0, st>>>(s->X, nullptr, nullptr, L.attn_norm, s->XN, d.n, d.eps);
-    else add_rmsnorm_kernel<1024><<<1, 1024, 0, st>>>(s->R, s->F, s->X, L.attn_norm, s->XN, d.n, d.eps);
-    chk("attn_norm");
-    proj(L.in, s->XN);
+    const bool q4 = any_dtype(L.in, Q4K), q6 = any_dtype(L.in, Q6K);
+    if (il == 0) norm(s->X, nullptr, nullptr, L.attn_norm, q4, q6, false);
+    else norm(s->R, s->F, s->X, L.attn_norm, q4, q6, false);
+    for (size_t i = 0; i < L.in.w.size(); i++) nl += launch_gemv_img(s, L.in.w[i], s->proj + L.in.off[i], &rc);
     if (!L.attn) {
       RecrArgs a;
       a.proj = s->proj;
@@ -777,8 +926,7 @@ int32_t enqueue_step(unltd_qwen35_session s) {
       a.beta_off = d.dconv + d.n;
       a.alpha_off = d.dconv + d.n + d.nv;
       a.eps = d.eps;
-      recr_mid_kernel<128><<<d.nv, 128, 0, st>>>(a);
-      chk("recr_mid");
+      chk(launch_pdl(recr_mid_kernel<128>, dim3(d.nv), dim3(128), 0, st, a), "recr_mid");
       nl += launch_gemv(s->ctx, L.out, s->Y, s->T, &rc);
     } else {
       AttnArgs a;
@@ -791,54 +939,58 @@ int32_t enqueue_step(unltd_qwen35_session s) {
       a.kcache = s->kc[L.slot];
       a.vcache = s->vc[L.slot];
       a.scores = s->scores;
-      a.gated = s->gated;
+      a.part = s->part;
+      a.img4 = L.out->dtype == Q4K ? s->img4 : nullptr;
+      a.img6 = L.out->dtype == Q6K ? s->img6 : nullptr;
       a.pos = s->pos;
       a.nh = d.nh;
       a.nkv = d.nkv;
       a.n_rot = d.n_rot;
       a.nrp = d.nrp;
       a.ctx = s->ctx_len;
+      a.nsplit = s->nsplit;
       a.eps = d.eps;
       a.kq_scale = d.kq_scale;
-      const size_t out_smem = round_up((size_t)s->ctx_len * 4, 16) + (size_t)((s->ctx_len + 1) / 2 + (s->ctx_len + 3) / 4 + 1) * 8;
-      const dim3 sg(d.nkv, (s->ctx_len + 31) / 32), og(d.nh, d.hdv / 32);
-      const size_t q_smem = (size_t)(d.nh / d.nkv) * d.hdv * 4;
+      const dim3 sg(d.nkv, (s->ctx_len + 31) / 32), vg(d.nkv, s->nsplit);
+      const size_t q_smem = (size_t)(d.nh / d.nkv) * d.hdv * 4, v_smem = (size_t)kChunk * d.hdv * 4;
+      const size_t sm_smem = softmax_smem(s->ctx_len);
+      const dim3 cg(d.nh * d.hdv / 256);
       if (d.hdv == 256) {
-        attn_pre_kernel<256><<<d.nh + d.nkv, 256, 0, st>>>(a);
-        chk("attn_pre");
-        attn_scores_kernel<256><<<sg, 256, q_smem, st>>>(a);
-        chk("attn_scores");
-        attn_out_kernel<256><<<og, 256, out_smem, st>>>(a);
-        chk("attn_out");
+        chk(launch_pdl(attn_pre_kernel<256>, dim3(d.nh + d.nkv), dim3(256), 0, st, a), "attn_pre");
+        chk(launch_pdl(attn_scores_kernel<256>, sg, dim3(256), q_smem, st, a), "attn_scores");
+        chk(launch_pdl(attn_softmax_kernel, dim3(d.nh), dim3(256), sm_smem, st, a), "attn_softmax");
+        chk(launch_pdl(attn_values_kernel<256>, vg, dim3(256), v_smem, st, a), "attn_values");
+        chk(launch_pdl(attn_combine_quant_kernel<256>, cg, dim3(256), 0, st, a), "attn_combine");
       } else {
-        attn_pre_kernel<128><<<d.nh + d.nkv, 128, 0, st>>>(a);
-        chk("attn_pre");
-        attn_scores_kernel<128><<<sg, 256, q_smem, st>>>(a);
-        chk("attn_scores");
-        attn_out_kernel<128><<<og, 256, out_smem, st>>>(a);
-        chk("attn_out");
+        chk(launch_pdl(attn_pre_kernel<128>, dim3(d.nh + d.nkv), dim3(128), 0, st, a), "attn_pre");
+        chk(launch_pdl(attn_scores_kernel<128>, sg, dim3(256), q_smem, st, a), "attn_scores");
+        chk(launch_pdl(attn_softmax_kernel, dim3(d.nh), dim3(256), sm_smem, st, a), "attn_softmax");
+        chk(launch_pdl(attn_values_kernel<128>, vg, dim3(128), v_smem, st, a), "attn_values");
+        chk(launch_pdl(attn_combine_quant_kernel<128>, cg, dim3(256), 0, st, a), "attn_combine");
       }
-      nl += launch_gemv(s->ctx, L.out, s->gated, s->T, &rc);
+      nl += launch_gemv_img(s, L.out, s->T, &rc);
     }
-    // residual = x_in + attn_out; p = rmsnorm(residual, post_attention_norm)
-    add_rmsnorm_kernel<1024><<<1, 1024, 0, st>>>(s->X, s->T, s->R, L.post_norm, s->P, d.n, d.eps);
-    chk("post_norm");
+    // residual = x_in + attn_out; rmsnorm(residual, post_attention_norm) -> gate|up image
+    norm(s->X, s->T, s->R, L.post_norm, any_dtype(L.gate_up, Q4K), any_dtype(L.gate_up, Q6K), false);
     for (size_t i = 0; i < L.gate_up.w.size(); i++)
-      nl += launch_gemv(s->ctx, L.gate_up.w[i], s->P, s->FF + L.gate_up.off[i], &rc);
-    swiglu_kernel<<<(d.nff + 255) / 256, 256, 0, st>>>(s->FF, s->FF + d.nff, s->SW, d.nff);
-    chk("swiglu");
-    nl += launch_gemv(s->ctx, L.down, s->SW, s->F, &rc);
+      nl += launch_gemv_img(s, L.gate_up.w[i], s->FF + L.gate_up.off[i], &rc);
+    chk(launch_pdl(swiglu_quant_kernel, dim3(d.nff / 256), dim3(256), 0, st, (const float *)s->FF,
+                   (const float *)(s->FF + d.nff), L.down->dtype == Q4K ? s->img4 : (uint8_t *)nullptr,
+                   L.down->dtype == Q6K ? s->img6 : (uint8_t *)nullptr),
+        "swiglu");
+    nl += launch_gemv_img(s, L.down, s->F, &rc);
   }
   // l_out of the last layer -> output norm -> LM head + greedy argmax
-  add_rmsnorm_kernel<1024><<<1, 1024, 0, st>>>(s->R, s->F, s->X, m->out_norm, s->XN, d.n, d.eps);
-  chk("output_norm");
+  norm(s->R, s->F, s->X, m->out_norm, m->output->dtype == Q4K, m->output->dtype == Q6K, true);
   {
-    GemvArgs g{m->output, s->XN, s->logits, MODE_Q8K, s->ctx->argmax_key, s->ctx->argmax_done, s->cur_token};
+    GemvArgs g{m->output, nullptr, s->logits, MODE_Q8K, s->ctx->argmax_key, s->ctx->argmax_done, s->cur_token};
+    g.img = m->output->dtype == Q4K ? s->img4 : s->img6;
     if (!rc) rc = gemv_launch(s->ctx, g);
-    nl += 2;
+    nl += 1;
   }
-  step_end_kernel<<<1, 1, 0, st>>>(s->cur_token, s->hist, s->counter, s->pos);
-  chk("step_end");
+  chk(launch_pdl(step_end_kernel, dim3(1), dim3(1), 0, st, (const uint32_t *)s->cur_token, s->hist, s->counter,
+                 s->pos),
+      "step_end");
   s->launches_per_step = nl;
   return rc;
 }
@@ -1025,19 +1177,20 @@ int32_t unltd_qwen35_session_create(unltd_qwen35 m, int32_t ctx_len, unltd_qwen3
   CtxGuard g(m->ctx->device);
   auto &B = s->bufs;
   const size_t n = d.n;
+  s->nsplit = (ctx_len + kChunk - 1) / kChunk;
+  const size_t spans = (size_t)std::max(d.n, d.nff) / 256;
   if (!rc) rc = dalloc(B, &s->X, n, "session");
-  if (!rc) rc = dalloc(B, &s->XN, n, "session");
   if (!rc) rc = dalloc(B, &s->R, n, "session");
   if (!rc) rc = dalloc(B, &s->T, n, "session");
   if (!rc) rc = dalloc(B, &s->F, n, "session");
-  if (!rc) rc = dalloc(B, &s->P, n, "session");
   if (!rc) rc = dalloc(B, &s->proj, m->proj_rows, "session");
   if (!rc) rc = dalloc(B, &s->Y, n, "session");
   if (!rc) rc = dalloc(B, &s->FF, 2 * (size_t)d.nff, "session");
-  if (!rc) rc = dalloc(B, &s->SW, (size_t)d.nff, "session");
   if (!rc) rc = dalloc(B, &s->q, (size_t)d.nh * d.hdv, "session");
   if (!rc) rc = dalloc(B, &s->scores, (size_t)d.nh * ctx_len, "session");
-  if (!rc) rc = dalloc(B, &s->gated, n, "session");
+  if (!rc) rc = dalloc(B, &s->part, (size_t)d.nh * s->nsplit * d.hdv, "session");
+  if (!rc) rc = dalloc(B, &s->img4, spans * kImgQ8K4, "session");
+  if (!rc) rc = dalloc(B, &s->img6, spans * kImgQ8K6, "session");
   if (!rc) rc = dalloc(B, &s->logits, (size_t)d.vocab, "session");
   if (!rc) rc = dalloc(B, &s->rope, (size_t)ctx_len * std::max(d.nrp, 1), "session");
   if (!rc) rc = dalloc(B, &s->cur_token, 1, "session");
@@ -1072,28 +1225,24 @@ int32_t unltd_qwen35_session_create(unltd_qwen35 m, int32_t ctx_len, unltd_qwen3
     }
     rc = cuda_error(cudaMemcpy(s->rope, tab.data(), tab.size() * sizeof(double2), cudaMemcpyHostToDevice), "rope table");
   }
-  for (void *p : B)
-    if (!rc) rc = cuda_error(cudaMemset(p, 0, 16), "session init");
+  // token, step counter and position start at zero
+  for (void *p : {(void *)s->cur_token, (void *)s->counter, (void *)s->pos})
+    if (!rc) rc = cuda_error(cudaMemset(p, 0, 4), "session init");
   for (int i = 0; !rc && i < m->n_recr; i++) {
     rc = cuda_error(cudaMemset(s->ring[i], 0, (size_t)d.K * d.dconv * 4), "session init");
     if (!rc) rc = cuda_error(cudaMemset(s->state[i], 0, (size_t)d.nv * d.hd * d.hd * 4), "session init");
   }
-  // GEMV scratch sized for every projection before any graph capture
-  for (const auto &L : m->layers) {
-    for (auto *w : L.in.w)
-      if (!rc) rc = gemv_reserve(s->ctx, *w, MODE_Q8K);
-    for (auto *w : L.gate_up.w)
-      if (!rc) rc = gemv_reserve(s->ctx, *w, MODE_Q8K);
-    if (!rc) rc = gemv_reserve(s->ctx, *L.out, MODE_Q8K);
-    if (!rc) rc = gemv_reserve(s->ctx, *L.down, MODE_Q8K);
-  }
-  if (!rc) rc = gemv_reserve(s->ctx, *m->output, MODE_Q8K);
+  // GEMV scratch (the projections that still run a prep kernel) sized before
+  // any graph capture
+  for (const auto &L : m->layers)
+    if (!rc && !L.attn) rc = gemv_reserve(s->ctx, *L.out, MODE_Q8K);
   if (!rc) {
-    const size_t out_smem =
-        round_up((size_t)ctx_len * 4, 16) + (size_t)((ctx_len + 1) / 2 + (ctx_len + 3) / 4 + 1) * 8;
-    cudaError_t e = cudaFuncSetAttribute(attn_out_kernel<256>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)out_smem);
+    const int sm_smem = (int)softmax_smem(ctx_len);
+    cudaError_t e = cudaFuncSetAttribute(attn_softmax_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, sm_smem);
     if (e == cudaSuccess)
-      e = cudaFuncSetAttribute(attn_out_kernel<128>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)out_smem);
+      e = cudaFuncSetAttribute(attn_values_kernel<256>, cudaFuncAttributeMaxDynamicSharedMemorySize, kChunk * 256 * 4);
+    if (e == cudaSuccess)
+      e = cudaFuncSetAttribute(attn_values_kernel<128>, cudaFuncAttributeMaxDynamicSharedMemorySize, kChunk * 128 * 4);
     rc = cuda_error(e, "attention smem");
   }
   if (!rc) rc = cuda_error(cudaDeviceSynchronize(), "session init");
@@ -1148,6 +1297,30 @@ int32_t unltd_qwen35_session_set_state(unltd_qwen35_session s, int32_t position,
   if (e != cudaSuccess) return cuda_error(e, "qwen35_set_state");
   s->host_pos = position;
   return UNLTD_OK;
+}
+
+// Copy the session state out in the layout set_state takes (the inverse of
+// unltd_qwen35_session_set_state at the current position); NULL skips.
+int32_t unltd_qwen35_session_get_state(unltd_qwen35_session s, float *const *conv, float *const *gdn,
+                                       float *const *kcache, float *const *vcache) {
+  if (!s) return set_error(UNLTD_ERR_INVALID_ARG, "qwen35_get_state: NULL session");
+  const Derived &d = s->m->d;
+  CtxGuard g(s->m->ctx->device);
+  cudaError_t e = cudaStreamSynchronize(s->ctx->stream);
+  const int position = s->host_pos;
+  for (int i = 0; e == cudaSuccess && i < s->m->n_recr; i++) {
+    for (int tau = 0; e == cudaSuccess && conv && conv[i] && tau < d.K - 1; tau++)
+      e = cudaMemcpy(conv[i] + (size_t)tau * d.dconv, s->ring[i] + (size_t)((position + tau) % d.K) * d.dconv,
+                     (size_t)d.dconv * 4, cudaMemcpyDeviceToHost);
+    if (e == cudaSuccess && gdn && gdn[i])
+      e = cudaMemcpy(gdn[i], s->state[i], (size_t)d.nv * d.hd * d.hd * 4, cudaMemcpyDeviceToHost);
+  }
+  for (int i = 0; e == cudaSuccess && i < s->m->n_attn; i++) {
+    const size_t part = (size_t)position * d.kvlen * 4;
+    if (part && kcache && kcache[i]) e = cudaMemcpy(kcache[i], s->kc[i], part, cudaMemcpyDeviceToHost);
+    if (e == cudaSuccess && part && vcache && vcache[i]) e = cudaMemcpy(vcache[i], s->vc[i], part, cudaMemcpyDeviceToHost);
+  }
+  return cuda_error(e, "qwen35_get_state");
 }
 
 // Teacher-forced steps over `tokens` (a prompt); then *next_token = the

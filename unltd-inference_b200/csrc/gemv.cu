@@ -34,6 +34,7 @@
 #include <utility>
 #include <vector>
 
+#include "q8k_span.cuh"
 #include "unltd_host.h"
 #include "unltd_internal.cuh"
 
@@ -120,77 +121,17 @@ __global__ void __launch_bounds__(kThreads) prep_q8k(const float *__restrict__ x
                                                      uint8_t *__restrict__ img,
                                                      unsigned long long *key, unsigned *done) {
   pdl_trigger();
-  __shared__ float red_a[8];
-  __shared__ int red_i[8];
-  __shared__ int hsum[16];
+  __shared__ Q8KSpanSmem sm;
   const int t = threadIdx.x;
   const size_t span = blockIdx.x;
   const size_t e = span * kQK + t;
-  if (t < 16) hsum[t] = 0;
   if (key && span == 0 && t == 0) {
     *key = 0ull;
     *done = 0u;
   }
-  float v = e < dim_in ? x[e] : 0.0f;
-  // first strict argmax of |x|; NaN never wins (the reference's `ax > amax`)
-  float a = fabsf(v);
-  if (isnan(a)) a = -1.0f;
-  int idx = t;
-  for (int o = 16; o; o >>= 1) {
-    float oa = __shfl_xor_sync(0xffffffffu, a, o);
-    int oi = __shfl_xor_sync(0xffffffffu, idx, o);
-    if (oa > a || (oa == a && oi < idx)) {
-      a = oa;
-      idx = oi;
-    }
-  }
-  if ((t & 31) == 0) {
-    red_a[t >> 5] = a;
-    red_i[t >> 5] = idx;
-  }
-  __syncthreads();
-  float amax = red_a[0];
-  int imax = red_i[0];
-  for (int w = 1; w < 8; w++) {
-    if (red_a[w] > amax || (red_a[w] == amax && red_i[w] < imax)) {
-      amax = red_a[w];
-      imax = red_i[w];
-    }
-  }
-  int q = 0;
-  float d = 0.0f;
-  if (amax > 0.0f) {
-    size_t em = span * kQK + imax;
-    float mx = em < dim_in ? x[em] : 0.0f;
-    float iscale = __fdiv_rn(-127.0f, mx);
-    float prod = __fmul_rn(iscale, v);
-    int ni = (__float_as_int(__fadd_rn(prod, 12582912.0f)) & 0x007fffff) - 0x00400000;
-    q = ni < 127 ? ni : 127;
-    d = __fdiv_rn(1.0f, iscale);
-  }
-  if constexpr (FMT == Q4K) {
-    uint8_t *im = img + span * kImgQ8K4;
-    im[q4_xpos(t)] = (uint8_t)(int8_t)q;
-    int p = t >> 6, half = (t >> 5) & 1, k = t & 7;
-    atomicAdd(&hsum[2 * (2 * p + (k >> 2)) + half], q);
-    __syncthreads();
-    if (t == 0) *reinterpret_cast<float *>(im + kImgQ8K4_D) = d;
-    if (t < 16) reinterpret_cast<int *>(im + kImgQ8K4_BS)[t] = hsum[t];
-  } else {
-    // Q6_K: element -> (lane j, half hh, run position ipos); word w = (ipos%8)/2
-    // holds run positions (2w, 2w+8 | 2w+1, 2w+9); masked copies A (bytes 0,1)
-    // and B (bytes 2,3). Each element writes its byte into one copy and a zero
-    // into the same byte of the other, so every byte is written once.
-    uint8_t *im = img + span * kImgQ8K6;
-    int h = t >> 7, pos = t & 127, hh = pos >> 6, c = pos & 63, u = c >> 4, ipos = c & 15;
-    int j = 4 * h + u;
-    int pic = q6_pic(ipos);
-    int w = pic >> 2, bpos = pic & 3;
-    int own = bpos < 2 ? 0 : 1;
-    im[q6_q8k_byte(j, hh, w, own, bpos)] = (uint8_t)(int8_t)q;
-    im[q6_q8k_byte(j, hh, w, 1 - own, bpos)] = 0;
-    if (t == 0) *reinterpret_cast<float *>(im + kImgQ8K6_D) = d;
-  }
+  const float v = e < dim_in ? x[e] : 0.0f;
+  if constexpr (FMT == Q4K) q8k_span_write(v, img + span * kImgQ8K4, nullptr, sm);
+  else q8k_span_write(v, nullptr, img + span * kImgQ8K6, sm);
 }
 
 // ---------------------------------------------------------------- gemv ----
@@ -473,6 +414,9 @@ __global__ void __launch_bounds__(kGemvThreads, 1) gemv_kernel(Params P) {
   uint8_t *ximg = smem + kBarBytes;
   float *cbuf0 = reinterpret_cast<float *>(ximg + P.img_bytes);
   uint8_t *stages = reinterpret_cast<uint8_t *>(cbuf0) + 2 * P.cbuf_bytes;
+  // let the next kernel of the stream get resident; it waits for this grid's
+  // completion (griddepcontrol.wait) before touching anything this grid uses
+  pdl_trigger();
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int G = gridDim.x;
@@ -783,7 +727,9 @@ int32_t gemv_launch(unltd_ctx ctx, const GemvArgs &a) {
   const int nspans = fmt == Q8_0 ? (int)((w.nb + 7) / 8) : (int)w.nb;
   const int nbu = nspans;
   const int img_bytes = nspans * img_stride(fmt, mode);
-  if (int32_t rc = gemv_reserve(ctx, w, mode)) return rc;
+  if (!a.img) {
+    if (int32_t rc = gemv_reserve(ctx, w, mode)) return rc;
+  }
 
   // ---- tiling: rows per tile T, stages S, shared-memory plan ----
   const int rows = (int)w.dim_out;
@@ -826,10 +772,12 @@ int32_t gemv_launch(unltd_ctx ctx, const GemvArgs &a) {
   const int smem = kBarBytes + img_bytes + 2 * cbuf + S * stage_bytes;
   const int grid = std::max(1, std::min(ctx->num_sms, (rows + T - 1) / T));
 
-  // 1) prep
+  // 1) prep (skipped when the caller's kernel already wrote the image)
   unsigned long long *key = am ? a.argmax_key : nullptr;
   unsigned *done = am ? a.argmax_done : nullptr;
-  if (mode == MODE_F32X) {
+  cudaError_t e = cudaSuccess;
+  if (a.img) {
+  } else if (mode == MODE_F32X) {
     if (fmt == Q4K) prep_f32x<Q4K><<<nspans, kThreads, 0, st>>>(a.x, w.dim_in, ctx->scratch, key, done);
     else if (fmt == Q6K) prep_f32x<Q6K><<<nspans, kThreads, 0, st>>>(a.x, w.dim_in, ctx->scratch, key, done);
     else prep_f32x<Q8_0><<<nspans, kThreads, 0, st>>>(a.x, w.dim_in, ctx->scratch, key, done);
@@ -837,9 +785,11 @@ int32_t gemv_launch(unltd_ctx ctx, const GemvArgs &a) {
     if (fmt == Q4K) prep_q8k<Q4K><<<nspans, kThreads, 0, st>>>(a.x, w.dim_in, ctx->scratch, key, done);
     else prep_q8k<Q6K><<<nspans, kThreads, 0, st>>>(a.x, w.dim_in, ctx->scratch, key, done);
   }
-  cudaError_t e = cudaGetLastError();
-  if (e != cudaSuccess) return cuda_error(e, "gemv prep");
-  ctx->launches += 1;
+  if (!a.img) {
+    e = cudaGetLastError();
+    if (e != cudaSuccess) return cuda_error(e, "gemv prep");
+    ctx->launches += 1;
+  }
 
   // 2) gemv, programmatic dependent launch
   GemvFn fn = am ? pick<true>(fmt, mode, R) : pick<false>(fmt, mode, R);
@@ -851,7 +801,7 @@ int32_t gemv_launch(unltd_ctx ctx, const GemvArgs &a) {
   P.nb = (int)w.nb;
   P.nbu = nbu;
   P.rows = rows;
-  P.img = ctx->scratch;
+  P.img = a.img ? a.img : ctx->scratch;
   P.img_bytes = img_bytes;
   P.y = a.y;
   P.key = a.argmax_key;

@@ -1,0 +1,90 @@
+// Exact quantize_q8_k (crates/unltd-tensor/src/quants.rs:250-290) of one
+// 256-element span held one element per thread by a 256-thread CTA, written
+// into the GEMV x images (layouts in unltd_internal.cuh). Shared by the GEMV
+// prep kernel and the fused producer kernels of the decode step.
+#pragma once
+
+#include "unltd_internal.cuh"
+
+namespace unltd {
+
+struct Q8KSpanSmem {
+  float a[8];
+  float v[8];
+  int i[8];
+  int hsum[16];
+};
+
+// v = element t (threadIdx.x) of the span. im4 / im6 (either may be null):
+// this span's Q4_K / Q6_K image. All 256 threads must call.
+__device__ __forceinline__ void q8k_span_write(float v, uint8_t *im4, uint8_t *im6, Q8KSpanSmem &s) {
+  const int t = threadIdx.x;
+  if (t < 16) s.hsum[t] = 0;
+  // first strict argmax of |x|; NaN never wins (the reference's `ax > amax`)
+  float a = fabsf(v);
+  if (isnan(a)) a = -1.0f;
+  int idx = t;
+  float val = v;
+#pragma unroll
+  for (int o = 16; o; o >>= 1) {
+    const float oa = __shfl_xor_sync(0xffffffffu, a, o);
+    const int oi = __shfl_xor_sync(0xffffffffu, idx, o);
+    const float ov = __shfl_xor_sync(0xffffffffu, val, o);
+    if (oa > a || (oa == a && oi < idx)) {
+      a = oa;
+      idx = oi;
+      val = ov;
+    }
+  }
+  if ((t & 31) == 0) {
+    s.a[t >> 5] = a;
+    s.i[t >> 5] = idx;
+    s.v[t >> 5] = val;
+  }
+  __syncthreads();
+  float amax = s.a[0], mx = s.v[0];
+  int imax = s.i[0];
+#pragma unroll
+  for (int w = 1; w < 8; w++) {
+    if (s.a[w] > amax || (s.a[w] == amax && s.i[w] < imax)) {
+      amax = s.a[w];
+      imax = s.i[w];
+      mx = s.v[w];
+    }
+  }
+  int q = 0;
+  float d = 0.0f;
+  if (amax > 0.0f) {
+    const float iscale = __fdiv_rn(-127.0f, mx);
+    const float prod = __fmul_rn(iscale, v);
+    const int ni = (__float_as_int(__fadd_rn(prod, 12582912.0f)) & 0x007fffff) - 0x00400000;
+    q = ni < 127 ? ni : 127;
+    d = __fdiv_rn(1.0f, iscale);
+  }
+  if (im4) {
+    im4[q4_xpos(t)] = (uint8_t)(int8_t)q;
+    const int p = t >> 6, half = (t >> 5) & 1, k = t & 7;
+    atomicAdd(&s.hsum[2 * (2 * p + (k >> 2)) + half], q);
+  }
+  if (im6) {
+    // element -> (lane j, half hh, run position ipos); word w = (ipos%8)/2 holds
+    // run positions (2w, 2w+8 | 2w+1, 2w+9); masked copies A (bytes 0,1) and
+    // B (bytes 2,3): each element writes its byte into one copy and a zero
+    // into the same byte of the other, so every byte is written once.
+    const int h = t >> 7, pos = t & 127, hh = pos >> 6, c = pos & 63, u = c >> 4, ipos = c & 15;
+    const int j = 4 * h + u;
+    const int pic = q6_pic(ipos);
+    const int w = pic >> 2, bpos = pic & 3;
+    const int own = bpos < 2 ? 0 : 1;
+    im6[q6_q8k_byte(j, hh, w, own, bpos)] = (uint8_t)(int8_t)q;
+    im6[q6_q8k_byte(j, hh, w, 1 - own, bpos)] = 0;
+    if (t == 0) *reinterpret_cast<float *>(im6 + kImgQ8K6_D) = d;
+  }
+  __syncthreads();
+  if (im4) {
+    if (t == 0) *reinterpret_cast<float *>(im4 + kImgQ8K4_D) = d;
+    if (t < 16) reinterpret_cast<int *>(im4 + kImgQ8K4_BS)[t] = s.hsum[t];
+  }
+}
+
+}  // namespace unltd

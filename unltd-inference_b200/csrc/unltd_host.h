@@ -75,6 +75,9 @@ struct GemvArgs {
   unsigned long long *argmax_key;  // non-null: fused argmax
   unsigned int *argmax_done;
   uint32_t *token;
+  // Non-null: the x image was already written (by a fused producer kernel
+  // that ran before on the same stream, in this mode's layout); no prep.
+  const uint8_t *img = nullptr;
 };
 int32_t gemv_launch(unltd_ctx ctx, const GemvArgs &a);
 // Grow the context's x-image scratch for w (call before stream capture).

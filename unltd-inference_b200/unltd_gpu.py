@@ -11,8 +11,11 @@ raises ``UnltdError`` when it fails or when no device is present.
 """
 from __future__ import annotations
 
+import atexit
 import ctypes
 import os
+import sys
+import weakref
 
 import numpy as np
 
@@ -60,6 +63,7 @@ SIGNATURES = [
     ("unltd_qwen35_session_create", _I, [_P, _I, ctypes.POINTER(_P)]),
     ("unltd_qwen35_session_destroy", _I, [_P]),
     ("unltd_qwen35_session_set_state", _I, [_P, _I, _P, _P, _P, _P]),
+    ("unltd_qwen35_session_get_state", _I, [_P, _P, _P, _P, _P]),
     ("unltd_qwen35_feed", _I, [_P, _P, _I, _P]),
     ("unltd_qwen35_decode", _I, [_P, ctypes.c_uint32, _I, _P]),
     ("unltd_qwen35_session_info", _I, [_P, ctypes.POINTER(_I), ctypes.POINTER(_P), ctypes.POINTER(_I64)]),
@@ -74,6 +78,25 @@ class UnltdError(RuntimeError):
 
 
 _lib = None
+
+# Live handles by release order (sessions, models, weights, contexts): closed
+# in that order at interpreter exit, before module teardown, so no handle is
+# released after the context it lives in.
+_live = [weakref.WeakSet() for _ in range(4)]
+
+
+def _track(obj, rank: int):
+    _live[rank].add(obj)
+
+
+@atexit.register
+def _close_all():
+    for group in _live:
+        for o in list(group):
+            try:
+                o.close()
+            except Exception:
+                pass
 
 
 def lib():
@@ -123,6 +146,7 @@ class Context:
         _check(lib().unltd_ctx_create(device, ctypes.byref(h)))
         self.h = h
         self.device = device
+        _track(self, 3)
         if stream is not None:
             self.set_stream(stream)
 
@@ -173,7 +197,9 @@ class Context:
             lib().unltd_ctx_destroy(self.h)
             self.h = None
 
-    def __del__(self):
+    def __del__(self, _finalizing=sys.is_finalizing):
+        if _finalizing():
+            return
         try:
             self.close()
         except Exception:
@@ -183,6 +209,7 @@ class Context:
 class Weight:
     def __init__(self, ctx: Context, h, dtype, dim_in, dim_out):
         self.ctx, self.h, self.dtype, self.dim_in, self.dim_out = ctx, h, dtype, dim_in, dim_out
+        _track(self, 2)
 
     def info(self):
         dt, di, do, nb = _I(), _S(), _S(), _S()
@@ -194,7 +221,11 @@ class Weight:
             lib().unltd_weight_free(self.h)
             self.h = None
 
-    def __del__(self):
+    close = free
+
+    def __del__(self, _finalizing=sys.is_finalizing):
+        if _finalizing():
+            return
         try:
             if self.ctx.h:
                 self.free()
@@ -248,6 +279,7 @@ class Qwen35Model:
         h = ctypes.c_void_p()
         _check(lib().unltd_qwen35_create(ctx.h, ctypes.byref(self._c), ctypes.byref(h)))
         self.h = h
+        _track(self, 1)
 
     def set_tensor(self, name: str, data: np.ndarray, dtype: int):
         data = np.ascontiguousarray(data)
@@ -269,7 +301,9 @@ class Qwen35Model:
             lib().unltd_qwen35_destroy(self.h)
             self.h = None
 
-    def __del__(self):
+    def __del__(self, _finalizing=sys.is_finalizing):
+        if _finalizing():
+            return
         try:
             self.close()
         except Exception:
@@ -287,10 +321,27 @@ def _ptr_array(arrs):
 class Qwen35Session:
     def __init__(self, model: Qwen35Model, h, ctx_len: int):
         self.model, self.h, self.ctx_len = model, h, ctx_len
+        _track(self, 0)
 
     def set_state(self, position: int, conv=None, gdn=None, kcache=None, vcache=None):
         ptrs = [_ptr_array(a) for a in (conv, gdn, kcache, vcache)]
         _check(lib().unltd_qwen35_session_set_state(self.h, position, *[p[0] for p in ptrs]))
+
+    def get_state(self) -> dict:
+        """The state at the current position: conv windows, GDN matrices, K/V rows."""
+        cfg = self.model.cfg
+        hd = cfg["d_inner"] // (2 * cfg["group_count"])
+        nv, dconv, kvlen = cfg["d_inner"] // hd, 2 * cfg["d_inner"], cfg["n_head_kv"] * cfg["head_dim"]
+        attn = [(il + 1) % cfg["full_attn_interval"] == 0 for il in range(cfg["n_layer"])]
+        pos = self.info()["position"]
+        st = {"conv": [np.zeros((cfg["conv_kernel"] - 1, dconv), np.float32) for a in attn if not a],
+              "gdn": [np.zeros((nv, hd, hd), np.float32) for a in attn if not a],
+              "k": [np.zeros((pos, kvlen), np.float32) for a in attn if a],
+              "v": [np.zeros((pos, kvlen), np.float32) for a in attn if a]}
+        ptrs = [_ptr_array(st[k]) for k in ("conv", "gdn", "k", "v")]
+        # _ptr_array copies non-contiguous inputs; these are contiguous, so it points at st's arrays
+        _check(lib().unltd_qwen35_session_get_state(self.h, *[p[0] for p in ptrs]))
+        return st
 
     def feed(self, tokens) -> int:
         t = np.ascontiguousarray(tokens, dtype=np.uint32)
@@ -321,7 +372,9 @@ class Qwen35Session:
             lib().unltd_qwen35_session_destroy(self.h)
             self.h = None
 
-    def __del__(self):
+    def __del__(self, _finalizing=sys.is_finalizing):
+        if _finalizing():
+            return
         try:
             if self.model.h:
                 self.close()
