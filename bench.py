@@ -193,6 +193,83 @@ def cpu_baseline(steps=3):
     }
 
 
+def decode_bytes_per_token(cfg, position):
+    """Bytes one greedy decode step must move: every projection's packed
+    weights, the LM head, one embedding row, the f32 norms and conv kernels,
+    the GDN matrices (read and written), the conv windows and the K/V rows of
+    the `position + 1` cached positions (qwen35_forward.rs step)."""
+    d = synth.qwen35_dims(cfg)
+    total = 0
+    for nm, dt, di, do in synth.qwen35_tensor_list(cfg):
+        if nm == "token_embd.weight":
+            total += synth.row_bytes(dt, di)
+        else:
+            total += synth.row_bytes(dt, di) * do
+    n_attn = sum(d["attn"])
+    n_recr = cfg["n_layer"] - n_attn
+    total += n_recr * (2 * 4 * d["nv"] * d["hd"] * d["hd"] + 4 * cfg["conv_kernel"] * d["dconv"])
+    total += n_attn * 2 * 4 * (position + 1) * d["kvlen"]
+    return total
+
+
+def decode_bench(n_tokens, with_cpu):
+    """greedy decode of the synthetic 9B-class hybrid model
+    from a 2048-position context, one GPU, through unltd_qwen35_decode."""
+    import torch
+
+    import unltd_gpu as ug
+
+    cfg = synth.QWEN35_9B
+    pos0 = 2048
+    tensors = synth.qwen35_model(cfg, 2026)
+    st = synth.qwen35_state(cfg, pos0, 2027)
+    ctx = ug.Context(torch.cuda.current_device())
+    m = ug.Qwen35Model(ctx, cfg)
+    m.load(tensors)
+    s = m.session(pos0 + n_tokens + 16)
+    s.set_state(pos0, st["conv"], st["gdn"], st["k"], st["v"])
+    warm = s.decode(1000, 8)
+    info = s.info()
+    ext = torch.cuda.ExternalStream(info["stream"])
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    torch.cuda.synchronize()
+    t0 = time.perf_counter()
+    e0.record(ext)
+    toks = s.decode(int(warm[-1]), n_tokens)
+    e1.record(ext)
+    torch.cuda.synchronize()
+    wall = time.perf_counter() - t0
+    ms_tok = e0.elapsed_time(e1) / n_tokens
+    bpt = decode_bytes_per_token(cfg, pos0 + 8 + n_tokens // 2)
+    peak, peak_kind = _peaks()
+    out = {
+        "workload": "config3_qwen35_9b_synthetic_greedy_decode_ctx2048", "n_tokens": n_tokens,
+        "tok_s": round(1e3 / ms_tok, 2), "ms_per_token": round(ms_tok, 4),
+        "e2e_tok_s": round(n_tokens / wall, 2),
+        "bytes_per_token": bpt, "hbm_gbs": round(bpt / (ms_tok * 1e-3) / 1e9, 1),
+        "roofline_frac": round(bpt / (ms_tok * 1e-3) / 1e9 / peak, 4), "peak": peak, "peak_kind": peak_kind,
+        "launches_per_step": info["launches_per_step"], "graph": "one CUDA graph per token",
+        "arithmetic": "Q8K_EXACT projections; f32/f64 ops in the reference's order (hidden states bit-identical to the oracle)",
+        "tokens_tail": [int(t) for t in toks[-4:]],
+    }
+    s.close()
+    m.close()
+    ctx.close()
+    if with_cpu:
+        import oracle
+
+        o = oracle.Qwen35Oracle(cfg, tensors, pos0 + 8, st, pos0)
+        ncores = os.cpu_count() or 1
+        t0 = time.perf_counter()
+        o.step(1000, nthreads=ncores)
+        cpu_s = time.perf_counter() - t0
+        out["cpu_baseline"] = {"tok_s": round(1.0 / cpu_s, 4), "cores": ncores, "kind": "port",
+                               "sample": "1 decode step of the same model and state (oracle restatement of "
+                                         "qwen35_forward.rs, projections row-parallel on all cores)"}
+    del tensors
+    return out
+
+
 def run_reference(args):
     rank, world, _ = _dist_env()
     if rank != 0:
@@ -245,6 +322,8 @@ def main():
     ap.add_argument("--no-gemm", action="store_true")
     ap.add_argument("--only", default=None, help="comma-separated subset of the mix (profiling)")
     ap.add_argument("--mode", default="q8k", choices=["q8k", "f32x"], help="arithmetic of the K-quant GEMVs")
+    ap.add_argument("--no-decode", action="store_true", help="skip the config-3 decode measurement")
+    ap.add_argument("--decode-tokens", type=int, default=64)
     args = ap.parse_args()
     if args.impl == "reference":
         return run_reference(args)
@@ -415,10 +494,14 @@ def main():
             "workload": "config2_prefill_gemm_q4k_512x4096x12288", "ms": round(gms, 4),
             "tflops": round(flops / (gms * 1e-3) / 1e12, 1), "peak_tflops": peak_tf, "peak_kind": peak_tf_kind,
             "frac": round(flops / (gms * 1e-3) / 1e12 / peak_tf, 4),
-            "note": "includes the X f32->bf16 conversion kernel; bf16 operands, f32 accumulation",
+            "note": "includes the X f32->fp16 conversion kernel; fp16 operands, f32 accumulation",
         }
         gw.free()
         del GX, GY
+
+    decode = None
+    if world == 1 and args.only is None and not args.no_decode:
+        decode = decode_bench(args.decode_tokens, with_cpu=not args.no_cpu_baseline)
 
     peak, peak_kind = _peaks()
     step_bytes = sum(it["bytes"] for it in items)
@@ -450,6 +533,7 @@ def main():
         "clocks": sampler.summary(),
         "e2e": e2e,
         "gemm_prefill": gemm,
+        "decode": decode,
     }
     if rank == 0 and world == 1 and not args.no_cpu_baseline and args.only is None:
         line["cpu_baseline"] = cpu_baseline()
