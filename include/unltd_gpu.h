@@ -157,6 +157,16 @@ int32_t unltd_dequant(unltd_ctx ctx, unltd_weight w, float *out_dev);
  * (symbol address, kernel attributes); make it before any stream capture. */
 int32_t unltd_gemv_noalloc(unltd_weight w, const float *x_dev, float *y_dev, int32_t mode, void *stream);
 
+/* ---- NCCL communicators (tensor parallelism, one process per GPU) ----------
+ * NCCL is loaded at run time (libnccl.so.2, the copy the process already has
+ * if any). Rank 0 creates the 128-byte id, the caller distributes it (e.g. a
+ * torch.distributed broadcast), every rank calls unltd_comm_init. */
+int32_t unltd_comm_unique_id(void *id_out, size_t id_bytes);
+int32_t unltd_comm_init(unltd_ctx ctx, int32_t rank, int32_t world, const void *id, size_t id_bytes);
+/* In-place all-reduces on the context's stream. */
+int32_t unltd_allreduce_sum_f32(unltd_ctx ctx, float *buf_dev, size_t count);
+int32_t unltd_allreduce_max_u64(unltd_ctx ctx, uint64_t *buf_dev, size_t count);
+
 /* ---- Qwen3.5-style hybrid decode step ------------------------------------
  * Replaces Qwen35Forward (crates/unltd-generation/src/qwen35_forward.rs):
  * open (139-232: every tensor checked for shape and dtype), new_session
@@ -177,6 +187,21 @@ typedef struct unltd_qwen35_s *unltd_qwen35;
 typedef struct unltd_qwen35_session_s *unltd_qwen35_session;
 
 int32_t unltd_qwen35_create(unltd_ctx ctx, const unltd_qwen35_config *cfg, unltd_qwen35 *out);
+/* Tensor-parallel shard `rank` of `world` GPUs (one process per GPU; the
+ * context needs a communicator, unltd_comm_init). set_tensor still takes the
+ * full GGUF tensors and keeps this rank's part: q/k/v, qkv/z/beta/alpha and
+ * gate/up by output rows (heads), ffn_down, ssm_out and attn_output by input
+ * columns with an NCCL all-reduce of their partial outputs, the LM head by
+ * vocab rows with a cross-GPU argmax (all-reduce MAX of 64-bit keys). */
+int32_t unltd_qwen35_create_tp(unltd_ctx ctx, const unltd_qwen35_config *cfg, int32_t rank, int32_t world,
+                               unltd_qwen35 *out);
+/* Host-only (no GPU): the part of tensor `name` that rank `rank` of `world`
+ * keeps, as source row ranges [ranges[2i], ranges[2i+1]) (element ranges for
+ * F32 tensors), concatenated in order, each row restricted to input columns
+ * [*in_begin, *in_end). */
+int32_t unltd_qwen35_shard(const unltd_qwen35_config *cfg, int32_t rank, int32_t world, const char *name,
+                           int64_t *ranges, int32_t max_ranges, int32_t *n_ranges, int64_t *in_begin,
+                           int64_t *in_end);
 /* Upload one GGUF tensor by its name ("blk.3.attn_q.weight", "output.weight",
  * ...): packed bytes or F32 values, checked against the configuration. */
 int32_t unltd_qwen35_set_tensor(unltd_qwen35 m, const char *name, const void *host, size_t nbytes, int32_t dtype);
@@ -208,7 +233,12 @@ int32_t unltd_qwen35_decode(unltd_qwen35_session s, uint32_t token, int32_t n_st
 /* Position, the session's cudaStream_t, kernels launched per step. */
 int32_t unltd_qwen35_session_info(unltd_qwen35_session s, int32_t *position, void **stream,
                                   int64_t *launches_per_step);
-/* Last step's logits (vocab) and hidden state (l_out of the last layer). */
+/* Per-rank sizes: conv window row (channels), GDN heads, K/V row, and the
+ * vocab rows [begin, end) whose logits this rank holds. */
+int32_t unltd_qwen35_session_shape(unltd_qwen35_session s, int64_t *conv_row, int64_t *gdn_heads,
+                                   int64_t *kv_row, int64_t *vocab_begin, int64_t *vocab_end);
+/* Last step's logits (this rank's vocab rows) and hidden state (l_out of the
+ * last layer, full n_embd on every rank). */
 int32_t unltd_qwen35_session_read(unltd_qwen35_session s, float *logits, float *hidden);
 
 /* ---- reference-signature API (host buffers, synchronous) ---------------- */

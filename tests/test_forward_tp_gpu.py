@@ -1,0 +1,44 @@
+"""Tensor-parallel decode on 2 GPUs (tests/tp_decode_check.py under torchrun)
+against the CPU oracle: identical greedy stream, logits and hidden state
+within 1e-3 max-rel (the row-split projections sum partial outputs across
+GPUs, so the f32 rounding differs from the single-device reference)."""
+import json
+import os
+import socket
+import subprocess
+import sys
+
+import pytest
+
+pytestmark = pytest.mark.gpu
+torch = pytest.importorskip("torch")
+HERE = os.path.dirname(os.path.abspath(__file__))
+TOL = 1e-3
+
+
+def _port():
+    s = socket.socket()
+    s.bind(("127.0.0.1", 0))
+    p = s.getsockname()[1]
+    s.close()
+    return p
+
+
+def test_tp2_tiny_decode_matches_oracle():
+    if not torch.cuda.is_available() or torch.cuda.device_count() < 2:
+        pytest.skip("needs 2 GPUs")
+    from __graft_entry__ import build
+
+    build()
+    env = dict(os.environ, NCCL_NVLS_ENABLE="0")
+    cmd = ["timeout", "-k", "30", "600", sys.executable, "-m", "torch.distributed.run", "--nnodes=1",
+           "--nproc-per-node", "2", "--master-addr", "127.0.0.1", "--master-port", str(_port()),
+           os.path.join(HERE, "tp_decode_check.py"), "--model", "tiny", "--steps", "8"]
+    r = subprocess.run(cmd, capture_output=True, text=True, env=env)
+    assert r.returncode == 0, r.stderr[-3000:]
+    line = [l for l in r.stdout.splitlines() if l.startswith("{")][-1]
+    out = json.loads(line)
+    print(out)
+    assert out["same_stream_on_all_ranks"] and out["argmax_matches_gathered_logits"]
+    assert out["stream_matches_oracle"], out
+    assert out["logits_maxrel"] <= TOL and out["hidden_maxrel"] <= TOL, out

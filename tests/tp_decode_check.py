@@ -1,0 +1,93 @@
+"""Tensor-parallel greedy decode on N GPUs against the single-process CPU
+oracle; run with torchrun (one process per GPU), e.g.
+
+    python -m torch.distributed.run --nnodes=1 --nproc-per-node 2 \
+        --master-addr 127.0.0.1 --master-port 29512 tests/tp_decode_check.py --model tiny
+
+Every rank holds its shard (unltd_qwen35_create_tp); rank 0 compares the
+greedy stream, the full logits (gathered from the vocab shards) and the
+hidden state with the oracle and prints one JSON line. The row-split
+projections sum their partial outputs across GPUs, so logits and hidden
+states match the oracle within a tolerance rather than bit for bit; the
+token stream must be identical.
+"""
+import argparse
+import datetime
+import json
+import os
+import sys
+import time
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+REPO = os.path.dirname(HERE)
+sys.path[:0] = [os.path.join(REPO, "unltd-inference_b200"), os.path.join(REPO, "oracle"), REPO]
+
+import numpy as np  # noqa: E402
+import torch  # noqa: E402
+import torch.distributed as dist  # noqa: E402
+
+import synth  # noqa: E402
+import unltd_gpu as ug  # noqa: E402
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--model", default="tiny", choices=["tiny", "9b"])
+    ap.add_argument("--steps", type=int, default=8)
+    ap.add_argument("--position", type=int, default=40)
+    ap.add_argument("--no-oracle", action="store_true")
+    args = ap.parse_args()
+    rank, world, local = int(os.environ["RANK"]), int(os.environ["WORLD_SIZE"]), int(os.environ["LOCAL_RANK"])
+    torch.cuda.set_device(local)
+    dist.init_process_group("gloo", timeout=datetime.timedelta(seconds=300))
+    cfg = synth.QWEN35_TINY if args.model == "tiny" else synth.QWEN35_9B
+    seed = 11 if args.model == "tiny" else 2026
+    pos0, n = args.position, args.steps
+    tensors = synth.qwen35_model(cfg, seed)
+    st = synth.qwen35_state(cfg, pos0, seed + 1)
+    ctx = ug.Context(local)
+    ctx.comm_init(rank, world, ug.exchange_unique_id())
+    m = ug.Qwen35Model(ctx, cfg, rank, world)
+    m.load(tensors)
+    s = m.session(pos0 + n + 10)
+    s.set_state(pos0, st["conv"], st["gdn"], st["k"], st["v"])
+    warm = s.decode(5 if args.model == "tiny" else 1000, 2)  # captures the step graph
+    dist.barrier()
+    torch.cuda.synchronize()
+    t0 = time.perf_counter()
+    toks = s.decode(int(warm[-1]), n)
+    dt = time.perf_counter() - t0
+    toks = np.concatenate([warm, toks])
+    lg, hd = s.read()
+    v0, v1 = s.shape()["vocab"]
+    parts = [None] * world
+    dist.all_gather_object(parts, (v0, v1, lg))
+    streams = [None] * world
+    dist.all_gather_object(streams, toks.tolist())
+    out = {"model": args.model, "world": world, "steps": n, "position": pos0, "tokens": toks.tolist(),
+           "same_stream_on_all_ranks": all(x == streams[0] for x in streams),
+           "tok_s": round(n / dt, 2), "ms_per_token": round(dt / n * 1e3, 4)}
+    if rank == 0:
+        logits = np.zeros(cfg["vocab"], np.float32)
+        for a, b, l in parts:
+            logits[a:b] = l
+        out["argmax_matches_gathered_logits"] = bool(int(np.argmax(logits)) == int(toks[-1]))
+        if not args.no_oracle:
+            import oracle
+
+            o = oracle.Qwen35Oracle(cfg, tensors, pos0 + n + 10, st, pos0)
+            otoks, ol, oh = o.greedy(5 if args.model == "tiny" else 1000, n + 2, nthreads=os.cpu_count() or 8)
+            out["oracle_tokens"] = otoks
+            out["stream_matches_oracle"] = otoks == toks.tolist()
+            out["logits_maxrel"] = float(np.max(np.abs(logits - ol)) / np.max(np.abs(ol)))
+            out["hidden_maxrel"] = float(np.max(np.abs(hd - oh)) / np.max(np.abs(oh)))
+        print(json.dumps(out), flush=True)
+    s.close()
+    m.close()
+    ctx.close()
+    dist.barrier()
+    dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

@@ -84,7 +84,7 @@ def build(force: bool = False, jobs: int = 8, verbose: bool = False, ptxas_v: bo
                 if verbose and msg:
                     print(f"== {os.path.basename(futs[f])}\n{msg}")
     if force or todo or not os.path.exists(LIB):
-        cmd = [nvcc()] + ARCH + ["-shared", "-o", LIB] + objs + ["-lcuda"]
+        cmd = [nvcc()] + ARCH + ["-shared", "-o", LIB] + objs + ["-lcuda", "-ldl"]
         r = subprocess.run(cmd, capture_output=True, text=True)
         if r.returncode != 0:
             raise RuntimeError("link failed:\n" + r.stderr)

@@ -132,6 +132,7 @@ int32_t unltd_ctx_destroy(unltd_ctx c) {
   if (!c) return UNLTD_OK;
   CtxGuard g(c->device);
   cudaStreamSynchronize(c->stream);
+  comm_destroy(c);
   if (c->scratch) cudaFree(c->scratch);
   if (c->gemm_scratch) cudaFree(c->gemm_scratch);
   if (c->argmax_key) cudaFree(c->argmax_key);

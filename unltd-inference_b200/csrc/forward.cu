@@ -576,6 +576,14 @@ __global__ void __launch_bounds__(256) attn_combine_quant_kernel(AttnArgs a) {
                  a.img6 ? a.img6 + (size_t)span * kImgQ8K6 : nullptr, sm);
 }
 
+// greedy token from the cross-GPU maximum of the argmax keys
+// (orderable(logit) << 32 | ~global_row): the first index of the maximum
+__global__ void key_to_token_kernel(const unsigned long long *key, uint32_t *token) {
+  pdl_trigger();
+  pdl_wait();
+  *token = 0xffffffffu - (uint32_t)(*key & 0xffffffffull);
+}
+
 // token bookkeeping at the end of a step
 __global__ void step_end_kernel(const uint32_t *cur, uint32_t *hist, int *counter, int *pos) {
   pdl_trigger();
@@ -599,6 +607,14 @@ struct Derived {
   int n, nff, nh, nkv, hdv, n_rot, K, nqk, hd, nv, dconv, kvlen, vocab, n_layer, interval, nrp;
   float eps, kq_scale;
   double theta_scale;
+  // tensor-parallel shard of this rank (rank 0 of 1: the whole model)
+  int rank = 0, world = 1;
+  int nvl, nqkl, dconvl;   // recurrent: local v heads, local qk heads, local conv channels
+  int vh0;                 // first local v head
+  int nhl, nkvl, kvlenl;   // attention: local q heads, local kv heads
+  int qh0, kv0;            // first local q head / kv head
+  int nffl;                // local FFN width
+  int v0, v1;              // local vocab rows [v0, v1)
 };
 
 struct Part {
@@ -659,6 +675,7 @@ struct unltd_qwen35_session_s {
   float *q = nullptr, *scores = nullptr, *logits = nullptr;
   double2 *rope = nullptr, *part = nullptr;
   uint8_t *img4 = nullptr, *img6 = nullptr;  // x images written by the fused producer kernels
+  unsigned long long *tpkey = nullptr;       // this rank's LM-head argmax key, then the global one
   int nsplit = 0;
   uint32_t *cur_token = nullptr, *hist = nullptr, *feed = nullptr;
   int *counter = nullptr, *pos = nullptr;
@@ -721,7 +738,148 @@ int32_t derive(const unltd_qwen35_config &c, Derived *d) {
   return UNLTD_OK;
 }
 
+int32_t derive_tp(Derived *d, int rank, int world);
+
 bool is_attn(const Derived &d, int il) { return (il + 1) % d.interval == 0; }
+
+// Tensor-parallel split of rank `rank` of `world`: gate/up and the q/k/v and
+// qkv/z/beta/alpha projections by output rows (heads), down and the output
+// projections by input columns (their partial outputs are summed across
+// ranks), the LM head by vocab rows; norms, conv and GDN parameters follow
+// their heads; the embedding is replicated.
+int32_t derive_tp(Derived *d, int rank, int world) {
+  auto unsup = [](const std::string &m) { return set_error(UNLTD_ERR_UNSUPPORTED, "qwen35 tensor parallel: " + m); };
+  if (world < 1 || rank < 0 || rank >= world) return set_error(UNLTD_ERR_INVALID_ARG, "qwen35: bad rank/world");
+  d->rank = rank;
+  d->world = world;
+  if (d->nv % world) return unsup("v heads not divisible by the GPU count");
+  d->nvl = d->nv / world;
+  if (d->nvl <= d->nqk) {
+    d->nqkl = d->nvl;
+  } else {
+    if (d->nvl % d->nqk) return unsup("local v heads not a multiple of the qk heads");
+    d->nqkl = d->nqk;
+  }
+  d->vh0 = rank * d->nvl;
+  d->dconvl = 2 * d->nqkl * d->hd + d->nvl * d->hd;
+  if (world > 1 && (d->nvl * d->hd) % 256) return unsup("local recurrent width not a multiple of 256");
+  if (d->nh % world) return unsup("q heads not divisible by the GPU count");
+  d->nhl = d->nh / world;
+  const int G = d->nh / d->nkv;
+  if (d->nhl >= G) {
+    if (d->nhl % G) return unsup("local q heads split a kv group");
+    d->nkvl = d->nhl / G;
+  } else {
+    if (G % d->nhl) return unsup("kv group not divisible by the local q heads");
+    d->nkvl = 1;
+  }
+  d->qh0 = rank * d->nhl;
+  d->kv0 = d->qh0 / G;
+  d->kvlenl = d->nkvl * d->hdv;
+  if (world > 1 && (d->nhl * d->hdv) % 256) return unsup("local attention width not a multiple of 256");
+  if (d->nff % (256 * world)) return unsup("n_ff not a multiple of 256 x GPU count");
+  d->nffl = d->nff / world;
+  const int per = (d->vocab + world - 1) / world;
+  d->v0 = std::min(d->vocab, rank * per);
+  d->v1 = std::min(d->vocab, d->v0 + per);
+  if (d->v1 <= d->v0) return unsup("vocab smaller than the GPU count");
+  return UNLTD_OK;
+}
+
+// The rank's part of a tensor: source row ranges (element ranges for F32
+// tensors) concatenated in order, each row restricted to input columns
+// [in0, in1).
+struct Shard {
+  std::vector<std::pair<size_t, size_t>> rows;
+  size_t in0 = 0, in1 = 0;
+  size_t nrows() const {
+    size_t r = 0;
+    for (auto &p : rows) r += p.second - p.first;
+    return r;
+  }
+};
+
+Shard shard_of(const Derived &d, const std::string &name, size_t dim_in, size_t dim_out) {
+  Shard s;
+  s.in0 = 0;
+  s.in1 = dim_in;
+  const bool f32 = dim_out == 1;  // F32 tensors: "rows" are elements
+  const size_t len = f32 ? dim_in : dim_out;
+  if (f32) s.in1 = 1;
+  const std::string kind = name.compare(0, 4, "blk.") == 0 ? name.substr(name.find('.', 4) + 1) : name;
+  const size_t hd = d.hd, hdv = d.hdv;
+  auto all = [&]() { s.rows.push_back({0, len}); };
+  auto qk_rows = [&](size_t base, size_t unit) {  // rows of the local qk heads, in local order
+    for (int j = 0; j < d.nqkl; j++) {
+      const size_t gq = (size_t)((d.vh0 + j) % d.nqk);
+      s.rows.push_back({base + gq * unit, base + (gq + 1) * unit});
+    }
+  };
+  if (kind == "output.weight") {
+    s.rows.push_back({(size_t)d.v0, (size_t)d.v1});
+  } else if (kind == "ffn_gate.weight" || kind == "ffn_up.weight") {
+    s.rows.push_back({(size_t)d.rank * d.nffl, (size_t)(d.rank + 1) * d.nffl});
+  } else if (kind == "ffn_down.weight") {
+    all();
+    s.in0 = (size_t)d.rank * d.nffl;
+    s.in1 = s.in0 + d.nffl;
+  } else if (kind == "attn_q.weight") {
+    s.rows.push_back({(size_t)d.qh0 * 2 * hdv, (size_t)(d.qh0 + d.nhl) * 2 * hdv});
+  } else if (kind == "attn_k.weight" || kind == "attn_v.weight") {
+    s.rows.push_back({(size_t)d.kv0 * hdv, (size_t)(d.kv0 + d.nkvl) * hdv});
+  } else if (kind == "attn_output.weight") {
+    all();
+    s.in0 = (size_t)d.qh0 * hdv;
+    s.in1 = s.in0 + (size_t)d.nhl * hdv;
+  } else if (kind == "attn_qkv.weight") {
+    qk_rows(0, hd);
+    qk_rows((size_t)d.nqk * hd, hd);
+    s.rows.push_back({2 * (size_t)d.nqk * hd + (size_t)d.vh0 * hd, 2 * (size_t)d.nqk * hd + (size_t)(d.vh0 + d.nvl) * hd});
+  } else if (kind == "ssm_conv1d.weight") {  // [channel][tau]: channel ranges times K
+    const size_t K = d.K;
+    for (int j = 0; j < d.nqkl; j++) {
+      const size_t gq = (size_t)((d.vh0 + j) % d.nqk);
+      s.rows.push_back({gq * hd * K, (gq + 1) * hd * K});
+    }
+    for (int j = 0; j < d.nqkl; j++) {
+      const size_t gq = (size_t)((d.vh0 + j) % d.nqk);
+      s.rows.push_back({((size_t)d.nqk + gq) * hd * K, ((size_t)d.nqk + gq + 1) * hd * K});
+    }
+    s.rows.push_back({(2 * (size_t)d.nqk * hd + (size_t)d.vh0 * hd) * K, (2 * (size_t)d.nqk * hd + (size_t)(d.vh0 + d.nvl) * hd) * K});
+  } else if (kind == "attn_gate.weight") {
+    s.rows.push_back({(size_t)d.vh0 * hd, (size_t)(d.vh0 + d.nvl) * hd});
+  } else if (kind == "ssm_beta.weight" || kind == "ssm_alpha.weight" || kind == "ssm_dt.bias" || kind == "ssm_a") {
+    s.rows.push_back({(size_t)d.vh0, (size_t)(d.vh0 + d.nvl)});
+  } else if (kind == "ssm_out.weight") {
+    all();
+    s.in0 = (size_t)d.vh0 * hd;
+    s.in1 = s.in0 + (size_t)d.nvl * hd;
+  } else {
+    all();  // embedding, norms: replicated
+  }
+  // merge adjacent ranges (one range per tensor on a single GPU)
+  std::vector<std::pair<size_t, size_t>> merged;
+  for (auto &r : s.rows) {
+    if (!merged.empty() && merged.back().second == r.first) merged.back().second = r.second;
+    else merged.push_back(r);
+  }
+  s.rows = merged;
+  return s;
+}
+
+// Gather the rank's bytes of a host tensor (rows of row_bytes, blocks of
+// block_bytes covering block_elems input elements each).
+std::vector<uint8_t> gather_shard(const Shard &sh, const uint8_t *host, size_t row_bytes, size_t elem_per_block,
+                                  size_t block_bytes) {
+  const size_t b0 = sh.in0 / elem_per_block, b1 = sh.in1 / elem_per_block;
+  const size_t out_rb = (b1 - b0) * block_bytes;
+  std::vector<uint8_t> out(sh.nrows() * out_rb);
+  size_t o = 0;
+  for (auto &r : sh.rows)
+    for (size_t row = r.first; row < r.second; row++, o += out_rb)
+      memcpy(out.data() + o, host + row * row_bytes + b0 * block_bytes, out_rb);
+  return out;
+}
 
 // Expected tensors (qwen35_forward.rs:139-221, min_forward.rs): name -> shape, dtypes.
 std::vector<Part> expected(const Derived &d) {
@@ -891,6 +1049,12 @@ int32_t enqueue_step(unltd_qwen35_session s) {
     if (!rc) rc = cuda_error(e, what);
     nl++;
   };
+  // partial outputs of the input-split projections: sum over the ranks (NCCL)
+  auto allreduce = [&](float *buf, int count) {
+    if (d.world == 1) return;
+    if (!rc) rc = comm_allreduce(m->ctx, st, buf, (size_t)count, false);
+    nl++;
+  };
   auto norm = [&](const float *a, const float *b, float *r_out, const float *w, bool q4, bool q6, bool argmax) {
     NormArgs p{a, b, r_out, w, d.n, d.eps, q4 ? s->img4 : nullptr, q6 ? s->img6 : nullptr,
                argmax ? s->ctx->argmax_key : nullptr, argmax ? s->ctx->argmax_done : nullptr};
@@ -919,19 +1083,20 @@ int32_t enqueue_step(unltd_qwen35_session s) {
       a.y = s->Y;
       a.pos = s->pos;
       a.K = d.K;
-      a.nqk = d.nqk;
-      a.nv = d.nv;
-      a.dconv = d.dconv;
-      a.z_off = d.dconv;
-      a.beta_off = d.dconv + d.n;
-      a.alpha_off = d.dconv + d.n + d.nv;
+      a.nqk = d.nqkl;
+      a.nv = d.nvl;
+      a.dconv = d.dconvl;
+      a.z_off = d.dconvl;
+      a.beta_off = d.dconvl + d.nvl * d.hd;
+      a.alpha_off = a.beta_off + d.nvl;
       a.eps = d.eps;
-      chk(launch_pdl(recr_mid_kernel<128>, dim3(d.nv), dim3(128), 0, st, a), "recr_mid");
+      chk(launch_pdl(recr_mid_kernel<128>, dim3(d.nvl), dim3(128), 0, st, a), "recr_mid");
       nl += launch_gemv(s->ctx, L.out, s->Y, s->T, &rc);
+      allreduce(s->T, d.n);
     } else {
       AttnArgs a;
       a.qk = s->proj;
-      a.v = s->proj + 2 * d.n + d.kvlen;
+      a.v = s->proj + 2 * d.nhl * d.hdv + d.kvlenl;
       a.q_norm = L.q_norm;
       a.k_norm = L.k_norm;
       a.rope = s->rope;
@@ -943,50 +1108,61 @@ int32_t enqueue_step(unltd_qwen35_session s) {
       a.img4 = L.out->dtype == Q4K ? s->img4 : nullptr;
       a.img6 = L.out->dtype == Q6K ? s->img6 : nullptr;
       a.pos = s->pos;
-      a.nh = d.nh;
-      a.nkv = d.nkv;
+      a.nh = d.nhl;
+      a.nkv = d.nkvl;
       a.n_rot = d.n_rot;
       a.nrp = d.nrp;
       a.ctx = s->ctx_len;
       a.nsplit = s->nsplit;
       a.eps = d.eps;
       a.kq_scale = d.kq_scale;
-      const dim3 sg(d.nkv, (s->ctx_len + 31) / 32), vg(d.nkv, s->nsplit);
-      const size_t q_smem = (size_t)(d.nh / d.nkv) * d.hdv * 4, v_smem = (size_t)kChunk * d.hdv * 4;
+      const dim3 sg(d.nkvl, (s->ctx_len + 31) / 32), vg(d.nkvl, s->nsplit);
+      const size_t q_smem = (size_t)(d.nhl / d.nkvl) * d.hdv * 4, v_smem = (size_t)kChunk * d.hdv * 4;
       const size_t sm_smem = softmax_smem(s->ctx_len);
-      const dim3 cg(d.nh * d.hdv / 256);
+      const dim3 cg(d.nhl * d.hdv / 256), pg(d.nhl + d.nkvl), smg(d.nhl);
       if (d.hdv == 256) {
-        chk(launch_pdl(attn_pre_kernel<256>, dim3(d.nh + d.nkv), dim3(256), 0, st, a), "attn_pre");
+        chk(launch_pdl(attn_pre_kernel<256>, pg, dim3(256), 0, st, a), "attn_pre");
         chk(launch_pdl(attn_scores_kernel<256>, sg, dim3(256), q_smem, st, a), "attn_scores");
-        chk(launch_pdl(attn_softmax_kernel, dim3(d.nh), dim3(256), sm_smem, st, a), "attn_softmax");
+        chk(launch_pdl(attn_softmax_kernel, smg, dim3(256), sm_smem, st, a), "attn_softmax");
         chk(launch_pdl(attn_values_kernel<256>, vg, dim3(256), v_smem, st, a), "attn_values");
         chk(launch_pdl(attn_combine_quant_kernel<256>, cg, dim3(256), 0, st, a), "attn_combine");
       } else {
-        chk(launch_pdl(attn_pre_kernel<128>, dim3(d.nh + d.nkv), dim3(128), 0, st, a), "attn_pre");
+        chk(launch_pdl(attn_pre_kernel<128>, pg, dim3(128), 0, st, a), "attn_pre");
         chk(launch_pdl(attn_scores_kernel<128>, sg, dim3(256), q_smem, st, a), "attn_scores");
-        chk(launch_pdl(attn_softmax_kernel, dim3(d.nh), dim3(256), sm_smem, st, a), "attn_softmax");
+        chk(launch_pdl(attn_softmax_kernel, smg, dim3(256), sm_smem, st, a), "attn_softmax");
         chk(launch_pdl(attn_values_kernel<128>, vg, dim3(128), v_smem, st, a), "attn_values");
         chk(launch_pdl(attn_combine_quant_kernel<128>, cg, dim3(256), 0, st, a), "attn_combine");
       }
       nl += launch_gemv_img(s, L.out, s->T, &rc);
+      allreduce(s->T, d.n);
     }
     // residual = x_in + attn_out; rmsnorm(residual, post_attention_norm) -> gate|up image
     norm(s->X, s->T, s->R, L.post_norm, any_dtype(L.gate_up, Q4K), any_dtype(L.gate_up, Q6K), false);
     for (size_t i = 0; i < L.gate_up.w.size(); i++)
       nl += launch_gemv_img(s, L.gate_up.w[i], s->FF + L.gate_up.off[i], &rc);
-    chk(launch_pdl(swiglu_quant_kernel, dim3(d.nff / 256), dim3(256), 0, st, (const float *)s->FF,
-                   (const float *)(s->FF + d.nff), L.down->dtype == Q4K ? s->img4 : (uint8_t *)nullptr,
+    chk(launch_pdl(swiglu_quant_kernel, dim3(d.nffl / 256), dim3(256), 0, st, (const float *)s->FF,
+                   (const float *)(s->FF + d.nffl), L.down->dtype == Q4K ? s->img4 : (uint8_t *)nullptr,
                    L.down->dtype == Q6K ? s->img6 : (uint8_t *)nullptr),
         "swiglu");
     nl += launch_gemv_img(s, L.down, s->F, &rc);
+    allreduce(s->F, d.n);
   }
   // l_out of the last layer -> output norm -> LM head + greedy argmax
   norm(s->R, s->F, s->X, m->out_norm, m->output->dtype == Q4K, m->output->dtype == Q6K, true);
   {
     GemvArgs g{m->output, nullptr, s->logits, MODE_Q8K, s->ctx->argmax_key, s->ctx->argmax_done, s->cur_token};
     g.img = m->output->dtype == Q4K ? s->img4 : s->img6;
+    g.argmax_row0 = d.v0;
+    if (d.world > 1) g.key_out = s->tpkey;
     if (!rc) rc = gemv_launch(s->ctx, g);
     nl += 1;
+    if (d.world > 1) {  // vocab shards: MAX of the packed keys, then the token
+      if (!rc) rc = comm_allreduce(m->ctx, st, s->tpkey, 1, true);
+      nl += 1;
+      chk(launch_pdl(key_to_token_kernel, dim3(1), dim3(1), 0, st, (const unsigned long long *)s->tpkey,
+                     s->cur_token),
+          "key_to_token");
+    }
   }
   chk(launch_pdl(step_end_kernel, dim3(1), dim3(1), 0, st, (const uint32_t *)s->cur_token, s->hist, s->counter,
                  s->pos),
@@ -1027,17 +1203,50 @@ int32_t run_step(unltd_qwen35_session s) {
 
 extern "C" {
 
-int32_t unltd_qwen35_create(unltd_ctx ctx, const unltd_qwen35_config *cfg, unltd_qwen35 *out) {
+int32_t unltd_qwen35_create_tp(unltd_ctx ctx, const unltd_qwen35_config *cfg, int32_t rank, int32_t world,
+                               unltd_qwen35 *out) {
   if (!ctx || !cfg || !out) return set_error(UNLTD_ERR_INVALID_ARG, "qwen35_create: NULL argument");
   *out = nullptr;
   Derived d;
   if (int32_t rc = derive(*cfg, &d)) return rc;
+  if (int32_t rc = derive_tp(&d, rank, world)) return rc;
+  if (world > 1 && (!ctx->comm || ctx->rank != rank || ctx->world != world))
+    return set_error(UNLTD_ERR_INVALID_ARG, "qwen35_create_tp: the context needs a communicator of this rank/world "
+                                            "(unltd_comm_init)");
   unltd_qwen35 m = new unltd_qwen35_s();
   m->ctx = ctx;
   m->cfg = *cfg;
   m->d = d;
   *out = m;
   return UNLTD_OK;
+}
+
+int32_t unltd_qwen35_create(unltd_ctx ctx, const unltd_qwen35_config *cfg, unltd_qwen35 *out) {
+  return unltd_qwen35_create_tp(ctx, cfg, 0, 1, out);
+}
+
+int32_t unltd_qwen35_shard(const unltd_qwen35_config *cfg, int32_t rank, int32_t world, const char *name,
+                           int64_t *ranges, int32_t max_ranges, int32_t *n_ranges, int64_t *in_begin,
+                           int64_t *in_end) {
+  if (!cfg || !name || !n_ranges || !in_begin || !in_end || (max_ranges > 0 && !ranges))
+    return set_error(UNLTD_ERR_INVALID_ARG, "qwen35_shard: NULL argument");
+  Derived d;
+  if (int32_t rc = derive(*cfg, &d)) return rc;
+  if (int32_t rc = derive_tp(&d, rank, world)) return rc;
+  for (const auto &p : expected(d)) {
+    if (p.name != name) continue;
+    const Shard sh = shard_of(d, p.name, p.dim_in, p.dim_out);
+    *n_ranges = (int32_t)sh.rows.size();
+    if ((int32_t)sh.rows.size() > max_ranges) return set_error(UNLTD_ERR_LENGTH, "qwen35_shard: too many ranges");
+    for (size_t i = 0; i < sh.rows.size(); i++) {
+      ranges[2 * i] = (int64_t)sh.rows[i].first;
+      ranges[2 * i + 1] = (int64_t)sh.rows[i].second;
+    }
+    *in_begin = (int64_t)sh.in0;
+    *in_end = (int64_t)sh.in1;
+    return UNLTD_OK;
+  }
+  return set_error(UNLTD_ERR_INVALID_ARG, std::string("qwen35_shard: unexpected tensor '") + name + "'");
 }
 
 int32_t unltd_qwen35_set_tensor(unltd_qwen35 m, const char *name, const void *host, size_t nbytes, int32_t dtype) {
@@ -1066,12 +1275,21 @@ int32_t unltd_qwen35_set_tensor(unltd_qwen35 m, const char *name, const void *ho
     if (it->second.f) cudaFree(it->second.f);
     m->staged.erase(it);
   }
+  const Shard sh = shard_of(m->d, pt->name, pt->dim_in, pt->dim_out);
+  const uint8_t *src = static_cast<const uint8_t *>(host);
   if (dtype == F32) {
-    cudaError_t e = cudaMalloc(&s.f, nbytes);
-    if (e == cudaSuccess) e = cudaMemcpy(s.f, host, nbytes, cudaMemcpyHostToDevice);
+    const std::vector<uint8_t> loc = gather_shard(sh, src, 4, 1, 4);
+    cudaError_t e = cudaMalloc(&s.f, std::max<size_t>(loc.size(), 16));
+    if (e == cudaSuccess) e = cudaMemcpy(s.f, loc.data(), loc.size(), cudaMemcpyHostToDevice);
     if (e != cudaSuccess) return cuda_error(e, "qwen35_set_tensor");
-  } else {
+  } else if (m->d.world == 1) {
     int32_t rc = unltd_weight_upload(m->ctx, host, nbytes, dtype, pt->dim_in, pt->dim_out, &s.w);
+    if (rc) return rc;
+  } else {
+    const size_t epb = dtype == Q8_0 ? kQ80Elems : kQK;
+    const size_t bb = gguf_row_bytes(dtype, epb);
+    const std::vector<uint8_t> loc = gather_shard(sh, src, gguf_row_bytes(dtype, pt->dim_in), epb, bb);
+    int32_t rc = unltd_weight_upload(m->ctx, loc.data(), loc.size(), dtype, sh.in1 - sh.in0, sh.nrows(), &s.w);
     if (rc) return rc;
   }
   m->staged[name] = s;
@@ -1185,13 +1403,14 @@ int32_t unltd_qwen35_session_create(unltd_qwen35 m, int32_t ctx_len, unltd_qwen3
   if (!rc) rc = dalloc(B, &s->F, n, "session");
   if (!rc) rc = dalloc(B, &s->proj, m->proj_rows, "session");
   if (!rc) rc = dalloc(B, &s->Y, n, "session");
-  if (!rc) rc = dalloc(B, &s->FF, 2 * (size_t)d.nff, "session");
-  if (!rc) rc = dalloc(B, &s->q, (size_t)d.nh * d.hdv, "session");
-  if (!rc) rc = dalloc(B, &s->scores, (size_t)d.nh * ctx_len, "session");
-  if (!rc) rc = dalloc(B, &s->part, (size_t)d.nh * s->nsplit * d.hdv, "session");
+  if (!rc) rc = dalloc(B, &s->FF, 2 * (size_t)d.nffl, "session");
+  if (!rc) rc = dalloc(B, &s->q, (size_t)d.nhl * d.hdv, "session");
+  if (!rc) rc = dalloc(B, &s->scores, (size_t)d.nhl * ctx_len, "session");
+  if (!rc) rc = dalloc(B, &s->part, (size_t)d.nhl * s->nsplit * d.hdv, "session");
+  if (!rc) rc = dalloc(B, &s->tpkey, 1, "session");
   if (!rc) rc = dalloc(B, &s->img4, spans * kImgQ8K4, "session");
   if (!rc) rc = dalloc(B, &s->img6, spans * kImgQ8K6, "session");
-  if (!rc) rc = dalloc(B, &s->logits, (size_t)d.vocab, "session");
+  if (!rc) rc = dalloc(B, &s->logits, (size_t)(d.v1 - d.v0), "session");
   if (!rc) rc = dalloc(B, &s->rope, (size_t)ctx_len * std::max(d.nrp, 1), "session");
   if (!rc) rc = dalloc(B, &s->cur_token, 1, "session");
   if (!rc) rc = dalloc(B, &s->hist, (size_t)ctx_len + 1, "session");
@@ -1200,15 +1419,15 @@ int32_t unltd_qwen35_session_create(unltd_qwen35 m, int32_t ctx_len, unltd_qwen3
   if (!rc) rc = dalloc(B, &s->pos, 1, "session");
   for (int i = 0; !rc && i < m->n_recr; i++) {
     float *r = nullptr, *st = nullptr;
-    rc = dalloc(B, &r, (size_t)d.K * d.dconv, "session ring");
-    if (!rc) rc = dalloc(B, &st, (size_t)d.nv * d.hd * d.hd, "session state");
+    rc = dalloc(B, &r, (size_t)d.K * d.dconvl, "session ring");
+    if (!rc) rc = dalloc(B, &st, (size_t)d.nvl * d.hd * d.hd, "session state");
     s->ring.push_back(r);
     s->state.push_back(st);
   }
   for (int i = 0; !rc && i < m->n_attn; i++) {
     float *k = nullptr, *v = nullptr;
-    rc = dalloc(B, &k, (size_t)ctx_len * d.kvlen, "session kv cache");
-    if (!rc) rc = dalloc(B, &v, (size_t)ctx_len * d.kvlen, "session kv cache");
+    rc = dalloc(B, &k, (size_t)ctx_len * d.kvlenl, "session kv cache");
+    if (!rc) rc = dalloc(B, &v, (size_t)ctx_len * d.kvlenl, "session kv cache");
     s->kc.push_back(k);
     s->vc.push_back(v);
   }
@@ -1229,8 +1448,8 @@ int32_t unltd_qwen35_session_create(unltd_qwen35 m, int32_t ctx_len, unltd_qwen3
   for (void *p : {(void *)s->cur_token, (void *)s->counter, (void *)s->pos})
     if (!rc) rc = cuda_error(cudaMemset(p, 0, 4), "session init");
   for (int i = 0; !rc && i < m->n_recr; i++) {
-    rc = cuda_error(cudaMemset(s->ring[i], 0, (size_t)d.K * d.dconv * 4), "session init");
-    if (!rc) rc = cuda_error(cudaMemset(s->state[i], 0, (size_t)d.nv * d.hd * d.hd * 4), "session init");
+    rc = cuda_error(cudaMemset(s->ring[i], 0, (size_t)d.K * d.dconvl * 4), "session init");
+    if (!rc) rc = cuda_error(cudaMemset(s->state[i], 0, (size_t)d.nvl * d.hd * d.hd * 4), "session init");
   }
   // GEMV scratch (the projections that still run a prep kernel) sized before
   // any graph capture
@@ -1246,6 +1465,15 @@ int32_t unltd_qwen35_session_create(unltd_qwen35 m, int32_t ctx_len, unltd_qwen3
     rc = cuda_error(e, "attention smem");
   }
   if (!rc) rc = cuda_error(cudaDeviceSynchronize(), "session init");
+  if (!rc && d.world > 1) {
+    // set up NCCL's connections for both collectives of a step before any
+    // graph capture (its lazy set-up allocates)
+    rc = cuda_error(cudaMemset(s->T, 0, (size_t)d.n * 4), "session init");
+    if (!rc) rc = cuda_error(cudaMemset(s->tpkey, 0, 8), "session init");
+    if (!rc) rc = comm_allreduce(m->ctx, s->ctx->stream, s->T, (size_t)d.n, false);
+    if (!rc) rc = comm_allreduce(m->ctx, s->ctx->stream, s->tpkey, 1, true);
+    if (!rc) rc = cuda_error(cudaStreamSynchronize(s->ctx->stream), "session init");
+  }
   if (rc) {
     unltd_qwen35_session_destroy(s);
     return rc;
@@ -1265,6 +1493,20 @@ int32_t unltd_qwen35_session_destroy(unltd_qwen35_session s) {
   return UNLTD_OK;
 }
 
+// The rank's conv channels, in its local order: [q of the local qk heads |
+// k of the local qk heads | v of the local v heads] (the sharded qkv rows).
+std::vector<std::pair<size_t, size_t>> conv_channel_ranges(const Derived &d) {
+  std::vector<std::pair<size_t, size_t>> r;
+  const size_t hd = d.hd;
+  for (int part = 0; part < 2; part++)
+    for (int j = 0; j < d.nqkl; j++) {
+      const size_t gq = (size_t)((d.vh0 + j) % d.nqk) + (size_t)part * d.nqk;
+      r.push_back({gq * hd, (gq + 1) * hd});
+    }
+  r.push_back({2 * (size_t)d.nqk * hd + (size_t)d.vh0 * hd, 2 * (size_t)d.nqk * hd + (size_t)(d.vh0 + d.nvl) * hd});
+  return r;
+}
+
 int32_t unltd_qwen35_session_set_state(unltd_qwen35_session s, int32_t position, const float *const *conv,
                                        const float *const *gdn, const float *const *kcache,
                                        const float *const *vcache) {
@@ -1275,23 +1517,35 @@ int32_t unltd_qwen35_session_set_state(unltd_qwen35_session s, int32_t position,
   CtxGuard g(s->m->ctx->device);
   cudaStream_t st = s->ctx->stream;
   cudaError_t e = cudaStreamSynchronize(st);
+  const auto chans = conv_channel_ranges(d);
+  std::vector<float> row((size_t)d.dconvl);
   for (int i = 0; e == cudaSuccess && i < s->m->n_recr; i++) {
-    e = cudaMemset(s->ring[i], 0, (size_t)d.K * d.dconv * 4);
+    e = cudaMemset(s->ring[i], 0, (size_t)d.K * d.dconvl * 4);
     // row tau of the window (oldest first) lives in slot (position + tau) % K
-    for (int tau = 0; e == cudaSuccess && conv && conv[i] && tau < d.K - 1; tau++)
-      e = cudaMemcpy(s->ring[i] + (size_t)((position + tau) % d.K) * d.dconv, conv[i] + (size_t)tau * d.dconv,
-                     (size_t)d.dconv * 4, cudaMemcpyHostToDevice);
+    for (int tau = 0; e == cudaSuccess && conv && conv[i] && tau < d.K - 1; tau++) {
+      size_t o = 0;
+      for (auto &c : chans)
+        for (size_t ch = c.first; ch < c.second; ch++) row[o++] = conv[i][(size_t)tau * d.dconv + ch];
+      e = cudaMemcpy(s->ring[i] + (size_t)((position + tau) % d.K) * d.dconvl, row.data(), (size_t)d.dconvl * 4,
+                     cudaMemcpyHostToDevice);
+    }
+    const size_t hh = (size_t)d.hd * d.hd;
     if (e == cudaSuccess) {
-      if (gdn && gdn[i]) e = cudaMemcpy(s->state[i], gdn[i], (size_t)d.nv * d.hd * d.hd * 4, cudaMemcpyHostToDevice);
-      else e = cudaMemset(s->state[i], 0, (size_t)d.nv * d.hd * d.hd * 4);
+      if (gdn && gdn[i]) e = cudaMemcpy(s->state[i], gdn[i] + (size_t)d.vh0 * hh, (size_t)d.nvl * hh * 4, cudaMemcpyHostToDevice);
+      else e = cudaMemset(s->state[i], 0, (size_t)d.nvl * hh * 4);
     }
   }
   for (int i = 0; e == cudaSuccess && i < s->m->n_attn; i++) {
-    const size_t full = (size_t)s->ctx_len * d.kvlen * 4, part = (size_t)position * d.kvlen * 4;
+    const size_t full = (size_t)s->ctx_len * d.kvlenl * 4;
     e = cudaMemset(s->kc[i], 0, full);
     if (e == cudaSuccess) e = cudaMemset(s->vc[i], 0, full);
-    if (e == cudaSuccess && part && kcache && kcache[i]) e = cudaMemcpy(s->kc[i], kcache[i], part, cudaMemcpyHostToDevice);
-    if (e == cudaSuccess && part && vcache && vcache[i]) e = cudaMemcpy(s->vc[i], vcache[i], part, cudaMemcpyHostToDevice);
+    const size_t col0 = (size_t)d.kv0 * d.hdv;  // the local kv heads' columns of each full row
+    if (e == cudaSuccess && position && kcache && kcache[i])
+      e = cudaMemcpy2D(s->kc[i], (size_t)d.kvlenl * 4, kcache[i] + col0, (size_t)d.kvlen * 4, (size_t)d.kvlenl * 4,
+                       (size_t)position, cudaMemcpyHostToDevice);
+    if (e == cudaSuccess && position && vcache && vcache[i])
+      e = cudaMemcpy2D(s->vc[i], (size_t)d.kvlenl * 4, vcache[i] + col0, (size_t)d.kvlen * 4, (size_t)d.kvlenl * 4,
+                       (size_t)position, cudaMemcpyHostToDevice);
   }
   if (e == cudaSuccess) e = cudaMemcpy(s->pos, &position, 4, cudaMemcpyHostToDevice);
   if (e != cudaSuccess) return cuda_error(e, "qwen35_set_state");
@@ -1299,8 +1553,10 @@ int32_t unltd_qwen35_session_set_state(unltd_qwen35_session s, int32_t position,
   return UNLTD_OK;
 }
 
-// Copy the session state out in the layout set_state takes (the inverse of
-// unltd_qwen35_session_set_state at the current position); NULL skips.
+// Copy the session state out at the current position: per recurrent layer
+// the conv window ((K-1) x local channels, oldest row first) and the local
+// GDN matrices, per attention layer `position` rows of the local K and V
+// columns. With one GPU this is exactly the layout set_state takes.
 int32_t unltd_qwen35_session_get_state(unltd_qwen35_session s, float *const *conv, float *const *gdn,
                                        float *const *kcache, float *const *vcache) {
   if (!s) return set_error(UNLTD_ERR_INVALID_ARG, "qwen35_get_state: NULL session");
@@ -1310,17 +1566,30 @@ int32_t unltd_qwen35_session_get_state(unltd_qwen35_session s, float *const *con
   const int position = s->host_pos;
   for (int i = 0; e == cudaSuccess && i < s->m->n_recr; i++) {
     for (int tau = 0; e == cudaSuccess && conv && conv[i] && tau < d.K - 1; tau++)
-      e = cudaMemcpy(conv[i] + (size_t)tau * d.dconv, s->ring[i] + (size_t)((position + tau) % d.K) * d.dconv,
-                     (size_t)d.dconv * 4, cudaMemcpyDeviceToHost);
+      e = cudaMemcpy(conv[i] + (size_t)tau * d.dconvl, s->ring[i] + (size_t)((position + tau) % d.K) * d.dconvl,
+                     (size_t)d.dconvl * 4, cudaMemcpyDeviceToHost);
     if (e == cudaSuccess && gdn && gdn[i])
-      e = cudaMemcpy(gdn[i], s->state[i], (size_t)d.nv * d.hd * d.hd * 4, cudaMemcpyDeviceToHost);
+      e = cudaMemcpy(gdn[i], s->state[i], (size_t)d.nvl * d.hd * d.hd * 4, cudaMemcpyDeviceToHost);
   }
   for (int i = 0; e == cudaSuccess && i < s->m->n_attn; i++) {
-    const size_t part = (size_t)position * d.kvlen * 4;
+    const size_t part = (size_t)position * d.kvlenl * 4;
     if (part && kcache && kcache[i]) e = cudaMemcpy(kcache[i], s->kc[i], part, cudaMemcpyDeviceToHost);
     if (e == cudaSuccess && part && vcache && vcache[i]) e = cudaMemcpy(vcache[i], s->vc[i], part, cudaMemcpyDeviceToHost);
   }
   return cuda_error(e, "qwen35_get_state");
+}
+
+// Element counts of the rank's state pieces and its vocab rows.
+int32_t unltd_qwen35_session_shape(unltd_qwen35_session s, int64_t *conv_row, int64_t *gdn_heads,
+                                   int64_t *kv_row, int64_t *vocab_begin, int64_t *vocab_end) {
+  if (!s) return set_error(UNLTD_ERR_INVALID_ARG, "qwen35_session_shape: NULL session");
+  const Derived &d = s->m->d;
+  if (conv_row) *conv_row = d.dconvl;
+  if (gdn_heads) *gdn_heads = d.nvl;
+  if (kv_row) *kv_row = d.kvlenl;
+  if (vocab_begin) *vocab_begin = d.v0;
+  if (vocab_end) *vocab_end = d.v1;
+  return UNLTD_OK;
 }
 
 // Teacher-forced steps over `tokens` (a prompt); then *next_token = the
@@ -1388,7 +1657,8 @@ int32_t unltd_qwen35_session_read(unltd_qwen35_session s, float *logits, float *
   CtxGuard g(s->m->ctx->device);
   cudaStream_t st = s->ctx->stream;
   cudaError_t e = cudaStreamSynchronize(st);
-  if (e == cudaSuccess && logits) e = cudaMemcpy(logits, s->logits, (size_t)s->m->d.vocab * 4, cudaMemcpyDeviceToHost);
+  if (e == cudaSuccess && logits)
+    e = cudaMemcpy(logits, s->logits, (size_t)(s->m->d.v1 - s->m->d.v0) * 4, cudaMemcpyDeviceToHost);
   if (e == cudaSuccess && hidden) e = cudaMemcpy(hidden, s->X, (size_t)s->m->d.n * 4, cudaMemcpyDeviceToHost);
   return cuda_error(e, "qwen35_session_read");
 }

@@ -148,6 +148,8 @@ struct Params {
   unsigned long long *key;
   unsigned *done;
   uint32_t *token;
+  unsigned long long *key_out;  // non-null: also store the final argmax key
+  int row0;                     // global index of row 0 (vocab-split LM head)
   int *err;
   int T;           // rows per tile
   int S;           // stages
@@ -522,7 +524,7 @@ __global__ void __launch_bounds__(kGemvThreads, 1) gemv_kernel(Params P) {
         const int row = r0 + t;
         if (P.y) P.y[row] = v;
         if (ARGMAX) {
-          const unsigned long long kk = argmax_key(v, row);
+          const unsigned long long kk = argmax_key(v, P.row0 + row);
           best = kk > best ? kk : best;
         }
       }
@@ -556,7 +558,7 @@ __global__ void __launch_bounds__(kGemvThreads, 1) gemv_kernel(Params P) {
         if (k == 0) {
           if (P.y) P.y[row] = acc;
           if (ARGMAX) {
-            const unsigned long long kk = argmax_key(acc, row);
+            const unsigned long long kk = argmax_key(acc, P.row0 + row);
             best = kk > best ? kk : best;
           }
         }
@@ -582,6 +584,7 @@ __global__ void __launch_bounds__(kGemvThreads, 1) gemv_kernel(Params P) {
         __threadfence();
         const unsigned long long k = atomicAdd(P.key, 0ull);
         *P.token = 0xffffffffu - (uint32_t)(k & 0xffffffffull);
+        if (P.key_out) *P.key_out = k;
         *P.key = 0ull;
         *P.done = 0u;
       }
@@ -807,6 +810,8 @@ int32_t gemv_launch(unltd_ctx ctx, const GemvArgs &a) {
   P.key = a.argmax_key;
   P.done = a.argmax_done;
   P.token = a.token;
+  P.key_out = a.key_out;
+  P.row0 = a.argmax_row0;
   P.err = ctx->err;
   P.T = T;
   P.S = S;

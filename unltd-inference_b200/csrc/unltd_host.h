@@ -28,6 +28,7 @@ struct unltd_ctx_s {
   size_t gemm_scratch_bytes = 0;
   std::atomic<int64_t> launches{0};
   void *comm = nullptr;  // ncclComm_t once unltd_comm_init ran
+  int rank = 0, world = 1;
 };
 
 struct unltd_weight_s {
@@ -78,11 +79,19 @@ struct GemvArgs {
   // Non-null: the x image was already written (by a fused producer kernel
   // that ran before on the same stream, in this mode's layout); no prep.
   const uint8_t *img = nullptr;
+  // Fused argmax of a vocab shard: global index of row 0, and where to store
+  // the final 64-bit key (for the cross-GPU MAX) besides the token.
+  int argmax_row0 = 0;
+  unsigned long long *key_out = nullptr;
 };
 int32_t gemv_launch(unltd_ctx ctx, const GemvArgs &a);
 // Grow the context's x-image scratch for w (call before stream capture).
 int32_t gemv_reserve(unltd_ctx ctx, const unltd_weight_s &w, int mode);
 void gemv_prewarm(int device);
+
+// comm.cu (NCCL through dlopen)
+int32_t comm_allreduce(unltd_ctx c, cudaStream_t st, void *buf, size_t count, bool max_u64);
+void comm_destroy(unltd_ctx c);
 
 // gemm_tc.cu
 int32_t gemm_launch(unltd_ctx ctx, const unltd_weight_s &w, const float *X, float *Y, size_t M);

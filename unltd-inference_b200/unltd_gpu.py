@@ -56,7 +56,16 @@ SIGNATURES = [
     ("unltd_dequantize_q4_k", _I, [_P, _S, _P, _S]),
     ("unltd_set_default_device", _I, [_I]),
     ("unltd_forget_host_weights", _I, []),
+    ("unltd_comm_unique_id", _I, [_P, _S]),
+    ("unltd_comm_init", _I, [_P, _I, _I, _P, _S]),
+    ("unltd_allreduce_sum_f32", _I, [_P, _P, _S]),
+    ("unltd_allreduce_max_u64", _I, [_P, _P, _S]),
     ("unltd_qwen35_create", _I, [_P, _P, ctypes.POINTER(_P)]),
+    ("unltd_qwen35_create_tp", _I, [_P, _P, _I, _I, ctypes.POINTER(_P)]),
+    ("unltd_qwen35_shard", _I, [_P, _I, _I, ctypes.c_char_p, _P, _I, ctypes.POINTER(_I), ctypes.POINTER(_I64),
+                                ctypes.POINTER(_I64)]),
+    ("unltd_qwen35_session_shape", _I, [_P, ctypes.POINTER(_I64), ctypes.POINTER(_I64), ctypes.POINTER(_I64),
+                                        ctypes.POINTER(_I64), ctypes.POINTER(_I64)]),
     ("unltd_qwen35_set_tensor", _I, [_P, ctypes.c_char_p, _P, _S, _I]),
     ("unltd_qwen35_finalize", _I, [_P]),
     ("unltd_qwen35_destroy", _I, [_P]),
@@ -192,6 +201,18 @@ class Context:
     def dequant(self, w: "Weight", out):
         _check(lib().unltd_dequant(self.h, w.h, _ptr(out)))
 
+    def comm_init(self, rank: int, world: int, uid: bytes):
+        """NCCL communicator for tensor parallelism (uid from comm_unique_id on rank 0)."""
+        buf = ctypes.create_string_buffer(bytes(uid), 128)
+        _check(lib().unltd_comm_init(self.h, rank, world, buf, 128))
+        self.rank, self.world = rank, world
+
+    def allreduce_sum(self, buf, count: int):
+        _check(lib().unltd_allreduce_sum_f32(self.h, _ptr(buf), count))
+
+    def allreduce_max_u64(self, buf, count: int):
+        _check(lib().unltd_allreduce_max_u64(self.h, _ptr(buf), count))
+
     def close(self):
         if getattr(self, "h", None):
             lib().unltd_ctx_destroy(self.h)
@@ -270,14 +291,43 @@ class Qwen35Config(ctypes.Structure):
         return cls(**{k: d[k] for k, _ in cls._fields_})
 
 
-class Qwen35Model:
-    """Qwen35Forward::open on the device: tensors uploaded by GGUF name."""
+def comm_unique_id() -> bytes:
+    """A fresh 128-byte NCCL id (call on one rank and distribute it)."""
+    buf = ctypes.create_string_buffer(128)
+    _check(lib().unltd_comm_unique_id(buf, 128))
+    return buf.raw
 
-    def __init__(self, ctx: Context, cfg: dict):
-        self.ctx, self.cfg = ctx, dict(cfg)
+
+def exchange_unique_id(group=None) -> bytes:
+    """Rank 0 creates the NCCL id and every rank of the torch.distributed
+    group receives it (works over gloo or nccl process groups)."""
+    import torch.distributed as dist
+
+    obj = [comm_unique_id() if dist.get_rank(group) == 0 else None]
+    dist.broadcast_object_list(obj, src=0, group=group)
+    return obj[0]
+
+
+def qwen35_shard(cfg: dict, rank: int, world: int, name: str):
+    """Host-only shard plan: ([(row_begin, row_end), ...], (in_begin, in_end))."""
+    c = Qwen35Config.from_dict(cfg)
+    ranges = (ctypes.c_int64 * 512)()
+    n, i0, i1 = _I(), _I64(), _I64()
+    _check(lib().unltd_qwen35_shard(ctypes.byref(c), rank, world, name.encode(), ranges, 256, ctypes.byref(n),
+                                    ctypes.byref(i0), ctypes.byref(i1)))
+    return [(ranges[2 * k], ranges[2 * k + 1]) for k in range(n.value)], (i0.value, i1.value)
+
+
+class Qwen35Model:
+    """Qwen35Forward::open on the device: tensors uploaded by GGUF name. With
+    world > 1 this is the tensor-parallel shard of `rank` (the context needs
+    comm_init first); set_tensor still takes the full tensors."""
+
+    def __init__(self, ctx: Context, cfg: dict, rank: int = 0, world: int = 1):
+        self.ctx, self.cfg, self.rank, self.world = ctx, dict(cfg), rank, world
         self._c = Qwen35Config.from_dict(cfg)
         h = ctypes.c_void_p()
-        _check(lib().unltd_qwen35_create(ctx.h, ctypes.byref(self._c), ctypes.byref(h)))
+        _check(lib().unltd_qwen35_create_tp(ctx.h, ctypes.byref(self._c), rank, world, ctypes.byref(h)))
         self.h = h
         _track(self, 1)
 
@@ -327,11 +377,19 @@ class Qwen35Session:
         ptrs = [_ptr_array(a) for a in (conv, gdn, kcache, vcache)]
         _check(lib().unltd_qwen35_session_set_state(self.h, position, *[p[0] for p in ptrs]))
 
+    def shape(self) -> dict:
+        cr, gh, kv, v0, v1 = _I64(), _I64(), _I64(), _I64(), _I64()
+        _check(lib().unltd_qwen35_session_shape(self.h, ctypes.byref(cr), ctypes.byref(gh), ctypes.byref(kv),
+                                                ctypes.byref(v0), ctypes.byref(v1)))
+        return {"conv_row": cr.value, "gdn_heads": gh.value, "kv_row": kv.value, "vocab": (v0.value, v1.value)}
+
     def get_state(self) -> dict:
-        """The state at the current position: conv windows, GDN matrices, K/V rows."""
+        """The state at the current position: conv windows, GDN matrices, K/V
+        rows (this rank's slices under tensor parallelism)."""
         cfg = self.model.cfg
         hd = cfg["d_inner"] // (2 * cfg["group_count"])
-        nv, dconv, kvlen = cfg["d_inner"] // hd, 2 * cfg["d_inner"], cfg["n_head_kv"] * cfg["head_dim"]
+        sh = self.shape()
+        nv, dconv, kvlen = sh["gdn_heads"], sh["conv_row"], sh["kv_row"]
         attn = [(il + 1) % cfg["full_attn_interval"] == 0 for il in range(cfg["n_layer"])]
         pos = self.info()["position"]
         st = {"conv": [np.zeros((cfg["conv_kernel"] - 1, dconv), np.float32) for a in attn if not a],
@@ -361,7 +419,8 @@ class Qwen35Session:
 
     def read(self, logits: bool = True, hidden: bool = True):
         cfg = self.model.cfg
-        lg = np.empty(cfg["vocab"], np.float32) if logits else None
+        v0, v1 = self.shape()["vocab"]
+        lg = np.empty(v1 - v0, np.float32) if logits else None
         hd = np.empty(cfg["n_embd"], np.float32) if hidden else None
         _check(lib().unltd_qwen35_session_read(self.h, None if lg is None else lg.ctypes.data,
                                                None if hd is None else hd.ctypes.data))
