@@ -212,9 +212,11 @@ def decode_bytes_per_token(cfg, position):
     return total
 
 
-def decode_bench(n_tokens, with_cpu):
-    """greedy decode of the synthetic 9B-class hybrid model
-    from a 2048-position context, one GPU, through unltd_qwen35_decode."""
+def decode_bench(n_tokens, with_cpu, rank=0, world=1, dist=None):
+    """BASELINE configs 3 and 4: greedy decode of the synthetic 9B-class hybrid
+    model from a 2048-position context through unltd_qwen35_decode, on one GPU
+    or tensor-parallel over `world` GPUs (one process each). Device-timed on
+    each rank's session stream; the max over ranks is reported."""
     import torch
 
     import unltd_gpu as ug
@@ -224,7 +226,9 @@ def decode_bench(n_tokens, with_cpu):
     tensors = synth.qwen35_model(cfg, 2026)
     st = synth.qwen35_state(cfg, pos0, 2027)
     ctx = ug.Context(torch.cuda.current_device())
-    m = ug.Qwen35Model(ctx, cfg)
+    if world > 1:
+        ctx.comm_init(rank, world, ug.exchange_unique_id())
+    m = ug.Qwen35Model(ctx, cfg, rank, world)
     m.load(tensors)
     s = m.session(pos0 + n_tokens + 16)
     s.set_state(pos0, st["conv"], st["gdn"], st["k"], st["v"])
@@ -233,6 +237,8 @@ def decode_bench(n_tokens, with_cpu):
     ext = torch.cuda.ExternalStream(info["stream"])
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     torch.cuda.synchronize()
+    if dist:
+        dist.barrier()
     t0 = time.perf_counter()
     e0.record(ext)
     toks = s.decode(int(warm[-1]), n_tokens)
@@ -240,22 +246,32 @@ def decode_bench(n_tokens, with_cpu):
     torch.cuda.synchronize()
     wall = time.perf_counter() - t0
     ms_tok = e0.elapsed_time(e1) / n_tokens
+    if dist:
+        tt = torch.tensor([ms_tok, wall], device="cuda", dtype=torch.float64)
+        dist.all_reduce(tt, op=dist.ReduceOp.MAX)
+        ms_tok, wall = float(tt[0]), float(tt[1])
     bpt = decode_bytes_per_token(cfg, pos0 + 8 + n_tokens // 2)
     peak, peak_kind = _peaks()
+    gbs = bpt / (ms_tok * 1e-3) / 1e9  # whole job; each GPU moves about 1/world of it
     out = {
-        "workload": "config3_qwen35_9b_synthetic_greedy_decode_ctx2048", "n_tokens": n_tokens,
+        "workload": ("config3_qwen35_9b_synthetic_greedy_decode_ctx2048" if world == 1 else
+                     f"config4_qwen35_9b_synthetic_greedy_decode_ctx2048_tp{world}"),
+        "n_tokens": n_tokens, "batch": 1, "n_gpus": world,
         "tok_s": round(1e3 / ms_tok, 2), "ms_per_token": round(ms_tok, 4),
         "e2e_tok_s": round(n_tokens / wall, 2),
-        "bytes_per_token": bpt, "hbm_gbs": round(bpt / (ms_tok * 1e-3) / 1e9, 1),
-        "roofline_frac": round(bpt / (ms_tok * 1e-3) / 1e9 / peak, 4), "peak": peak, "peak_kind": peak_kind,
+        "bytes_per_token": bpt, "hbm_gbs": round(gbs, 1), "hbm_gbs_per_gpu": round(gbs / world, 1),
+        "roofline_frac": round(gbs / world / peak, 4), "peak": peak, "peak_kind": peak_kind,
         "launches_per_step": info["launches_per_step"], "graph": "one CUDA graph per token",
-        "arithmetic": "Q8K_EXACT projections; f32/f64 ops in the reference's order (hidden states bit-identical to the oracle)",
+        "arithmetic": ("Q8K_EXACT projections; f32/f64 ops in the reference's order (hidden states bit-identical to "
+                       "the oracle)" if world == 1 else
+                       "Q8K_EXACT projections; row-split partial outputs summed by NCCL all-reduce (logits within "
+                       "1e-3 max-rel of the oracle, same greedy stream)"),
         "tokens_tail": [int(t) for t in toks[-4:]],
     }
     s.close()
     m.close()
     ctx.close()
-    if with_cpu:
+    if with_cpu and rank == 0:
         import oracle
 
         o = oracle.Qwen35Oracle(cfg, tensors, pos0 + 8, st, pos0)
@@ -334,6 +350,10 @@ def main():
 
     rank, world, local = _dist_env()
     torch.cuda.set_device(local)
+    # exactly one JSON line on stdout: everything else (NCCL's banner included)
+    # goes to stderr; the line is written to the saved stdout at the end
+    out_fd = os.dup(1)
+    os.dup2(2, 1)
     dist = None
     if world > 1:
         import datetime
@@ -500,8 +520,9 @@ def main():
         del GX, GY
 
     decode = None
-    if world == 1 and args.only is None and not args.no_decode:
-        decode = decode_bench(args.decode_tokens, with_cpu=not args.no_cpu_baseline)
+    if args.only is None and not args.no_decode:
+        decode = decode_bench(args.decode_tokens, with_cpu=not args.no_cpu_baseline and world == 1, rank=rank,
+                              world=world, dist=dist)
 
     peak, peak_kind = _peaks()
     step_bytes = sum(it["bytes"] for it in items)
@@ -538,7 +559,8 @@ def main():
     if rank == 0 and world == 1 and not args.no_cpu_baseline and args.only is None:
         line["cpu_baseline"] = cpu_baseline()
     if rank == 0:
-        print(json.dumps(line), flush=True)
+        sys.stdout.flush()
+        os.write(out_fd, (json.dumps(line) + "\n").encode())
     for it in items:
         it["w"].free()
     ctx.close()

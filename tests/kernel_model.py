@@ -68,25 +68,30 @@ def q4_scales(hdr: np.ndarray, p: int):
 
 # ---- Q8_K exact: per-block integer lane sums -------------------------------------
 
+def q4k_q8k_xpos(e):
+    e = np.asarray(e)
+    g = e >> 5
+    return 128 * (g >> 2) + 16 * (e & 7) + 4 * (g & 3) + ((e >> 3) & 3)
+
+
 def q4k_block_sumi_model(blk: np.ndarray, q8: np.ndarray):
-    """Per-class sums sumi[k] and minsum of one block, via the kernel's lanes."""
+    """Per-class sums sumi[k] and minsum of one block, via the kernel's lanes:
+    lane j owns class j (its qs words at 32p + 4j, its q8 words at 16j and
+    128 + 16j of the class-major image) and group j's min term."""
     hdr, qs = repack_q4k_block(blk)
     img = np.zeros(256, np.int64)
-    img[q4_xpos(np.arange(256))] = q8
+    img[q4k_q8k_xpos(np.arange(256))] = q8
+    bs = q8.astype(np.int64).reshape(8, 32).sum(1)
     sumi = np.zeros(8, np.int64)
     msum = 0
     for j in range(8):
-        p, kh = j >> 1, j & 1
-        (sc_lo, m_lo), (sc_hi, m_hi) = q4_scales(hdr, p)
-        w = _bytes(qs[32 * p + 16 * kh: 32 * p + 16 * kh + 16]).reshape(4, 4)
-        qa = img[16 * j: 16 * j + 16].reshape(4, 4)
-        qb = img[128 + 16 * j: 128 + 16 * j + 16].reshape(4, 4)
-        for t in range(4):
-            lo, hi = w[t] & 0xF, w[t] >> 4
-            sumi[4 * kh + t] += sc_lo * int((lo * qa[t]).sum()) + sc_hi * int((hi * qb[t]).sum())
-        bs_lo = int(q8[(64 * p + np.arange(32))[((np.arange(32) & 7) >> 2) == kh]].sum())
-        bs_hi = int(q8[(64 * p + 32 + np.arange(32))[((np.arange(32) & 7) >> 2) == kh]].sum())
-        msum += m_lo * bs_lo + m_hi * bs_hi
+        xg = np.concatenate([img[16 * j: 16 * j + 16], img[128 + 16 * j: 128 + 16 * j + 16]]).reshape(8, 4)
+        for p in range(4):
+            (sc_lo, _), (sc_hi, _) = q4_scales(hdr, p)
+            w = _bytes(qs[32 * p + 4 * j: 32 * p + 4 * j + 4])
+            sumi[j] += sc_lo * int(((w & 0xF) * xg[2 * p]).sum()) + sc_hi * int(((w >> 4) * xg[2 * p + 1]).sum())
+        m_j = q4_scales(hdr, j >> 1)[j & 1][1]  # group j's min, taken by lane j
+        msum += m_j * int(bs[j])
     return sumi, msum
 
 

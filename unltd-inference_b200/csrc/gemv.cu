@@ -321,42 +321,39 @@ __device__ __forceinline__ void integer_item(const uint8_t *const (&rowp)[R], co
     const int rs2 = P.rs / 8;
     const float xd = *reinterpret_cast<const float *>(im + (FMT == Q4K ? kImgQ8K4_D : kImgQ8K6_D));
     if constexpr (FMT == Q4K) {
-      const int p = j >> 1, kh = j & 1;
-      const uint4 q80 = lds128(im + 16 * j), q81 = lds128(im + 128 + 16 * j);
-      const int bs_lo = reinterpret_cast<const int *>(im + kImgQ8K4_BS)[2 * j];
-      const int bs_hi = reinterpret_cast<const int *>(im + kImgQ8K4_BS)[2 * j + 1];
-      const uint32_t qa[4] = {q80.x, q80.y, q80.z, q80.w}, qb[4] = {q81.x, q81.y, q81.z, q81.w};
-      const bool b2 = (j >> 2) & 1, b1 = (j >> 1) & 1;
-      const int kj = 4 * kh + 2 * b2 + b1;  // class held after the reduction
+      // Lane j computes the class-j sum sumi[j] of the block by itself: its
+      // four qs words at 32p + 4j hold class j's elements 64p + j + 8i of
+      // groups 2p (low nibbles) and 2p+1 (high nibbles); the image's class-j
+      // row holds the matching q8 words, one per group. The min term takes
+      // group j per lane and is summed over the eight lanes.
+      const uint4 xa = lds128(im + 16 * j), xb = lds128(im + 128 + 16 * j);
+      const uint32_t xg[8] = {xa.x, xa.y, xa.z, xa.w, xb.x, xb.y, xb.z, xb.w};
+      const int bsj = reinterpret_cast<const int *>(im + kImgQ8K4_BS)[j];
 #pragma unroll
       for (int r = 0; r < R; r++) {
         const uint4 hq = lds128(rowp[r] + b * 16);
-        const uint4 q = lds128(rowp[r] + nb * 16 + b * 128 + 32 * p + 16 * kh);
-        int sc_lo, sc_hi, m_lo, m_hi;
-        q4_scales(hq, p, sc_lo, sc_hi, m_lo, m_hi);
-        const uint32_t w[4] = {q.x, q.y, q.z, q.w};
-        int P4[4];
+        const uint8_t *qs = rowp[r] + nb * 16 + b * 128 + 4 * j;
+        const uint32_t SC03 = hq.y & 0x3F3F3F3Fu, M03 = hq.z & 0x3F3F3F3Fu;
+        const uint32_t SC47 = (hq.w & 0x0F0F0F0Fu) | ((hq.y >> 2) & 0x30303030u);
+        const uint32_t M47 = ((hq.w >> 4) & 0x0F0F0F0Fu) | ((hq.z >> 2) & 0x30303030u);
+        int acc = 0;
 #pragma unroll
-        for (int t = 0; t < 4; t++) {
-          const uint32_t lo = w[t] & 0x0F0F0F0Fu, hi = (w[t] >> 4) & 0x0F0F0F0Fu;
-          P4[t] = sc_lo * dp4a_us(lo, qa[t], 0) + sc_hi * dp4a_us(hi, qb[t], 0);
+        for (int p = 0; p < 4; p++) {
+          const uint32_t w = *reinterpret_cast<const uint32_t *>(qs + 32 * p);
+          const uint32_t SC = p < 2 ? SC03 : SC47;
+          const int sh = (p & 1) * 16;
+          const int sc_lo = (SC >> sh) & 0xFF, sc_hi = (SC >> (sh + 8)) & 0xFF;
+          acc += sc_lo * dp4a_us(w & 0x0F0F0F0Fu, xg[2 * p], 0) + sc_hi * dp4a_us((w >> 4) & 0x0F0F0F0Fu, xg[2 * p + 1], 0);
         }
-        int msum = m_lo * bs_lo + m_hi * bs_hi;
-        // reduce over the four lanes sharing kh (lane bits 1, 2): recursive halving
-        int k0 = b2 ? P4[2] : P4[0], k1 = b2 ? P4[3] : P4[1];
-        const int s0 = b2 ? P4[0] : P4[2], s1 = b2 ? P4[1] : P4[3];
-        k0 += __shfl_xor_sync(m, s0, 4);
-        k1 += __shfl_xor_sync(m, s1, 4);
-        int keep = b1 ? k1 : k0;
-        const int send = b1 ? k0 : k1;
-        keep += __shfl_xor_sync(m, send, 2);
+        const uint32_t MM = j < 4 ? M03 : M47;
+        int msum = (int)((MM >> (8 * (j & 3))) & 0xFFu) * bsj;
         msum += __shfl_xor_sync(m, msum, 4);
         msum += __shfl_xor_sync(m, msum, 2);
         msum += __shfl_xor_sync(m, msum, 1);
         const float d = __fmul_rn(xd, h2f_bits(hq.x & 0xFFFFu));   // q8.d * f16(d)
         const float dm = __fmul_rn(h2f_bits(hq.x >> 16), xd);      // f16(dmin) * q8.d
         if (rv[r]) {
-          tk[r * P.rs + 8 * b + kj] = __fmul_rn(d, (float)keep);
+          tk[r * P.rs + 8 * b + j] = __fmul_rn(d, (float)acc);
           if (j == 0) tm[r * rs2 + b] = __fmul_rn(dm, (float)msum);
         }
       }

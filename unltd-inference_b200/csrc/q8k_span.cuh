@@ -62,9 +62,9 @@ __device__ __forceinline__ void q8k_span_write(float v, uint8_t *im4, uint8_t *i
     d = __fdiv_rn(1.0f, iscale);
   }
   if (im4) {
-    im4[q4_xpos(t)] = (uint8_t)(int8_t)q;
-    const int p = t >> 6, half = (t >> 5) & 1, k = t & 7;
-    atomicAdd(&s.hsum[2 * (2 * p + (k >> 2)) + half], q);
+    // class-major (q4k_q8k_xpos); hsum[g] = sum of group g's q8 values
+    im4[q4k_q8k_xpos(t)] = (uint8_t)(int8_t)q;
+    atomicAdd(&s.hsum[t >> 5], q);
   }
   if (im6) {
     // element -> (lane j, half hh, run position ipos); word w = (ipos%8)/2 holds

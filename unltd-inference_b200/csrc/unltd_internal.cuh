@@ -43,7 +43,8 @@ enum Mode : int { MODE_F32X = 0, MODE_Q8K = 1 };
 constexpr int kImgF32X = 848;
 constexpr int kImgF32X_XS = 768;
 constexpr int kImgF32X_XSUM = 784;
-// Q8K for Q4_K: q8 (256 B, Q4_K lane order) | d f32 | pad | 16 x i32 lane-half sums
+// Q8K for Q4_K: q8 (256 B, class-major: q4k_q8k_xpos) | d f32 | pad | 8 x i32
+// group sums (then 8 zero words)
 constexpr int kImgQ8K4 = 336;
 constexpr int kImgQ8K4_D = 256;
 constexpr int kImgQ8K4_BS = 272;
@@ -68,6 +69,14 @@ __host__ __device__ inline int q4_xpos(int e) {
   int p = e >> 6, half = (e >> 5) & 1, r = e & 31;
   return 128 * half + 32 * p + 4 * (r & 7) + (r >> 3);
 }
+// Q8K image of a Q4_K span: element e = 32g + 8i + k (group g, class k = e % 8)
+// at 128*(g/4) + 16k + 4*(g%4) + i, so lane k reads its class's q8 words for
+// groups 0..3 at 16k and 4..7 at 128 + 16k (eight lanes: 128 contiguous bytes).
+__host__ __device__ inline int q4k_q8k_xpos(int e) {
+  const int g = e >> 5;
+  return 128 * (g >> 2) + 16 * (e & 7) + 4 * (g & 3) + ((e >> 3) & 3);
+}
+
 // In-chunk position of run position ipos (0..15) for Q6_K: word t holds run
 // positions (2t, 2t+8, 2t+1, 2t+9), i.e. Q8_K lane classes 2t and 2t+1.
 __host__ __device__ inline int q6_pic(int ipos) {
