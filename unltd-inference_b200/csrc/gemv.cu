@@ -45,6 +45,8 @@ constexpr int kThreads = 256;  // prep kernels
 constexpr int kConsumerWarps = 16;
 constexpr int kConsumers = kConsumerWarps * 32;
 constexpr int kGemvThreads = kConsumers + 32;  // + one producer warp
+constexpr int kMmaWarps = 16;                     // consumer warps of the tensor-core Q4_K Q8K kernel
+static_assert(kMmaWarps * 32 + 32 <= 1024 && kGemvThreads <= 1024, "a CTA has at most 1024 threads");
 constexpr int kMaxStages = 8;
 constexpr int kBarBytes = 128;
 
@@ -151,6 +153,8 @@ struct Params {
   unsigned long long *key_out;  // non-null: also store the final argmax key
   int row0;                     // global index of row 0 (vocab-split LM head)
   int *err;
+  int pstride;     // shared-memory row stride in a stage (> stride: padded rows)
+  int mma;         // Q4_K Q8K: integer phase on the tensor cores (T a multiple of 16)
   int T;           // rows per tile
   int S;           // stages
   int stage_bytes; // bytes per stage buffer (>= T * stride, multiple of 128)
@@ -159,6 +163,89 @@ struct Params {
 };
 
 __device__ __forceinline__ uint4 lds128(const uint8_t *p) { return *reinterpret_cast<const uint4 *>(p); }
+__device__ __forceinline__ uint2 lds64(const uint8_t *p) { return *reinterpret_cast<const uint2 *>(p); }
+
+// D = A(16x32 s8, row) * B(32x8 s8, col), exact int32 (tensor cores)
+__device__ __forceinline__ void mma_s8(uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3, uint32_t b0, uint32_t b1,
+                                       int &d0, int &d1, int &d2, int &d3) {
+  asm("mma.sync.aligned.m16n8k32.row.col.s32.s8.s8.s32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%10,%10,%10,%10};"
+      : "=r"(d0), "=r"(d1), "=r"(d2), "=r"(d3)
+      : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1), "r"(0));
+}
+
+// byte k (0..3) of w as an int
+__device__ __forceinline__ int byte_of(uint32_t w, int k) { return (int)__byte_perm(w, 0u, 0x4440u | (uint32_t)k); }
+
+// Q8K, Q4_K on the tensor cores: one warp takes 16 rows x one block. For
+// each scale group g an int8 MMA m16n8k32 multiplies the 16 rows' 32 quants
+// of the group (A: thread (r, t) holds words 2t and 2t+1 of the row's 32-byte
+// qs segment, i.e. classes 2t and 2t+1, each four elements) by the class-
+// masked q8 values (B column n = class n: only the thread owning class n,
+// r == 2t (+1), holds its class's q8 word), giving every (row, class)
+// integer partial of the group at once; the group scales are applied per
+// row in int32 (exact). The min term takes groups 2t, 2t+1 per thread.
+__device__ __forceinline__ void q4k_q8k_mma_item(const uint8_t *tile, int nr, int g16, int b, const uint8_t *im,
+                                                 const Params &P, float *tk, float *tm, float xd) {
+  const int lane = threadIdx.x & 31, gid = lane >> 2, tig = lane & 3;
+  const int lr0 = g16 * 16 + gid, lr1 = lr0 + 8;
+  const bool v0 = lr0 < nr, v1 = lr1 < nr;
+  const uint8_t *row0 = tile + (size_t)(v0 ? lr0 : 0) * P.pstride;
+  const uint8_t *row1 = tile + (size_t)(v1 ? lr1 : 0) * P.pstride;
+  const bool own0 = gid == 2 * tig, own1 = gid == 2 * tig + 1;
+  uint4 xa = make_uint4(0u, 0u, 0u, 0u), xb = xa;
+  if (own0 || own1) {
+    xa = lds128(im + 16 * gid);
+    xb = lds128(im + 128 + 16 * gid);
+  }
+  const uint32_t xg[8] = {xa.x, xa.y, xa.z, xa.w, xb.x, xb.y, xb.z, xb.w};
+  const uint4 h0 = lds128(row0 + b * 16), h1 = lds128(row1 + b * 16);
+  const uint32_t SCa0 = h0.y & 0x3F3F3F3Fu, SCb0 = (h0.w & 0x0F0F0F0Fu) | ((h0.y >> 2) & 0x30303030u);
+  const uint32_t SCa1 = h1.y & 0x3F3F3F3Fu, SCb1 = (h1.w & 0x0F0F0F0Fu) | ((h1.y >> 2) & 0x30303030u);
+  const uint8_t *q0 = row0 + P.nb * 16 + b * 128 + 8 * tig, *q1 = row1 + P.nb * 16 + b * 128 + 8 * tig;
+  int acc0 = 0, acc1 = 0, acc2 = 0, acc3 = 0;
+#pragma unroll
+  for (int p = 0; p < 4; p++) {
+    const uint2 w0 = lds64(q0 + 32 * p), w1 = lds64(q1 + 32 * p);
+#pragma unroll
+    for (int h = 0; h < 2; h++) {
+      const int g = 2 * p + h;
+      const uint32_t a0 = (h ? w0.x >> 4 : w0.x) & 0x0F0F0F0Fu, a1 = (h ? w1.x >> 4 : w1.x) & 0x0F0F0F0Fu;
+      const uint32_t a2 = (h ? w0.y >> 4 : w0.y) & 0x0F0F0F0Fu, a3 = (h ? w1.y >> 4 : w1.y) & 0x0F0F0F0Fu;
+      int d0, d1, d2, d3;
+      mma_s8(a0, a1, a2, a3, own0 ? xg[g] : 0u, own1 ? xg[g] : 0u, d0, d1, d2, d3);
+      const int s0 = byte_of(g < 4 ? SCa0 : SCb0, g & 3), s1 = byte_of(g < 4 ? SCa1 : SCb1, g & 3);
+      acc0 += s0 * d0;
+      acc1 += s0 * d1;
+      acc2 += s1 * d2;
+      acc3 += s1 * d3;
+    }
+  }
+  // min term: sum over groups of m_g * (sum of group g's q8), groups 2t and 2t+1 here
+  const int2 bs = *reinterpret_cast<const int2 *>(im + kImgQ8K4_BS + 8 * tig);
+  const uint32_t MA0 = h0.z & 0x3F3F3F3Fu, MB0 = ((h0.w >> 4) & 0x0F0F0F0Fu) | ((h0.z >> 2) & 0x30303030u);
+  const uint32_t MA1 = h1.z & 0x3F3F3F3Fu, MB1 = ((h1.w >> 4) & 0x0F0F0F0Fu) | ((h1.z >> 2) & 0x30303030u);
+  const uint32_t MM0 = tig < 2 ? MA0 : MB0, MM1 = tig < 2 ? MA1 : MB1;
+  const int k0 = (2 * tig) & 3;
+  int ms0 = byte_of(MM0, k0) * bs.x + byte_of(MM0, k0 + 1) * bs.y;
+  int ms1 = byte_of(MM1, k0) * bs.x + byte_of(MM1, k0 + 1) * bs.y;
+  ms0 += __shfl_xor_sync(0xffffffffu, ms0, 1);
+  ms1 += __shfl_xor_sync(0xffffffffu, ms1, 1);
+  ms0 += __shfl_xor_sync(0xffffffffu, ms0, 2);
+  ms1 += __shfl_xor_sync(0xffffffffu, ms1, 2);
+  const int rs2 = P.rs / 8;
+  if (v0) {
+    const float d = __fmul_rn(xd, h2f_bits(h0.x & 0xFFFFu)), dm = __fmul_rn(h2f_bits(h0.x >> 16), xd);
+    tk[lr0 * P.rs + 8 * b + 2 * tig] = __fmul_rn(d, (float)acc0);
+    tk[lr0 * P.rs + 8 * b + 2 * tig + 1] = __fmul_rn(d, (float)acc1);
+    if (tig == 0) tm[lr0 * rs2 + b] = __fmul_rn(dm, (float)ms0);
+  }
+  if (v1) {
+    const float d = __fmul_rn(xd, h2f_bits(h1.x & 0xFFFFu)), dm = __fmul_rn(h2f_bits(h1.x >> 16), xd);
+    tk[lr1 * P.rs + 8 * b + 2 * tig] = __fmul_rn(d, (float)acc2);
+    tk[lr1 * P.rs + 8 * b + 2 * tig + 1] = __fmul_rn(d, (float)acc3);
+    if (tig == 0) tm[lr1 * rs2 + b] = __fmul_rn(dm, (float)ms1);
+  }
+}
 
 __device__ __forceinline__ unsigned long long argmax_key(float v, int row) {
   if (isnan(v)) return row == 0 ? ~0ull : 0ull;
@@ -405,8 +492,9 @@ __device__ __forceinline__ void integer_item(const uint8_t *const (&rowp)[R], co
   }
 }
 
-template <int FMT, int MODE, int R, bool ARGMAX>
-__global__ void __launch_bounds__(kGemvThreads, 1) gemv_kernel(Params P) {
+template <int FMT, int MODE, int R, bool ARGMAX, int NW = kConsumerWarps, bool MMA = false>
+__global__ void __launch_bounds__(NW * 32 + 32, 1) gemv_kernel(Params P) {
+  constexpr int kCW = NW, kCons = NW * 32;  // consumer warps / threads
   extern __shared__ __align__(128) uint8_t smem[];
   uint64_t *full = reinterpret_cast<uint64_t *>(smem);
   uint64_t *empty = full + kMaxStages;
@@ -426,13 +514,13 @@ __global__ void __launch_bounds__(kGemvThreads, 1) gemv_kernel(Params P) {
   if (threadIdx.x == 0) {
     for (int s = 0; s < P.S; s++) {
       mbar_init(&full[s], 1);
-      mbar_init(&empty[s], kConsumerWarps);
+      mbar_init(&empty[s], kCW);
     }
     fence_mbar_init();
   }
   __syncthreads();
 
-  if (warp == kConsumerWarps) {
+  if (warp == kCW) {
     // ---------------- producer: one thread streams row tiles -------------
     if (lane == 0) {
       int issued = 0;
@@ -445,7 +533,13 @@ __global__ void __launch_bounds__(kGemvThreads, 1) gemv_kernel(Params P) {
         const int nr = min(P.T, re - r0);
         const uint32_t bytes = (uint32_t)(nr * P.stride);
         mbar_expect_tx(&full[s], bytes);
-        bulk_g2s(stages + (size_t)s * P.stage_bytes, P.W + (size_t)r0 * P.stride, bytes, &full[s]);
+        if (P.pstride == (int)P.stride) {
+          bulk_g2s(stages + (size_t)s * P.stage_bytes, P.W + (size_t)r0 * P.stride, bytes, &full[s]);
+        } else {  // padded rows: one copy per row
+          for (int rr = 0; rr < nr; rr++)
+            bulk_g2s(stages + (size_t)s * P.stage_bytes + (size_t)rr * P.pstride, P.W + (size_t)(r0 + rr) * P.stride,
+                     (uint32_t)P.stride, &full[s]);
+        }
         issued = i + 1;
       }
       // never leave with copies in flight: wait (bounded) for the last copy of each stage
@@ -460,14 +554,14 @@ __global__ void __launch_bounds__(kGemvThreads, 1) gemv_kernel(Params P) {
   {
     const uint4 *src = reinterpret_cast<const uint4 *>(P.img);
     uint4 *dst = reinterpret_cast<uint4 *>(ximg);
-    for (int i = threadIdx.x; i < P.img_bytes / 16; i += kConsumers) dst[i] = src[i];
+    for (int i = threadIdx.x; i < P.img_bytes / 16; i += kCons) dst[i] = src[i];
   }
-  named_bar_sync(1, kConsumers);
+  named_bar_sync(1, kCons);
 
   const int s_in = lane >> 3, j = lane & 7;
   const unsigned subm = 0xFFu << (lane & 24);
   const int sg = warp * 4 + s_in;  // subgroup id
-  constexpr int kSubgroups = kConsumerWarps * 4;
+  constexpr int kSubgroups = kCW * 4;
   unsigned long long best = 0ull;
   const int istr = MODE == MODE_F32X ? kImgF32X : (FMT == Q4K ? kImgQ8K4 : kImgQ8K6);
 
@@ -484,9 +578,20 @@ __global__ void __launch_bounds__(kGemvThreads, 1) gemv_kernel(Params P) {
     float *cb = reinterpret_cast<float *>(reinterpret_cast<uint8_t *>(cbuf0) + (i & 1) * P.cbuf_bytes);
 
     // integer phase
+    constexpr bool use_mma = FMT == Q4K && MODE == MODE_Q8K && MMA;
+    if constexpr (use_mma) {
+      const int ng16 = (nr + 15) / 16;
+      const int nit = got ? ng16 * P.nbu : 0;
+      for (int it = warp; it < nit; it += kCW) {
+        const int g16 = it / P.nbu, b = it - g16 * P.nbu;
+        const uint8_t *im = ximg + (size_t)b * kImgQ8K4;
+        q4k_q8k_mma_item(tile, nr, g16, b, im, P, cb, cb + P.T * P.rs,
+                         *reinterpret_cast<const float *>(im + kImgQ8K4_D));
+      }
+    }
     const int ngroups = (nr + R - 1) / R;
-    const int nitems = got ? ngroups * P.nbu : 0;
-    for (int it = sg; it < nitems; it += kSubgroups) {
+    const int nitems = (got && !use_mma) ? ngroups * P.nbu : 0;
+    for (int it = sg; it < nitems && !use_mma; it += kSubgroups) {
       const int g = it / P.nbu, b = it - g * P.nbu;
       const uint8_t *rowp[R];
       bool rv[R];
@@ -494,7 +599,7 @@ __global__ void __launch_bounds__(kGemvThreads, 1) gemv_kernel(Params P) {
       for (int r = 0; r < R; r++) {
         const int lr = g * R + r;
         rv[r] = lr < nr;
-        rowp[r] = tile + (size_t)(rv[r] ? lr : 0) * P.stride;
+        rowp[r] = tile + (size_t)(rv[r] ? lr : 0) * P.pstride;
       }
       float *cbr = cb + g * R * P.rs;                       // this group's first chain row
       float *cmr = cb + P.T * P.rs + g * R * (P.rs / 8);    // Q8K: its dmin*minsum row
@@ -503,7 +608,7 @@ __global__ void __launch_bounds__(kGemvThreads, 1) gemv_kernel(Params P) {
     __syncwarp();
     if (lane == 0) mbar_arrive(&empty[s]);  // this warp is done with the weight stage
     // uniform exit if any consumer timed out waiting for this tile
-    if (!named_bar_red_and(1, kConsumers, got)) break;
+    if (!named_bar_red_and(1, kCons, got)) break;
 
     // chain phase: loads hoisted ahead of the dependent adds, 8 at a time
     if constexpr (MODE == MODE_F32X) {
@@ -564,16 +669,16 @@ __global__ void __launch_bounds__(kGemvThreads, 1) gemv_kernel(Params P) {
   }
 
   if constexpr (ARGMAX) {
-    __shared__ unsigned long long cta_best[kConsumerWarps];
+    __shared__ unsigned long long cta_best[kCW];
     for (int o = 16; o; o >>= 1) {
       const unsigned long long other = __shfl_xor_sync(0xffffffffu, best, o);
       best = other > best ? other : best;
     }
     if (lane == 0) cta_best[warp] = best;
-    named_bar_sync(1, kConsumers);
+    named_bar_sync(1, kCons);
     if (threadIdx.x == 0) {
       unsigned long long b = cta_best[0];
-      for (int i = 1; i < kConsumerWarps; i++) b = cta_best[i] > b ? cta_best[i] : b;
+      for (int i = 1; i < kCW; i++) b = cta_best[i] > b ? cta_best[i] : b;
       atomicMax(P.key, b);
       __threadfence();
       const unsigned prev = atomicAdd(P.done, 1u);
@@ -639,7 +744,8 @@ GemvFn pick_r(int R) {
 }
 
 template <bool AM>
-GemvFn pick(int fmt, int mode, int R) {
+GemvFn pick(int fmt, int mode, int R, bool mma = false) {
+  if (mma) return gemv_kernel<Q4K, MODE_Q8K, 2, AM, kMmaWarps, true>;
   if (mode == MODE_F32X) {
     if (fmt == Q4K) return pick_r<Q4K, MODE_F32X, AM>(R);
     if (fmt == Q6K) return pick_r<Q6K, MODE_F32X, AM>(R);
@@ -685,6 +791,10 @@ void gemv_prewarm(int device) {
       for (int r = 1; r <= 2; r++) {
         ensure_smem_attr(pick<false>(fmt, mode, r), m);
         ensure_smem_attr(pick<true>(fmt, mode, r), m);
+        if (fmt == Q4K && mode == MODE_Q8K) {
+          ensure_smem_attr(pick<false>(fmt, mode, r, true), m);
+          ensure_smem_attr(pick<true>(fmt, mode, r, true), m);
+        }
       }
     }
 }
@@ -743,10 +853,36 @@ int32_t gemv_launch(unltd_ctx ctx, const GemvArgs &a) {
   // Pick rows per tile T: stages of at most 56 KB, at least 2 (preferably 3+)
   // stages in flight, and (T/R) * nbu items a multiple of the 64 subgroups so
   // the integer phase is balanced; then the largest such T.
-  int R = 1, T = 0, S = 0, stage_bytes = 0, cbuf = 0;
+  int R = 1, T = 0, S = 0, stage_bytes = 0, cbuf = 0, pstride = stride, mma = 0;
   double best_score = -1.0;
   const int nsub = kConsumerWarps * 4;
-  for (int t = 1; t <= 32; t++) {
+  // Q4_K Q8K: tensor-core tiles of 16 rows; rows padded in shared memory to a
+  // stride of 32 (mod 128) bytes so eight rows' loads hit distinct banks
+  if (fmt == Q4K && mode == MODE_Q8K) {
+    const int ps = (int)round_up((size_t)stride, 128) + 32;
+    // 32-row tiles (two MMA row groups per block item) measured faster than
+    // 16-row tiles with deeper rings
+    for (int t = 16; t <= 32; t += 16) {
+      const int sb = (int)round_up((size_t)t * ps, 128);
+      const int cb = cbuf_for(t);
+      const int fixed = kBarBytes + img_bytes + 2 * cb;
+      const int s = std::min(kMaxStages, (smem_max - fixed) / sb);
+      if (s < 2) continue;
+      const int items = (t / 16) * nbu;
+      const double score = (items % kMmaWarps == 0 ? 2.0 : 0.0) + (items >= kMmaWarps ? 1.0 : 0.0) + t / 16.0;
+      if (score > best_score) {
+        best_score = score;
+        T = t;
+        R = 2;
+        S = s;
+        stage_bytes = sb;
+        cbuf = cb;
+        pstride = ps;
+        mma = 1;
+      }
+    }
+  }
+  for (int t = 1; t <= 32 && !mma; t++) {
     const int r = t >= 2 ? 2 : 1;
     if (t % r) continue;
     const int sb = (int)round_up((size_t)t * stride, 128);
@@ -792,7 +928,7 @@ int32_t gemv_launch(unltd_ctx ctx, const GemvArgs &a) {
   }
 
   // 2) gemv, programmatic dependent launch
-  GemvFn fn = am ? pick<true>(fmt, mode, R) : pick<false>(fmt, mode, R);
+  GemvFn fn = am ? pick<true>(fmt, mode, R, mma) : pick<false>(fmt, mode, R, mma);
   ensure_smem_attr(fn, smem);
 
   Params P;
@@ -810,6 +946,8 @@ int32_t gemv_launch(unltd_ctx ctx, const GemvArgs &a) {
   P.key_out = a.key_out;
   P.row0 = a.argmax_row0;
   P.err = ctx->err;
+  P.pstride = pstride;
+  P.mma = mma;
   P.T = T;
   P.S = S;
   P.stage_bytes = stage_bytes;
@@ -818,7 +956,7 @@ int32_t gemv_launch(unltd_ctx ctx, const GemvArgs &a) {
 
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(grid);
-  cfg.blockDim = dim3(kGemvThreads);
+  cfg.blockDim = dim3(mma ? kMmaWarps * 32 + 32 : kGemvThreads);
   cfg.dynamicSmemBytes = smem;
   cfg.stream = st;
   cudaLaunchAttribute attr[1];
