@@ -131,9 +131,20 @@ __global__ void __launch_bounds__(256) norm_quant_kernel(NormArgs p) {
   const int t = threadIdx.x, span = blockIdx.x;
   auto R = [&](int i) { return p.b ? __fadd_rn(p.a[i], p.b[i]) : p.a[i]; };
   double S = 0.0, A = 0.0;
-  for (int i = t; i < p.n; i += 256) {
-    const float r = R(i);
-    S += (double)__fmul_rn(r, r);
+  // loads in batches of 8 per thread, all in flight before they are used
+  for (int i0 = t; i0 < p.n; i0 += 8 * 256) {
+    float ra[8], rb[8];
+#pragma unroll
+    for (int u = 0; u < 8; u++) {
+      const int i = i0 + u * 256;
+      ra[u] = i < p.n ? p.a[i] : 0.0f;
+      rb[u] = (i < p.n && p.b) ? p.b[i] : 0.0f;
+    }
+#pragma unroll
+    for (int u = 0; u < 8; u++) {
+      const float r = p.b ? __fadd_rn(ra[u], rb[u]) : ra[u];
+      S += (double)__fmul_rn(r, r);
+    }
   }
   block_sum2<256>(S, A, red);
   float mean;
@@ -205,39 +216,147 @@ struct RecrArgs {
   float eps;
 };
 
-// One CTA per v-head h, one thread per channel j of the head. Thread j owns
-// column j of the head's GDN state (gdn_fused_step, kernels.rs:316-372,
-// touches column j only through the dots over i), kept in registers.
-template <int HD>
+// One CTA per (v-head h, quarter of its columns), one thread per channel of
+// the head: the conv, silu and l2 norms of the head's q and k (recomputed by
+// each quarter; the window update is written by quarter 0 only) and the
+// head's beta/gate; then gdn_fused_step (kernels.rs:316-372) for the
+// quarter's 32 state columns. Column j is touched only through the dots over
+// i, so a thread owns a column: its two dots are the reference's sequential
+// f64 sums. The quarter's state slice (HD x 32) is staged in shared memory.
+// Output: the head's GDN output before the gated norm.
+constexpr int kGdnCols = 32;
+
+// One dot of gdn_fused_step, sum_i (double)(st_i * x_i) in the reference's
+// left-to-right f64 order, rounded to f32: four lanes (w = 0..3) each sum RW
+// consecutive terms in order, the chunks are combined in order and resolved
+// with the running-error bound (see attn_combine_quant_kernel); when the
+// bound cannot decide, the column's terms go through shared memory and lane
+// w == 0 sums all of them left to right.
+template <int RW>
+__device__ __forceinline__ float gdn_dot(const float (&st)[RW], const float *xw, const float *x, float *fb, int w) {
+  double Sw = 0.0, Qw = 0.0;
+#pragma unroll
+  for (int ii = 0; ii < RW; ii++) {
+    Sw = __dadd_rn(Sw, (double)__fmul_rn(st[ii], xw[ii]));
+    Qw = __dadd_rn(Qw, fabs(Sw));
+  }
+  const int base = threadIdx.x & ~3;  // lane of chunk 0 of this column (same warp)
+  double O = 0.0, T1 = 0.0, T2 = 0.0, T3 = 0.0;
+#pragma unroll
+  for (int c = 0; c < 4; c++) {
+    const double Sc = __shfl_sync(~0u, Sw, (base + c) & 31), Qc = __shfl_sync(~0u, Qw, (base + c) & 31);
+    T1 += Qc;
+    T2 += (double)RW * fabs(O);
+    O = __dadd_rn(O, Sc);
+    T3 += fabs(O);
+  }
+  const double B = 0x1p-51 * (2.0 * T1 + T2 + T3);
+  float r = (float)(O - B);
+  const bool amb = r != (float)(O + B);
+  if (__any_sync(~0u, amb)) {  // rare: sequential sum of the column's terms
+    if (amb) {
+#pragma unroll
+      for (int ii = 0; ii < RW; ii++) fb[RW * w + ii] = st[ii];
+    }
+    __syncwarp();
+    if (amb && w == 0) {
+      double s = 0.0;
+#pragma unroll 1
+      for (int i = 0; i < 4 * RW; i++) s = __dadd_rn(s, (double)__fmul_rn(fb[i], x[i]));
+      fb[0] = (float)s;
+    }
+    __syncwarp();
+    if (amb) r = fb[0];
+    __syncwarp();
+  }
+  return r;
+}
+
+template <int HD, int KT>  // KT: conv_kernel known at compile time (0: a.K at run time)
 __global__ void __launch_bounds__(HD) recr_mid_kernel(RecrArgs a) {
   pdl_trigger();
-  __shared__ float qs[HD], ks[HD], os[HD];
+  __shared__ float qs[HD], ks[HD];
+  __shared__ float gdn_fb[kGdnCols * HD];  // fallback of gdn_dot: one column's terms
   __shared__ double red[2 * HD / 32];
   __shared__ float s_f[2];
   pdl_wait();
-  const int h = blockIdx.x, j = threadIdx.x;
+  const int h = blockIdx.x, quarter = blockIdx.y, j = threadIdx.x;
   const int qk = h % a.nqk;  // periodic qk-head of v-head h (qwen35_forward.rs:464)
   const int pos = *a.pos, K = a.K;
-  const int chq = qk * HD + j, chk = a.nqk * HD + qk * HD + j, chv = 2 * a.nqk * HD + h * HD + j;
+  const int c0 = quarter * kGdnCols;
+  const int chq = qk * HD + j, chk = a.nqk * HD + qk * HD + j;
+  // this thread's state chunk: column c0 + j/4, rows [RW w, RW w + RW); loaded
+  // first so the loads overlap the conv and norms
+  const int jc = j >> 2, w = j & 3;
+  constexpr int RW = HD / 4;
+  float *S = a.state + (size_t)h * HD * HD + c0 + jc;
+  float st[RW];
+#pragma unroll
+  for (int ii = 0; ii < RW; ii++) st[ii] = S[(size_t)(RW * w + ii) * HD];
+
+  // the head's beta/alpha inputs, loaded with everything else
+  const float beta_raw = a.proj[a.beta_off + h], alpha = a.proj[a.alpha_off + h];
+  const float dtb = a.dt_bias[h], ssa = a.ssm_a[h];
 
   // depthwise conv over [window rows, current qkv] (kernels.rs:265-310), silu
-  auto conv = [&](int ch) {
-    float s = 0.0f;
-    for (int tau = 0; tau < K; tau++) {
-      const float xv = tau < K - 1 ? a.ring[(size_t)((pos + tau) % K) * a.dconv + ch] : a.proj[ch];
-      s = __fadd_rn(s, __fmul_rn(xv, a.convw[(size_t)ch * K + tau]));
+  const int chv = 2 * a.nqk * HD + h * HD + c0 + (j & (kGdnCols - 1));
+  float q, k, v = 0.0f;
+  if constexpr (KT > 0) {
+    // every ring slot is loaded (no wait on pos for the addresses), then the
+    // window is taken in slot order (pos + tau) % K
+    float xr[3][KT], wr[3][KT], cur[3];
+    const int chs[3] = {chq, chk, chv};
+#pragma unroll
+    for (int c = 0; c < 3; c++) {
+#pragma unroll
+      for (int sl = 0; sl < KT; sl++) {
+        xr[c][sl] = a.ring[(size_t)sl * a.dconv + chs[c]];
+        wr[c][sl] = a.convw[(size_t)chs[c] * KT + sl];
+      }
+      cur[c] = a.proj[chs[c]];
     }
-    return s;
-  };
-  float q = silu_f(conv(chq)), k = silu_f(conv(chk));
-  const float v = silu_f(conv(chv));
+    float r3[3];
+#pragma unroll
+    for (int c = 0; c < 3; c++) {
+      float sacc = 0.0f;
+#pragma unroll
+      for (int tau = 0; tau < KT; tau++) {
+        float xv = cur[c];
+        if (tau < KT - 1) {
+          const int sl = (pos + tau) % KT;
+#pragma unroll
+          for (int u = 0; u < KT; u++)
+            if (u == sl) xv = xr[c][u];
+        }
+        sacc = __fadd_rn(sacc, __fmul_rn(xv, wr[c][tau]));
+      }
+      r3[c] = sacc;
+    }
+    q = silu_f(r3[0]);
+    k = silu_f(r3[1]);
+    if (j < kGdnCols) v = silu_f(r3[2]);
+  } else {
+    auto conv = [&](int ch) {
+      float sacc = 0.0f;
+      for (int tau = 0; tau < K; tau++) {
+        const float xv = tau < K - 1 ? a.ring[(size_t)((pos + tau) % K) * a.dconv + ch] : a.proj[ch];
+        sacc = __fadd_rn(sacc, __fmul_rn(xv, a.convw[(size_t)ch * K + tau]));
+      }
+      return sacc;
+    };
+    q = silu_f(conv(chq));
+    k = silu_f(conv(chk));
+    if (j < kGdnCols) v = silu_f(conv(chv));
+  }
   // the current row enters the window: it becomes row K-2 of the next step
   const size_t ws = (size_t)((pos + K - 1) % K) * a.dconv;
-  if (h < a.nqk) {
+  // (all slots were loaded above; slot ws is not part of this window, and
+  // only its owner CTA rewrites a channel's slot, after its own loads)
+  if (j < kGdnCols) a.ring[ws + chv] = a.proj[chv];
+  if (h < a.nqk && quarter == 0) {
     a.ring[ws + chq] = a.proj[chq];
     a.ring[ws + chk] = a.proj[chk];
   }
-  a.ring[ws + chv] = a.proj[chv];
 
   // l2_norm_rows of q and k (kernels.rs:236-252)
   qs[j] = q;
@@ -267,53 +386,70 @@ __global__ void __launch_bounds__(HD) recr_mid_kernel(RecrArgs a) {
   ks[j] = k;
 
   // beta = sigmoid(beta_raw); gate = softplus(alpha + dt_bias) * ssm_a
-  const float beta = sigmoid_f(a.proj[a.beta_off + h]);
-  const float gate = __fmul_rn(softplus_f(__fadd_rn(a.proj[a.alpha_off + h], a.dt_bias[h])), a.ssm_a[h]);
+  const float beta = sigmoid_f(beta_raw);
+  const float gate = __fmul_rn(softplus_f(__fadd_rn(alpha, dtb)), ssa);
+  const float g = exp_cr(gate);
+  // v of the column this thread works on (computed above by threads j < 32)
+  __shared__ float vs[kGdnCols];
+  if (j < kGdnCols) vs[j] = v;
   __syncthreads();
 
-  // gdn_fused_step, column j
-  float st[HD];
-  float *S = a.state + (size_t)h * HD * HD;
+  // gdn_fused_step: column jc = c0 + j/4; rows [32w, 32w+32) in registers,
+  // w = j % 4. Each dot over i is evaluated as four in-order chunk sums whose
+  // combination is resolved exactly (gdn_dot); the four lanes of a column
+  // hold the same results.
 #pragma unroll
-  for (int i = 0; i < HD; i++) st[i] = S[(size_t)i * HD + j];
-  const float g = exp_cr(gate);
-  double acc = 0.0;
+  for (int ii = 0; ii < RW; ii++) st[ii] = __fmul_rn(st[ii], g);
+  const float dk = gdn_dot<RW>(st, ks + RW * w, ks, gdn_fb + jc * HD, w);
+  const float d = __fmul_rn(__fsub_rn(vs[jc], dk), beta);
 #pragma unroll
-  for (int i = 0; i < HD; i++) {
-    st[i] = __fmul_rn(st[i], g);
-    acc = __dadd_rn(acc, (double)__fmul_rn(st[i], ks[i]));
-  }
-  const float d = __fmul_rn(__fsub_rn(v, (float)acc), beta);
-  acc = 0.0;
+  for (int ii = 0; ii < RW; ii++) st[ii] = __fadd_rn(st[ii], __fmul_rn(ks[RW * w + ii], d));
+  const float dq = gdn_dot<RW>(st, qs + RW * w, qs, gdn_fb + jc * HD, w);
+  if (w == 0) a.y[h * HD + c0 + jc] = __fmul_rn(dq, __fdiv_rn(1.0f, __fsqrt_rn((float)HD)));
 #pragma unroll
-  for (int i = 0; i < HD; i++) {
-    st[i] = __fadd_rn(st[i], __fmul_rn(ks[i], d));
-    acc = __dadd_rn(acc, (double)__fmul_rn(st[i], qs[i]));
-  }
-#pragma unroll
-  for (int i = 0; i < HD; i++) S[(size_t)i * HD + j] = st[i];
-  const float o = __fmul_rn((float)acc, __fdiv_rn(1.0f, __fsqrt_rn((float)HD)));
+  for (int ii = 0; ii < RW; ii++) S[(size_t)(RW * w + ii) * HD] = st[ii];
+}
 
-  // rmsnorm over the head with ssm_norm, times silu(z)
-  os[j] = o;
-  double So = (double)__fmul_rn(o, o), dummy = 0.0;
-  block_sum2<HD>(So, dummy, red);
+// The gated norm of the recurrent output (qwen35_forward.rs:482-498) fused
+// with the Q8_K image of ssm_out's input: per head, rmsnorm of the GDN output
+// with ssm_norm, times silu(z). One CTA per 256-element span (256 / HD heads).
+template <int HD>
+__global__ void __launch_bounds__(256) gated_norm_quant_kernel(const float *o, const float *z, const float *w,
+                                                               float eps, uint8_t *img4, uint8_t *img6) {
+  pdl_trigger();
+  __shared__ double red[16];
+  __shared__ float s_mean[256 / HD];
+  __shared__ float so[256];
+  __shared__ Q8KSpanSmem sm;
+  pdl_wait();
+  const int span = blockIdx.x, t = threadIdx.x, e = span * 256 + t;
+  const int hl = t / HD, jj = t % HD;  // head within the span, column
+  const float x = o[e];
+  so[t] = x;
+  // per-head sums: warps of one head reduce together
+  double S = (double)__fmul_rn(x, x);
+#pragma unroll
+  for (int off = 16; off; off >>= 1) S += __shfl_xor_sync(~0u, S, off);
+  if ((t & 31) == 0) red[t >> 5] = S;
+  __syncthreads();
+  S = 0.0;
+  for (int w8 = hl * (HD / 32); w8 < (hl + 1) * (HD / 32); w8++) S += red[w8];
   float mean;
   const MeanOf f{HD};
-  if (!resolve_sum(So, So, HD, f, &mean)) {
-    __syncthreads();
-    if (j == 0) {
+  if (!resolve_sum(S, S, HD, f, &mean)) {  // uniform per head
+    if (jj == 0) {
       double s = 0.0;
 #pragma unroll 1
-      for (int i = 0; i < HD; i++) s = __dadd_rn(s, (double)__fmul_rn(os[i], os[i]));
-      s_f[0] = f(s);
+      for (int i = 0; i < HD; i++) s = __dadd_rn(s, (double)__fmul_rn(so[hl * HD + i], so[hl * HD + i]));
+      s_mean[hl] = f(s);
     }
-    __syncthreads();
-    mean = s_f[0];
   }
-  const float scale = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(mean, a.eps)));
-  const float yn = __fmul_rn(__fmul_rn(o, scale), a.ssm_norm[j]);
-  a.y[h * HD + j] = __fmul_rn(yn, silu_f(a.proj[a.z_off + h * HD + j]));
+  __syncthreads();
+  if (!resolve_sum(S, S, HD, f, &mean)) mean = s_mean[hl];
+  const float scale = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(mean, eps)));
+  const float yn = __fmul_rn(__fmul_rn(x, scale), w[jj]);
+  q8k_span_write(__fmul_rn(yn, silu_f(z[e])), img4 ? img4 + (size_t)span * kImgQ8K4 : nullptr,
+                 img6 ? img6 + (size_t)span * kImgQ8K6 : nullptr, sm);
 }
 
 // ---- full-attention layer (qwen35_forward.rs:584-686) ----------------------
@@ -406,6 +542,7 @@ __global__ void __launch_bounds__(256) attn_scores_kernel(AttnArgs a) {
   const int n_ctx = *a.pos + 1;
   const int p0 = blockIdx.y * 32;
   if (p0 >= n_ctx) return;
+#pragma unroll 4
   for (int i = threadIdx.x; i < G * HDV; i += 256) qsm[i] = a.q[(size_t)(kvh * G) * HDV + i];
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const size_t kvlen = (size_t)a.nkv * HDV;
@@ -454,9 +591,14 @@ __global__ void __launch_bounds__(256) attn_softmax_kernel(AttnArgs a) {
   double *l1 = l0 + (a.ctx + 1) / 2;
   float *sc = a.scores + (size_t)h * a.ctx;
   float m = -INFINITY;
-  for (int p = tid; p < n; p += 256) m = fmaxf(m, sc[p]);
+#pragma unroll 8
+  for (int p = tid; p < n; p += 256) {
+    const float v = sc[p];
+    e[p] = v;
+    m = fmaxf(m, v);
+  }
   m = block_max<256>(m, redf);
-  for (int p = tid; p < n; p += 256) e[p] = exp_cr(__fmul_rn(__fsub_rn(sc[p], m), a.kq_scale));
+  for (int p = tid; p < n; p += 256) e[p] = exp_cr(__fmul_rn(__fsub_rn(e[p], m), a.kq_scale));
   __syncthreads();
   // pairwise_sum_f64 (kernels.rs:24-38): pairs (2i, 2i+1) per level, odd tail carried
   int len = (n + 1) / 2;
@@ -552,13 +694,20 @@ __global__ void __launch_bounds__(256) attn_combine_quant_kernel(AttnArgs a) {
   const int nw = (n + kChunk - 1) / kChunk;
   const double2 *pp = a.part + (size_t)h * a.nsplit * HDV + c;
   double O = 0.0, T1 = 0.0, T2 = 0.0, T3 = 0.0;
-  for (int w = 0; w < nw; w++) {
-    const double2 sq = pp[(size_t)w * HDV];
-    const int len = min(kChunk, n - w * kChunk);
-    T1 += sq.y;
-    T2 += (double)len * fabs(O);
-    O = __dadd_rn(O, sq.x);
-    T3 += fabs(O);
+  for (int w0 = 0; w0 < nw; w0 += 8) {  // 8 chunks' partials in flight at a time
+    double2 sq[8];
+#pragma unroll
+    for (int u = 0; u < 8; u++) sq[u] = w0 + u < nw ? pp[(size_t)(w0 + u) * HDV] : make_double2(0.0, 0.0);
+#pragma unroll
+    for (int u = 0; u < 8; u++) {
+      if (w0 + u < nw) {
+        const int len = min(kChunk, n - (w0 + u) * kChunk);
+        T1 += sq[u].y;
+        T2 += (double)len * fabs(O);
+        O = __dadd_rn(O, sq[u].x);
+        T3 += fabs(O);
+      }
+    }
   }
   const double B = 0x1p-51 * (2.0 * T1 + T2 + T3);
   float attn = (float)(O - B);
@@ -1090,8 +1239,14 @@ int32_t enqueue_step(unltd_qwen35_session s) {
       a.beta_off = d.dconvl + d.nvl * d.hd;
       a.alpha_off = a.beta_off + d.nvl;
       a.eps = d.eps;
-      chk(launch_pdl(recr_mid_kernel<128>, dim3(d.nvl), dim3(128), 0, st, a), "recr_mid");
-      nl += launch_gemv(s->ctx, L.out, s->Y, s->T, &rc);
+      if (d.K == 4) chk(launch_pdl(recr_mid_kernel<128, 4>, dim3(d.nvl, 128 / kGdnCols), dim3(128), 0, st, a), "recr_mid");
+      else chk(launch_pdl(recr_mid_kernel<128, 0>, dim3(d.nvl, 128 / kGdnCols), dim3(128), 0, st, a), "recr_mid");
+      chk(launch_pdl(gated_norm_quant_kernel<128>, dim3(d.nvl * 128 / 256), dim3(256), 0, st, (const float *)s->Y,
+                     (const float *)(s->proj + a.z_off), (const float *)L.ssm_norm, d.eps,
+                     L.out->dtype == Q4K ? s->img4 : (uint8_t *)nullptr,
+                     L.out->dtype == Q6K ? s->img6 : (uint8_t *)nullptr),
+          "gated_norm");
+      nl += launch_gemv_img(s, L.out, s->T, &rc);
       allreduce(s->T, d.n);
     } else {
       AttnArgs a;
@@ -1453,8 +1608,6 @@ int32_t unltd_qwen35_session_create(unltd_qwen35 m, int32_t ctx_len, unltd_qwen3
   }
   // GEMV scratch (the projections that still run a prep kernel) sized before
   // any graph capture
-  for (const auto &L : m->layers)
-    if (!rc && !L.attn) rc = gemv_reserve(s->ctx, *L.out, MODE_Q8K);
   if (!rc) {
     const int sm_smem = (int)softmax_smem(ctx_len);
     cudaError_t e = cudaFuncSetAttribute(attn_softmax_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, sm_smem);
