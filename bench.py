@@ -212,7 +212,7 @@ def decode_bytes_per_token(cfg, position):
     return total
 
 
-def decode_bench(n_tokens, with_cpu, rank=0, world=1, dist=None):
+def decode_bench(n_tokens, with_cpu, rank=0, world=1, dist=None, profile_region=False):
     """BASELINE configs 3 and 4: greedy decode of the synthetic 9B-class hybrid
     model from a 2048-position context through unltd_qwen35_decode, on one GPU
     or tensor-parallel over `world` GPUs (one process each). Device-timed on
@@ -239,12 +239,16 @@ def decode_bench(n_tokens, with_cpu, rank=0, world=1, dist=None):
     torch.cuda.synchronize()
     if dist:
         dist.barrier()
+    if profile_region:
+        torch.cuda.profiler.start()
     t0 = time.perf_counter()
     e0.record(ext)
     toks = s.decode(int(warm[-1]), n_tokens)
     e1.record(ext)
     torch.cuda.synchronize()
     wall = time.perf_counter() - t0
+    if profile_region:
+        torch.cuda.profiler.stop()
     ms_tok = e0.elapsed_time(e1) / n_tokens
     if dist:
         tt = torch.tensor([ms_tok, wall], device="cuda", dtype=torch.float64)
@@ -340,6 +344,9 @@ def main():
     ap.add_argument("--mode", default="q8k", choices=["q8k", "f32x"], help="arithmetic of the K-quant GEMVs")
     ap.add_argument("--no-decode", action="store_true", help="skip the config-3 decode measurement")
     ap.add_argument("--decode-tokens", type=int, default=64)
+    ap.add_argument("--decode-only", action="store_true", help="measure only the decode step (profiling)")
+    ap.add_argument("--profile-region", action="store_true",
+                    help="bracket the timed decode with cudaProfilerStart/Stop (ncu --profile-from-start off)")
     args = ap.parse_args()
     if args.impl == "reference":
         return run_reference(args)
@@ -364,6 +371,17 @@ def main():
     torch.cuda.set_stream(torch.cuda.Stream())
     stream = torch.cuda.current_stream()
     ctx = ug.Context(local, stream=stream.cuda_stream)
+
+    if args.decode_only:
+        d = decode_bench(args.decode_tokens, with_cpu=False, rank=rank, world=world, dist=dist,
+                         profile_region=args.profile_region)
+        if rank == 0:
+            os.write(out_fd, (json.dumps({"metric": "decode tok/s", "decode": d}) + "\n").encode())
+        ctx.close()
+        if dist:
+            dist.barrier()
+            dist.destroy_process_group()
+        return
 
     # ---- workload ----
     items = []
