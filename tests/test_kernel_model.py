@@ -17,6 +17,19 @@ def test_permutations_are_bijections():
     assert sorted(km.q6_pic(np.arange(16)).tolist()) == list(range(16))
 
 
+def test_warp_span_writer_positions():
+    # q8k_span_write_warp: lane l writes element 8l + k at base(l) + 16k with
+    # base = 128 (g >> 2) + 4 (g & 3) + (l & 3), g = l >> 2; the same bytes as
+    # the per-element class-major position q4k_q8k_xpos, and group g's sum is
+    # the sum of lanes 4g .. 4g+3
+    lane = np.arange(32)[:, None]
+    k = np.arange(8)[None, :]
+    g = lane >> 2
+    warp_pos = 128 * (g >> 2) + 4 * (g & 3) + (lane & 3) + 16 * k
+    assert np.array_equal(warp_pos, km.q4k_q8k_xpos(8 * lane + k))
+    assert np.array_equal((8 * lane + k) >> 5, np.broadcast_to(g, (32, 8)))
+
+
 def test_q4k_lane_classes_are_pure():
     # every 4-byte word a lane loads holds 4 elements of one scale group and one class e%8
     e = np.arange(256)

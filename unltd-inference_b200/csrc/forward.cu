@@ -88,25 +88,6 @@ __device__ __forceinline__ float block_max(float v, float *red) {
   return v;
 }
 
-// f(seq) for the reference's left-to-right f64 sum `seq` of n terms, given
-// the parallel sum S of the same terms and their absolute sum A, with f a
-// monotone non-decreasing map to f32. True when the bound decides it.
-template <class F>
-__device__ __forceinline__ bool resolve_sum(double S, double A, int n, F f, float *out) {
-  const double B = (double)(n + 8) * 0x1p-51 * A;
-  const float lo = f(S - B), hi = f(S + B);
-  *out = lo;
-  return lo == hi;
-}
-
-struct MeanOf {
-  int n;
-  __device__ float operator()(double s) const { return (float)(s / (double)n); }
-};
-struct ToF32 {
-  __device__ float operator()(double s) const { return (float)s; }
-};
-
 // ---- RMSNorm (kernels.rs:61-78) fused with the Q8_K image of its output ---
 // r = a (+ b); r_out = r (when non-null); xn = rmsnorm(r, w), quantized
 // (quantize_q8_k) straight into the x images of the GEMVs that consume it.
@@ -1209,6 +1190,33 @@ int32_t enqueue_step(unltd_qwen35_session s) {
                argmax ? s->ctx->argmax_key : nullptr, argmax ? s->ctx->argmax_done : nullptr};
     chk(launch_pdl(norm_quant_kernel, dim3(d.n / 256), dim3(256), 0, st, p), "norm");
   };
+  // RMSNorm of a (+ b) feeding projection p (outputs at out + p.off[i]): fused
+  // into the prologue of p's first tensor-core Q4_K GEMV when it has one,
+  // which then also writes the images p's other GEMVs read; else the
+  // stand-alone norm kernel followed by the GEMVs.
+  auto norm_proj = [&](const float *a, const float *b, float *r_out, const float *w, const Proj &p, float *out) {
+    int fi = -1;
+    for (size_t i = 0; i < p.w.size() && fi < 0; i++)
+      if (gemv_norm_fusable(s->ctx, *p.w[i], MODE_Q8K)) fi = (int)i;
+    if (fi < 0) {
+      norm(a, b, r_out, w, any_dtype(p, Q4K), any_dtype(p, Q6K), false);
+      for (size_t i = 0; i < p.w.size(); i++) nl += launch_gemv_img(s, p.w[i], out + p.off[i], &rc);
+      return;
+    }
+    bool need4 = false, need6 = false;
+    for (size_t i = 0; i < p.w.size(); i++) {
+      if ((int)i == fi) continue;
+      need4 |= p.w[i]->dtype == Q4K;
+      need6 |= p.w[i]->dtype == Q6K;
+    }
+    const GemvNorm gn{a, b, r_out, w, d.eps, need4 ? s->img4 : nullptr, need6 ? s->img6 : nullptr};
+    GemvArgs g{p.w[fi], nullptr, out + p.off[fi], MODE_Q8K, nullptr, nullptr, nullptr};
+    g.norm = &gn;
+    if (!rc) rc = gemv_launch(s->ctx, g);
+    nl++;
+    for (size_t i = 0; i < p.w.size(); i++)
+      if ((int)i != fi) nl += launch_gemv_img(s, p.w[i], out + p.off[i], &rc);
+  };
   chk(launch_pdl(embed_q4k_kernel, dim3(d.n / 256), dim3(256), 0, st, (const uint8_t *)m->embd->dev,
                  m->embd->row_stride, m->embd->nb, (const uint32_t *)s->cur_token, (uint32_t)d.vocab, s->X, d.n,
                  s->ctx->err),
@@ -1216,10 +1224,8 @@ int32_t enqueue_step(unltd_qwen35_session s) {
   for (int il = 0; il < d.n_layer; il++) {
     const Layer &L = m->layers[il];
     // layer input = l_out of the previous layer (residual + ffn), fused into the norm
-    const bool q4 = any_dtype(L.in, Q4K), q6 = any_dtype(L.in, Q6K);
-    if (il == 0) norm(s->X, nullptr, nullptr, L.attn_norm, q4, q6, false);
-    else norm(s->R, s->F, s->X, L.attn_norm, q4, q6, false);
-    for (size_t i = 0; i < L.in.w.size(); i++) nl += launch_gemv_img(s, L.in.w[i], s->proj + L.in.off[i], &rc);
+    if (il == 0) norm_proj(s->X, nullptr, nullptr, L.attn_norm, L.in, s->proj);
+    else norm_proj(s->R, s->F, s->X, L.attn_norm, L.in, s->proj);
     if (!L.attn) {
       RecrArgs a;
       a.proj = s->proj;
@@ -1292,9 +1298,7 @@ int32_t enqueue_step(unltd_qwen35_session s) {
       allreduce(s->T, d.n);
     }
     // residual = x_in + attn_out; rmsnorm(residual, post_attention_norm) -> gate|up image
-    norm(s->X, s->T, s->R, L.post_norm, any_dtype(L.gate_up, Q4K), any_dtype(L.gate_up, Q6K), false);
-    for (size_t i = 0; i < L.gate_up.w.size(); i++)
-      nl += launch_gemv_img(s, L.gate_up.w[i], s->FF + L.gate_up.off[i], &rc);
+    norm_proj(s->X, s->T, s->R, L.post_norm, L.gate_up, s->FF);
     chk(launch_pdl(swiglu_quant_kernel, dim3(d.nffl / 256), dim3(256), 0, st, (const float *)s->FF,
                    (const float *)(s->FF + d.nffl), L.down->dtype == Q4K ? s->img4 : (uint8_t *)nullptr,
                    L.down->dtype == Q6K ? s->img6 : (uint8_t *)nullptr),

@@ -160,6 +160,13 @@ struct Params {
   int stage_bytes; // bytes per stage buffer (>= T * stride, multiple of 128)
   int rs;          // chain-buffer row stride in floats
   int cbuf_bytes;  // one chain buffer
+  // fused RMSNorm of the input (tensor-core kernel; nn = its length, 0: none)
+  const float *norm_a, *norm_b;
+  float *norm_r;
+  const float *norm_w;
+  float norm_eps;
+  uint8_t *norm_img4, *norm_img6;
+  int nn;
 };
 
 __device__ __forceinline__ uint4 lds128(const uint8_t *p) { return *reinterpret_cast<const uint4 *>(p); }
@@ -198,30 +205,41 @@ __device__ __forceinline__ void q4k_q8k_mma_item(const uint8_t *tile, int nr, in
     xb = lds128(im + 128 + 16 * gid);
   }
   const uint32_t xg[8] = {xa.x, xa.y, xa.z, xa.w, xb.x, xb.y, xb.z, xb.w};
+  // every shared-memory load of the item first: headers, the two rows' four
+  // segments, the group sums
   const uint4 h0 = lds128(row0 + b * 16), h1 = lds128(row1 + b * 16);
-  const uint32_t SCa0 = h0.y & 0x3F3F3F3Fu, SCb0 = (h0.w & 0x0F0F0F0Fu) | ((h0.y >> 2) & 0x30303030u);
-  const uint32_t SCa1 = h1.y & 0x3F3F3F3Fu, SCb1 = (h1.w & 0x0F0F0F0Fu) | ((h1.y >> 2) & 0x30303030u);
   const uint8_t *q0 = row0 + P.nb * 16 + b * 128 + 8 * tig, *q1 = row1 + P.nb * 16 + b * 128 + 8 * tig;
-  int acc0 = 0, acc1 = 0, acc2 = 0, acc3 = 0;
+  uint2 w0[4], w1[4];
 #pragma unroll
   for (int p = 0; p < 4; p++) {
-    const uint2 w0 = lds64(q0 + 32 * p), w1 = lds64(q1 + 32 * p);
+    w0[p] = lds64(q0 + 32 * p);
+    w1[p] = lds64(q1 + 32 * p);
+  }
+  const int2 bs = *reinterpret_cast<const int2 *>(im + kImgQ8K4_BS + 8 * tig);
+  // the eight group MMAs (independent), then the int32 scaling
+  int dd[8][4];
+#pragma unroll
+  for (int p = 0; p < 4; p++) {
 #pragma unroll
     for (int h = 0; h < 2; h++) {
       const int g = 2 * p + h;
-      const uint32_t a0 = (h ? w0.x >> 4 : w0.x) & 0x0F0F0F0Fu, a1 = (h ? w1.x >> 4 : w1.x) & 0x0F0F0F0Fu;
-      const uint32_t a2 = (h ? w0.y >> 4 : w0.y) & 0x0F0F0F0Fu, a3 = (h ? w1.y >> 4 : w1.y) & 0x0F0F0F0Fu;
-      int d0, d1, d2, d3;
-      mma_s8(a0, a1, a2, a3, own0 ? xg[g] : 0u, own1 ? xg[g] : 0u, d0, d1, d2, d3);
-      const int s0 = byte_of(g < 4 ? SCa0 : SCb0, g & 3), s1 = byte_of(g < 4 ? SCa1 : SCb1, g & 3);
-      acc0 += s0 * d0;
-      acc1 += s0 * d1;
-      acc2 += s1 * d2;
-      acc3 += s1 * d3;
+      const uint32_t a0 = (h ? w0[p].x >> 4 : w0[p].x) & 0x0F0F0F0Fu, a1 = (h ? w1[p].x >> 4 : w1[p].x) & 0x0F0F0F0Fu;
+      const uint32_t a2 = (h ? w0[p].y >> 4 : w0[p].y) & 0x0F0F0F0Fu, a3 = (h ? w1[p].y >> 4 : w1[p].y) & 0x0F0F0F0Fu;
+      mma_s8(a0, a1, a2, a3, own0 ? xg[g] : 0u, own1 ? xg[g] : 0u, dd[g][0], dd[g][1], dd[g][2], dd[g][3]);
     }
   }
+  const uint32_t SCa0 = h0.y & 0x3F3F3F3Fu, SCb0 = (h0.w & 0x0F0F0F0Fu) | ((h0.y >> 2) & 0x30303030u);
+  const uint32_t SCa1 = h1.y & 0x3F3F3F3Fu, SCb1 = (h1.w & 0x0F0F0F0Fu) | ((h1.y >> 2) & 0x30303030u);
+  int acc0 = 0, acc1 = 0, acc2 = 0, acc3 = 0;
+#pragma unroll
+  for (int g = 0; g < 8; g++) {
+    const int s0 = byte_of(g < 4 ? SCa0 : SCb0, g & 3), s1 = byte_of(g < 4 ? SCa1 : SCb1, g & 3);
+    acc0 += s0 * dd[g][0];
+    acc1 += s0 * dd[g][1];
+    acc2 += s1 * dd[g][2];
+    acc3 += s1 * dd[g][3];
+  }
   // min term: sum over groups of m_g * (sum of group g's q8), groups 2t and 2t+1 here
-  const int2 bs = *reinterpret_cast<const int2 *>(im + kImgQ8K4_BS + 8 * tig);
   const uint32_t MA0 = h0.z & 0x3F3F3F3Fu, MB0 = ((h0.w >> 4) & 0x0F0F0F0Fu) | ((h0.z >> 2) & 0x30303030u);
   const uint32_t MA1 = h1.z & 0x3F3F3F3Fu, MB1 = ((h1.w >> 4) & 0x0F0F0F0Fu) | ((h1.z >> 2) & 0x30303030u);
   const uint32_t MM0 = tig < 2 ? MA0 : MB0, MM1 = tig < 2 ? MA1 : MB1;
@@ -694,6 +712,278 @@ __global__ void __launch_bounds__(NW * 32 + 32, 1) gemv_kernel(Params P) {
   }
 }
 
+// Tensor-core Q4_K Q8K GEMV with the chain phase on warps of its own: the
+// integer (MMA) warps hand each finished tile to the chain warps through an
+// mbarrier and go on to the next tile; two chain buffers alternate, recycled
+// through a second mbarrier pair. Nothing waits on a CTA-wide barrier per
+// tile. Every wait is bounded.
+constexpr int kTcIntWarps = 16, kTcChainWarps = 4;
+constexpr int kTcThreads = (kTcIntWarps + kTcChainWarps + 1) * 32;
+constexpr int kTcBarBytes = 256;
+// 256-element spans of a fused RMSNorm each integer warp keeps in registers.
+constexpr int kNormSpans = 2;
+static_assert(kTcThreads <= 1024, "a CTA has at most 1024 threads");
+static_assert((2 * kMaxStages + 4) * 8 <= kTcBarBytes, "barrier area");
+
+// RMSNorm (kernels.rs:61-78) of r = a (+ b) fused into the integer warps'
+// prologue, after griddepcontrol.wait: every CTA sums the n squares itself
+// (the reference's sequential f64 sum, resolved exactly as in the stand-alone
+// norm kernel), then each warp quantizes whole spans of xn = rmsnorm(r, w)
+// (quantize_q8_k) into the CTA's shared-memory image: warp w takes spans w
+// and w + 16, lane l their elements 8l .. 8l+7. CTA 0 also stores r and,
+// when asked, the Q4_K / Q6_K images for later GEMVs. All pointers are
+// 16-byte aligned (checked by gemv_launch).
+__device__ __forceinline__ void tc_norm_prologue(const Params &P, uint8_t *ximg) {
+  constexpr int NT = kTcIntWarps * 32;
+  __shared__ double red[kTcIntWarps];
+  __shared__ float s_mean;
+  const int t = threadIdx.x, warp = t >> 5, lane = t & 31, n = P.nn, nsp = n >> 8;
+  const bool cta0 = blockIdx.x == 0;
+  float r[kNormSpans][8], wv[kNormSpans][8];
+#pragma unroll
+  for (int u = 0; u < kNormSpans; u++) {
+    const int e0 = (warp + kTcIntWarps * u) * 256 + 8 * lane;
+    float4 a0 = make_float4(0.f, 0.f, 0.f, 0.f), a1 = a0, b0 = a0, b1 = a0, w0 = a0, w1 = a0;
+    if (e0 < n) {  // warp-uniform
+      const float4 *pa = reinterpret_cast<const float4 *>(P.norm_a + e0);
+      const float4 *pw = reinterpret_cast<const float4 *>(P.norm_w + e0);
+      a0 = pa[0];
+      a1 = pa[1];
+      w0 = pw[0];
+      w1 = pw[1];
+      if (P.norm_b) {
+        const float4 *pb = reinterpret_cast<const float4 *>(P.norm_b + e0);
+        b0 = pb[0];
+        b1 = pb[1];
+      }
+    }
+    const float av[8] = {a0.x, a0.y, a0.z, a0.w, a1.x, a1.y, a1.z, a1.w};
+    const float bv[8] = {b0.x, b0.y, b0.z, b0.w, b1.x, b1.y, b1.z, b1.w};
+    const float ww[8] = {w0.x, w0.y, w0.z, w0.w, w1.x, w1.y, w1.z, w1.w};
+#pragma unroll
+    for (int k = 0; k < 8; k++) {
+      r[u][k] = P.norm_b ? __fadd_rn(av[k], bv[k]) : av[k];
+      wv[u][k] = ww[k];
+    }
+  }
+  double S = 0.0;
+#pragma unroll
+  for (int u = 0; u < kNormSpans; u++)
+#pragma unroll
+    for (int k = 0; k < 8; k++) S += (double)__fmul_rn(r[u][k], r[u][k]);
+  if (cta0 && P.norm_r) {
+#pragma unroll
+    for (int u = 0; u < kNormSpans; u++) {
+      const int e0 = (warp + kTcIntWarps * u) * 256 + 8 * lane;
+      if (e0 < n) {
+        float4 *pr = reinterpret_cast<float4 *>(P.norm_r + e0);
+        pr[0] = make_float4(r[u][0], r[u][1], r[u][2], r[u][3]);
+        pr[1] = make_float4(r[u][4], r[u][5], r[u][6], r[u][7]);
+      }
+    }
+  }
+#pragma unroll
+  for (int o = 16; o; o >>= 1) S += __shfl_xor_sync(0xffffffffu, S, o);
+  if (lane == 0) red[warp] = S;
+  named_bar_sync(1, NT);
+  S = 0.0;
+#pragma unroll
+  for (int w = 0; w < kTcIntWarps; w++) S += red[w];
+  float mean;
+  const MeanOf f{n};
+  if (!resolve_sum(S, S, n, f, &mean)) {  // S is the same in every thread
+    if (t == 0) {
+      double q = 0.0;
+#pragma unroll 1
+      for (int i = 0; i < n; i++) {
+        const float v = P.norm_b ? __fadd_rn(P.norm_a[i], P.norm_b[i]) : P.norm_a[i];
+        q = __dadd_rn(q, (double)__fmul_rn(v, v));
+      }
+      s_mean = f(q);
+    }
+    named_bar_sync(1, NT);
+    mean = s_mean;
+  }
+  const float scale = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(mean, P.norm_eps)));
+#pragma unroll
+  for (int u = 0; u < kNormSpans; u++) {
+    const int span = warp + kTcIntWarps * u;
+    if (span < nsp) {  // warp-uniform
+      float xn[8];
+#pragma unroll
+      for (int k = 0; k < 8; k++) xn[k] = __fmul_rn(__fmul_rn(r[u][k], scale), wv[u][k]);
+      q8k_span_write_warp(xn, lane, ximg + (size_t)span * kImgQ8K4,
+                          cta0 && P.norm_img6 ? P.norm_img6 + (size_t)span * kImgQ8K6 : nullptr);
+    }
+  }
+  named_bar_sync(1, NT);
+  if (cta0 && P.norm_img4) {
+    const uint4 *src = reinterpret_cast<const uint4 *>(ximg);
+    uint4 *dst = reinterpret_cast<uint4 *>(P.norm_img4);
+    for (int k = t; k < P.img_bytes / 16; k += NT) dst[k] = src[k];
+  }
+}
+
+template <bool ARGMAX>
+__global__ void __launch_bounds__(kTcThreads, 1) gemv_tc_kernel(Params P) {
+  extern __shared__ __align__(128) uint8_t smem[];
+  uint64_t *full = reinterpret_cast<uint64_t *>(smem);
+  uint64_t *empty = full + kMaxStages;
+  uint64_t *intdone = empty + kMaxStages;  // [2]: a tile's integer results are in its chain buffer
+  uint64_t *chaindone = intdone + 2;       // [2]: the chain buffer is free again
+  uint8_t *ximg = smem + kTcBarBytes;
+  float *cbuf0 = reinterpret_cast<float *>(ximg + P.img_bytes);
+  uint8_t *stages = reinterpret_cast<uint8_t *>(cbuf0) + 2 * P.cbuf_bytes;
+  pdl_trigger();
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int G = gridDim.x;
+  const int rb = (int)((long long)P.rows * blockIdx.x / G);
+  const int re = (int)((long long)P.rows * (blockIdx.x + 1) / G);
+  const int ntiles = (re - rb + P.T - 1) / P.T;
+
+  if (threadIdx.x == 0) {
+    for (int st = 0; st < P.S; st++) {
+      mbar_init(&full[st], 1);
+      mbar_init(&empty[st], kTcIntWarps);
+    }
+    for (int b = 0; b < 2; b++) {
+      mbar_init(&intdone[b], kTcIntWarps);
+      mbar_init(&chaindone[b], kTcChainWarps);
+    }
+    fence_mbar_init();
+  }
+  __syncthreads();
+
+  if (warp == kTcIntWarps + kTcChainWarps) {
+    // ---------------- producer: padded rows, one bulk copy per row ----------
+    if (lane == 0) {
+      int issued = 0;
+      bool ok = true;
+      for (int i = 0; i < ntiles && ok; i++) {
+        const int st = i % P.S;
+        if (i >= P.S) ok = mbar_wait_bounded(&empty[st], ((i / P.S) - 1) & 1, P.err);
+        if (!ok) break;
+        const int r0 = rb + i * P.T;
+        const int nr = min(P.T, re - r0);
+        mbar_expect_tx(&full[st], (uint32_t)(nr * P.stride));
+        for (int rr = 0; rr < nr; rr++)
+          bulk_g2s(stages + (size_t)st * P.stage_bytes + (size_t)rr * P.pstride, P.W + (size_t)(r0 + rr) * P.stride,
+                   (uint32_t)P.stride, &full[st]);
+        issued = i + 1;
+      }
+      for (int i = max(0, issued - P.S); i < issued; i++)
+        mbar_wait_bounded(&full[i % P.S], (i / P.S) & 1, P.err);
+    }
+    return;
+  }
+
+  pdl_wait();
+  if (warp < kTcIntWarps) {
+    // ---------------- integer warps -------------------------------------------
+    if (P.nn) {
+      tc_norm_prologue(P, ximg);
+    } else {
+      const uint4 *src = reinterpret_cast<const uint4 *>(P.img);
+      uint4 *dst = reinterpret_cast<uint4 *>(ximg);
+      for (int k = threadIdx.x; k < P.img_bytes / 16; k += kTcIntWarps * 32) dst[k] = src[k];
+      named_bar_sync(1, kTcIntWarps * 32);
+    }
+    for (int i = 0; i < ntiles; i++) {
+      const int st = i % P.S;
+      const int r0 = rb + i * P.T;
+      const int nr = min(P.T, re - r0);
+      if (!mbar_wait_bounded(&full[st], (i / P.S) & 1, P.err)) break;
+      if (i >= 2 && !mbar_wait_bounded(&chaindone[i & 1], ((i >> 1) - 1) & 1, P.err)) break;
+      const uint8_t *tile = stages + (size_t)st * P.stage_bytes;
+      float *cb = reinterpret_cast<float *>(reinterpret_cast<uint8_t *>(cbuf0) + (i & 1) * P.cbuf_bytes);
+      const int nit = ((nr + 15) / 16) * P.nbu;
+      for (int it = warp; it < nit; it += kTcIntWarps) {
+        const int g16 = it / P.nbu, b = it - g16 * P.nbu;
+        const uint8_t *im = ximg + (size_t)b * kImgQ8K4;
+        q4k_q8k_mma_item(tile, nr, g16, b, im, P, cb, cb + P.T * P.rs,
+                         *reinterpret_cast<const float *>(im + kImgQ8K4_D));
+      }
+      __syncwarp();
+      if (lane == 0) {
+        mbar_arrive(&empty[st]);     // weight stage free
+        mbar_arrive(&intdone[i & 1]);  // integer results ready
+      }
+    }
+    return;
+  }
+
+  // ---------------- chain warps: the sequential per-row epilogue ------------
+  const int ct = threadIdx.x - kTcIntWarps * 32;  // 0 .. 32 * kTcChainWarps - 1
+  const int k = ct & 7;
+  const unsigned gm = 0xFFu << (lane & 24);
+  unsigned long long best = 0ull;
+  for (int i = 0; i < ntiles; i++) {
+    if (!mbar_wait_bounded(&intdone[i & 1], (i >> 1) & 1, P.err)) break;
+    const int r0 = rb + i * P.T;
+    const int nr = min(P.T, re - r0);
+    const float *cb = reinterpret_cast<const float *>(reinterpret_cast<const uint8_t *>(cbuf0) + (i & 1) * P.cbuf_bytes);
+    for (int lr = ct >> 3; lr < nr; lr += kTcChainWarps * 4) {
+      const float *tk = cb + lr * P.rs + k;
+      const float *tm = cb + P.T * P.rs + lr * (P.rs / 8);
+      float sums = 0.0f, sumf = 0.0f;
+      for (int b = 0; b < P.nbu; b += 8) {
+        float a[8], mm[8];
+#pragma unroll
+        for (int q = 0; q < 8; q++) {
+          const bool in = b + q < P.nbu;
+          a[q] = in ? tk[8 * (b + q)] : 0.0f;
+          mm[q] = in ? tm[b + q] : 0.0f;
+        }
+#pragma unroll
+        for (int q = 0; q < 8; q++) {
+          if (b + q < P.nbu) {
+            sums = __fadd_rn(sums, a[q]);
+            sumf = __fsub_rn(sumf, mm[q]);
+          }
+        }
+      }
+      float acc = sumf;
+#pragma unroll
+      for (int kk = 0; kk < 8; kk++) acc = __fadd_rn(acc, __shfl_sync(gm, sums, (lane & 24) + kk));
+      if (k == 0) {
+        const int row = r0 + lr;
+        if (P.y) P.y[row] = acc;
+        if (ARGMAX) {
+          const unsigned long long kk2 = argmax_key(acc, P.row0 + row);
+          best = kk2 > best ? kk2 : best;
+        }
+      }
+    }
+    __syncwarp();
+    if (lane == 0) mbar_arrive(&chaindone[i & 1]);
+  }
+  if constexpr (ARGMAX) {
+    __shared__ unsigned long long cta_best[kTcChainWarps];
+    for (int o = 16; o; o >>= 1) {
+      const unsigned long long other = __shfl_xor_sync(0xffffffffu, best, o);
+      best = other > best ? other : best;
+    }
+    if (lane == 0) cta_best[warp - kTcIntWarps] = best;
+    named_bar_sync(2, kTcChainWarps * 32);
+    if (ct == 0) {
+      unsigned long long b = cta_best[0];
+      for (int w2 = 1; w2 < kTcChainWarps; w2++) b = cta_best[w2] > b ? cta_best[w2] : b;
+      atomicMax(P.key, b);
+      __threadfence();
+      const unsigned prev = atomicAdd(P.done, 1u);
+      if (prev == gridDim.x - 1) {
+        __threadfence();
+        const unsigned long long kf = atomicAdd(P.key, 0ull);
+        *P.token = 0xffffffffu - (uint32_t)(kf & 0xffffffffull);
+        if (P.key_out) *P.key_out = kf;
+        *P.key = 0ull;
+        *P.done = 0u;
+      }
+    }
+  }
+}
+
 // Plain f32 weights (gemv_quant's F32 case): one warp per row, f32 FMA.
 __global__ void __launch_bounds__(kThreads) gemv_f32_kernel(const uint8_t *__restrict__ W, size_t stride,
                                                             int dim_in, int rows, const float *__restrict__ x,
@@ -745,7 +1035,7 @@ GemvFn pick_r(int R) {
 
 template <bool AM>
 GemvFn pick(int fmt, int mode, int R, bool mma = false) {
-  if (mma) return gemv_kernel<Q4K, MODE_Q8K, 2, AM, kMmaWarps, true>;
+  if (mma) return gemv_tc_kernel<AM>;
   if (mode == MODE_F32X) {
     if (fmt == Q4K) return pick_r<Q4K, MODE_F32X, AM>(R);
     if (fmt == Q6K) return pick_r<Q6K, MODE_F32X, AM>(R);
@@ -813,33 +1103,17 @@ int32_t gemv_reserve(unltd_ctx ctx, const unltd_weight_s &w, int mode) {
   return UNLTD_OK;
 }
 
-int32_t gemv_launch(unltd_ctx ctx, const GemvArgs &a) {
-  const unltd_weight_s &w = *a.w;
-  cudaStream_t st = ctx->stream;
-  const bool am = a.argmax_key != nullptr;
-  if (w.dim_out == 0) return UNLTD_OK;
+// Tile plan of a quantized GEMV: rows per tile T (R rows per work item),
+// stages S, shared-memory layout, grid. S < 2: the row does not fit.
+struct Plan {
+  int nbu, img_bytes, rows, R, T, S, stage_bytes, cbuf, pstride, mma, rs, smem, grid;
+};
 
-  if (w.dtype == F32) {
-    if (am) {
-      cudaError_t e = cudaMemsetAsync(a.argmax_key, 0, sizeof(unsigned long long), st);
-      if (e == cudaSuccess) e = cudaMemsetAsync(a.argmax_done, 0, sizeof(unsigned), st);
-      if (e != cudaSuccess) return cuda_error(e, "argmax reset");
-    }
-    const int rows = (int)w.dim_out;
-    int grid = std::min((rows + 7) / 8, ctx->num_sms * 8);
-    gemv_f32_kernel<<<grid, kThreads, 0, st>>>(w.dev, w.row_stride, (int)w.dim_in, rows, a.x, a.y,
-                                               a.argmax_key, a.argmax_done, a.token);
-    ctx->launches += 1;
-    return cuda_error(cudaGetLastError(), "gemv_f32");
-  }
-
-  const int fmt = w.dtype, mode = a.mode;
+Plan plan_gemv(unltd_ctx ctx, const unltd_weight_s &w, int mode) {
+  const int fmt = w.dtype;
   const int nspans = fmt == Q8_0 ? (int)((w.nb + 7) / 8) : (int)w.nb;
   const int nbu = nspans;
   const int img_bytes = nspans * img_stride(fmt, mode);
-  if (!a.img) {
-    if (int32_t rc = gemv_reserve(ctx, w, mode)) return rc;
-  }
 
   // ---- tiling: rows per tile T, stages S, shared-memory plan ----
   const int rows = (int)w.dim_out;
@@ -865,7 +1139,7 @@ int32_t gemv_launch(unltd_ctx ctx, const GemvArgs &a) {
     for (int t = 16; t <= 32; t += 16) {
       const int sb = (int)round_up((size_t)t * ps, 128);
       const int cb = cbuf_for(t);
-      const int fixed = kBarBytes + img_bytes + 2 * cb;
+      const int fixed = kTcBarBytes + img_bytes + 2 * cb;
       const int s = std::min(kMaxStages, (smem_max - fixed) / sb);
       if (s < 2) continue;
       const int items = (t / 16) * nbu;
@@ -903,16 +1177,77 @@ int32_t gemv_launch(unltd_ctx ctx, const GemvArgs &a) {
       cbuf = cb;
     }
   }
-  if (S < 2)
-    return set_error(UNLTD_ERR_UNSUPPORTED, "gemv: row too long for the shared-memory pipeline (dim_in too large)");
-  const int smem = kBarBytes + img_bytes + 2 * cbuf + S * stage_bytes;
-  const int grid = std::max(1, std::min(ctx->num_sms, (rows + T - 1) / T));
+  Plan p;
+  p.nbu = nbu;
+  p.img_bytes = img_bytes;
+  p.rows = rows;
+  p.R = R;
+  p.T = T;
+  p.S = S;
+  p.stage_bytes = stage_bytes;
+  p.cbuf = cbuf;
+  p.pstride = pstride;
+  p.mma = mma;
+  p.rs = rs;
+  p.smem = (mma ? kTcBarBytes : kBarBytes) + img_bytes + 2 * cbuf + S * stage_bytes;
+  p.grid = T ? std::max(1, std::min(ctx->num_sms, (rows + T - 1) / T)) : 1;
+  return p;
+}
 
-  // 1) prep (skipped when the caller's kernel already wrote the image)
+bool gemv_norm_fusable(unltd_ctx ctx, const unltd_weight_s &w, int mode) {
+  if (w.dtype != Q4K || mode != MODE_Q8K || w.dim_out == 0) return false;
+  if (w.dim_in > (size_t)kNormSpans * kTcIntWarps * 256) return false;
+  const Plan p = plan_gemv(ctx, w, mode);
+  return p.S >= 2 && p.mma;
+}
+
+int32_t gemv_launch(unltd_ctx ctx, const GemvArgs &a) {
+  const unltd_weight_s &w = *a.w;
+  cudaStream_t st = ctx->stream;
+  const bool am = a.argmax_key != nullptr;
+  if (w.dim_out == 0) return UNLTD_OK;
+
+  if (w.dtype == F32) {
+    if (am) {
+      cudaError_t e = cudaMemsetAsync(a.argmax_key, 0, sizeof(unsigned long long), st);
+      if (e == cudaSuccess) e = cudaMemsetAsync(a.argmax_done, 0, sizeof(unsigned), st);
+      if (e != cudaSuccess) return cuda_error(e, "argmax reset");
+    }
+    const int rows = (int)w.dim_out;
+    int grid = std::min((rows + 7) / 8, ctx->num_sms * 8);
+    gemv_f32_kernel<<<grid, kThreads, 0, st>>>(w.dev, w.row_stride, (int)w.dim_in, rows, a.x, a.y,
+                                               a.argmax_key, a.argmax_done, a.token);
+    ctx->launches += 1;
+    return cuda_error(cudaGetLastError(), "gemv_f32");
+  }
+
+  const int fmt = w.dtype, mode = a.mode;
+  const bool fuse = a.norm != nullptr;
+  if (fuse && (am || !gemv_norm_fusable(ctx, w, mode)))
+    return set_error(UNLTD_ERR_INVALID_ARG, "gemv: RMSNorm fusion needs a tensor-core Q4_K Q8K GEMV without argmax");
+  if (fuse) {
+    const GemvNorm &g = *a.norm;
+    const void *ptrs[6] = {g.a, g.b, g.r_out, g.w, g.img4_out, g.img6_out};
+    for (const void *p : ptrs)
+      if ((uintptr_t)p % 16) return set_error(UNLTD_ERR_INVALID_ARG, "gemv: fused RMSNorm pointers must be 16-byte aligned");
+    if (!g.a || !g.w) return set_error(UNLTD_ERR_INVALID_ARG, "gemv: fused RMSNorm needs a and w");
+  }
+  if (!a.img && !fuse) {
+    if (int32_t rc = gemv_reserve(ctx, w, mode)) return rc;
+  }
+  const Plan pl = plan_gemv(ctx, w, mode);
+  if (pl.S < 2)
+    return set_error(UNLTD_ERR_UNSUPPORTED, "gemv: row too long for the shared-memory pipeline (dim_in too large)");
+  const int nspans = pl.nbu, nbu = pl.nbu, img_bytes = pl.img_bytes, rows = pl.rows;
+  const int R = pl.R, T = pl.T, S = pl.S, stage_bytes = pl.stage_bytes, cbuf = pl.cbuf, pstride = pl.pstride;
+  const int mma = pl.mma, rs = pl.rs, smem = pl.smem, grid = pl.grid;
+
+  // 1) prep (skipped when the caller's kernel already wrote the image, or
+  // when the GEMV's own prologue quantizes a fused RMSNorm)
   unsigned long long *key = am ? a.argmax_key : nullptr;
   unsigned *done = am ? a.argmax_done : nullptr;
   cudaError_t e = cudaSuccess;
-  if (a.img) {
+  if (a.img || fuse) {
   } else if (mode == MODE_F32X) {
     if (fmt == Q4K) prep_f32x<Q4K><<<nspans, kThreads, 0, st>>>(a.x, w.dim_in, ctx->scratch, key, done);
     else if (fmt == Q6K) prep_f32x<Q6K><<<nspans, kThreads, 0, st>>>(a.x, w.dim_in, ctx->scratch, key, done);
@@ -921,7 +1256,7 @@ int32_t gemv_launch(unltd_ctx ctx, const GemvArgs &a) {
     if (fmt == Q4K) prep_q8k<Q4K><<<nspans, kThreads, 0, st>>>(a.x, w.dim_in, ctx->scratch, key, done);
     else prep_q8k<Q6K><<<nspans, kThreads, 0, st>>>(a.x, w.dim_in, ctx->scratch, key, done);
   }
-  if (!a.img) {
+  if (!a.img && !fuse) {
     e = cudaGetLastError();
     if (e != cudaSuccess) return cuda_error(e, "gemv prep");
     ctx->launches += 1;
@@ -953,10 +1288,18 @@ int32_t gemv_launch(unltd_ctx ctx, const GemvArgs &a) {
   P.stage_bytes = stage_bytes;
   P.rs = rs;
   P.cbuf_bytes = cbuf;
+  P.norm_a = fuse ? a.norm->a : nullptr;
+  P.norm_b = fuse ? a.norm->b : nullptr;
+  P.norm_r = fuse ? a.norm->r_out : nullptr;
+  P.norm_w = fuse ? a.norm->w : nullptr;
+  P.norm_eps = fuse ? a.norm->eps : 0.0f;
+  P.norm_img4 = fuse ? a.norm->img4_out : nullptr;
+  P.norm_img6 = fuse ? a.norm->img6_out : nullptr;
+  P.nn = fuse ? (int)w.dim_in : 0;
 
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(grid);
-  cfg.blockDim = dim3(mma ? kMmaWarps * 32 + 32 : kGemvThreads);
+  cfg.blockDim = dim3(mma ? kTcThreads : kGemvThreads);
   cfg.dynamicSmemBytes = smem;
   cfg.stream = st;
   cudaLaunchAttribute attr[1];

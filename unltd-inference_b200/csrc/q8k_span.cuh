@@ -87,4 +87,80 @@ __device__ __forceinline__ void q8k_span_write(float v, uint8_t *im4, uint8_t *i
   }
 }
 
+// The same quantize_q8_k of one span held by ONE warp: lane l holds elements
+// 8l .. 8l+7 in v[0..7]. Warp shuffles only, no block barrier, so the warps
+// of a CTA quantize their spans concurrently.
+__device__ __forceinline__ void q8k_span_write_warp(const float (&v)[8], int lane, uint8_t *im4, uint8_t *im6) {
+  // first strict argmax of |x| (ties: lowest index); NaN never wins
+  float a = -1.0f, val = 0.0f;
+  int idx = 8 * lane;
+#pragma unroll
+  for (int k = 0; k < 8; k++) {
+    float ak = fabsf(v[k]);
+    if (isnan(ak)) ak = -1.0f;
+    if (ak > a) {
+      a = ak;
+      idx = 8 * lane + k;
+      val = v[k];
+    }
+  }
+#pragma unroll
+  for (int o = 16; o; o >>= 1) {
+    const float oa = __shfl_xor_sync(0xffffffffu, a, o);
+    const int oi = __shfl_xor_sync(0xffffffffu, idx, o);
+    const float ov = __shfl_xor_sync(0xffffffffu, val, o);
+    if (oa > a || (oa == a && oi < idx)) {
+      a = oa;
+      idx = oi;
+      val = ov;
+    }
+  }
+  int q[8];
+  float d = 0.0f;
+  if (a > 0.0f) {
+    const float iscale = __fdiv_rn(-127.0f, val);
+#pragma unroll
+    for (int k = 0; k < 8; k++) {
+      const float prod = __fmul_rn(iscale, v[k]);
+      const int ni = (__float_as_int(__fadd_rn(prod, 12582912.0f)) & 0x007fffff) - 0x00400000;
+      q[k] = ni < 127 ? ni : 127;
+    }
+    d = __fdiv_rn(1.0f, iscale);
+  } else {
+#pragma unroll
+    for (int k = 0; k < 8; k++) q[k] = 0;
+  }
+  if (im4) {
+    // class-major (q4k_q8k_xpos of e = 8 lane + k); group g = lane / 4
+    const int g = lane >> 2;
+    const int base = 128 * (g >> 2) + 4 * (g & 3) + (lane & 3);
+    int hs = 0;
+#pragma unroll
+    for (int k = 0; k < 8; k++) {
+      im4[base + 16 * k] = (uint8_t)(int8_t)q[k];
+      hs += q[k];
+    }
+    hs += __shfl_xor_sync(0xffffffffu, hs, 1);
+    hs += __shfl_xor_sync(0xffffffffu, hs, 2);
+    int *bs = reinterpret_cast<int *>(im4 + kImgQ8K4_BS);
+    if ((lane & 3) == 0) bs[g] = hs;
+    if (lane < 8) bs[8 + lane] = 0;
+    if (lane == 0) *reinterpret_cast<float *>(im4 + kImgQ8K4_D) = d;
+  }
+  if (im6) {
+#pragma unroll
+    for (int k = 0; k < 8; k++) {
+      const int t = 8 * lane + k;
+      const int h = t >> 7, pos = t & 127, hh = pos >> 6, c = pos & 63, u = c >> 4, ipos = c & 15;
+      const int j = 4 * h + u;
+      const int pic = q6_pic(ipos);
+      const int w = pic >> 2, bpos = pic & 3;
+      const int own = bpos < 2 ? 0 : 1;
+      im6[q6_q8k_byte(j, hh, w, own, bpos)] = (uint8_t)(int8_t)q[k];
+      im6[q6_q8k_byte(j, hh, w, 1 - own, bpos)] = 0;
+    }
+    if (lane == 0) *reinterpret_cast<float *>(im6 + kImgQ8K6_D) = d;
+  }
+}
+
 }  // namespace unltd

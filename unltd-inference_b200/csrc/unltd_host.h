@@ -68,6 +68,13 @@ cudaError_t launch_repack(const unltd_weight_s &w, const uint8_t *raw_dev, size_
 cudaError_t launch_dequant(const unltd_weight_s &w, float *out, cudaStream_t s);
 
 // gemv.cu
+struct GemvNorm {
+  const float *a, *b;
+  float *r_out;
+  const float *w;
+  float eps;
+  uint8_t *img4_out, *img6_out;
+};
 struct GemvArgs {
   const unltd_weight_s *w;
   const float *x;
@@ -83,8 +90,15 @@ struct GemvArgs {
   // the final 64-bit key (for the cross-GPU MAX) besides the token.
   int argmax_row0 = 0;
   unsigned long long *key_out = nullptr;
+  // Non-null: RMSNorm fused into the GEMV's prologue (tensor-core Q4_K Q8K
+  // path only, see gemv_norm_fusable): x = rmsnorm(a (+ b), w) is quantized
+  // by every CTA into its own image; CTA 0 also stores r = a (+ b) to r_out
+  // and the Q4_K / Q6_K images to img4_out / img6_out for later GEMVs.
+  const GemvNorm *norm = nullptr;
 };
 int32_t gemv_launch(unltd_ctx ctx, const GemvArgs &a);
+// True when gemv_launch can fuse an RMSNorm of length w.dim_in into w's GEMV.
+bool gemv_norm_fusable(unltd_ctx ctx, const unltd_weight_s &w, int mode);
 // Grow the context's x-image scratch for w (call before stream capture).
 int32_t gemv_reserve(unltd_ctx ctx, const unltd_weight_s &w, int mode);
 void gemv_prewarm(int device);

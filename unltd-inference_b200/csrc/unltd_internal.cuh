@@ -250,4 +250,23 @@ __device__ __forceinline__ float q4k_row_elem(const uint8_t *row, size_t nb, siz
   return __fsub_rn(__fmul_rn(d1, (float)q), m1);
 }
 
+// f(seq) for the reference's left-to-right f64 sum `seq` of n terms, given
+// the parallel sum S of the same terms and their absolute sum A, with f a
+// monotone non-decreasing map to f32. True when the bound decides it.
+template <class F>
+__device__ __forceinline__ bool resolve_sum(double S, double A, int n, F f, float *out) {
+  const double B = (double)(n + 8) * 0x1p-51 * A;
+  const float lo = f(S - B), hi = f(S + B);
+  *out = lo;
+  return lo == hi;
+}
+
+struct MeanOf {
+  int n;
+  __device__ float operator()(double s) const { return (float)(s / (double)n); }
+};
+struct ToF32 {
+  __device__ float operator()(double s) const { return (float)s; }
+};
+
 }  // namespace unltd
