@@ -45,8 +45,7 @@ constexpr int kThreads = 256;  // prep kernels
 constexpr int kConsumerWarps = 16;
 constexpr int kConsumers = kConsumerWarps * 32;
 constexpr int kGemvThreads = kConsumers + 32;  // + one producer warp
-constexpr int kMmaWarps = 16;                     // consumer warps of the tensor-core Q4_K Q8K kernel
-static_assert(kMmaWarps * 32 + 32 <= 1024 && kGemvThreads <= 1024, "a CTA has at most 1024 threads");
+static_assert(kGemvThreads <= 1024, "a CTA has at most 1024 threads");
 constexpr int kMaxStages = 8;
 constexpr int kBarBytes = 128;
 
@@ -183,21 +182,28 @@ __device__ __forceinline__ void mma_s8(uint32_t a0, uint32_t a1, uint32_t a2, ui
 // byte k (0..3) of w as an int
 __device__ __forceinline__ int byte_of(uint32_t w, int k) { return (int)__byte_perm(w, 0u, 0x4440u | (uint32_t)k); }
 
-// Q8K, Q4_K on the tensor cores: one warp takes 16 rows x one block. For
-// each scale group g an int8 MMA m16n8k32 multiplies the 16 rows' 32 quants
-// of the group (A: thread (r, t) holds words 2t and 2t+1 of the row's 32-byte
-// qs segment, i.e. classes 2t and 2t+1, each four elements) by the class-
-// masked q8 values (B column n = class n: only the thread owning class n,
-// r == 2t (+1), holds its class's q8 word), giving every (row, class)
-// integer partial of the group at once; the group scales are applied per
-// row in int32 (exact). The min term takes groups 2t, 2t+1 per thread.
-__device__ __forceinline__ void q4k_q8k_mma_item(const uint8_t *tile, int nr, int g16, int b, const uint8_t *im,
-                                                 const Params &P, float *tk, float *tm, float xd) {
+// A(16x32 u8, row) * B(32x8 s8, col), exact int32: the high nibbles of the
+// Q4_K words taken in place (w & 0xF0F0F0F0, i.e. 16 x nibble)
+__device__ __forceinline__ void mma_u8s8(uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3, uint32_t b0, uint32_t b1,
+                                         int &d0, int &d1, int &d2, int &d3) {
+  asm("mma.sync.aligned.m16n8k32.row.col.s32.u8.s8.s32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%10,%10,%10,%10};"
+      : "=r"(d0), "=r"(d1), "=r"(d2), "=r"(d3)
+      : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1), "r"(0));
+}
+
+// One block of the class-major Q8_K x image as the MMA B operands of this
+// lane: column n of B is class n, and lane (gid, tig) holds B[k-quad tig][gid]
+// (class 2 tig elements) and B[k-quad 4 + tig][gid] (class 2 tig + 1), nonzero
+// only when gid is that class; plus the group sums 2 tig, 2 tig + 1 (min
+// term) and the block's d.
+struct XBlock {
+  uint32_t b0[8], b1[8];
+  int2 bs;
+  float xd;
+};
+
+__device__ __forceinline__ void load_xblock(const uint8_t *im, XBlock &x) {
   const int lane = threadIdx.x & 31, gid = lane >> 2, tig = lane & 3;
-  const int lr0 = g16 * 16 + gid, lr1 = lr0 + 8;
-  const bool v0 = lr0 < nr, v1 = lr1 < nr;
-  const uint8_t *row0 = tile + (size_t)(v0 ? lr0 : 0) * P.pstride;
-  const uint8_t *row1 = tile + (size_t)(v1 ? lr1 : 0) * P.pstride;
   const bool own0 = gid == 2 * tig, own1 = gid == 2 * tig + 1;
   uint4 xa = make_uint4(0u, 0u, 0u, 0u), xb = xa;
   if (own0 || own1) {
@@ -205,62 +211,86 @@ __device__ __forceinline__ void q4k_q8k_mma_item(const uint8_t *tile, int nr, in
     xb = lds128(im + 128 + 16 * gid);
   }
   const uint32_t xg[8] = {xa.x, xa.y, xa.z, xa.w, xb.x, xb.y, xb.z, xb.w};
-  // every shared-memory load of the item first: headers, the two rows' four
-  // segments, the group sums
+#pragma unroll
+  for (int g = 0; g < 8; g++) {
+    x.b0[g] = own0 ? xg[g] : 0u;
+    x.b1[g] = own1 ? xg[g] : 0u;
+  }
+  x.bs = *reinterpret_cast<const int2 *>(im + kImgQ8K4_BS + 8 * tig);
+  x.xd = *reinterpret_cast<const float *>(im + kImgQ8K4_D);
+}
+
+// Q8K, Q4_K on the tensor cores: one warp takes 16 rows x one block. For
+// each scale group g an int8 MMA m16n8k32 multiplies the 16 rows' 32 quants
+// of the group (A: thread (r, t) holds words 2t and 2t+1 of the row's 32-byte
+// qs segment, i.e. classes 2t and 2t+1, each four elements) by the class-
+// masked q8 values (XBlock), giving every (row, class) integer partial of the
+// group at once; the group scales are applied per row in int32 (exact). The
+// odd groups (high nibbles) enter as 16 x nibble and their scaled sum is
+// divided by 16 at the end (exact: every term is a multiple of 16, and the
+// sum stays below 2^31). The min term takes groups 2t, 2t+1 per thread.
+__device__ __forceinline__ void q4k_q8k_mma_item(const uint8_t *tile, int nr, int g16, int b, const XBlock &x,
+                                                 const Params &P, float *tk, float *tm) {
+  const int lane = threadIdx.x & 31, gid = lane >> 2, tig = lane & 3;
+  const int lr0 = g16 * 16 + gid, lr1 = lr0 + 8;
+  const bool v0 = lr0 < nr, v1 = lr1 < nr;
+  const uint8_t *row0 = tile + (v0 ? lr0 : 0) * P.pstride;
+  const uint8_t *row1 = tile + (v1 ? lr1 : 0) * P.pstride;
   const uint4 h0 = lds128(row0 + b * 16), h1 = lds128(row1 + b * 16);
-  const uint8_t *q0 = row0 + P.nb * 16 + b * 128 + 8 * tig, *q1 = row1 + P.nb * 16 + b * 128 + 8 * tig;
+  const int qo = P.nb * 16 + b * 128 + 8 * tig;
   uint2 w0[4], w1[4];
 #pragma unroll
   for (int p = 0; p < 4; p++) {
-    w0[p] = lds64(q0 + 32 * p);
-    w1[p] = lds64(q1 + 32 * p);
-  }
-  const int2 bs = *reinterpret_cast<const int2 *>(im + kImgQ8K4_BS + 8 * tig);
-  // the eight group MMAs (independent), then the int32 scaling
-  int dd[8][4];
-#pragma unroll
-  for (int p = 0; p < 4; p++) {
-#pragma unroll
-    for (int h = 0; h < 2; h++) {
-      const int g = 2 * p + h;
-      const uint32_t a0 = (h ? w0[p].x >> 4 : w0[p].x) & 0x0F0F0F0Fu, a1 = (h ? w1[p].x >> 4 : w1[p].x) & 0x0F0F0F0Fu;
-      const uint32_t a2 = (h ? w0[p].y >> 4 : w0[p].y) & 0x0F0F0F0Fu, a3 = (h ? w1[p].y >> 4 : w1[p].y) & 0x0F0F0F0Fu;
-      mma_s8(a0, a1, a2, a3, own0 ? xg[g] : 0u, own1 ? xg[g] : 0u, dd[g][0], dd[g][1], dd[g][2], dd[g][3]);
-    }
+    w0[p] = lds64(row0 + qo + 32 * p);
+    w1[p] = lds64(row1 + qo + 32 * p);
   }
   const uint32_t SCa0 = h0.y & 0x3F3F3F3Fu, SCb0 = (h0.w & 0x0F0F0F0Fu) | ((h0.y >> 2) & 0x30303030u);
   const uint32_t SCa1 = h1.y & 0x3F3F3F3Fu, SCb1 = (h1.w & 0x0F0F0F0Fu) | ((h1.y >> 2) & 0x30303030u);
-  int acc0 = 0, acc1 = 0, acc2 = 0, acc3 = 0;
+  int lo0 = 0, lo1 = 0, lo2 = 0, lo3 = 0, hi0 = 0, hi1 = 0, hi2 = 0, hi3 = 0;
 #pragma unroll
-  for (int g = 0; g < 8; g++) {
-    const int s0 = byte_of(g < 4 ? SCa0 : SCb0, g & 3), s1 = byte_of(g < 4 ? SCa1 : SCb1, g & 3);
-    acc0 += s0 * dd[g][0];
-    acc1 += s0 * dd[g][1];
-    acc2 += s1 * dd[g][2];
-    acc3 += s1 * dd[g][3];
+  for (int p = 0; p < 4; p++) {
+    const uint32_t S0 = p < 2 ? SCa0 : SCb0, S1 = p < 2 ? SCa1 : SCb1;
+    const int k = (2 * p) & 3;
+    int d0, d1, d2, d3, e0, e1, e2, e3;
+    mma_s8(w0[p].x & 0x0F0F0F0Fu, w1[p].x & 0x0F0F0F0Fu, w0[p].y & 0x0F0F0F0Fu, w1[p].y & 0x0F0F0F0Fu, x.b0[2 * p],
+           x.b1[2 * p], d0, d1, d2, d3);
+    mma_u8s8(w0[p].x & 0xF0F0F0F0u, w1[p].x & 0xF0F0F0F0u, w0[p].y & 0xF0F0F0F0u, w1[p].y & 0xF0F0F0F0u,
+             x.b0[2 * p + 1], x.b1[2 * p + 1], e0, e1, e2, e3);
+    const int s0 = byte_of(S0, k), s1 = byte_of(S1, k), t0 = byte_of(S0, k + 1), t1 = byte_of(S1, k + 1);
+    lo0 += s0 * d0;
+    lo1 += s0 * d1;
+    lo2 += s1 * d2;
+    lo3 += s1 * d3;
+    hi0 += t0 * e0;
+    hi1 += t0 * e1;
+    hi2 += t1 * e2;
+    hi3 += t1 * e3;
   }
+  const int acc0 = lo0 + (hi0 >> 4), acc1 = lo1 + (hi1 >> 4), acc2 = lo2 + (hi2 >> 4), acc3 = lo3 + (hi3 >> 4);
   // min term: sum over groups of m_g * (sum of group g's q8), groups 2t and 2t+1 here
   const uint32_t MA0 = h0.z & 0x3F3F3F3Fu, MB0 = ((h0.w >> 4) & 0x0F0F0F0Fu) | ((h0.z >> 2) & 0x30303030u);
   const uint32_t MA1 = h1.z & 0x3F3F3F3Fu, MB1 = ((h1.w >> 4) & 0x0F0F0F0Fu) | ((h1.z >> 2) & 0x30303030u);
   const uint32_t MM0 = tig < 2 ? MA0 : MB0, MM1 = tig < 2 ? MA1 : MB1;
   const int k0 = (2 * tig) & 3;
-  int ms0 = byte_of(MM0, k0) * bs.x + byte_of(MM0, k0 + 1) * bs.y;
-  int ms1 = byte_of(MM1, k0) * bs.x + byte_of(MM1, k0 + 1) * bs.y;
+  int ms0 = byte_of(MM0, k0) * x.bs.x + byte_of(MM0, k0 + 1) * x.bs.y;
+  int ms1 = byte_of(MM1, k0) * x.bs.x + byte_of(MM1, k0 + 1) * x.bs.y;
   ms0 += __shfl_xor_sync(0xffffffffu, ms0, 1);
   ms1 += __shfl_xor_sync(0xffffffffu, ms1, 1);
   ms0 += __shfl_xor_sync(0xffffffffu, ms0, 2);
   ms1 += __shfl_xor_sync(0xffffffffu, ms1, 2);
   const int rs2 = P.rs / 8;
   if (v0) {
-    const float d = __fmul_rn(xd, h2f_bits(h0.x & 0xFFFFu)), dm = __fmul_rn(h2f_bits(h0.x >> 16), xd);
-    tk[lr0 * P.rs + 8 * b + 2 * tig] = __fmul_rn(d, (float)acc0);
-    tk[lr0 * P.rs + 8 * b + 2 * tig + 1] = __fmul_rn(d, (float)acc1);
+    const float d = __fmul_rn(x.xd, h2f_bits(h0.x & 0xFFFFu)), dm = __fmul_rn(h2f_bits(h0.x >> 16), x.xd);
+    float *t = tk + lr0 * P.rs + 8 * b + 2 * tig;
+    t[0] = __fmul_rn(d, (float)acc0);
+    t[1] = __fmul_rn(d, (float)acc1);
     if (tig == 0) tm[lr0 * rs2 + b] = __fmul_rn(dm, (float)ms0);
   }
   if (v1) {
-    const float d = __fmul_rn(xd, h2f_bits(h1.x & 0xFFFFu)), dm = __fmul_rn(h2f_bits(h1.x >> 16), xd);
-    tk[lr1 * P.rs + 8 * b + 2 * tig] = __fmul_rn(d, (float)acc2);
-    tk[lr1 * P.rs + 8 * b + 2 * tig + 1] = __fmul_rn(d, (float)acc3);
+    const float d = __fmul_rn(x.xd, h2f_bits(h1.x & 0xFFFFu)), dm = __fmul_rn(h2f_bits(h1.x >> 16), x.xd);
+    float *t = tk + lr1 * P.rs + 8 * b + 2 * tig;
+    t[0] = __fmul_rn(d, (float)acc2);
+    t[1] = __fmul_rn(d, (float)acc3);
     if (tig == 0) tm[lr1 * rs2 + b] = __fmul_rn(dm, (float)ms1);
   }
 }
@@ -510,7 +540,7 @@ __device__ __forceinline__ void integer_item(const uint8_t *const (&rowp)[R], co
   }
 }
 
-template <int FMT, int MODE, int R, bool ARGMAX, int NW = kConsumerWarps, bool MMA = false>
+template <int FMT, int MODE, int R, bool ARGMAX, int NW = kConsumerWarps>
 __global__ void __launch_bounds__(NW * 32 + 32, 1) gemv_kernel(Params P) {
   constexpr int kCW = NW, kCons = NW * 32;  // consumer warps / threads
   extern __shared__ __align__(128) uint8_t smem[];
@@ -596,20 +626,9 @@ __global__ void __launch_bounds__(NW * 32 + 32, 1) gemv_kernel(Params P) {
     float *cb = reinterpret_cast<float *>(reinterpret_cast<uint8_t *>(cbuf0) + (i & 1) * P.cbuf_bytes);
 
     // integer phase
-    constexpr bool use_mma = FMT == Q4K && MODE == MODE_Q8K && MMA;
-    if constexpr (use_mma) {
-      const int ng16 = (nr + 15) / 16;
-      const int nit = got ? ng16 * P.nbu : 0;
-      for (int it = warp; it < nit; it += kCW) {
-        const int g16 = it / P.nbu, b = it - g16 * P.nbu;
-        const uint8_t *im = ximg + (size_t)b * kImgQ8K4;
-        q4k_q8k_mma_item(tile, nr, g16, b, im, P, cb, cb + P.T * P.rs,
-                         *reinterpret_cast<const float *>(im + kImgQ8K4_D));
-      }
-    }
     const int ngroups = (nr + R - 1) / R;
-    const int nitems = (got && !use_mma) ? ngroups * P.nbu : 0;
-    for (int it = sg; it < nitems && !use_mma; it += kSubgroups) {
+    const int nitems = got ? ngroups * P.nbu : 0;
+    for (int it = sg; it < nitems; it += kSubgroups) {
       const int g = it / P.nbu, b = it - g * P.nbu;
       const uint8_t *rowp[R];
       bool rv[R];
@@ -717,7 +736,7 @@ __global__ void __launch_bounds__(NW * 32 + 32, 1) gemv_kernel(Params P) {
 // mbarrier and go on to the next tile; two chain buffers alternate, recycled
 // through a second mbarrier pair. Nothing waits on a CTA-wide barrier per
 // tile. Every wait is bounded.
-constexpr int kTcIntWarps = 16, kTcChainWarps = 4;
+constexpr int kTcIntWarps = 16, kTcChainWarps = 3;
 constexpr int kTcThreads = (kTcIntWarps + kTcChainWarps + 1) * 32;
 constexpr int kTcBarBytes = 256;
 // 256-element spans of a fused RMSNorm each integer warp keeps in registers.
@@ -889,6 +908,13 @@ __global__ void __launch_bounds__(kTcThreads, 1) gemv_tc_kernel(Params P) {
       for (int k = threadIdx.x; k < P.img_bytes / 16; k += kTcIntWarps * 32) dst[k] = src[k];
       named_bar_sync(1, kTcIntWarps * 32);
     }
+    // when the block count divides the warp count, a warp always takes the
+    // same block (row groups rg0, rg0 + rgs, ...): its x operands stay in
+    // registers for the whole kernel
+    const bool fixed = kTcIntWarps % P.nbu == 0;
+    const int myb = warp % P.nbu, rg0 = warp / P.nbu, rgs = kTcIntWarps / P.nbu;
+    XBlock xb;
+    if (fixed) load_xblock(ximg + (size_t)myb * kImgQ8K4, xb);
     for (int i = 0; i < ntiles; i++) {
       const int st = i % P.S;
       const int r0 = rb + i * P.T;
@@ -897,12 +923,17 @@ __global__ void __launch_bounds__(kTcThreads, 1) gemv_tc_kernel(Params P) {
       if (i >= 2 && !mbar_wait_bounded(&chaindone[i & 1], ((i >> 1) - 1) & 1, P.err)) break;
       const uint8_t *tile = stages + (size_t)st * P.stage_bytes;
       float *cb = reinterpret_cast<float *>(reinterpret_cast<uint8_t *>(cbuf0) + (i & 1) * P.cbuf_bytes);
-      const int nit = ((nr + 15) / 16) * P.nbu;
-      for (int it = warp; it < nit; it += kTcIntWarps) {
-        const int g16 = it / P.nbu, b = it - g16 * P.nbu;
-        const uint8_t *im = ximg + (size_t)b * kImgQ8K4;
-        q4k_q8k_mma_item(tile, nr, g16, b, im, P, cb, cb + P.T * P.rs,
-                         *reinterpret_cast<const float *>(im + kImgQ8K4_D));
+      float *cm = cb + P.T * P.rs;
+      const int ng = (nr + 15) / 16;
+      if (fixed) {
+        for (int g16 = rg0; g16 < ng; g16 += rgs) q4k_q8k_mma_item(tile, nr, g16, myb, xb, P, cb, cm);
+      } else {
+        for (int it = warp; it < ng * P.nbu; it += kTcIntWarps) {
+          const int g16 = it / P.nbu, b = it - g16 * P.nbu;
+          XBlock xv;
+          load_xblock(ximg + (size_t)b * kImgQ8K4, xv);
+          q4k_q8k_mma_item(tile, nr, g16, b, xv, P, cb, cm);
+        }
       }
       __syncwarp();
       if (lane == 0) {
@@ -1143,7 +1174,7 @@ Plan plan_gemv(unltd_ctx ctx, const unltd_weight_s &w, int mode) {
       const int s = std::min(kMaxStages, (smem_max - fixed) / sb);
       if (s < 2) continue;
       const int items = (t / 16) * nbu;
-      const double score = (items % kMmaWarps == 0 ? 2.0 : 0.0) + (items >= kMmaWarps ? 1.0 : 0.0) + t / 16.0;
+      const double score = (items % kTcIntWarps == 0 ? 2.0 : 0.0) + (items >= kTcIntWarps ? 1.0 : 0.0) + t / 16.0;
       if (score > best_score) {
         best_score = score;
         T = t;

@@ -98,6 +98,19 @@ def _track(obj, rank: int):
     _live[rank].add(obj)
 
 
+def _owner(obj):
+    """The Context a session, model or weight lives in."""
+    if hasattr(obj, "model"):
+        obj = obj.model
+    return getattr(obj, "ctx", None)
+
+
+def _alive(obj) -> bool:
+    """True while obj holds a handle and its context has not been destroyed."""
+    c = _owner(obj)
+    return bool(getattr(obj, "h", None)) and (c is None or bool(getattr(c, "h", None)))
+
+
 @atexit.register
 def _close_all():
     for group in _live:
@@ -215,6 +228,12 @@ class Context:
 
     def close(self):
         if getattr(self, "h", None):
+            # release what lives in this context first (sessions, models,
+            # weights), so no handle outlives it
+            for group in _live[:3]:
+                for o in list(group):
+                    if _owner(o) is self:
+                        o.close()
             lib().unltd_ctx_destroy(self.h)
             self.h = None
 
@@ -238,9 +257,9 @@ class Weight:
         return dt.value, di.value, do.value, nb.value
 
     def free(self):
-        if getattr(self, "h", None):
+        if _alive(self):
             lib().unltd_weight_free(self.h)
-            self.h = None
+        self.h = None
 
     close = free
 
@@ -347,9 +366,12 @@ class Qwen35Model:
         return Qwen35Session(self, h, ctx_len)
 
     def close(self):
-        if getattr(self, "h", None):
+        if _alive(self):
+            for o in list(_live[0]):  # its sessions first
+                if getattr(o, "model", None) is self:
+                    o.close()
             lib().unltd_qwen35_destroy(self.h)
-            self.h = None
+        self.h = None
 
     def __del__(self, _finalizing=sys.is_finalizing):
         if _finalizing():
@@ -427,9 +449,9 @@ class Qwen35Session:
         return lg, hd
 
     def close(self):
-        if getattr(self, "h", None):
+        if _alive(self) and getattr(self.model, "h", None):
             lib().unltd_qwen35_session_destroy(self.h)
-            self.h = None
+        self.h = None
 
     def __del__(self, _finalizing=sys.is_finalizing):
         if _finalizing():
