@@ -149,6 +149,70 @@ def q6k_block_sumi_model(blk: np.ndarray, q8: np.ndarray):
     return tot >> 2
 
 
+def q6_q8k_byte(j, hh, w, ab, bpos):
+    return 128 * (2 * hh + (w >> 1)) + 16 * j + 4 * (2 * (w & 1) + ab) + bpos
+
+
+def q6k_q8k_image(q8: np.ndarray) -> np.ndarray:
+    """The 512 masked-word bytes of the Q6_K Q8_K x image (q8k_span_write)."""
+    im = np.zeros(512, np.int64)
+    for e in range(256):
+        h, pos = e >> 7, e & 127
+        hh, c = pos >> 6, pos & 63
+        u, ipos = c >> 4, c & 15
+        j = 4 * h + u
+        pic = int(q6_pic(ipos))
+        w, bpos = pic >> 2, pic & 3
+        own = 0 if bpos < 2 else 1
+        im[q6_q8k_byte(j, hh, w, own, bpos)] = int(q8[e])
+        im[q6_q8k_byte(j, hh, w, 1 - own, bpos)] = 0
+    return im
+
+
+def q6k_rows_mma_model(blks: list, q8: np.ndarray) -> np.ndarray:
+    """sumi[row][class] of one block for 16 rows, through the fragments of
+    q6k_q8k_mma_item: per (chunk j, half hh) an m16n8k16 MMA with A[r][4t+i]
+    = byte i of 4 (raw6 - 32) built from word t of row r's ql/qh chunk, and
+    B[4t+i][n] = byte i of lane (gid n, tig t)'s XBlock6 word b[2j+hh]; then
+    the per-row int8 scales and the final division by 4."""
+    assert len(blks) == 16
+    im = q6k_q8k_image(q8)
+    rows = [repack_q6k_block(b) for b in blks]
+    # XBlock6 of every lane (gid, tig)
+    breg = np.zeros((8, 4, 16, 4), np.int64)  # [gid, tig, 2j+hh, byte]
+    for gid in range(8):
+        for tig in range(4):
+            own, ab = (gid >> 1) == tig, gid & 1
+            for j in range(8):
+                for hh in range(2):
+                    if own:
+                        o = q6_q8k_byte(j, hh, tig, ab, 0)
+                        breg[gid, tig, 2 * j + hh] = im[o:o + 4]
+    acc = np.zeros((16, 8), np.int64)
+    for j in range(8):
+        h, u = j >> 2, j & 3
+        sl, c = 2 * (u >> 1), 2 * h + (u & 1)
+        for hh in range(2):
+            s_idx = 8 * h + u + 4 * hh
+            A = np.zeros((16, 16), np.int64)
+            for r, (ql, qh, sc, _) in enumerate(rows):
+                for t in range(4):
+                    wl = ql[16 * j + 4 * t: 16 * j + 4 * t + 4].astype(np.int64)
+                    wh = qh[16 * c + 4 * t: 16 * c + 4 * t + 4].astype(np.int64)
+                    nib = (wl & 0xF) if hh == 0 else (wl >> 4)
+                    hi2 = (wh >> (sl + 4 * hh)) & 3
+                    A[r, 4 * t: 4 * t + 4] = 4 * ((nib | (hi2 << 4)) - 32)
+            B = np.zeros((16, 8), np.int64)
+            for n in range(8):
+                for t in range(4):
+                    B[4 * t: 4 * t + 4, n] = breg[n, t, 2 * j + hh]
+            D = A @ B
+            for r, (ql, qh, sc, _) in enumerate(rows):
+                acc[r] += sc[s_idx] * D[r]
+    assert np.all(acc % 4 == 0) and np.all(np.abs(acc) < 2**31)
+    return acc >> 2
+
+
 def q6k_block_sumi_reference(blk: np.ndarray, q8: np.ndarray):
     ql, qh = blk[:128].astype(np.int64), blk[128:192].astype(np.int64)
     sc = blk[192:208].view(np.int8).astype(np.int64)

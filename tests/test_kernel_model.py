@@ -80,3 +80,17 @@ def test_q4k_f32x_model_within_tolerance(ora, seed):
     deq = ora.dequantize_q4_k(blk, 256).astype(np.float64)
     scale = float(np.abs(deq * x).sum())
     assert abs(got - exact) <= 1e-6 * scale
+
+
+@pytest.mark.parametrize("seed", [0, 1, 2])
+def test_q6k_mma_fragments_match_reference(seed):
+    # the tensor-core Q6_K item's fragment mapping gives the reference's
+    # per-class integer sums for 16 rows of random blocks
+    import synth
+    rng = np.random.default_rng(seed)
+    wb = synth.quant_weights(6, 256, 16, seed=100 + seed)
+    blks = [wb[r * 210:(r + 1) * 210] for r in range(16)]
+    q8 = rng.integers(-127, 128, size=256).astype(np.int64)
+    got = km.q6k_rows_mma_model(blks, q8)
+    for r in range(16):
+        assert np.array_equal(got[r], km.q6k_block_sumi_reference(blks[r], q8))

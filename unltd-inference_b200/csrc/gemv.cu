@@ -32,6 +32,7 @@
 #include <cstdio>
 #include <mutex>
 #include <utility>
+#include <type_traits>
 #include <vector>
 
 #include "q8k_span.cuh"
@@ -295,6 +296,115 @@ __device__ __forceinline__ void q4k_q8k_mma_item(const uint8_t *tile, int nr, in
   }
 }
 
+// Q6_K: a word of 4*(raw6 - 32) as s8 from ql/qh words (2-bit field of qh at
+// shift sl for the low-nibble half, sl + 4 for the high half).
+__device__ __forceinline__ uint32_t q6_a4_lo(uint32_t ql, uint32_t qh, int sl) {
+  return (((ql << 2) & 0x3C3C3C3Cu) | ((qh << (6 - sl)) & 0xC0C0C0C0u)) ^ 0x80808080u;
+}
+__device__ __forceinline__ uint32_t q6_a4_hi(uint32_t ql, uint32_t qh, int sl) {
+  return (((ql >> 2) & 0x3C3C3C3Cu) | ((qh << (2 - sl)) & 0xC0C0C0C0u)) ^ 0x80808080u;
+}
+
+// D = A(16x16 s8, row) * B(16x8 s8, col), exact int32 (tensor cores)
+__device__ __forceinline__ void mma_s8_k16(uint32_t a0, uint32_t a1, uint32_t b0, int &d0, int &d1, int &d2, int &d3) {
+  asm("mma.sync.aligned.m16n8k16.row.col.s32.s8.s8.s32 {%0,%1,%2,%3}, {%4,%5}, {%6}, {%7,%7,%7,%7};"
+      : "=r"(d0), "=r"(d1), "=r"(d2), "=r"(d3)
+      : "r"(a0), "r"(a1), "r"(b0), "r"(0));
+}
+
+// signed byte k (0..3) of w: prmt with the sign-replicate selector bit (the
+// __byte_perm intrinsic ignores that bit)
+__device__ __forceinline__ int sbyte_of(uint32_t w, int k) {
+  int r;
+  asm("prmt.b32 %0, %1, 0, %2;" : "=r"(r) : "r"(w), "r"(0x8880u | (0x1111u * (uint32_t)k)));
+  return r;
+}
+
+// One block of the Q6_K Q8_K x image as MMA B operands of this lane: for
+// ql chunk j and half hh (the 16-element sub-blocks 8h + u and 8h + 4 + u,
+// j = 4h + u), the k-quad tig of the chunk's words holds run positions
+// (2 tig, 2 tig + 8, 2 tig + 1, 2 tig + 9), i.e. classes 2 tig (bytes 0, 1)
+// and 2 tig + 1 (bytes 2, 3); column gid of B keeps only its class: the
+// image's masked copy A when gid = 2 tig, copy B when gid = 2 tig + 1.
+struct XBlock6 {
+  uint32_t b[16];  // [2 j + hh]
+  float xd;
+};
+
+__device__ __forceinline__ void load_xblock6(const uint8_t *im, XBlock6 &x) {
+  const int lane = threadIdx.x & 31, gid = lane >> 2, tig = lane & 3;
+  const bool own = (gid >> 1) == tig;
+  const int ab = gid & 1;
+#pragma unroll
+  for (int j = 0; j < 8; j++)
+#pragma unroll
+    for (int hh = 0; hh < 2; hh++)
+      x.b[2 * j + hh] =
+          own ? *reinterpret_cast<const uint32_t *>(im + q6_q8k_byte(j, hh, tig, ab, 0)) : 0u;
+  x.xd = *reinterpret_cast<const float *>(im + kImgQ8K6_D);
+}
+
+// Q8K, Q6_K on the tensor cores: one warp takes 16 rows x one block. Per
+// sub-block (16 elements, one int8 scale) an int8 MMA m16n8k16 multiplies the
+// 16 rows' quads (A: thread (r, t) holds word t of the row's ql/qh chunk as
+// 4 (raw6 - 32) in s8) by the class-masked q8 values (XBlock6), giving every
+// (row, class) partial of the sub-block; the per-row scales are applied in
+// int32 and the 4x removed at the end (exact: every term is a multiple of 4
+// and |sum| < 2^31). No min term (quants.rs:371-412).
+__device__ __forceinline__ void q6k_q8k_mma_item(const uint8_t *tile, int nr, int g16, int b, const XBlock6 &x,
+                                                 const Params &P, float *tk) {
+  const int lane = threadIdx.x & 31, gid = lane >> 2, tig = lane & 3;
+  const int lr0 = g16 * 16 + gid, lr1 = lr0 + 8;
+  const bool v0 = lr0 < nr, v1 = lr1 < nr;
+  const uint8_t *row0 = tile + (v0 ? lr0 : 0) * P.pstride;
+  const uint8_t *row1 = tile + (v1 ? lr1 : 0) * P.pstride;
+  const int nb = P.nb;
+  const int qlo = b * 128 + 4 * tig, qho = nb * 128 + b * 64 + 4 * tig;
+  uint32_t l0[8], l1[8], h0[4], h1[4];
+#pragma unroll
+  for (int j = 0; j < 8; j++) {
+    l0[j] = *reinterpret_cast<const uint32_t *>(row0 + qlo + 16 * j);
+    l1[j] = *reinterpret_cast<const uint32_t *>(row1 + qlo + 16 * j);
+  }
+#pragma unroll
+  for (int c = 0; c < 4; c++) {
+    h0[c] = *reinterpret_cast<const uint32_t *>(row0 + qho + 16 * c);
+    h1[c] = *reinterpret_cast<const uint32_t *>(row1 + qho + 16 * c);
+  }
+  const uint4 sc0 = lds128(row0 + nb * 192 + b * 16), sc1 = lds128(row1 + nb * 192 + b * 16);
+  const uint32_t S0[4] = {sc0.x, sc0.y, sc0.z, sc0.w}, S1[4] = {sc1.x, sc1.y, sc1.z, sc1.w};
+  const uint32_t db0 = *reinterpret_cast<const unsigned short *>(row0 + nb * 208 + b * 2);
+  const uint32_t db1 = *reinterpret_cast<const unsigned short *>(row1 + nb * 208 + b * 2);
+  int acc0 = 0, acc1 = 0, acc2 = 0, acc3 = 0;
+#pragma unroll
+  for (int j = 0; j < 8; j++) {
+    const int h = j >> 2, u = j & 3, sl = 2 * (u >> 1), c = 2 * h + (u & 1);
+    const int slo = 8 * h + u, shi = slo + 4;  // the chunk's two sub-blocks
+    int d0, d1, d2, d3, e0, e1, e2, e3;
+    mma_s8_k16(q6_a4_lo(l0[j], h0[c], sl), q6_a4_lo(l1[j], h1[c], sl), x.b[2 * j], d0, d1, d2, d3);
+    mma_s8_k16(q6_a4_hi(l0[j], h0[c], sl), q6_a4_hi(l1[j], h1[c], sl), x.b[2 * j + 1], e0, e1, e2, e3);
+    const int s0 = sbyte_of(S0[slo >> 2], slo & 3), s1 = sbyte_of(S1[slo >> 2], slo & 3);
+    const int t0 = sbyte_of(S0[shi >> 2], shi & 3), t1 = sbyte_of(S1[shi >> 2], shi & 3);
+    acc0 += s0 * d0 + t0 * e0;
+    acc1 += s0 * d1 + t0 * e1;
+    acc2 += s1 * d2 + t1 * e2;
+    acc3 += s1 * d3 + t1 * e3;
+  }
+  if (v0) {
+    const float d = __fmul_rn(x.xd, h2f_bits(db0));
+    float *t = tk + lr0 * P.rs + 8 * b + 2 * tig;
+    t[0] = __fmul_rn(d, (float)(acc0 >> 2));
+    t[1] = __fmul_rn(d, (float)(acc1 >> 2));
+  }
+  if (v1) {
+    const float d = __fmul_rn(x.xd, h2f_bits(db1));
+    float *t = tk + lr1 * P.rs + 8 * b + 2 * tig;
+    t[0] = __fmul_rn(d, (float)(acc2 >> 2));
+    t[1] = __fmul_rn(d, (float)(acc3 >> 2));
+  }
+}
+
+
 __device__ __forceinline__ unsigned long long argmax_key(float v, int row) {
   if (isnan(v)) return row == 0 ? ~0ull : 0ull;
   return ((unsigned long long)orderable(v) << 32) | (0xffffffffu - (uint32_t)row);
@@ -317,15 +427,6 @@ __device__ __forceinline__ void q4_scales(const uint4 &hq, int p, int &sc_lo, in
   sc_hi = (SC >> (sh + 8)) & 0xFF;
   m_lo = (MM >> sh) & 0xFF;
   m_hi = (MM >> (sh + 8)) & 0xFF;
-}
-
-// Q6_K: a word of 4*(raw6 - 32) as s8 from ql/qh words (2-bit field of qh at
-// shift sl for the low-nibble half, sl + 4 for the high half).
-__device__ __forceinline__ uint32_t q6_a4_lo(uint32_t ql, uint32_t qh, int sl) {
-  return (((ql << 2) & 0x3C3C3C3Cu) | ((qh << (6 - sl)) & 0xC0C0C0C0u)) ^ 0x80808080u;
-}
-__device__ __forceinline__ uint32_t q6_a4_hi(uint32_t ql, uint32_t qh, int sl) {
-  return (((ql >> 2) & 0x3C3C3C3Cu) | ((qh << (2 - sl)) & 0xC0C0C0C0u)) ^ 0x80808080u;
 }
 
 __device__ __forceinline__ float sub_sum(float v, unsigned m) {
@@ -843,8 +944,9 @@ __device__ __forceinline__ void tc_norm_prologue(const Params &P, uint8_t *ximg)
   }
 }
 
-template <bool ARGMAX>
+template <int FMT, bool ARGMAX>
 __global__ void __launch_bounds__(kTcThreads, 1) gemv_tc_kernel(Params P) {
+  constexpr int kImg = FMT == Q4K ? kImgQ8K4 : kImgQ8K6;
   extern __shared__ __align__(128) uint8_t smem[];
   uint64_t *full = reinterpret_cast<uint64_t *>(smem);
   uint64_t *empty = full + kMaxStages;
@@ -900,7 +1002,7 @@ __global__ void __launch_bounds__(kTcThreads, 1) gemv_tc_kernel(Params P) {
   pdl_wait();
   if (warp < kTcIntWarps) {
     // ---------------- integer warps -------------------------------------------
-    if (P.nn) {
+    if (FMT == Q4K && P.nn) {
       tc_norm_prologue(P, ximg);
     } else {
       const uint4 *src = reinterpret_cast<const uint4 *>(P.img);
@@ -913,8 +1015,17 @@ __global__ void __launch_bounds__(kTcThreads, 1) gemv_tc_kernel(Params P) {
     // registers for the whole kernel
     const bool fixed = kTcIntWarps % P.nbu == 0;
     const int myb = warp % P.nbu, rg0 = warp / P.nbu, rgs = kTcIntWarps / P.nbu;
-    XBlock xb;
-    if (fixed) load_xblock(ximg + (size_t)myb * kImgQ8K4, xb);
+    using XB = std::conditional_t<FMT == Q4K, XBlock, XBlock6>;
+    XB xb;
+    auto load_xb = [&](int b, XB &x) {
+      if constexpr (FMT == Q4K) load_xblock(ximg + (size_t)b * kImg, x);
+      else load_xblock6(ximg + (size_t)b * kImg, x);
+    };
+    auto item = [&](const uint8_t *tile, int nr, int g16, int b, const XB &x, float *cb, float *cm) {
+      if constexpr (FMT == Q4K) q4k_q8k_mma_item(tile, nr, g16, b, x, P, cb, cm);
+      else q6k_q8k_mma_item(tile, nr, g16, b, x, P, cb);
+    };
+    if (fixed) load_xb(myb, xb);
     for (int i = 0; i < ntiles; i++) {
       const int st = i % P.S;
       const int r0 = rb + i * P.T;
@@ -926,13 +1037,13 @@ __global__ void __launch_bounds__(kTcThreads, 1) gemv_tc_kernel(Params P) {
       float *cm = cb + P.T * P.rs;
       const int ng = (nr + 15) / 16;
       if (fixed) {
-        for (int g16 = rg0; g16 < ng; g16 += rgs) q4k_q8k_mma_item(tile, nr, g16, myb, xb, P, cb, cm);
+        for (int g16 = rg0; g16 < ng; g16 += rgs) item(tile, nr, g16, myb, xb, cb, cm);
       } else {
         for (int it = warp; it < ng * P.nbu; it += kTcIntWarps) {
           const int g16 = it / P.nbu, b = it - g16 * P.nbu;
-          XBlock xv;
-          load_xblock(ximg + (size_t)b * kImgQ8K4, xv);
-          q4k_q8k_mma_item(tile, nr, g16, b, xv, P, cb, cm);
+          XB xv;
+          load_xb(b, xv);
+          item(tile, nr, g16, b, xv, cb, cm);
         }
       }
       __syncwarp();
@@ -964,13 +1075,13 @@ __global__ void __launch_bounds__(kTcThreads, 1) gemv_tc_kernel(Params P) {
         for (int q = 0; q < 8; q++) {
           const bool in = b + q < P.nbu;
           a[q] = in ? tk[8 * (b + q)] : 0.0f;
-          mm[q] = in ? tm[b + q] : 0.0f;
+          mm[q] = (FMT == Q4K && in) ? tm[b + q] : 0.0f;
         }
 #pragma unroll
         for (int q = 0; q < 8; q++) {
           if (b + q < P.nbu) {
             sums = __fadd_rn(sums, a[q]);
-            sumf = __fsub_rn(sumf, mm[q]);
+            if (FMT == Q4K) sumf = __fsub_rn(sumf, mm[q]);  // Q6_K: no min term, s starts at 0
           }
         }
       }
@@ -1066,7 +1177,7 @@ GemvFn pick_r(int R) {
 
 template <bool AM>
 GemvFn pick(int fmt, int mode, int R, bool mma = false) {
-  if (mma) return gemv_tc_kernel<AM>;
+  if (mma) return fmt == Q4K ? gemv_tc_kernel<Q4K, AM> : gemv_tc_kernel<Q6K, AM>;
   if (mode == MODE_F32X) {
     if (fmt == Q4K) return pick_r<Q4K, MODE_F32X, AM>(R);
     if (fmt == Q6K) return pick_r<Q6K, MODE_F32X, AM>(R);
@@ -1112,7 +1223,7 @@ void gemv_prewarm(int device) {
       for (int r = 1; r <= 2; r++) {
         ensure_smem_attr(pick<false>(fmt, mode, r), m);
         ensure_smem_attr(pick<true>(fmt, mode, r), m);
-        if (fmt == Q4K && mode == MODE_Q8K) {
+        if (fmt != Q8_0 && mode == MODE_Q8K) {
           ensure_smem_attr(pick<false>(fmt, mode, r, true), m);
           ensure_smem_attr(pick<true>(fmt, mode, r, true), m);
         }
@@ -1161,10 +1272,12 @@ Plan plan_gemv(unltd_ctx ctx, const unltd_weight_s &w, int mode) {
   int R = 1, T = 0, S = 0, stage_bytes = 0, cbuf = 0, pstride = stride, mma = 0;
   double best_score = -1.0;
   const int nsub = kConsumerWarps * 4;
-  // Q4_K Q8K: tensor-core tiles of 16 rows; rows padded in shared memory to a
-  // stride of 32 (mod 128) bytes so eight rows' loads hit distinct banks
-  if (fmt == Q4K && mode == MODE_Q8K) {
-    const int ps = (int)round_up((size_t)stride, 128) + 32;
+  // Q4_K / Q6_K Q8K: tensor-core tiles of 16 rows; rows padded in shared
+  // memory so the eight rows of an MMA fragment load from distinct banks (a
+  // stride of 32 mod 128 bytes for the 8-byte Q4_K loads, 16 for the 4-byte
+  // Q6_K loads)
+  if ((fmt == Q4K || fmt == Q6K) && mode == MODE_Q8K) {
+    const int ps = (int)round_up((size_t)stride, 128) + (fmt == Q4K ? 32 : 16);
     // 32-row tiles (two MMA row groups per block item) measured faster than
     // 16-row tiles with deeper rings
     for (int t = 16; t <= 32; t += 16) {
