@@ -62,7 +62,9 @@ def _abs_mag(wb, dtype, dim_in, dim_out, x):
     return np.abs(deq) @ np.abs(x.astype(np.float64))
 
 
-SHAPES_K = [(256, 1), (512, 3), (1024, 37), (4096, 256), (4096, 4096), (12288, 64), (768, 9000)]
+# (6144, 77): K-chunks of 8 blocks; (8192, 300) and (12288, 64): chunks of 16
+SHAPES_K = [(256, 1), (512, 3), (1024, 37), (4096, 256), (4096, 4096), (6144, 77), (8192, 300), (12288, 64),
+            (768, 9000)]
 
 
 @pytest.mark.parametrize("dtype", [ug.Q4K, ug.Q6K])
