@@ -351,11 +351,13 @@ __device__ __forceinline__ void load_xblock6(const uint8_t *im, XBlock6 &x) {
 // (row, class) partial of the sub-block; the per-row scales are applied in
 // int32 and the 4x removed at the end (exact: every term is a multiple of 4
 // and |sum| < 2^31). No min term (quants.rs:371-412).
+template <bool R8>
 __device__ __forceinline__ void q6k_q8k_mma_item(const uint8_t *tile, int nr, int g16, int b, const XBlock6 &x,
                                                  const Params &P, float *tk) {
+  // R8: 8-row tiles; rows 8..15 of the MMA fragments stay zero and are not built
   const int lane = threadIdx.x & 31, gid = lane >> 2, tig = lane & 3;
-  const int lr0 = g16 * 16 + gid, lr1 = lr0 + 8;
-  const bool v0 = lr0 < nr, v1 = lr1 < nr;
+  const int lr0 = (R8 ? 8 : 16) * g16 + gid, lr1 = lr0 + 8;
+  const bool v0 = lr0 < nr, v1 = !R8 && lr1 < nr;
   const uint8_t *row0 = tile + (v0 ? lr0 : 0) * P.pstride;
   const uint8_t *row1 = tile + (v1 ? lr1 : 0) * P.pstride;
   const int nb = P.nb;
@@ -364,31 +366,34 @@ __device__ __forceinline__ void q6k_q8k_mma_item(const uint8_t *tile, int nr, in
 #pragma unroll
   for (int j = 0; j < 8; j++) {
     l0[j] = *reinterpret_cast<const uint32_t *>(row0 + qlo + 16 * j);
-    l1[j] = *reinterpret_cast<const uint32_t *>(row1 + qlo + 16 * j);
+    l1[j] = R8 ? 0u : *reinterpret_cast<const uint32_t *>(row1 + qlo + 16 * j);
   }
 #pragma unroll
   for (int c = 0; c < 4; c++) {
     h0[c] = *reinterpret_cast<const uint32_t *>(row0 + qho + 16 * c);
-    h1[c] = *reinterpret_cast<const uint32_t *>(row1 + qho + 16 * c);
+    h1[c] = R8 ? 0u : *reinterpret_cast<const uint32_t *>(row1 + qho + 16 * c);
   }
-  const uint4 sc0 = lds128(row0 + nb * 192 + b * 16), sc1 = lds128(row1 + nb * 192 + b * 16);
+  const uint4 sc0 = lds128(row0 + nb * 192 + b * 16);
+  const uint4 sc1 = R8 ? make_uint4(0u, 0u, 0u, 0u) : lds128(row1 + nb * 192 + b * 16);
   const uint32_t S0[4] = {sc0.x, sc0.y, sc0.z, sc0.w}, S1[4] = {sc1.x, sc1.y, sc1.z, sc1.w};
   const uint32_t db0 = *reinterpret_cast<const unsigned short *>(row0 + nb * 208 + b * 2);
-  const uint32_t db1 = *reinterpret_cast<const unsigned short *>(row1 + nb * 208 + b * 2);
+  const uint32_t db1 = R8 ? 0u : *reinterpret_cast<const unsigned short *>(row1 + nb * 208 + b * 2);
   int acc0 = 0, acc1 = 0, acc2 = 0, acc3 = 0;
 #pragma unroll
   for (int j = 0; j < 8; j++) {
     const int h = j >> 2, u = j & 3, sl = 2 * (u >> 1), c = 2 * h + (u & 1);
     const int slo = 8 * h + u, shi = slo + 4;  // the chunk's two sub-blocks
     int d0, d1, d2, d3, e0, e1, e2, e3;
-    mma_s8_k16(q6_a4_lo(l0[j], h0[c], sl), q6_a4_lo(l1[j], h1[c], sl), x.b[2 * j], d0, d1, d2, d3);
-    mma_s8_k16(q6_a4_hi(l0[j], h0[c], sl), q6_a4_hi(l1[j], h1[c], sl), x.b[2 * j + 1], e0, e1, e2, e3);
-    const int s0 = sbyte_of(S0[slo >> 2], slo & 3), s1 = sbyte_of(S1[slo >> 2], slo & 3);
-    const int t0 = sbyte_of(S0[shi >> 2], shi & 3), t1 = sbyte_of(S1[shi >> 2], shi & 3);
+    mma_s8_k16(q6_a4_lo(l0[j], h0[c], sl), R8 ? 0u : q6_a4_lo(l1[j], h1[c], sl), x.b[2 * j], d0, d1, d2, d3);
+    mma_s8_k16(q6_a4_hi(l0[j], h0[c], sl), R8 ? 0u : q6_a4_hi(l1[j], h1[c], sl), x.b[2 * j + 1], e0, e1, e2, e3);
+    const int s0 = sbyte_of(S0[slo >> 2], slo & 3), t0 = sbyte_of(S0[shi >> 2], shi & 3);
     acc0 += s0 * d0 + t0 * e0;
     acc1 += s0 * d1 + t0 * e1;
-    acc2 += s1 * d2 + t1 * e2;
-    acc3 += s1 * d3 + t1 * e3;
+    if (!R8) {
+      const int s1 = sbyte_of(S1[slo >> 2], slo & 3), t1 = sbyte_of(S1[shi >> 2], shi & 3);
+      acc2 += s1 * d2 + t1 * e2;
+      acc3 += s1 * d3 + t1 * e3;
+    }
   }
   if (v0) {
     const float d = __fmul_rn(x.xd, h2f_bits(db0));
@@ -944,7 +949,7 @@ __device__ __forceinline__ void tc_norm_prologue(const Params &P, uint8_t *ximg)
   }
 }
 
-template <int FMT, bool ARGMAX>
+template <int FMT, bool ARGMAX, bool R8 = false>
 __global__ void __launch_bounds__(kTcThreads, 1) gemv_tc_kernel(Params P) {
   constexpr int kImg = FMT == Q4K ? kImgQ8K4 : kImgQ8K6;
   extern __shared__ __align__(128) uint8_t smem[];
@@ -1023,7 +1028,7 @@ __global__ void __launch_bounds__(kTcThreads, 1) gemv_tc_kernel(Params P) {
     };
     auto item = [&](const uint8_t *tile, int nr, int g16, int b, const XB &x, float *cb, float *cm) {
       if constexpr (FMT == Q4K) q4k_q8k_mma_item(tile, nr, g16, b, x, P, cb, cm);
-      else q6k_q8k_mma_item(tile, nr, g16, b, x, P, cb);
+      else q6k_q8k_mma_item<R8>(tile, nr, g16, b, x, P, cb);
     };
     if (fixed) load_xb(myb, xb);
     for (int i = 0; i < ntiles; i++) {
@@ -1035,7 +1040,7 @@ __global__ void __launch_bounds__(kTcThreads, 1) gemv_tc_kernel(Params P) {
       const uint8_t *tile = stages + (size_t)st * P.stage_bytes;
       float *cb = reinterpret_cast<float *>(reinterpret_cast<uint8_t *>(cbuf0) + (i & 1) * P.cbuf_bytes);
       float *cm = cb + P.T * P.rs;
-      const int ng = (nr + 15) / 16;
+      const int ng = R8 ? (nr + 7) / 8 : (nr + 15) / 16;  // row groups of the item
       if (fixed) {
         for (int g16 = rg0; g16 < ng; g16 += rgs) item(tile, nr, g16, myb, xb, cb, cm);
       } else {
@@ -1176,7 +1181,8 @@ GemvFn pick_r(int R) {
 }
 
 template <bool AM>
-GemvFn pick(int fmt, int mode, int R, bool mma = false) {
+GemvFn pick(int fmt, int mode, int R, int mma = 0) {
+  if (mma == 2) return gemv_tc_kernel<Q6K, AM, true>;  // 8-row tiles (Q6_K only)
   if (mma) return fmt == Q4K ? gemv_tc_kernel<Q4K, AM> : gemv_tc_kernel<Q6K, AM>;
   if (mode == MODE_F32X) {
     if (fmt == Q4K) return pick_r<Q4K, MODE_F32X, AM>(R);
@@ -1224,8 +1230,12 @@ void gemv_prewarm(int device) {
         ensure_smem_attr(pick<false>(fmt, mode, r), m);
         ensure_smem_attr(pick<true>(fmt, mode, r), m);
         if (fmt != Q8_0 && mode == MODE_Q8K) {
-          ensure_smem_attr(pick<false>(fmt, mode, r, true), m);
-          ensure_smem_attr(pick<true>(fmt, mode, r, true), m);
+          ensure_smem_attr(pick<false>(fmt, mode, r, 1), m);
+          ensure_smem_attr(pick<true>(fmt, mode, r, 1), m);
+          if (fmt == Q6K) {
+            ensure_smem_attr(pick<false>(fmt, mode, r, 2), m);
+            ensure_smem_attr(pick<true>(fmt, mode, r, 2), m);
+          }
         }
       }
     }
@@ -1279,15 +1289,17 @@ Plan plan_gemv(unltd_ctx ctx, const unltd_weight_s &w, int mode) {
   if ((fmt == Q4K || fmt == Q6K) && mode == MODE_Q8K) {
     const int ps = (int)round_up((size_t)stride, 128) + (fmt == Q4K ? 32 : 16);
     // 32-row tiles (two MMA row groups per block item) measured faster than
-    // 16-row tiles with deeper rings
-    for (int t = 16; t <= 32; t += 16) {
+    // 16-row tiles with deeper rings; Q6_K rows too long for two 16-row
+    // stages take 8-row tiles (half-height MMA items)
+    for (int t = fmt == Q6K ? 8 : 16; t <= 32; t *= 2) {
       const int sb = (int)round_up((size_t)t * ps, 128);
       const int cb = cbuf_for(t);
       const int fixed = kTcBarBytes + img_bytes + 2 * cb;
       const int s = std::min(kMaxStages, (smem_max - fixed) / sb);
       if (s < 2) continue;
-      const int items = (t / 16) * nbu;
-      const double score = (items % kTcIntWarps == 0 ? 2.0 : 0.0) + (items >= kTcIntWarps ? 1.0 : 0.0) + t / 16.0;
+      const int items = (t < 16 ? 1 : t / 16) * nbu;
+      const double score = (items % kTcIntWarps == 0 ? 2.0 : 0.0) + (items >= kTcIntWarps ? 1.0 : 0.0) + t / 16.0 -
+                           (t < 16 ? 4.0 : 0.0);
       if (score > best_score) {
         best_score = score;
         T = t;
@@ -1296,7 +1308,7 @@ Plan plan_gemv(unltd_ctx ctx, const unltd_weight_s &w, int mode) {
         stage_bytes = sb;
         cbuf = cb;
         pstride = ps;
-        mma = 1;
+        mma = t < 16 ? 2 : 1;
       }
     }
   }
