@@ -228,6 +228,7 @@ def decode_bench(n_tokens, with_cpu, rank=0, world=1, dist=None, profile_region=
     ctx = ug.Context(torch.cuda.current_device())
     if world > 1:
         ctx.comm_init(rank, world, ug.exchange_unique_id())
+        ctx.peer_init()  # the step's all-reduces as one NVLink peer kernel each
     m = ug.Qwen35Model(ctx, cfg, rank, world)
     m.load(tensors)
     s = m.session(pos0 + n_tokens + 16)

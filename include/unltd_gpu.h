@@ -163,6 +163,15 @@ int32_t unltd_gemv_noalloc(unltd_weight w, const float *x_dev, float *y_dev, int
  * torch.distributed broadcast), every rank calls unltd_comm_init. */
 int32_t unltd_comm_unique_id(void *id_out, size_t id_bytes);
 int32_t unltd_comm_init(unltd_ctx ctx, int32_t rank, int32_t world, const void *id, size_t id_bytes);
+/* Optional NVLink peer all-reduce (after unltd_comm_init): every rank calls
+ * unltd_peer_export (64-byte CUDA IPC handle of its receive area), the
+ * caller gathers the handles in rank order (e.g. torch.distributed
+ * all_gather_object), every rank calls unltd_peer_import with all of them.
+ * From then on the all-reduces below of up to 16384 elements run as one
+ * kernel that exchanges the data over peer memory and sums in rank order
+ * (identical bits on every rank); larger ones use NCCL. */
+int32_t unltd_peer_export(unltd_ctx ctx, void *handle_out, size_t handle_bytes);
+int32_t unltd_peer_import(unltd_ctx ctx, const void *handles, size_t handle_bytes);
 /* In-place all-reduces on the context's stream. */
 int32_t unltd_allreduce_sum_f32(unltd_ctx ctx, float *buf_dev, size_t count);
 int32_t unltd_allreduce_max_u64(unltd_ctx ctx, uint64_t *buf_dev, size_t count);

@@ -1,7 +1,8 @@
 """Tensor-parallel decode on 2 GPUs (tests/tp_decode_check.py under torchrun)
 against the CPU oracle: identical greedy stream, logits and hidden state
 within 1e-3 max-rel (the row-split projections sum partial outputs across
-GPUs, so the f32 rounding differs from the single-device reference)."""
+GPUs, so the f32 rounding differs from the single-device reference). Both
+all-reduce paths: the NVLink peer kernel and NCCL."""
 import json
 import os
 import socket
@@ -24,7 +25,8 @@ def _port():
     return p
 
 
-def test_tp2_tiny_decode_matches_oracle():
+@pytest.mark.parametrize("allreduce", ["peer", "nccl"])
+def test_tp2_tiny_decode_matches_oracle(allreduce):
     if not torch.cuda.is_available() or torch.cuda.device_count() < 2:
         pytest.skip("needs 2 GPUs")
     from __graft_entry__ import build
@@ -33,7 +35,7 @@ def test_tp2_tiny_decode_matches_oracle():
     env = dict(os.environ, NCCL_NVLS_ENABLE="0")
     cmd = ["timeout", "-k", "30", "600", sys.executable, "-m", "torch.distributed.run", "--nnodes=1",
            "--nproc-per-node", "2", "--master-addr", "127.0.0.1", "--master-port", str(_port()),
-           os.path.join(HERE, "tp_decode_check.py"), "--model", "tiny", "--steps", "8"]
+           os.path.join(HERE, "tp_decode_check.py"), "--model", "tiny", "--steps", "8", "--allreduce", allreduce]
     r = subprocess.run(cmd, capture_output=True, text=True, env=env)
     assert r.returncode == 0, r.stderr[-3000:]
     line = [l for l in r.stdout.splitlines() if l.startswith("{")][-1]

@@ -36,6 +36,8 @@ def main():
     ap.add_argument("--steps", type=int, default=8)
     ap.add_argument("--position", type=int, default=40)
     ap.add_argument("--no-oracle", action="store_true")
+    ap.add_argument("--allreduce", default="peer", choices=["peer", "nccl"],
+                    help="peer: one kernel over NVLink peer memory; nccl: ncclAllReduce")
     args = ap.parse_args()
     rank, world, local = int(os.environ["RANK"]), int(os.environ["WORLD_SIZE"]), int(os.environ["LOCAL_RANK"])
     torch.cuda.set_device(local)
@@ -47,6 +49,8 @@ def main():
     st = synth.qwen35_state(cfg, pos0, seed + 1)
     ctx = ug.Context(local)
     ctx.comm_init(rank, world, ug.exchange_unique_id())
+    if args.allreduce == "peer":
+        ctx.peer_init()
     m = ug.Qwen35Model(ctx, cfg, rank, world)
     m.load(tensors)
     s = m.session(pos0 + n + 10)
@@ -64,7 +68,8 @@ def main():
     dist.all_gather_object(parts, (v0, v1, lg))
     streams = [None] * world
     dist.all_gather_object(streams, toks.tolist())
-    out = {"model": args.model, "world": world, "steps": n, "position": pos0, "tokens": toks.tolist(),
+    out = {"model": args.model, "world": world, "allreduce": args.allreduce, "steps": n, "position": pos0,
+           "tokens": toks.tolist(),
            "same_stream_on_all_ranks": all(x == streams[0] for x in streams),
            "tok_s": round(n / dt, 2), "ms_per_token": round(dt / n * 1e3, 4)}
     if rank == 0:

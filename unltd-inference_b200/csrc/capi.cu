@@ -77,6 +77,7 @@ int32_t check_device_error(unltd_ctx c, const char *who) {
   if (v == 0) return UNLTD_OK;
   cudaMemset(c->err, 0, sizeof(int));
   if (v == 2) return set_error(UNLTD_ERR_INVALID_ARG, std::string(who) + ": a token id outside the vocabulary reached the embedding");
+  if (v == 3) return set_error(UNLTD_ERR_TIMEOUT, std::string(who) + ": a peer all-reduce gave up waiting for another rank");
   return set_error(UNLTD_ERR_TIMEOUT, std::string(who) + ": a kernel gave up waiting on a pipeline barrier");
 }
 

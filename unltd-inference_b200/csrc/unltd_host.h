@@ -29,6 +29,13 @@ struct unltd_ctx_s {
   std::atomic<int64_t> launches{0};
   void *comm = nullptr;  // ncclComm_t once unltd_comm_init ran
   int rank = 0, world = 1;
+  // Peer all-reduce over NVLink (comm.cu): this rank's receive area
+  // (exported through CUDA IPC), every rank's area mapped into this process
+  // (own = peer_area), and the device counter of all-reduces issued.
+  void *peer_area = nullptr;
+  void *peer_map[8] = {};
+  unsigned *peer_ctr = nullptr;
+  bool peer_ok = false;
 };
 
 struct unltd_weight_s {

@@ -58,6 +58,8 @@ SIGNATURES = [
     ("unltd_forget_host_weights", _I, []),
     ("unltd_comm_unique_id", _I, [_P, _S]),
     ("unltd_comm_init", _I, [_P, _I, _I, _P, _S]),
+    ("unltd_peer_export", _I, [_P, _P, _S]),
+    ("unltd_peer_import", _I, [_P, _P, _S]),
     ("unltd_allreduce_sum_f32", _I, [_P, _P, _S]),
     ("unltd_allreduce_max_u64", _I, [_P, _P, _S]),
     ("unltd_qwen35_create", _I, [_P, _P, ctypes.POINTER(_P)]),
@@ -219,6 +221,19 @@ class Context:
         buf = ctypes.create_string_buffer(bytes(uid), 128)
         _check(lib().unltd_comm_init(self.h, rank, world, buf, 128))
         self.rank, self.world = rank, world
+
+    def peer_init(self, group=None):
+        """Switch this context's all-reduces to the NVLink peer kernel: exchange
+        the CUDA IPC handles of every rank's receive area over the
+        torch.distributed group (call on every rank after comm_init)."""
+        import torch.distributed as dist
+
+        h = ctypes.create_string_buffer(64)
+        _check(lib().unltd_peer_export(self.h, h, 64))
+        hs = [None] * self.world
+        dist.all_gather_object(hs, h.raw, group=group)
+        buf = ctypes.create_string_buffer(b"".join(hs), 64 * self.world)
+        _check(lib().unltd_peer_import(self.h, buf, 64 * self.world))
 
     def allreduce_sum(self, buf, count: int):
         _check(lib().unltd_allreduce_sum_f32(self.h, _ptr(buf), count))
