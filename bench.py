@@ -565,7 +565,7 @@ def main():
                      for i, it in enumerate(items)},
         "f32x_mode": {"value": round(step_bytes / (ms_f32x * 1e-3) / 1e9, 2), "unit": UNIT,
                       "ms_per_step": round(ms_f32x, 4)},
-        "roofline": {"bound": "hbm", "kernel": "gemv Q6_K Q8K_EXACT + fused argmax (LM head, prep+gemv)",
+        "roofline": {"bound": "hbm", "kernel": "gemv_tc_kernel Q6_K Q8K_EXACT on the int8 tensor cores + fused argmax (LM head, prep+gemv)",
                      "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
                      "frac": round(achieved / peak, 4), "peak_kind": peak_kind,
                      "traffic": traffic},
