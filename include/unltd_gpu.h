@@ -176,6 +176,24 @@ int32_t unltd_peer_import(unltd_ctx ctx, const void *handles, size_t handle_byte
 int32_t unltd_allreduce_sum_f32(unltd_ctx ctx, float *buf_dev, size_t count);
 int32_t unltd_allreduce_max_u64(unltd_ctx ctx, uint64_t *buf_dev, size_t count);
 
+/* ---- GGUF files (gguf.rs:353-520, weights.rs:32-92) ----------------------
+ * unltd_gguf_open maps a GGUF (v2/v3) file read-only and parses its metadata
+ * and tensor table, every field bounds-checked; tensors are zero-copy views
+ * of the mapping, valid until unltd_gguf_close. dtype: the unltd ordinal of
+ * the tensor's ggml type, -1 for a type this path does not read (data NULL).
+ * ne: the dims, ne[0] fastest (a weight is ne = [dim_in, dim_out]). */
+typedef struct unltd_gguf_s *unltd_gguf;
+int32_t unltd_gguf_open(const char *path, unltd_gguf *out);
+int32_t unltd_gguf_close(unltd_gguf g);
+int64_t unltd_gguf_tensor_count(unltd_gguf g);
+int32_t unltd_gguf_tensor_info(unltd_gguf g, int64_t index, const char **name, int32_t *dtype, int64_t ne[4],
+                               int32_t *ndims, const void **data, size_t *nbytes);
+int32_t unltd_gguf_find_tensor(unltd_gguf g, const char *name, int64_t *index);
+/* Scalar metadata: integer types (bool as 0/1), f32/f64, strings. */
+int32_t unltd_gguf_get_int(unltd_gguf g, const char *key, int64_t *out);
+int32_t unltd_gguf_get_float(unltd_gguf g, const char *key, double *out);
+int32_t unltd_gguf_get_string(unltd_gguf g, const char *key, const char **out);
+
 /* ---- Qwen3.5-style hybrid decode step ------------------------------------
  * Replaces Qwen35Forward (crates/unltd-generation/src/qwen35_forward.rs):
  * open (139-232: every tensor checked for shape and dtype), new_session
@@ -191,6 +209,10 @@ typedef struct {
     int32_t conv_kernel, state_size, group_count, time_step_rank, d_inner, full_attn_interval, vocab;
     float freq_base, rms_eps;
 } unltd_qwen35_config; /* qwen35.rs:46-80 */
+/* Qwen35Config::from_gguf (qwen35.rs:23-42, 130-200): the qwen35.* keys, each
+ * required with its type (rope.dimension_sections i32[4]); vocab = the rows of
+ * token_embd.weight. The structural checks run in unltd_qwen35_create. */
+int32_t unltd_qwen35_config_from_gguf(unltd_gguf g, unltd_qwen35_config *cfg);
 
 typedef struct unltd_qwen35_s *unltd_qwen35;
 typedef struct unltd_qwen35_session_s *unltd_qwen35_session;
@@ -217,6 +239,10 @@ int32_t unltd_qwen35_set_tensor(unltd_qwen35 m, const char *name, const void *ho
 /* Check that every tensor is present and merge same-input projections
  * (qkv|z|beta|alpha, q|k|v, gate|up) into single GEMVs. */
 int32_t unltd_qwen35_finalize(unltd_qwen35 m);
+/* Every tensor of the model from an opened GGUF file (zero-copy views of its
+ * mapping, checked for name, dtype and shape like set_tensor), then
+ * finalize. weights.rs:32-92 + Qwen35Forward::open (qwen35_forward.rs:139-232). */
+int32_t unltd_qwen35_load_gguf(unltd_qwen35 m, unltd_gguf g);
 int32_t unltd_qwen35_destroy(unltd_qwen35 m);
 /* A session: conv windows, GDN states and K/V cache for ctx_len positions,
  * all zero, position 0 (new_session). Has its own stream. */

@@ -68,6 +68,30 @@ def test_tiny_greedy_stream_bit_exact(tiny):
     s.close()
 
 
+def test_tiny_loaded_from_gguf_matches_oracle(ctx, tiny, tmp_path):
+    """The model written as a GGUF file and loaded from its mapping
+    (unltd_qwen35_config_from_gguf + unltd_qwen35_load_gguf) decodes the same
+    greedy stream and logits as the oracle."""
+    cfg, tensors, _ = tiny
+    path = str(tmp_path / "tiny.gguf")
+    synth.write_qwen35_gguf(path, cfg, tensors)
+    with ug.Gguf(path) as g:
+        gcfg = g.qwen35_config()
+        m = ug.Qwen35Model(ctx, gcfg)
+        m.load_gguf(g)
+    st = synth.qwen35_state(cfg, 40, 12)
+    s = m.session(64)
+    s.set_state(40, st["conv"], st["gdn"], st["k"], st["v"])
+    toks = s.decode(5, 12)
+    o = oracle.Qwen35Oracle(cfg, tensors, 64, st, 40)
+    otoks, ologits, _ = o.greedy(5, 12)
+    assert toks.tolist() == otoks
+    lg, _ = s.read()
+    assert (bits(lg) == bits(ologits)).all()
+    s.close()
+    m.close()
+
+
 def test_tiny_prompt_from_position_zero(tiny):
     """feed() teacher-forces a prompt from an empty state (n_ctx = 1 at the
     first step), then decode() continues greedily."""

@@ -1455,6 +1455,27 @@ int32_t unltd_qwen35_set_tensor(unltd_qwen35 m, const char *name, const void *ho
   return UNLTD_OK;
 }
 
+// Every tensor Qwen35Forward::open checks (qwen35_forward.rs:139-232), taken
+// from the GGUF mapping: a weight must be 2-D with ne = [dim_in, dim_out], a
+// vector (norms, conv taps, dt bias, A) must hold dim_in elements; dtype and
+// byte count are checked again by set_tensor.
+int32_t unltd_qwen35_load_gguf(unltd_qwen35 m, unltd_gguf g) {
+  if (!m || !g) return set_error(UNLTD_ERR_INVALID_ARG, "qwen35_load_gguf: NULL argument");
+  if (m->finalized) return set_error(UNLTD_ERR_INVALID_ARG, "qwen35_load_gguf: model already finalized");
+  for (const Part &p : expected(m->d)) {
+    GgufTensorView t;
+    if (!gguf_tensor(g, p.name, &t)) return set_error(UNLTD_ERR_INVALID_ARG, "gguf: missing tensor '" + p.name + "'");
+    if (!t.data)
+      return set_error(UNLTD_ERR_UNSUPPORTED, "gguf: tensor '" + p.name + "' has a type this path does not read");
+    const int64_t nel = t.ne[0] * t.ne[1] * t.ne[2] * t.ne[3];
+    const bool shape_ok = p.dim_out > 1 ? (t.ndims == 2 && t.ne[0] == (int64_t)p.dim_in && t.ne[1] == (int64_t)p.dim_out)
+                                        : nel == (int64_t)p.dim_in;
+    if (!shape_ok) return set_error(UNLTD_ERR_LENGTH, "gguf: tensor '" + p.name + "' has the wrong shape");
+    if (int32_t rc = unltd_qwen35_set_tensor(m, p.name.c_str(), t.data, t.nbytes, t.dtype)) return rc;
+  }
+  return unltd_qwen35_finalize(m);
+}
+
 int32_t unltd_qwen35_finalize(unltd_qwen35 m) {
   if (!m) return set_error(UNLTD_ERR_INVALID_ARG, "qwen35_finalize: NULL model");
   if (m->finalized) return UNLTD_OK;

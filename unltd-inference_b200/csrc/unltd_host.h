@@ -110,6 +110,17 @@ bool gemv_norm_fusable(unltd_ctx ctx, const unltd_weight_s &w, int mode);
 int32_t gemv_reserve(unltd_ctx ctx, const unltd_weight_s &w, int mode);
 void gemv_prewarm(int device);
 
+// gguf.cu: a tensor of an opened GGUF file (data: a view into the mapping,
+// null when its type is not one this path reads)
+struct GgufTensorView {
+  const void *data;
+  size_t nbytes;
+  int dtype;
+  uint32_t ndims;
+  int64_t ne[4];
+};
+bool gguf_tensor(unltd_gguf g, const std::string &name, GgufTensorView *out);
+
 // comm.cu (NCCL through dlopen)
 int32_t comm_allreduce(unltd_ctx c, cudaStream_t st, void *buf, size_t count, bool max_u64);
 void comm_destroy(unltd_ctx c);

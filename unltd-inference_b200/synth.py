@@ -72,6 +72,7 @@ def row_bytes(dtype: int, dim_in: int) -> int:
 # The session state stands in for a prefilled context: K and V cache rows
 # ~ N(0, 1), conv windows ~ N(0, 1), GDN matrices ~ N(0, 0.05^2).
 
+import struct
 import zlib
 
 QWEN35_9B = dict(
@@ -176,3 +177,85 @@ def qwen35_state(cfg: dict, position: int, seed: int) -> dict:
             st["conv"].append(rng.standard_normal((cfg["conv_kernel"] - 1, d["dconv"]), dtype=np.float32))
             st["gdn"].append((0.05 * rng.standard_normal((d["nv"], d["hd"], d["hd"]), dtype=np.float32)).astype(np.float32))
     return st
+
+
+# ---- synthetic GGUF files (the reference's loader reads gguf.rs:353-520) ----
+
+_GGML_TYPE = {F32: 0, Q8_0: 8, Q4K: 12, Q6K: 14}
+_GGUF_U32, _GGUF_I32, _GGUF_F32, _GGUF_STRING, _GGUF_ARRAY = 4, 5, 6, 8, 9
+
+
+def _gguf_str(b: bytearray, s: str):
+    e = s.encode()
+    b += struct.pack("<Q", len(e)) + e
+
+
+def write_gguf(path: str, kvs: list, tensors: list, alignment: int = 32):
+    """GGUF v3: kvs = [(key, kind, value)] with kind in 'u32', 'i32', 'f32',
+    'str', 'i32[]'; tensors = [(name, ggml_type, ne (ne[0] fastest), bytes)]."""
+    b = bytearray(b"GGUF")
+    b += struct.pack("<IQQ", 3, len(tensors), len(kvs) + 1)
+    _gguf_str(b, "general.alignment")
+    b += struct.pack("<II", _GGUF_U32, alignment)
+    for key, kind, val in kvs:
+        _gguf_str(b, key)
+        if kind == "u32":
+            b += struct.pack("<II", _GGUF_U32, val)
+        elif kind == "i32":
+            b += struct.pack("<Ii", _GGUF_I32, val)
+        elif kind == "f32":
+            b += struct.pack("<If", _GGUF_F32, val)
+        elif kind == "str":
+            b += struct.pack("<I", _GGUF_STRING)
+            _gguf_str(b, val)
+        elif kind == "i32[]":
+            b += struct.pack("<IIQ", _GGUF_ARRAY, _GGUF_I32, len(val)) + struct.pack(f"<{len(val)}i", *val)
+        else:
+            raise ValueError(kind)
+    off = 0
+    offsets = []
+    for name, gt, ne, data in tensors:
+        _gguf_str(b, name)
+        b += struct.pack("<I", len(ne)) + struct.pack(f"<{len(ne)}Q", *ne)
+        b += struct.pack("<IQ", gt, off)
+        offsets.append(off)
+        off += (len(data) + alignment - 1) // alignment * alignment
+    b += bytes((-len(b)) % alignment)
+    with open(path, "wb") as fh:
+        fh.write(b)
+        for (name, gt, ne, data), o in zip(tensors, offsets):
+            fh.write(data)
+            fh.write(bytes((-len(data)) % alignment))
+
+
+def write_qwen35_gguf(path: str, cfg: dict, tensors: dict, context_length: int = 262144):
+    """The model as a qwen35 GGUF file: the metadata keys Qwen35Config::from_gguf
+    requires (qwen35.rs:23-42) and every tensor in GGUF shape (a weight ne =
+    [dim_in, dim_out]; ssm_conv1d.weight ne = [conv_kernel, channels])."""
+    a = "qwen35."
+    kvs = [("general.architecture", "str", "qwen35"),
+           (a + "block_count", "u32", cfg["n_layer"]), (a + "context_length", "u32", context_length),
+           (a + "embedding_length", "u32", cfg["n_embd"]), (a + "feed_forward_length", "u32", cfg["n_ff"]),
+           (a + "attention.head_count", "u32", cfg["n_head"]),
+           (a + "attention.head_count_kv", "u32", cfg["n_head_kv"]),
+           (a + "attention.key_length", "u32", cfg["head_dim"]),
+           (a + "attention.value_length", "u32", cfg["head_dim_v"]),
+           (a + "attention.layer_norm_rms_epsilon", "f32", cfg["rms_eps"]),
+           (a + "rope.dimension_count", "u32", cfg["n_rot"]),
+           (a + "rope.dimension_sections", "i32[]", [11, 11, 10, 0]),
+           (a + "rope.freq_base", "f32", cfg["freq_base"]),
+           (a + "ssm.conv_kernel", "u32", cfg["conv_kernel"]), (a + "ssm.state_size", "u32", cfg["state_size"]),
+           (a + "ssm.group_count", "u32", cfg["group_count"]),
+           (a + "ssm.time_step_rank", "u32", cfg["time_step_rank"]),
+           (a + "ssm.inner_size", "u32", cfg["d_inner"]),
+           (a + "full_attention_interval", "u32", cfg["full_attn_interval"])]
+    out = []
+    for name, dt, dim_in, dim_out in qwen35_tensor_list(cfg):
+        _, arr = tensors[name]
+        data = np.ascontiguousarray(arr).tobytes()
+        if dt == F32:
+            ne = [cfg["conv_kernel"], dim_in // cfg["conv_kernel"]] if name.endswith("ssm_conv1d.weight") else [dim_in]
+        else:
+            ne = [dim_in, dim_out]
+        out.append((name, _GGML_TYPE[dt], ne, data))
+    write_gguf(path, kvs, out)

@@ -58,6 +58,16 @@ SIGNATURES = [
     ("unltd_forget_host_weights", _I, []),
     ("unltd_comm_unique_id", _I, [_P, _S]),
     ("unltd_comm_init", _I, [_P, _I, _I, _P, _S]),
+    ("unltd_gguf_open", _I, [ctypes.c_char_p, _P]),
+    ("unltd_gguf_close", _I, [_P]),
+    ("unltd_gguf_tensor_count", ctypes.c_int64, [_P]),
+    ("unltd_gguf_tensor_info", _I, [_P, ctypes.c_int64, _P, _P, _P, _P, _P, _P]),
+    ("unltd_gguf_find_tensor", _I, [_P, ctypes.c_char_p, _P]),
+    ("unltd_gguf_get_int", _I, [_P, ctypes.c_char_p, _P]),
+    ("unltd_gguf_get_float", _I, [_P, ctypes.c_char_p, _P]),
+    ("unltd_gguf_get_string", _I, [_P, ctypes.c_char_p, _P]),
+    ("unltd_qwen35_config_from_gguf", _I, [_P, _P]),
+    ("unltd_qwen35_load_gguf", _I, [_P, _P]),
     ("unltd_peer_export", _I, [_P, _P, _S]),
     ("unltd_peer_import", _I, [_P, _P, _S]),
     ("unltd_allreduce_sum_f32", _I, [_P, _P, _S]),
@@ -352,6 +362,75 @@ def qwen35_shard(cfg: dict, rank: int, world: int, name: str):
     return [(ranges[2 * k], ranges[2 * k + 1]) for k in range(n.value)], (i0.value, i1.value)
 
 
+class Gguf:
+    """An opened GGUF file (unltd_gguf_open): metadata and zero-copy tensor
+    views of its read-only mapping (gguf.rs:353-520, weights.rs:32-92)."""
+
+    def __init__(self, path: str):
+        h = ctypes.c_void_p()
+        _check(lib().unltd_gguf_open(os.fsencode(path), ctypes.byref(h)))
+        self.h = h
+
+    def tensors(self) -> list:
+        """[(name, dtype, ne (4 dims, ne[0] fastest), ndims, nbytes, address)]"""
+        out = []
+        for i in range(lib().unltd_gguf_tensor_count(self.h)):
+            name, dt, nd, data, nb = ctypes.c_char_p(), ctypes.c_int32(), ctypes.c_int32(), ctypes.c_void_p(), _S()
+            ne = (ctypes.c_int64 * 4)()
+            _check(lib().unltd_gguf_tensor_info(self.h, i, ctypes.byref(name), ctypes.byref(dt), ne, ctypes.byref(nd),
+                                                ctypes.byref(data), ctypes.byref(nb)))
+            out.append((name.value.decode(errors="replace"), dt.value, tuple(ne), nd.value, nb.value, data.value))
+        return out
+
+    def tensor_bytes(self, name: str) -> bytes:
+        i = ctypes.c_int64()
+        _check(lib().unltd_gguf_find_tensor(self.h, name.encode(), ctypes.byref(i)))
+        data, nb = ctypes.c_void_p(), _S()
+        _check(lib().unltd_gguf_tensor_info(self.h, i.value, None, None, None, None, ctypes.byref(data),
+                                            ctypes.byref(nb)))
+        return ctypes.string_at(data.value, nb.value) if data.value else b""
+
+    def get_int(self, key: str) -> int:
+        v = ctypes.c_int64()
+        _check(lib().unltd_gguf_get_int(self.h, key.encode(), ctypes.byref(v)))
+        return v.value
+
+    def get_float(self, key: str) -> float:
+        v = ctypes.c_double()
+        _check(lib().unltd_gguf_get_float(self.h, key.encode(), ctypes.byref(v)))
+        return v.value
+
+    def get_string(self, key: str) -> str:
+        v = ctypes.c_char_p()
+        _check(lib().unltd_gguf_get_string(self.h, key.encode(), ctypes.byref(v)))
+        return v.value.decode()
+
+    def qwen35_config(self) -> dict:
+        """Qwen35Config::from_gguf (qwen35.rs:130-200) as a config dict."""
+        c = Qwen35Config()
+        _check(lib().unltd_qwen35_config_from_gguf(self.h, ctypes.byref(c)))
+        return {k: getattr(c, k) for k, _ in Qwen35Config._fields_}
+
+    def close(self):
+        if getattr(self, "h", None):
+            lib().unltd_gguf_close(self.h)
+            self.h = None
+
+    def __enter__(self):
+        return self
+
+    def __exit__(self, *exc):
+        self.close()
+
+    def __del__(self, _finalizing=sys.is_finalizing):
+        if _finalizing():
+            return
+        try:
+            self.close()
+        except Exception:
+            pass
+
+
 class Qwen35Model:
     """Qwen35Forward::open on the device: tensors uploaded by GGUF name. With
     world > 1 this is the tensor-parallel shard of `rank` (the context needs
@@ -374,6 +453,10 @@ class Qwen35Model:
         for name, (dt, arr) in tensors.items():
             self.set_tensor(name, arr, dt)
         _check(lib().unltd_qwen35_finalize(self.h))
+
+    def load_gguf(self, g: "Gguf"):
+        """Every tensor from an opened GGUF file (zero-copy views), then finalize."""
+        _check(lib().unltd_qwen35_load_gguf(self.h, g.h))
 
     def session(self, ctx_len: int) -> "Qwen35Session":
         h = ctypes.c_void_p()
