@@ -167,6 +167,9 @@ struct Params {
   float norm_eps;
   uint8_t *norm_img4, *norm_img6;
   int nn;
+  // non-null: x in f32 (dim_in elements, 16-byte aligned), quantized into the
+  // CTA's image in the prologue instead of by a separate prep kernel
+  const float *xq;
 };
 
 __device__ __forceinline__ uint4 lds128(const uint8_t *p) { return *reinterpret_cast<const uint4 *>(p); }
@@ -949,6 +952,37 @@ __device__ __forceinline__ void tc_norm_prologue(const Params &P, uint8_t *ximg)
   }
 }
 
+// quantize_q8_k of x (quants.rs:250-290) in the integer warps' prologue,
+// after griddepcontrol.wait, while the producer already streams weights:
+// warp w takes spans w, w + 16, ... (lane l: elements 8l .. 8l+7), loads of
+// up to three spans in flight.
+template <int FMT>
+__device__ __noinline__ void tc_quant_prologue(const float *__restrict__ x, int nsp, uint8_t *ximg) {
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  for (int s0 = warp; s0 < nsp; s0 += 3 * kTcIntWarps) {
+    float4 v[3][2];
+#pragma unroll
+    for (int q = 0; q < 3; q++) {
+      const int span = s0 + kTcIntWarps * q;
+      v[q][0] = v[q][1] = make_float4(0.f, 0.f, 0.f, 0.f);
+      if (span < nsp) {
+        const float4 *p = reinterpret_cast<const float4 *>(x + (size_t)span * 256 + 8 * lane);
+        v[q][0] = p[0];
+        v[q][1] = p[1];
+      }
+    }
+#pragma unroll
+    for (int q = 0; q < 3; q++) {
+      const int span = s0 + kTcIntWarps * q;
+      if (span >= nsp) break;
+      const float e[8] = {v[q][0].x, v[q][0].y, v[q][0].z, v[q][0].w, v[q][1].x, v[q][1].y, v[q][1].z, v[q][1].w};
+      if constexpr (FMT == Q4K) q8k_span_write_warp(e, lane, ximg + (size_t)span * kImgQ8K4, nullptr);
+      else q8k_span_write_warp(e, lane, nullptr, ximg + (size_t)span * kImgQ8K6);
+    }
+  }
+  named_bar_sync(1, kTcIntWarps * 32);
+}
+
 template <int FMT, bool ARGMAX, bool R8 = false>
 __global__ void __launch_bounds__(kTcThreads, 1) gemv_tc_kernel(Params P) {
   constexpr int kImg = FMT == Q4K ? kImgQ8K4 : kImgQ8K6;
@@ -1009,6 +1043,8 @@ __global__ void __launch_bounds__(kTcThreads, 1) gemv_tc_kernel(Params P) {
     // ---------------- integer warps -------------------------------------------
     if (FMT == Q4K && P.nn) {
       tc_norm_prologue(P, ximg);
+    } else if (P.xq) {
+      tc_quant_prologue<FMT>(P.xq, P.nbu, ximg);
     } else {
       const uint4 *src = reinterpret_cast<const uint4 *>(P.img);
       uint4 *dst = reinterpret_cast<uint4 *>(ximg);
@@ -1388,10 +1424,12 @@ int32_t gemv_launch(unltd_ctx ctx, const GemvArgs &a) {
       if ((uintptr_t)p % 16) return set_error(UNLTD_ERR_INVALID_ARG, "gemv: fused RMSNorm pointers must be 16-byte aligned");
     if (!g.a || !g.w) return set_error(UNLTD_ERR_INVALID_ARG, "gemv: fused RMSNorm needs a and w");
   }
-  if (!a.img && !fuse) {
+  const Plan pl = plan_gemv(ctx, w, mode);
+  // tensor-core GEMV of a plain f32 x: quantized in its own prologue
+  const bool xpro = pl.mma && mode == MODE_Q8K && !a.img && !fuse && !am && a.x && (uintptr_t)a.x % 16 == 0;
+  if (!a.img && !fuse && !xpro) {
     if (int32_t rc = gemv_reserve(ctx, w, mode)) return rc;
   }
-  const Plan pl = plan_gemv(ctx, w, mode);
   if (pl.S < 2)
     return set_error(UNLTD_ERR_UNSUPPORTED, "gemv: row too long for the shared-memory pipeline (dim_in too large)");
   const int nspans = pl.nbu, nbu = pl.nbu, img_bytes = pl.img_bytes, rows = pl.rows;
@@ -1403,7 +1441,7 @@ int32_t gemv_launch(unltd_ctx ctx, const GemvArgs &a) {
   unsigned long long *key = am ? a.argmax_key : nullptr;
   unsigned *done = am ? a.argmax_done : nullptr;
   cudaError_t e = cudaSuccess;
-  if (a.img || fuse) {
+  if (a.img || fuse || xpro) {
   } else if (mode == MODE_F32X) {
     if (fmt == Q4K) prep_f32x<Q4K><<<nspans, kThreads, 0, st>>>(a.x, w.dim_in, ctx->scratch, key, done);
     else if (fmt == Q6K) prep_f32x<Q6K><<<nspans, kThreads, 0, st>>>(a.x, w.dim_in, ctx->scratch, key, done);
@@ -1412,7 +1450,7 @@ int32_t gemv_launch(unltd_ctx ctx, const GemvArgs &a) {
     if (fmt == Q4K) prep_q8k<Q4K><<<nspans, kThreads, 0, st>>>(a.x, w.dim_in, ctx->scratch, key, done);
     else prep_q8k<Q6K><<<nspans, kThreads, 0, st>>>(a.x, w.dim_in, ctx->scratch, key, done);
   }
-  if (!a.img && !fuse) {
+  if (!a.img && !fuse && !xpro) {
     e = cudaGetLastError();
     if (e != cudaSuccess) return cuda_error(e, "gemv prep");
     ctx->launches += 1;
@@ -1452,6 +1490,7 @@ int32_t gemv_launch(unltd_ctx ctx, const GemvArgs &a) {
   P.norm_img4 = fuse ? a.norm->img4_out : nullptr;
   P.norm_img6 = fuse ? a.norm->img6_out : nullptr;
   P.nn = fuse ? (int)w.dim_in : 0;
+  P.xq = xpro ? a.x : nullptr;
 
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(grid);
