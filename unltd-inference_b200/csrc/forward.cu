@@ -508,23 +508,99 @@ __global__ void __launch_bounds__(HDV) attn_pre_kernel(AttnArgs a) {
   }
 }
 
+// Across-lane part of the pairwise tree for L scores held by every lane
+// (v[i]: this lane's subtree sum of score i): levels pair lanes xor 1, 2, 4,
+// 8, 16 in that order, exactly as the tree pairs (2j, 2j+1) of the previous
+// level. While a lane holds more than one score it keeps half of them and
+// sends the other half to its partner (recursive halving): 5 levels cost
+// L - 1 + (5 - log2 L) f64 exchanges instead of 5 L. Returns the full sum of
+// score `idx`; lanes < L hold distinct scores.
+template <int LEN, int B>
+__device__ __forceinline__ void tree_level(double (&v)[16], int lane, int &base) {
+  if constexpr (B < 5) {
+    constexpr int m = 1 << B;
+    const bool hi = (lane & m) != 0;
+    if constexpr (LEN > 1) {
+      constexpr int half = LEN / 2;
+#pragma unroll
+      for (int i = 0; i < half; i++) {
+        const double send = hi ? v[i] : v[half + i];
+        const double keep = hi ? v[half + i] : v[i];
+        v[i] = __dadd_rn(keep, __shfl_xor_sync(~0u, send, m));
+      }
+      if (hi) base += half;
+      tree_level<half, B + 1>(v, lane, base);
+    } else {
+      v[0] = __dadd_rn(v[0], __shfl_xor_sync(~0u, v[0], m));
+      tree_level<1, B + 1>(v, lane, base);
+    }
+  }
+}
+
+template <int L>
+__device__ __forceinline__ double tree_reduce_lanes(double (&v)[16], int lane, int &idx) {
+  int base = 0;
+  tree_level<L, 0>(v, lane, base);
+  idx = base;
+  return v[0];
+}
+
+// One pass of the score kernel over heads g0 .. g0 + gn - 1 (gn <= GN) and
+// the warp's four positions: slot r * GN + gi holds (position r, head gi).
+template <int HDV, int GN>
+__device__ __forceinline__ void score_pass(const double *qsm, const float (&kv)[4][HDV / 32], const AttnArgs &a,
+                                           int kvh, int G, int g0, int gn, int p0, int n_ctx, int warp, int lane) {
+  constexpr int E = HDV / 32, L = 4 * GN;
+  double v[16];
+#pragma unroll
+  for (int i = 0; i < 16; i++) v[i] = 0.0;
+#pragma unroll
+  for (int r = 0; r < 4; r++) {
+    double kd[E];  // position r's k row, converted once for all heads
+#pragma unroll
+    for (int t = 0; t < E; t++) kd[t] = (double)kv[r][t];
+#pragma unroll
+    for (int gi = 0; gi < GN; gi++) {
+      if (gi < gn) {
+        const double *qg = qsm + (g0 + gi) * HDV + lane * E;
+        double pr[E];
+#pragma unroll
+        for (int t = 0; t < E; t++) pr[t] = __dmul_rn(qg[t], kd[t]);
+#pragma unroll
+        for (int w = 1; w < E; w <<= 1)
+#pragma unroll
+          for (int t = 0; t < E; t += 2 * w) pr[t] = __dadd_rn(pr[t], pr[t + w]);
+        v[r * GN + gi] = pr[0];
+      }
+    }
+  }
+  int idx = 0;
+  const double sum = tree_reduce_lanes<L>(v, lane, idx);
+  if (lane < L) {
+    const int r = idx / GN, gi = idx % GN;
+    const int p = p0 + warp + 8 * r;
+    if (gi < gn && p < n_ctx) a.scores[(size_t)(kvh * G + g0 + gi) * a.ctx + p] = (float)sum;
+  }
+}
+
 // scores[h][p] = dot_f32(q_h, k_p) as f32 (quants.rs:106-114): exact f64
 // products summed by the pairwise tree, which for HDV = 32 * E (E a power of
-// two) is lane-local subtrees over E contiguous elements and then a butterfly.
-// A warp takes four positions (all loads issued first), all q heads of the
-// kv group; 32 positions per CTA.
+// two) is lane-local subtrees over E contiguous elements and then the lanes
+// (tree_reduce_lanes). A warp takes four positions (all loads issued first)
+// and the q heads of the kv group, up to four at a time; 32 positions per
+// CTA. q is converted to double once per CTA, each k row once per position.
 template <int HDV>
-__global__ void __launch_bounds__(256) attn_scores_kernel(AttnArgs a) {
+__global__ void __launch_bounds__(256, 2) attn_scores_kernel(AttnArgs a) {
   constexpr int E = HDV / 32;
   pdl_trigger();
-  extern __shared__ float qsm[];  // G x HDV
+  extern __shared__ double qsm[];  // G x HDV
   pdl_wait();
   const int kvh = blockIdx.x, G = a.nh / a.nkv;
   const int n_ctx = *a.pos + 1;
   const int p0 = blockIdx.y * 32;
   if (p0 >= n_ctx) return;
 #pragma unroll 4
-  for (int i = threadIdx.x; i < G * HDV; i += 256) qsm[i] = a.q[(size_t)(kvh * G) * HDV + i];
+  for (int i = threadIdx.x; i < G * HDV; i += 256) qsm[i] = (double)a.q[(size_t)(kvh * G) * HDV + i];
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const size_t kvlen = (size_t)a.nkv * HDV;
   float kv[4][E];
@@ -539,23 +615,11 @@ __global__ void __launch_bounds__(256) attn_scores_kernel(AttnArgs a) {
     }
   }
   __syncthreads();
-#pragma unroll
-  for (int r = 0; r < 4; r++) {
-    const int p = p0 + warp + 8 * r;
-    if (p >= n_ctx) break;
-    for (int g = 0; g < G; g++) {
-      double pr[E];
-#pragma unroll
-      for (int t = 0; t < E; t++) pr[t] = __dmul_rn((double)qsm[g * HDV + lane * E + t], (double)kv[r][t]);
-#pragma unroll
-      for (int w = 1; w < E; w <<= 1)
-#pragma unroll
-        for (int t = 0; t < E; t += 2 * w) pr[t] = __dadd_rn(pr[t], pr[t + w]);
-      double s = pr[0];
-#pragma unroll
-      for (int o = 1; o < 32; o <<= 1) s = __dadd_rn(s, __shfl_xor_sync(~0u, s, o));
-      if (lane == 0) a.scores[(size_t)(kvh * G + g) * a.ctx + p] = (float)s;
-    }
+  for (int g0 = 0; g0 < G; g0 += 4) {
+    const int gn = min(4, G - g0);  // heads in this pass
+    if (gn > 2) score_pass<HDV, 4>(qsm, kv, a, kvh, G, g0, gn, p0, n_ctx, warp, lane);
+    else if (gn == 2) score_pass<HDV, 2>(qsm, kv, a, kvh, G, g0, gn, p0, n_ctx, warp, lane);
+    else score_pass<HDV, 1>(qsm, kv, a, kvh, G, g0, gn, p0, n_ctx, warp, lane);
   }
 }
 
@@ -609,7 +673,7 @@ template <int HDV>
 __global__ void __launch_bounds__(HDV) attn_values_kernel(AttnArgs a) {
   pdl_trigger();
   extern __shared__ __align__(16) float vsm[];  // kChunk x HDV
-  __shared__ float ssoft[kMaxGroup][kChunk];
+  __shared__ double ssoft[kMaxGroup][kChunk];  // converted once, not per column
   pdl_wait();
   const int kvh = blockIdx.x, split = blockIdx.y, c = threadIdx.x;
   const int n = *a.pos + 1, G = a.nh / a.nkv;
@@ -629,7 +693,7 @@ __global__ void __launch_bounds__(HDV) attn_values_kernel(AttnArgs a) {
   }
   for (int i = c; i < G * kChunk; i += HDV) {
     const int g = i / kChunk, pp = i % kChunk;
-    ssoft[g][pp] = pp < len ? a.scores[(size_t)(kvh * G + g) * a.ctx + p0 + pp] : 0.0f;
+    ssoft[g][pp] = pp < len ? (double)a.scores[(size_t)(kvh * G + g) * a.ctx + p0 + pp] : 0.0;
   }
 #pragma unroll
   for (int i = 0; i < V4; i++) reinterpret_cast<float4 *>(vsm)[i * HDV + c] = buf[i];
@@ -642,7 +706,7 @@ __global__ void __launch_bounds__(HDV) attn_values_kernel(AttnArgs a) {
 #pragma unroll
     for (int g = 0; g < kMaxGroup; g++) {
       if (g < G) {
-        S[g] = __dadd_rn(S[g], __dmul_rn((double)ssoft[g][p], v));
+        S[g] = __dadd_rn(S[g], __dmul_rn(ssoft[g][p], v));
         Q[g] = __dadd_rn(Q[g], fabs(S[g]));
       }
     }
@@ -1278,7 +1342,7 @@ int32_t enqueue_step(unltd_qwen35_session s) {
       a.eps = d.eps;
       a.kq_scale = d.kq_scale;
       const dim3 sg(d.nkvl, (s->ctx_len + 31) / 32), vg(d.nkvl, s->nsplit);
-      const size_t q_smem = (size_t)(d.nhl / d.nkvl) * d.hdv * 4, v_smem = (size_t)kChunk * d.hdv * 4;
+      const size_t q_smem = (size_t)(d.nhl / d.nkvl) * d.hdv * 8, v_smem = (size_t)kChunk * d.hdv * 4;
       const size_t sm_smem = softmax_smem(s->ctx_len);
       const dim3 cg(d.nhl * d.hdv / 256), pg(d.nhl + d.nkvl), smg(d.nhl);
       if (d.hdv == 256) {
