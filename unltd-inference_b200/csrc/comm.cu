@@ -53,15 +53,8 @@ int32_t nccl_error(ncclResult_t r, const char *what) {
 }  // namespace
 
 // ---- peer all-reduce: one kernel over NVLink peer memory ------------------
-// Every rank's receive area: 64 flag words (flag[src] = the last all-reduce
-// number rank src completed writing here), then two parities x kPeerMaxRanks
-// source slots of kPeerMaxCount 8-byte words.
-constexpr int kPeerMaxRanks = 8;
-constexpr size_t kPeerMaxCount = 16384;  // floats (or u64) per all-reduce
-constexpr size_t kPeerFlagBytes = 256;
-constexpr size_t kPeerSlotBytes = kPeerMaxCount * 8;
-constexpr size_t kPeerAreaBytes = kPeerFlagBytes + 2 * kPeerMaxRanks * kPeerSlotBytes;
-constexpr int kErrPeer = 3;
+// The receive area layout (kPeer* in unltd_host.h): flags, then two
+// parities of per-source slots.
 
 struct PeerArgs {
   uint8_t *map[kPeerMaxRanks];  // every rank's area as mapped here
@@ -173,6 +166,7 @@ void peer_close(unltd_ctx c) {
   if (c->peer_ctr) cudaFree(c->peer_ctr);
   c->peer_area = nullptr;
   c->peer_ctr = nullptr;
+  c->peer_done = nullptr;
   c->peer_ok = false;
 }
 
@@ -235,8 +229,9 @@ int32_t unltd_peer_export(unltd_ctx c, void *handle_out, size_t handle_bytes) {
   if (!c->peer_area) {
     cudaError_t e = cudaMalloc(&c->peer_area, kPeerAreaBytes);
     if (e == cudaSuccess) e = cudaMemset(c->peer_area, 0, kPeerAreaBytes);
-    if (e == cudaSuccess) e = cudaMalloc(&c->peer_ctr, sizeof(unsigned));
-    if (e == cudaSuccess) e = cudaMemset(c->peer_ctr, 0, sizeof(unsigned));
+    if (e == cudaSuccess) e = cudaMalloc(&c->peer_ctr, 2 * sizeof(unsigned));
+    if (e == cudaSuccess) e = cudaMemset(c->peer_ctr, 0, 2 * sizeof(unsigned));
+    c->peer_done = c->peer_ctr + 1;
     if (e != cudaSuccess) {
       peer_close(c);
       return cuda_error(e, "peer_export: area");

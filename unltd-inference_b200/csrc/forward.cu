@@ -1197,9 +1197,10 @@ int64_t launch_gemv(unltd_ctx c, const unltd_weight_s *w, const float *x, float 
 }
 
 // GEMV whose x image a fused producer kernel already wrote.
-int64_t launch_gemv_img(unltd_qwen35_session s, const unltd_weight_s *w, float *y, int32_t *rc) {
-  GemvArgs g{w, nullptr, y, MODE_Q8K, nullptr, nullptr, nullptr};
+int64_t launch_gemv_img(unltd_qwen35_session s, const unltd_weight_s *w, float *y, int32_t *rc, bool send = false) {
+  GemvArgs g{w, nullptr, send ? nullptr : y, MODE_Q8K, nullptr, nullptr, nullptr};
   g.img = w->dtype == Q4K ? s->img4 : s->img6;
+  g.peer_send = send;
   if (!*rc) *rc = gemv_launch(s->ctx, g);
   return 1;
 }
@@ -1258,7 +1259,19 @@ int32_t enqueue_step(unltd_qwen35_session s) {
   // into the prologue of p's first tensor-core Q4_K GEMV when it has one,
   // which then also writes the images p's other GEMVs read; else the
   // stand-alone norm kernel followed by the GEMVs.
-  auto norm_proj = [&](const float *a, const float *b, float *r_out, const float *w, const Proj &p, float *out) {
+  // Tensor parallelism with peer memory: a row-split GEMV (ssm_out /
+  // attn_output, ffn_down) stores its partial rows into every rank's peer area
+  // and the consuming GEMV's fused norm sums them in rank order: no separate
+  // all-reduce kernel. The last layer's down keeps the all-reduce (the output
+  // norm is a kernel of its own).
+  const bool peer_sum = d.world > 1 && s->ctx->peer_ok && (size_t)d.n <= kPeerMaxCount;
+  auto proj_fusable = [&](const Proj &p) {
+    for (auto *w : p.w)
+      if (gemv_norm_fusable(s->ctx, *w, MODE_Q8K)) return true;
+    return false;
+  };
+  auto norm_proj = [&](const float *a, const float *b, float *r_out, const float *w, const Proj &p, float *out,
+                       bool recv = false) {
     int fi = -1;
     for (size_t i = 0; i < p.w.size() && fi < 0; i++)
       if (gemv_norm_fusable(s->ctx, *p.w[i], MODE_Q8K)) fi = (int)i;
@@ -1273,7 +1286,8 @@ int32_t enqueue_step(unltd_qwen35_session s) {
       need4 |= p.w[i]->dtype == Q4K;
       need6 |= p.w[i]->dtype == Q6K;
     }
-    const GemvNorm gn{a, b, r_out, w, d.eps, need4 ? s->img4 : nullptr, need6 ? s->img6 : nullptr};
+    GemvNorm gn{a, recv ? nullptr : b, r_out, w, d.eps, need4 ? s->img4 : nullptr, need6 ? s->img6 : nullptr};
+    gn.peer_recv = recv;
     GemvArgs g{p.w[fi], nullptr, out + p.off[fi], MODE_Q8K, nullptr, nullptr, nullptr};
     g.norm = &gn;
     if (!rc) rc = gemv_launch(s->ctx, g);
@@ -1285,11 +1299,15 @@ int32_t enqueue_step(unltd_qwen35_session s) {
                  m->embd->row_stride, m->embd->nb, (const uint32_t *)s->cur_token, (uint32_t)d.vocab, s->X, d.n,
                  s->ctx->err),
       "embed");
+  bool down_sent = false;  // the previous layer's down GEMV sent its rows to the peers
   for (int il = 0; il < d.n_layer; il++) {
     const Layer &L = m->layers[il];
+    const bool out_send = peer_sum && proj_fusable(L.gate_up) && gemv_tc_eligible(s->ctx, *L.out, MODE_Q8K);
+    const bool down_send = peer_sum && il + 1 < d.n_layer && proj_fusable(m->layers[il + 1].in) &&
+                           gemv_tc_eligible(s->ctx, *L.down, MODE_Q8K);
     // layer input = l_out of the previous layer (residual + ffn), fused into the norm
     if (il == 0) norm_proj(s->X, nullptr, nullptr, L.attn_norm, L.in, s->proj);
-    else norm_proj(s->R, s->F, s->X, L.attn_norm, L.in, s->proj);
+    else norm_proj(s->R, s->F, s->X, L.attn_norm, L.in, s->proj, down_sent);
     if (!L.attn) {
       RecrArgs a;
       a.proj = s->proj;
@@ -1316,8 +1334,8 @@ int32_t enqueue_step(unltd_qwen35_session s) {
                      L.out->dtype == Q4K ? s->img4 : (uint8_t *)nullptr,
                      L.out->dtype == Q6K ? s->img6 : (uint8_t *)nullptr),
           "gated_norm");
-      nl += launch_gemv_img(s, L.out, s->T, &rc);
-      allreduce(s->T, d.n);
+      nl += launch_gemv_img(s, L.out, s->T, &rc, out_send);
+      if (!out_send) allreduce(s->T, d.n);
     } else {
       AttnArgs a;
       a.qk = s->proj;
@@ -1358,17 +1376,18 @@ int32_t enqueue_step(unltd_qwen35_session s) {
         chk(launch_pdl(attn_values_kernel<128>, vg, dim3(128), v_smem, st, a), "attn_values");
         chk(launch_pdl(attn_combine_quant_kernel<128>, cg, dim3(256), 0, st, a), "attn_combine");
       }
-      nl += launch_gemv_img(s, L.out, s->T, &rc);
-      allreduce(s->T, d.n);
+      nl += launch_gemv_img(s, L.out, s->T, &rc, out_send);
+      if (!out_send) allreduce(s->T, d.n);
     }
     // residual = x_in + attn_out; rmsnorm(residual, post_attention_norm) -> gate|up image
-    norm_proj(s->X, s->T, s->R, L.post_norm, L.gate_up, s->FF);
+    norm_proj(s->X, s->T, s->R, L.post_norm, L.gate_up, s->FF, out_send);
     chk(launch_pdl(swiglu_quant_kernel, dim3(d.nffl / 256), dim3(256), 0, st, (const float *)s->FF,
                    (const float *)(s->FF + d.nffl), L.down->dtype == Q4K ? s->img4 : (uint8_t *)nullptr,
                    L.down->dtype == Q6K ? s->img6 : (uint8_t *)nullptr),
         "swiglu");
-    nl += launch_gemv_img(s, L.down, s->F, &rc);
-    allreduce(s->F, d.n);
+    nl += launch_gemv_img(s, L.down, s->F, &rc, down_send);
+    if (!down_send) allreduce(s->F, d.n);
+    down_sent = down_send;
   }
   // l_out of the last layer -> output norm -> LM head + greedy argmax
   norm(s->R, s->F, s->X, m->out_norm, m->output->dtype == Q4K, m->output->dtype == Q6K, true);

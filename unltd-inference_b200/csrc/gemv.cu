@@ -170,7 +170,31 @@ struct Params {
   // non-null: x in f32 (dim_in elements, 16-byte aligned), quantized into the
   // CTA's image in the prologue instead of by a separate prep kernel
   const float *xq;
+  // tensor-parallel row-split sum over NVLink peer memory, the all-reduce
+  // protocol of the peer kernel split in two (peer_n > 0):
+  // peer_send: the chain stores each y row into this rank's slot of every
+  //   rank's receive area (not into y); the last CTA raises this rank's flag
+  //   in every area and advances the all-reduce counter
+  // peer_recv (with the fused norm): the prologue waits for every rank's
+  //   flag and takes b = the slots summed in rank order
+  uint8_t *peer_map[kPeerMaxRanks];
+  unsigned *peer_ctr, *peer_done;
+  int peer_rank, peer_n, peer_send, peer_recv;
 };
+
+__device__ __forceinline__ unsigned peer_ld_acquire(const unsigned *p) {
+  unsigned v;
+  asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
+__device__ __forceinline__ void peer_st_release(unsigned *p, unsigned v) {
+  asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+// slot `src` of parity (ep & 1) in the area `area`
+__device__ __forceinline__ float *peer_slot(uint8_t *area, unsigned ep, int src) {
+  return reinterpret_cast<float *>(area + kPeerFlagBytes + (size_t)(ep & 1u) * kPeerMaxRanks * kPeerSlotBytes +
+                                   (size_t)src * kPeerSlotBytes);
+}
 
 __device__ __forceinline__ uint4 lds128(const uint8_t *p) { return *reinterpret_cast<const uint4 *>(p); }
 __device__ __forceinline__ uint2 lds64(const uint8_t *p) { return *reinterpret_cast<const uint2 *>(p); }
@@ -867,6 +891,26 @@ __device__ __forceinline__ void tc_norm_prologue(const Params &P, uint8_t *ximg)
   __shared__ float s_mean;
   const int t = threadIdx.x, warp = t >> 5, lane = t & 31, n = P.nn, nsp = n >> 8;
   const bool cta0 = blockIdx.x == 0;
+  if (P.peer_recv) {
+    // every rank's partial rows must have landed here: wait (bounded) for its
+    // flag to reach this all-reduce's number
+    if (t < P.peer_n) {
+      const unsigned ep = *P.peer_ctr;
+      const unsigned *flag = reinterpret_cast<const unsigned *>(P.peer_map[P.peer_rank]) + t;
+      if (peer_ld_acquire(flag) - ep > 0x7fffffffu) {
+        const uint64_t t0 = global_ns();
+        for (uint32_t it = 1;; ++it) {
+          if (peer_ld_acquire(flag) - ep <= 0x7fffffffu) break;
+          if ((it & 255u) == 0 && global_ns() - t0 > 2000000000ull) {
+            atomicExch(P.err, kErrPeer);
+            break;
+          }
+        }
+      }
+    }
+    named_bar_sync(1, NT);
+  }
+  const bool has_b = P.norm_b || P.peer_recv;
   float r[kNormSpans][8], wv[kNormSpans][8];
 #pragma unroll
   for (int u = 0; u < kNormSpans; u++) {
@@ -883,6 +927,17 @@ __device__ __forceinline__ void tc_norm_prologue(const Params &P, uint8_t *ximg)
         const float4 *pb = reinterpret_cast<const float4 *>(P.norm_b + e0);
         b0 = pb[0];
         b1 = pb[1];
+      } else if (P.peer_recv) {  // b = the ranks' partial rows, summed in rank order
+        const unsigned ep = *P.peer_ctr;
+        const float *s0 = peer_slot(P.peer_map[P.peer_rank], ep, 0) + e0;
+        b0 = __ldcv(reinterpret_cast<const float4 *>(s0));
+        b1 = __ldcv(reinterpret_cast<const float4 *>(s0) + 1);
+        for (int r = 1; r < P.peer_n; r++) {
+          const float4 *sr = reinterpret_cast<const float4 *>(peer_slot(P.peer_map[P.peer_rank], ep, r) + e0);
+          const float4 c0 = __ldcv(sr), c1 = __ldcv(sr + 1);
+          b0 = make_float4(__fadd_rn(b0.x, c0.x), __fadd_rn(b0.y, c0.y), __fadd_rn(b0.z, c0.z), __fadd_rn(b0.w, c0.w));
+          b1 = make_float4(__fadd_rn(b1.x, c1.x), __fadd_rn(b1.y, c1.y), __fadd_rn(b1.z, c1.z), __fadd_rn(b1.w, c1.w));
+        }
       }
     }
     const float av[8] = {a0.x, a0.y, a0.z, a0.w, a1.x, a1.y, a1.z, a1.w};
@@ -890,7 +945,7 @@ __device__ __forceinline__ void tc_norm_prologue(const Params &P, uint8_t *ximg)
     const float ww[8] = {w0.x, w0.y, w0.z, w0.w, w1.x, w1.y, w1.z, w1.w};
 #pragma unroll
     for (int k = 0; k < 8; k++) {
-      r[u][k] = P.norm_b ? __fadd_rn(av[k], bv[k]) : av[k];
+      r[u][k] = has_b ? __fadd_rn(av[k], bv[k]) : av[k];
       wv[u][k] = ww[k];
     }
   }
@@ -924,7 +979,15 @@ __device__ __forceinline__ void tc_norm_prologue(const Params &P, uint8_t *ximg)
       double q = 0.0;
 #pragma unroll 1
       for (int i = 0; i < n; i++) {
-        const float v = P.norm_b ? __fadd_rn(P.norm_a[i], P.norm_b[i]) : P.norm_a[i];
+        float b = 0.0f;
+        if (P.norm_b) {
+          b = P.norm_b[i];
+        } else if (P.peer_recv) {
+          const unsigned ep = *P.peer_ctr;
+          b = __ldcv(peer_slot(P.peer_map[P.peer_rank], ep, 0) + i);
+          for (int rr = 1; rr < P.peer_n; rr++) b = __fadd_rn(b, __ldcv(peer_slot(P.peer_map[P.peer_rank], ep, rr) + i));
+        }
+        const float v = has_b ? __fadd_rn(P.norm_a[i], b) : P.norm_a[i];
         q = __dadd_rn(q, (double)__fmul_rn(v, v));
       }
       s_mean = f(q);
@@ -1101,6 +1164,7 @@ __global__ void __launch_bounds__(kTcThreads, 1) gemv_tc_kernel(Params P) {
   const int k = ct & 7;
   const unsigned gm = 0xFFu << (lane & 24);
   unsigned long long best = 0ull;
+  const unsigned send_ep = P.peer_send ? *P.peer_ctr + 1u : 0u;  // the all-reduce this GEMV feeds
   for (int i = 0; i < ntiles; i++) {
     if (!mbar_wait_bounded(&intdone[i & 1], (i >> 1) & 1, P.err)) break;
     const int r0 = rb + i * P.T;
@@ -1132,6 +1196,8 @@ __global__ void __launch_bounds__(kTcThreads, 1) gemv_tc_kernel(Params P) {
       if (k == 0) {
         const int row = r0 + lr;
         if (P.y) P.y[row] = acc;
+        if (P.peer_send)  // this rank's partial row into every rank's slot
+          for (int rr = 0; rr < P.peer_n; rr++) peer_slot(P.peer_map[rr], send_ep, P.peer_rank)[row] = acc;
         if (ARGMAX) {
           const unsigned long long kk2 = argmax_key(acc, P.row0 + row);
           best = kk2 > best ? kk2 : best;
@@ -1140,6 +1206,22 @@ __global__ void __launch_bounds__(kTcThreads, 1) gemv_tc_kernel(Params P) {
     }
     __syncwarp();
     if (lane == 0) mbar_arrive(&chaindone[i & 1]);
+  }
+  if (P.peer_send) {
+    // the last CTA to finish raises this rank's flag in every area (after a
+    // system fence) and advances the all-reduce counter
+    __threadfence_system();
+    named_bar_sync(2, kTcChainWarps * 32);
+    if (ct == 0) {
+      const unsigned prev = atomicAdd(P.peer_done, 1u);
+      if (prev == gridDim.x - 1) {
+        __threadfence_system();
+        for (int rr = 0; rr < P.peer_n; rr++)
+          peer_st_release(reinterpret_cast<unsigned *>(P.peer_map[rr]) + P.peer_rank, send_ep);
+        *P.peer_ctr = send_ep;
+        *P.peer_done = 0u;
+      }
+    }
   }
   if constexpr (ARGMAX) {
     __shared__ unsigned long long cta_best[kTcChainWarps];
@@ -1386,6 +1468,12 @@ Plan plan_gemv(unltd_ctx ctx, const unltd_weight_s &w, int mode) {
   return p;
 }
 
+bool gemv_tc_eligible(unltd_ctx ctx, const unltd_weight_s &w, int mode) {
+  if (w.dtype == F32 || w.dim_out == 0) return false;
+  const Plan p = plan_gemv(ctx, w, mode);
+  return p.S >= 2 && p.mma;
+}
+
 bool gemv_norm_fusable(unltd_ctx ctx, const unltd_weight_s &w, int mode) {
   if (w.dtype != Q4K || mode != MODE_Q8K || w.dim_out == 0) return false;
   if (w.dim_in > (size_t)kNormSpans * kTcIntWarps * 256) return false;
@@ -1491,6 +1579,16 @@ int32_t gemv_launch(unltd_ctx ctx, const GemvArgs &a) {
   P.norm_img6 = fuse ? a.norm->img6_out : nullptr;
   P.nn = fuse ? (int)w.dim_in : 0;
   P.xq = xpro ? a.x : nullptr;
+  const bool send = a.peer_send, recv = fuse && a.norm->peer_recv;
+  if ((send || recv) && (!pl.mma || am || !ctx->peer_ok || w.dim_out > kPeerMaxCount || w.dim_in > kPeerMaxCount))
+    return set_error(UNLTD_ERR_INVALID_ARG, "gemv: the peer row-split sum needs a tensor-core GEMV and peer_import");
+  for (int r = 0; r < kPeerMaxRanks; r++) P.peer_map[r] = static_cast<uint8_t *>(ctx->peer_map[r]);
+  P.peer_ctr = ctx->peer_ctr;
+  P.peer_done = ctx->peer_done;
+  P.peer_rank = ctx->rank;
+  P.peer_n = ctx->world;
+  P.peer_send = send;
+  P.peer_recv = recv;
 
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(grid);

@@ -35,8 +35,21 @@ struct unltd_ctx_s {
   void *peer_area = nullptr;
   void *peer_map[8] = {};
   unsigned *peer_ctr = nullptr;
+  unsigned *peer_done = nullptr;  // CTAs of a sending GEMV that finished (reset by the last)
   bool peer_ok = false;
 };
+
+namespace unltd {
+// Every rank's peer receive area: 64 flag words (flag[src] = the last
+// all-reduce number rank src completed writing here), then two parities x
+// kPeerMaxRanks source slots of kPeerMaxCount 8-byte words.
+constexpr int kPeerMaxRanks = 8;
+constexpr size_t kPeerMaxCount = 16384;  // floats (or u64) per all-reduce
+constexpr size_t kPeerFlagBytes = 256;
+constexpr size_t kPeerSlotBytes = kPeerMaxCount * 8;
+constexpr size_t kPeerAreaBytes = kPeerFlagBytes + 2 * kPeerMaxRanks * kPeerSlotBytes;
+constexpr int kErrPeer = 3;
+}  // namespace unltd
 
 struct unltd_weight_s {
   unltd_ctx ctx = nullptr;
@@ -81,6 +94,9 @@ struct GemvNorm {
   const float *w;
   float eps;
   uint8_t *img4_out, *img6_out;
+  // b is the tensor-parallel row-split sum received over peer memory (b
+  // null): the slots of the last all-reduce summed in rank order
+  bool peer_recv = false;
 };
 struct GemvArgs {
   const unltd_weight_s *w;
@@ -102,10 +118,16 @@ struct GemvArgs {
   // by every CTA into its own image; CTA 0 also stores r = a (+ b) to r_out
   // and the Q4_K / Q6_K images to img4_out / img6_out for later GEMVs.
   const GemvNorm *norm = nullptr;
+  // Tensor parallelism with peer_import done: instead of y, store the rows
+  // into this rank's slot of every rank's peer area and raise the flag (the
+  // consumer's fused norm receives them with GemvNorm::peer_recv).
+  bool peer_send = false;
 };
 int32_t gemv_launch(unltd_ctx ctx, const GemvArgs &a);
 // True when gemv_launch can fuse an RMSNorm of length w.dim_in into w's GEMV.
 bool gemv_norm_fusable(unltd_ctx ctx, const unltd_weight_s &w, int mode);
+// True when w's GEMV runs on the tensor-core kernel (peer row-split sums).
+bool gemv_tc_eligible(unltd_ctx ctx, const unltd_weight_s &w, int mode);
 // Grow the context's x-image scratch for w (call before stream capture).
 int32_t gemv_reserve(unltd_ctx ctx, const unltd_weight_s &w, int mode);
 void gemv_prewarm(int device);
