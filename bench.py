@@ -540,8 +540,11 @@ def main():
 
     decode = None
     if args.only is None and not args.no_decode:
-        decode = decode_bench(args.decode_tokens, with_cpu=not args.no_cpu_baseline and world == 1, rank=rank,
-                              world=world, dist=dist)
+        try:
+            decode = decode_bench(args.decode_tokens, with_cpu=not args.no_cpu_baseline and world == 1, rank=rank,
+                                  world=world, dist=dist)
+        except Exception as e:  # report it in the line; the GEMV measurement above stands
+            decode = {"error": f"{type(e).__name__}: {e}"[:400]}
 
     peak, peak_kind = _peaks()
     step_bytes = sum(it["bytes"] for it in items)
