@@ -249,4 +249,47 @@ def test_full_size_lm_head_q8k_and_argmax(ctx):
 def test_launches_are_counted(ctx):
     n0 = ctx.launch_count()
     _run(ctx, synth.quant_weights(ug.Q4K, 256, 4, seed=1), ug.Q4K, 256, 4, synth.activations(256, seed=2), ug.MODE_F32X)
-    assert ctx.launch_count() >= n0 + 3  # repack + prep + gemv
+    assert ctx.launch_count() >= n0 + 2  # repack + gemv (x quantized in the GEMV's prologue)
+
+
+def _misaligned(x):
+    """x on the device at an address 4 bytes past a 16-byte boundary: the
+    GEMV cannot load it as float4 and falls back to the prep kernel."""
+    buf = torch.zeros(x.size + 4, device="cuda")
+    v = buf[1:1 + x.size]
+    v.copy_(torch.from_numpy(x))
+    assert v.data_ptr() % 16 == 4
+    return v
+
+
+@pytest.mark.parametrize("dtype,mode", [(ug.Q4K, ug.MODE_F32X), (ug.Q6K, ug.MODE_F32X), (ug.Q8_0, ug.MODE_F32X),
+                                        (ug.Q4K, ug.MODE_Q8K), (ug.Q6K, ug.MODE_Q8K)])
+@pytest.mark.parametrize("dim_in,dim_out", [(256, 3), (4096, 300), (12288, 40), (4096 + 96, 33)])
+def test_prologue_quantization_equals_prep(ctx, dtype, mode, dim_in, dim_out):
+    """x quantized in the GEMV's own prologue (aligned x) gives the same bits
+    as the image of the separate prep kernel (misaligned x), with and without
+    the fused argmax, zero spans and outliers included."""
+    if dtype != ug.Q8_0 and dim_in % 256:
+        pytest.skip("K-quants need dim_in % 256 == 0")
+    wb = synth.quant_weights(dtype, dim_in, dim_out, seed=dim_in + 5 * dim_out)
+    w = ctx.upload(wb, dtype, dim_in, dim_out)
+    xs = [synth.activations(dim_in, seed=dim_out + 9)]
+    x2 = xs[0].copy()
+    x2[:256] = 0.0           # a zero span
+    # F32X: a non-finite last span (NaN outputs either way); Q8K: a large outlier
+    x2[-1] = np.float32(np.inf) if mode == ug.MODE_F32X else np.float32(-1e30)
+    xs.append(x2)
+    for x in xs:
+        outs = []
+        for xd in (_dev(x), _misaligned(x)):
+            y = torch.full((dim_out,), 1.0, device="cuda")
+            ctx.gemv(w, xd, y, mode)
+            tok = torch.full((1,), -1, dtype=torch.int32, device="cuda")
+            lg = torch.full((dim_out,), 2.0, device="cuda")
+            ctx.gemv_argmax(w, xd, tok, logits=lg, mode=mode)
+            ctx.synchronize()
+            outs.append((y.cpu().numpy(), lg.cpu().numpy(), int(tok.item())))
+        assert _same_bits(outs[0][0], outs[1][0])
+        assert _same_bits(outs[0][1], outs[1][1]) and _same_bits(outs[0][0], outs[0][1])
+        assert outs[0][2] == outs[1][2] == oracle.argmax(outs[0][1])
+    w.free()

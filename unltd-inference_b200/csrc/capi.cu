@@ -69,13 +69,18 @@ int32_t check_view(int dtype, size_t dim_in, size_t dim_out, size_t nbytes, cons
 
 namespace unltd {
 
-// Reads and clears the context's device error word (bounded-wait timeouts).
-int32_t check_device_error(unltd_ctx c, const char *who) {
-  int v = 0;
-  cudaError_t e = cudaMemcpy(&v, c->err, sizeof(int), cudaMemcpyDeviceToHost);
+// The error word is copied into pinned host memory behind the queued work, so
+// one synchronisation covers the results and the error check.
+int32_t sync_and_check(unltd_ctx c, cudaStream_t st, const char *who) {
+  cudaError_t e = cudaMemcpyAsync(c->err_host, c->err, sizeof(int), cudaMemcpyDeviceToHost, st);
+  if (e == cudaSuccess) e = cudaStreamSynchronize(st);
   if (e != cudaSuccess) return cuda_error(e, who);
+  const int v = *c->err_host;
   if (v == 0) return UNLTD_OK;
-  cudaMemset(c->err, 0, sizeof(int));
+  *c->err_host = 0;
+  e = cudaMemsetAsync(c->err, 0, sizeof(int), st);
+  if (e == cudaSuccess) e = cudaStreamSynchronize(st);
+  if (e != cudaSuccess) return cuda_error(e, who);
   if (v == 2) return set_error(UNLTD_ERR_INVALID_ARG, std::string(who) + ": a token id outside the vocabulary reached the embedding");
   if (v == 3) return set_error(UNLTD_ERR_TIMEOUT, std::string(who) + ": a peer all-reduce gave up waiting for another rank");
   return set_error(UNLTD_ERR_TIMEOUT, std::string(who) + ": a kernel gave up waiting on a pipeline barrier");
@@ -117,10 +122,13 @@ int32_t unltd_ctx_create(int32_t device, unltd_ctx *out) {
     c->scratch_bytes = 256 * 1024;
     e = cudaMalloc(&c->scratch, c->scratch_bytes);
   }
+  if (e == cudaSuccess) e = cudaHostAlloc(&c->err_host, 64, cudaHostAllocDefault);
+  if (e == cudaSuccess) *c->err_host = 0;
   if (e != cudaSuccess) {
     int32_t rc = cuda_error(e, "ctx_create");
     if (c->own_stream) cudaStreamDestroy(c->own_stream);
     if (c->argmax_key) cudaFree(c->argmax_key);
+    if (c->scratch) cudaFree(c->scratch);
     delete c;
     return rc;
   }
@@ -137,6 +145,7 @@ int32_t unltd_ctx_destroy(unltd_ctx c) {
   if (c->scratch) cudaFree(c->scratch);
   if (c->gemm_scratch) cudaFree(c->gemm_scratch);
   if (c->argmax_key) cudaFree(c->argmax_key);
+  if (c->err_host) cudaFreeHost(c->err_host);
   if (c->own_stream) cudaStreamDestroy(c->own_stream);
   delete c;
   return UNLTD_OK;
@@ -157,9 +166,7 @@ int32_t unltd_ctx_set_stream(unltd_ctx c, void *s) {
 int32_t unltd_ctx_synchronize(unltd_ctx c) {
   if (!c) return set_error(UNLTD_ERR_INVALID_ARG, "ctx_synchronize: NULL ctx");
   CtxGuard g(c->device);
-  int32_t rc = cuda_error(cudaStreamSynchronize(c->stream), "ctx_synchronize");
-  if (rc) return rc;
-  return check_device_error(c, "ctx_synchronize");
+  return sync_and_check(c, c->stream, "ctx_synchronize");
 }
 
 int64_t unltd_ctx_launch_count(unltd_ctx c) { return c ? c->launches.load() : -1; }
@@ -348,9 +355,8 @@ int32_t host_gemv(float *out, size_t out_len, const float *x, size_t x_len, cons
   GemvArgs a{wh, s.xbuf, s.ybuf, mode, nullptr, nullptr, nullptr};
   if ((rc = gemv_launch(s.ctx, a))) return rc;
   e = cudaMemcpyAsync(out, s.ybuf, dim_out * sizeof(float), cudaMemcpyDeviceToHost, st);
-  if (e == cudaSuccess) e = cudaStreamSynchronize(st);
   if ((rc = cuda_error(e, who))) return rc;
-  return check_device_error(s.ctx, who);
+  return sync_and_check(s.ctx, st, who);
 }
 
 }  // namespace

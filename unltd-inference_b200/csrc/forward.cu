@@ -1874,8 +1874,7 @@ int32_t unltd_qwen35_feed(unltd_qwen35_session s, const uint32_t *tokens, int32_
     if (!rc) rc = run_step(s);
   }
   if (!rc && next_token && n > 0) rc = cuda_error(cudaMemcpyAsync(next_token, s->cur_token, 4, cudaMemcpyDeviceToHost, st), "qwen35_feed");
-  if (!rc) rc = cuda_error(cudaStreamSynchronize(st), "qwen35_feed");
-  if (!rc) rc = check_device_error(s->ctx, "qwen35_feed");
+  if (!rc) rc = sync_and_check(s->ctx, st, "qwen35_feed");
   if (!rc) s->host_pos += n;
   return rc;
 }
@@ -1897,8 +1896,7 @@ int32_t unltd_qwen35_decode(unltd_qwen35_session s, uint32_t token, int32_t n_st
   for (int i = 0; !rc && i < n_steps; i++) rc = run_step(s);
   if (!rc && n_steps > 0)
     rc = cuda_error(cudaMemcpyAsync(tokens_out, s->hist, (size_t)n_steps * 4, cudaMemcpyDeviceToHost, st), "qwen35_decode");
-  if (!rc) rc = cuda_error(cudaStreamSynchronize(st), "qwen35_decode");
-  if (!rc) rc = check_device_error(s->ctx, "qwen35_decode");
+  if (!rc) rc = sync_and_check(s->ctx, st, "qwen35_decode");
   if (!rc) s->host_pos += n_steps;
   return rc;
 }

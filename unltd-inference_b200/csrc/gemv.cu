@@ -117,6 +117,82 @@ __global__ void __launch_bounds__(kThreads) prep_f32x(const float *__restrict__ 
   }
 }
 
+// prep_f32x's arithmetic for one span by one warp, lane l holding elements
+// 8l .. 8l+7 of v: the same amax, exponent, xi and scale (and, for Q4_K, the
+// same integer half sums), so a GEMV whose prologue writes its image this way
+// gives the same bits as one fed by prep_f32x.
+template <int FMT>
+__device__ __forceinline__ void f32x_span_write_warp(const float (&v)[8], int lane, uint8_t *im) {
+  float amax = 0.0f;
+  bool bad = false;
+#pragma unroll
+  for (int k = 0; k < 8; k++) {
+    bad |= !isfinite(v[k]);
+    amax = fmaxf(amax, fabsf(v[k]));
+  }
+#pragma unroll
+  for (int o = 16; o; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
+  bad = __any_sync(0xffffffffu, bad);
+  int ex = 0;
+  frexpf(amax, &ex);
+  int xi[8];
+#pragma unroll
+  for (int k = 0; k < 8; k++) xi[k] = amax > 0.0f ? __float2int_rn(ldexpf(v[k], 22 - ex)) : 0;
+  float xs = amax > 0.0f ? ldexpf(1.0f, ex - 22) : 0.0f;
+  if (bad) xs = __int_as_float(0x7fc00000);
+#pragma unroll
+  for (int k = 0; k < 8; k++) {
+    const int pos = f32x_pos<FMT>(8 * lane + k);
+    im[pos] = (uint8_t)(xi[k] >> 16);
+    im[256 + pos] = (uint8_t)((xi[k] >> 8) & 0xFF);
+    im[512 + pos] = (uint8_t)(xi[k] & 0xFF);
+  }
+  if (lane == 0) *reinterpret_cast<float *>(im + kImgF32X_XS) = xs;
+  if constexpr (FMT == Q4K) {
+    // half sums for the min term: elements of class < 4 / >= 4 of nibble
+    // group (p, half); the four lanes l with the same l >> 2 share them
+    int s0 = xi[0] + xi[1] + xi[2] + xi[3], s1 = xi[4] + xi[5] + xi[6] + xi[7];
+    s0 += __shfl_xor_sync(0xffffffffu, s0, 1);
+    s1 += __shfl_xor_sync(0xffffffffu, s1, 1);
+    s0 += __shfl_xor_sync(0xffffffffu, s0, 2);
+    s1 += __shfl_xor_sync(0xffffffffu, s1, 2);
+    if ((lane & 3) == 0) {
+      const int p = lane >> 3, half = (lane >> 2) & 1;
+      float *xsum = reinterpret_cast<float *>(im + kImgF32X_XSUM);
+      xsum[2 * (2 * p) + half] = (float)s0 * xs;
+      xsum[2 * (2 * p + 1) + half] = (float)s1 * xs;
+    }
+  }
+}
+
+// F32X image of an f32 x (16-byte aligned) in a GEMV's prologue: warp w of
+// nw takes spans w, w + nw, ...; elements past dim_in (a Q8_0 row whose last
+// span is partial) are zero, as in prep_f32x.
+template <int FMT>
+__device__ __noinline__ void f32x_prologue(const float *__restrict__ x, int dim_in, int nsp, uint8_t *ximg, int nw) {
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  for (int s0 = warp; s0 < nsp; s0 += 3 * nw) {
+    float4 v[3][2];
+#pragma unroll
+    for (int q = 0; q < 3; q++) {
+      const int e0 = (s0 + nw * q) * 256 + 8 * lane;
+      v[q][0] = v[q][1] = make_float4(0.f, 0.f, 0.f, 0.f);
+      if (s0 + nw * q < nsp && e0 < dim_in) {  // dim_in is a multiple of 32: all 8 in or all out
+        const float4 *p = reinterpret_cast<const float4 *>(x + e0);
+        v[q][0] = p[0];
+        v[q][1] = p[1];
+      }
+    }
+#pragma unroll
+    for (int q = 0; q < 3; q++) {
+      const int span = s0 + nw * q;
+      if (span >= nsp) break;
+      const float e[8] = {v[q][0].x, v[q][0].y, v[q][0].z, v[q][0].w, v[q][1].x, v[q][1].y, v[q][1].z, v[q][1].w};
+      f32x_span_write_warp<FMT>(e, lane, ximg + (size_t)span * kImgF32X);
+    }
+  }
+}
+
 // Exact restatement of quantize_q8_k (quants.rs:250-290), one span per CTA.
 template <int FMT>
 __global__ void __launch_bounds__(kThreads) prep_q8k(const float *__restrict__ x, size_t dim_in,
@@ -732,7 +808,9 @@ __global__ void __launch_bounds__(NW * 32 + 32, 1) gemv_kernel(Params P) {
 
   // ---------------- consumers ---------------------------------------------
   pdl_wait();
-  {
+  if (MODE == MODE_F32X && P.xq) {
+    f32x_prologue<FMT>(P.xq, FMT == Q8_0 ? 32 * P.nb : 256 * P.nb, P.nbu, ximg, kCW);
+  } else {
     const uint4 *src = reinterpret_cast<const uint4 *>(P.img);
     uint4 *dst = reinterpret_cast<uint4 *>(ximg);
     for (int i = threadIdx.x; i < P.img_bytes / 16; i += kCons) dst[i] = src[i];
@@ -1513,8 +1591,12 @@ int32_t gemv_launch(unltd_ctx ctx, const GemvArgs &a) {
     if (!g.a || !g.w) return set_error(UNLTD_ERR_INVALID_ARG, "gemv: fused RMSNorm needs a and w");
   }
   const Plan pl = plan_gemv(ctx, w, mode);
-  // tensor-core GEMV of a plain f32 x: quantized in its own prologue
-  const bool xpro = pl.mma && mode == MODE_Q8K && !a.img && !fuse && !am && a.x && (uintptr_t)a.x % 16 == 0;
+  // a plain f32 x is quantized in the GEMV's own prologue (Q8_K images on the
+  // tensor-core kernel, F32X images on the DP4A kernel), no prep launch. The
+  // argmax state needs no reset there: the last CTA of every argmax GEMV
+  // leaves it zero, and the context starts with it zero.
+  const bool xpro = !a.img && !fuse && a.x && (uintptr_t)a.x % 16 == 0 &&
+                    ((pl.mma && mode == MODE_Q8K) || (!pl.mma && mode == MODE_F32X));
   if (!a.img && !fuse && !xpro) {
     if (int32_t rc = gemv_reserve(ctx, w, mode)) return rc;
   }

@@ -23,6 +23,9 @@ struct unltd_ctx_s {
   unsigned int *argmax_done = nullptr;
   // Device error word: kernels write a nonzero code on a bounded-wait timeout.
   int *err = nullptr;
+  // Pinned host copy of the error word: read back with the call's own results
+  // so a synchronous call needs one stream synchronisation, not two.
+  int *err_host = nullptr;
   // Scratch of the prefill GEMM (bf16 copy of X), grown on demand.
   uint8_t *gemm_scratch = nullptr;
   size_t gemm_scratch_bytes = 0;
@@ -80,7 +83,9 @@ struct CtxGuard {
 // Thread-local error message behind unltd_last_error().
 int32_t set_error(int32_t status, const std::string &msg);
 int32_t cuda_error(cudaError_t e, const char *what);
-int32_t check_device_error(unltd_ctx c, const char *who);
+// Waits for the work queued on `st` and reads c's device error word in the
+// same round trip; a nonzero word is cleared and returned as an error status.
+int32_t sync_and_check(unltd_ctx c, cudaStream_t st, const char *who);
 
 // weights.cu
 cudaError_t launch_repack(const unltd_weight_s &w, const uint8_t *raw_dev, size_t row0_local,
