@@ -210,6 +210,24 @@ def test_reference_signature_host_api(ctx):
         ug.gemv_quant(out, x, wb, dim_in, dim_out, dtype)
         truth = oracle.gemv_quant_f64(x, wb, dim_in, dim_out, dtype)
         assert np.max(np.abs(out - truth)) <= F32X_NORMWISE * np.max(np.abs(truth))
+    # out in pinned (device-mapped) host memory: the GEMV writes it directly
+    pinned = torch.full((dim_out,), float("nan")).pin_memory().numpy()
+    for dtype in (ug.Q4K, ug.Q6K):
+        wb = synth.quant_weights(dtype, dim_in, dim_out, seed=44)
+        x = synth.activations(dim_in, seed=45)
+        ug.gemv_quant_q8k(pinned, x, wb, dim_in, dim_out, dtype)
+        assert _same_bits(pinned, oracle.gemv_quant_q8k(x, wb, dim_in, dim_out, dtype))
+    # one buffer rewritten in place with other weights: the cache, keyed by
+    # the pointer, notices (sampled fingerprint) and uploads again
+    buf = synth.quant_weights(ug.Q4K, dim_in, dim_out, seed=47).copy()
+    for seed in (47, 48):
+        buf[:] = synth.quant_weights(ug.Q4K, dim_in, dim_out, seed=seed)
+        ug.gemv_quant_q8k(pinned, x, buf, dim_in, dim_out, ug.Q4K)
+        assert _same_bits(pinned, oracle.gemv_quant_q8k(x, buf, dim_in, dim_out, ug.Q4K))
+    wq = synth.quant_weights(ug.Q8_0, dim_in, dim_out, seed=46)
+    ug.gemv_quant(pinned, x, wq, dim_in, dim_out, ug.Q8_0)
+    truth = oracle.gemv_quant_f64(x, wq, dim_in, dim_out, ug.Q8_0)
+    assert np.max(np.abs(pinned - truth)) <= F32X_NORMWISE * np.max(np.abs(truth))
     wb = synth.quant_weights(ug.Q4K, 4096, 1, seed=43)
     out = np.zeros(4096, np.float32)
     ug.dequantize_q4_k(out, wb)

@@ -2,6 +2,7 @@
 // the reference-signature host-buffer API. See include/unltd_gpu.h.
 #include <cuda_runtime.h>
 
+#include <algorithm>
 #include <cstdio>
 #include <cstring>
 #include <map>
@@ -299,10 +300,31 @@ struct HostState {
   std::mutex mu;
   int device = 0;
   unltd_ctx ctx = nullptr;
-  std::map<std::tuple<const void *, size_t, int, size_t, size_t>, unltd_weight> cache;
+  struct Cached {
+    unltd_weight w;
+    uint64_t fp;  // sampled fingerprint of the bytes uploaded
+  };
+  std::map<std::tuple<const void *, size_t, int, size_t, size_t>, Cached> cache;
   float *xbuf = nullptr, *ybuf = nullptr;
   size_t xcap = 0, ycap = 0;
 };
+
+// FNV-1a over the first and last 64 bytes and 64 words spread over the view:
+// a cheap check that the bytes behind a cached pointer are still the ones
+// uploaded (an address freed and reused by other weights of the same size).
+// The reference reads w afresh on every call; weights rewritten in place in
+// only a few bytes are not caught, and need unltd_forget_host_weights.
+uint64_t view_fingerprint(const uint8_t *w, size_t n) {
+  uint64_t h = 1469598103934665603ull;
+  auto mix = [&](const uint8_t *p, size_t len) {
+    for (size_t i = 0; i < len; i++) h = (h ^ p[i]) * 1099511628211ull;
+  };
+  mix(w, std::min<size_t>(n, 64));
+  if (n > 64) mix(w + n - std::min<size_t>(n - 64, 64), std::min<size_t>(n - 64, 64));
+  if (n >= 8 * 64)
+    for (size_t i = 0; i < 64; i++) mix(w + (n / 64) * i, 8);
+  return h;
+}
 
 HostState &hs() {
   static HostState s;
@@ -339,23 +361,41 @@ int32_t host_gemv(float *out, size_t out_len, const float *x, size_t x_len, cons
   CtxGuard g(s.ctx->device);
   auto key = std::make_tuple((const void *)w, w_len, (int)dtype, dim_in, dim_out);
   auto it = s.cache.find(key);
+  const uint64_t fp = view_fingerprint(w, w_len);
+  if (it != s.cache.end() && it->second.fp != fp) {  // other bytes at this address: upload again
+    unltd_weight_free(it->second.w);
+    s.cache.erase(it);
+    it = s.cache.end();
+  }
   unltd_weight wh;
   if (it == s.cache.end()) {
     rc = unltd_weight_upload(s.ctx, w, w_len, dtype, dim_in, dim_out, &wh);
     if (rc) return rc;
-    s.cache[key] = wh;
+    s.cache[key] = HostState::Cached{wh, fp};
   } else {
-    wh = it->second;
+    wh = it->second.w;
   }
   if ((rc = ensure_buf(&s.xbuf, &s.xcap, dim_in))) return rc;
-  if ((rc = ensure_buf(&s.ybuf, &s.ycap, dim_out))) return rc;
+  // `out` in page-locked host memory mapped into the device's address space
+  // (cudaHostAlloc / cudaHostRegister): the GEMV stores y there itself, over
+  // the bus while it runs, and no copy follows; otherwise y goes through a
+  // device buffer and one copy.
+  float *ydev = nullptr;
+  cudaPointerAttributes pa{};
+  if (cudaPointerGetAttributes(&pa, out) == cudaSuccess && pa.type == cudaMemoryTypeHost && pa.devicePointer)
+    ydev = static_cast<float *>(pa.devicePointer);
+  else
+    cudaGetLastError();  // pageable memory: not an error
+  if (!ydev && (rc = ensure_buf(&s.ybuf, &s.ycap, dim_out))) return rc;
   cudaStream_t st = s.ctx->stream;
   cudaError_t e = cudaMemcpyAsync(s.xbuf, x, dim_in * sizeof(float), cudaMemcpyHostToDevice, st);
   if (e != cudaSuccess) return cuda_error(e, who);
-  GemvArgs a{wh, s.xbuf, s.ybuf, mode, nullptr, nullptr, nullptr};
+  GemvArgs a{wh, s.xbuf, ydev ? ydev : s.ybuf, mode, nullptr, nullptr, nullptr};
   if ((rc = gemv_launch(s.ctx, a))) return rc;
-  e = cudaMemcpyAsync(out, s.ybuf, dim_out * sizeof(float), cudaMemcpyDeviceToHost, st);
-  if ((rc = cuda_error(e, who))) return rc;
+  if (!ydev) {
+    e = cudaMemcpyAsync(out, s.ybuf, dim_out * sizeof(float), cudaMemcpyDeviceToHost, st);
+    if ((rc = cuda_error(e, who))) return rc;
+  }
   return sync_and_check(s.ctx, st, who);
 }
 
@@ -374,7 +414,7 @@ int32_t unltd_set_default_device(int32_t device) {
 int32_t unltd_forget_host_weights(void) {
   HostState &s = hs();
   std::lock_guard<std::mutex> lk(s.mu);
-  for (auto &kv : s.cache) unltd_weight_free(kv.second);
+  for (auto &kv : s.cache) unltd_weight_free(kv.second.w);
   s.cache.clear();
   return UNLTD_OK;
 }
