@@ -42,13 +42,28 @@ def repack_q4k_block(blk: np.ndarray):
 
 
 def repack_q6k_block(blk: np.ndarray):
+    """repack_q6k (weights.cu): ql and qh permuted within 16-byte chunks, qh
+    stored with the top bit of every 2-bit field flipped (^ 0xAA)."""
     ql = np.zeros(128, np.uint8)
     qh = np.zeros(64, np.uint8)
     o = np.arange(128)
     ql[16 * (o >> 4) + q6_pic(o & 15)] = blk[o]
     o = np.arange(64)
-    qh[16 * (o >> 4) + q6_pic(o & 15)] = blk[128 + o]
+    qh[16 * (o >> 4) + q6_pic(o & 15)] = blk[128 + o] ^ 0xAA
     return ql, qh, blk[192:208].view(np.int8).astype(np.int64), blk[208:210].view(np.float16)[0]
+
+
+def q6_a4_bytes(wl: np.ndarray, wh: np.ndarray, sl: int, hh: int) -> np.ndarray:
+    """Bytes of q6_a4_lo (hh = 0) / q6_a4_hi (hh = 1) from device ql / qh
+    bytes, as signed values: no sign flip of their own (the stored qh carries
+    it)."""
+    wl, wh = wl.astype(np.int64), wh.astype(np.int64)
+    if hh == 0:
+        b = ((wl << 2) & 0x3C) | ((wh << (6 - sl)) & 0xC0)
+    else:
+        b = ((wl >> 2) & 0x3C) | ((wh << (2 - sl)) & 0xC0)
+    b &= 0xFF
+    return np.where(b >= 128, b - 256, b)
 
 
 def _bytes(words_u8: np.ndarray) -> np.ndarray:
@@ -139,9 +154,12 @@ def q6k_block_sumi_model(blk: np.ndarray, q8: np.ndarray):
         wh = _bytes(qh[16 * (2 * h + (u & 1)): 16 * (2 * h + (u & 1)) + 16]).reshape(4, 4)
         sc_lo, sc_hi = sc[8 * h + u], sc[8 * h + 4 + u]
         for t in range(4):
-            raw_lo = (wl[t] & 0xF) | (((wh[t] >> sl) & 3) << 4)
-            raw_hi = (wl[t] >> 4) | (((wh[t] >> (sl + 4)) & 3) << 4)
+            whr = wh[t] ^ 0xAA  # the stored qh is flipped
+            raw_lo = (wl[t] & 0xF) | (((whr >> sl) & 3) << 4)
+            raw_hi = (wl[t] >> 4) | (((whr >> (sl + 4)) & 3) << 4)
             a_lo, a_hi = 4 * (raw_lo - 32), 4 * (raw_hi - 32)
+            assert np.array_equal(a_lo, q6_a4_bytes(wl[t], wh[t], sl, 0))
+            assert np.array_equal(a_hi, q6_a4_bytes(wl[t], wh[t], sl, 1))
             P[j, 2 * t] += sc_lo * int((a_lo * A[j, 0, t]).sum()) + sc_hi * int((a_hi * A[j, 1, t]).sum())
             P[j, 2 * t + 1] += sc_lo * int((a_lo * B[j, 0, t]).sum()) + sc_hi * int((a_hi * B[j, 1, t]).sum())
     tot = P.sum(0)
@@ -199,9 +217,7 @@ def q6k_rows_mma_model(blks: list, q8: np.ndarray) -> np.ndarray:
                 for t in range(4):
                     wl = ql[16 * j + 4 * t: 16 * j + 4 * t + 4].astype(np.int64)
                     wh = qh[16 * c + 4 * t: 16 * c + 4 * t + 4].astype(np.int64)
-                    nib = (wl & 0xF) if hh == 0 else (wl >> 4)
-                    hi2 = (wh >> (sl + 4 * hh)) & 3
-                    A[r, 4 * t: 4 * t + 4] = 4 * ((nib | (hi2 << 4)) - 32)
+                    A[r, 4 * t: 4 * t + 4] = q6_a4_bytes(wl, wh, sl, hh)
             B = np.zeros((16, 8), np.int64)
             for n in range(8):
                 for t in range(4):
@@ -263,3 +279,33 @@ def q4k_block_f32x_model(blk: np.ndarray, x: np.ndarray) -> float:
         xsh = float(img[o_hi:o_hi + 16].sum()) * xs
         tot += d * xs * F - dmin * (m_lo * xsl + m_hi * xsh)
     return tot
+
+
+def q4k_minsum_mma_model(hdrs: list, q8: np.ndarray) -> np.ndarray:
+    """minsum of 16 Q4_K rows (one block each) through the fragments of the
+    min-term MMA in q4k_q8k_mma_item: m16n8k16 int8, A[r][4t+i] = byte i of
+    lane (r, t)'s A word (tig 0: mins of groups 0..3 = hdr bytes 8..11 & 63;
+    tig 1: groups 4..7 from the packed high bits; tig 2, 3: zero), B[4t+i][n]
+    = byte i of lane (n, t)'s XBlock::bm (n = 0: balanced low bytes, n = 1:
+    high bytes of the eight group sums); minsum = D[r][0] + 256 D[r][1]."""
+    gs = q8.astype(np.int64).reshape(8, 32).sum(1)
+    lo = ((gs + 128) & 255) - 128
+    hi = (gs - lo) >> 8
+    assert np.all(np.abs(hi) < 128)
+    B = np.zeros((16, 8), np.int64)
+    for t in range(2):
+        for i in range(4):
+            B[4 * t + i, 0] = lo[4 * t + i]
+            B[4 * t + i, 1] = hi[4 * t + i]
+    A = np.zeros((16, 16), np.int64)
+    for r, hdr in enumerate(hdrs):
+        w = hdr.astype(np.uint32)
+        z = int(w[8]) | int(w[9]) << 8 | int(w[10]) << 16 | int(w[11]) << 24   # header word .z
+        ww = int(w[12]) | int(w[13]) << 8 | int(w[14]) << 16 | int(w[15]) << 24  # header word .w
+        ma = z & 0x3F3F3F3F
+        mb = ((ww >> 4) & 0x0F0F0F0F) | ((z >> 2) & 0x30303030)
+        for i in range(4):
+            A[r, i] = (ma >> (8 * i)) & 0xFF
+            A[r, 4 + i] = (mb >> (8 * i)) & 0xFF
+    D = A @ B
+    return D[:, 0] + 256 * D[:, 1]

@@ -94,3 +94,19 @@ def test_q6k_mma_fragments_match_reference(seed):
     got = km.q6k_rows_mma_model(blks, q8)
     for r in range(16):
         assert np.array_equal(got[r], km.q6k_block_sumi_reference(blks[r], q8))
+
+
+@pytest.mark.parametrize("seed", [0, 1, 2])
+def test_q4k_minsum_mma_fragments_match_reference(seed):
+    # the Q4_K item's min-term MMA (6-bit mins x group sums split into two
+    # byte columns) gives the reference's minsum for 16 rows, extreme q8 too
+    import synth
+    rng = np.random.default_rng(seed)
+    wb = synth.quant_weights(synth.Q4K, 256, 16, seed=200 + seed)
+    blks = [wb[r * 144:(r + 1) * 144] for r in range(16)]
+    for q8 in (rng.integers(-127, 128, size=256), np.full(256, 127), np.full(256, -127),
+               np.where(np.arange(256) % 3 == 0, 127, -127)):
+        q8 = q8.astype(np.int64)
+        got = km.q4k_minsum_mma_model([km.repack_q4k_block(b)[0] for b in blks], q8)
+        for r in range(16):
+            assert got[r] == km.q4k_block_sumi_reference(blks[r], q8)[1]

@@ -191,10 +191,14 @@ struct RecrArgs {
   const float *convw;   // ssm_conv1d.weight as stored, [channel][tau]
   const float *dt_bias, *ssm_a, *ssm_norm;
   float *state;         // nv x HD x HD, state[h][i][j]
-  float *y;             // nv*HD gated output
+  float *y;             // nv*HD GDN output (before the gated norm)
   const int *pos;
   int K, nqk, nv, dconv, z_off, beta_off, alpha_off;
   float eps;
+  // per 256-element span of y: CTAs done (the last one runs the gated norm
+  // and writes the span's Q8_K image(s) of ssm_out's input, then resets it)
+  unsigned *span_ctr;
+  uint8_t *img4, *img6;
 };
 
 // One CTA per (v-head h, quarter of its columns), one thread per channel of
@@ -251,6 +255,71 @@ __device__ __forceinline__ float gdn_dot(const float (&st)[RW], const float *xw,
     __syncwarp();
   }
   return r;
+}
+
+// The gated norm of the recurrent output (qwen35_forward.rs:482-498) for one
+// 256-element span of y (two heads of HD = 128), by the CTA that completed
+// the span: per head rmsnorm with ssm_norm (the reference's f64 sum of
+// squares, resolved exactly), times silu(z), then the span's Q8_K image(s)
+// (quantize_q8_k) by warp 0. Thread j takes column j of both heads.
+template <int HD>
+__device__ __noinline__ void gated_norm_span(const float *y, const float *z, const float *ssm_norm, float eps,
+                                             uint8_t *img4, uint8_t *img6, int span) {
+  static_assert(HD == 128, "a span holds two heads of 128");
+  __shared__ double red2[2][HD / 32];
+  __shared__ float so[256];
+  __shared__ float s_mean2[2];
+  const int j = threadIdx.x, lane = j & 31, wp = j >> 5;
+  const size_t e0 = (size_t)span * 256;
+  float x[2];
+  double S[2];
+#pragma unroll
+  for (int hh = 0; hh < 2; hh++) {
+    x[hh] = __ldcg(y + e0 + hh * HD + j);  // written by other CTAs of this grid
+    so[hh * HD + j] = x[hh];
+    S[hh] = (double)__fmul_rn(x[hh], x[hh]);
+#pragma unroll
+    for (int off = 16; off; off >>= 1) S[hh] += __shfl_xor_sync(~0u, S[hh], off);
+    if (lane == 0) red2[hh][wp] = S[hh];
+  }
+  __syncthreads();
+  const MeanOf f{HD};
+  float mean[2];
+  bool ok[2];
+#pragma unroll
+  for (int hh = 0; hh < 2; hh++) {
+    S[hh] = 0.0;
+#pragma unroll
+    for (int w = 0; w < HD / 32; w++) S[hh] += red2[hh][w];
+    ok[hh] = resolve_sum(S[hh], S[hh], HD, f, &mean[hh]);  // uniform over the CTA
+  }
+  if (!ok[0] || !ok[1]) {
+    if (j < 2 && !ok[j]) {  // rare: the reference's left-to-right sum
+      double q = 0.0;
+#pragma unroll 1
+      for (int i = 0; i < HD; i++) q = __dadd_rn(q, (double)__fmul_rn(so[j * HD + i], so[j * HD + i]));
+      s_mean2[j] = f(q);
+    }
+    __syncthreads();
+    if (!ok[0]) mean[0] = s_mean2[0];
+    if (!ok[1]) mean[1] = s_mean2[1];
+  }
+  __syncthreads();  // so[] is overwritten below
+  const float wj = ssm_norm[j];
+#pragma unroll
+  for (int hh = 0; hh < 2; hh++) {
+    const float scale = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(mean[hh], eps)));
+    const float yn = __fmul_rn(__fmul_rn(x[hh], scale), wj);
+    so[hh * HD + j] = __fmul_rn(yn, silu_f(z[e0 + hh * HD + j]));
+  }
+  __syncthreads();
+  if (wp == 0) {
+    float v[8];
+#pragma unroll
+    for (int k = 0; k < 8; k++) v[k] = so[8 * lane + k];
+    q8k_span_write_warp(v, lane, img4 ? img4 + (size_t)span * kImgQ8K4 : nullptr,
+                        img6 ? img6 + (size_t)span * kImgQ8K6 : nullptr);
+  }
 }
 
 template <int HD, int KT>  // KT: conv_kernel known at compile time (0: a.K at run time)
@@ -389,48 +458,25 @@ __global__ void __launch_bounds__(HD) recr_mid_kernel(RecrArgs a) {
   if (w == 0) a.y[h * HD + c0 + jc] = __fmul_rn(dq, __fdiv_rn(1.0f, __fsqrt_rn((float)HD)));
 #pragma unroll
   for (int ii = 0; ii < RW; ii++) S[(size_t)(RW * w + ii) * HD] = st[ii];
-}
 
-// The gated norm of the recurrent output (qwen35_forward.rs:482-498) fused
-// with the Q8_K image of ssm_out's input: per head, rmsnorm of the GDN output
-// with ssm_norm, times silu(z). One CTA per 256-element span (256 / HD heads).
-template <int HD>
-__global__ void __launch_bounds__(256) gated_norm_quant_kernel(const float *o, const float *z, const float *w,
-                                                               float eps, uint8_t *img4, uint8_t *img6) {
-  pdl_trigger();
-  __shared__ double red[16];
-  __shared__ float s_mean[256 / HD];
-  __shared__ float so[256];
-  __shared__ Q8KSpanSmem sm;
-  pdl_wait();
-  const int span = blockIdx.x, t = threadIdx.x, e = span * 256 + t;
-  const int hl = t / HD, jj = t % HD;  // head within the span, column
-  const float x = o[e];
-  so[t] = x;
-  // per-head sums: warps of one head reduce together
-  double S = (double)__fmul_rn(x, x);
-#pragma unroll
-  for (int off = 16; off; off >>= 1) S += __shfl_xor_sync(~0u, S, off);
-  if ((t & 31) == 0) red[t >> 5] = S;
+  // the last of the CTAs writing this 256-element span of y (its 256 / HD
+  // heads x the quarters) runs the gated norm of the span: y is published by
+  // a fence before the count, read after it (no waiting on other CTAs)
+  __shared__ unsigned s_last;
+  const int span = (h * HD) >> 8;
+  __threadfence();
   __syncthreads();
-  S = 0.0;
-  for (int w8 = hl * (HD / 32); w8 < (hl + 1) * (HD / 32); w8++) S += red[w8];
-  float mean;
-  const MeanOf f{HD};
-  if (!resolve_sum(S, S, HD, f, &mean)) {  // uniform per head
-    if (jj == 0) {
-      double s = 0.0;
-#pragma unroll 1
-      for (int i = 0; i < HD; i++) s = __dadd_rn(s, (double)__fmul_rn(so[hl * HD + i], so[hl * HD + i]));
-      s_mean[hl] = f(s);
-    }
+  if (j == 0) {
+    const unsigned n = (256 / HD) * gridDim.y;
+    const unsigned prev = atomicAdd(a.span_ctr + span, 1u);
+    s_last = prev == n - 1;
+    if (prev == n - 1) a.span_ctr[span] = 0u;  // every CTA of the span has counted
   }
   __syncthreads();
-  if (!resolve_sum(S, S, HD, f, &mean)) mean = s_mean[hl];
-  const float scale = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(mean, eps)));
-  const float yn = __fmul_rn(__fmul_rn(x, scale), w[jj]);
-  q8k_span_write(__fmul_rn(yn, silu_f(z[e])), img4 ? img4 + (size_t)span * kImgQ8K4 : nullptr,
-                 img6 ? img6 + (size_t)span * kImgQ8K6 : nullptr, sm);
+  if (s_last) {
+    __threadfence();
+    gated_norm_span<HD>(a.y, a.proj + a.z_off, a.ssm_norm, a.eps, a.img4, a.img6, span);
+  }
 }
 
 // ---- full-attention layer (qwen35_forward.rs:584-686) ----------------------
@@ -873,6 +919,7 @@ struct unltd_qwen35_session_s {
   int nsplit = 0;
   uint32_t *cur_token = nullptr, *hist = nullptr, *feed = nullptr;
   int *counter = nullptr, *pos = nullptr;
+  unsigned *span_ctr = nullptr;  // recurrent layers: CTAs done per span of the GDN output
   std::vector<float *> ring, state, kc, vc;
   std::vector<void *> bufs;
   cudaGraphExec_t graph = nullptr;
@@ -1327,13 +1374,11 @@ int32_t enqueue_step(unltd_qwen35_session s) {
       a.beta_off = d.dconvl + d.nvl * d.hd;
       a.alpha_off = a.beta_off + d.nvl;
       a.eps = d.eps;
+      a.span_ctr = s->span_ctr;
+      a.img4 = L.out->dtype == Q4K ? s->img4 : nullptr;
+      a.img6 = L.out->dtype == Q6K ? s->img6 : nullptr;
       if (d.K == 4) chk(launch_pdl(recr_mid_kernel<128, 4>, dim3(d.nvl, 128 / kGdnCols), dim3(128), 0, st, a), "recr_mid");
       else chk(launch_pdl(recr_mid_kernel<128, 0>, dim3(d.nvl, 128 / kGdnCols), dim3(128), 0, st, a), "recr_mid");
-      chk(launch_pdl(gated_norm_quant_kernel<128>, dim3(d.nvl * 128 / 256), dim3(256), 0, st, (const float *)s->Y,
-                     (const float *)(s->proj + a.z_off), (const float *)L.ssm_norm, d.eps,
-                     L.out->dtype == Q4K ? s->img4 : (uint8_t *)nullptr,
-                     L.out->dtype == Q6K ? s->img6 : (uint8_t *)nullptr),
-          "gated_norm");
       nl += launch_gemv_img(s, L.out, s->T, &rc, out_send);
       if (!out_send) allreduce(s->T, d.n);
     } else {
@@ -1680,6 +1725,8 @@ int32_t unltd_qwen35_session_create(unltd_qwen35 m, int32_t ctx_len, unltd_qwen3
   if (!rc) rc = dalloc(B, &s->feed, (size_t)ctx_len + 1, "session");
   if (!rc) rc = dalloc(B, &s->counter, 1, "session");
   if (!rc) rc = dalloc(B, &s->pos, 1, "session");
+  if (!rc) rc = dalloc(B, &s->span_ctr, (size_t)d.nvl * d.hd / 256 + 1, "session");
+  if (!rc) rc = cuda_error(cudaMemset(s->span_ctr, 0, ((size_t)d.nvl * d.hd / 256 + 1) * 4), "session init");
   for (int i = 0; !rc && i < m->n_recr; i++) {
     float *r = nullptr, *st = nullptr;
     rc = dalloc(B, &r, (size_t)d.K * d.dconvl, "session ring");

@@ -295,14 +295,21 @@ __device__ __forceinline__ void mma_u8s8(uint32_t a0, uint32_t a1, uint32_t a2, 
       : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1), "r"(0));
 }
 
+// D = A(16x16 s8, row) * B(16x8 s8, col), exact int32 (tensor cores)
+__device__ __forceinline__ void mma_s8_k16(uint32_t a0, uint32_t a1, uint32_t b0, int &d0, int &d1, int &d2, int &d3) {
+  asm("mma.sync.aligned.m16n8k16.row.col.s32.s8.s8.s32 {%0,%1,%2,%3}, {%4,%5}, {%6}, {%7,%7,%7,%7};"
+      : "=r"(d0), "=r"(d1), "=r"(d2), "=r"(d3)
+      : "r"(a0), "r"(a1), "r"(b0), "r"(0));
+}
+
 // One block of the class-major Q8_K x image as the MMA B operands of this
 // lane: column n of B is class n, and lane (gid, tig) holds B[k-quad tig][gid]
 // (class 2 tig elements) and B[k-quad 4 + tig][gid] (class 2 tig + 1), nonzero
-// only when gid is that class; plus the group sums 2 tig, 2 tig + 1 (min
-// term) and the block's d.
+// only when gid is that class; plus the B operand of the min term's MMA and
+// the block's d.
 struct XBlock {
   uint32_t b0[8], b1[8];
-  int2 bs;
+  uint32_t bm;  // min term: B[k][0 | 1] = low / high byte of group sum k
   float xd;
 };
 
@@ -320,7 +327,21 @@ __device__ __forceinline__ void load_xblock(const uint8_t *im, XBlock &x) {
     x.b0[g] = own0 ? xg[g] : 0u;
     x.b1[g] = own1 ? xg[g] : 0u;
   }
-  x.bs = *reinterpret_cast<const int2 *>(im + kImgQ8K4_BS + 8 * tig);
+  // min term (m16n8k16): lane (gid, tig) holds B[4 tig .. 4 tig + 3][gid];
+  // column 0 = the balanced low bytes bl = ((s + 128) & 255) - 128 of the
+  // eight group sums s, column 1 = the high bytes (s - bl) / 256 (|s| <=
+  // 32 * 127, so both fit s8); rows 8..15 and columns 2..7 are zero
+  uint32_t bm = 0u;
+  if (gid < 2 && tig < 2) {
+    const int4 g4 = *reinterpret_cast<const int4 *>(im + kImgQ8K4_BS + 16 * tig);
+    const int gv[4] = {g4.x, g4.y, g4.z, g4.w};
+#pragma unroll
+    for (int i = 0; i < 4; i++) {
+      const int lo = ((gv[i] + 128) & 255) - 128, hi = (gv[i] - lo) >> 8;
+      bm |= (uint32_t)((gid == 0 ? lo : hi) & 0xFF) << (8 * i);
+    }
+  }
+  x.bm = bm;
   x.xd = *reinterpret_cast<const float *>(im + kImgQ8K4_D);
 }
 
@@ -332,7 +353,9 @@ __device__ __forceinline__ void load_xblock(const uint8_t *im, XBlock &x) {
 // group at once; the group scales are applied per row in int32 (exact). The
 // odd groups (high nibbles) enter as 16 x nibble and their scaled sum is
 // divided by 16 at the end (exact: every term is a multiple of 16, and the
-// sum stays below 2^31). The min term takes groups 2t, 2t+1 per thread.
+// sum stays below 2^31). The min term sum_g m_g * s_g (s_g: group sum of the
+// q8 values) is one more int8 MMA m16n8k16: A[r][k] = the 6-bit min of group
+// k of row r (k < 8), B = the group sums as two byte columns (XBlock::bm).
 __device__ __forceinline__ void q4k_q8k_mma_item(const uint8_t *tile, int nr, int g16, int b, const XBlock &x,
                                                  const Params &P, float *tk, float *tm) {
   const int lane = threadIdx.x & 31, gid = lane >> 2, tig = lane & 3;
@@ -371,17 +394,14 @@ __device__ __forceinline__ void q4k_q8k_mma_item(const uint8_t *tile, int nr, in
     hi3 += t1 * e3;
   }
   const int acc0 = lo0 + (hi0 >> 4), acc1 = lo1 + (hi1 >> 4), acc2 = lo2 + (hi2 >> 4), acc3 = lo3 + (hi3 >> 4);
-  // min term: sum over groups of m_g * (sum of group g's q8), groups 2t and 2t+1 here
+  // min term: A k-quad 0 = mins of groups 0..3 (lanes tig 0), k-quad 1 = groups
+  // 4..7 (tig 1), the rest zero; lanes tig 0 get minsum = D[r][0] + 256 D[r][1]
   const uint32_t MA0 = h0.z & 0x3F3F3F3Fu, MB0 = ((h0.w >> 4) & 0x0F0F0F0Fu) | ((h0.z >> 2) & 0x30303030u);
   const uint32_t MA1 = h1.z & 0x3F3F3F3Fu, MB1 = ((h1.w >> 4) & 0x0F0F0F0Fu) | ((h1.z >> 2) & 0x30303030u);
-  const uint32_t MM0 = tig < 2 ? MA0 : MB0, MM1 = tig < 2 ? MA1 : MB1;
-  const int k0 = (2 * tig) & 3;
-  int ms0 = byte_of(MM0, k0) * x.bs.x + byte_of(MM0, k0 + 1) * x.bs.y;
-  int ms1 = byte_of(MM1, k0) * x.bs.x + byte_of(MM1, k0 + 1) * x.bs.y;
-  ms0 += __shfl_xor_sync(0xffffffffu, ms0, 1);
-  ms1 += __shfl_xor_sync(0xffffffffu, ms1, 1);
-  ms0 += __shfl_xor_sync(0xffffffffu, ms0, 2);
-  ms1 += __shfl_xor_sync(0xffffffffu, ms1, 2);
+  int mn0, mn1, mn2, mn3;
+  mma_s8_k16(tig == 0 ? MA0 : (tig == 1 ? MB0 : 0u), tig == 0 ? MA1 : (tig == 1 ? MB1 : 0u), x.bm, mn0, mn1, mn2,
+             mn3);
+  const int ms0 = mn0 + mn1 * 256, ms1 = mn2 + mn3 * 256;
   const int rs2 = P.rs / 8;
   if (v0) {
     const float d = __fmul_rn(x.xd, h2f_bits(h0.x & 0xFFFFu)), dm = __fmul_rn(h2f_bits(h0.x >> 16), x.xd);
@@ -400,19 +420,15 @@ __device__ __forceinline__ void q4k_q8k_mma_item(const uint8_t *tile, int nr, in
 }
 
 // Q6_K: a word of 4*(raw6 - 32) as s8 from ql/qh words (2-bit field of qh at
-// shift sl for the low-nibble half, sl + 4 for the high half).
+// shift sl for the low-nibble half, sl + 4 for the high half). The device
+// layout stores qh with the top bit of every field flipped (repack_q6k), so
+// the field lands in bits 6-7 already as the sign-flipped high bits of
+// 4*raw6 - 128.
 __device__ __forceinline__ uint32_t q6_a4_lo(uint32_t ql, uint32_t qh, int sl) {
-  return (((ql << 2) & 0x3C3C3C3Cu) | ((qh << (6 - sl)) & 0xC0C0C0C0u)) ^ 0x80808080u;
+  return ((ql << 2) & 0x3C3C3C3Cu) | ((qh << (6 - sl)) & 0xC0C0C0C0u);
 }
 __device__ __forceinline__ uint32_t q6_a4_hi(uint32_t ql, uint32_t qh, int sl) {
-  return (((ql >> 2) & 0x3C3C3C3Cu) | ((qh << (2 - sl)) & 0xC0C0C0C0u)) ^ 0x80808080u;
-}
-
-// D = A(16x16 s8, row) * B(16x8 s8, col), exact int32 (tensor cores)
-__device__ __forceinline__ void mma_s8_k16(uint32_t a0, uint32_t a1, uint32_t b0, int &d0, int &d1, int &d2, int &d3) {
-  asm("mma.sync.aligned.m16n8k16.row.col.s32.s8.s8.s32 {%0,%1,%2,%3}, {%4,%5}, {%6}, {%7,%7,%7,%7};"
-      : "=r"(d0), "=r"(d1), "=r"(d2), "=r"(d3)
-      : "r"(a0), "r"(a1), "r"(b0), "r"(0));
+  return ((ql >> 2) & 0x3C3C3C3Cu) | ((qh << (2 - sl)) & 0xC0C0C0C0u);
 }
 
 // signed byte k (0..3) of w: prmt with the sign-replicate selector bit (the

@@ -8,7 +8,8 @@
 //   Q4_K  [hdr  nb x 16 B: d f16 | dmin f16 | scales[12] (unchanged)]
 //         [qs   nb x 128 B, permuted: old qs[32p + k + 8i] -> new 32p + 4k + i]
 //   Q6_K  [ql   nb x 128 B, permuted within each 16-byte chunk by PIC6]
-//         [qh   nb x 64 B,  permuted within each 16-byte chunk by PIC6]
+//         [qh   nb x 64 B,  permuted within each 16-byte chunk by PIC6, every
+//                           2-bit field's top bit flipped (byte ^ 0xAA)]
 //         [sc   nb x 16 B  (int8 scales, unchanged)]
 //         [d    nb x 2 B   (f16)]
 //   Q8_0  [qs   nb x 32 B][d nb x 2 B]          (nb = dim_in / 32 here)

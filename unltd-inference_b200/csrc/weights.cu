@@ -38,7 +38,9 @@ __global__ void repack_q6k(const uint8_t *__restrict__ raw, uint8_t *__restrict_
   uint8_t *ql = row + b * 128, *qh = row + nb * 128 + b * 64;
   uint8_t *sc = row + nb * 192 + b * 16, *d = row + nb * 208 + b * 2;
   for (int o = 0; o < 128; o++) ql[16 * (o >> 4) + q6_pic(o & 15)] = src[o];
-  for (int o = 0; o < 64; o++) qh[16 * (o >> 4) + q6_pic(o & 15)] = src[128 + o];
+  // the top bit of every 2-bit field flipped: the GEMVs' 4*(q - 32) operand
+  // words then need no sign flip of their own (q6_a4_lo / q6_a4_hi)
+  for (int o = 0; o < 64; o++) qh[16 * (o >> 4) + q6_pic(o & 15)] = src[128 + o] ^ 0xAAu;
   for (int i = 0; i < 16; i++) sc[i] = src[192 + i];
   d[0] = src[208];
   d[1] = src[209];
@@ -86,7 +88,7 @@ __global__ void dequant_q6k(const uint8_t *__restrict__ dev, float *__restrict__
   int qlo = 64 * h + (pos & 63);
   int qho = 32 * h + (pos & 31);
   uint8_t lb = row[b * 128 + 16 * (qlo >> 4) + q6_pic(qlo & 15)];
-  uint8_t hb = row[nb * 128 + b * 64 + 16 * (qho >> 4) + q6_pic(qho & 15)];
+  uint8_t hb = row[nb * 128 + b * 64 + 16 * (qho >> 4) + q6_pic(qho & 15)] ^ 0xAAu;  // stored flipped
   int nib = pos < 64 ? (lb & 0xF) : (lb >> 4);
   int hi2 = (hb >> (2 * (pos >> 5))) & 3;
   int q = (nib | (hi2 << 4)) - 32;
