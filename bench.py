@@ -384,6 +384,22 @@ def main():
             dist.destroy_process_group()
         return
 
+    # N > 1: the row-split sums and the cross-GPU argmax MAX through the
+    # library's own all-reduce (one NVLink peer kernel each; NCCL if the
+    # peer mapping is unavailable), the same on every rank
+    lib_comm = False
+    if world > 1:
+        ok = 1
+        try:
+            ctx.comm_init(rank, world, ug.exchange_unique_id())
+            ctx.peer_init()
+        except Exception as e:  # noqa: BLE001
+            print(f"library all-reduce unavailable ({e}); using torch.distributed", file=sys.stderr)
+            ok = 0
+        flag = torch.tensor([ok], device="cuda")
+        dist.all_reduce(flag, op=dist.ReduceOp.MIN)
+        lib_comm = bool(flag.item())
+
     # ---- workload ----
     items = []
     mix = [m for m in MIX if args.only is None or m[0] in args.only.split(",")]
@@ -408,6 +424,10 @@ def main():
     def run_item(it, mode=None):
         m = it["mode"] if mode is None else (ug.MODE_F32X if it["dtype"] == Q8_0 else mode)
         if it["name"].startswith("d_"):
+            if lib_comm:  # vocab shard: this shard's key, then the MAX over ranks
+                ctx.gemv_argmax_shard(it["w"], it["x"], key, it["off"], logits=it["y"], mode=m)
+                ctx.allreduce_max_u64(key, 1)
+                return
             ctx.gemv_argmax(it["w"], it["x"], tok, logits=it["y"], mode=m)
             if world > 1:
                 # local index -> global key (orderable(logit) << 32 | ~global_idx), then MAX
@@ -420,7 +440,10 @@ def main():
         else:
             ctx.gemv(it["w"], it["x"], it["y"], m)
             if world > 1 and it["split"] == "cols":
-                dist.all_reduce(it["y"])
+                if lib_comm:
+                    ctx.allreduce_sum(it["y"], it["y"].numel())
+                else:
+                    dist.all_reduce(it["y"])
 
     # the roofline's kernel: the LM head, 85% of the step's bytes
     dom = max(range(len(items)), key=lambda i: items[i]["bytes"])
@@ -571,7 +594,9 @@ def main():
         "data": "synthetic (seeded weights and x ~ N(0,1), BASELINE config 1 shapes)",
         "config": {
             "workload": "config1_mixed_gemv_decode", "gemvs": [it["name"] for it in items], "step_bytes": step_bytes,
-            "parallelism": f"tp{world}" if world > 1 else "single", "l2": "inputs larger than L2 (598 MB/step)",
+            "parallelism": f"tp{world}" if world > 1 else "single",
+            "collectives": ("library all-reduce (NVLink peer kernel)" if lib_comm else
+                            "torch.distributed NCCL") if world > 1 else None, "l2": "inputs larger than L2 (598 MB/step)",
             "mode": "Q8K_EXACT (Q8_0 in F32X)",
         },
         "per_gemv": {it["name"]: {"ms": round(per_item_ms[i], 4),
@@ -596,6 +621,9 @@ def main():
         os.write(out_fd, (json.dumps(line) + "\n").encode())
     for it in items:
         it["w"].free()
+    if dist:
+        torch.cuda.synchronize()
+        dist.barrier()  # no rank unmaps its peer area while another still sums
     ctx.close()
     if dist:
         dist.barrier()

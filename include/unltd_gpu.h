@@ -129,6 +129,16 @@ int32_t unltd_gemv(unltd_ctx ctx, unltd_weight w, const float *x_dev, float *y_d
 int32_t unltd_gemv_argmax(unltd_ctx ctx, unltd_weight w, const float *x_dev, float *logits_dev,
                           uint32_t *token_dev, int32_t mode);
 
+/* The LM head split by vocab rows across GPUs (min_forward.rs:210-266 with
+ * greedy.rs:18-27 over all shards): `w` holds rows [row0, row0 + dim_out) of
+ * the full head. Writes this shard's argmax as the 64-bit key
+ * (orderable(logit) << 32) | (0xFFFFFFFF - global row) to `key_dev`; after
+ * unltd_allreduce_max_u64 over the ranks, every rank holds the key of the
+ * first-index maximum of the whole vocabulary, token = 0xFFFFFFFF - (key &
+ * 0xFFFFFFFF). NaN rules as unltd_gemv_argmax (global row 0 only). */
+int32_t unltd_gemv_argmax_shard(unltd_ctx ctx, unltd_weight w, const float *x_dev, float *logits_dev,
+                                uint64_t *key_dev, uint32_t row0, int32_t mode);
+
 /* Batched prefill: Y[m][n] = sum_k X[m][k] * W[n][k] for m < m_tokens, X f32
  * row-major [m_tokens][dim_in], Y f32 row-major [m_tokens][dim_out]. This is
  * gemv_quant (quants.rs:422) applied to every token at once; the reference

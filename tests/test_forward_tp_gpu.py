@@ -1,5 +1,6 @@
 """Tensor-parallel decode on 2 GPUs (tests/tp_decode_check.py under torchrun)
-against the CPU oracle: identical greedy stream, logits and hidden state
+against the CPU oracle, and the sharded GEMV forms through the C ABI
+(tests/tp_shard_check.py): identical greedy stream, logits and hidden state
 within 1e-3 max-rel (the row-split projections sum partial outputs across
 GPUs, so the f32 rounding differs from the single-device reference). Both
 all-reduce paths: the NVLink peer kernel and NCCL."""
@@ -44,3 +45,24 @@ def test_tp2_tiny_decode_matches_oracle(allreduce):
     assert out["same_stream_on_all_ranks"] and out["argmax_matches_gathered_logits"]
     assert out["stream_matches_oracle"], out
     assert out["logits_maxrel"] <= TOL and out["hidden_maxrel"] <= TOL, out
+
+
+@pytest.mark.parametrize("allreduce", ["peer", "nccl"])
+def test_tp2_vocab_split_argmax_and_column_split_gemv(allreduce):
+    if not torch.cuda.is_available() or torch.cuda.device_count() < 2:
+        pytest.skip("needs 2 GPUs")
+    from __graft_entry__ import build
+
+    build()
+    env = dict(os.environ, NCCL_NVLS_ENABLE="0")
+    cmd = ["timeout", "-k", "30", "600", sys.executable, "-m", "torch.distributed.run", "--nnodes=1",
+           "--nproc-per-node", "2", "--master-addr", "127.0.0.1", "--master-port", str(_port()),
+           os.path.join(HERE, "tp_shard_check.py"), "--allreduce", allreduce]
+    r = subprocess.run(cmd, capture_output=True, text=True, env=env)
+    assert r.returncode == 0, r.stderr[-3000:]
+    out = json.loads([l for l in r.stdout.splitlines() if l.startswith("{")][-1])
+    print(out)
+    assert out["same_token_on_all_ranks"] and out["token_matches_oracle"] and out["logits_bit_identical"], out
+    assert out["colsplit_maxrel"] <= 1e-4, out
+    if allreduce == "peer":  # rank-order sums: the same bits everywhere
+        assert out["colsplit_same_on_all_ranks"], out

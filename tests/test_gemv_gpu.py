@@ -174,6 +174,29 @@ def test_fused_argmax_matches_greedy(ctx, mode):
     w.free()
 
 
+def test_argmax_shard_key(ctx):
+    """unltd_gemv_argmax_shard on one GPU: the key of rows [row0, row0 + n)
+    of a head is orderable(max logit) << 32 | 0xFFFFFFFF - (row0 + first
+    local argmax), over three calls in a row."""
+    dim_in, vocab, row0, n = 4096, 9000, 3000, 4000
+    wb = synth.quant_weights(ug.Q6K, dim_in, vocab, seed=81)
+    x = synth.activations(dim_in, seed=82)
+    ref = oracle.gemv_quant_q8k(x, wb, dim_in, vocab, ug.Q6K, nthreads=8)[row0:row0 + n]
+    w = ctx.upload(wb, ug.Q6K, dim_in, vocab, row0=row0, rows=n)
+    key = torch.zeros(1, dtype=torch.int64, device="cuda")
+    lg = torch.empty(n, device="cuda")
+    i = oracle.argmax(ref)
+    b = int(ref[i:i + 1].view(np.uint32)[0])
+    ordv = (~b & 0xFFFFFFFF) if b >= 0x80000000 else (b | 0x80000000)
+    want = (ordv << 32) | (0xFFFFFFFF - (row0 + i))
+    for _ in range(3):
+        ctx.gemv_argmax_shard(w, _dev(x), key, row0, logits=lg, mode=ug.MODE_Q8K)
+        ctx.synchronize()
+        assert _same_bits(lg.cpu().numpy(), ref)
+        assert int(key.item()) & 0xFFFFFFFFFFFFFFFF == want
+    w.free()
+
+
 def test_argmax_nan_rules(ctx):
     """A NaN logit never wins, except at index 0 (greedy.rs strict '>')."""
     dim_in, dim_out = 256, 50

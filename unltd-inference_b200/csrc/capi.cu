@@ -274,6 +274,25 @@ int32_t unltd_gemv_argmax(unltd_ctx c, unltd_weight w, const float *x, float *lo
   return gemv_launch(c, a);
 }
 
+int32_t unltd_gemv_argmax_shard(unltd_ctx c, unltd_weight w, const float *x, float *logits, uint64_t *key,
+                                uint32_t row0, int32_t mode) {
+  if (!c || !w || !x || !key) return set_error(UNLTD_ERR_INVALID_ARG, "gemv_argmax_shard: NULL argument");
+  if (w->ctx != c) return set_error(UNLTD_ERR_INVALID_ARG, "gemv_argmax_shard: weight belongs to another context");
+  if (w->dim_out == 0) return set_error(UNLTD_ERR_LENGTH, "gemv_argmax_shard: empty shard");
+  if ((uint64_t)row0 + w->dim_out > 0x7FFFFFFFull)
+    return set_error(UNLTD_ERR_LENGTH, "gemv_argmax_shard: global row index beyond 2^31");
+  if (w->dtype == F32) return set_error(UNLTD_ERR_UNSUPPORTED, "gemv_argmax_shard: packed weights only");
+  int32_t rc = check_mode(w, mode, "gemv_argmax_shard");
+  if (rc) return rc;
+  CtxGuard g(c->device);
+  // the local token goes to a spare word of the context's argmax block
+  uint32_t *tok = reinterpret_cast<uint32_t *>(reinterpret_cast<uint8_t *>(c->argmax_key) + 16);
+  GemvArgs a{w, x, logits, mode, c->argmax_key, c->argmax_done, tok};
+  a.argmax_row0 = (int)row0;
+  a.key_out = reinterpret_cast<unsigned long long *>(key);
+  return gemv_launch(c, a);
+}
+
 int32_t unltd_gemm(unltd_ctx c, unltd_weight w, const float *X, float *Y, size_t m_tokens) {
   if (!c || !w || !X || !Y) return set_error(UNLTD_ERR_INVALID_ARG, "gemm: NULL argument");
   if (w->ctx != c) return set_error(UNLTD_ERR_INVALID_ARG, "gemm: weight belongs to another context");

@@ -48,6 +48,7 @@ SIGNATURES = [
     ("unltd_weight_info", _I, [_P, ctypes.POINTER(_I), ctypes.POINTER(_S), ctypes.POINTER(_S), ctypes.POINTER(_S)]),
     ("unltd_gemv", _I, [_P, _P, _P, _P, _I]),
     ("unltd_gemv_argmax", _I, [_P, _P, _P, _P, _P, _I]),
+    ("unltd_gemv_argmax_shard", _I, [_P, _P, _P, _P, _P, ctypes.c_uint32, _I]),
     ("unltd_dequant", _I, [_P, _P, _P]),
     ("unltd_gemv_noalloc", _I, [_P, _P, _P, _I, _P]),
     ("unltd_gemm", _I, [_P, _P, _P, _P, _S]),
@@ -218,6 +219,14 @@ class Context:
     def gemv_argmax(self, w: "Weight", x, token, logits=None, mode: int = MODE_Q8K):
         _check(lib().unltd_gemv_argmax(self.h, w.h, _ptr(x), _ptr(logits) if logits is not None else None,
                                        _ptr(token), mode))
+
+    def gemv_argmax_shard(self, w: "Weight", x, key, row0: int, logits=None, mode: int = MODE_Q8K):
+        """Vocab shard [row0, row0 + dim_out) of the LM head: this shard's
+        argmax key (orderable(logit) << 32 | 0xFFFFFFFF - global row) into
+        `key` (one int64); allreduce_max_u64 over the ranks then gives the
+        whole vocabulary's first-index maximum."""
+        _check(lib().unltd_gemv_argmax_shard(self.h, w.h, _ptr(x), _ptr(logits) if logits is not None else None,
+                                             _ptr(key), row0, mode))
 
     def gemm(self, w: "Weight", X, Y, m_tokens: int):
         """Y[m][n] = sum_k X[m][k] W[n][k] on the tensor cores (fp16 operands, f32 accumulate)."""
