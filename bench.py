@@ -269,8 +269,9 @@ def decode_bench(n_tokens, with_cpu, rank=0, world=1, dist=None, profile_region=
         "launches_per_step": info["launches_per_step"], "graph": "one CUDA graph per token",
         "arithmetic": ("Q8K_EXACT projections; f32/f64 ops in the reference's order (hidden states bit-identical to "
                        "the oracle)" if world == 1 else
-                       "Q8K_EXACT projections; row-split partial outputs summed by NCCL all-reduce (logits within "
-                       "1e-3 max-rel of the oracle, same greedy stream)"),
+                       "Q8K_EXACT projections; row-split partial outputs summed in rank order over NVLink peer "
+                       "memory, fused into the GEMVs (logits within 1e-3 max-rel of the oracle, same greedy "
+                       "stream)"),
         "tokens_tail": [int(t) for t in toks[-4:]],
     }
     s.close()
