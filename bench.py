@@ -13,8 +13,12 @@ reference and runs MODE_F32X. The F32X rate of the whole mix is reported too.
 
 N > 1 GPUs (torchrun): the projections are sharded as in a tensor-parallel
 decode: (a) and (c) column-split (rows), (b) row-split on its inputs followed
-by an NCCL all-reduce of y, (d) vocab-split with a cross-GPU argmax
-(all-reduce MAX of a packed 64-bit key). Total work is fixed: strong scaling.
+by an all-reduce of y, (d) vocab-split with a cross-GPU argmax (all-reduce MAX
+of a packed 64-bit key); both all-reduces are the library's NVLink peer kernel
+(NCCL through torch.distributed if the peer mapping is unavailable). Total work
+is fixed: strong scaling. `e2e` at N > 1 adds, every step, each rank's x copy
+from pinned host memory and its y shard and the token back into pinned host
+memory, device-timed and taken as the max over ranks.
 
 --impl reference times the reference's CPU implementation of the same step
 (the oracle restatement of quants.rs: gemv_quant_q8k single-threaded per
@@ -270,8 +274,8 @@ def decode_bench(n_tokens, with_cpu, rank=0, world=1, dist=None, profile_region=
         "arithmetic": ("Q8K_EXACT projections; f32/f64 ops in the reference's order (hidden states bit-identical to "
                        "the oracle)" if world == 1 else
                        "Q8K_EXACT projections; row-split partial outputs summed in rank order over NVLink peer "
-                       "memory, fused into the GEMVs (logits within 1e-3 max-rel of the oracle, same greedy "
-                       "stream)"),
+                       "memory, fused into the GEMVs (same greedy stream as the oracle; hidden state within 1e-3 "
+                       "max-rel of it, logits bit-identical given that hidden state)"),
         "tokens_tail": [int(t) for t in toks[-4:]],
     }
     s.close()
@@ -544,6 +548,46 @@ def main():
             "path": "unltd_gemv_quant_q8k / unltd_gemv_quant (host buffers, pinned; weights cached after first call)",
         }
         ug.forget_host_weights()
+    elif world > 1 and not args.no_e2e and args.only is None:
+        # every rank: its x slice from pinned host memory, the sharded mix with
+        # its all-reduces, its y shard and the greedy token back into pinned
+        # host memory, one stream synchronisation per step (the host reads the
+        # token); device-timed on the launch stream, max over ranks
+        xin = [it["x"].cpu().pin_memory() for it in items]
+        yout = [torch.empty(it["y"].numel(), dtype=torch.float32).pin_memory() for it in items]
+        kout = torch.empty(1, dtype=torch.int64).pin_memory()
+
+        def e2e_step_tp():
+            for i, it in enumerate(items):
+                it["x"].copy_(xin[i], non_blocking=True)
+                run_item(it)
+                yout[i].copy_(it["y"], non_blocking=True)
+                if it["name"].startswith("d_"):
+                    kout.copy_(key, non_blocking=True)
+            stream.synchronize()
+            return 0xFFFFFFFF - (int(kout.item()) & 0xFFFFFFFF)
+
+        for _ in range(2):
+            e2e_step_tp()
+        dist.barrier()
+        torch.cuda.synchronize()
+        t_start.record(stream)
+        for _ in range(K):
+            e2e_step_tp()
+        t_end.record(stream)
+        torch.cuda.synchronize()
+        io = torch.tensor([t_start.elapsed_time(t_end) / K, sum(4 * x.numel() for x in xin),
+                           sum(4 * y.numel() for y in yout) + 8], device="cuda", dtype=torch.float64)
+        ms_e2e = io[:1].clone()
+        dist.all_reduce(ms_e2e, op=dist.ReduceOp.MAX)
+        dist.all_reduce(io, op=dist.ReduceOp.SUM)
+        e2e = {
+            "value": round(STEP_BYTES / (float(ms_e2e.item()) * 1e-3) / 1e9, 2), "unit": UNIT,
+            "h2d_bytes_per_step": int(io[1].item()), "d2h_bytes_per_step": int(io[2].item()),
+            "ms_per_step": round(float(ms_e2e.item()), 4),
+            "path": "Context.gemv / gemv_argmax_shard + library all-reduce on every rank; x from and y, token "
+                    "to pinned host buffers each step (bytes summed over ranks); device-timed, max over ranks",
+        }
 
     # ---- batched prefill GEMM on the tensor cores ----
     gemm = None

@@ -86,6 +86,14 @@ def main():
             out["stream_matches_oracle"] = otoks == toks.tolist()
             out["logits_maxrel"] = float(np.max(np.abs(logits - ol)) / np.max(np.abs(ol)))
             out["hidden_maxrel"] = float(np.max(np.abs(hd - oh)) / np.max(np.abs(oh)))
+            # the oracle's output norm and LM head (gemv_quant_q8k) applied to this
+            # run's own final hidden state: the vocab-split head depends on its
+            # input only, so given the same hidden state its logits are the same bits
+            xn = oracle.rmsnorm(hd, tensors["output_norm.weight"][1], cfg["rms_eps"])
+            own = oracle.gemv_quant_q8k(xn, tensors["output.weight"][1], cfg["n_embd"], cfg["vocab"], ug.Q6K,
+                                        nthreads=os.cpu_count() or 8)
+            out["logits_bit_identical_given_hidden"] = bool(np.array_equal(own.view(np.uint32),
+                                                                           logits.view(np.uint32)))
         print(json.dumps(out), flush=True)
     s.close()
     m.close()
