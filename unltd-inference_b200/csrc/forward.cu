@@ -32,7 +32,7 @@
 namespace unltd {
 namespace {
 
-constexpr int kErrTimeout = 1;
+[[maybe_unused]] constexpr int kErrTimeout = 1;
 constexpr int kErrToken = 2;
 
 // ---- scalar functions (kernels.rs:198-226, 174-182) ----------------------
@@ -1235,12 +1235,6 @@ int32_t dalloc(std::vector<void *> &bufs, T **p, size_t n, const char *what) {
   if (e != cudaSuccess) return cuda_error(e, what);
   bufs.push_back(*p);
   return UNLTD_OK;
-}
-
-int64_t launch_gemv(unltd_ctx c, const unltd_weight_s *w, const float *x, float *y, int32_t *rc) {
-  GemvArgs g{w, x, y, MODE_Q8K, nullptr, nullptr, nullptr};
-  if (!*rc) *rc = gemv_launch(c, g);
-  return 2;
 }
 
 // GEMV whose x image a fused producer kernel already wrote.
