@@ -287,6 +287,27 @@ def test_full_size_lm_head_q8k_and_argmax(ctx):
     w.free()
 
 
+# BASELINE configs 1a-1c at full size, on the benchmark's own seeded inputs
+# (bench.py SEEDS: weights 1000 + i, x 1001 + i)
+FULL_CONFIG1 = [("1a_q4k_gate_up", ug.Q4K, 4096, 12288, 1000), ("1b_q6k_down", ug.Q6K, 12288, 4096, 1001),
+                ("1c_q8_0", ug.Q8_0, 4096, 4096, 1002)]
+
+
+@pytest.mark.parametrize("name,dtype,dim_in,dim_out,seed", FULL_CONFIG1, ids=[c[0] for c in FULL_CONFIG1])
+def test_full_size_config1_gemvs(ctx, name, dtype, dim_in, dim_out, seed):
+    """Q8K_EXACT bit-identical to gemv_quant_q8k (the K-quants; the reference
+    has no Q8_0 dot), F32X within the stated bounds of the f64 truth."""
+    wb = synth.quant_weights(dtype, dim_in, dim_out, seed)
+    x = synth.activations(dim_in, seed + 1)
+    if dtype != ug.Q8_0:
+        got = _run(ctx, wb, dtype, dim_in, dim_out, x, ug.MODE_Q8K)
+        assert _same_bits(got, oracle.gemv_quant_q8k(x, wb, dim_in, dim_out, dtype, nthreads=8))
+    got = _run(ctx, wb, dtype, dim_in, dim_out, x, ug.MODE_F32X).astype(np.float64)
+    truth = oracle.gemv_quant_f64(x, wb, dim_in, dim_out, dtype, nthreads=8)
+    assert np.max(np.abs(got - truth)) <= F32X_NORMWISE * np.max(np.abs(truth))
+    assert np.all(np.abs(got - truth) <= F32X_ELEMWISE * _abs_mag(wb, dtype, dim_in, dim_out, x) + 1e-30)
+
+
 def test_launches_are_counted(ctx):
     n0 = ctx.launch_count()
     _run(ctx, synth.quant_weights(ug.Q4K, 256, 4, seed=1), ug.Q4K, 256, 4, synth.activations(256, seed=2), ug.MODE_F32X)
