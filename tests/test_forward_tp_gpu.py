@@ -1,9 +1,11 @@
-"""Tensor-parallel decode on 2 GPUs (tests/tp_decode_check.py under torchrun)
-against the CPU oracle, and the sharded GEMV forms through the C ABI
-(tests/tp_shard_check.py): identical greedy stream, logits and hidden state
-within 1e-3 max-rel (the row-split projections sum partial outputs across
-GPUs, so the f32 rounding differs from the single-device reference). Both
-all-reduce paths: the NVLink peer kernel and NCCL."""
+"""Tensor-parallel decode (tests/tp_decode_check.py under torchrun) against
+the CPU oracle, and the sharded GEMV forms through the C ABI
+(tests/tp_shard_check.py). On 2 GPUs with the small model: identical greedy
+stream, logits and hidden state within 1e-3 max-rel (the row-split
+projections sum partial outputs across GPUs, so the f32 rounding differs from
+the single-device reference), through both all-reduce paths, the NVLink peer
+kernel and NCCL. On 4 and 8 GPUs (skipped on smaller boxes) with the 9B-class
+model: see test_tp_9b_decode_matches_oracle."""
 import json
 import os
 import socket
