@@ -309,3 +309,42 @@ def q4k_minsum_mma_model(hdrs: list, q8: np.ndarray) -> np.ndarray:
             A[r, 4 + i] = (mb >> (8 * i)) & 0xFF
     D = A @ B
     return D[:, 0] + 256 * D[:, 1]
+
+
+# ---- batched decode (design model): scales folded into the A operand -------
+
+def q4k_sumi_scale_split_batched(blks: list, q8s: np.ndarray) -> np.ndarray:
+    """sumi[r][b][k] of rows `blks` (one Q4_K block each) against B Q8_K
+    blocks `q8s` [B, 256], as two integer matrix products over the whole
+    block (K = 256) instead of one product per scale group.
+
+    A row's 6-bit group scale is split as sc = 8 * sc_hi + sc_lo (3 bits
+    each), so both A operands sc_lo * a and sc_hi * a (a = the 4-bit quant)
+    lie in [0, 105] and fit the u8 operand of an int8 MMA; B holds, per
+    sequence b and lane class k, the q8 values of the elements e with
+    e % 8 == k (zero elsewhere), i.e. N = 8 * B columns. Then
+    sumi = 8 * (A_hi @ B) + (A_lo @ B), every partial exact in int32
+    (|A_lo @ B| <= 256 * 105 * 127 < 2^23)."""
+    R, B = len(blks), q8s.shape[0]
+    a_lo = np.zeros((R, 256), np.int64)
+    a_hi = np.zeros((R, 256), np.int64)
+    e = np.arange(256)
+    pos = e % 64
+    for r, blk in enumerate(blks):
+        s = blk[4:16].astype(np.int64)
+        sc = [(s[g] & 63) if g < 4 else ((s[g + 4] & 0xF) | ((s[g - 4] >> 6) << 4)) for g in range(8)]
+        qs = blk[16:].astype(np.int64)
+        byte = qs[32 * (e // 64) + pos % 32]
+        a = np.where(pos < 32, byte & 0xF, byte >> 4)
+        scv = np.array(sc, np.int64)[e // 32]
+        a_lo[r] = (scv & 7) * a
+        a_hi[r] = (scv >> 3) * a
+    bmat = np.zeros((256, B * 8), np.int64)
+    for b in range(B):
+        for k in range(8):
+            sel = e % 8 == k
+            bmat[sel, 8 * b + k] = q8s[b, sel]
+    assert a_lo.max() <= 105 and a_hi.max() <= 105
+    d_lo, d_hi = a_lo @ bmat, a_hi @ bmat
+    assert np.abs(d_lo).max() < 2 ** 31 and np.abs(d_hi).max() < 2 ** 31
+    return (8 * d_hi + d_lo).reshape(R, B, 8)

@@ -110,3 +110,22 @@ def test_q4k_minsum_mma_fragments_match_reference(seed):
         got = km.q4k_minsum_mma_model([km.repack_q4k_block(b)[0] for b in blks], q8)
         for r in range(16):
             assert got[r] == km.q4k_block_sumi_reference(blks[r], q8)[1]
+
+
+def test_q4k_scale_split_batched_sums_equal_reference():
+    # design model of a batched (several sequences) Q4_K Q8_K dot: the
+    # per-class integer sums of every (row, sequence) pair equal the
+    # reference's sumi (quants.rs:328-351), including all-63 scales and the
+    # extreme q8 values
+    rng = np.random.default_rng(41)
+    blks = [rng.integers(0, 256, size=144).astype(np.uint8) for _ in range(12)]
+    blks[0][4:16] = 0xFF  # every 6-bit scale and min = 63
+    blks[0][16:] = 0xFF  # every quant = 15
+    q8s = rng.integers(-127, 128, size=(5, 256)).astype(np.int64)
+    q8s[0] = 127
+    q8s[1] = -127
+    got = km.q4k_sumi_scale_split_batched(blks, q8s)
+    for r, blk in enumerate(blks):
+        for b in range(q8s.shape[0]):
+            ref, _ = km.q4k_block_sumi_reference(blk, q8s[b])
+            assert np.array_equal(got[r, b], ref), (r, b)
