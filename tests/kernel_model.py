@@ -348,3 +348,40 @@ def q4k_sumi_scale_split_batched(blks: list, q8s: np.ndarray) -> np.ndarray:
     d_lo, d_hi = a_lo @ bmat, a_hi @ bmat
     assert np.abs(d_lo).max() < 2 ** 31 and np.abs(d_hi).max() < 2 ** 31
     return (8 * d_hi + d_lo).reshape(R, B, 8)
+
+
+def q4k_gemv_q8k_batched_model(wb: np.ndarray, dim_in: int, dim_out: int, q8_d: np.ndarray,
+                               q8_qs: np.ndarray) -> np.ndarray:
+    """y[b][r] = dot_q4_k_q8_k of row r with Q8_K vector b (quants.rs:312-360),
+    for B vectors at once: the integer sums of every (row, sequence) from
+    q4k_sumi_scale_split_batched, the min term as an (8 x B) integer product,
+    then the reference's f32 epilogue per (row, sequence) in its order
+    (d = q8.d * f16(d); sums[k] += d * sumi[k]; sumf -= (f16(dmin) * q8.d) *
+    minsum; s = sumf + sums[0] + ... + sums[7]), every operation rounded
+    separately in f32. q8_d: [B, nb] f32; q8_qs: [B, nb, 256] int."""
+    nb = dim_in // 256
+    B = q8_qs.shape[0]
+    f32 = np.float32
+    rows = wb.reshape(dim_out, nb, 144)
+    y = np.zeros((B, dim_out), f32)
+    bsums = q8_qs.astype(np.int64).reshape(B, nb, 16, 16).sum(3)  # [B, nb, 16]
+    for r in range(dim_out):
+        sums = np.zeros((B, 8), f32)
+        sumf = np.zeros(B, f32)
+        for i in range(nb):
+            blk = rows[r, i]
+            sumi = q4k_sumi_scale_split_batched([blk], q8_qs[:, i, :])[0]  # [B, 8]
+            s = blk[4:16].astype(np.int64)
+            m = [(s[g + 4] & 63) if g < 4 else ((s[g + 4] >> 4) | ((s[g] >> 6) << 4)) for g in range(8)]
+            m16 = np.repeat(np.array(m, np.int64), 2)  # bsums group g pairs with m[g // 2]
+            minsum = bsums[:, i, :] @ m16  # [B]
+            dd = blk[0:2].view(np.float16).astype(f32)[0]
+            dmin = blk[2:4].view(np.float16).astype(f32)[0]
+            d = (q8_d[:, i].astype(f32) * dd).astype(f32)
+            sums = (sums + (d[:, None] * sumi.astype(f32)).astype(f32)).astype(f32)
+            sumf = (sumf - ((dmin * q8_d[:, i].astype(f32)).astype(f32) * minsum.astype(f32)).astype(f32)).astype(f32)
+        out = sumf
+        for k in range(8):
+            out = (out + sums[:, k]).astype(f32)
+        y[:, r] = out
+    return y

@@ -129,3 +129,22 @@ def test_q4k_scale_split_batched_sums_equal_reference():
         for b in range(q8s.shape[0]):
             ref, _ = km.q4k_block_sumi_reference(blk, q8s[b])
             assert np.array_equal(got[r, b], ref), (r, b)
+
+
+def test_q4k_batched_gemv_model_bit_identical_to_oracle():
+    # the whole batched Q4_K Q8_K GEMV of the design model: for every
+    # sequence, the same bits as the reference's gemv_quant_q8k
+    import oracle
+    import synth
+
+    dim_in, dim_out, B = 1024, 24, 6
+    wb = synth.quant_weights(synth.Q4K, dim_in, dim_out, seed=43)
+    xs = [synth.activations(dim_in, seed=44 + b) for b in range(B)]
+    xs[1][:256] = 0.0  # an all-zero block: d = 0, qs = 0
+    q8 = [oracle.quantize_q8_k(x) for x in xs]
+    q8_d = np.array([[blk.d for blk in q] for q in q8], np.float32)
+    q8_qs = np.array([[list(blk.qs) for blk in q] for q in q8], np.int64)
+    got = km.q4k_gemv_q8k_batched_model(wb, dim_in, dim_out, q8_d, q8_qs)
+    for b in range(B):
+        ref = oracle.gemv_quant_q8k(xs[b], wb, dim_in, dim_out, synth.Q4K)
+        assert np.array_equal(got[b].view(np.uint32), ref.view(np.uint32)), b
