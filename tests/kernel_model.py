@@ -385,3 +385,48 @@ def q4k_gemv_q8k_batched_model(wb: np.ndarray, dim_in: int, dim_out: int, q8_d: 
             out = (out + sums[:, k]).astype(f32)
         y[:, r] = out
     return y
+
+
+def q6k_gemv_q8k_batched_model(wb: np.ndarray, dim_in: int, dim_out: int, q8_d: np.ndarray,
+                               q8_qs: np.ndarray) -> np.ndarray:
+    """y[b][r] = dot_q6_k_q8_k of row r with Q8_K vector b (quants.rs:371-412)
+    for B vectors at once. The scaled quant w = sc * (raw6 - 32) lies in
+    [-4064, 4096]; it enters the int8 MMA as two operands w = 128 * w1 + w0,
+    w0 = w & 127 in [0, 127], w1 = w >> 7 in [-32, 32], so per block
+    sumi = 128 * (W1 @ Bq) + (W0 @ Bq) with the class-masked q8 columns Bq of
+    q4k_sumi_scale_split_batched (|W0 @ Bq| <= 256 * 127 * 127 < 2^23). The
+    f32 epilogue follows the reference per (row, sequence): d = q8.d * f16(d),
+    sums[k] += d * sumi[k], s = sums[0] + ... + sums[7] from 0."""
+    nb = dim_in // 256
+    B = q8_qs.shape[0]
+    f32 = np.float32
+    rows = wb.reshape(dim_out, nb, 210)
+    e = np.arange(256)
+    pos = e % 128
+    bq = np.zeros((nb, 256, B * 8), np.int64)
+    for b in range(B):
+        for k in range(8):
+            sel = e % 8 == k
+            bq[:, sel, 8 * b + k] = q8_qs[b][:, sel]
+    y = np.zeros((B, dim_out), f32)
+    for r in range(dim_out):
+        sums = np.zeros((B, 8), f32)
+        for i in range(nb):
+            blk = rows[r, i]
+            ql, qh = blk[:128].astype(np.int64), blk[128:192].astype(np.int64)
+            sc = blk[192:208].view(np.int8).astype(np.int64)
+            byte = ql[64 * (e // 128) + pos % 64]
+            nib = np.where(pos < 64, byte & 0xF, byte >> 4)
+            hi2 = (qh[32 * (e // 128) + pos % 32] >> (2 * (pos // 32))) & 3
+            w = sc[e // 16] * ((nib | (hi2 << 4)) - 32)
+            w0, w1 = w & 127, w >> 7
+            assert w0.min() >= 0 and w0.max() <= 127 and w1.min() >= -32 and w1.max() <= 32
+            sumi = (128 * (w1 @ bq[i]) + (w0 @ bq[i])).reshape(B, 8)
+            dd = blk[208:210].view(np.float16).astype(f32)[0]
+            d = (q8_d[:, i].astype(f32) * dd).astype(f32)
+            sums = (sums + (d[:, None] * sumi.astype(f32)).astype(f32)).astype(f32)
+        out = np.zeros(B, f32)
+        for k in range(8):
+            out = (out + sums[:, k]).astype(f32)
+        y[:, r] = out
+    return y

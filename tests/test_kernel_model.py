@@ -148,3 +148,27 @@ def test_q4k_batched_gemv_model_bit_identical_to_oracle():
     for b in range(B):
         ref = oracle.gemv_quant_q8k(xs[b], wb, dim_in, dim_out, synth.Q4K)
         assert np.array_equal(got[b].view(np.uint32), ref.view(np.uint32)), b
+
+
+def test_q6k_batched_gemv_model_bit_identical_to_oracle():
+    # Q6_K with full-range int8 scales (-128 and 127 included): the two-operand
+    # split of sc * (raw6 - 32) stays exact and the batch gives the
+    # reference's bits for every sequence
+    import oracle
+    import synth
+
+    dim_in, dim_out, B = 768, 20, 5
+    wb = synth.quant_weights(synth.Q6K, dim_in, dim_out, seed=45).copy()
+    blocks = wb.reshape(-1, 210)
+    blocks[0, 192:208] = np.array([-128, 127] * 8, np.int8).view(np.uint8)
+    blocks[0, :192] = 0xFF  # raw6 = 63 everywhere in that block
+    blocks[1, :192] = 0x00  # raw6 = 0 everywhere: a = -32
+    blocks[1, 192:208] = np.array([-128] * 16, np.int8).view(np.uint8)
+    xs = [synth.activations(dim_in, seed=46 + b) for b in range(B)]
+    q8 = [oracle.quantize_q8_k(x) for x in xs]
+    q8_d = np.array([[blk.d for blk in q] for q in q8], np.float32)
+    q8_qs = np.array([[list(blk.qs) for blk in q] for q in q8], np.int64)
+    got = km.q6k_gemv_q8k_batched_model(wb, dim_in, dim_out, q8_d, q8_qs)
+    for b in range(B):
+        ref = oracle.gemv_quant_q8k(xs[b], wb, dim_in, dim_out, synth.Q6K)
+        assert np.array_equal(got[b].view(np.uint32), ref.view(np.uint32)), b
