@@ -76,3 +76,25 @@ def test_config1_shards_partition_the_weights(world, item):
             assert p[1] % be == 0 and p[3] % be == 0 and p[2] == do
             assert p[0].size == do * (p[1] // be) * bb
         assert sum(p[1] for p in parts) == di
+
+
+def test_decode_bytes_per_token_components():
+    # the 9B-class model at a 2048-position context: packed projection and
+    # LM-head weights with the one embedding row 4,826,052,864 B, K/V rows
+    # 134,217,728 B, GDN matrices read and written 2 x 50,331,648 B, plus the
+    # f32 tensors and the conv windows
+    cfg = synth.QWEN35_9B
+    d = synth.qwen35_dims(cfg)
+    packed = f32_bytes = embd = 0
+    for nm, dt, di, do in synth.qwen35_tensor_list(cfg):
+        if nm == "token_embd.weight":
+            embd = synth.row_bytes(dt, di)
+        elif dt == synth.F32:
+            f32_bytes += 4 * di * do
+        else:
+            packed += synth.row_bytes(dt, di) * do
+    assert packed + embd == 4_826_052_864
+    n_recr = cfg["n_layer"] - sum(d["attn"])
+    conv = n_recr * 4 * cfg["conv_kernel"] * d["dconv"]
+    expect = packed + f32_bytes + embd + 134_217_728 + 2 * 50_331_648 + conv
+    assert bench.decode_bytes_per_token(cfg, 2047) == expect
