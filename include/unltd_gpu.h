@@ -164,7 +164,11 @@ int32_t unltd_dequant(unltd_ctx ctx, unltd_weight w, float *out_dev);
  * All calls on a device share the array: calls whose kernels overlap on the
  * GPU race; order them on one stream. `stream` is a cudaStream_t (NULL = the
  * legacy default stream). The first call on a device sets up that device
- * (symbol address, kernel attributes); make it before any stream capture. */
+ * (symbol address, kernel attributes); make it before any stream capture (a
+ * failed set-up is retried by the next call). A kernel that gives up on a
+ * bounded pipeline wait records the timeout in the error word of w's
+ * context: after `stream` has finished, unltd_ctx_synchronize on that
+ * context returns UNLTD_ERR_TIMEOUT (y is then not valid). */
 int32_t unltd_gemv_noalloc(unltd_weight w, const float *x_dev, float *y_dev, int32_t mode, void *stream);
 
 /* ---- NCCL communicators (tensor parallelism, one process per GPU) ----------

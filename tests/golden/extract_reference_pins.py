@@ -8,7 +8,8 @@ This script reads that Rust file as text and writes the bytes and expected
 values as a JSON fixture, so the tests can pin the oracle without the
 reference tree being present.
 
-Usage: python tests/golden/extract_reference_pins.py [path/to/quants.rs]
+Usage: python tests/golden/extract_reference_pins.py path/to/quants.rs
+   or: UNLTD_REFERENCE=<reference checkout> python tests/golden/extract_reference_pins.py
 """
 from __future__ import annotations
 
@@ -18,9 +19,7 @@ import re
 import sys
 
 HERE = os.path.dirname(os.path.abspath(__file__))
-DEFAULT_SRC = os.path.join(
-    os.environ.get("UNLTD_REFERENCE", "/root/reference"), "crates/unltd-tensor/src/quants.rs"
-)
+QUANTS_RS = "crates/unltd-tensor/src/quants.rs"
 
 
 def extract(src_text: str) -> dict:
@@ -58,7 +57,12 @@ def extract(src_text: str) -> dict:
 
 
 def main() -> None:
-    src = sys.argv[1] if len(sys.argv) > 1 else DEFAULT_SRC
+    if len(sys.argv) > 1:
+        src = sys.argv[1]
+    elif os.environ.get("UNLTD_REFERENCE"):
+        src = os.path.join(os.environ["UNLTD_REFERENCE"], QUANTS_RS)
+    else:
+        raise SystemExit("give the path of quants.rs, or set UNLTD_REFERENCE to the reference checkout")
     with open(src, encoding="utf-8") as f:
         data = extract(f.read())
     out = os.path.join(HERE, "ornith_pins.json")

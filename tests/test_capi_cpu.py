@@ -38,6 +38,26 @@ def test_every_declared_symbol_is_exported(L):
     assert syms <= bound, syms - bound
 
 
+def test_rust_binding_declares_exported_symbols(L):
+    """Every extern "C" function the Rust FFI crate (rust/unltd-tensor-gpu)
+    declares is exported by the library and declared in the header, with the
+    same number of parameters as the header's prototype."""
+    src = open(os.path.join(REPO, "rust", "unltd-tensor-gpu", "src", "lib.rs")).read()
+    block = src[src.index('extern "C" {'):]
+    block = block[:block.index("\n}\n")]
+    decls = dict(re.findall(r"fn (unltd_[a-z_0-9]+)\(([^)]*)\)", block, re.S))
+    assert {"unltd_gemv_quant", "unltd_gemv_quant_q8k", "unltd_dequantize_q4_k", "unltd_gemv"} <= set(decls)
+    header = "".join(open(os.path.join(REPO, "include", n)).read() for n in os.listdir(os.path.join(REPO, "include"))
+                     if n.endswith(".h"))
+    for name, args in decls.items():
+        assert hasattr(L, name), name
+        m = re.search(r"\b%s\(([^)]*)\)" % name, header, re.S)
+        assert m, name
+        n_h = 0 if m.group(1).strip() in ("", "void") else m.group(1).count(",") + 1
+        n_r = 0 if not args.strip() else args.count(",") + 1
+        assert n_h == n_r, (name, n_h, n_r)
+
+
 def test_row_bytes_match_reference_sizing(L):  # min_forward.rs:52-80
     assert ug.row_bytes(ug.F32, 4096) == 16384
     assert ug.row_bytes(ug.Q4K, 4096) == 16 * 144

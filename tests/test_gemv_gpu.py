@@ -149,6 +149,45 @@ def test_reference_hand_blocks_through_gpu(ctx):
     assert _run(ctx, blk6, ug.Q6K, 256, 1, x, ug.MODE_Q8K)[0] == 3937.0
 
 
+def test_reference_golden_blocks_through_gpu(ctx):
+    """The reference's real-model blocks (two Q6_K, two Q4_K of a Q4_K_M GGUF,
+    quants.rs:1094-1152, fixture tests/golden/ornith_pins.json) through the
+    GPU: the dequantized weights bit-exact with the oracle and equal to the
+    gguf-py single weights w[7], w[200] the reference pins (quants.rs:1169-1198);
+    F32X dots within the reference's 1e-4 of the gguf-py values for both
+    deterministic x (quants.rs:1157-1166); Q8K_EXACT dots bit-identical to the
+    oracle's gemv_quant_q8k."""
+    import json
+    import os
+
+    with open(os.path.join(os.path.dirname(os.path.abspath(__file__)), "golden", "ornith_pins.json")) as f:
+        pins = json.load(f)
+    i = np.arange(256)
+    xp = (((i * 7919) % 1009).astype(np.float32) / np.float32(1009.0) - np.float32(0.5)).astype(np.float32)
+    xa = (((i * 31 + 17) % 257).astype(np.float32) / np.float32(257.0) - np.float32(0.5)).astype(np.float32)
+    tol = pins["tolerance"]
+    for case in pins["cases"]:
+        raw = np.frombuffer(bytes.fromhex(pins["blocks_hex"][case["block"]]), np.uint8)
+        dtype = ug.Q4K if case["block"].startswith("Q4K") else ug.Q6K
+        w = ctx.upload(raw, dtype, 256, 1)
+        deq = torch.empty(256, device="cuda")
+        ctx.dequant(w, deq)
+        ctx.synchronize()
+        got = deq.cpu().numpy()
+        assert _same_bits(got, oracle.dequantize(raw, 256, dtype)), case["block"]
+        assert abs(float(got[7]) - case["w7"]) <= tol and abs(float(got[200]) - case["w200"]) <= tol, case
+        for x, want in ((xp, case["dot_x_pattern"]), (xa, case["dot_x_alt"])):
+            y = torch.full((1,), float("nan"), device="cuda")
+            ctx.gemv(w, _dev(x), y, ug.MODE_F32X)
+            ctx.synchronize()
+            assert abs(float(y.item()) - want) <= tol, (case["block"], float(y.item()), want)
+            ctx.gemv(w, _dev(x), y, ug.MODE_Q8K)
+            ctx.synchronize()
+            ref = oracle.gemv_quant_q8k(x, raw, 256, 1, dtype)
+            assert _same_bits(y.cpu().numpy(), ref), case["block"]
+        w.free()
+
+
 @pytest.mark.parametrize("mode", [ug.MODE_Q8K, ug.MODE_F32X])
 def test_fused_argmax_matches_greedy(ctx, mode):
     dim_in, dim_out = 4096, 20000

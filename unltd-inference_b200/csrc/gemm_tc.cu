@@ -33,6 +33,7 @@
 #include <algorithm>
 #include <mutex>
 #include <string>
+#include <vector>
 
 #include "unltd_host.h"
 #include "unltd_internal.cuh"
@@ -440,10 +441,17 @@ int32_t gemm_launch(unltd_ctx ctx, const unltd_weight_s &w, const float *X, floa
   P.err = ctx->err;
   P.tiles_n = (P.N + kTileN - 1) / kTileN;
   P.ntiles = ((P.M + kTileM - 1) / kTileM) * P.tiles_n;
-  static std::once_flag attr_once;
-  std::call_once(attr_once, [] {
-    cudaFuncSetAttribute(gemm_q4k_tc, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemBytes);
-  });
+  {
+    // the attribute belongs to the current device's context: set it once per device
+    static std::mutex mu;
+    static std::vector<int> done;
+    std::lock_guard<std::mutex> lk(mu);
+    if (std::find(done.begin(), done.end(), ctx->device) == done.end()) {
+      cudaError_t e = cudaFuncSetAttribute(gemm_q4k_tc, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemBytes);
+      if (e != cudaSuccess) return cuda_error(e, "gemm: shared-memory attribute");
+      done.push_back(ctx->device);
+    }
+  }
   const int grid = std::min(P.ntiles, ctx->num_sms);
   gemm_q4k_tc<<<grid, kThreadsG, kSmemBytes, st>>>(tmA, tmWq, tmWh, P);
   cudaError_t e = cudaGetLastError();

@@ -1417,40 +1417,56 @@ int max_smem_optin(int device) {
   return v;
 }
 
-void ensure_smem_attr(GemvFn fn, int smem) {
+// cudaFuncSetAttribute applies to the current device's context, so the cache
+// is keyed by (device, kernel): a process that drives several GPUs sets the
+// limit on each of them.
+cudaError_t ensure_smem_attr(int device, GemvFn fn, int smem) {
+  struct Entry {
+    int device;
+    GemvFn fn;
+    int smem;
+  };
   static std::mutex mu;
-  static std::vector<std::pair<GemvFn, int>> done;
+  static std::vector<Entry> done;
   std::lock_guard<std::mutex> lk(mu);
   for (auto &e : done)
-    if (e.first == fn && e.second >= smem) return;
-  cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
-  done.push_back({fn, smem});
+    if (e.device == device && e.fn == fn && e.smem >= smem) return cudaSuccess;
+  const cudaError_t err = cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+  if (err == cudaSuccess) done.push_back({device, fn, smem});
+  return err;
 }
 
 }  // namespace
 
 // Sets the dynamic shared-memory limit of every quantized GEMV kernel to the
-// largest plan gemv_launch can choose on `device`, so later launches find
-// their attribute already set (no host-side cache growth on the hot path).
-void gemv_prewarm(int device) {
+// largest plan gemv_launch can choose on `device` (which must be current), so
+// later launches find their attribute already set (no host-side cache growth
+// on the hot path). Returns the first error of cudaFuncSetAttribute.
+cudaError_t gemv_prewarm(int device) {
   const int m = max_smem_optin(device) - 1024;
   const int fmts[3] = {Q4K, Q6K, Q8_0};
+  cudaError_t first = cudaSuccess;
+  auto set = [&](GemvFn fn) {
+    const cudaError_t e = ensure_smem_attr(device, fn, m);
+    if (first == cudaSuccess) first = e;
+  };
   for (int fmt : fmts)
     for (int mode = MODE_F32X; mode <= MODE_Q8K; mode++) {
       if (mode == MODE_Q8K && fmt == Q8_0) continue;
       for (int r = 1; r <= 2; r++) {
-        ensure_smem_attr(pick<false>(fmt, mode, r), m);
-        ensure_smem_attr(pick<true>(fmt, mode, r), m);
+        set(pick<false>(fmt, mode, r));
+        set(pick<true>(fmt, mode, r));
         if (fmt != Q8_0 && mode == MODE_Q8K) {
-          ensure_smem_attr(pick<false>(fmt, mode, r, 1), m);
-          ensure_smem_attr(pick<true>(fmt, mode, r, 1), m);
+          set(pick<false>(fmt, mode, r, 1));
+          set(pick<true>(fmt, mode, r, 1));
           if (fmt == Q6K) {
-            ensure_smem_attr(pick<false>(fmt, mode, r, 2), m);
-            ensure_smem_attr(pick<true>(fmt, mode, r, 2), m);
+            set(pick<false>(fmt, mode, r, 2));
+            set(pick<true>(fmt, mode, r, 2));
           }
         }
       }
     }
+  return first;
 }
 
 int32_t gemv_reserve(unltd_ctx ctx, const unltd_weight_s &w, int mode) {
@@ -1458,6 +1474,8 @@ int32_t gemv_reserve(unltd_ctx ctx, const unltd_weight_s &w, int mode) {
   const int nspans = w.dtype == Q8_0 ? (int)((w.nb + 7) / 8) : (int)w.nb;
   const size_t img_bytes = (size_t)nspans * img_stride(w.dtype, mode);
   if (ctx->scratch_bytes >= img_bytes) return UNLTD_OK;
+  if (ctx->scratch_fixed)  // a fixed array the context does not own: never freed or grown
+    return set_error(UNLTD_ERR_UNSUPPORTED, "gemv: x image larger than the fixed scratch");
   if (ctx->scratch) cudaFree(ctx->scratch);
   ctx->scratch = nullptr;
   ctx->scratch_bytes = 0;
@@ -1644,7 +1662,8 @@ int32_t gemv_launch(unltd_ctx ctx, const GemvArgs &a) {
 
   // 2) gemv, programmatic dependent launch
   GemvFn fn = am ? pick<true>(fmt, mode, R, mma) : pick<false>(fmt, mode, R, mma);
-  ensure_smem_attr(fn, smem);
+  e = ensure_smem_attr(ctx->device, fn, smem);
+  if (e != cudaSuccess) return cuda_error(e, "gemv: shared-memory attribute");
 
   Params P;
   P.W = w.dev;

@@ -2,13 +2,13 @@
 // memory.
 //
 // The ordinary entry points keep their per-call scratch (the x image the prep
-// kernel builds, and a timeout flag) in memory owned by a unltd_ctx, which
-// cudaMalloc'ed it and grows it with cudaMalloc when a larger dim_in arrives.
-// Some callers cannot do that: code running inside an allocator or a memory
-// pool that must not re-enter it, hosts that pre-reserve all device memory
-// and forbid further cudaMalloc, or code that may not trigger the implicit
-// device synchronisation cudaMalloc/cudaFree can cause. This variant takes
-// its scratch from a fixed array compiled into the library instead, so a call
+// kernel builds) in memory owned by a unltd_ctx, which cudaMalloc'ed it and
+// grows it with cudaMalloc when a larger dim_in arrives. Some callers cannot
+// do that: code running inside an allocator or a memory pool that must not
+// re-enter it, hosts that pre-reserve all device memory and forbid further
+// cudaMalloc, or code that may not trigger the implicit device
+// synchronisation cudaMalloc/cudaFree can cause. This variant takes its
+// scratch from a fixed array compiled into the library instead, so a call
 // allocates nothing (no cudaMalloc, no cudaFree, no torch allocation).
 //
 // Limits and sharing:
@@ -23,7 +23,12 @@
 //    Order them on one stream, or with events.
 //  * the first call on each device does the set-up below (symbol address and
 //    kernel attributes) with that device current; make that first call
-//    before any stream capture begins.
+//    before any stream capture begins. A set-up that failed is retried by the
+//    next call.
+//  * a kernel that gives up on a bounded pipeline wait records the timeout in
+//    the error word of the weight's context (allocated when that context was
+//    created): once the stream passed here has finished, unltd_ctx_synchronize
+//    on that context returns UNLTD_ERR_TIMEOUT.
 #include <cuda_runtime.h>
 
 #include <mutex>
@@ -35,7 +40,6 @@
 namespace {
 
 constexpr size_t kNoallocScratchBytes = 64 * 1024;
-constexpr size_t kNoallocImageOffset = 256;  // [0, 4): timeout flag; image from 256
 constexpr size_t kNoallocMaxDimIn = 16384;
 
 // The scratch. Its name in host code is only a handle for the runtime; the
@@ -44,23 +48,30 @@ static __device__ __align__(256) uint8_t g_noalloc_scratch[kNoallocScratchBytes]
 
 constexpr int kMaxDevices = 64;
 struct DeviceSetup {
-  std::once_flag once;
-  cudaError_t status = cudaSuccess;
+  bool done = false;
   uint8_t *scratch = nullptr;
   int num_sms = 0;
 };
+std::mutex g_setup_mu;
 DeviceSetup g_setup[kMaxDevices];
 
-void setup_device(int device, DeviceSetup &s) {
-  // The caller made `device` current.
+// With `device` current: the symbol's device address and the kernels'
+// shared-memory attributes. Marks the device done only when every step
+// succeeded, so a failure (for example a first call made during stream
+// capture) is retried by the next call.
+cudaError_t setup_device(int device, DeviceSetup &s) {
   void *p = nullptr;
-  s.status = cudaGetSymbolAddress(&p, g_noalloc_scratch);
-  if (s.status != cudaSuccess) return;
+  cudaError_t e = cudaGetSymbolAddress(&p, g_noalloc_scratch);
+  if (e != cudaSuccess) return e;
+  int sms = 0;
+  e = cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, device);
+  if (e != cudaSuccess) return e;
+  e = unltd::gemv_prewarm(device);
+  if (e != cudaSuccess) return e;
   s.scratch = static_cast<uint8_t *>(p);
-  s.status = cudaDeviceGetAttribute(&s.num_sms, cudaDevAttrMultiProcessorCount, device);
-  if (s.status != cudaSuccess) return;
-  unltd::gemv_prewarm(device);
-  s.status = cudaGetLastError();
+  s.num_sms = sms;
+  s.done = true;
+  return cudaSuccess;
 }
 
 }  // namespace
@@ -80,39 +91,47 @@ extern "C" int32_t unltd_gemv_noalloc(unltd_weight w, const float *x_dev, float 
                                                 " exceeds the fixed scratch limit of 16384");
   const int nspans = w->dtype == Q8_0 ? (int)((w->nb + 7) / 8) : (int)w->nb;
   const size_t img = (size_t)nspans * img_stride(w->dtype, mode);
-  if (img > kNoallocScratchBytes - kNoallocImageOffset)
+  if (img > kNoallocScratchBytes)
     return set_error(UNLTD_ERR_UNSUPPORTED, "gemv_noalloc: x image does not fit the fixed scratch");
 
   const int device = w->ctx->device;
   if (device < 0 || device >= kMaxDevices) return set_error(UNLTD_ERR_INVALID_ARG, "gemv_noalloc: device id");
   int prev = -1;
-  cudaGetDevice(&prev);
-  if (prev != device) cudaSetDevice(device);
-  DeviceSetup &s = g_setup[device];
-  std::call_once(s.once, setup_device, device, std::ref(s));
+  cudaError_t e = cudaGetDevice(&prev);
+  if (e != cudaSuccess) return cuda_error(e, "gemv_noalloc: current device");
+  if (prev != device) {
+    e = cudaSetDevice(device);
+    if (e != cudaSuccess) return cuda_error(e, "gemv_noalloc: select the weight's device");
+  }
   int32_t rc = UNLTD_OK;
-  if (s.status != cudaSuccess) {
-    rc = cuda_error(s.status, "gemv_noalloc: set-up (cudaGetSymbolAddress)");
+  DeviceSetup s;
+  {
+    std::lock_guard<std::mutex> lk(g_setup_mu);
+    DeviceSetup &g = g_setup[device];
+    if (!g.done) e = setup_device(device, g);
+    s = g;
+  }
+  if (!s.done) {
+    rc = cuda_error(e, "gemv_noalloc: set-up (cudaGetSymbolAddress, kernel attributes)");
   } else {
-    // A context on the stack: no allocation; it only carries the stream and
-    // points the scratch and the timeout flag at the fixed array.
+    // A context on the stack: no allocation; it carries the stream, points the
+    // image scratch at the fixed array (never freed or grown: scratch_fixed)
+    // and records timeouts in the weight's context error word.
     unltd_ctx_s c;
     c.device = device;
     c.num_sms = s.num_sms;
     c.stream = static_cast<cudaStream_t>(stream);
     c.own_stream = c.stream;
-    c.scratch = s.scratch + kNoallocImageOffset;
-    c.scratch_bytes = kNoallocScratchBytes - kNoallocImageOffset;
-    c.err = reinterpret_cast<int *>(s.scratch);
-    // the timeout flag must start at zero; the image is fully rewritten by prep
-    cudaError_t e = cudaMemsetAsync(c.err, 0, sizeof(int), c.stream);
-    if (e != cudaSuccess) {
-      rc = cuda_error(e, "gemv_noalloc: clear flag");
-    } else {
-      GemvArgs a{w, x_dev, y_dev, mode, nullptr, nullptr, nullptr};
-      rc = gemv_launch(&c, a);
-    }
+    c.scratch = s.scratch;
+    c.scratch_bytes = kNoallocScratchBytes;
+    c.scratch_fixed = true;
+    c.err = w->ctx->err;
+    GemvArgs a{w, x_dev, y_dev, mode, nullptr, nullptr, nullptr};
+    rc = gemv_launch(&c, a);
   }
-  if (prev >= 0 && prev != device) cudaSetDevice(prev);
+  if (prev >= 0 && prev != device) {
+    e = cudaSetDevice(prev);
+    if (e != cudaSuccess && rc == UNLTD_OK) rc = cuda_error(e, "gemv_noalloc: restore the caller's device");
+  }
   return rc;
 }

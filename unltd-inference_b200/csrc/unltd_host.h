@@ -18,6 +18,9 @@ struct unltd_ctx_s {
   // Scratch for per-call x images (grown on demand, never shrunk).
   uint8_t *scratch = nullptr;
   size_t scratch_bytes = 0;
+  // The scratch is a fixed array the context does not own (unltd_gemv_noalloc):
+  // gemv_reserve must neither free nor grow it.
+  bool scratch_fixed = false;
   // Argmax reduction state: a 64-bit key and a CTA-completion counter.
   unsigned long long *argmax_key = nullptr;
   unsigned int *argmax_done = nullptr;
@@ -135,7 +138,7 @@ bool gemv_norm_fusable(unltd_ctx ctx, const unltd_weight_s &w, int mode);
 bool gemv_tc_eligible(unltd_ctx ctx, const unltd_weight_s &w, int mode);
 // Grow the context's x-image scratch for w (call before stream capture).
 int32_t gemv_reserve(unltd_ctx ctx, const unltd_weight_s &w, int mode);
-void gemv_prewarm(int device);
+cudaError_t gemv_prewarm(int device);
 
 // gguf.cu: a tensor of an opened GGUF file (data: a view into the mapping,
 // null when its type is not one this path reads)
