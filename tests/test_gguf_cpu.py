@@ -119,3 +119,31 @@ def test_mutations_never_crash(tmp_path):
         except ug.UnltdError:
             pass
     assert parsed > 0
+
+
+def test_centered_q4k_model_blocks(ora):
+    """The model generator's Q4_K blocks: every group's min equals its scale
+    (scale_min_k4 of the packed bytes, quants.rs:92-102), dmin = f16(7.5 d),
+    and the dequantized weights have mean ~0 (uniform blocks: ~+1.2)."""
+    import numpy as np
+
+    import synth
+
+    w = synth.centered_q4k_weights(4096, 16, seed=5)
+    blocks = w.reshape(-1, 144)
+    for blk in blocks[:8]:
+        s = blk[4:16]
+        for g in range(8):
+            if g < 4:
+                sc, m = s[g] & 63, s[g + 4] & 63
+            else:
+                sc = (s[g + 4] & 0xF) | ((s[g - 4] >> 6) << 4)
+                m = (s[g + 4] >> 4) | ((s[g] >> 6) << 4)
+            assert sc == m
+        d = np.frombuffer(blk[0:2].tobytes(), np.float16)[0]
+        dmin = np.frombuffer(blk[2:4].tobytes(), np.float16)[0]
+        assert dmin == np.float16(np.float32(d) * np.float32(7.5))
+    deq = ora.dequantize_q4_k(w, 4096 * 16)
+    assert abs(float(deq.mean())) < 0.02 and 0.5 < float(deq.std()) < 2.0
+    plain = ora.dequantize_q4_k(synth.quant_weights(synth.Q4K, 4096, 16, seed=5), 4096 * 16)
+    assert float(plain.mean()) > 0.5

@@ -44,6 +44,41 @@ def quant_weights(dtype: int, dim_in: int, dim_out: int, seed: int) -> np.ndarra
     return w.reshape(-1)
 
 
+def _pack_scale_min_k4(sc: np.ndarray, m: np.ndarray) -> np.ndarray:
+    """The 12 packed bytes of eight 6-bit scales and mins per block (the
+    inverse of scale_min_k4, quants.rs:92-102): bytes 0-3 hold sc[0..3] with
+    the top two bits of sc[4..7], bytes 4-7 m[0..3] with the top two bits of
+    m[4..7], bytes 8-11 the low nibbles of sc[4..7] | m[4..7] << 4."""
+    sc = sc.astype(np.uint8)
+    m = m.astype(np.uint8)
+    out = np.empty(sc.shape[:-1] + (12,), np.uint8)
+    out[..., 0:4] = (sc[..., 0:4] & 63) | ((sc[..., 4:8] >> 4) << 6)
+    out[..., 4:8] = (m[..., 0:4] & 63) | ((m[..., 4:8] >> 4) << 6)
+    out[..., 8:12] = (sc[..., 4:8] & 0xF) | ((m[..., 4:8] & 0xF) << 4)
+    return out
+
+
+def centered_q4k_weights(dim_in: int, dim_out: int, seed: int) -> np.ndarray:
+    """Q4_K blocks whose dequantized values have mean ~0: uniform quants and
+    6-bit scales, each group's min equal to its scale and dmin = f16(7.5 d),
+    so w = d*sc*q - dmin*sc ~ d*sc*(q - 7.5). Uniform scale/min bytes (the
+    benchmark kernels' distribution) give every weight a mean of about
+    +240 d, which adds the same large common-mode vector to the residual at
+    every layer of a model; with it the greedy stream settles on the vocab
+    row with the largest sum. The model generator uses these blocks."""
+    rng = np.random.default_rng(seed)
+    nblk = dim_out * (dim_in // 256)
+    w = np.empty((nblk, 144), np.uint8)
+    d = rng.uniform(1e-3, 1e-2, size=nblk).astype(np.float32)
+    dh = d.astype(np.float16)
+    w[:, 0:2] = dh.view(np.uint8).reshape(-1, 2)
+    w[:, 2:4] = (dh.astype(np.float32) * np.float32(7.5)).astype(np.float16).view(np.uint8).reshape(-1, 2)
+    sc = rng.integers(0, 64, size=(nblk, 8), dtype=np.uint8)
+    w[:, 4:16] = _pack_scale_min_k4(sc, sc)
+    w[:, 16:144] = rng.integers(0, 256, size=(nblk, 128), dtype=np.uint8)
+    return w.reshape(-1)
+
+
 def activations(n: int, seed: int, rows: int | None = None) -> np.ndarray:
     rng = np.random.default_rng(seed)
     if rows is None:
@@ -60,13 +95,13 @@ def row_bytes(dtype: int, dim_in: int) -> int:
 # ---- synthetic Qwen3.5-style hybrid model ------------------------------------
 # Shapes follow crates/unltd-generation/src/qwen35_forward.rs:139-221; the
 # dtypes follow the Q4_K_M mix (Q4_K for most projections and the embedding,
-# Q6_K for attn_v, ffn_down and the LM head). Quantized tensors use the block
-# distributions above. f32 tensors (the reference loads them from the GGUF):
+# Q6_K for attn_v, ffn_down and the LM head). Q6_K tensors use the block
+# distribution above; Q4_K tensors use centered_q4k_weights (zero-mean
+# weights: with uniform scale/min bytes every Q4_K projection adds a large
+# common-mode vector to the residual stream and the greedy stream settles on
+# one vocab row). f32 tensors (the reference loads them from the GGUF):
 #   attn_norm / post_attention_norm / output_norm / ssm_norm ~ U[2e-4, 6e-4]
-#     (uniform Q4_K blocks are positively biased, so each projection adds a
-#     large common-mode term to the residual stream; small norm weights keep
-#     that term from swamping the token embedding, so the greedy stream
-#     depends on the tokens instead of settling on one vocab row),
+#     (keeps the 32-layer residual stream at an rms of ~20),
 #   attn_q_norm / attn_k_norm ~ U[0.5, 1.5], ssm_conv1d ~ U[-0.5, 0.5],
 #   ssm_dt.bias ~ U[-1, 1], ssm_a ~ -U[0.1, 1].
 # The session state stands in for a prefilled context: K and V cache rows
@@ -126,6 +161,9 @@ def qwen35_tensor_list(cfg: dict) -> list:
     return t
 
 
+NORM_RANGE = (2e-4, 6e-4)
+
+
 def _tensor_seed(seed: int, name: str) -> int:
     return (seed * 1000003 + zlib.crc32(name.encode())) & 0xFFFFFFFF
 
@@ -133,7 +171,7 @@ def _tensor_seed(seed: int, name: str) -> int:
 def _f32_tensor(name: str, n: int, seed: int) -> np.ndarray:
     rng = np.random.default_rng(_tensor_seed(seed, name))
     if name.endswith(("attn_norm.weight", "post_attention_norm.weight", "ssm_norm.weight")) or name == "output_norm.weight":
-        lo, hi = 2e-4, 6e-4
+        lo, hi = NORM_RANGE
     elif name.endswith(("attn_q_norm.weight", "attn_k_norm.weight")):
         lo, hi = 0.5, 1.5
     elif name.endswith("ssm_conv1d.weight"):
@@ -153,6 +191,8 @@ def qwen35_tensor(cfg: dict, name: str, seed: int):
         if nm == name:
             if dt == F32:
                 return dt, _f32_tensor(nm, di, seed)
+            if dt == Q4K:
+                return dt, centered_q4k_weights(di, do, _tensor_seed(seed, nm))
             return dt, quant_weights(dt, di, do, _tensor_seed(seed, nm))
     raise KeyError(name)
 
