@@ -159,8 +159,20 @@ void ora_softmax(float *out, const float *x, int n, float scale) {
 
 static size_t rb(int dtype, int n) { return ora_row_bytes(dtype, (size_t)n); }
 
+/* 0: every projection through gemv_quant_q8k, as the reference's forward
+ * does. 1: through gemv_quant (f64 dots rounded once to f32) instead, to
+ * measure how far the reference's own Q8_K activation quantization moves
+ * the hidden state (the yardstick for sharded runs, whose rank-order sums
+ * move it too). Test infrastructure only. */
+static int g_exact_gemv = 0;
+
+void ora_forward_exact_gemv(int on) { g_exact_gemv = on; }
+
 static void gemv(float *out, const float *x, const uint8_t *w, int dtype, int din, int dout, int nthreads) {
-    ora_gemv_quant_q8k(out, x, w, rb(dtype, din) * (size_t)dout, (size_t)din, (size_t)dout, dtype, nthreads);
+    if (g_exact_gemv)
+        ora_gemv_quant(out, x, w, rb(dtype, din) * (size_t)dout, (size_t)din, (size_t)dout, dtype, nthreads);
+    else
+        ora_gemv_quant_q8k(out, x, w, rb(dtype, din) * (size_t)dout, (size_t)din, (size_t)dout, dtype, nthreads);
 }
 
 #define T(L, f) (tensors[ORA_T_GLOBALS + (L) * ORA_T_PER_LAYER + (f)])

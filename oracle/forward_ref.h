@@ -75,6 +75,10 @@ void ora_ssm_conv(float *out, const float *x, int ncs, const float *kernel, int 
  * oldest row first) and `gdn[i]` (n_v x hd x hd) belong to the i-th recurrent
  * layer, `kcache/vcache[i]` (ctx x n_head_kv*head_dim) to the i-th attention
  * layer; all are updated in place. `hidden_out` (n_embd) may be NULL. */
+/* Projections through gemv_quant (on = 1) instead of gemv_quant_q8k (0, the
+ * default and the reference's choice); process-wide. */
+void ora_forward_exact_gemv(int on);
+
 int ora_decode_token(const ora_model_cfg *c, void **tensors, const int *dtypes, float **conv, float **gdn,
                      float **kcache, float **vcache, int position, uint32_t token, float *logits, float *hidden_out,
                      int nthreads);

@@ -286,6 +286,12 @@ class Qwen35Oracle:
         self.position += 1
         return logits, hidden
 
+    @staticmethod
+    def exact_gemv(on: bool):
+        """Process-wide: every projection through gemv_quant (f64 dots)
+        instead of gemv_quant_q8k; measures the reference's own Q8_K error."""
+        lib().ora_forward_exact_gemv(1 if on else 0)
+
     def greedy(self, token: int, n_steps: int, nthreads: int = 8):
         """greedy.rs: step, argmax (first index of the max), feed back."""
         out, logits, hidden = [], None, None

@@ -82,7 +82,7 @@ def _run_torchrun(world, script, *args):
     return out
 
 
-@pytest.mark.parametrize("world", [4, 8])
+@pytest.mark.parametrize("world", [2, 4, 8])
 def test_tp_9b_decode_matches_oracle(world):
     """The 9B-class model at 4 and 8 GPUs: at 8 every rank holds one KV head
     shared by its pair of query heads and 4 of the 32 recurrent v heads; the

@@ -35,6 +35,7 @@ def main():
     ap.add_argument("--model", default="tiny", choices=["tiny", "9b"])
     ap.add_argument("--steps", type=int, default=8)
     ap.add_argument("--position", type=int, default=40)
+    ap.add_argument("--start", type=int, default=None, help="first token (default: 5 tiny, 7 for the 9B model)")
     ap.add_argument("--no-oracle", action="store_true")
     ap.add_argument("--allreduce", default="peer", choices=["peer", "nccl"],
                     help="peer: one kernel over NVLink peer memory; nccl: ncclAllReduce")
@@ -55,7 +56,8 @@ def main():
     m.load(tensors)
     s = m.session(pos0 + n + 10)
     s.set_state(pos0, st["conv"], st["gdn"], st["k"], st["v"])
-    warm = s.decode(5 if args.model == "tiny" else 1000, 2)  # captures the step graph
+    start = args.start if args.start is not None else (5 if args.model == "tiny" else 7)
+    warm = s.decode(start, 2)  # captures the step graph
     dist.barrier()
     torch.cuda.synchronize()
     t0 = time.perf_counter()
@@ -81,8 +83,17 @@ def main():
             import oracle
 
             o = oracle.Qwen35Oracle(cfg, tensors, pos0 + n + 10, st, pos0)
-            otoks, ol, oh = o.greedy(5 if args.model == "tiny" else 1000, n + 2, nthreads=os.cpu_count() or 8)
+            # the oracle's greedy loop, keeping every step's top-2 logit margin
+            otoks, margins, tok = [], [], start
+            for _ in range(n + 2):
+                ol, oh = o.step(tok, nthreads=os.cpu_count() or 8)
+                tok = oracle.argmax(ol)
+                top2 = np.sort(ol)[-2:]
+                otoks.append(tok)
+                margins.append(float((top2[1] - top2[0]) / abs(top2[1])))
             out["oracle_tokens"] = otoks
+            out["oracle_top2_margin_rel"] = [round(m, 6) for m in margins]
+            out["distinct_tokens"] = len(set(otoks))
             out["stream_matches_oracle"] = otoks == toks.tolist()
             out["logits_maxrel"] = float(np.max(np.abs(logits - ol)) / np.max(np.abs(ol)))
             out["hidden_maxrel"] = float(np.max(np.abs(hd - oh)) / np.max(np.abs(oh)))

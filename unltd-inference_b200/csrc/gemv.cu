@@ -331,17 +331,8 @@ __device__ __forceinline__ void load_xblock(const uint8_t *im, XBlock &x) {
   // column 0 = the balanced low bytes bl = ((s + 128) & 255) - 128 of the
   // eight group sums s, column 1 = the high bytes (s - bl) / 256 (|s| <=
   // 32 * 127, so both fit s8); rows 8..15 and columns 2..7 are zero
-  uint32_t bm = 0u;
-  if (gid < 2 && tig < 2) {
-    const int4 g4 = *reinterpret_cast<const int4 *>(im + kImgQ8K4_BS + 16 * tig);
-    const int gv[4] = {g4.x, g4.y, g4.z, g4.w};
-#pragma unroll
-    for (int i = 0; i < 4; i++) {
-      const int lo = ((gv[i] + 128) & 255) - 128, hi = (gv[i] - lo) >> 8;
-      bm |= (uint32_t)((gid == 0 ? lo : hi) & 0xFF) << (8 * i);
-    }
-  }
-  x.bm = bm;
+  // (precomputed by the image writer, kImgQ8K4_BM)
+  x.bm = (gid < 2 && tig < 2) ? *reinterpret_cast<const uint32_t *>(im + kImgQ8K4_BM + 4 * (2 * gid + tig)) : 0u;
   x.xd = *reinterpret_cast<const float *>(im + kImgQ8K4_D);
 }
 
@@ -963,6 +954,8 @@ __global__ void __launch_bounds__(NW * 32 + 32, 1) gemv_kernel(Params P) {
 // mbarrier and go on to the next tile; two chain buffers alternate, recycled
 // through a second mbarrier pair. Nothing waits on a CTA-wide barrier per
 // tile. Every wait is bounded.
+// The warp counts are template parameters (NIW integer warps, NCW chain
+// warps, one producer warp); the launches use kTcIntWarps / kTcChainWarps.
 constexpr int kTcIntWarps = 16, kTcChainWarps = 3;
 constexpr int kTcThreads = (kTcIntWarps + kTcChainWarps + 1) * 32;
 constexpr int kTcBarBytes = 256;
@@ -975,13 +968,14 @@ static_assert((2 * kMaxStages + 4) * 8 <= kTcBarBytes, "barrier area");
 // prologue, after griddepcontrol.wait: every CTA sums the n squares itself
 // (the reference's sequential f64 sum, resolved exactly as in the stand-alone
 // norm kernel), then each warp quantizes whole spans of xn = rmsnorm(r, w)
-// (quantize_q8_k) into the CTA's shared-memory image: warp w takes spans w
-// and w + 16, lane l their elements 8l .. 8l+7. CTA 0 also stores r and,
+// (quantize_q8_k) into the CTA's shared-memory image: warp w of NIW takes
+// spans w and w + NIW, lane l their elements 8l .. 8l+7. CTA 0 also stores r and,
 // when asked, the Q4_K / Q6_K images for later GEMVs. All pointers are
 // 16-byte aligned (checked by gemv_launch).
+template <int NIW>
 __device__ __forceinline__ void tc_norm_prologue(const Params &P, uint8_t *ximg) {
-  constexpr int NT = kTcIntWarps * 32;
-  __shared__ double red[kTcIntWarps];
+  constexpr int NT = NIW * 32;
+  __shared__ double red[NIW];
   __shared__ float s_mean;
   const int t = threadIdx.x, warp = t >> 5, lane = t & 31, n = P.nn, nsp = n >> 8;
   const bool cta0 = blockIdx.x == 0;
@@ -1008,7 +1002,7 @@ __device__ __forceinline__ void tc_norm_prologue(const Params &P, uint8_t *ximg)
   float r[kNormSpans][8], wv[kNormSpans][8];
 #pragma unroll
   for (int u = 0; u < kNormSpans; u++) {
-    const int e0 = (warp + kTcIntWarps * u) * 256 + 8 * lane;
+    const int e0 = (warp + NIW * u) * 256 + 8 * lane;
     float4 a0 = make_float4(0.f, 0.f, 0.f, 0.f), a1 = a0, b0 = a0, b1 = a0, w0 = a0, w1 = a0;
     if (e0 < n) {  // warp-uniform
       const float4 *pa = reinterpret_cast<const float4 *>(P.norm_a + e0);
@@ -1051,7 +1045,7 @@ __device__ __forceinline__ void tc_norm_prologue(const Params &P, uint8_t *ximg)
   if (cta0 && P.norm_r) {
 #pragma unroll
     for (int u = 0; u < kNormSpans; u++) {
-      const int e0 = (warp + kTcIntWarps * u) * 256 + 8 * lane;
+      const int e0 = (warp + NIW * u) * 256 + 8 * lane;
       if (e0 < n) {
         float4 *pr = reinterpret_cast<float4 *>(P.norm_r + e0);
         pr[0] = make_float4(r[u][0], r[u][1], r[u][2], r[u][3]);
@@ -1065,7 +1059,7 @@ __device__ __forceinline__ void tc_norm_prologue(const Params &P, uint8_t *ximg)
   named_bar_sync(1, NT);
   S = 0.0;
 #pragma unroll
-  for (int w = 0; w < kTcIntWarps; w++) S += red[w];
+  for (int w = 0; w < NIW; w++) S += red[w];
   float mean;
   const MeanOf f{n};
   if (!resolve_sum(S, S, n, f, &mean)) {  // S is the same in every thread
@@ -1092,7 +1086,7 @@ __device__ __forceinline__ void tc_norm_prologue(const Params &P, uint8_t *ximg)
   const float scale = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(mean, P.norm_eps)));
 #pragma unroll
   for (int u = 0; u < kNormSpans; u++) {
-    const int span = warp + kTcIntWarps * u;
+    const int span = warp + NIW * u;
     if (span < nsp) {  // warp-uniform
       float xn[8];
 #pragma unroll
@@ -1111,16 +1105,16 @@ __device__ __forceinline__ void tc_norm_prologue(const Params &P, uint8_t *ximg)
 
 // quantize_q8_k of x (quants.rs:250-290) in the integer warps' prologue,
 // after griddepcontrol.wait, while the producer already streams weights:
-// warp w takes spans w, w + 16, ... (lane l: elements 8l .. 8l+7), loads of
-// up to three spans in flight.
-template <int FMT>
+// warp w of NIW takes spans w, w + NIW, ... (lane l: elements 8l .. 8l+7),
+// loads of up to three spans in flight.
+template <int FMT, int NIW>
 __device__ __noinline__ void tc_quant_prologue(const float *__restrict__ x, int nsp, uint8_t *ximg) {
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  for (int s0 = warp; s0 < nsp; s0 += 3 * kTcIntWarps) {
+  for (int s0 = warp; s0 < nsp; s0 += 3 * NIW) {
     float4 v[3][2];
 #pragma unroll
     for (int q = 0; q < 3; q++) {
-      const int span = s0 + kTcIntWarps * q;
+      const int span = s0 + NIW * q;
       v[q][0] = v[q][1] = make_float4(0.f, 0.f, 0.f, 0.f);
       if (span < nsp) {
         const float4 *p = reinterpret_cast<const float4 *>(x + (size_t)span * 256 + 8 * lane);
@@ -1130,18 +1124,18 @@ __device__ __noinline__ void tc_quant_prologue(const float *__restrict__ x, int 
     }
 #pragma unroll
     for (int q = 0; q < 3; q++) {
-      const int span = s0 + kTcIntWarps * q;
+      const int span = s0 + NIW * q;
       if (span >= nsp) break;
       const float e[8] = {v[q][0].x, v[q][0].y, v[q][0].z, v[q][0].w, v[q][1].x, v[q][1].y, v[q][1].z, v[q][1].w};
       if constexpr (FMT == Q4K) q8k_span_write_warp(e, lane, ximg + (size_t)span * kImgQ8K4, nullptr);
       else q8k_span_write_warp(e, lane, nullptr, ximg + (size_t)span * kImgQ8K6);
     }
   }
-  named_bar_sync(1, kTcIntWarps * 32);
+  named_bar_sync(1, NIW * 32);
 }
 
-template <int FMT, bool ARGMAX, bool R8 = false>
-__global__ void __launch_bounds__(kTcThreads, 1) gemv_tc_kernel(Params P) {
+template <int FMT, bool ARGMAX, bool R8, int NIW, int NCW, int MINB>
+__global__ void __launch_bounds__((NIW + NCW + 1) * 32, MINB) gemv_tc_kernel(Params P) {
   constexpr int kImg = FMT == Q4K ? kImgQ8K4 : kImgQ8K6;
   extern __shared__ __align__(128) uint8_t smem[];
   uint64_t *full = reinterpret_cast<uint64_t *>(smem);
@@ -1162,17 +1156,17 @@ __global__ void __launch_bounds__(kTcThreads, 1) gemv_tc_kernel(Params P) {
   if (threadIdx.x == 0) {
     for (int st = 0; st < P.S; st++) {
       mbar_init(&full[st], 1);
-      mbar_init(&empty[st], kTcIntWarps);
+      mbar_init(&empty[st], NIW);
     }
     for (int b = 0; b < 2; b++) {
-      mbar_init(&intdone[b], kTcIntWarps);
-      mbar_init(&chaindone[b], kTcChainWarps);
+      mbar_init(&intdone[b], NIW);
+      mbar_init(&chaindone[b], NCW);
     }
     fence_mbar_init();
   }
   __syncthreads();
 
-  if (warp == kTcIntWarps + kTcChainWarps) {
+  if (warp == NIW + NCW) {
     // ---------------- producer: padded rows, one bulk copy per row ----------
     if (lane == 0) {
       int issued = 0;
@@ -1196,23 +1190,23 @@ __global__ void __launch_bounds__(kTcThreads, 1) gemv_tc_kernel(Params P) {
   }
 
   pdl_wait();
-  if (warp < kTcIntWarps) {
+  if (warp < NIW) {
     // ---------------- integer warps -------------------------------------------
     if (FMT == Q4K && P.nn) {
-      tc_norm_prologue(P, ximg);
+      tc_norm_prologue<NIW>(P, ximg);
     } else if (P.xq) {
-      tc_quant_prologue<FMT>(P.xq, P.nbu, ximg);
+      tc_quant_prologue<FMT, NIW>(P.xq, P.nbu, ximg);
     } else {
       const uint4 *src = reinterpret_cast<const uint4 *>(P.img);
       uint4 *dst = reinterpret_cast<uint4 *>(ximg);
-      for (int k = threadIdx.x; k < P.img_bytes / 16; k += kTcIntWarps * 32) dst[k] = src[k];
-      named_bar_sync(1, kTcIntWarps * 32);
+      for (int k = threadIdx.x; k < P.img_bytes / 16; k += NIW * 32) dst[k] = src[k];
+      named_bar_sync(1, NIW * 32);
     }
     // when the block count divides the warp count, a warp always takes the
     // same block (row groups rg0, rg0 + rgs, ...): its x operands stay in
     // registers for the whole kernel
-    const bool fixed = kTcIntWarps % P.nbu == 0;
-    const int myb = warp % P.nbu, rg0 = warp / P.nbu, rgs = kTcIntWarps / P.nbu;
+    const bool fixed = NIW % P.nbu == 0;
+    const int myb = warp % P.nbu, rg0 = warp / P.nbu, rgs = NIW / P.nbu;
     using XB = std::conditional_t<FMT == Q4K, XBlock, XBlock6>;
     XB xb;
     auto load_xb = [&](int b, XB &x) {
@@ -1237,7 +1231,7 @@ __global__ void __launch_bounds__(kTcThreads, 1) gemv_tc_kernel(Params P) {
       if (fixed) {
         for (int g16 = rg0; g16 < ng; g16 += rgs) item(tile, nr, g16, myb, xb, cb, cm);
       } else {
-        for (int it = warp; it < ng * P.nbu; it += kTcIntWarps) {
+        for (int it = warp; it < ng * P.nbu; it += NIW) {
           const int g16 = it / P.nbu, b = it - g16 * P.nbu;
           XB xv;
           load_xb(b, xv);
@@ -1254,7 +1248,7 @@ __global__ void __launch_bounds__(kTcThreads, 1) gemv_tc_kernel(Params P) {
   }
 
   // ---------------- chain warps: the sequential per-row epilogue ------------
-  const int ct = threadIdx.x - kTcIntWarps * 32;  // 0 .. 32 * kTcChainWarps - 1
+  const int ct = threadIdx.x - NIW * 32;  // 0 .. 32 * NCW - 1
   const int k = ct & 7;
   const unsigned gm = 0xFFu << (lane & 24);
   unsigned long long best = 0ull;
@@ -1264,7 +1258,7 @@ __global__ void __launch_bounds__(kTcThreads, 1) gemv_tc_kernel(Params P) {
     const int r0 = rb + i * P.T;
     const int nr = min(P.T, re - r0);
     const float *cb = reinterpret_cast<const float *>(reinterpret_cast<const uint8_t *>(cbuf0) + (i & 1) * P.cbuf_bytes);
-    for (int lr = ct >> 3; lr < nr; lr += kTcChainWarps * 4) {
+    for (int lr = ct >> 3; lr < nr; lr += NCW * 4) {
       const float *tk = cb + lr * P.rs + k;
       const float *tm = cb + P.T * P.rs + lr * (P.rs / 8);
       float sums = 0.0f, sumf = 0.0f;
@@ -1305,7 +1299,7 @@ __global__ void __launch_bounds__(kTcThreads, 1) gemv_tc_kernel(Params P) {
     // the last CTA to finish raises this rank's flag in every area (after a
     // system fence) and advances the all-reduce counter
     __threadfence_system();
-    named_bar_sync(2, kTcChainWarps * 32);
+    named_bar_sync(2, NCW * 32);
     if (ct == 0) {
       const unsigned prev = atomicAdd(P.peer_done, 1u);
       if (prev == gridDim.x - 1) {
@@ -1318,17 +1312,373 @@ __global__ void __launch_bounds__(kTcThreads, 1) gemv_tc_kernel(Params P) {
     }
   }
   if constexpr (ARGMAX) {
-    __shared__ unsigned long long cta_best[kTcChainWarps];
+    __shared__ unsigned long long cta_best[NCW];
     for (int o = 16; o; o >>= 1) {
       const unsigned long long other = __shfl_xor_sync(0xffffffffu, best, o);
       best = other > best ? other : best;
     }
-    if (lane == 0) cta_best[warp - kTcIntWarps] = best;
-    named_bar_sync(2, kTcChainWarps * 32);
+    if (lane == 0) cta_best[warp - NIW] = best;
+    named_bar_sync(2, NCW * 32);
     if (ct == 0) {
       unsigned long long b = cta_best[0];
-      for (int w2 = 1; w2 < kTcChainWarps; w2++) b = cta_best[w2] > b ? cta_best[w2] : b;
+      for (int w2 = 1; w2 < NCW; w2++) b = cta_best[w2] > b ? cta_best[w2] : b;
       atomicMax(P.key, b);
+      __threadfence();
+      const unsigned prev = atomicAdd(P.done, 1u);
+      if (prev == gridDim.x - 1) {
+        __threadfence();
+        const unsigned long long kf = atomicAdd(P.key, 0ull);
+        *P.token = 0xffffffffu - (uint32_t)(kf & 0xffffffffull);
+        if (P.key_out) *P.key_out = kf;
+        *P.key = 0ull;
+        *P.done = 0u;
+      }
+    }
+  }
+}
+
+// ---------------------------------------------------------------- lean ----
+// The tensor-core GEMV specialised on its shape: blocks per row (NBU), rows
+// per tile (T) and the padded shared-memory row stride are compile-time
+// constants, so every shared-memory address is a register plus an immediate
+// and the loops unroll without bounds checks. Used for the decode step's
+// shapes (4096 or 12288 inputs); other shapes take gemv_tc_kernel. The same
+// arithmetic, so the same bits.
+//
+//  * integer warps: with NBU == NIW a warp owns one block for the whole
+//    kernel (its x operands stay in registers) and runs that block for every
+//    16-row group of a tile; otherwise it takes blocks warp, warp + NIW, ...
+//    and loads the block's x operands per item. Rows past the end of a
+//    partial tile compute on stale shared memory; the chain never reads them.
+//  * chain warp(s): T >= 16: lane = row, each lane runs the nine sequential
+//    f32 chains of its row (sums[0..7] and the min term) over the blocks with
+//    128-bit loads of the row's eight class products per block; T == 8:
+//    lane = (row, class) as in gemv_tc_kernel.
+template <int FMT, int NBU>
+struct LeanShape {
+  static constexpr int kRowBytes = NBU * (FMT == Q4K ? 144 : 210);
+  static constexpr int kPs = (kRowBytes + 127) / 128 * 128 + (FMT == Q4K ? 32 : 16);
+  static constexpr int kImg = FMT == Q4K ? kImgQ8K4 : kImgQ8K6;
+  static constexpr int kRs = 8 * NBU + 4;   // chain row: eight class products per block (+4: bank spread)
+  static constexpr int kRsm = NBU + 1;      // Q4_K min-term row
+};
+
+template <int FMT, int NBU, int T>
+constexpr int lean_cbuf_bytes() {
+  return ((T * LeanShape<FMT, NBU>::kRs + (FMT == Q4K ? T * LeanShape<FMT, NBU>::kRsm : 0)) * 4 + 127) / 128 * 128;
+}
+
+template <int NBU, int PS, int RS, int RSM>
+__device__ __forceinline__ void q4k_item_lean(const uint8_t *tile, int g16, int b, const XBlock &x, float *tk,
+                                              float *tm) {
+  const int lane = threadIdx.x & 31, gid = lane >> 2, tig = lane & 3;
+  const int lr0 = g16 * 16 + gid;
+  const uint8_t *row0 = tile + lr0 * PS;
+  const uint8_t *row1 = row0 + 8 * PS;
+  const uint4 h0 = lds128(row0 + b * 16), h1 = lds128(row1 + b * 16);
+  const int qo = NBU * 16 + b * 128 + 8 * tig;
+  uint2 w0[4], w1[4];
+#pragma unroll
+  for (int p = 0; p < 4; p++) {
+    w0[p] = lds64(row0 + qo + 32 * p);
+    w1[p] = lds64(row1 + qo + 32 * p);
+  }
+  const uint32_t SCa0 = h0.y & 0x3F3F3F3Fu, SCb0 = (h0.w & 0x0F0F0F0Fu) | ((h0.y >> 2) & 0x30303030u);
+  const uint32_t SCa1 = h1.y & 0x3F3F3F3Fu, SCb1 = (h1.w & 0x0F0F0F0Fu) | ((h1.y >> 2) & 0x30303030u);
+  int lo0 = 0, lo1 = 0, lo2 = 0, lo3 = 0, hi0 = 0, hi1 = 0, hi2 = 0, hi3 = 0;
+#pragma unroll
+  for (int p = 0; p < 4; p++) {
+    const uint32_t S0 = p < 2 ? SCa0 : SCb0, S1 = p < 2 ? SCa1 : SCb1;
+    const int k = (2 * p) & 3;
+    int d0, d1, d2, d3, e0, e1, e2, e3;
+    mma_s8(w0[p].x & 0x0F0F0F0Fu, w1[p].x & 0x0F0F0F0Fu, w0[p].y & 0x0F0F0F0Fu, w1[p].y & 0x0F0F0F0Fu, x.b0[2 * p],
+           x.b1[2 * p], d0, d1, d2, d3);
+    mma_u8s8(w0[p].x & 0xF0F0F0F0u, w1[p].x & 0xF0F0F0F0u, w0[p].y & 0xF0F0F0F0u, w1[p].y & 0xF0F0F0F0u,
+             x.b0[2 * p + 1], x.b1[2 * p + 1], e0, e1, e2, e3);
+    const int s0 = byte_of(S0, k), s1 = byte_of(S1, k), t0 = byte_of(S0, k + 1), t1 = byte_of(S1, k + 1);
+    lo0 += s0 * d0;
+    lo1 += s0 * d1;
+    lo2 += s1 * d2;
+    lo3 += s1 * d3;
+    hi0 += t0 * e0;
+    hi1 += t0 * e1;
+    hi2 += t1 * e2;
+    hi3 += t1 * e3;
+  }
+  const int acc0 = lo0 + (hi0 >> 4), acc1 = lo1 + (hi1 >> 4), acc2 = lo2 + (hi2 >> 4), acc3 = lo3 + (hi3 >> 4);
+  const uint32_t MA0 = h0.z & 0x3F3F3F3Fu, MB0 = ((h0.w >> 4) & 0x0F0F0F0Fu) | ((h0.z >> 2) & 0x30303030u);
+  const uint32_t MA1 = h1.z & 0x3F3F3F3Fu, MB1 = ((h1.w >> 4) & 0x0F0F0F0Fu) | ((h1.z >> 2) & 0x30303030u);
+  int mn0, mn1, mn2, mn3;
+  mma_s8_k16(tig == 0 ? MA0 : (tig == 1 ? MB0 : 0u), tig == 0 ? MA1 : (tig == 1 ? MB1 : 0u), x.bm, mn0, mn1, mn2,
+             mn3);
+  const float d0 = __fmul_rn(x.xd, h2f_bits(h0.x & 0xFFFFu)), dm0 = __fmul_rn(h2f_bits(h0.x >> 16), x.xd);
+  const float d1 = __fmul_rn(x.xd, h2f_bits(h1.x & 0xFFFFu)), dm1 = __fmul_rn(h2f_bits(h1.x >> 16), x.xd);
+  *reinterpret_cast<float2 *>(tk + lr0 * RS + 8 * b + 2 * tig) =
+      make_float2(__fmul_rn(d0, (float)acc0), __fmul_rn(d0, (float)acc1));
+  *reinterpret_cast<float2 *>(tk + (lr0 + 8) * RS + 8 * b + 2 * tig) =
+      make_float2(__fmul_rn(d1, (float)acc2), __fmul_rn(d1, (float)acc3));
+  if (tig == 0) {
+    tm[lr0 * RSM + b] = __fmul_rn(dm0, (float)(mn0 + mn1 * 256));
+    tm[(lr0 + 8) * RSM + b] = __fmul_rn(dm1, (float)(mn2 + mn3 * 256));
+  }
+}
+
+template <bool R8, int NBU, int PS, int RS>
+__device__ __forceinline__ void q6k_item_lean(const uint8_t *tile, int g16, int b, const XBlock6 &x, float *tk) {
+  const int lane = threadIdx.x & 31, gid = lane >> 2, tig = lane & 3;
+  const int lr0 = (R8 ? 8 : 16) * g16 + gid;
+  const uint8_t *row0 = tile + lr0 * PS;
+  const uint8_t *row1 = row0 + 8 * PS;
+  const int qlo = b * 128 + 4 * tig, qho = NBU * 128 + b * 64 + 4 * tig;
+  uint32_t l0[8], l1[8], h0[4], h1[4];
+#pragma unroll
+  for (int j = 0; j < 8; j++) {
+    l0[j] = *reinterpret_cast<const uint32_t *>(row0 + qlo + 16 * j);
+    l1[j] = R8 ? 0u : *reinterpret_cast<const uint32_t *>(row1 + qlo + 16 * j);
+  }
+#pragma unroll
+  for (int c = 0; c < 4; c++) {
+    h0[c] = *reinterpret_cast<const uint32_t *>(row0 + qho + 16 * c);
+    h1[c] = R8 ? 0u : *reinterpret_cast<const uint32_t *>(row1 + qho + 16 * c);
+  }
+  const uint4 sc0 = lds128(row0 + NBU * 192 + b * 16);
+  const uint4 sc1 = R8 ? make_uint4(0u, 0u, 0u, 0u) : lds128(row1 + NBU * 192 + b * 16);
+  const uint32_t S0[4] = {sc0.x, sc0.y, sc0.z, sc0.w}, S1[4] = {sc1.x, sc1.y, sc1.z, sc1.w};
+  const uint32_t db0 = *reinterpret_cast<const unsigned short *>(row0 + NBU * 208 + b * 2);
+  const uint32_t db1 = R8 ? 0u : *reinterpret_cast<const unsigned short *>(row1 + NBU * 208 + b * 2);
+  int acc0 = 0, acc1 = 0, acc2 = 0, acc3 = 0;
+#pragma unroll
+  for (int j = 0; j < 8; j++) {
+    const int h = j >> 2, u = j & 3, sl = 2 * (u >> 1), c = 2 * h + (u & 1);
+    const int slo = 8 * h + u, shi = slo + 4;
+    int d0, d1, d2, d3, e0, e1, e2, e3;
+    mma_s8_k16(q6_a4_lo(l0[j], h0[c], sl), R8 ? 0u : q6_a4_lo(l1[j], h1[c], sl), x.b[2 * j], d0, d1, d2, d3);
+    mma_s8_k16(q6_a4_hi(l0[j], h0[c], sl), R8 ? 0u : q6_a4_hi(l1[j], h1[c], sl), x.b[2 * j + 1], e0, e1, e2, e3);
+    const int s0 = sbyte_of(S0[slo >> 2], slo & 3), t0 = sbyte_of(S0[shi >> 2], shi & 3);
+    acc0 += s0 * d0 + t0 * e0;
+    acc1 += s0 * d1 + t0 * e1;
+    if (!R8) {
+      const int s1 = sbyte_of(S1[slo >> 2], slo & 3), t1 = sbyte_of(S1[shi >> 2], shi & 3);
+      acc2 += s1 * d2 + t1 * e2;
+      acc3 += s1 * d3 + t1 * e3;
+    }
+  }
+  const float d0 = __fmul_rn(x.xd, h2f_bits(db0));
+  *reinterpret_cast<float2 *>(tk + lr0 * RS + 8 * b + 2 * tig) =
+      make_float2(__fmul_rn(d0, (float)(acc0 >> 2)), __fmul_rn(d0, (float)(acc1 >> 2)));
+  if (!R8) {
+    const float d1 = __fmul_rn(x.xd, h2f_bits(db1));
+    *reinterpret_cast<float2 *>(tk + (lr0 + 8) * RS + 8 * b + 2 * tig) =
+        make_float2(__fmul_rn(d1, (float)(acc2 >> 2)), __fmul_rn(d1, (float)(acc3 >> 2)));
+  }
+}
+
+// Emits one finished row: y, this rank's slot of every peer area, the argmax key.
+template <bool ARGMAX>
+__device__ __forceinline__ void lean_emit_row(const Params &P, int row, float acc, unsigned send_ep,
+                                              unsigned long long &best) {
+  if (P.y) P.y[row] = acc;
+  if (P.peer_send)
+    for (int rr = 0; rr < P.peer_n; rr++) peer_slot(P.peer_map[rr], send_ep, P.peer_rank)[row] = acc;
+  if (ARGMAX) {
+    const unsigned long long k2 = argmax_key(acc, P.row0 + row);
+    best = k2 > best ? k2 : best;
+  }
+}
+
+template <int FMT, int NBU, int T, int NIW, int NCW, bool ARGMAX, int MINB>
+__global__ void __launch_bounds__((NIW + NCW + 1) * 32, MINB) gemv_lean_kernel(Params P) {
+  using Sh = LeanShape<FMT, NBU>;
+  constexpr bool R8 = T == 8;
+  constexpr int PS = Sh::kPs, RS = Sh::kRs, RSM = Sh::kRsm;
+  constexpr int STAGE = (T * PS + 127) / 128 * 128;
+  constexpr int CBUF = lean_cbuf_bytes<FMT, NBU, T>();
+  extern __shared__ __align__(128) uint8_t smem[];
+  uint64_t *full = reinterpret_cast<uint64_t *>(smem);
+  uint64_t *empty = full + kMaxStages;
+  uint64_t *intdone = empty + kMaxStages;
+  uint64_t *chaindone = intdone + 2;
+  uint8_t *ximg = smem + kTcBarBytes;
+  uint8_t *cbase = ximg + NBU * Sh::kImg;
+  uint8_t *stages = cbase + 2 * CBUF;
+  const int S = P.S;
+  pdl_trigger();
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int G = gridDim.x;
+  const int rb = (int)((long long)P.rows * blockIdx.x / G);
+  const int re = (int)((long long)P.rows * (blockIdx.x + 1) / G);
+  const int ntiles = (re - rb + T - 1) / T;
+
+  if (threadIdx.x == 0) {
+    for (int st = 0; st < S; st++) {
+      mbar_init(&full[st], 1);
+      mbar_init(&empty[st], NIW);
+    }
+    for (int bb = 0; bb < 2; bb++) {
+      mbar_init(&intdone[bb], NIW);
+      mbar_init(&chaindone[bb], NCW);
+    }
+    fence_mbar_init();
+  }
+  __syncthreads();
+
+  if (warp == NIW + NCW) {
+    // ---------------- producer: one bulk copy per (padded) row --------------
+    if (lane == 0) {
+      int issued = 0;
+      for (int i = 0; i < ntiles; i++) {
+        const int st = i % S;
+        if (i >= S && !mbar_wait_bounded(&empty[st], ((i / S) - 1) & 1, P.err)) break;
+        const int r0 = rb + i * T;
+        const int nr = min(T, re - r0);
+        mbar_expect_tx(&full[st], (uint32_t)(nr * Sh::kRowBytes));
+        const uint8_t *src = P.W + (size_t)r0 * Sh::kRowBytes;
+        uint8_t *dst = stages + (size_t)st * STAGE;
+        for (int rr = 0; rr < nr; rr++) bulk_g2s(dst + rr * PS, src + (size_t)rr * Sh::kRowBytes, Sh::kRowBytes, &full[st]);
+        issued = i + 1;
+      }
+      for (int i = max(0, issued - S); i < issued; i++) mbar_wait_bounded(&full[i % S], (i / S) & 1, P.err);
+    }
+    return;
+  }
+
+  pdl_wait();
+  if (warp < NIW) {
+    // ---------------- integer warps -------------------------------------------
+    if (FMT == Q4K && P.nn) {
+      tc_norm_prologue<NIW>(P, ximg);
+    } else if (P.xq) {
+      tc_quant_prologue<FMT, NIW>(P.xq, NBU, ximg);
+    } else {
+      const uint4 *src = reinterpret_cast<const uint4 *>(P.img);
+      uint4 *dst = reinterpret_cast<uint4 *>(ximg);
+      for (int k = threadIdx.x; k < NBU * Sh::kImg / 16; k += NIW * 32) dst[k] = src[k];
+      named_bar_sync(1, NIW * 32);
+    }
+    using XB = std::conditional_t<FMT == Q4K, XBlock, XBlock6>;
+    auto load_xb = [&](int b, XB &x) {
+      if constexpr (FMT == Q4K) load_xblock(ximg + (size_t)b * Sh::kImg, x);
+      else load_xblock6(ximg + (size_t)b * Sh::kImg, x);
+    };
+    constexpr int NG = R8 ? 1 : T / 16;  // 16-row groups of a tile (R8: one half-height group)
+    constexpr bool kFixed = NBU == NIW;
+    XB xb;
+    if (kFixed) load_xb(warp, xb);
+    for (int i = 0; i < ntiles; i++) {
+      const int st = i % S;
+      if (!mbar_wait_bounded(&full[st], (i / S) & 1, P.err)) break;
+      if (i >= 2 && !mbar_wait_bounded(&chaindone[i & 1], ((i >> 1) - 1) & 1, P.err)) break;
+      const uint8_t *tile = stages + (size_t)st * STAGE;
+      float *tk = reinterpret_cast<float *>(cbase + (i & 1) * CBUF);
+      float *tm = tk + T * RS;
+      if constexpr (kFixed) {
+#pragma unroll
+        for (int g = 0; g < NG; g++) {
+          if constexpr (FMT == Q4K) q4k_item_lean<NBU, PS, RS, RSM>(tile, g, warp, xb, tk, tm);
+          else q6k_item_lean<R8, NBU, PS, RS>(tile, g, warp, xb, tk);
+        }
+      } else {
+#pragma unroll 1
+        for (int b = warp; b < NBU; b += NIW) {
+          XB xv;
+          load_xb(b, xv);
+#pragma unroll
+          for (int g = 0; g < NG; g++) {
+            if constexpr (FMT == Q4K) q4k_item_lean<NBU, PS, RS, RSM>(tile, g, b, xv, tk, tm);
+            else q6k_item_lean<R8, NBU, PS, RS>(tile, g, b, xv, tk);
+          }
+        }
+      }
+      __syncwarp();
+      if (lane == 0) {
+        mbar_arrive(&empty[st]);
+        mbar_arrive(&intdone[i & 1]);
+      }
+    }
+    return;
+  }
+
+  // ---------------- chain warp(s): the sequential per-row epilogue -----------
+  const int ct = threadIdx.x - NIW * 32;
+  unsigned long long best = 0ull;
+  const unsigned send_ep = P.peer_send ? *P.peer_ctr + 1u : 0u;
+  for (int i = 0; i < ntiles; i++) {
+    if (!mbar_wait_bounded(&intdone[i & 1], (i >> 1) & 1, P.err)) break;
+    const int r0 = rb + i * T;
+    const int nr = min(T, re - r0);
+    const float *tk = reinterpret_cast<const float *>(cbase + (i & 1) * CBUF);
+    const float *tm = tk + T * RS;
+    if constexpr (!R8) {
+      // lane = row: sums[k] += d * sumi[k] over the blocks (the products are
+      // in tk), sumf -= dmin * minsum, then s = sumf + sums[0] + ... + sums[7]
+      for (int lr = ct; lr < nr; lr += NCW * 32) {
+        const float *row = tk + lr * RS;
+        float s[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+        float sumf = 0.0f;
+#pragma unroll
+        for (int b = 0; b < NBU; b++) {
+          const float4 a = *reinterpret_cast<const float4 *>(row + 8 * b);
+          const float4 c = *reinterpret_cast<const float4 *>(row + 8 * b + 4);
+          s[0] = __fadd_rn(s[0], a.x);
+          s[1] = __fadd_rn(s[1], a.y);
+          s[2] = __fadd_rn(s[2], a.z);
+          s[3] = __fadd_rn(s[3], a.w);
+          s[4] = __fadd_rn(s[4], c.x);
+          s[5] = __fadd_rn(s[5], c.y);
+          s[6] = __fadd_rn(s[6], c.z);
+          s[7] = __fadd_rn(s[7], c.w);
+          if constexpr (FMT == Q4K) sumf = __fsub_rn(sumf, tm[lr * RSM + b]);
+        }
+        float acc = sumf;
+#pragma unroll
+        for (int k = 0; k < 8; k++) acc = __fadd_rn(acc, s[k]);
+        lean_emit_row<ARGMAX>(P, r0 + lr, acc, send_ep, best);
+      }
+    } else {
+      // lane = (row, class): 8-row tiles of long rows (Q6_K, no min term)
+      const int k = ct & 7;
+      const unsigned gm = 0xFFu << (lane & 24);
+      for (int lr = ct >> 3; lr < T; lr += NCW * 4) {
+        const float *tkr = tk + lr * RS + k;
+        float sums = 0.0f;
+#pragma unroll 16
+        for (int b = 0; b < NBU; b++) sums = __fadd_rn(sums, tkr[8 * b]);
+        float acc = 0.0f;
+#pragma unroll
+        for (int kk = 0; kk < 8; kk++) acc = __fadd_rn(acc, __shfl_sync(gm, sums, (lane & 24) + kk));
+        if (k == 0 && lr < nr) lean_emit_row<ARGMAX>(P, r0 + lr, acc, send_ep, best);
+      }
+    }
+    __syncwarp();
+    if (lane == 0) mbar_arrive(&chaindone[i & 1]);
+  }
+  if (P.peer_send) {
+    __threadfence_system();
+    named_bar_sync(2, NCW * 32);
+    if (ct == 0) {
+      const unsigned prev = atomicAdd(P.peer_done, 1u);
+      if (prev == gridDim.x - 1) {
+        __threadfence_system();
+        for (int rr = 0; rr < P.peer_n; rr++)
+          peer_st_release(reinterpret_cast<unsigned *>(P.peer_map[rr]) + P.peer_rank, send_ep);
+        *P.peer_ctr = send_ep;
+        *P.peer_done = 0u;
+      }
+    }
+  }
+  if constexpr (ARGMAX) {
+    __shared__ unsigned long long cta_best[NCW];
+    for (int o = 16; o; o >>= 1) {
+      const unsigned long long other = __shfl_xor_sync(0xffffffffu, best, o);
+      best = other > best ? other : best;
+    }
+    if (lane == 0) cta_best[warp - NIW] = best;
+    named_bar_sync(2, NCW * 32);
+    if (ct == 0) {
+      unsigned long long bb = cta_best[0];
+      for (int w2 = 1; w2 < NCW; w2++) bb = cta_best[w2] > bb ? cta_best[w2] : bb;
+      atomicMax(P.key, bb);
       __threadfence();
       const unsigned prev = atomicAdd(P.done, 1u);
       if (prev == gridDim.x - 1) {
@@ -1392,10 +1742,13 @@ GemvFn pick_r(int R) {
   return R == 1 ? gemv_kernel<FMT, MODE, 1, AM> : gemv_kernel<FMT, MODE, 2, AM>;
 }
 
+// mma: 0 DP4A kernel; tensor-core kernel 1 (16-row MMA items), 2 with 8-row
+// tiles (Q6_K)
 template <bool AM>
 GemvFn pick(int fmt, int mode, int R, int mma = 0) {
-  if (mma == 2) return gemv_tc_kernel<Q6K, AM, true>;  // 8-row tiles (Q6_K only)
-  if (mma) return fmt == Q4K ? gemv_tc_kernel<Q4K, AM> : gemv_tc_kernel<Q6K, AM>;
+  constexpr int FI = kTcIntWarps, FC = kTcChainWarps;
+  if (mma == 2) return gemv_tc_kernel<Q6K, AM, true, FI, FC, 1>;  // 8-row tiles (Q6_K only)
+  if (mma) return fmt == Q4K ? gemv_tc_kernel<Q4K, AM, false, FI, FC, 1> : gemv_tc_kernel<Q6K, AM, false, FI, FC, 1>;
   if (mode == MODE_F32X) {
     if (fmt == Q4K) return pick_r<Q4K, MODE_F32X, AM>(R);
     if (fmt == Q6K) return pick_r<Q6K, MODE_F32X, AM>(R);
@@ -1405,17 +1758,20 @@ GemvFn pick(int fmt, int mode, int R, int mma = 0) {
   return pick_r<Q6K, MODE_Q8K, AM>(R);
 }
 
-int max_smem_optin(int device) {
+int device_attr_cached(int device, cudaDeviceAttr attr) {
   static std::mutex mu;
-  static std::vector<std::pair<int, int>> cache;
+  static std::vector<std::pair<std::pair<int, int>, int>> cache;
   std::lock_guard<std::mutex> lk(mu);
   for (auto &e : cache)
-    if (e.first == device) return e.second;
+    if (e.first.first == device && e.first.second == (int)attr) return e.second;
   int v = 0;
-  cudaDeviceGetAttribute(&v, cudaDevAttrMaxSharedMemoryPerBlockOptin, device);
-  cache.push_back({device, v});
+  cudaDeviceGetAttribute(&v, attr, device);
+  cache.push_back({{device, (int)attr}, v});
   return v;
 }
+
+int max_smem_optin(int device) { return device_attr_cached(device, cudaDevAttrMaxSharedMemoryPerBlockOptin); }
+
 
 // cudaFuncSetAttribute applies to the current device's context, so the cache
 // is keyed by (device, kernel): a process that drives several GPUs sets the
@@ -1434,6 +1790,40 @@ cudaError_t ensure_smem_attr(int device, GemvFn fn, int smem) {
   const cudaError_t err = cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
   if (err == cudaSuccess) done.push_back({device, fn, smem});
   return err;
+}
+
+// The shape-specialised kernel for w in Q8K mode, or null: Q4_K or Q6_K rows
+// of 4096 inputs, Q6_K rows of 12288, every row a whole number of blocks
+// with no padding. Fills the tile rows, stages, dynamic shared memory and
+// block size of its launch.
+struct LeanPlan {
+  GemvFn fn = nullptr;
+  int T = 0, S = 0, smem = 0, threads = 0, img_bytes = 0;
+};
+
+template <int FMT, int NBU, int T, int NIW = kTcIntWarps, int MINB = 1>
+LeanPlan lean_plan(bool am, int smem_max) {
+  using Sh = LeanShape<FMT, NBU>;
+  constexpr int stage = (T * Sh::kPs + 127) / 128 * 128;
+  constexpr int fixed = kTcBarBytes + NBU * Sh::kImg + 2 * lean_cbuf_bytes<FMT, NBU, T>();
+  LeanPlan p;
+  p.S = std::min(kMaxStages, (smem_max - fixed) / stage);
+  if (p.S < 2) return p;
+  p.fn = am ? gemv_lean_kernel<FMT, NBU, T, NIW, 1, true, MINB> : gemv_lean_kernel<FMT, NBU, T, NIW, 1, false, MINB>;
+  p.T = T;
+  p.smem = fixed + p.S * stage;
+  p.threads = (NIW + 2) * 32;
+  p.img_bytes = NBU * Sh::kImg;
+  return p;
+}
+
+LeanPlan lean_for(int device, const unltd_weight_s &w, int mode, bool am) {
+  if (mode != MODE_Q8K || w.row_stride != w.row_bytes) return LeanPlan();
+  const int smem_max = max_smem_optin(device) - 1024;
+  if (w.dtype == Q4K && w.dim_in == 4096) return lean_plan<Q4K, 16, 32>(am, smem_max);
+  if (w.dtype == Q6K && w.dim_in == 4096) return lean_plan<Q6K, 16, 16>(am, smem_max);
+  if (w.dtype == Q6K && w.dim_in == 12288) return lean_plan<Q6K, 48, 8>(am, smem_max);
+  return LeanPlan();
 }
 
 }  // namespace
@@ -1457,15 +1847,20 @@ cudaError_t gemv_prewarm(int device) {
         set(pick<false>(fmt, mode, r));
         set(pick<true>(fmt, mode, r));
         if (fmt != Q8_0 && mode == MODE_Q8K) {
-          set(pick<false>(fmt, mode, r, 1));
-          set(pick<true>(fmt, mode, r, 1));
-          if (fmt == Q6K) {
-            set(pick<false>(fmt, mode, r, 2));
-            set(pick<true>(fmt, mode, r, 2));
+          for (int mma = 1; mma <= 2; mma++) {
+            if (mma == 2 && fmt != Q6K) continue;
+            set(pick<false>(fmt, mode, r, mma));
+            set(pick<true>(fmt, mode, r, mma));
           }
         }
       }
     }
+  for (int am = 0; am < 2; am++) {
+    const GemvFn lean[3] = {lean_plan<Q4K, 16, 32>(am, m).fn, lean_plan<Q6K, 16, 16>(am, m).fn,
+                            lean_plan<Q6K, 48, 8>(am, m).fn};
+    for (GemvFn fn : lean)
+      if (fn) set(fn);
+  }
   return first;
 }
 
@@ -1488,7 +1883,7 @@ int32_t gemv_reserve(unltd_ctx ctx, const unltd_weight_s &w, int mode) {
 // Tile plan of a quantized GEMV: rows per tile T (R rows per work item),
 // stages S, shared-memory layout, grid. S < 2: the row does not fit.
 struct Plan {
-  int nbu, img_bytes, rows, R, T, S, stage_bytes, cbuf, pstride, mma, rs, smem, grid;
+  int nbu, img_bytes, rows, R, T, S, stage_bytes, cbuf, pstride, mma, rs, smem, grid, threads, niw;
 };
 
 Plan plan_gemv(unltd_ctx ctx, const unltd_weight_s &w, int mode) {
@@ -1516,7 +1911,7 @@ Plan plan_gemv(unltd_ctx ctx, const unltd_weight_s &w, int mode) {
   // memory so the eight rows of an MMA fragment load from distinct banks (a
   // stride of 32 mod 128 bytes for the 8-byte Q4_K loads, 16 for the 4-byte
   // Q6_K loads)
-  if ((fmt == Q4K || fmt == Q6K) && mode == MODE_Q8K) {
+  if ((fmt == Q4K || fmt == Q6K) && mode == MODE_Q8K && !mma) {
     const int ps = (int)round_up((size_t)stride, 128) + (fmt == Q4K ? 32 : 16);
     // 32-row tiles (two MMA row groups per block item) measured faster than
     // 16-row tiles with deeper rings; Q6_K rows too long for two 16-row
@@ -1577,6 +1972,8 @@ Plan plan_gemv(unltd_ctx ctx, const unltd_weight_s &w, int mode) {
   p.rs = rs;
   p.smem = (mma ? kTcBarBytes : kBarBytes) + img_bytes + 2 * cbuf + S * stage_bytes;
   p.grid = T ? std::max(1, std::min(ctx->num_sms, (rows + T - 1) / T)) : 1;
+  p.threads = mma ? kTcThreads : kGemvThreads;
+  p.niw = kTcIntWarps;
   return p;
 }
 
@@ -1588,9 +1985,8 @@ bool gemv_tc_eligible(unltd_ctx ctx, const unltd_weight_s &w, int mode) {
 
 bool gemv_norm_fusable(unltd_ctx ctx, const unltd_weight_s &w, int mode) {
   if (w.dtype != Q4K || mode != MODE_Q8K || w.dim_out == 0) return false;
-  if (w.dim_in > (size_t)kNormSpans * kTcIntWarps * 256) return false;
   const Plan p = plan_gemv(ctx, w, mode);
-  return p.S >= 2 && p.mma;
+  return p.S >= 2 && p.mma && w.dim_in <= (size_t)kNormSpans * p.niw * 256;
 }
 
 int32_t gemv_launch(unltd_ctx ctx, const GemvArgs &a) {
@@ -1660,11 +2056,26 @@ int32_t gemv_launch(unltd_ctx ctx, const GemvArgs &a) {
     ctx->launches += 1;
   }
 
-  // 2) gemv, programmatic dependent launch
+  // 2) gemv, programmatic dependent launch: the shape-specialised kernel
+  // when there is one for w, else the generic one of the plan
   GemvFn fn = am ? pick<true>(fmt, mode, R, mma) : pick<false>(fmt, mode, R, mma);
-  e = ensure_smem_attr(ctx->device, fn, smem);
+  int launch_smem = smem, launch_grid = grid, launch_threads = pl.threads, launch_S = S;
+  if (pl.mma) {
+    const LeanPlan lp = lean_for(ctx->device, w, mode, am);
+    if (lp.fn && lp.img_bytes == img_bytes) {
+      fn = lp.fn;
+      launch_smem = lp.smem;
+      launch_threads = lp.threads;
+      launch_S = lp.S;
+      launch_grid = std::max(1, std::min(ctx->num_sms, (rows + lp.T - 1) / lp.T));
+    }
+  }
+  e = ensure_smem_attr(ctx->device, fn, launch_smem);
   if (e != cudaSuccess) return cuda_error(e, "gemv: shared-memory attribute");
 
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
   Params P;
   P.W = w.dev;
   P.stride = w.row_stride;
@@ -1683,7 +2094,7 @@ int32_t gemv_launch(unltd_ctx ctx, const GemvArgs &a) {
   P.pstride = pstride;
   P.mma = mma;
   P.T = T;
-  P.S = S;
+  P.S = launch_S;
   P.stage_bytes = stage_bytes;
   P.rs = rs;
   P.cbuf_bytes = cbuf;
@@ -1708,13 +2119,10 @@ int32_t gemv_launch(unltd_ctx ctx, const GemvArgs &a) {
   P.peer_recv = recv;
 
   cudaLaunchConfig_t cfg = {};
-  cfg.gridDim = dim3(grid);
-  cfg.blockDim = dim3(mma ? kTcThreads : kGemvThreads);
-  cfg.dynamicSmemBytes = smem;
+  cfg.gridDim = dim3(launch_grid);
+  cfg.blockDim = dim3(launch_threads);
+  cfg.dynamicSmemBytes = launch_smem;
   cfg.stream = st;
-  cudaLaunchAttribute attr[1];
-  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
-  attr[0].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
   e = cudaLaunchKernelEx(&cfg, fn, P);

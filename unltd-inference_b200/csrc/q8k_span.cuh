@@ -84,6 +84,17 @@ __device__ __forceinline__ void q8k_span_write(float v, uint8_t *im4, uint8_t *i
   if (im4) {
     if (t == 0) *reinterpret_cast<float *>(im4 + kImgQ8K4_D) = d;
     if (t < 16) reinterpret_cast<int *>(im4 + kImgQ8K4_BS)[t] = s.hsum[t];
+    if (t < 4) {  // the min term's B operand words (kImgQ8K4_BM)
+      const int c = t >> 1, tg = t & 1;
+      uint32_t bm = 0u;
+#pragma unroll
+      for (int i = 0; i < 4; i++) {
+        const int g = s.hsum[4 * tg + i];
+        const int lo = ((g + 128) & 255) - 128, hi = (g - lo) >> 8;
+        bm |= (uint32_t)((c == 0 ? lo : hi) & 0xFF) << (8 * i);
+      }
+      reinterpret_cast<uint32_t *>(im4 + kImgQ8K4_BM)[t] = bm;
+    }
   }
 }
 
@@ -146,6 +157,16 @@ __device__ __forceinline__ void q8k_span_write_warp(const float (&v)[8], int lan
     if ((lane & 3) == 0) bs[g] = hs;
     if (lane < 8) bs[8 + lane] = 0;
     if (lane == 0) *reinterpret_cast<float *>(im4 + kImgQ8K4_D) = d;
+    // the min term's B operand words (kImgQ8K4_BM): lane 2c + t packs the
+    // low (c = 0) or high (c = 1) bytes of group sums 4t .. 4t + 3
+    uint32_t bm = 0u;
+#pragma unroll
+    for (int i = 0; i < 4; i++) {
+      const int gs = __shfl_sync(0xffffffffu, hs, 16 * (lane & 1) + 4 * i);
+      const int lo = ((gs + 128) & 255) - 128, hi = (gs - lo) >> 8;
+      bm |= (uint32_t)(((lane >> 1) & 1 ? hi : lo) & 0xFF) << (8 * i);
+    }
+    if (lane < 4) reinterpret_cast<uint32_t *>(im4 + kImgQ8K4_BM)[lane] = bm;
   }
   if (im6) {
 #pragma unroll

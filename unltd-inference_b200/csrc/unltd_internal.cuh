@@ -45,10 +45,13 @@ constexpr int kImgF32X = 848;
 constexpr int kImgF32X_XS = 768;
 constexpr int kImgF32X_XSUM = 784;
 // Q8K for Q4_K: q8 (256 B, class-major: q4k_q8k_xpos) | d f32 | pad | 8 x i32
-// group sums (then 8 zero words)
-constexpr int kImgQ8K4 = 336;
+// group sums (then 8 zero words) | the min term's MMA B operand: 4 words,
+// word 2c + t = the balanced low (c = 0) or high (c = 1) bytes of the group
+// sums 4t .. 4t + 3 (low = ((s + 128) & 255) - 128, high = (s - low) / 256)
+constexpr int kImgQ8K4 = 352;
 constexpr int kImgQ8K4_D = 256;
 constexpr int kImgQ8K4_BS = 272;
+constexpr int kImgQ8K4_BM = 336;
 // Q8K for Q6_K: for lane j, half h, word t: two masked q8 words (A: bytes
 // 0,1; B: bytes 2,3) -> 8*2*4*2 words = 512 B | d f32 | pad
 constexpr int kImgQ8K6 = 528;
