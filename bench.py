@@ -7,6 +7,12 @@ One step = one pass of (a)-(d) on seeded synthetic weights and x ~ N(0,1).
 The weights of one step (598 MB) exceed the 126 MB L2, so every step streams
 them from HBM; no separate flush is needed.
 
+`gemv_back_to_back` (one GPU): BASELINE config 0 (Q4_K 4096 x 4096) and each
+config-1 shape alone, as device throughput of GEMVs issued back to back: a
+CUDA graph of launches cycling through distinct uploads of the weights whose
+total exceeds the L2, CUDA-event timed (the decode step issues its GEMVs this
+way).
+
 Arithmetic: the K-quant GEMVs run MODE_Q8K_EXACT (bit-identical to the
 reference's gemv_quant_q8k, its production path); Q8_0 has no Q8_K path in the
 reference and runs MODE_F32X. The F32X rate of the whole mix is reported too.
@@ -166,6 +172,54 @@ def shard_weights(wb, dtype, dim_in, dim_out, split, rank, world):
     return np.ascontiguousarray(m).reshape(-1), (b1 - b0) * be, dim_out, b0 * be
 
 
+L2_BYTES = 126 * 2**20
+
+
+def back_to_back(ctx, stream, dt, di, do, seed, mode, reps_min=24):
+    """Device throughput of one GEMV shape issued back to back: C distinct
+    uploads of the weights (C x bytes > L2, so every launch streams its
+    weights from HBM), R launches cycling through them captured in one CUDA
+    graph (no host launch gaps; consecutive GEMVs chain with programmatic
+    dependent launch as in the decode step), timed with CUDA events on the
+    launch stream. Returns (us per GEMV, GB/s of algorithmic bytes)."""
+    import torch
+
+    base = synth.quant_weights(dt, di, do, seed)
+    wbytes = synth.row_bytes(dt, di) * do
+    C = max(1, -(-int(1.2 * L2_BYTES) // wbytes))
+    ws = []
+    for c in range(C):
+        wb = base.copy()
+        wb[:16] ^= np.uint8(c)  # a distinct tensor per copy
+        ws.append(ctx.upload(wb, dt, di, do))
+    x = torch.from_numpy(synth.activations(di, seed + 1)).cuda()
+    y = torch.empty(do, device="cuda")
+    R = max(reps_min, C)
+    R = -(-R // C) * C
+    for w in ws:
+        ctx.gemv(w, x, y, mode)
+    torch.cuda.synchronize()
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g, stream=stream):
+        ctx.set_stream(torch.cuda.current_stream().cuda_stream)
+        for r in range(R):
+            ctx.gemv(ws[r % C], x, y, mode)
+    ctx.set_stream(stream.cuda_stream)
+    g.replay()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for _ in range(3):
+        g.replay()
+    e1.record(stream)
+    torch.cuda.synchronize()
+    us = e0.elapsed_time(e1) * 1e3 / (3 * R)
+    del g
+    for w in ws:
+        w.free()
+    return us, algorithmic_bytes(dt, di, do) / (us * 1e-6) / 1e9
+
+
 def cpu_baseline(steps=3):
     """The oracle (reference restatement) on one full config-1 step, median of `steps`."""
     import oracle
@@ -277,6 +331,7 @@ def decode_bench(n_tokens, with_cpu, rank=0, world=1, dist=None, profile_region=
                        "memory, fused into the GEMVs (same greedy stream as the oracle; hidden state within 1e-3 "
                        "max-rel of it, logits bit-identical given that hidden state)"),
         "tokens_tail": [int(t) for t in toks[-4:]],
+        "distinct_tokens": len(set(int(t) for t in toks)),
     }
     s.close()
     m.close()
@@ -500,6 +555,20 @@ def main():
     torch.cuda.synchronize()
     per_item_ms = [statistics.mean(ev[k][i][0].elapsed_time(ev[k][i][1]) for k in range(K)) for i in range(len(items))]
 
+    # ---- per-shape device throughput, back to back (BASELINE config 0 and the
+    # config-1 shapes): CUDA graphs over distinct weight copies ----
+    b2b = None
+    if world == 1 and args.only is None:
+        peak_b, _ = _peaks()
+        b2b = {}
+        shapes = [("config0_q4k_4096x4096", Q4K, 4096, 4096, 1234)] + [(n, dt, di, do, SEEDS[n]) for n, dt, di, do, _
+                                                                       in MIX]
+        for name, dt, di, do, seed in shapes:
+            m = ug.MODE_F32X if dt == Q8_0 else head_mode
+            us, gbs = back_to_back(ctx, stream, dt, di, do, seed, m)
+            b2b[name] = {"us": round(us, 3), "gbs": round(gbs, 1), "frac": round(gbs / peak_b, 4),
+                         "mode": "F32X" if m == ug.MODE_F32X else "Q8K_EXACT"}
+
     # ---- F32X rate of the same mix ----
     for _ in range(2):
         step(mode=ug.MODE_F32X)
@@ -647,6 +716,7 @@ def main():
         "per_gemv": {it["name"]: {"ms": round(per_item_ms[i], 4),
                                   "gbs": round(it["local_bytes"] / (per_item_ms[i] * 1e-3) / 1e9, 1)}
                      for i, it in enumerate(items)},
+        "gemv_back_to_back": b2b,
         "f32x_mode": {"value": round(step_bytes / (ms_f32x * 1e-3) / 1e9, 2), "unit": UNIT,
                       "ms_per_step": round(ms_f32x, 4)},
         "roofline": {"bound": "hbm", "kernel": "gemv_tc_kernel Q6_K Q8K_EXACT on the int8 tensor cores + fused argmax (LM head, x quantized in its prologue)",

@@ -182,22 +182,25 @@ def test_model_and_session_errors(ctx, tiny):
 
 def test_9b_greedy_stream_from_2048_context(ctx):
     """the synthetic 9B-class model, KV cache prefilled to
-    2048 positions; the greedy stream and the final logits match the oracle."""
+    2048 positions; 16 greedy tokens (at least 8 distinct: the stream does not
+    settle on one vocab row), the final hidden state and logits bit-identical
+    to the oracle."""
     cfg = synth.QWEN35_9B
     tensors = synth.qwen35_model(cfg, 2026)
     st = synth.qwen35_state(cfg, 2048, 2027)
     m = ug.Qwen35Model(ctx, cfg)
     m.load(tensors)
-    s = m.session(2048 + 8)
+    n = 16
+    s = m.session(2048 + n + 4)
     s.set_state(2048, st["conv"], st["gdn"], st["k"], st["v"])
-    n = 4
     toks = s.decode(1000, n)
     lg, hd = s.read()
     s.close()
     m.close()
-    o = oracle.Qwen35Oracle(cfg, tensors, 2048 + 8, st, 2048)
+    o = oracle.Qwen35Oracle(cfg, tensors, 2048 + n + 4, st, 2048)
     otoks, ologits, ohidden = o.greedy(1000, n, nthreads=os.cpu_count() or 8)
     print("9B greedy stream:", toks.tolist(), "oracle:", otoks)
     assert toks.tolist() == otoks
+    assert len(set(otoks)) >= 8, otoks
     assert (bits(hd) == bits(ohidden)).all()
     assert (bits(lg) == bits(ologits)).all()

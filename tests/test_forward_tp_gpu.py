@@ -82,29 +82,54 @@ def _run_torchrun(world, script, *args):
     return out
 
 
+def _reference_drift():
+    """tests/golden/reference_drift_9b.json (tests/golden/make_reference_drift.py):
+    per step, how far the reference's own Q8_K activation quantization moves
+    the hidden state and logits of this model from the same forward with
+    exact (gemv_quant) projections."""
+    with open(os.path.join(HERE, "golden", "reference_drift_9b.json")) as f:
+        return json.load(f)
+
+
 @pytest.mark.parametrize("world", [2, 4, 8])
 def test_tp_9b_decode_matches_oracle(world):
-    """The 9B-class model at 4 and 8 GPUs: at 8 every rank holds one KV head
-    shared by its pair of query heads and 4 of the 32 recurrent v heads; the
-    row-split sums run through the NVLink peer kernel fused into the GEMVs.
+    """The 9B-class model at 2, 4 and 8 GPUs, six greedy steps from a
+    40-position context: at 8 every rank holds one KV head shared by its pair
+    of query heads and 4 of the 32 recurrent v heads; the row-split sums run
+    through the NVLink peer kernel fused into the GEMVs.
 
-    Over 32 layers the f32 rounding of the split sums moves a few Q8_K
-    activation quants by one step, so the final hidden state drifts from the
-    single-device oracle (8.8e-4 max-rel at 8 GPUs), and the LM head, whose
-    dot products cancel, amplifies that drift in its logits (5.1e-3 max-rel
-    at 8 GPUs). The logits are therefore checked bit for bit against the
-    oracle's output norm and LM head applied to this run's own hidden state,
-    the hidden state within 1e-3, and the greedy stream exactly."""
+    The rank-order f32 sums of the split projections round differently from
+    the reference's single chain, and the Q8_K quantizer of the next
+    projection's input turns an ulp now and then into a one-step change of a
+    quant, so the hidden state moves away from the single-device oracle. The
+    bar for that drift is the reference's own, since the sharded run's extra
+    roundings are of the same kind and size as the requantization the
+    reference itself applies before every projection: normwise (L2), the
+    sharded hidden state and logits must stay closer to the oracle than the
+    oracle's Q8_K forward is to the same forward with exact projections over
+    the same tokens; max-rel (a max over 151936 logits, a noisy statistic)
+    within twice that. The greedy stream must equal the oracle's (the
+    oracle's top-2 margins are reported beside it), and the gathered logits
+    must be bit-identical to the oracle's output norm and LM head applied to
+    this run's own hidden state (the vocab-split head is exact given its
+    input)."""
     if not torch.cuda.is_available() or torch.cuda.device_count() < world:
         pytest.skip(f"needs {world} GPUs")
     from __graft_entry__ import build
 
     build()
-    out = _run_torchrun(world, "tp_decode_check.py", "--model", "9b", "--steps", "4", "--allreduce", "peer")
+    ref = _reference_drift()
+    steps = len(ref["steps"]) - 2
+    out = _run_torchrun(world, "tp_decode_check.py", "--model", "9b", "--steps", str(steps), "--allreduce", "peer",
+                        "--position", str(ref["position"]), "--start", str(ref["start"]))
+    last = ref["steps"][-1]
+    print("reference Q8_K drift at the last step:", last)
     assert out["same_stream_on_all_ranks"] and out["argmax_matches_gathered_logits"]
     assert out["stream_matches_oracle"], out
     assert out["logits_bit_identical_given_hidden"], out
-    assert out["hidden_maxrel"] <= TOL, out
+    for key, factor in (("hidden_normwise", 1.0), ("logits_normwise", 1.0), ("hidden_maxrel", 2.0),
+                        ("logits_maxrel", 2.0)):
+        assert out[key] <= factor * last[key], (key, out[key], last[key])
 
 
 @pytest.mark.parametrize("world", [4, 8])

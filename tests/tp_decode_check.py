@@ -30,6 +30,26 @@ import synth  # noqa: E402
 import unltd_gpu as ug  # noqa: E402
 
 
+def load_model(cfg, seed, rank, model_name):
+    """The synthetic model, generated once per machine: rank 0 writes every
+    tensor to a cache directory (one .npy each, a marker file last); the
+    other ranks, and later runs, map the files read-only."""
+    cache = os.path.join(os.environ.get("UNLTD_MODEL_CACHE", "/tmp/unltd_model_cache"), f"{model_name}_{seed}")
+    marker = os.path.join(cache, "complete")
+    if rank == 0 and not os.path.exists(marker):
+        tensors = synth.qwen35_model(cfg, seed)
+        os.makedirs(cache, exist_ok=True)
+        for name, (dt, arr) in tensors.items():
+            np.save(os.path.join(cache, name + ".npy"), arr)
+        with open(marker, "w") as f:
+            f.write("ok")
+    dist.barrier()
+    out = {}
+    for name, dt, _, _ in synth.qwen35_tensor_list(cfg):
+        out[name] = (dt, np.load(os.path.join(cache, name + ".npy"), mmap_mode="r"))
+    return out
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--model", default="tiny", choices=["tiny", "9b"])
@@ -46,7 +66,7 @@ def main():
     cfg = synth.QWEN35_TINY if args.model == "tiny" else synth.QWEN35_9B
     seed = 11 if args.model == "tiny" else 2026
     pos0, n = args.position, args.steps
-    tensors = synth.qwen35_model(cfg, seed)
+    tensors = load_model(cfg, seed, rank, args.model)
     st = synth.qwen35_state(cfg, pos0, seed + 1)
     ctx = ug.Context(local)
     ctx.comm_init(rank, world, ug.exchange_unique_id())
@@ -97,6 +117,9 @@ def main():
             out["stream_matches_oracle"] = otoks == toks.tolist()
             out["logits_maxrel"] = float(np.max(np.abs(logits - ol)) / np.max(np.abs(ol)))
             out["hidden_maxrel"] = float(np.max(np.abs(hd - oh)) / np.max(np.abs(oh)))
+            d64 = lambda a, b: float(np.linalg.norm(np.asarray(a, np.float64) - b) / np.linalg.norm(np.asarray(b, np.float64)))
+            out["logits_normwise"] = d64(logits, ol)
+            out["hidden_normwise"] = d64(hd, oh)
             # the oracle's output norm and LM head (gemv_quant_q8k) applied to this
             # run's own final hidden state: the vocab-split head depends on its
             # input only, so given the same hidden state its logits are the same bits
