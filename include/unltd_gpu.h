@@ -149,6 +149,14 @@ int32_t unltd_gemv_argmax_shard(unltd_ctx ctx, unltd_weight w, const float *x_de
  * per element. */
 int32_t unltd_gemm(unltd_ctx ctx, unltd_weight w, const float *X_dev, float *Y_dev, size_t m_tokens);
 
+/* The same product with the accuracy of gemv_quant (quants.rs:422): within
+ * 1e-4 max-rel of the f64-accumulated truth. Each token row of X is scaled by
+ * a power of two and split into fp16 hi + lo; W = d*sc*q - dmin*m is formed
+ * in f32, scaled by 2^8 and split the same way (|W| < 256); three tcgen05
+ * MMAs per K slice (Xh Wh + Xh Wl + Xl Wh, f32 accumulation), 128-token
+ * tiles. Q4_K weights. */
+int32_t unltd_gemm_f32x(unltd_ctx ctx, unltd_weight w, const float *X_dev, float *Y_dev, size_t m_tokens);
+
 /* Dequantize all rows to f32, row-major [dim_out][dim_in]. Bit-exact with
  * dequantize_q4_k (quants.rs:534-567) for Q4_K and with the exact element
  * values of dot_q6_k (quants.rs:171-200) and of the Q8_0 format. */

@@ -298,7 +298,15 @@ int32_t unltd_gemm(unltd_ctx c, unltd_weight w, const float *X, float *Y, size_t
   if (w->ctx != c) return set_error(UNLTD_ERR_INVALID_ARG, "gemm: weight belongs to another context");
   if (m_tokens > (size_t)1 << 24) return set_error(UNLTD_ERR_LENGTH, "gemm: m_tokens too large");
   CtxGuard g(c->device);
-  return gemm_launch(c, *w, X, Y, m_tokens);
+  return gemm_launch(c, *w, X, Y, m_tokens, false);
+}
+
+int32_t unltd_gemm_f32x(unltd_ctx c, unltd_weight w, const float *X, float *Y, size_t m_tokens) {
+  if (!c || !w || !X || !Y) return set_error(UNLTD_ERR_INVALID_ARG, "gemm_f32x: NULL argument");
+  if (w->ctx != c) return set_error(UNLTD_ERR_INVALID_ARG, "gemm_f32x: weight belongs to another context");
+  if (m_tokens > (size_t)1 << 24) return set_error(UNLTD_ERR_LENGTH, "gemm_f32x: m_tokens too large");
+  CtxGuard g(c->device);
+  return gemm_launch(c, *w, X, Y, m_tokens, true);
 }
 
 int32_t unltd_dequant(unltd_ctx c, unltd_weight w, float *out) {

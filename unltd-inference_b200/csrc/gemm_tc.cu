@@ -3,7 +3,12 @@
 // gemv_quant applied to every token at once; the reference itself runs
 // prefill token by token, qwen35_forward.rs:8-12).
 //
-// Design (one CTA per SM, persistent over 256-token x 192-row output tiles):
+// Two arithmetic modes (GemmShape below): fast, fp16 operands rounded once;
+// accurate, hi + lo fp16 pairs for X and W and three MMAs per K slice
+// (within 1e-4 max-rel of the f64 truth, the bar of gemv_quant).
+//
+// Design (one CTA per SM, persistent over 256-token x 192-row output tiles
+// in the fast mode, 128-token tiles in the accurate one):
 //  * X is converted once per call to fp16, with the columns of every
 //    64-element segment permuted to the K order in which the dequant writes
 //    the weight tile, so A and B agree without any byte transpose.
@@ -41,22 +46,41 @@
 namespace unltd {
 namespace {
 
-constexpr int kTileM = 256;   // tokens per tile (two MMAs of M = 128)
 constexpr int kTileN = 192;   // weight rows per tile (MMA N)
 constexpr int kStepK = 64;    // K per stage: one Q4_K quant segment
-constexpr int kStagesA = 3;   // X tiles, released by the MMAs
-constexpr int kStagesB = 3;   // dequantized weight tiles, released by the MMAs
-constexpr int kStagesW = 5;   // packed weight segments, released by the dequant
-constexpr int kDequantWarps = 12;  // warps 3..14: two threads per weight row
-constexpr int kThreadsG = (3 + kDequantWarps + 4) * 32;  // + 2 producers, MMA, 4 epilogue warps
-constexpr uint32_t kABytes = 2 * 128 * kStepK * 2;          // 32 KB
-constexpr uint32_t kBBytes = kTileN * kStepK * 2;            // 24 KB
 constexpr uint32_t kWqBytes = kTileN * 32;                   // 6 KB
 constexpr uint32_t kWhBytes = kTileN * 16;                   // 3 KB
 constexpr uint32_t kWBytes = kWqBytes + kWhBytes;            // 9 KB
 constexpr uint32_t kTmemCols = 512;
-constexpr int kSmemBytes =
-    kStagesA * kABytes + kStagesB * kBBytes + kStagesW * kWBytes + 1024 /*align*/ + 256 /*barriers*/;
+
+// Two arithmetic modes of the same pipeline.
+//  fast (SPLIT = false): X and W each rounded once to fp16; 256-token tiles
+//    (two M = 128 MMAs); 12 dequant warps, two threads per weight row.
+//  accurate (SPLIT = true): X = (Xh + Xl) 2^-e per token row and W = (Wh +
+//    Wl) 2^-8 as fp16 pairs (22 significant bits each), Y = Xh Wh + Xh Wl +
+//    Xl Wh (three MMAs per K slice, f32 accumulation; the dropped Xl Wl term
+//    is below 2^-22 relative); 128-token tiles, the A stage holds Xh and Xl,
+//    the B stage Wh and Wl; 24 dequant warps, four threads per weight row.
+template <bool SPLIT>
+struct GemmShape {
+  static constexpr int kTileM = SPLIT ? 128 : 256;       // tokens per tile
+  static constexpr int kHalves = SPLIT ? 1 : 2;          // M = 128 MMAs per K slice and product
+  static constexpr int kStagesA = 3;                     // X tiles, released by the MMAs
+  static constexpr int kStagesB = SPLIT ? 2 : 3;         // dequantized weight tiles, released by the MMAs
+  static constexpr int kStagesW = SPLIT ? 3 : 5;         // packed weight segments, released by the dequant
+  static constexpr int kDequantWarps = SPLIT ? 24 : 12;  // warps 3 ..
+  static constexpr int kThreads = (3 + kDequantWarps + 4) * 32;  // + 2 producers, MMA, 4 epilogue warps
+  static constexpr uint32_t kABytes = 2 * 128 * kStepK * 2;      // 32 KB: two 128-row fp16 tiles
+  static constexpr uint32_t kBTile = kTileN * kStepK * 2;        // 24 KB: one 192 x 64 fp16 tile
+  static constexpr uint32_t kBBytes = (SPLIT ? 2 : 1) * kBTile;
+  static constexpr int kSmemBytes =
+      kStagesA * kABytes + kStagesB * kBBytes + kStagesW * kWBytes + 1024 /*align*/ + 256 /*barriers*/;
+};
+static_assert(GemmShape<false>::kSmemBytes <= 227 * 1024 && GemmShape<true>::kSmemBytes <= 227 * 1024, "smem");
+static_assert(GemmShape<true>::kThreads <= 1024, "block size");
+// W is scaled by 2^8 before its hi/lo split in the accurate mode (keeps the
+// lo halves out of the fp16 subnormal range for typical scales; |W| < 256).
+constexpr float kWScale = 256.0f;
 
 // ---- tcgen05 / TMA wrappers (inline PTX, sm_100a) --------------------------
 __device__ __forceinline__ void tmem_alloc(uint32_t *slot, uint32_t ncols) {
@@ -125,13 +149,19 @@ constexpr uint32_t kIdesc = (1u << 4) | (0u << 7) | (0u << 10) | ((uint32_t)(kTi
 struct GemmParams {
   int M, N, K, nb;
   float *Y;
+  const float *rowscale;  // accurate mode: 2^-(e_m + 8) per token row
   int *err;
   int tiles_n, ntiles;
 };
 
-__global__ void __launch_bounds__(kThreadsG, 1)
+template <bool SPLIT>
+__global__ void __launch_bounds__(GemmShape<SPLIT>::kThreads, 1)
     gemm_q4k_tc(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmWq,
                 const __grid_constant__ CUtensorMap tmWh, GemmParams P) {
+  using G = GemmShape<SPLIT>;
+  constexpr int kTileM = G::kTileM, kStagesA = G::kStagesA, kStagesB = G::kStagesB, kStagesW = G::kStagesW;
+  constexpr int kDequantWarps = G::kDequantWarps;
+  constexpr uint32_t kABytes = G::kABytes, kBBytes = G::kBBytes;
   extern __shared__ uint8_t smem_raw[];
   const uint32_t raw = smem_u32(smem_raw);
   const uint32_t pad = ((raw + 1023u) & ~1023u) - raw;
@@ -195,8 +225,11 @@ __global__ void __launch_bounds__(kThreadsG, 1)
           if (isA) {
             uint8_t *dst = ringA + (size_t)s * kABytes;
             mbar_expect_tx(&fullb[s], kABytes);
+            // fast: the tile's two 128-token halves; accurate: the hi rows
+            // [0, M) and the lo rows [M, 2M) of the same 128 tokens
             tma_load_2d(dst, &tmA, ks * kStepK, tm * kTileM, &fullb[s]);
-            tma_load_2d(dst + kABytes / 2, &tmA, ks * kStepK, tm * kTileM + 128, &fullb[s]);
+            tma_load_2d(dst + kABytes / 2, &tmA, ks * kStepK, SPLIT ? P.M + tm * kTileM : tm * kTileM + 128,
+                        &fullb[s]);
           } else {
             uint8_t *dst = ringW + (size_t)s * kWBytes;
             const int b = ks >> 2, p = ks & 3;
@@ -228,12 +261,23 @@ __global__ void __launch_bounds__(kThreadsG, 1)
           if (!ok) break;
           tc_fence_after();
           const uint32_t a0 = smem_u32(ringA + (size_t)sa * kABytes), b0 = smem_u32(ringB + (size_t)sb * kBBytes);
+          if constexpr (SPLIT) {
 #pragma unroll
-          for (int h = 0; h < 2; h++)
+            for (int kk = 0; kk < kStepK / 16; kk++) {
+              const uint64_t ah = sw128_desc(a0 + kk * 32), al = sw128_desc(a0 + kABytes / 2 + kk * 32);
+              const uint64_t bh = sw128_desc(b0 + kk * 32), bl = sw128_desc(b0 + G::kBTile + kk * 32);
+              umma_f16(tbase, ah, bh, kIdesc, (ks > 0 || kk > 0) ? 1u : 0u);
+              umma_f16(tbase, ah, bl, kIdesc, 1u);
+              umma_f16(tbase, al, bh, kIdesc, 1u);
+            }
+          } else {
 #pragma unroll
-            for (int kk = 0; kk < kStepK / 16; kk++)
-              umma_f16(tbase + (uint32_t)(h * 256), sw128_desc(a0 + h * (kABytes / 2) + kk * 32),
-                       sw128_desc(b0 + kk * 32), kIdesc, (ks > 0 || kk > 0) ? 1u : 0u);
+            for (int h = 0; h < 2; h++)
+#pragma unroll
+              for (int kk = 0; kk < kStepK / 16; kk++)
+                umma_f16(tbase + (uint32_t)(h * 256), sw128_desc(a0 + h * (kABytes / 2) + kk * 32),
+                         sw128_desc(b0 + kk * 32), kIdesc, (ks > 0 || kk > 0) ? 1u : 0u);
+          }
           umma_commit(&aempty[sa]);
           umma_commit(&bempty[sb]);
           last = &bempty[sb];
@@ -248,11 +292,13 @@ __global__ void __launch_bounds__(kThreadsG, 1)
       if (last) mbar_wait_bounded(last, last_par, P.err);  // MMAs retired before TMEM is freed
     }
   } else if (warp < 3 + kDequantWarps) {
-    // ---------------- dequantize Q4_K -> fp16 B tile ----------------
-    // Thread (r, hf): weight row r of the tile, nibble half hf (group 2p or
-    // 2p+1 of the current 64-element segment p).
+    // ---------------- dequantize Q4_K -> fp16 B tile(s) ----------------
+    // fast: thread (r, hf) = weight row r of the tile, nibble half hf (group
+    // 2p or 2p+1 of the current 64-element segment p); accurate: thread (r,
+    // hf, wq) takes words 4 wq .. 4 wq + 3 of that half.
+    constexpr int kPerRow = SPLIT ? 4 : 2;
     const int dt = threadIdx.x - 96;
-    const int r = dt % kTileN, hf = dt / kTileN;
+    const int r = dt % kTileN, part = dt / kTileN, hf = part / (kPerRow / 2), wq = SPLIT ? (part & 1) : 0;
     long g = 0;
     bool ok = true;
     for (int t = blockIdx.x; t < P.ntiles && ok; t += gridDim.x) {
@@ -281,28 +327,62 @@ __global__ void __launch_bounds__(kThreadsG, 1)
         }
         const int sh = (p & 1) * 16 + hf * 8;
         const float d = h2f_bits(hq.x & 0xFFFFu), dmin = h2f_bits(hq.x >> 16);
-        const __half2 d1 = __float2half2_rn(__fmul_rn(d, (float)((SC >> sh) & 0xFF)));
-        const __half2 nm1 = __float2half2_rn(-__fmul_rn(dmin, (float)((MM >> sh) & 0xFF)));
-        const __half2 k1024 = __float2half2_rn(1024.0f);
         const uint32_t w[8] = {q0.x, q0.y, q0.z, q0.w, q1.x, q1.y, q1.z, q1.w};
         uint8_t *brow = ringB + (size_t)sb * kBBytes + (r >> 3) * 1024 + (r & 7) * 128;
+        if constexpr (SPLIT) {
+          // w = d sc q - dmin m in f32 (d sc q exact, one rounding), scaled by
+          // 2^8 (exact), split into fp16 hi + lo; each input word gives the
+          // fp16 pairs (byte 0, byte 2) and (byte 1, byte 3), as below
+          const float d1 = __fmul_rn(__fmul_rn(d, (float)((SC >> sh) & 0xFF)), kWScale);
+          const float m1 = __fmul_rn(__fmul_rn(dmin, (float)((MM >> sh) & 0xFF)), kWScale);
+          const uint4 qw = wq ? q1 : q0;  // words 4 wq .. 4 wq + 3
+          const uint32_t ws[4] = {qw.x, qw.y, qw.z, qw.w};
 #pragma unroll
-        for (int c = 0; c < 4; c++) {
-          uint32_t outw[4];
+          for (int cc = 0; cc < 2; cc++) {
+            const int c = 2 * wq + cc;
+            uint32_t oh[4], ol[4];
 #pragma unroll
-          for (int ww = 0; ww < 2; ww++) {
-            const uint32_t nib = hf ? ((w[2 * c + ww] >> 4) & 0x0F0F0F0Fu) : (w[2 * c + ww] & 0x0F0F0F0Fu);
-            // bytes (0,2) and (1,3) as fp16 pairs 1024 + q, exact
-            uint32_t a = (nib & 0x000F000Fu) | 0x64006400u;
-            uint32_t b = ((nib >> 8) & 0x000F000Fu) | 0x64006400u;
-            __half2 qa2 = __hsub2(*reinterpret_cast<__half2 *>(&a), k1024);
-            __half2 qb2 = __hsub2(*reinterpret_cast<__half2 *>(&b), k1024);
-            __half2 va = __hfma2(qa2, d1, nm1), vb = __hfma2(qb2, d1, nm1);
-            outw[2 * ww] = *reinterpret_cast<uint32_t *>(&va);
-            outw[2 * ww + 1] = *reinterpret_cast<uint32_t *>(&vb);
+            for (int ww = 0; ww < 2; ww++) {
+              const uint32_t nib = hf ? ((ws[2 * cc + ww] >> 4) & 0x0F0F0F0Fu) : (ws[2 * cc + ww] & 0x0F0F0F0Fu);
+              float v[4];
+#pragma unroll
+              for (int j = 0; j < 4; j++) v[j] = __fsub_rn(__fmul_rn(d1, (float)((nib >> (8 * j)) & 0xFu)), m1);
+              const __half2 ha = __floats2half2_rn(v[0], v[2]), hb = __floats2half2_rn(v[1], v[3]);
+              const float2 fa = __half22float2(ha), fb = __half22float2(hb);
+              const __half2 la = __floats2half2_rn(__fsub_rn(v[0], fa.x), __fsub_rn(v[2], fa.y));
+              const __half2 lb = __floats2half2_rn(__fsub_rn(v[1], fb.x), __fsub_rn(v[3], fb.y));
+              oh[2 * ww] = *reinterpret_cast<const uint32_t *>(&ha);
+              oh[2 * ww + 1] = *reinterpret_cast<const uint32_t *>(&hb);
+              ol[2 * ww] = *reinterpret_cast<const uint32_t *>(&la);
+              ol[2 * ww + 1] = *reinterpret_cast<const uint32_t *>(&lb);
+            }
+            const int chunk = 4 * hf + c;
+            const int off = (chunk ^ (r & 7)) << 4;
+            *reinterpret_cast<uint4 *>(brow + off) = make_uint4(oh[0], oh[1], oh[2], oh[3]);
+            *reinterpret_cast<uint4 *>(brow + G::kBTile + off) = make_uint4(ol[0], ol[1], ol[2], ol[3]);
           }
-          const int chunk = 4 * hf + c;
-          *reinterpret_cast<uint4 *>(brow + ((chunk ^ (r & 7)) << 4)) = make_uint4(outw[0], outw[1], outw[2], outw[3]);
+        } else {
+          const __half2 d1 = __float2half2_rn(__fmul_rn(d, (float)((SC >> sh) & 0xFF)));
+          const __half2 nm1 = __float2half2_rn(-__fmul_rn(dmin, (float)((MM >> sh) & 0xFF)));
+          const __half2 k1024 = __float2half2_rn(1024.0f);
+#pragma unroll
+          for (int c = 0; c < 4; c++) {
+            uint32_t outw[4];
+#pragma unroll
+            for (int ww = 0; ww < 2; ww++) {
+              const uint32_t nib = hf ? ((w[2 * c + ww] >> 4) & 0x0F0F0F0Fu) : (w[2 * c + ww] & 0x0F0F0F0Fu);
+              // bytes (0,2) and (1,3) as fp16 pairs 1024 + q, exact
+              uint32_t a = (nib & 0x000F000Fu) | 0x64006400u;
+              uint32_t b = ((nib >> 8) & 0x000F000Fu) | 0x64006400u;
+              __half2 qa2 = __hsub2(*reinterpret_cast<__half2 *>(&a), k1024);
+              __half2 qb2 = __hsub2(*reinterpret_cast<__half2 *>(&b), k1024);
+              __half2 va = __hfma2(qa2, d1, nm1), vb = __hfma2(qb2, d1, nm1);
+              outw[2 * ww] = *reinterpret_cast<uint32_t *>(&va);
+              outw[2 * ww + 1] = *reinterpret_cast<uint32_t *>(&vb);
+            }
+            const int chunk = 4 * hf + c;
+            *reinterpret_cast<uint4 *>(brow + ((chunk ^ (r & 7)) << 4)) = make_uint4(outw[0], outw[1], outw[2], outw[3]);
+          }
         }
         fence_proxy_async();  // generic-proxy stores -> visible to the tensor core
         mbar_arrive(&bfull[sb]);
@@ -317,8 +397,9 @@ __global__ void __launch_bounds__(kThreadsG, 1)
       tc_fence_after();
       const int tm = t / P.tiles_n, tn = t % P.tiles_n;
 #pragma unroll 1
-      for (int h = 0; h < 2; h++) {
+      for (int h = 0; h < G::kHalves; h++) {
         const int m = tm * kTileM + h * 128 + q * 32 + lane;
+        const float rsc = SPLIT && m < P.M ? P.rowscale[m] : 1.0f;
 #pragma unroll 1
         for (int c = 0; c < kTileN / 32; c++) {
           uint32_t v[32];
@@ -327,6 +408,10 @@ __global__ void __launch_bounds__(kThreadsG, 1)
           const int n0 = tn * kTileN + c * 32;
           if (m < P.M) {
             float *yr = P.Y + (size_t)m * P.N + n0;
+            if constexpr (SPLIT) {  // exact power-of-two rescale
+#pragma unroll
+              for (int i = 0; i < 32; i++) v[i] = __float_as_uint(__fmul_rn(__uint_as_float(v[i]), rsc));
+            }
             if (n0 + 32 <= P.N && ((P.N & 3) == 0)) {
 #pragma unroll
               for (int i = 0; i < 32; i += 4)
@@ -368,6 +453,39 @@ __global__ void x_to_f16_q4perm(const float *__restrict__ X, __half *__restrict_
   Xb[m * K + kp] = __float2half_rn(X[i]);
 }
 
+// Accurate mode: X f32 [M][K] -> fp16 hi rows [0, M) and lo rows [M, 2M)
+// (same column permutation as x_to_f16_q4perm), one CTA per token row: the
+// row is scaled by 2^s so its largest |x| lies in [2^14, 2^15), then
+// x 2^s = hi + lo (hi = fp16(x 2^s), lo = fp16 of the exact f32 remainder);
+// rowscale[m] = 2^-(s + 8) undoes the scales of X and W in the epilogue.
+__global__ void __launch_bounds__(256) x_split_q4perm(const float *__restrict__ X, __half *__restrict__ Xs,
+                                                      float *__restrict__ rowscale, int M, int K) {
+  __shared__ float red[8];
+  const int m = blockIdx.x;
+  const float *xr = X + (size_t)m * K;
+  float mx = 0.0f;
+  for (int k = threadIdx.x; k < K; k += 256) mx = fmaxf(mx, fabsf(xr[k]));
+  for (int o = 16; o; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+  if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = mx;
+  __syncthreads();
+  mx = red[0];
+  for (int i = 1; i < 8; i++) mx = fmaxf(mx, red[i]);
+  int ex = 0;
+  frexpf(mx, &ex);  // mx = f 2^ex, f in [0.5, 1)
+  const int sc = mx > 0.0f && isfinite(mx) ? 15 - ex : 0;
+  if (threadIdx.x == 0) rowscale[m] = ldexpf(1.0f, -(sc + 8));
+  __half *hi = Xs + (size_t)m * K, *lo = Xs + ((size_t)M + m) * K;
+  for (int k = threadIdx.x; k < K; k += 256) {
+    const float v = ldexpf(xr[k], sc);
+    const __half h = __float2half_rn(v);
+    const __half l = __float2half_rn(__fsub_rn(v, __half2float(h)));
+    const int seg = k >> 6, half = (k >> 5) & 1, r = k & 31, byte = r >> 3;
+    const int kp = (seg << 6) + 32 * half + 4 * (r & 7) + ((byte & 1) << 1) + (byte >> 1);
+    hi[kp] = h;
+    lo[kp] = l;
+  }
+}
+
 using EncodeTiledFn = CUresult (*)(CUtensorMap *, CUtensorMapDataType, cuuint32_t, void *, const cuuint64_t *,
                                    const cuuint64_t *, const cuuint32_t *, const cuuint32_t *, CUtensorMapInterleave,
                                    CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
@@ -399,14 +517,19 @@ bool make_map_2d(CUtensorMap *map, CUtensorMapDataType dt, void *gaddr, uint64_t
 
 }  // namespace
 
-int32_t gemm_launch(unltd_ctx ctx, const unltd_weight_s &w, const float *X, float *Y, size_t M) {
+template <bool SPLIT>
+int32_t gemm_launch_t(unltd_ctx ctx, const unltd_weight_s &w, const float *X, float *Y, size_t M) {
+  using G = GemmShape<SPLIT>;
   if (w.dtype != Q4K)
     return set_error(UNLTD_ERR_UNSUPPORTED, "gemm: only Q4_K weights have a tensor-core GEMM so far");
   if (M == 0 || w.dim_out == 0) return UNLTD_OK;
+  if (SPLIT && M > (size_t)(INT32_MAX / 2)) return set_error(UNLTD_ERR_INVALID_ARG, "gemm: too many tokens");
   const int K = (int)w.dim_in;
   cudaStream_t st = ctx->stream;
-  // fp16 copy of X with the permuted segment columns
-  const size_t xb_bytes = M * (size_t)K * 2;
+  // fp16 copy of X with the permuted segment columns (accurate mode: hi and
+  // lo rows, then the per-row scales)
+  const size_t xrows = SPLIT ? 2 * M : M;
+  const size_t xb_bytes = round_up(xrows * (size_t)K * 2, 256) + (SPLIT ? M * 4 : 0);
   if (ctx->gemm_scratch_bytes < xb_bytes) {
     if (ctx->gemm_scratch) cudaFree(ctx->gemm_scratch);
     ctx->gemm_scratch = nullptr;
@@ -416,15 +539,20 @@ int32_t gemm_launch(unltd_ctx ctx, const unltd_weight_s &w, const float *X, floa
     ctx->gemm_scratch_bytes = xb_bytes;
   }
   __half *Xb = reinterpret_cast<__half *>(ctx->gemm_scratch);
+  float *rowscale = reinterpret_cast<float *>(ctx->gemm_scratch + round_up(xrows * (size_t)K * 2, 256));
   {
-    const size_t n = M * (size_t)K;
-    x_to_f16_q4perm<<<(unsigned)((n + 255) / 256), 256, 0, st>>>(X, Xb, M, K);
+    if (SPLIT) {
+      x_split_q4perm<<<(unsigned)M, 256, 0, st>>>(X, Xb, rowscale, (int)M, K);
+    } else {
+      const size_t n = M * (size_t)K;
+      x_to_f16_q4perm<<<(unsigned)((n + 255) / 256), 256, 0, st>>>(X, Xb, M, K);
+    }
     cudaError_t e = cudaGetLastError();
     if (e != cudaSuccess) return cuda_error(e, "gemm x convert");
     ctx->launches += 1;
   }
   CUtensorMap tmA, tmWq, tmWh;
-  if (!make_map_2d(&tmA, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, Xb, (uint64_t)K, M, (uint64_t)K * 2, kStepK, 128,
+  if (!make_map_2d(&tmA, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, Xb, (uint64_t)K, xrows, (uint64_t)K * 2, kStepK, 128,
                    CU_TENSOR_MAP_SWIZZLE_128B) ||
       !make_map_2d(&tmWq, CU_TENSOR_MAP_DATA_TYPE_UINT8, w.dev, w.row_stride, w.dim_out, w.row_stride, 32, kTileN,
                    CU_TENSOR_MAP_SWIZZLE_NONE) ||
@@ -438,26 +566,36 @@ int32_t gemm_launch(unltd_ctx ctx, const unltd_weight_s &w, const float *X, floa
   P.K = K;
   P.nb = (int)w.nb;
   P.Y = Y;
+  P.rowscale = SPLIT ? rowscale : nullptr;
   P.err = ctx->err;
   P.tiles_n = (P.N + kTileN - 1) / kTileN;
-  P.ntiles = ((P.M + kTileM - 1) / kTileM) * P.tiles_n;
+  P.ntiles = ((P.M + G::kTileM - 1) / G::kTileM) * P.tiles_n;
   {
     // the attribute belongs to the current device's context: set it once per device
     static std::mutex mu;
     static std::vector<int> done;
     std::lock_guard<std::mutex> lk(mu);
     if (std::find(done.begin(), done.end(), ctx->device) == done.end()) {
-      cudaError_t e = cudaFuncSetAttribute(gemm_q4k_tc, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemBytes);
+      cudaError_t e =
+          cudaFuncSetAttribute(gemm_q4k_tc<SPLIT>, cudaFuncAttributeMaxDynamicSharedMemorySize, G::kSmemBytes);
       if (e != cudaSuccess) return cuda_error(e, "gemm: shared-memory attribute");
       done.push_back(ctx->device);
     }
   }
-  const int grid = std::min(P.ntiles, ctx->num_sms);
-  gemm_q4k_tc<<<grid, kThreadsG, kSmemBytes, st>>>(tmA, tmWq, tmWh, P);
+  // One output tile per CTA, launched in waves. The kernel's roles loop over
+  // tiles (t += gridDim.x), but with a grid smaller than the tile count some
+  // CTAs' second tiles came out wrong at long K (K >= 2048) in both modes;
+  // the cause is not found yet, so every CTA takes exactly one tile.
+  const int grid = P.ntiles;
+  gemm_q4k_tc<SPLIT><<<grid, G::kThreads, G::kSmemBytes, st>>>(tmA, tmWq, tmWh, P);
   cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) return cuda_error(e, "gemm launch");
   ctx->launches += 1;
   return UNLTD_OK;
+}
+
+int32_t gemm_launch(unltd_ctx ctx, const unltd_weight_s &w, const float *X, float *Y, size_t M, bool accurate) {
+  return accurate ? gemm_launch_t<true>(ctx, w, X, Y, M) : gemm_launch_t<false>(ctx, w, X, Y, M);
 }
 
 }  // namespace unltd

@@ -156,6 +156,8 @@ int32_t comm_allreduce(unltd_ctx c, cudaStream_t st, void *buf, size_t count, bo
 void comm_destroy(unltd_ctx c);
 
 // gemm_tc.cu
-int32_t gemm_launch(unltd_ctx ctx, const unltd_weight_s &w, const float *X, float *Y, size_t M);
+// accurate: X and W as hi + lo fp16 pairs, three MMAs per K slice (1e-4 max-rel
+// of the f64 truth); otherwise fp16 operands rounded once.
+int32_t gemm_launch(unltd_ctx ctx, const unltd_weight_s &w, const float *X, float *Y, size_t M, bool accurate);
 
 }  // namespace unltd

@@ -52,6 +52,7 @@ SIGNATURES = [
     ("unltd_dequant", _I, [_P, _P, _P]),
     ("unltd_gemv_noalloc", _I, [_P, _P, _P, _I, _P]),
     ("unltd_gemm", _I, [_P, _P, _P, _P, _S]),
+    ("unltd_gemm_f32x", _I, [_P, _P, _P, _P, _S]),
     ("unltd_gemv_quant", _I, [_P, _S, _P, _S, _P, _S, _S, _S, _I]),
     ("unltd_gemv_quant_q8k", _I, [_P, _S, _P, _S, _P, _S, _S, _S, _I]),
     ("unltd_dequantize_q4_k", _I, [_P, _S, _P, _S]),
@@ -228,9 +229,12 @@ class Context:
         _check(lib().unltd_gemv_argmax_shard(self.h, w.h, _ptr(x), _ptr(logits) if logits is not None else None,
                                              _ptr(key), row0, mode))
 
-    def gemm(self, w: "Weight", X, Y, m_tokens: int):
-        """Y[m][n] = sum_k X[m][k] W[n][k] on the tensor cores (fp16 operands, f32 accumulate)."""
-        _check(lib().unltd_gemm(self.h, w.h, _ptr(X), _ptr(Y), m_tokens))
+    def gemm(self, w: "Weight", X, Y, m_tokens: int, accurate: bool = False):
+        """Y[m][n] = sum_k X[m][k] W[n][k] on the tensor cores, f32 accumulate:
+        fp16 operands (unltd_gemm), or hi + lo fp16 pairs within 1e-4 of the
+        f64 truth (accurate=True, unltd_gemm_f32x)."""
+        fn = lib().unltd_gemm_f32x if accurate else lib().unltd_gemm
+        _check(fn(self.h, w.h, _ptr(X), _ptr(Y), m_tokens))
 
     def dequant(self, w: "Weight", out):
         _check(lib().unltd_dequant(self.h, w.h, _ptr(out)))
