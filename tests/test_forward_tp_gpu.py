@@ -121,7 +121,7 @@ def test_tp_9b_decode_matches_oracle(world):
     ref = _reference_drift()
     steps = len(ref["steps"]) - 2
     out = _run_torchrun(world, "tp_decode_check.py", "--model", "9b", "--steps", str(steps), "--allreduce", "peer",
-                        "--position", str(ref["position"]), "--start", str(ref["start"]))
+                        "--position", str(ref["position"]), "--first-token", str(ref["start"]))
     last = ref["steps"][-1]
     print("reference Q8_K drift at the last step:", last)
     assert out["same_stream_on_all_ranks"] and out["argmax_matches_gathered_logits"]

@@ -55,7 +55,7 @@ def main():
     ap.add_argument("--model", default="tiny", choices=["tiny", "9b"])
     ap.add_argument("--steps", type=int, default=8)
     ap.add_argument("--position", type=int, default=40)
-    ap.add_argument("--start", type=int, default=None, help="first token (default: 5 tiny, 7 for the 9B model)")
+    ap.add_argument("--first-token", type=int, default=None, help="first token (default: 5 tiny, 7 for the 9B model)")
     ap.add_argument("--no-oracle", action="store_true")
     ap.add_argument("--allreduce", default="peer", choices=["peer", "nccl"],
                     help="peer: one kernel over NVLink peer memory; nccl: ncclAllReduce")
@@ -76,7 +76,7 @@ def main():
     m.load(tensors)
     s = m.session(pos0 + n + 10)
     s.set_state(pos0, st["conv"], st["gdn"], st["k"], st["v"])
-    start = args.start if args.start is not None else (5 if args.model == "tiny" else 7)
+    start = args.first_token if args.first_token is not None else (5 if args.model == "tiny" else 7)
     warm = s.decode(start, 2)  # captures the step graph
     dist.barrier()
     torch.cuda.synchronize()
