@@ -802,14 +802,40 @@ __global__ void __launch_bounds__(256) attn_combine_quant_kernel(AttnArgs a) {
   }
   const double B = 0x1p-51 * (2.0 * T1 + T2 + T3);
   float attn = (float)(O - B);
-  if (attn != (float)(O + B)) {
+  const bool need = attn != (float)(O + B);
+  if (__syncthreads_or(need)) {
+    // some column's value is not resolved by the bound: its left-to-right
+    // f64 sum is recomputed. For each such column (in turn), the whole CTA
+    // forms its products soft[p] * v[p][c] into shared memory, 2048
+    // positions at a time (each thread a few strided loads, all in flight at
+    // once), and the column's own thread adds them up in order.
+    constexpr int kFbChunk = 2048;
+    __shared__ double fb_prod[kFbChunk];
+    __shared__ int fb_list[256];
+    __shared__ int fb_count;
+    if (t == 0) fb_count = 0;
+    __syncthreads();
+    if (need) fb_list[atomicAdd(&fb_count, 1)] = t;
+    __syncthreads();
+    const int nfb = fb_count;
     const size_t kvlen = (size_t)a.nkv * HDV;
-    const float *vcol = a.vcache + (size_t)kvh * HDV + c;
-    const float *soft = a.scores + (size_t)h * a.ctx;
-    double s = 0.0;
-#pragma unroll 8
-    for (int p = 0; p < n; p++) s = __dadd_rn(s, __dmul_rn((double)soft[p], (double)vcol[(size_t)p * kvlen]));
-    attn = (float)s;
+    for (int j = 0; j < nfb; j++) {
+      const int owner = fb_list[j];
+      const int eo = span * 256 + owner, ho = eo / HDV, co = eo % HDV;
+      const float *vcol = a.vcache + (size_t)(ho / (a.nh / a.nkv)) * HDV + co;
+      const float *soft = a.scores + (size_t)ho * a.ctx;
+      double s = 0.0;
+      for (int p0 = 0; p0 < n; p0 += kFbChunk) {
+        const int len = min(kFbChunk, n - p0);
+        for (int q = t; q < len; q += 256)
+          fb_prod[q] = __dmul_rn((double)soft[p0 + q], (double)vcol[(size_t)(p0 + q) * kvlen]);
+        __syncthreads();
+        if (t == owner)
+          for (int q = 0; q < len; q++) s = __dadd_rn(s, fb_prod[q]);
+        __syncthreads();
+      }
+      if (t == owner) attn = (float)s;
+    }
   }
   const float gate = a.qk[(size_t)h * 2 * HDV + HDV + c];
   q8k_span_write(__fmul_rn(attn, sigmoid_f(gate)), a.img4 ? a.img4 + (size_t)span * kImgQ8K4 : nullptr,
