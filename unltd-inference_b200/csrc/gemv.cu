@@ -441,6 +441,19 @@ struct XBlock6 {
   float xd;
 };
 
+// Block b of a Q6_K row in shared memory: moves row to the planes holding
+// it (its 16-block chunk when the row is chunked) and returns b's index
+// there, with the block count those planes are laid out for in nbl.
+__device__ __forceinline__ int q6_planes(const uint8_t *&row, int nb, int b, int &nbl) {
+  if (q6_chunked((size_t)nb)) {
+    row += (b / kQ6Chunk) * (kQ6Chunk * 210);
+    nbl = kQ6Chunk;
+    return b % kQ6Chunk;
+  }
+  nbl = nb;
+  return b;
+}
+
 __device__ __forceinline__ void load_xblock6(const uint8_t *im, XBlock6 &x) {
   const int lane = threadIdx.x & 31, gid = lane >> 2, tig = lane & 3;
   const bool own = (gid >> 1) == tig;
@@ -470,8 +483,10 @@ __device__ __forceinline__ void q6k_q8k_mma_item(const uint8_t *tile, int nr, in
   const bool v0 = lr0 < nr, v1 = !R8 && lr1 < nr;
   const uint8_t *row0 = tile + (v0 ? lr0 : 0) * P.pstride;
   const uint8_t *row1 = tile + (v1 ? lr1 : 0) * P.pstride;
-  const int nb = P.nb;
-  const int qlo = b * 128 + 4 * tig, qho = nb * 128 + b * 64 + 4 * tig;
+  int nb;
+  const int bl = q6_planes(row0, P.nb, b, nb);
+  if (q6_chunked((size_t)P.nb)) row1 += (b / kQ6Chunk) * (kQ6Chunk * 210);
+  const int qlo = bl * 128 + 4 * tig, qho = nb * 128 + bl * 64 + 4 * tig;
   uint32_t l0[8], l1[8], h0[4], h1[4];
 #pragma unroll
   for (int j = 0; j < 8; j++) {
@@ -483,11 +498,11 @@ __device__ __forceinline__ void q6k_q8k_mma_item(const uint8_t *tile, int nr, in
     h0[c] = *reinterpret_cast<const uint32_t *>(row0 + qho + 16 * c);
     h1[c] = R8 ? 0u : *reinterpret_cast<const uint32_t *>(row1 + qho + 16 * c);
   }
-  const uint4 sc0 = lds128(row0 + nb * 192 + b * 16);
-  const uint4 sc1 = R8 ? make_uint4(0u, 0u, 0u, 0u) : lds128(row1 + nb * 192 + b * 16);
+  const uint4 sc0 = lds128(row0 + nb * 192 + bl * 16);
+  const uint4 sc1 = R8 ? make_uint4(0u, 0u, 0u, 0u) : lds128(row1 + nb * 192 + bl * 16);
   const uint32_t S0[4] = {sc0.x, sc0.y, sc0.z, sc0.w}, S1[4] = {sc1.x, sc1.y, sc1.z, sc1.w};
-  const uint32_t db0 = *reinterpret_cast<const unsigned short *>(row0 + nb * 208 + b * 2);
-  const uint32_t db1 = R8 ? 0u : *reinterpret_cast<const unsigned short *>(row1 + nb * 208 + b * 2);
+  const uint32_t db0 = *reinterpret_cast<const unsigned short *>(row0 + nb * 208 + bl * 2);
+  const uint32_t db1 = R8 ? 0u : *reinterpret_cast<const unsigned short *>(row1 + nb * 208 + bl * 2);
   int acc0 = 0, acc1 = 0, acc2 = 0, acc3 = 0;
 #pragma unroll
   for (int j = 0; j < 8; j++) {
@@ -611,11 +626,13 @@ __device__ __forceinline__ void integer_item(const uint8_t *const (&rowp)[R], co
 #pragma unroll
       for (int r = 0; r < R; r++) {
         const uint8_t *row = rowp[r];
-        const uint4 ql = lds128(row + b * 128 + 16 * j);
-        const uint4 qh = lds128(row + nb * 128 + b * 64 + 16 * (2 * h + (u & 1)));
-        const int8_t *scp = reinterpret_cast<const int8_t *>(row + nb * 192 + b * 16);
+        int nbl;
+        const int bl = q6_planes(row, nb, b, nbl);
+        const uint4 ql = lds128(row + bl * 128 + 16 * j);
+        const uint4 qh = lds128(row + nbl * 128 + bl * 64 + 16 * (2 * h + (u & 1)));
+        const int8_t *scp = reinterpret_cast<const int8_t *>(row + nbl * 192 + bl * 16);
         const int sc_lo = scp[8 * h + u], sc_hi = scp[8 * h + 4 + u];
-        const float d = h2f_bits(*reinterpret_cast<const unsigned short *>(row + nb * 208 + b * 2));
+        const float d = h2f_bits(*reinterpret_cast<const unsigned short *>(row + nbl * 208 + bl * 2));
         const uint32_t wl[4] = {ql.x, ql.y, ql.z, ql.w}, wh[4] = {qh.x, qh.y, qh.z, qh.w};
         int shl = 0, sml = 0, sll = 0, shh = 0, smh = 0, slh = 0;
 #pragma unroll
@@ -718,11 +735,13 @@ __device__ __forceinline__ void integer_item(const uint8_t *const (&rowp)[R], co
 #pragma unroll
       for (int r = 0; r < R; r++) {
         const uint8_t *row = rowp[r];
-        const uint4 ql = lds128(row + b * 128 + 16 * j);
-        const uint4 qh = lds128(row + nb * 128 + b * 64 + 16 * (2 * h + (u & 1)));
-        const int8_t *scp = reinterpret_cast<const int8_t *>(row + nb * 192 + b * 16);
+        int nbl;
+        const int bl = q6_planes(row, nb, b, nbl);
+        const uint4 ql = lds128(row + bl * 128 + 16 * j);
+        const uint4 qh = lds128(row + nbl * 128 + bl * 64 + 16 * (2 * h + (u & 1)));
+        const int8_t *scp = reinterpret_cast<const int8_t *>(row + nbl * 192 + bl * 16);
         const int sc_lo = scp[8 * h + u], sc_hi = scp[8 * h + 4 + u];
-        const uint32_t dbits = *reinterpret_cast<const unsigned short *>(row + nb * 208 + b * 2);
+        const uint32_t dbits = *reinterpret_cast<const unsigned short *>(row + nbl * 208 + bl * 2);
         const uint32_t wl[4] = {ql.x, ql.y, ql.z, ql.w}, wh[4] = {qh.x, qh.y, qh.z, qh.w};
         int P4[8];
 #pragma unroll
@@ -1354,6 +1373,10 @@ __global__ void __launch_bounds__((NIW + NCW + 1) * 32, MINB) gemv_tc_kernel(Par
 //    f32 chains of its row (sums[0..7] and the min term) over the blocks with
 //    128-bit loads of the row's eight class products per block; T == 8:
 //    lane = (row, class) as in gemv_tc_kernel.
+//  * chunked Q6_K rows (12288 inputs): a work unit is a 16-row tile of one
+//    16-block chunk (3360 bytes per row, one bulk copy each), so a stage
+//    holds full-height MMA items for 16 rows in 55 KB; the tile's three
+//    chunks run in order and the chain carries sums[0..7] across them.
 template <int FMT, int NBU>
 struct LeanShape {
   static constexpr int kRowBytes = NBU * (FMT == Q4K ? 144 : 210);
@@ -1486,13 +1509,20 @@ __device__ __forceinline__ void lean_emit_row(const Params &P, int row, float ac
   }
 }
 
-template <int FMT, int NBU, int T, int NIW, int NCW, bool ARGMAX, int MINB>
+template <int FMT, int NBU, int T, int NIW, int NCW, bool ARGMAX, int MINB, int NBC>
 __global__ void __launch_bounds__((NIW + NCW + 1) * 32, MINB) gemv_lean_kernel(Params P) {
-  using Sh = LeanShape<FMT, NBU>;
+  // A work unit is one tile of T rows by NBC blocks: the whole row, or one
+  // 16-block chunk of a chunked Q6_K row (NBC = 16 < NBU), the tile's chunks
+  // in order so the chain keeps the reference's block order.
+  using Sh = LeanShape<FMT, NBC>;
   constexpr bool R8 = T == 8;
+  constexpr int NCH = NBU / NBC;
+  constexpr int kFullRow = NBU * (FMT == Q4K ? 144 : 210);
+  static_assert(NBU % NBC == 0 && (NCH == 1 || (FMT == Q6K && NBC == kQ6Chunk && !R8)), "chunked units: Q6_K only");
+  static_assert(R8 || T <= NCW * 32, "the chain takes one row per lane");
   constexpr int PS = Sh::kPs, RS = Sh::kRs, RSM = Sh::kRsm;
   constexpr int STAGE = (T * PS + 127) / 128 * 128;
-  constexpr int CBUF = lean_cbuf_bytes<FMT, NBU, T>();
+  constexpr int CBUF = lean_cbuf_bytes<FMT, NBC, T>();
   extern __shared__ __align__(128) uint8_t smem[];
   uint64_t *full = reinterpret_cast<uint64_t *>(smem);
   uint64_t *empty = full + kMaxStages;
@@ -1509,6 +1539,7 @@ __global__ void __launch_bounds__((NIW + NCW + 1) * 32, MINB) gemv_lean_kernel(P
   const int rb = (int)((long long)P.rows * blockIdx.x / G);
   const int re = (int)((long long)P.rows * (blockIdx.x + 1) / G);
   const int ntiles = (re - rb + T - 1) / T;
+  const int nunits = ntiles * NCH;
 
   if (threadIdx.x == 0) {
     for (int st = 0; st < S; st++) {
@@ -1527,16 +1558,16 @@ __global__ void __launch_bounds__((NIW + NCW + 1) * 32, MINB) gemv_lean_kernel(P
     // ---------------- producer: one bulk copy per (padded) row --------------
     if (lane == 0) {
       int issued = 0;
-      for (int i = 0; i < ntiles; i++) {
-        const int st = i % S;
-        if (i >= S && !mbar_wait_bounded(&empty[st], ((i / S) - 1) & 1, P.err)) break;
-        const int r0 = rb + i * T;
+      for (int u = 0; u < nunits; u++) {
+        const int st = u % S;
+        if (u >= S && !mbar_wait_bounded(&empty[st], ((u / S) - 1) & 1, P.err)) break;
+        const int r0 = rb + (u / NCH) * T;
         const int nr = min(T, re - r0);
         mbar_expect_tx(&full[st], (uint32_t)(nr * Sh::kRowBytes));
-        const uint8_t *src = P.W + (size_t)r0 * Sh::kRowBytes;
+        const uint8_t *src = P.W + (size_t)r0 * kFullRow + (size_t)(u % NCH) * Sh::kRowBytes;
         uint8_t *dst = stages + (size_t)st * STAGE;
-        for (int rr = 0; rr < nr; rr++) bulk_g2s(dst + rr * PS, src + (size_t)rr * Sh::kRowBytes, Sh::kRowBytes, &full[st]);
-        issued = i + 1;
+        for (int rr = 0; rr < nr; rr++) bulk_g2s(dst + rr * PS, src + (size_t)rr * kFullRow, Sh::kRowBytes, &full[st]);
+        issued = u + 1;
       }
       for (int i = max(0, issued - S); i < issued; i++) mbar_wait_bounded(&full[i % S], (i / S) & 1, P.err);
     }
@@ -1562,38 +1593,39 @@ __global__ void __launch_bounds__((NIW + NCW + 1) * 32, MINB) gemv_lean_kernel(P
       else load_xblock6(ximg + (size_t)b * Sh::kImg, x);
     };
     constexpr int NG = R8 ? 1 : T / 16;  // 16-row groups of a tile (R8: one half-height group)
-    constexpr bool kFixed = NBU == NIW;
+    constexpr bool kFixed = NBC == NIW;
     XB xb;
-    if (kFixed) load_xb(warp, xb);
-    for (int i = 0; i < ntiles; i++) {
-      const int st = i % S;
-      if (!mbar_wait_bounded(&full[st], (i / S) & 1, P.err)) break;
-      if (i >= 2 && !mbar_wait_bounded(&chaindone[i & 1], ((i >> 1) - 1) & 1, P.err)) break;
+    if (kFixed && NCH == 1) load_xb(warp, xb);
+    for (int u = 0; u < nunits; u++) {
+      const int st = u % S, cb = (u % NCH) * NBC;  // cb: the unit's first block
+      if (!mbar_wait_bounded(&full[st], (u / S) & 1, P.err)) break;
+      if (u >= 2 && !mbar_wait_bounded(&chaindone[u & 1], ((u >> 1) - 1) & 1, P.err)) break;
       const uint8_t *tile = stages + (size_t)st * STAGE;
-      float *tk = reinterpret_cast<float *>(cbase + (i & 1) * CBUF);
+      float *tk = reinterpret_cast<float *>(cbase + (u & 1) * CBUF);
       float *tm = tk + T * RS;
       if constexpr (kFixed) {
+        if constexpr (NCH > 1) load_xb(cb + warp, xb);
 #pragma unroll
         for (int g = 0; g < NG; g++) {
-          if constexpr (FMT == Q4K) q4k_item_lean<NBU, PS, RS, RSM>(tile, g, warp, xb, tk, tm);
-          else q6k_item_lean<R8, NBU, PS, RS>(tile, g, warp, xb, tk);
+          if constexpr (FMT == Q4K) q4k_item_lean<NBC, PS, RS, RSM>(tile, g, warp, xb, tk, tm);
+          else q6k_item_lean<R8, NBC, PS, RS>(tile, g, warp, xb, tk);
         }
       } else {
 #pragma unroll 1
-        for (int b = warp; b < NBU; b += NIW) {
+        for (int b = warp; b < NBC; b += NIW) {
           XB xv;
-          load_xb(b, xv);
+          load_xb(cb + b, xv);
 #pragma unroll
           for (int g = 0; g < NG; g++) {
-            if constexpr (FMT == Q4K) q4k_item_lean<NBU, PS, RS, RSM>(tile, g, b, xv, tk, tm);
-            else q6k_item_lean<R8, NBU, PS, RS>(tile, g, b, xv, tk);
+            if constexpr (FMT == Q4K) q4k_item_lean<NBC, PS, RS, RSM>(tile, g, b, xv, tk, tm);
+            else q6k_item_lean<R8, NBC, PS, RS>(tile, g, b, xv, tk);
           }
         }
       }
       __syncwarp();
       if (lane == 0) {
         mbar_arrive(&empty[st]);
-        mbar_arrive(&intdone[i & 1]);
+        mbar_arrive(&intdone[u & 1]);
       }
     }
     return;
@@ -1603,21 +1635,28 @@ __global__ void __launch_bounds__((NIW + NCW + 1) * 32, MINB) gemv_lean_kernel(P
   const int ct = threadIdx.x - NIW * 32;
   unsigned long long best = 0ull;
   const unsigned send_ep = P.peer_send ? *P.peer_ctr + 1u : 0u;
-  for (int i = 0; i < ntiles; i++) {
-    if (!mbar_wait_bounded(&intdone[i & 1], (i >> 1) & 1, P.err)) break;
-    const int r0 = rb + i * T;
+  // lane = row (T >= 16): the row's chains, carried across its chunks
+  float s[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+  float sumf = 0.0f;
+  for (int u = 0; u < nunits; u++) {
+    if (!mbar_wait_bounded(&intdone[u & 1], (u >> 1) & 1, P.err)) break;
+    const int r0 = rb + (u / NCH) * T, c = u % NCH;
     const int nr = min(T, re - r0);
-    const float *tk = reinterpret_cast<const float *>(cbase + (i & 1) * CBUF);
+    const float *tk = reinterpret_cast<const float *>(cbase + (u & 1) * CBUF);
     const float *tm = tk + T * RS;
     if constexpr (!R8) {
       // lane = row: sums[k] += d * sumi[k] over the blocks (the products are
       // in tk), sumf -= dmin * minsum, then s = sumf + sums[0] + ... + sums[7]
-      for (int lr = ct; lr < nr; lr += NCW * 32) {
+      const int lr = ct;
+      if (lr < nr) {
         const float *row = tk + lr * RS;
-        float s[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
-        float sumf = 0.0f;
+        if (c == 0) {
 #pragma unroll
-        for (int b = 0; b < NBU; b++) {
+          for (int k = 0; k < 8; k++) s[k] = 0.0f;
+          sumf = 0.0f;
+        }
+#pragma unroll
+        for (int b = 0; b < NBC; b++) {
           const float4 a = *reinterpret_cast<const float4 *>(row + 8 * b);
           const float4 c = *reinterpret_cast<const float4 *>(row + 8 * b + 4);
           s[0] = __fadd_rn(s[0], a.x);
@@ -1630,10 +1669,12 @@ __global__ void __launch_bounds__((NIW + NCW + 1) * 32, MINB) gemv_lean_kernel(P
           s[7] = __fadd_rn(s[7], c.w);
           if constexpr (FMT == Q4K) sumf = __fsub_rn(sumf, tm[lr * RSM + b]);
         }
-        float acc = sumf;
+        if (c == NCH - 1) {
+          float acc = sumf;
 #pragma unroll
-        for (int k = 0; k < 8; k++) acc = __fadd_rn(acc, s[k]);
-        lean_emit_row<ARGMAX>(P, r0 + lr, acc, send_ep, best);
+          for (int k = 0; k < 8; k++) acc = __fadd_rn(acc, s[k]);
+          lean_emit_row<ARGMAX>(P, r0 + lr, acc, send_ep, best);
+        }
       }
     } else {
       // lane = (row, class): 8-row tiles of long rows (Q6_K, no min term)
@@ -1643,7 +1684,7 @@ __global__ void __launch_bounds__((NIW + NCW + 1) * 32, MINB) gemv_lean_kernel(P
         const float *tkr = tk + lr * RS + k;
         float sums = 0.0f;
 #pragma unroll 16
-        for (int b = 0; b < NBU; b++) sums = __fadd_rn(sums, tkr[8 * b]);
+        for (int b = 0; b < NBC; b++) sums = __fadd_rn(sums, tkr[8 * b]);
         float acc = 0.0f;
 #pragma unroll
         for (int kk = 0; kk < 8; kk++) acc = __fadd_rn(acc, __shfl_sync(gm, sums, (lane & 24) + kk));
@@ -1651,7 +1692,7 @@ __global__ void __launch_bounds__((NIW + NCW + 1) * 32, MINB) gemv_lean_kernel(P
       }
     }
     __syncwarp();
-    if (lane == 0) mbar_arrive(&chaindone[i & 1]);
+    if (lane == 0) mbar_arrive(&chaindone[u & 1]);
   }
   if (P.peer_send) {
     __threadfence_system();
@@ -1801,15 +1842,16 @@ struct LeanPlan {
   int T = 0, S = 0, smem = 0, threads = 0, img_bytes = 0;
 };
 
-template <int FMT, int NBU, int T, int NIW = kTcIntWarps, int MINB = 1>
+template <int FMT, int NBU, int T, int NBC = NBU, int NIW = kTcIntWarps, int MINB = 1>
 LeanPlan lean_plan(bool am, int smem_max) {
-  using Sh = LeanShape<FMT, NBU>;
+  using Sh = LeanShape<FMT, NBC>;
   constexpr int stage = (T * Sh::kPs + 127) / 128 * 128;
-  constexpr int fixed = kTcBarBytes + NBU * Sh::kImg + 2 * lean_cbuf_bytes<FMT, NBU, T>();
+  constexpr int fixed = kTcBarBytes + NBU * Sh::kImg + 2 * lean_cbuf_bytes<FMT, NBC, T>();
   LeanPlan p;
   p.S = std::min(kMaxStages, (smem_max - fixed) / stage);
   if (p.S < 2) return p;
-  p.fn = am ? gemv_lean_kernel<FMT, NBU, T, NIW, 1, true, MINB> : gemv_lean_kernel<FMT, NBU, T, NIW, 1, false, MINB>;
+  p.fn = am ? gemv_lean_kernel<FMT, NBU, T, NIW, 1, true, MINB, NBC>
+            : gemv_lean_kernel<FMT, NBU, T, NIW, 1, false, MINB, NBC>;
   p.T = T;
   p.smem = fixed + p.S * stage;
   p.threads = (NIW + 2) * 32;
@@ -1822,7 +1864,7 @@ LeanPlan lean_for(int device, const unltd_weight_s &w, int mode, bool am) {
   const int smem_max = max_smem_optin(device) - 1024;
   if (w.dtype == Q4K && w.dim_in == 4096) return lean_plan<Q4K, 16, 32>(am, smem_max);
   if (w.dtype == Q6K && w.dim_in == 4096) return lean_plan<Q6K, 16, 16>(am, smem_max);
-  if (w.dtype == Q6K && w.dim_in == 12288) return lean_plan<Q6K, 48, 8>(am, smem_max);
+  if (w.dtype == Q6K && w.dim_in == 12288) return lean_plan<Q6K, 48, 16, kQ6Chunk>(am, smem_max);
   return LeanPlan();
 }
 
@@ -1857,7 +1899,7 @@ cudaError_t gemv_prewarm(int device) {
     }
   for (int am = 0; am < 2; am++) {
     const GemvFn lean[3] = {lean_plan<Q4K, 16, 32>(am, m).fn, lean_plan<Q6K, 16, 16>(am, m).fn,
-                            lean_plan<Q6K, 48, 8>(am, m).fn};
+                            lean_plan<Q6K, 48, 16, kQ6Chunk>(am, m).fn};
     for (GemvFn fn : lean)
       if (fn) set(fn);
   }

@@ -105,6 +105,27 @@ __host__ __device__ inline int q6_q8k_byte(int j, int hh, int w, int ab, int bpo
   return 128 * (2 * hh + (w >> 1)) + 16 * j + 4 * (2 * (w & 1) + ab) + bpos;
 }
 
+// Q6_K rows of more than 16 blocks (a multiple of 16) are stored as chunks of
+// 16 blocks, each laid out like a 16-block row ([ql][qh][scales][d]), so a
+// 16-block slice of a long row is one contiguous 3360-byte range (the
+// tensor-core GEMV streams rows of 12288 inputs as three such chunks). Other
+// rows keep the planes of the whole row.
+constexpr int kQ6Chunk = 16;
+__host__ __device__ inline bool q6_chunked(size_t nb) { return nb > (size_t)kQ6Chunk && nb % kQ6Chunk == 0; }
+// Block b of a Q6_K row: byte offset of the planes holding it (its chunk, or
+// the row), the block count those planes are laid out for, and b's index there.
+__host__ __device__ inline void q6_locate(size_t nb, size_t b, size_t &off, int &nbl, int &bl) {
+  if (q6_chunked(nb)) {
+    off = (b / kQ6Chunk) * (size_t)(kQ6Chunk * 210);
+    nbl = kQ6Chunk;
+    bl = (int)(b % kQ6Chunk);
+  } else {
+    off = 0;
+    nbl = (int)nb;
+    bl = (int)b;
+  }
+}
+
 __host__ __device__ inline size_t round_up(size_t v, size_t a) { return (v + a - 1) / a * a; }
 
 // GGUF bytes of one row (min_forward.rs:52-80); 0 when not a whole number of blocks.

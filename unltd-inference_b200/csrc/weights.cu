@@ -34,9 +34,12 @@ __global__ void repack_q6k(const uint8_t *__restrict__ raw, uint8_t *__restrict_
   if (t >= rows * nb) return;
   size_t r = t / nb, b = t % nb;
   const uint8_t *src = raw + r * row_bytes + b * kQ6Bytes;
-  uint8_t *row = dev + r * stride;
-  uint8_t *ql = row + b * 128, *qh = row + nb * 128 + b * 64;
-  uint8_t *sc = row + nb * 192 + b * 16, *d = row + nb * 208 + b * 2;
+  size_t off;
+  int nbl, bl;
+  q6_locate(nb, b, off, nbl, bl);
+  uint8_t *row = dev + r * stride + off;
+  uint8_t *ql = row + bl * 128, *qh = row + nbl * 128 + bl * 64;
+  uint8_t *sc = row + nbl * 192 + bl * 16, *d = row + nbl * 208 + bl * 2;
   for (int o = 0; o < 128; o++) ql[16 * (o >> 4) + q6_pic(o & 15)] = src[o];
   // the top bit of every 2-bit field flipped: the GEMVs' 4*(q - 32) operand
   // words then need no sign flip of their own (q6_a4_lo / q6_a4_hi)
@@ -81,19 +84,22 @@ __global__ void dequant_q6k(const uint8_t *__restrict__ dev, float *__restrict__
   size_t n = nb * kQK;
   size_t t = blockIdx.x * (size_t)blockDim.x + threadIdx.x;
   if (t >= rows * n) return;
-  size_t r = t / n, e = t % n, b = e / kQK;
+  size_t r = t / n, e = t % n;
+  size_t off;
+  int nbl, b;
+  q6_locate(nb, e / kQK, off, nbl, b);
   int el = (int)(e % kQK);
-  const uint8_t *row = dev + r * stride;
+  const uint8_t *row = dev + r * stride + off;
   int h = el >> 7, pos = el & 127;
   int qlo = 64 * h + (pos & 63);
   int qho = 32 * h + (pos & 31);
   uint8_t lb = row[b * 128 + 16 * (qlo >> 4) + q6_pic(qlo & 15)];
-  uint8_t hb = row[nb * 128 + b * 64 + 16 * (qho >> 4) + q6_pic(qho & 15)] ^ 0xAAu;  // stored flipped
+  uint8_t hb = row[nbl * 128 + b * 64 + 16 * (qho >> 4) + q6_pic(qho & 15)] ^ 0xAAu;  // stored flipped
   int nib = pos < 64 ? (lb & 0xF) : (lb >> 4);
   int hi2 = (hb >> (2 * (pos >> 5))) & 3;
   int q = (nib | (hi2 << 4)) - 32;
-  int sc = (int8_t)row[nb * 192 + b * 16 + (el >> 4)];
-  const uint8_t *dp = row + nb * 208 + b * 2;
+  int sc = (int8_t)row[nbl * 192 + b * 16 + (el >> 4)];
+  const uint8_t *dp = row + nbl * 208 + b * 2;
   float d = h2f_bits(dp[0] | (dp[1] << 8));
   // f32 product, not an integer one: keeps the sign of a zero weight
   // (a negative scale times q = 0 is -0.0 in the reference's f64 decode).
