@@ -251,26 +251,64 @@ def cpu_baseline(steps=3):
     }
 
 
-def decode_bytes_per_token(cfg, position):
+def decode_bytes_per_token(cfg, position, n_seq=1):
     """Bytes one greedy decode step must move: every projection's packed
-    weights, the LM head, one embedding row, the f32 norms and conv kernels,
-    the GDN matrices (read and written), the conv windows and the K/V rows of
-    the `position + 1` cached positions (qwen35_forward.rs step)."""
+    weights, the LM head, the f32 norms and conv kernels (once per step), and
+    per sequence one embedding row, the GDN matrices (read and written), the
+    conv windows and the K/V rows of the `position + 1` cached positions
+    (qwen35_forward.rs step)."""
     d = synth.qwen35_dims(cfg)
     total = 0
     for nm, dt, di, do in synth.qwen35_tensor_list(cfg):
         if nm == "token_embd.weight":
-            total += synth.row_bytes(dt, di)
+            total += n_seq * synth.row_bytes(dt, di)
         else:
             total += synth.row_bytes(dt, di) * do
     n_attn = sum(d["attn"])
     n_recr = cfg["n_layer"] - n_attn
-    total += n_recr * (2 * 4 * d["nv"] * d["hd"] * d["hd"] + 4 * cfg["conv_kernel"] * d["dconv"])
-    total += n_attn * 2 * 4 * (position + 1) * d["kvlen"]
+    total += n_seq * n_recr * (2 * 4 * d["nv"] * d["hd"] * d["hd"] + 4 * cfg["conv_kernel"] * d["dconv"])
+    total += n_seq * n_attn * 2 * 4 * (position + 1) * d["kvlen"]
     return total
 
 
-def decode_bench(n_tokens, with_cpu, rank=0, world=1, dist=None, profile_region=False):
+def decode_batch_bench(m, cfg, st, pos0, n_seq, n_steps):
+    """BASELINE config 4 at batch n_seq on one GPU: n_seq sequences from the
+    2048-position state (each its own first token) decoded together through
+    unltd_qwen35_batch_decode; every weight matrix is read once per step for
+    all sequences. Device-timed on the session stream."""
+    import torch
+
+    b = m.batch_session(pos0 + n_steps + 16, n_seq)
+    for z in range(n_seq):
+        b.set_state(z, pos0, st["conv"], st["gdn"], st["k"], st["v"])
+    first = [1000 + 37 * z for z in range(n_seq)]
+    warm = b.decode(first, 4)
+    ext = torch.cuda.ExternalStream(b.info()["stream"])
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    torch.cuda.synchronize()
+    t0 = time.perf_counter()
+    e0.record(ext)
+    toks = b.decode(warm[:, -1], n_steps)
+    e1.record(ext)
+    torch.cuda.synchronize()
+    wall = time.perf_counter() - t0
+    ms_step = e0.elapsed_time(e1) / n_steps
+    bps = decode_bytes_per_token(cfg, pos0 + 4 + n_steps // 2, n_seq)
+    peak, peak_kind = _peaks()
+    gbs = bps / (ms_step * 1e-3) / 1e9
+    out = {"workload": f"config4_qwen35_9b_synthetic_greedy_decode_ctx2048_batch{n_seq}", "n_seq": n_seq,
+           "steps": n_steps, "n_gpus": 1, "tok_s": round(n_seq * 1e3 / ms_step, 1), "ms_per_step": round(ms_step, 4),
+           "e2e_tok_s": round(n_seq * n_steps / wall, 1), "bytes_per_step": bps, "hbm_gbs": round(gbs, 1),
+           "roofline_frac": round(gbs / peak, 4), "peak": peak, "peak_kind": peak_kind,
+           "launches_per_step": b.info()["launches_per_step"],
+           "arithmetic": "Q8K_EXACT projections (one weight pass for all sequences); every sequence bit-identical "
+                         "to a one-sequence session",
+           "distinct_tokens_seq0": len(set(int(t) for t in toks[0]))}
+    b.close()
+    return out
+
+
+def decode_bench(n_tokens, with_cpu, rank=0, world=1, dist=None, profile_region=False, batch=32):
     """BASELINE configs 3 and 4: greedy decode of the synthetic 9B-class hybrid
     model from a 2048-position context through unltd_qwen35_decode, on one GPU
     or tensor-parallel over `world` GPUs (one process each). Device-timed on
@@ -334,6 +372,9 @@ def decode_bench(n_tokens, with_cpu, rank=0, world=1, dist=None, profile_region=
         "distinct_tokens": len(set(int(t) for t in toks)),
     }
     s.close()
+    if world == 1 and batch > 1:
+        out["batch"] = 1
+        out["batch%d" % batch] = decode_batch_bench(m, cfg, st, pos0, batch, max(4, n_tokens // 4))
     m.close()
     ctx.close()
     if with_cpu and rank == 0:
@@ -445,6 +486,7 @@ def main():
     ap.add_argument("--mode", default="q8k", choices=["q8k", "f32x"], help="arithmetic of the K-quant GEMVs")
     ap.add_argument("--no-decode", action="store_true", help="skip the config-3 decode measurement")
     ap.add_argument("--decode-tokens", type=int, default=64)
+    ap.add_argument("--decode-batch", type=int, default=32, help="sequences of the batch-decode measurement (1: none)")
     ap.add_argument("--decode-only", action="store_true", help="measure only the decode step (profiling)")
     ap.add_argument("--gemm-only", action="store_true", help="measure only the config-2 GEMM (profiling)")
     ap.add_argument("--profile-region", action="store_true",
@@ -482,7 +524,7 @@ def main():
         return
 
     if args.decode_only:
-        d = decode_bench(args.decode_tokens, with_cpu=False, rank=rank, world=world, dist=dist,
+        d = decode_bench(args.decode_tokens, with_cpu=False, rank=rank, world=world, dist=dist, batch=args.decode_batch,
                          profile_region=args.profile_region)
         if rank == 0:
             os.write(out_fd, (json.dumps({"metric": "decode tok/s", "decode": d}) + "\n").encode())
@@ -718,7 +760,7 @@ def main():
     if args.only is None and not args.no_decode:
         try:
             decode = decode_bench(args.decode_tokens, with_cpu=not args.no_cpu_baseline and world == 1, rank=rank,
-                                  world=world, dist=dist)
+                                  world=world, dist=dist, batch=args.decode_batch)
         except Exception as e:  # report it in the line; the GEMV measurement above stands
             decode = {"error": f"{type(e).__name__}: {e}"[:400]}
 

@@ -139,6 +139,22 @@ int32_t unltd_gemv_argmax(unltd_ctx ctx, unltd_weight w, const float *x_dev, flo
 int32_t unltd_gemv_argmax_shard(unltd_ctx ctx, unltd_weight w, const float *x_dev, float *logits_dev,
                                 uint64_t *key_dev, uint32_t row0, int32_t mode);
 
+/* Batch decode: y_s = W . x_s for n_seq (1..32) sequences that share W,
+ * x_dev f32 [n_seq][dim_in], y_dev f32 [n_seq][dim_out]. Every y_s is the
+ * bits of unltd_gemv(..., UNLTD_MODE_Q8K_EXACT) on x_s alone, i.e.
+ * gemv_quant_q8k (quants.rs:474-515) per sequence; the reference decodes one
+ * sequence per step (qwen35_forward.rs:289), so this is its operator applied
+ * to each sequence of a batch, with W read from memory once. Q4_K and Q6_K
+ * weights, Q8K_EXACT mode only. */
+int32_t unltd_gemv_batch(unltd_ctx ctx, unltd_weight w, const float *x_dev, float *y_dev, int32_t n_seq,
+                         int32_t mode);
+
+/* The LM head of a batch: logits and greedy token of every sequence
+ * (unltd_gemv_argmax per sequence, same NaN rules). `logits_dev` [n_seq][dim_out]
+ * may be NULL; `tokens_dev` receives n_seq uint32 indices. */
+int32_t unltd_gemv_argmax_batch(unltd_ctx ctx, unltd_weight w, const float *x_dev, float *logits_dev,
+                                uint32_t *tokens_dev, int32_t n_seq, int32_t mode);
+
 /* Batched prefill: Y[m][n] = sum_k X[m][k] * W[n][k] for m < m_tokens, X f32
  * row-major [m_tokens][dim_in], Y f32 row-major [m_tokens][dim_out]. This is
  * gemv_quant (quants.rs:422) applied to every token at once; the reference
@@ -297,6 +313,28 @@ int32_t unltd_qwen35_session_shape(unltd_qwen35_session s, int64_t *conv_row, in
 /* Last step's logits (this rank's vocab rows) and hidden state (l_out of the
  * last layer, full n_embd on every rank). */
 int32_t unltd_qwen35_session_read(unltd_qwen35_session s, float *logits, float *hidden);
+
+/* Batch decode (batch 32): one session of n_seq (1..32)
+ * independent sequences that share the model, each with its own state and
+ * position; one step decodes every sequence, reading each weight matrix once
+ * (unltd_gemv_batch). Every sequence's tokens, logits and hidden states are
+ * those of a one-sequence session started from the same state: the
+ * reference's qwen35_forward.rs:289 step, applied per sequence. One GPU. */
+int32_t unltd_qwen35_session_create_batch(unltd_qwen35 m, int32_t ctx_len, int32_t n_seq,
+                                          unltd_qwen35_session *out);
+/* set_state / get_state / session_read of sequence `seq`. */
+int32_t unltd_qwen35_batch_set_state(unltd_qwen35_session s, int32_t seq, int32_t position,
+                                     const float *const *conv, const float *const *gdn,
+                                     const float *const *kcache, const float *const *vcache);
+int32_t unltd_qwen35_batch_get_state(unltd_qwen35_session s, int32_t seq, float *const *conv, float *const *gdn,
+                                     float *const *kcache, float *const *vcache);
+int32_t unltd_qwen35_batch_read(unltd_qwen35_session s, int32_t seq, float *logits, float *hidden);
+/* n_steps greedy steps of every sequence: step 0 of sequence z consumes
+ * tokens[z]; tokens_out[z * n_steps + i] = its token of step i. */
+int32_t unltd_qwen35_batch_decode(unltd_qwen35_session s, const uint32_t *tokens, int32_t n_steps,
+                                  uint32_t *tokens_out);
+/* The session's sequence count and each sequence's position (may be NULL). */
+int32_t unltd_qwen35_batch_info(unltd_qwen35_session s, int32_t *n_seq, int32_t *positions);
 
 /* ---- reference-signature API (host buffers, synchronous) ---------------- */
 /* quants.rs:422  pub fn gemv_quant(out, x, w, dim_in, dim_out, dtype) */

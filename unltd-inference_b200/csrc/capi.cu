@@ -113,11 +113,17 @@ int32_t unltd_ctx_create(int32_t device, unltd_ctx *out) {
   c->device = device;
   cudaDeviceGetAttribute(&c->num_sms, cudaDevAttrMultiProcessorCount, device);
   e = cudaStreamCreateWithFlags(&c->own_stream, cudaStreamNonBlocking);
-  if (e == cudaSuccess) e = cudaMalloc(&c->argmax_key, 64);
+  // [key | done | err | token | pad] then the batched argmax state: 32 keys,
+  // a counter, 32 tokens
+  if (e == cudaSuccess) e = cudaMalloc(&c->argmax_key, 512);
   if (e == cudaSuccess) {
-    c->argmax_done = reinterpret_cast<unsigned *>(reinterpret_cast<uint8_t *>(c->argmax_key) + 8);
-    c->err = reinterpret_cast<int *>(reinterpret_cast<uint8_t *>(c->argmax_key) + 12);
-    e = cudaMemset(c->argmax_key, 0, 64);
+    uint8_t *base = reinterpret_cast<uint8_t *>(c->argmax_key);
+    c->argmax_done = reinterpret_cast<unsigned *>(base + 8);
+    c->err = reinterpret_cast<int *>(base + 12);
+    c->bkey = reinterpret_cast<unsigned long long *>(base + 64);
+    c->bdone = reinterpret_cast<unsigned *>(base + 64 + 8 * kMaxBatch);
+    c->btok = reinterpret_cast<uint32_t *>(base + 128 + 8 * kMaxBatch);
+    e = cudaMemset(c->argmax_key, 0, 512);
   }
   if (e == cudaSuccess) {
     c->scratch_bytes = 256 * 1024;
@@ -291,6 +297,69 @@ int32_t unltd_gemv_argmax_shard(unltd_ctx c, unltd_weight w, const float *x, flo
   a.argmax_row0 = (int)row0;
   a.key_out = reinterpret_cast<unsigned long long *>(key);
   return gemv_launch(c, a);
+}
+
+static int32_t check_batch(unltd_ctx c, unltd_weight w, int32_t n_seq, int32_t mode, const char *fn) {
+  if (w->ctx != c) return set_error(UNLTD_ERR_INVALID_ARG, std::string(fn) + ": weight belongs to another context");
+  if (n_seq < 1 || n_seq > kMaxBatch)
+    return set_error(UNLTD_ERR_INVALID_ARG, std::string(fn) + ": n_seq must be 1..32");
+  if (mode != MODE_Q8K) return set_error(UNLTD_ERR_UNSUPPORTED, std::string(fn) + ": Q8K_EXACT mode only");
+  if (w->dtype != Q4K && w->dtype != Q6K)
+    return set_error(UNLTD_ERR_UNSUPPORTED, std::string(fn) + ": Q4_K and Q6_K weights only");
+  if (!gemv_batch_supported(c->device, *w))
+    return set_error(UNLTD_ERR_UNSUPPORTED, std::string(fn) + ": rows too long for a shared-memory tile");
+  return UNLTD_OK;
+}
+
+// Grows the context scratch to n_seq batched x images of w.
+static int32_t reserve_batch(unltd_ctx c, unltd_weight w, int32_t n_seq) {
+  const size_t need = gemv_batch_img_bytes(*w) * (size_t)n_seq;
+  if (c->scratch_bytes >= need) return UNLTD_OK;
+  if (c->scratch_fixed) return set_error(UNLTD_ERR_UNSUPPORTED, "gemv_batch: x images larger than the fixed scratch");
+  cudaError_t e = cudaStreamSynchronize(c->stream);
+  if (e == cudaSuccess && c->scratch) e = cudaFree(c->scratch);
+  c->scratch = nullptr;
+  c->scratch_bytes = 0;
+  if (e == cudaSuccess) e = cudaMalloc(&c->scratch, need);
+  if (e != cudaSuccess) return cuda_error(e, "gemv_batch scratch");
+  c->scratch_bytes = need;
+  return UNLTD_OK;
+}
+
+int32_t unltd_gemv_batch(unltd_ctx c, unltd_weight w, const float *x, float *y, int32_t n_seq, int32_t mode) {
+  if (!c || !w || !x || !y) return set_error(UNLTD_ERR_INVALID_ARG, "gemv_batch: NULL argument");
+  int32_t rc = check_batch(c, w, n_seq, mode, "gemv_batch");
+  if (rc) return rc;
+  CtxGuard g(c->device);
+  if ((rc = reserve_batch(c, w, n_seq))) return rc;
+  BatchGemvArgs a{w};
+  a.x = x;
+  a.xstride = w->dim_in;
+  a.y = y;
+  a.ystride = w->dim_out;
+  a.nseq = n_seq;
+  return gemv_batch_launch(c, a);
+}
+
+int32_t unltd_gemv_argmax_batch(unltd_ctx c, unltd_weight w, const float *x, float *logits, uint32_t *tokens,
+                                int32_t n_seq, int32_t mode) {
+  if (!c || !w || !x || !tokens) return set_error(UNLTD_ERR_INVALID_ARG, "gemv_argmax_batch: NULL argument");
+  if (w->dim_out == 0) return set_error(UNLTD_ERR_LENGTH, "gemv_argmax_batch: empty logits");
+  if (w->dim_out > 0x7FFFFFFFull) return set_error(UNLTD_ERR_LENGTH, "gemv_argmax_batch: vocab beyond 2^31");
+  int32_t rc = check_batch(c, w, n_seq, mode, "gemv_argmax_batch");
+  if (rc) return rc;
+  CtxGuard g(c->device);
+  if ((rc = reserve_batch(c, w, n_seq))) return rc;
+  BatchGemvArgs a{w};
+  a.x = x;
+  a.xstride = w->dim_in;
+  a.y = logits;
+  a.ystride = w->dim_out;
+  a.nseq = n_seq;
+  a.key = c->bkey;
+  a.done = c->bdone;
+  a.token = tokens;
+  return gemv_batch_launch(c, a);
 }
 
 int32_t unltd_gemm(unltd_ctx c, unltd_weight w, const float *X, float *Y, size_t m_tokens) {

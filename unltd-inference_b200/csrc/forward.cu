@@ -44,6 +44,17 @@ __device__ __forceinline__ float softplus_f(float x) {
   return x > 20.0f ? x : log_cr(__fadd_rn(1.0f, exp_cr(x)));
 }
 
+// ---- batch of sequences ---------------------------------------------------
+// A session of n_seq sequences keeps every per-sequence buffer in its own
+// arena; the arenas are ss bytes apart, so sequence z's copy of a buffer is
+// the pointer of sequence 0 plus z * ss. Kernels take the sequence from
+// blockIdx.z (grids are at most 2-D otherwise).
+template <class T>
+__device__ __forceinline__ T *seq_ptr(T *p, size_t off) {
+  return p ? reinterpret_cast<T *>(reinterpret_cast<uintptr_t>(p) + off) : p;
+}
+__device__ __forceinline__ size_t seq_off(size_t ss) { return (size_t)blockIdx.z * ss; }
+
 // ---- reductions -----------------------------------------------------------
 // Sum of a and b over the block; every thread receives the same values.
 template <int NT>
@@ -101,6 +112,7 @@ struct NormArgs {
   uint8_t *img4, *img6;     // Q4_K / Q6_K image (either may be null)
   unsigned long long *key;  // non-null: reset the LM-head argmax state
   unsigned *done;
+  size_t ss = 0;            // bytes between the sequences' arenas (a, b, r_out, images)
 };
 
 __global__ void __launch_bounds__(256) norm_quant_kernel(NormArgs p) {
@@ -109,6 +121,14 @@ __global__ void __launch_bounds__(256) norm_quant_kernel(NormArgs p) {
   __shared__ float s_mean;
   __shared__ Q8KSpanSmem sm;
   pdl_wait();
+  {
+    const size_t so = seq_off(p.ss);
+    p.a = seq_ptr(p.a, so);
+    p.b = seq_ptr(p.b, so);
+    p.r_out = seq_ptr(p.r_out, so);
+    p.img4 = seq_ptr(p.img4, so);
+    p.img6 = seq_ptr(p.img6, so);
+  }
   const int t = threadIdx.x, span = blockIdx.x;
   auto R = [&](int i) { return p.b ? __fadd_rn(p.a[i], p.b[i]) : p.a[i]; };
   double S = 0.0, A = 0.0;
@@ -158,9 +178,11 @@ __global__ void __launch_bounds__(256) norm_quant_kernel(NormArgs p) {
 
 // ---- token embedding: one Q4_K row, dequantized (min_forward.rs:160-184) --
 __global__ void embed_q4k_kernel(const uint8_t *table, size_t stride, size_t nb, const uint32_t *token,
-                                 uint32_t vocab, float *x, int n, int *err) {
+                                 uint32_t vocab, float *x, int n, int *err, size_t ss) {
   pdl_trigger();
   pdl_wait();
+  token = seq_ptr(token, seq_off(ss));
+  x = seq_ptr(x, seq_off(ss));
   uint32_t t = *token;
   if (t >= vocab) {
     if (blockIdx.x == 0 && threadIdx.x == 0) atomicExch(err, kErrToken);
@@ -173,10 +195,14 @@ __global__ void embed_q4k_kernel(const uint8_t *table, size_t stride, size_t nb,
 
 // ---- SwiGLU (kernels.rs:174-182) fused with the Q8_K image of its output ---
 __global__ void __launch_bounds__(256) swiglu_quant_kernel(const float *g, const float *u, uint8_t *img4,
-                                                           uint8_t *img6) {
+                                                           uint8_t *img6, size_t ss) {
   pdl_trigger();
   __shared__ Q8KSpanSmem sm;
   pdl_wait();
+  g = seq_ptr(g, seq_off(ss));
+  u = seq_ptr(u, seq_off(ss));
+  img4 = seq_ptr(img4, seq_off(ss));
+  img6 = seq_ptr(img6, seq_off(ss));
   const int span = blockIdx.x, e = span * 256 + threadIdx.x;
   const float t = g[e];
   const float s = __fdiv_rn(t, __fadd_rn(1.0f, exp_cr(-t)));
@@ -199,6 +225,7 @@ struct RecrArgs {
   // and writes the span's Q8_K image(s) of ssm_out's input, then resets it)
   unsigned *span_ctr;
   uint8_t *img4, *img6;
+  size_t ss = 0;  // bytes between the sequences' arenas
 };
 
 // One CTA per (v-head h, quarter of its columns), one thread per channel of
@@ -330,6 +357,17 @@ __global__ void __launch_bounds__(HD) recr_mid_kernel(RecrArgs a) {
   __shared__ double red[2 * HD / 32];
   __shared__ float s_f[2];
   pdl_wait();
+  {
+    const size_t so = seq_off(a.ss);
+    a.proj = seq_ptr(a.proj, so);
+    a.ring = seq_ptr(a.ring, so);
+    a.state = seq_ptr(a.state, so);
+    a.y = seq_ptr(a.y, so);
+    a.pos = seq_ptr(a.pos, so);
+    a.span_ctr = seq_ptr(a.span_ctr, so);
+    a.img4 = seq_ptr(a.img4, so);
+    a.img6 = seq_ptr(a.img6, so);
+  }
   const int h = blockIdx.x, quarter = blockIdx.y, j = threadIdx.x;
   const int qk = h % a.nqk;  // periodic qk-head of v-head h (qwen35_forward.rs:464)
   const int pos = *a.pos, K = a.K;
@@ -496,7 +534,23 @@ struct AttnArgs {
   const int *pos;
   int nh, nkv, n_rot, nrp, ctx, nsplit;
   float eps, kq_scale;
+  size_t ss = 0;  // bytes between the sequences' arenas
 };
+
+// This CTA's sequence's copies of the per-sequence buffers.
+__device__ __forceinline__ void attn_at_seq(AttnArgs &a) {
+  const size_t so = seq_off(a.ss);
+  a.qk = seq_ptr(a.qk, so);
+  a.v = seq_ptr(a.v, so);
+  a.q = seq_ptr(a.q, so);
+  a.kcache = seq_ptr(a.kcache, so);
+  a.vcache = seq_ptr(a.vcache, so);
+  a.scores = seq_ptr(a.scores, so);
+  a.part = seq_ptr(a.part, so);
+  a.img4 = seq_ptr(a.img4, so);
+  a.img6 = seq_ptr(a.img6, so);
+  a.pos = seq_ptr(a.pos, so);
+}
 
 // q/k head norms, IMROPE (kernels.rs:381-400) and the cache write. One CTA
 // per q head and per kv head.
@@ -507,6 +561,7 @@ __global__ void __launch_bounds__(HDV) attn_pre_kernel(AttnArgs a) {
   __shared__ float sx[HDV];
   __shared__ float s_mean;
   pdl_wait();
+  attn_at_seq(a);
   const int b = blockIdx.x, j = threadIdx.x;
   const bool isq = b < a.nh;
   const int hh = isq ? b : b - a.nh;
@@ -641,6 +696,7 @@ __global__ void __launch_bounds__(256, 2) attn_scores_kernel(AttnArgs a) {
   pdl_trigger();
   extern __shared__ double qsm[];  // G x HDV
   pdl_wait();
+  attn_at_seq(a);
   const int kvh = blockIdx.x, G = a.nh / a.nkv;
   const int n_ctx = *a.pos + 1;
   const int p0 = blockIdx.y * 32;
@@ -675,6 +731,7 @@ __global__ void __launch_bounds__(256) attn_softmax_kernel(AttnArgs a) {
   extern __shared__ __align__(16) uint8_t sm[];
   __shared__ float redf[8];
   pdl_wait();
+  attn_at_seq(a);
   const int h = blockIdx.x, tid = threadIdx.x;
   const int n = *a.pos + 1;
   float *e = reinterpret_cast<float *>(sm);
@@ -721,6 +778,7 @@ __global__ void __launch_bounds__(HDV) attn_values_kernel(AttnArgs a) {
   extern __shared__ __align__(16) float vsm[];  // kChunk x HDV
   __shared__ double ssoft[kMaxGroup][kChunk];  // converted once, not per column
   pdl_wait();
+  attn_at_seq(a);
   const int kvh = blockIdx.x, split = blockIdx.y, c = threadIdx.x;
   const int n = *a.pos + 1, G = a.nh / a.nkv;
   const int p0 = split * kChunk;
@@ -778,6 +836,7 @@ __global__ void __launch_bounds__(256) attn_combine_quant_kernel(AttnArgs a) {
   pdl_trigger();
   __shared__ Q8KSpanSmem sm;
   pdl_wait();
+  attn_at_seq(a);
   const int span = blockIdx.x, t = threadIdx.x;
   const int e = span * 256 + t, h = e / HDV, c = e % HDV;
   const int kvh = h / (a.nh / a.nkv);
@@ -851,9 +910,13 @@ __global__ void key_to_token_kernel(const unsigned long long *key, uint32_t *tok
 }
 
 // token bookkeeping at the end of a step
-__global__ void step_end_kernel(const uint32_t *cur, uint32_t *hist, int *counter, int *pos) {
+__global__ void step_end_kernel(const uint32_t *cur, uint32_t *hist, int *counter, int *pos, size_t ss) {
   pdl_trigger();
   pdl_wait();
+  cur = seq_ptr(cur, seq_off(ss));
+  hist = seq_ptr(hist, seq_off(ss));
+  counter = seq_ptr(counter, seq_off(ss));
+  pos = seq_ptr(pos, seq_off(ss));
   hist[*counter] = *cur;
   *counter += 1;
   *pos += 1;
@@ -935,6 +998,13 @@ struct unltd_qwen35_session_s {
   unltd_ctx ctx = nullptr;  // own context: stream, GEMV scratch, argmax state
   int ctx_len = 0;
   int host_pos = 0;
+  // batch decode: n_seq sequences, every per-sequence buffer in the
+  // sequence's arena (the pointers below are sequence 0's; sequence z's are
+  // ss bytes further per z), positions tracked per sequence on the host
+  int nseq = 1;
+  size_t ss = 0;
+  uint8_t *arena = nullptr;
+  std::vector<int> seq_pos;
   // activations
   float *X = nullptr, *R = nullptr, *T = nullptr, *F = nullptr;
   float *proj = nullptr, *Y = nullptr, *FF = nullptr;
@@ -1265,6 +1335,16 @@ int32_t dalloc(std::vector<void *> &bufs, T **p, size_t n, const char *what) {
 
 // GEMV whose x image a fused producer kernel already wrote.
 int64_t launch_gemv_img(unltd_qwen35_session s, const unltd_weight_s *w, float *y, int32_t *rc, bool send = false) {
+  if (s->nseq > 1) {  // every sequence's GEMV in one pass over w
+    BatchGemvArgs b{w};
+    b.img = w->dtype == Q4K ? s->img4 : s->img6;
+    b.istride = s->ss;
+    b.y = y;
+    b.ystride = s->ss / 4;
+    b.nseq = s->nseq;
+    if (!*rc) *rc = gemv_batch_launch(s->ctx, b);
+    return 1;
+  }
   GemvArgs g{w, nullptr, send ? nullptr : y, MODE_Q8K, nullptr, nullptr, nullptr};
   g.img = w->dtype == Q4K ? s->img4 : s->img6;
   g.peer_send = send;
@@ -1317,10 +1397,13 @@ int32_t enqueue_step(unltd_qwen35_session s) {
     if (!rc) rc = comm_allreduce(m->ctx, st, buf, (size_t)count, false);
     nl++;
   };
+  const bool batch = s->nseq > 1;
+  const unsigned nz = (unsigned)s->nseq;
   auto norm = [&](const float *a, const float *b, float *r_out, const float *w, bool q4, bool q6, bool argmax) {
     NormArgs p{a, b, r_out, w, d.n, d.eps, q4 ? s->img4 : nullptr, q6 ? s->img6 : nullptr,
-               argmax ? s->ctx->argmax_key : nullptr, argmax ? s->ctx->argmax_done : nullptr};
-    chk(launch_pdl(norm_quant_kernel, dim3(d.n / 256), dim3(256), 0, st, p), "norm");
+               argmax && !batch ? s->ctx->argmax_key : nullptr, argmax && !batch ? s->ctx->argmax_done : nullptr};
+    p.ss = s->ss;
+    chk(launch_pdl(norm_quant_kernel, dim3(d.n / 256, 1, nz), dim3(256), 0, st, p), "norm");
   };
   // RMSNorm of a (+ b) feeding projection p (outputs at out + p.off[i]): fused
   // into the prologue of p's first tensor-core Q4_K GEMV when it has one,
@@ -1340,7 +1423,7 @@ int32_t enqueue_step(unltd_qwen35_session s) {
   auto norm_proj = [&](const float *a, const float *b, float *r_out, const float *w, const Proj &p, float *out,
                        bool recv = false) {
     int fi = -1;
-    for (size_t i = 0; i < p.w.size() && fi < 0; i++)
+    for (size_t i = 0; i < p.w.size() && fi < 0 && !batch; i++)
       if (gemv_norm_fusable(s->ctx, *p.w[i], MODE_Q8K)) fi = (int)i;
     if (fi < 0) {
       norm(a, b, r_out, w, any_dtype(p, Q4K), any_dtype(p, Q6K), false);
@@ -1362,9 +1445,9 @@ int32_t enqueue_step(unltd_qwen35_session s) {
     for (size_t i = 0; i < p.w.size(); i++)
       if ((int)i != fi) nl += launch_gemv_img(s, p.w[i], out + p.off[i], &rc);
   };
-  chk(launch_pdl(embed_q4k_kernel, dim3(d.n / 256), dim3(256), 0, st, (const uint8_t *)m->embd->dev,
+  chk(launch_pdl(embed_q4k_kernel, dim3(d.n / 256, 1, nz), dim3(256), 0, st, (const uint8_t *)m->embd->dev,
                  m->embd->row_stride, m->embd->nb, (const uint32_t *)s->cur_token, (uint32_t)d.vocab, s->X, d.n,
-                 s->ctx->err),
+                 s->ctx->err, s->ss),
       "embed");
   bool down_sent = false;  // the previous layer's down GEMV sent its rows to the peers
   for (int il = 0; il < d.n_layer; il++) {
@@ -1397,8 +1480,10 @@ int32_t enqueue_step(unltd_qwen35_session s) {
       a.span_ctr = s->span_ctr;
       a.img4 = L.out->dtype == Q4K ? s->img4 : nullptr;
       a.img6 = L.out->dtype == Q6K ? s->img6 : nullptr;
-      if (d.K == 4) chk(launch_pdl(recr_mid_kernel<128, 4>, dim3(d.nvl, 128 / kGdnCols), dim3(128), 0, st, a), "recr_mid");
-      else chk(launch_pdl(recr_mid_kernel<128, 0>, dim3(d.nvl, 128 / kGdnCols), dim3(128), 0, st, a), "recr_mid");
+      a.ss = s->ss;
+      const dim3 rg(d.nvl, 128 / kGdnCols, nz);
+      if (d.K == 4) chk(launch_pdl(recr_mid_kernel<128, 4>, rg, dim3(128), 0, st, a), "recr_mid");
+      else chk(launch_pdl(recr_mid_kernel<128, 0>, rg, dim3(128), 0, st, a), "recr_mid");
       nl += launch_gemv_img(s, L.out, s->T, &rc, out_send);
       if (!out_send) allreduce(s->T, d.n);
     } else {
@@ -1424,10 +1509,11 @@ int32_t enqueue_step(unltd_qwen35_session s) {
       a.nsplit = s->nsplit;
       a.eps = d.eps;
       a.kq_scale = d.kq_scale;
-      const dim3 sg(d.nkvl, (s->ctx_len + 31) / 32), vg(d.nkvl, s->nsplit);
+      a.ss = s->ss;
+      const dim3 sg(d.nkvl, (s->ctx_len + 31) / 32, nz), vg(d.nkvl, s->nsplit, nz);
       const size_t q_smem = (size_t)(d.nhl / d.nkvl) * d.hdv * 8, v_smem = (size_t)kChunk * d.hdv * 4;
       const size_t sm_smem = softmax_smem(s->ctx_len);
-      const dim3 cg(d.nhl * d.hdv / 256), pg(d.nhl + d.nkvl), smg(d.nhl);
+      const dim3 cg(d.nhl * d.hdv / 256, 1, nz), pg(d.nhl + d.nkvl, 1, nz), smg(d.nhl, 1, nz);
       if (d.hdv == 256) {
         chk(launch_pdl(attn_pre_kernel<256>, pg, dim3(256), 0, st, a), "attn_pre");
         chk(launch_pdl(attn_scores_kernel<256>, sg, dim3(256), q_smem, st, a), "attn_scores");
@@ -1446,9 +1532,9 @@ int32_t enqueue_step(unltd_qwen35_session s) {
     }
     // residual = x_in + attn_out; rmsnorm(residual, post_attention_norm) -> gate|up image
     norm_proj(s->X, s->T, s->R, L.post_norm, L.gate_up, s->FF, out_send);
-    chk(launch_pdl(swiglu_quant_kernel, dim3(d.nffl / 256), dim3(256), 0, st, (const float *)s->FF,
+    chk(launch_pdl(swiglu_quant_kernel, dim3(d.nffl / 256, 1, nz), dim3(256), 0, st, (const float *)s->FF,
                    (const float *)(s->FF + d.nffl), L.down->dtype == Q4K ? s->img4 : (uint8_t *)nullptr,
-                   L.down->dtype == Q6K ? s->img6 : (uint8_t *)nullptr),
+                   L.down->dtype == Q6K ? s->img6 : (uint8_t *)nullptr, s->ss),
         "swiglu");
     nl += launch_gemv_img(s, L.down, s->F, &rc, down_send);
     if (!down_send) allreduce(s->F, d.n);
@@ -1456,7 +1542,20 @@ int32_t enqueue_step(unltd_qwen35_session s) {
   }
   // l_out of the last layer -> output norm -> LM head + greedy argmax
   norm(s->R, s->F, s->X, m->out_norm, m->output->dtype == Q4K, m->output->dtype == Q6K, true);
-  {
+  if (batch) {
+    BatchGemvArgs b{m->output};
+    b.img = m->output->dtype == Q4K ? s->img4 : s->img6;
+    b.istride = s->ss;
+    b.y = s->logits;
+    b.ystride = s->ss / 4;
+    b.nseq = s->nseq;
+    b.key = s->ctx->bkey;
+    b.done = s->ctx->bdone;
+    b.token = s->cur_token;
+    b.tstride = s->ss / 4;
+    if (!rc) rc = gemv_batch_launch(s->ctx, b);
+    nl += 1;
+  } else {
     GemvArgs g{m->output, nullptr, s->logits, MODE_Q8K, s->ctx->argmax_key, s->ctx->argmax_done, s->cur_token};
     g.img = m->output->dtype == Q4K ? s->img4 : s->img6;
     g.argmax_row0 = d.v0;
@@ -1471,8 +1570,8 @@ int32_t enqueue_step(unltd_qwen35_session s) {
           "key_to_token");
     }
   }
-  chk(launch_pdl(step_end_kernel, dim3(1), dim3(1), 0, st, (const uint32_t *)s->cur_token, s->hist, s->counter,
-                 s->pos),
+  chk(launch_pdl(step_end_kernel, dim3(1, 1, nz), dim3(1), 0, st, (const uint32_t *)s->cur_token, s->hist,
+                 s->counter, s->pos, s->ss),
       "step_end");
   s->launches_per_step = nl;
   return rc;
@@ -1504,6 +1603,28 @@ int32_t run_step(unltd_qwen35_session s) {
     return cuda_error(cudaGraphLaunch(s->graph, s->ctx->stream), "qwen35: graph launch");
   }
   return enqueue_step(s);
+}
+
+}  // namespace
+
+namespace {
+// Per-sequence buffers of a session laid out in one arena: offsets of every
+// buffer (256-byte aligned), then one allocation of n_seq arenas.
+struct ArenaPlan {
+  size_t bytes = 0;
+  std::vector<std::pair<void **, size_t>> slots;
+  template <class T>
+  void add(T **p, size_t n) {
+    bytes = round_up(bytes, 256);
+    slots.push_back({reinterpret_cast<void **>(p), bytes});
+    bytes += std::max<size_t>(n * sizeof(T), 16);
+  }
+};
+
+// Sequence seq's copy of a per-sequence buffer of s.
+template <class T>
+T *seq_buf(unltd_qwen35_session s, T *p, int seq) {
+  return reinterpret_cast<T *>(reinterpret_cast<uint8_t *>(p) + (size_t)seq * s->ss);
 }
 
 }  // namespace
@@ -1703,7 +1824,9 @@ int32_t unltd_qwen35_destroy(unltd_qwen35 m) {
 
 int32_t unltd_qwen35_session_destroy(unltd_qwen35_session s);
 
-int32_t unltd_qwen35_session_create(unltd_qwen35 m, int32_t ctx_len, unltd_qwen35_session *out) {
+
+int32_t unltd_qwen35_session_create_batch(unltd_qwen35 m, int32_t ctx_len, int32_t n_seq,
+                                          unltd_qwen35_session *out) {
   if (!m || !out) return set_error(UNLTD_ERR_INVALID_ARG, "qwen35_session_create: NULL argument");
   *out = nullptr;
   if (!m->finalized) {
@@ -1711,10 +1834,26 @@ int32_t unltd_qwen35_session_create(unltd_qwen35 m, int32_t ctx_len, unltd_qwen3
   }
   if (ctx_len < 1 || ctx_len > 16384)
     return set_error(UNLTD_ERR_UNSUPPORTED, "qwen35_session_create: ctx must be in [1, 16384]");
+  if (n_seq < 1 || n_seq > kMaxBatch)
+    return set_error(UNLTD_ERR_INVALID_ARG, "qwen35_session_create: n_seq must be in [1, 32]");
   const Derived &d = m->d;
+  if (n_seq > 1 && d.world > 1)
+    return set_error(UNLTD_ERR_UNSUPPORTED, "qwen35_session_create: batch decode runs on one GPU");
+  if (n_seq > 1) {  // every projection must have a batched GEMV
+    auto ok = [&](const unltd_weight_s *w) { return gemv_batch_supported(m->ctx->device, *w); };
+    bool all = ok(m->output);
+    for (const Layer &L : m->layers) {
+      for (auto *w : L.in.w) all &= ok(w);
+      for (auto *w : L.gate_up.w) all &= ok(w);
+      all &= ok(L.out) && ok(L.down);
+    }
+    if (!all) return set_error(UNLTD_ERR_UNSUPPORTED, "qwen35_session_create: a projection has no batched GEMV");
+  }
   unltd_qwen35_session s = new unltd_qwen35_session_s();
   s->m = m;
   s->ctx_len = ctx_len;
+  s->nseq = n_seq;
+  s->seq_pos.assign(n_seq, 0);
   int32_t rc = unltd_ctx_create(m->ctx->device, &s->ctx);
   if (rc) {
     delete s;
@@ -1725,42 +1864,47 @@ int32_t unltd_qwen35_session_create(unltd_qwen35 m, int32_t ctx_len, unltd_qwen3
   const size_t n = d.n;
   s->nsplit = (ctx_len + kChunk - 1) / kChunk;
   const size_t spans = (size_t)std::max(d.n, d.nff) / 256;
-  if (!rc) rc = dalloc(B, &s->X, n, "session");
-  if (!rc) rc = dalloc(B, &s->R, n, "session");
-  if (!rc) rc = dalloc(B, &s->T, n, "session");
-  if (!rc) rc = dalloc(B, &s->F, n, "session");
-  if (!rc) rc = dalloc(B, &s->proj, m->proj_rows, "session");
-  if (!rc) rc = dalloc(B, &s->Y, n, "session");
-  if (!rc) rc = dalloc(B, &s->FF, 2 * (size_t)d.nffl, "session");
-  if (!rc) rc = dalloc(B, &s->q, (size_t)d.nhl * d.hdv, "session");
-  if (!rc) rc = dalloc(B, &s->scores, (size_t)d.nhl * ctx_len, "session");
-  if (!rc) rc = dalloc(B, &s->part, (size_t)d.nhl * s->nsplit * d.hdv, "session");
-  if (!rc) rc = dalloc(B, &s->tpkey, 1, "session");
-  if (!rc) rc = dalloc(B, &s->img4, spans * kImgQ8K4, "session");
-  if (!rc) rc = dalloc(B, &s->img6, spans * kImgQ8K6, "session");
-  if (!rc) rc = dalloc(B, &s->logits, (size_t)(d.v1 - d.v0), "session");
+  ArenaPlan A;
+  A.add(&s->X, n);
+  A.add(&s->R, n);
+  A.add(&s->T, n);
+  A.add(&s->F, n);
+  A.add(&s->proj, m->proj_rows);
+  A.add(&s->Y, n);
+  A.add(&s->FF, 2 * (size_t)d.nffl);
+  A.add(&s->q, (size_t)d.nhl * d.hdv);
+  A.add(&s->scores, (size_t)d.nhl * ctx_len);
+  A.add(&s->part, (size_t)d.nhl * s->nsplit * d.hdv);
+  A.add(&s->tpkey, 1);
+  A.add(&s->img4, spans * kImgQ8K4);
+  A.add(&s->img6, spans * kImgQ8K6);
+  A.add(&s->logits, (size_t)(d.v1 - d.v0));
+  A.add(&s->cur_token, 1);
+  A.add(&s->hist, (size_t)ctx_len + 1);
+  A.add(&s->feed, (size_t)ctx_len + 1);
+  A.add(&s->counter, 1);
+  A.add(&s->pos, 1);
+  A.add(&s->span_ctr, (size_t)d.nvl * d.hd / 256 + 1);
+  s->ring.assign(m->n_recr, nullptr);
+  s->state.assign(m->n_recr, nullptr);
+  s->kc.assign(m->n_attn, nullptr);
+  s->vc.assign(m->n_attn, nullptr);
+  for (int i = 0; i < m->n_recr; i++) {
+    A.add(&s->ring[i], (size_t)d.K * d.dconvl);
+    A.add(&s->state[i], (size_t)d.nvl * d.hd * d.hd);
+  }
+  for (int i = 0; i < m->n_attn; i++) {
+    A.add(&s->kc[i], (size_t)ctx_len * d.kvlenl);
+    A.add(&s->vc[i], (size_t)ctx_len * d.kvlenl);
+  }
+  s->ss = round_up(A.bytes, 4096);
+  // everything starts at zero: token, step counter, position, span counters,
+  // conv windows, GDN states and caches
+  rc = dalloc(B, &s->arena, s->ss * (size_t)n_seq, "session arena");
+  if (!rc) rc = cuda_error(cudaMemset(s->arena, 0, s->ss * (size_t)n_seq), "session init");
+  if (!rc)
+    for (auto &sl : A.slots) *sl.first = s->arena + sl.second;
   if (!rc) rc = dalloc(B, &s->rope, (size_t)ctx_len * std::max(d.nrp, 1), "session");
-  if (!rc) rc = dalloc(B, &s->cur_token, 1, "session");
-  if (!rc) rc = dalloc(B, &s->hist, (size_t)ctx_len + 1, "session");
-  if (!rc) rc = dalloc(B, &s->feed, (size_t)ctx_len + 1, "session");
-  if (!rc) rc = dalloc(B, &s->counter, 1, "session");
-  if (!rc) rc = dalloc(B, &s->pos, 1, "session");
-  if (!rc) rc = dalloc(B, &s->span_ctr, (size_t)d.nvl * d.hd / 256 + 1, "session");
-  if (!rc) rc = cuda_error(cudaMemset(s->span_ctr, 0, ((size_t)d.nvl * d.hd / 256 + 1) * 4), "session init");
-  for (int i = 0; !rc && i < m->n_recr; i++) {
-    float *r = nullptr, *st = nullptr;
-    rc = dalloc(B, &r, (size_t)d.K * d.dconvl, "session ring");
-    if (!rc) rc = dalloc(B, &st, (size_t)d.nvl * d.hd * d.hd, "session state");
-    s->ring.push_back(r);
-    s->state.push_back(st);
-  }
-  for (int i = 0; !rc && i < m->n_attn; i++) {
-    float *k = nullptr, *v = nullptr;
-    rc = dalloc(B, &k, (size_t)ctx_len * d.kvlenl, "session kv cache");
-    if (!rc) rc = dalloc(B, &v, (size_t)ctx_len * d.kvlenl, "session kv cache");
-    s->kc.push_back(k);
-    s->vc.push_back(v);
-  }
   // IMROPE angles (kernels.rs:381-400): angle = pos * theta^ic by repeated
   // multiplication; (cos, sin) of the rotated pairs ic % 3 == 0, from libm.
   if (!rc && d.nrp > 0) {
@@ -1774,13 +1918,6 @@ int32_t unltd_qwen35_session_create(unltd_qwen35 m, int32_t ctx_len, unltd_qwen3
     }
     rc = cuda_error(cudaMemcpy(s->rope, tab.data(), tab.size() * sizeof(double2), cudaMemcpyHostToDevice), "rope table");
   }
-  // token, step counter and position start at zero
-  for (void *p : {(void *)s->cur_token, (void *)s->counter, (void *)s->pos})
-    if (!rc) rc = cuda_error(cudaMemset(p, 0, 4), "session init");
-  for (int i = 0; !rc && i < m->n_recr; i++) {
-    rc = cuda_error(cudaMemset(s->ring[i], 0, (size_t)d.K * d.dconvl * 4), "session init");
-    if (!rc) rc = cuda_error(cudaMemset(s->state[i], 0, (size_t)d.nvl * d.hd * d.hd * 4), "session init");
-  }
   // GEMV scratch (the projections that still run a prep kernel) sized before
   // any graph capture
   if (!rc) {
@@ -1792,6 +1929,7 @@ int32_t unltd_qwen35_session_create(unltd_qwen35 m, int32_t ctx_len, unltd_qwen3
       e = cudaFuncSetAttribute(attn_values_kernel<128>, cudaFuncAttributeMaxDynamicSharedMemorySize, kChunk * 128 * 4);
     rc = cuda_error(e, "attention smem");
   }
+  if (!rc && n_seq > 1) rc = cuda_error(gemv_batch_prewarm(m->ctx->device), "batched GEMV attributes");
   if (!rc) rc = cuda_error(cudaDeviceSynchronize(), "session init");
   if (!rc && d.world > 1) {
     // set up NCCL's connections for both collectives of a step before any
@@ -1808,6 +1946,10 @@ int32_t unltd_qwen35_session_create(unltd_qwen35 m, int32_t ctx_len, unltd_qwen3
   }
   *out = s;
   return UNLTD_OK;
+}
+
+int32_t unltd_qwen35_session_create(unltd_qwen35 m, int32_t ctx_len, unltd_qwen35_session *out) {
+  return unltd_qwen35_session_create_batch(m, ctx_len, 1, out);
 }
 
 int32_t unltd_qwen35_session_destroy(unltd_qwen35_session s) {
@@ -1835,76 +1977,96 @@ std::vector<std::pair<size_t, size_t>> conv_channel_ranges(const Derived &d) {
   return r;
 }
 
-int32_t unltd_qwen35_session_set_state(unltd_qwen35_session s, int32_t position, const float *const *conv,
-                                       const float *const *gdn, const float *const *kcache,
-                                       const float *const *vcache) {
+int32_t unltd_qwen35_batch_set_state(unltd_qwen35_session s, int32_t seq, int32_t position, const float *const *conv,
+                                     const float *const *gdn, const float *const *kcache,
+                                     const float *const *vcache) {
   if (!s) return set_error(UNLTD_ERR_INVALID_ARG, "qwen35_set_state: NULL session");
+  if (seq < 0 || seq >= s->nseq) return set_error(UNLTD_ERR_INVALID_ARG, "qwen35_set_state: sequence out of range");
   if (position < 0 || position >= s->ctx_len)
     return set_error(UNLTD_ERR_LENGTH, "qwen35_set_state: position outside the context");
   const Derived &d = s->m->d;
+  auto ring = [&](int i) { return seq_buf(s, s->ring[i], seq); };
+  auto state = [&](int i) { return seq_buf(s, s->state[i], seq); };
+  auto kc = [&](int i) { return seq_buf(s, s->kc[i], seq); };
+  auto vc = [&](int i) { return seq_buf(s, s->vc[i], seq); };
   CtxGuard g(s->m->ctx->device);
   cudaStream_t st = s->ctx->stream;
   cudaError_t e = cudaStreamSynchronize(st);
   const auto chans = conv_channel_ranges(d);
   std::vector<float> row((size_t)d.dconvl);
   for (int i = 0; e == cudaSuccess && i < s->m->n_recr; i++) {
-    e = cudaMemset(s->ring[i], 0, (size_t)d.K * d.dconvl * 4);
+    e = cudaMemset(ring(i), 0, (size_t)d.K * d.dconvl * 4);
     // row tau of the window (oldest first) lives in slot (position + tau) % K
     for (int tau = 0; e == cudaSuccess && conv && conv[i] && tau < d.K - 1; tau++) {
       size_t o = 0;
       for (auto &c : chans)
         for (size_t ch = c.first; ch < c.second; ch++) row[o++] = conv[i][(size_t)tau * d.dconv + ch];
-      e = cudaMemcpy(s->ring[i] + (size_t)((position + tau) % d.K) * d.dconvl, row.data(), (size_t)d.dconvl * 4,
+      e = cudaMemcpy(ring(i) + (size_t)((position + tau) % d.K) * d.dconvl, row.data(), (size_t)d.dconvl * 4,
                      cudaMemcpyHostToDevice);
     }
     const size_t hh = (size_t)d.hd * d.hd;
     if (e == cudaSuccess) {
-      if (gdn && gdn[i]) e = cudaMemcpy(s->state[i], gdn[i] + (size_t)d.vh0 * hh, (size_t)d.nvl * hh * 4, cudaMemcpyHostToDevice);
-      else e = cudaMemset(s->state[i], 0, (size_t)d.nvl * hh * 4);
+      if (gdn && gdn[i]) e = cudaMemcpy(state(i), gdn[i] + (size_t)d.vh0 * hh, (size_t)d.nvl * hh * 4, cudaMemcpyHostToDevice);
+      else e = cudaMemset(state(i), 0, (size_t)d.nvl * hh * 4);
     }
   }
   for (int i = 0; e == cudaSuccess && i < s->m->n_attn; i++) {
     const size_t full = (size_t)s->ctx_len * d.kvlenl * 4;
-    e = cudaMemset(s->kc[i], 0, full);
-    if (e == cudaSuccess) e = cudaMemset(s->vc[i], 0, full);
+    e = cudaMemset(kc(i), 0, full);
+    if (e == cudaSuccess) e = cudaMemset(vc(i), 0, full);
     const size_t col0 = (size_t)d.kv0 * d.hdv;  // the local kv heads' columns of each full row
     if (e == cudaSuccess && position && kcache && kcache[i])
-      e = cudaMemcpy2D(s->kc[i], (size_t)d.kvlenl * 4, kcache[i] + col0, (size_t)d.kvlen * 4, (size_t)d.kvlenl * 4,
+      e = cudaMemcpy2D(kc(i), (size_t)d.kvlenl * 4, kcache[i] + col0, (size_t)d.kvlen * 4, (size_t)d.kvlenl * 4,
                        (size_t)position, cudaMemcpyHostToDevice);
     if (e == cudaSuccess && position && vcache && vcache[i])
-      e = cudaMemcpy2D(s->vc[i], (size_t)d.kvlenl * 4, vcache[i] + col0, (size_t)d.kvlen * 4, (size_t)d.kvlenl * 4,
+      e = cudaMemcpy2D(vc(i), (size_t)d.kvlenl * 4, vcache[i] + col0, (size_t)d.kvlen * 4, (size_t)d.kvlenl * 4,
                        (size_t)position, cudaMemcpyHostToDevice);
   }
-  if (e == cudaSuccess) e = cudaMemcpy(s->pos, &position, 4, cudaMemcpyHostToDevice);
+  if (e == cudaSuccess) e = cudaMemcpy(seq_buf(s, s->pos, seq), &position, 4, cudaMemcpyHostToDevice);
   if (e != cudaSuccess) return cuda_error(e, "qwen35_set_state");
-  s->host_pos = position;
+  s->seq_pos[seq] = position;
+  if (seq == 0) s->host_pos = position;
   return UNLTD_OK;
+}
+
+int32_t unltd_qwen35_session_set_state(unltd_qwen35_session s, int32_t position, const float *const *conv,
+                                       const float *const *gdn, const float *const *kcache,
+                                       const float *const *vcache) {
+  return unltd_qwen35_batch_set_state(s, 0, position, conv, gdn, kcache, vcache);
 }
 
 // Copy the session state out at the current position: per recurrent layer
 // the conv window ((K-1) x local channels, oldest row first) and the local
 // GDN matrices, per attention layer `position` rows of the local K and V
 // columns. With one GPU this is exactly the layout set_state takes.
-int32_t unltd_qwen35_session_get_state(unltd_qwen35_session s, float *const *conv, float *const *gdn,
-                                       float *const *kcache, float *const *vcache) {
+int32_t unltd_qwen35_batch_get_state(unltd_qwen35_session s, int32_t seq, float *const *conv, float *const *gdn,
+                                     float *const *kcache, float *const *vcache) {
   if (!s) return set_error(UNLTD_ERR_INVALID_ARG, "qwen35_get_state: NULL session");
+  if (seq < 0 || seq >= s->nseq) return set_error(UNLTD_ERR_INVALID_ARG, "qwen35_get_state: sequence out of range");
   const Derived &d = s->m->d;
   CtxGuard g(s->m->ctx->device);
   cudaError_t e = cudaStreamSynchronize(s->ctx->stream);
-  const int position = s->host_pos;
+  const int position = s->seq_pos[seq];
   for (int i = 0; e == cudaSuccess && i < s->m->n_recr; i++) {
+    const float *ring = seq_buf(s, s->ring[i], seq);
     for (int tau = 0; e == cudaSuccess && conv && conv[i] && tau < d.K - 1; tau++)
-      e = cudaMemcpy(conv[i] + (size_t)tau * d.dconvl, s->ring[i] + (size_t)((position + tau) % d.K) * d.dconvl,
+      e = cudaMemcpy(conv[i] + (size_t)tau * d.dconvl, ring + (size_t)((position + tau) % d.K) * d.dconvl,
                      (size_t)d.dconvl * 4, cudaMemcpyDeviceToHost);
     if (e == cudaSuccess && gdn && gdn[i])
-      e = cudaMemcpy(gdn[i], s->state[i], (size_t)d.nvl * d.hd * d.hd * 4, cudaMemcpyDeviceToHost);
+      e = cudaMemcpy(gdn[i], seq_buf(s, s->state[i], seq), (size_t)d.nvl * d.hd * d.hd * 4, cudaMemcpyDeviceToHost);
   }
   for (int i = 0; e == cudaSuccess && i < s->m->n_attn; i++) {
     const size_t part = (size_t)position * d.kvlenl * 4;
-    if (part && kcache && kcache[i]) e = cudaMemcpy(kcache[i], s->kc[i], part, cudaMemcpyDeviceToHost);
-    if (e == cudaSuccess && part && vcache && vcache[i]) e = cudaMemcpy(vcache[i], s->vc[i], part, cudaMemcpyDeviceToHost);
+    if (part && kcache && kcache[i]) e = cudaMemcpy(kcache[i], seq_buf(s, s->kc[i], seq), part, cudaMemcpyDeviceToHost);
+    if (e == cudaSuccess && part && vcache && vcache[i])
+      e = cudaMemcpy(vcache[i], seq_buf(s, s->vc[i], seq), part, cudaMemcpyDeviceToHost);
   }
   return cuda_error(e, "qwen35_get_state");
+}
+
+int32_t unltd_qwen35_session_get_state(unltd_qwen35_session s, float *const *conv, float *const *gdn,
+                                       float *const *kcache, float *const *vcache) {
+  return unltd_qwen35_batch_get_state(s, 0, conv, gdn, kcache, vcache);
 }
 
 // Element counts of the rank's state pieces and its vocab rows.
@@ -1924,6 +2086,7 @@ int32_t unltd_qwen35_session_shape(unltd_qwen35_session s, int64_t *conv_row, in
 // greedy token after the last one (may be NULL).
 int32_t unltd_qwen35_feed(unltd_qwen35_session s, const uint32_t *tokens, int32_t n, uint32_t *next_token) {
   if (!s || (!tokens && n > 0)) return set_error(UNLTD_ERR_INVALID_ARG, "qwen35_feed: NULL argument");
+  if (s->nseq != 1) return set_error(UNLTD_ERR_INVALID_ARG, "qwen35_feed: a batch session (use qwen35_batch_decode)");
   if (n < 0 || n > s->ctx_len - s->host_pos)
     return set_error(UNLTD_ERR_LENGTH, "qwen35_feed: context full (" + std::to_string(s->host_pos) + " of " +
                                            std::to_string(s->ctx_len) + " positions used)");
@@ -1942,7 +2105,10 @@ int32_t unltd_qwen35_feed(unltd_qwen35_session s, const uint32_t *tokens, int32_
   }
   if (!rc && next_token && n > 0) rc = cuda_error(cudaMemcpyAsync(next_token, s->cur_token, 4, cudaMemcpyDeviceToHost, st), "qwen35_feed");
   if (!rc) rc = sync_and_check(s->ctx, st, "qwen35_feed");
-  if (!rc) s->host_pos += n;
+  if (!rc) {
+    s->host_pos += n;
+    s->seq_pos[0] = s->host_pos;
+  }
   return rc;
 }
 
@@ -1950,6 +2116,7 @@ int32_t unltd_qwen35_feed(unltd_qwen35_session s, const uint32_t *tokens, int32_
 // i-1 produced. tokens_out[i] = the greedy token of step i.
 int32_t unltd_qwen35_decode(unltd_qwen35_session s, uint32_t token, int32_t n_steps, uint32_t *tokens_out) {
   if (!s || (!tokens_out && n_steps > 0)) return set_error(UNLTD_ERR_INVALID_ARG, "qwen35_decode: NULL argument");
+  if (s->nseq != 1) return set_error(UNLTD_ERR_INVALID_ARG, "qwen35_decode: a batch session (use qwen35_batch_decode)");
   if (n_steps < 0 || n_steps > s->ctx_len - s->host_pos)
     return set_error(UNLTD_ERR_LENGTH, "qwen35_decode: context full (" + std::to_string(s->host_pos) + " of " +
                                            std::to_string(s->ctx_len) + " positions used)");
@@ -1964,7 +2131,46 @@ int32_t unltd_qwen35_decode(unltd_qwen35_session s, uint32_t token, int32_t n_st
   if (!rc && n_steps > 0)
     rc = cuda_error(cudaMemcpyAsync(tokens_out, s->hist, (size_t)n_steps * 4, cudaMemcpyDeviceToHost, st), "qwen35_decode");
   if (!rc) rc = sync_and_check(s->ctx, st, "qwen35_decode");
-  if (!rc) s->host_pos += n_steps;
+  if (!rc) {
+    s->host_pos += n_steps;
+    s->seq_pos[0] = s->host_pos;
+  }
+  return rc;
+}
+
+// Greedy decode of every sequence of a batch session: step 0 of sequence z
+// consumes tokens[z]; tokens_out[z * n_steps + i] = its greedy token of step i.
+int32_t unltd_qwen35_batch_decode(unltd_qwen35_session s, const uint32_t *tokens, int32_t n_steps,
+                                  uint32_t *tokens_out) {
+  if (!s || !tokens || (!tokens_out && n_steps > 0))
+    return set_error(UNLTD_ERR_INVALID_ARG, "qwen35_batch_decode: NULL argument");
+  int maxpos = 0;
+  for (int z = 0; z < s->nseq; z++) maxpos = std::max(maxpos, s->seq_pos[z]);
+  if (n_steps < 0 || n_steps > s->ctx_len - maxpos)
+    return set_error(UNLTD_ERR_LENGTH, "qwen35_batch_decode: context full (" + std::to_string(maxpos) + " of " +
+                                           std::to_string(s->ctx_len) + " positions used)");
+  for (int z = 0; z < s->nseq; z++)
+    if (tokens[z] >= (uint32_t)s->m->d.vocab)
+      return set_error(UNLTD_ERR_INVALID_ARG, "qwen35_batch_decode: token " + std::to_string(tokens[z]) +
+                                                  " outside the vocab");
+  CtxGuard g(s->m->ctx->device);
+  cudaStream_t st = s->ctx->stream;
+  cudaError_t e = cudaSuccess;
+  for (int z = 0; e == cudaSuccess && z < s->nseq; z++) {
+    e = cudaMemcpyAsync(seq_buf(s, s->cur_token, z), tokens + z, 4, cudaMemcpyHostToDevice, st);
+    if (e == cudaSuccess) e = cudaMemsetAsync(seq_buf(s, s->counter, z), 0, 4, st);
+  }
+  int32_t rc = cuda_error(e, "qwen35_batch_decode");
+  for (int i = 0; !rc && i < n_steps; i++) rc = run_step(s);
+  for (int z = 0; !rc && n_steps > 0 && z < s->nseq; z++)
+    rc = cuda_error(cudaMemcpyAsync(tokens_out + (size_t)z * n_steps, seq_buf(s, s->hist, z), (size_t)n_steps * 4,
+                                    cudaMemcpyDeviceToHost, st),
+                    "qwen35_batch_decode");
+  if (!rc) rc = sync_and_check(s->ctx, st, "qwen35_batch_decode");
+  if (!rc) {
+    for (int z = 0; z < s->nseq; z++) s->seq_pos[z] += n_steps;
+    s->host_pos = s->seq_pos[0];
+  }
   return rc;
 }
 
@@ -1978,15 +2184,28 @@ int32_t unltd_qwen35_session_info(unltd_qwen35_session s, int32_t *position, voi
 
 // Copy the last step's logits (vocab floats) and/or hidden state (l_out of
 // the last layer, n_embd floats) to host buffers (NULL skips).
-int32_t unltd_qwen35_session_read(unltd_qwen35_session s, float *logits, float *hidden) {
+int32_t unltd_qwen35_batch_read(unltd_qwen35_session s, int32_t seq, float *logits, float *hidden) {
   if (!s) return set_error(UNLTD_ERR_INVALID_ARG, "qwen35_session_read: NULL session");
+  if (seq < 0 || seq >= s->nseq) return set_error(UNLTD_ERR_INVALID_ARG, "qwen35_session_read: sequence out of range");
   CtxGuard g(s->m->ctx->device);
   cudaStream_t st = s->ctx->stream;
   cudaError_t e = cudaStreamSynchronize(st);
   if (e == cudaSuccess && logits)
-    e = cudaMemcpy(logits, s->logits, (size_t)(s->m->d.v1 - s->m->d.v0) * 4, cudaMemcpyDeviceToHost);
-  if (e == cudaSuccess && hidden) e = cudaMemcpy(hidden, s->X, (size_t)s->m->d.n * 4, cudaMemcpyDeviceToHost);
+    e = cudaMemcpy(logits, seq_buf(s, s->logits, seq), (size_t)(s->m->d.v1 - s->m->d.v0) * 4, cudaMemcpyDeviceToHost);
+  if (e == cudaSuccess && hidden)
+    e = cudaMemcpy(hidden, seq_buf(s, s->X, seq), (size_t)s->m->d.n * 4, cudaMemcpyDeviceToHost);
   return cuda_error(e, "qwen35_session_read");
+}
+
+int32_t unltd_qwen35_session_read(unltd_qwen35_session s, float *logits, float *hidden) {
+  return unltd_qwen35_batch_read(s, 0, logits, hidden);
+}
+
+int32_t unltd_qwen35_batch_info(unltd_qwen35_session s, int32_t *n_seq, int32_t *positions) {
+  if (!s) return set_error(UNLTD_ERR_INVALID_ARG, "qwen35_batch_info: NULL session");
+  if (n_seq) *n_seq = s->nseq;
+  for (int z = 0; positions && z < s->nseq; z++) positions[z] = s->seq_pos[z];
+  return UNLTD_OK;
 }
 
 }  // extern "C"

@@ -24,6 +24,11 @@ struct unltd_ctx_s {
   // Argmax reduction state: a 64-bit key and a CTA-completion counter.
   unsigned long long *argmax_key = nullptr;
   unsigned int *argmax_done = nullptr;
+  // Per-sequence argmax state of the batched GEMV (kMaxBatch keys, a counter,
+  // kMaxBatch tokens), inside the same allocation as argmax_key.
+  unsigned long long *bkey = nullptr;
+  unsigned int *bdone = nullptr;
+  uint32_t *btok = nullptr;
   // Device error word: kernels write a nonzero code on a bounded-wait timeout.
   int *err = nullptr;
   // Pinned host copy of the error word: read back with the call's own results
@@ -132,6 +137,29 @@ struct GemvArgs {
   bool peer_send = false;
 };
 int32_t gemv_launch(unltd_ctx ctx, const GemvArgs &a);
+
+// gemv_batch.cu: y_s = W . x_s for nseq sequences (Q8K_EXACT, Q4_K / Q6_K),
+// each y_s the bits of gemv_launch's on x_s alone.
+constexpr int kMaxBatch = 32;
+struct BatchGemvArgs {
+  const unltd_weight_s *w;
+  const float *x = nullptr;     // [nseq][xstride] f32 (null: img is given)
+  size_t xstride = 0;
+  const uint8_t *img = nullptr;  // non-null: the x images, sequence s at img + s * istride
+  size_t istride = 0;
+  float *y = nullptr;           // [nseq][ystride] (may be null with argmax)
+  size_t ystride = 0;
+  int nseq = 1;
+  unsigned long long *key = nullptr;  // non-null: fused argmax, one key per sequence
+  unsigned *done = nullptr;
+  uint32_t *token = nullptr;
+  size_t tstride = 1;                 // token of sequence s at token[s * tstride]
+};
+int32_t gemv_batch_launch(unltd_ctx ctx, const BatchGemvArgs &a);
+// Bytes of one sequence's x image for w (the stride of the batched images).
+size_t gemv_batch_img_bytes(const unltd_weight_s &w);
+bool gemv_batch_supported(int device, const unltd_weight_s &w);
+cudaError_t gemv_batch_prewarm(int device);
 // True when gemv_launch can fuse an RMSNorm of length w.dim_in into w's GEMV.
 bool gemv_norm_fusable(unltd_ctx ctx, const unltd_weight_s &w, int mode);
 // True when w's GEMV runs on the tensor-core kernel (peer row-split sums).

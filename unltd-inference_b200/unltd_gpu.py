@@ -49,6 +49,8 @@ SIGNATURES = [
     ("unltd_gemv", _I, [_P, _P, _P, _P, _I]),
     ("unltd_gemv_argmax", _I, [_P, _P, _P, _P, _P, _I]),
     ("unltd_gemv_argmax_shard", _I, [_P, _P, _P, _P, _P, ctypes.c_uint32, _I]),
+    ("unltd_gemv_batch", _I, [_P, _P, _P, _P, _I, _I]),
+    ("unltd_gemv_argmax_batch", _I, [_P, _P, _P, _P, _P, _I, _I]),
     ("unltd_dequant", _I, [_P, _P, _P]),
     ("unltd_gemv_noalloc", _I, [_P, _P, _P, _I, _P]),
     ("unltd_gemm", _I, [_P, _P, _P, _P, _S]),
@@ -91,6 +93,12 @@ SIGNATURES = [
     ("unltd_qwen35_decode", _I, [_P, ctypes.c_uint32, _I, _P]),
     ("unltd_qwen35_session_info", _I, [_P, ctypes.POINTER(_I), ctypes.POINTER(_P), ctypes.POINTER(_I64)]),
     ("unltd_qwen35_session_read", _I, [_P, _P, _P]),
+    ("unltd_qwen35_session_create_batch", _I, [_P, _I, _I, ctypes.POINTER(_P)]),
+    ("unltd_qwen35_batch_set_state", _I, [_P, _I, _I, _P, _P, _P, _P]),
+    ("unltd_qwen35_batch_get_state", _I, [_P, _I, _P, _P, _P, _P]),
+    ("unltd_qwen35_batch_read", _I, [_P, _I, _P, _P]),
+    ("unltd_qwen35_batch_decode", _I, [_P, _P, _I, _P]),
+    ("unltd_qwen35_batch_info", _I, [_P, ctypes.POINTER(_I), _P]),
 ]
 
 
@@ -228,6 +236,15 @@ class Context:
         whole vocabulary's first-index maximum."""
         _check(lib().unltd_gemv_argmax_shard(self.h, w.h, _ptr(x), _ptr(logits) if logits is not None else None,
                                              _ptr(key), row0, mode))
+
+    def gemv_batch(self, w: "Weight", X, Y, n_seq: int, mode: int = MODE_Q8K):
+        """Y[s] = W . X[s] for n_seq sequences (Q8K_EXACT): each row of Y the
+        bits of gemv(w, X[s], Y[s], MODE_Q8K)."""
+        _check(lib().unltd_gemv_batch(self.h, w.h, _ptr(X), _ptr(Y), n_seq, mode))
+
+    def gemv_argmax_batch(self, w: "Weight", X, tokens, n_seq: int, logits=None, mode: int = MODE_Q8K):
+        _check(lib().unltd_gemv_argmax_batch(self.h, w.h, _ptr(X), _ptr(logits) if logits is not None else None,
+                                             _ptr(tokens), n_seq, mode))
 
     def gemm(self, w: "Weight", X, Y, m_tokens: int, accurate: bool = False):
         """Y[m][n] = sum_k X[m][k] W[n][k] on the tensor cores, f32 accumulate:
@@ -476,6 +493,12 @@ class Qwen35Model:
         _check(lib().unltd_qwen35_session_create(self.h, ctx_len, ctypes.byref(h)))
         return Qwen35Session(self, h, ctx_len)
 
+    def batch_session(self, ctx_len: int, n_seq: int) -> "Qwen35BatchSession":
+        """n_seq sequences decoded together (unltd_qwen35_session_create_batch)."""
+        h = ctypes.c_void_p()
+        _check(lib().unltd_qwen35_session_create_batch(self.h, ctx_len, n_seq, ctypes.byref(h)))
+        return Qwen35BatchSession(self, h, ctx_len, n_seq)
+
     def close(self):
         if _alive(self):
             for o in list(_live[0]):  # its sessions first
@@ -572,3 +595,53 @@ class Qwen35Session:
                 self.close()
         except Exception:
             pass
+
+
+class Qwen35BatchSession(Qwen35Session):
+    """A batch session: every call names its sequence; decode steps all."""
+
+    def __init__(self, model: Qwen35Model, h, ctx_len: int, n_seq: int):
+        super().__init__(model, h, ctx_len)
+        self.n_seq = n_seq
+
+    def set_state(self, seq: int, position: int, conv=None, gdn=None, kcache=None, vcache=None):
+        ptrs = [_ptr_array(a) for a in (conv, gdn, kcache, vcache)]
+        _check(lib().unltd_qwen35_batch_set_state(self.h, seq, position, *[p[0] for p in ptrs]))
+
+    def positions(self) -> list:
+        n = _I()
+        pos = np.zeros(self.n_seq, np.int32)
+        _check(lib().unltd_qwen35_batch_info(self.h, ctypes.byref(n), pos.ctypes.data))
+        return pos.tolist()
+
+    def get_state(self, seq: int) -> dict:
+        cfg = self.model.cfg
+        hd = cfg["d_inner"] // (2 * cfg["group_count"])
+        sh = self.shape()
+        nv, dconv, kvlen = sh["gdn_heads"], sh["conv_row"], sh["kv_row"]
+        attn = [(il + 1) % cfg["full_attn_interval"] == 0 for il in range(cfg["n_layer"])]
+        pos = self.positions()[seq]
+        st = {"conv": [np.zeros((cfg["conv_kernel"] - 1, dconv), np.float32) for a in attn if not a],
+              "gdn": [np.zeros((nv, hd, hd), np.float32) for a in attn if not a],
+              "k": [np.zeros((pos, kvlen), np.float32) for a in attn if a],
+              "v": [np.zeros((pos, kvlen), np.float32) for a in attn if a]}
+        ptrs = [_ptr_array(st[k]) for k in ("conv", "gdn", "k", "v")]
+        _check(lib().unltd_qwen35_batch_get_state(self.h, seq, *[p[0] for p in ptrs]))
+        return st
+
+    def decode(self, tokens, n_steps: int) -> np.ndarray:
+        """tokens: the first token of every sequence; returns [n_seq][n_steps]."""
+        t = np.ascontiguousarray(tokens, dtype=np.uint32)
+        assert t.size == self.n_seq
+        out = np.zeros((self.n_seq, n_steps), np.uint32)
+        _check(lib().unltd_qwen35_batch_decode(self.h, t.ctypes.data, n_steps, out.ctypes.data))
+        return out
+
+    def read(self, seq: int, logits: bool = True, hidden: bool = True):
+        cfg = self.model.cfg
+        v0, v1 = self.shape()["vocab"]
+        lg = np.empty(v1 - v0, np.float32) if logits else None
+        hd = np.empty(cfg["n_embd"], np.float32) if hidden else None
+        _check(lib().unltd_qwen35_batch_read(self.h, seq, None if lg is None else lg.ctypes.data,
+                                             None if hd is None else hd.ctypes.data))
+        return lg, hd
