@@ -79,6 +79,10 @@ extern "C" {
                   mode: i32) -> i32;
     fn unltd_gemv_argmax(ctx: *mut CtxOpaque, w: *mut WeightOpaque, x_dev: *const f32, logits_dev: *mut f32,
                          token_dev: *mut u32, mode: i32) -> i32;
+    fn unltd_gemv_batch(ctx: *mut CtxOpaque, w: *mut WeightOpaque, x_dev: *const f32, y_dev: *mut f32,
+                        n_seq: i32, mode: i32) -> i32;
+    fn unltd_gemv_argmax_batch(ctx: *mut CtxOpaque, w: *mut WeightOpaque, x_dev: *const f32, logits_dev: *mut f32,
+                               tokens_dev: *mut u32, n_seq: i32, mode: i32) -> i32;
     fn unltd_gemm(ctx: *mut CtxOpaque, w: *mut WeightOpaque, x_dev: *const f32, y_dev: *mut f32,
                   m_tokens: usize) -> i32;
     fn unltd_dequant(ctx: *mut CtxOpaque, w: *mut WeightOpaque, out_dev: *mut f32) -> i32;
@@ -228,6 +232,28 @@ impl Context {
     pub unsafe fn gemv_argmax(&self, w: &Weight<'_>, x_dev: *const f32, logits_dev: *mut f32, token_dev: *mut u32,
                               mode: Mode) -> Result<(), Error> {
         status(unltd_gemv_argmax(self.h, w.h, x_dev, logits_dev, token_dev, mode as i32))
+    }
+
+    /// Batch decode: `Y[s] = W . X[s]` for `n_seq` (1..32) sequences sharing
+    /// W, each row the bits of [`Context::gemv`] in Q8K_EXACT mode on `X[s]`
+    /// alone (gemv_quant_q8k per sequence, quants.rs:474-515).
+    ///
+    /// # Safety
+    /// Device pointers of this context's device: X n_seq x dim_in f32,
+    /// Y n_seq x dim_out f32.
+    pub unsafe fn gemv_batch(&self, w: &Weight<'_>, x_dev: *const f32, y_dev: *mut f32, n_seq: i32)
+                             -> Result<(), Error> {
+        status(unltd_gemv_batch(self.h, w.h, x_dev, y_dev, n_seq, Mode::Q8kExact as i32))
+    }
+
+    /// The LM head of a batch: every sequence's logits (or null) and greedy token.
+    ///
+    /// # Safety
+    /// Device pointers of this context's device: X n_seq x dim_in f32, logits
+    /// n_seq x dim_out f32 (or null), tokens n_seq u32.
+    pub unsafe fn gemv_argmax_batch(&self, w: &Weight<'_>, x_dev: *const f32, logits_dev: *mut f32,
+                                    tokens_dev: *mut u32, n_seq: i32) -> Result<(), Error> {
+        status(unltd_gemv_argmax_batch(self.h, w.h, x_dev, logits_dev, tokens_dev, n_seq, Mode::Q8kExact as i32))
     }
 
     /// Batched prefill `Y = X . W^T` over `m_tokens` rows of X.

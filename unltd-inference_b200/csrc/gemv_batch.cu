@@ -73,9 +73,30 @@ struct Q4Chain {
   float m[4];     // sumf (min term), same order
 };
 
+// This lane's x operands of one block (from global memory): the B words of
+// sequence gid for the eight classes, its min-term words, and the d of the
+// two sequences of its D columns. Loaded one block ahead of their use.
+struct Q4X {
+  uint2 bx[8];
+  uint32_t bml, bmh;
+  float xd0, xd1;
+};
+
+__device__ __forceinline__ void q4x_load(const uint8_t *xg, bool xv, const uint8_t *xs0, bool v0, const uint8_t *xs1,
+                                         bool v1, Q4X &x) {
+  const int tig = threadIdx.x & 3;
+  const uint8_t *xw = xg + 128 * (tig >> 1) + 8 * (tig & 1);
+#pragma unroll
+  for (int k = 0; k < 8; k++) x.bx[k] = xv ? ldg64(xw + 16 * k) : make_uint2(0u, 0u);
+  const bool bmv = xv && tig < 2;
+  x.bml = bmv ? ldg32(xg + kImgQ8K4_BM + 4 * tig) : 0u;
+  x.bmh = bmv ? ldg32(xg + kImgQ8K4_BM + 4 * (2 + tig)) : 0u;
+  x.xd0 = v0 ? ldgf(xs0 + kImgQ8K4_D) : 0.0f;
+  x.xd1 = v1 ? ldgf(xs1 + kImgQ8K4_D) : 0.0f;
+}
+
 __device__ __forceinline__ void q4k_batch_block(const uint8_t *row0, const uint8_t *row1, int nbc, int b,
-                                                const uint8_t *xg, bool xv, const uint8_t *xs0, bool v0,
-                                                const uint8_t *xs1, bool v1, Q4Chain &c) {
+                                                const Q4X &x, Q4Chain &c) {
   const int lane = threadIdx.x & 31, tig = lane & 3;
   const uint4 h0 = lds128(row0 + b * 16), h1 = lds128(row1 + b * 16);
   const uint8_t *q0p = row0 + nbc * 16 + b * 128 + 32 * tig, *q1p = row1 + nbc * 16 + b * 128 + 32 * tig;
@@ -92,7 +113,7 @@ __device__ __forceinline__ void q4k_batch_block(const uint8_t *row0, const uint8
   const uint32_t l00 = s00 & 7, l01 = s01 & 7, l10 = s10 & 7, l11 = s11 & 7;
   const uint32_t g00 = s00 >> 3, g01 = s01 >> 3, g10 = s10 >> 3, g11 = s11 >> 3;
   // the sequences' d and the block's f16 d / dmin
-  const float xd0 = v0 ? ldgf(xs0 + kImgQ8K4_D) : 0.0f, xd1 = v1 ? ldgf(xs1 + kImgQ8K4_D) : 0.0f;
+  const float xd0 = x.xd0, xd1 = x.xd1;
   const float df0 = h2f_bits(h0.x & 0xFFFFu), df1 = h2f_bits(h1.x & 0xFFFFu);
   const float dm0 = h2f_bits(h0.x >> 16), dm1 = h2f_bits(h1.x >> 16);
   const float d[4] = {__fmul_rn(xd0, df0), __fmul_rn(xd1, df0), __fmul_rn(xd0, df1), __fmul_rn(xd1, df1)};
@@ -101,20 +122,16 @@ __device__ __forceinline__ void q4k_batch_block(const uint8_t *row0, const uint8
   const uint32_t MA0 = h0.z & 0x3F3F3F3Fu, MB0 = ((h0.w >> 4) & 0x0F0F0F0Fu) | ((h0.z >> 2) & 0x30303030u);
   const uint32_t MA1 = h1.z & 0x3F3F3F3Fu, MB1 = ((h1.w >> 4) & 0x0F0F0F0Fu) | ((h1.z >> 2) & 0x30303030u);
   const uint32_t am0 = tig == 0 ? MA0 : (tig == 1 ? MB0 : 0u), am1 = tig == 0 ? MA1 : (tig == 1 ? MB1 : 0u);
-  const bool bmv = xv && tig < 2;
-  const uint32_t bml = bmv ? ldg32(xg + kImgQ8K4_BM + 4 * tig) : 0u;
-  const uint32_t bmh = bmv ? ldg32(xg + kImgQ8K4_BM + 4 * (2 + tig)) : 0u;
   int ml[4], mh[4];
-  mma_s8_k16(am0, am1, bml, ml[0], ml[1], ml[2], ml[3]);
-  mma_s8_k16(am0, am1, bmh, mh[0], mh[1], mh[2], mh[3]);
+  mma_s8_k16(am0, am1, x.bml, ml[0], ml[1], ml[2], ml[3]);
+  mma_s8_k16(am0, am1, x.bmh, mh[0], mh[1], mh[2], mh[3]);
   const float dmv[4] = {__fmul_rn(dm0, xd0), __fmul_rn(dm0, xd1), __fmul_rn(dm1, xd0), __fmul_rn(dm1, xd1)};
 #pragma unroll
   for (int i = 0; i < 4; i++) c.m[i] = __fsub_rn(c.m[i], __fmul_rn(dmv[i], (float)(ml[i] + 256 * mh[i])));
   // x words of sequence gid: class k, groups 2 tig and 2 tig + 1
-  const uint8_t *xw = xg + 128 * (tig >> 1) + 8 * (tig & 1);
 #pragma unroll
   for (int k = 0; k < 8; k++) {
-    const uint2 bx = xv ? ldg64(xw + 16 * k) : make_uint2(0u, 0u);
+    const uint2 bx = x.bx[k];
     const uint32_t n0l = w0[k] & 0x0F0F0F0Fu, n0h = (w0[k] >> 4) & 0x0F0F0F0Fu;
     const uint32_t n1l = w1[k] & 0x0F0F0F0Fu, n1h = (w1[k] >> 4) & 0x0F0F0F0Fu;
     int L[4], H[4];
@@ -166,9 +183,7 @@ __device__ __forceinline__ void q6k_batch_frag(const uint8_t *row0, const uint8_
 
 // One sequence's products of the block: the chains of (row gid, classes 2 tig,
 // 2 tig + 1) and (row gid + 8, the same classes).
-__device__ __forceinline__ void q6k_batch_seq(const Q6Frag &f, const uint8_t *xim, float (&s)[4]) {
-  XBlock6 x;
-  load_xblock6(xim, x);
+__device__ __forceinline__ void q6k_batch_seq(const Q6Frag &f, const XBlock6 &x, float (&s)[4]) {
   int acc0 = 0, acc1 = 0, acc2 = 0, acc3 = 0;
 #pragma unroll
   for (int j = 0; j < 8; j++) {
@@ -259,6 +274,9 @@ __global__ void __launch_bounds__(kBatchThreads, 1) gemv_batch_kernel(BParams P)
     const uint8_t *im0 = P.img + (size_t)(v0 ? sa : 0) * P.istride;
     const uint8_t *im1 = P.img + (size_t)(v1 ? sb2 : 0) * P.istride;
     Q4Chain ch;
+    // x of block 0 (Q4_K rows are never chunked: every unit runs blocks 0 .. nbc-1)
+    Q4X xc;
+    q4x_load(imx, xv, im0, v0, im1, v1, xc);
     for (int u = 0; u < nunits; u++) {
       const int st = u % S, c = u % P.nch;
       if (!mbar_wait_bounded(&full[st], (u / S) & 1, P.err)) break;
@@ -275,8 +293,12 @@ __global__ void __launch_bounds__(kBatchThreads, 1) gemv_batch_kernel(BParams P)
         const uint8_t *row0 = tile + (16 * g + gid) * P.ps, *row1 = row0 + 8 * P.ps;
 #pragma unroll 1
         for (int b = 0; b < nbc; b++) {
-          const size_t xo = (size_t)(c * nbc + b) * kImgQ8K4;
-          q4k_batch_block(row0, row1, nbc, b, imx + xo, xv, im0 + xo, v0, im1 + xo, v1, ch);
+          // the next block's x (block 0 again after the last: the next tile's first)
+          const size_t xo = (size_t)(b + 1 < nbc ? b + 1 : 0) * kImgQ8K4;
+          Q4X xn;
+          q4x_load(imx + xo, xv, im0 + xo, v0, im1 + xo, v1, xn);
+          q4k_batch_block(row0, row1, nbc, b, xc, ch);
+          xc = xn;
         }
         if (c == P.nch - 1) {
           const int r0 = rb + (u / P.nch) * T + 16 * g + gid;
@@ -307,15 +329,27 @@ __global__ void __launch_bounds__(kBatchThreads, 1) gemv_batch_kernel(BParams P)
         }
         const uint8_t *tile = stages + (size_t)st * P.stage_bytes;
         const uint8_t *row0 = tile + (16 * g + gid) * P.ps, *row1 = row0 + 8 * P.ps;
+        // sequence q's x of block b, loaded one (block, sequence) step ahead
+        const int nvq = min(SB, P.nseq - sg * SB);  // this group's sequences (warp-uniform)
+        auto xim = [&](int b, int q) {
+          return P.img + (size_t)(sg * SB + q) * P.istride + (size_t)(c * nbc + b) * kImgQ8K6;
+        };
+        XBlock6 xc;
+        load_xblock6(xim(0, 0), xc);
 #pragma unroll 1
         for (int b = 0; b < nbc; b++) {
           Q6Frag f;
           q6k_batch_frag(row0, row1, nbc, b, f);
-          const size_t xo = (size_t)(c * nbc + b) * kImgQ8K6;
 #pragma unroll
           for (int q = 0; q < SB; q++) {
-            const int seq = sg * SB + q;  // warp-uniform
-            if (seq < P.nseq) q6k_batch_seq(f, P.img + (size_t)seq * P.istride + xo, ch[q]);
+            if (q < nvq) {
+              const bool lastq = q + 1 >= nvq;
+              const int bn = lastq ? b + 1 : b, qn = lastq ? 0 : q + 1;
+              XBlock6 xn = xc;
+              if (bn < nbc) load_xblock6(xim(bn, qn), xn);
+              q6k_batch_seq(f, xc, ch[q]);
+              xc = xn;
+            }
           }
         }
         if (c == P.nch - 1) {
