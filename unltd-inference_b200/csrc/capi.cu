@@ -234,6 +234,7 @@ int32_t unltd_weight_free(unltd_weight w) {
   CtxGuard g(w->ctx->device);
   cudaStreamSynchronize(w->ctx->stream);
   cudaFree(w->dev);
+  if (w->dev_b) cudaFree(w->dev_b);
   delete w;
   return UNLTD_OK;
 }
@@ -332,6 +333,7 @@ int32_t unltd_gemv_batch(unltd_ctx c, unltd_weight w, const float *x, float *y, 
   if (rc) return rc;
   CtxGuard g(c->device);
   if ((rc = reserve_batch(c, w, n_seq))) return rc;
+  if ((rc = gemv_batch_prepare(c, w))) return rc;
   BatchGemvArgs a{w};
   a.x = x;
   a.xstride = w->dim_in;
@@ -350,6 +352,7 @@ int32_t unltd_gemv_argmax_batch(unltd_ctx c, unltd_weight w, const float *x, flo
   if (rc) return rc;
   CtxGuard g(c->device);
   if ((rc = reserve_batch(c, w, n_seq))) return rc;
+  if ((rc = gemv_batch_prepare(c, w))) return rc;
   BatchGemvArgs a{w};
   a.x = x;
   a.xstride = w->dim_in;

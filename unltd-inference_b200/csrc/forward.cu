@@ -1337,7 +1337,7 @@ int32_t dalloc(std::vector<void *> &bufs, T **p, size_t n, const char *what) {
 int64_t launch_gemv_img(unltd_qwen35_session s, const unltd_weight_s *w, float *y, int32_t *rc, bool send = false) {
   if (s->nseq > 1) {  // every sequence's GEMV in one pass over w
     BatchGemvArgs b{w};
-    b.img = w->dtype == Q4K ? s->img4 : s->img6;
+    b.img = s->img4;  // the batched GEMV reads the class-major (Q4_K) image for both formats
     b.istride = s->ss;
     b.y = y;
     b.ystride = s->ss / 4;
@@ -1399,8 +1399,12 @@ int32_t enqueue_step(unltd_qwen35_session s) {
   };
   const bool batch = s->nseq > 1;
   const unsigned nz = (unsigned)s->nseq;
+  // the images a producer writes for its consumers: in a batch session the
+  // class-major (Q4_K) image only, which the batched GEMV reads for Q6_K too
+  auto im4 = [&](bool q4) { return batch || q4 ? s->img4 : nullptr; };
+  auto im6 = [&](bool q6) { return !batch && q6 ? s->img6 : nullptr; };
   auto norm = [&](const float *a, const float *b, float *r_out, const float *w, bool q4, bool q6, bool argmax) {
-    NormArgs p{a, b, r_out, w, d.n, d.eps, q4 ? s->img4 : nullptr, q6 ? s->img6 : nullptr,
+    NormArgs p{a, b, r_out, w, d.n, d.eps, im4(q4), im6(q6),
                argmax && !batch ? s->ctx->argmax_key : nullptr, argmax && !batch ? s->ctx->argmax_done : nullptr};
     p.ss = s->ss;
     chk(launch_pdl(norm_quant_kernel, dim3(d.n / 256, 1, nz), dim3(256), 0, st, p), "norm");
@@ -1478,8 +1482,8 @@ int32_t enqueue_step(unltd_qwen35_session s) {
       a.alpha_off = a.beta_off + d.nvl;
       a.eps = d.eps;
       a.span_ctr = s->span_ctr;
-      a.img4 = L.out->dtype == Q4K ? s->img4 : nullptr;
-      a.img6 = L.out->dtype == Q6K ? s->img6 : nullptr;
+      a.img4 = im4(L.out->dtype == Q4K);
+      a.img6 = im6(L.out->dtype == Q6K);
       a.ss = s->ss;
       const dim3 rg(d.nvl, 128 / kGdnCols, nz);
       if (d.K == 4) chk(launch_pdl(recr_mid_kernel<128, 4>, rg, dim3(128), 0, st, a), "recr_mid");
@@ -1498,8 +1502,8 @@ int32_t enqueue_step(unltd_qwen35_session s) {
       a.vcache = s->vc[L.slot];
       a.scores = s->scores;
       a.part = s->part;
-      a.img4 = L.out->dtype == Q4K ? s->img4 : nullptr;
-      a.img6 = L.out->dtype == Q6K ? s->img6 : nullptr;
+      a.img4 = im4(L.out->dtype == Q4K);
+      a.img6 = im6(L.out->dtype == Q6K);
       a.pos = s->pos;
       a.nh = d.nhl;
       a.nkv = d.nkvl;
@@ -1533,8 +1537,7 @@ int32_t enqueue_step(unltd_qwen35_session s) {
     // residual = x_in + attn_out; rmsnorm(residual, post_attention_norm) -> gate|up image
     norm_proj(s->X, s->T, s->R, L.post_norm, L.gate_up, s->FF, out_send);
     chk(launch_pdl(swiglu_quant_kernel, dim3(d.nffl / 256, 1, nz), dim3(256), 0, st, (const float *)s->FF,
-                   (const float *)(s->FF + d.nffl), L.down->dtype == Q4K ? s->img4 : (uint8_t *)nullptr,
-                   L.down->dtype == Q6K ? s->img6 : (uint8_t *)nullptr, s->ss),
+                   (const float *)(s->FF + d.nffl), im4(L.down->dtype == Q4K), im6(L.down->dtype == Q6K), s->ss),
         "swiglu");
     nl += launch_gemv_img(s, L.down, s->F, &rc, down_send);
     if (!down_send) allreduce(s->F, d.n);
@@ -1544,7 +1547,7 @@ int32_t enqueue_step(unltd_qwen35_session s) {
   norm(s->R, s->F, s->X, m->out_norm, m->output->dtype == Q4K, m->output->dtype == Q6K, true);
   if (batch) {
     BatchGemvArgs b{m->output};
-    b.img = m->output->dtype == Q4K ? s->img4 : s->img6;
+    b.img = s->img4;
     b.istride = s->ss;
     b.y = s->logits;
     b.ystride = s->ss / 4;
@@ -1930,6 +1933,17 @@ int32_t unltd_qwen35_session_create_batch(unltd_qwen35 m, int32_t ctx_len, int32
     rc = cuda_error(e, "attention smem");
   }
   if (!rc && n_seq > 1) rc = cuda_error(gemv_batch_prewarm(m->ctx->device), "batched GEMV attributes");
+  if (!rc && n_seq > 1) {  // the batched GEMV's operands of the Q6_K projections
+    std::vector<unltd_weight_s *> ws{m->output};
+    for (const Layer &L : m->layers) {
+      ws.insert(ws.end(), L.in.w.begin(), L.in.w.end());
+      ws.insert(ws.end(), L.gate_up.w.begin(), L.gate_up.w.end());
+      ws.push_back(L.out);
+      ws.push_back(L.down);
+    }
+    for (auto *w : ws)
+      if (!rc) rc = gemv_batch_prepare(m->ctx, w);
+  }
   if (!rc) rc = cuda_error(cudaDeviceSynchronize(), "session init");
   if (!rc && d.world > 1) {
     // set up NCCL's connections for both collectives of a step before any

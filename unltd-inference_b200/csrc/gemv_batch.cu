@@ -82,13 +82,14 @@ struct Q4X {
   float xd0, xd1;
 };
 
+template <bool MIN>
 __device__ __forceinline__ void q4x_load(const uint8_t *xg, bool xv, const uint8_t *xs0, bool v0, const uint8_t *xs1,
                                          bool v1, Q4X &x) {
   const int tig = threadIdx.x & 3;
   const uint8_t *xw = xg + 128 * (tig >> 1) + 8 * (tig & 1);
 #pragma unroll
   for (int k = 0; k < 8; k++) x.bx[k] = xv ? ldg64(xw + 16 * k) : make_uint2(0u, 0u);
-  const bool bmv = xv && tig < 2;
+  const bool bmv = MIN && xv && tig < 2;
   x.bml = bmv ? ldg32(xg + kImgQ8K4_BM + 4 * tig) : 0u;
   x.bmh = bmv ? ldg32(xg + kImgQ8K4_BM + 4 * (2 + tig)) : 0u;
   x.xd0 = v0 ? ldgf(xs0 + kImgQ8K4_D) : 0.0f;
@@ -142,64 +143,76 @@ __device__ __forceinline__ void q4k_batch_block(const uint8_t *row0, const uint8
   }
 }
 
-// ---- Q6_K: 16 rows, one sequence at a time ---------------------------------
-// The A operands (4 (raw6 - 32) as s8) and the sub-block scales of the block
-// for rows gid, gid + 8, built once and kept in registers.
-struct Q6Frag {
-  uint32_t alo0[8], ahi0[8], alo1[8], ahi1[8];
-  int s0[8], t0[8], s1[8], t1[8];
-  float df0, df1;
-};
+// ---- Q6_K: 16 rows x 8 sequences, one block, from the digit planes -------
+// Per block kBatch6Block bytes: plane w0 (256 B), plane w1 (256 B), f16 d.
+// v = sc * (q - 32) = 128 w1 + w0 (w0 in [0, 127], w1 in [-32, 32]), so
+// sumi[k] = D0 + 128 D1 exactly with D_p = sum over class k of w_p * q8. In
+// a plane, class pair j, lane tig's 16 bytes at 64 j + 16 tig hold classes
+// 2j and 2j + 1, each as the words of groups 2 tig and 2 tig + 1 (byte i of
+// a word: element 32 g + 8 i + k), the K order of the Q4_K x image.
+constexpr int kBatch6Block = 528;
 
-__device__ __forceinline__ void q6k_batch_frag(const uint8_t *row0, const uint8_t *row1, int nbc, int b, Q6Frag &f) {
-  const int lane = threadIdx.x & 31, tig = lane & 3;
-  const int qlo = b * 128 + 4 * tig, qho = nbc * 128 + b * 64 + 4 * tig;
-  uint32_t h0[4], h1[4];
-#pragma unroll
-  for (int c = 0; c < 4; c++) {
-    h0[c] = *reinterpret_cast<const uint32_t *>(row0 + qho + 16 * c);
-    h1[c] = *reinterpret_cast<const uint32_t *>(row1 + qho + 16 * c);
-  }
-  const uint4 sc0 = lds128(row0 + nbc * 192 + b * 16), sc1 = lds128(row1 + nbc * 192 + b * 16);
-  const uint32_t S0[4] = {sc0.x, sc0.y, sc0.z, sc0.w}, S1[4] = {sc1.x, sc1.y, sc1.z, sc1.w};
-#pragma unroll
-  for (int j = 0; j < 8; j++) {
-    const int h = j >> 2, u = j & 3, sl = 2 * (u >> 1), c = 2 * h + (u & 1);
-    const int slo = 8 * h + u, shi = slo + 4;  // the chunk's two sub-blocks
-    const uint32_t l0 = *reinterpret_cast<const uint32_t *>(row0 + qlo + 16 * j);
-    const uint32_t l1 = *reinterpret_cast<const uint32_t *>(row1 + qlo + 16 * j);
-    f.alo0[j] = q6_a4_lo(l0, h0[c], sl);
-    f.ahi0[j] = q6_a4_hi(l0, h0[c], sl);
-    f.alo1[j] = q6_a4_lo(l1, h1[c], sl);
-    f.ahi1[j] = q6_a4_hi(l1, h1[c], sl);
-    f.s0[j] = sbyte_of(S0[slo >> 2], slo & 3);
-    f.t0[j] = sbyte_of(S0[shi >> 2], shi & 3);
-    f.s1[j] = sbyte_of(S1[slo >> 2], slo & 3);
-    f.t1[j] = sbyte_of(S1[shi >> 2], shi & 3);
-  }
-  f.df0 = h2f_bits(*reinterpret_cast<const unsigned short *>(row0 + nbc * 208 + b * 2));
-  f.df1 = h2f_bits(*reinterpret_cast<const unsigned short *>(row1 + nbc * 208 + b * 2));
+__host__ __device__ inline int batch6_byte(int e, int plane) {
+  const int g = e >> 5, i = (e >> 3) & 3, k = e & 7;
+  return plane * 256 + (k >> 1) * 64 + (g >> 1) * 16 + (k & 1) * 8 + (g & 1) * 4 + i;
 }
 
-// One sequence's products of the block: the chains of (row gid, classes 2 tig,
-// 2 tig + 1) and (row gid + 8, the same classes).
-__device__ __forceinline__ void q6k_batch_seq(const Q6Frag &f, const XBlock6 &x, float (&s)[4]) {
-  int acc0 = 0, acc1 = 0, acc2 = 0, acc3 = 0;
+__device__ __forceinline__ void q6d_batch_block(const uint8_t *row0, const uint8_t *row1, int b, const Q4X &x,
+                                                Q4Chain &c) {
+  const int tig = threadIdx.x & 3;
+  const uint8_t *p0 = row0 + b * kBatch6Block + 16 * tig, *p1 = row1 + b * kBatch6Block + 16 * tig;
+  const float df0 = h2f_bits(*reinterpret_cast<const unsigned short *>(row0 + b * kBatch6Block + 512));
+  const float df1 = h2f_bits(*reinterpret_cast<const unsigned short *>(row1 + b * kBatch6Block + 512));
+  const float d[4] = {__fmul_rn(x.xd0, df0), __fmul_rn(x.xd1, df0), __fmul_rn(x.xd0, df1), __fmul_rn(x.xd1, df1)};
 #pragma unroll
-  for (int j = 0; j < 8; j++) {
-    int d0, d1, d2, d3, e0, e1, e2, e3;
-    mma_s8_k16(f.alo0[j], f.alo1[j], x.b[2 * j], d0, d1, d2, d3);
-    mma_s8_k16(f.ahi0[j], f.ahi1[j], x.b[2 * j + 1], e0, e1, e2, e3);
-    acc0 += f.s0[j] * d0 + f.t0[j] * e0;
-    acc1 += f.s0[j] * d1 + f.t0[j] * e1;
-    acc2 += f.s1[j] * d2 + f.t1[j] * e2;
-    acc3 += f.s1[j] * d3 + f.t1[j] * e3;
+  for (int j = 0; j < 4; j++) {
+    const uint4 a0 = lds128(p0 + 64 * j), a1 = lds128(p1 + 64 * j);              // w0: rows gid, gid + 8
+    const uint4 b0 = lds128(p0 + 256 + 64 * j), b1 = lds128(p1 + 256 + 64 * j);  // w1
+#pragma unroll
+    for (int kk = 0; kk < 2; kk++) {
+      const int k = 2 * j + kk;
+      const uint32_t r0g0 = kk ? a0.z : a0.x, r0g1 = kk ? a0.w : a0.y;
+      const uint32_t r1g0 = kk ? a1.z : a1.x, r1g1 = kk ? a1.w : a1.y;
+      const uint32_t s0g0 = kk ? b0.z : b0.x, s0g1 = kk ? b0.w : b0.y;
+      const uint32_t s1g0 = kk ? b1.z : b1.x, s1g1 = kk ? b1.w : b1.y;
+      int L[4], H[4];
+      mma_s8(r0g0, r1g0, r0g1, r1g1, x.bx[k].x, x.bx[k].y, L[0], L[1], L[2], L[3]);
+      mma_s8(s0g0, s1g0, s0g1, s1g1, x.bx[k].x, x.bx[k].y, H[0], H[1], H[2], H[3]);
+#pragma unroll
+      for (int i = 0; i < 4; i++) c.s[k][i] = __fadd_rn(c.s[k][i], __fmul_rn(d[i], (float)(L[i] + 128 * H[i])));
+    }
   }
-  const float d0 = __fmul_rn(x.xd, f.df0), d1 = __fmul_rn(x.xd, f.df1);
-  s[0] = __fadd_rn(s[0], __fmul_rn(d0, (float)(acc0 >> 2)));
-  s[1] = __fadd_rn(s[1], __fmul_rn(d0, (float)(acc1 >> 2)));
-  s[2] = __fadd_rn(s[2], __fmul_rn(d1, (float)(acc2 >> 2)));
-  s[3] = __fadd_rn(s[3], __fmul_rn(d1, (float)(acc3 >> 2)));
+}
+
+// Digit planes of a repacked Q6_K tensor: one thread per (row, block, element).
+__global__ void batch6_convert(const uint8_t *__restrict__ dev, size_t stride, size_t rows, size_t nb,
+                               uint8_t *__restrict__ out, size_t pitch) {
+  const size_t t = blockIdx.x * (size_t)blockDim.x + threadIdx.x;
+  if (t >= rows * nb * kQK) return;
+  const size_t r = t / (nb * kQK), rem = t % (nb * kQK);
+  const int e = (int)(rem % kQK);
+  size_t off;
+  int nbl, b;
+  q6_locate(nb, rem / kQK, off, nbl, b);
+  const uint8_t *row = dev + r * stride + off;
+  const int h = e >> 7, pos = e & 127;
+  const int qlo = 64 * h + (pos & 63), qho = 32 * h + (pos & 31);
+  const uint8_t lb = row[b * 128 + 16 * (qlo >> 4) + q6_pic(qlo & 15)];
+  const uint8_t hb = row[nbl * 128 + b * 64 + 16 * (qho >> 4) + q6_pic(qho & 15)] ^ 0xAAu;  // stored flipped
+  const int nib = pos < 64 ? (lb & 0xF) : (lb >> 4);
+  const int q = (nib | (((hb >> (2 * (pos >> 5))) & 3) << 4)) - 32;
+  const int sc = (int8_t)row[nbl * 192 + b * 16 + (e >> 4)];
+  const int v = sc * q;          // in [-4064, 4096]
+  const int w1 = v >> 7;         // floor(v / 128), in [-32, 32]
+  const int w0 = v - 128 * w1;   // in [0, 127]
+  uint8_t *blk = out + r * pitch + (rem / kQK) * kBatch6Block;
+  blk[batch6_byte(e, 0)] = (uint8_t)w0;
+  blk[batch6_byte(e, 1)] = (uint8_t)(int8_t)w1;
+  if (e == 0) {
+    blk[512] = row[nbl * 208 + b * 2];
+    blk[513] = row[nbl * 208 + b * 2 + 1];
+  }
+  if (e < 14) blk[514 + e] = 0;
 }
 
 __device__ __forceinline__ void batch_emit(const BParams &P, int row, int seq, float acc,
@@ -265,119 +278,58 @@ __global__ void __launch_bounds__(kBatchThreads, 1) gemv_batch_kernel(BParams P)
   const int nsg = (P.nseq + SB - 1) / SB;
   const bool active = sg < nsg;
   const int nbc = P.nbc;
-  if constexpr (FMT == Q4K) {
-    static_assert(SB == 8, "Q4_K: the 8 sequences of a group are the MMA's N");
-    const int sx = sg * 8 + gid;                          // B: sequence of column gid
-    const int sa = sg * 8 + 2 * tig, sb2 = sa + 1;         // D: sequences of this thread
-    const bool xv = sx < P.nseq, v0 = sa < P.nseq, v1 = sb2 < P.nseq;
-    const uint8_t *imx = P.img + (size_t)(xv ? sx : 0) * P.istride;
-    const uint8_t *im0 = P.img + (size_t)(v0 ? sa : 0) * P.istride;
-    const uint8_t *im1 = P.img + (size_t)(v1 ? sb2 : 0) * P.istride;
-    Q4Chain ch;
-    // x of block 0 (Q4_K rows are never chunked: every unit runs blocks 0 .. nbc-1)
-    Q4X xc;
-    q4x_load(imx, xv, im0, v0, im1, v1, xc);
-    for (int u = 0; u < nunits; u++) {
-      const int st = u % S, c = u % P.nch;
-      if (!mbar_wait_bounded(&full[st], (u / S) & 1, P.err)) break;
-      if (active) {
-        if (c == 0) {
+  static_assert(SB == 8, "the 8 sequences of a group are the MMA's N");
+  const int sx = sg * 8 + gid;                   // B: sequence of column gid
+  const int sa = sg * 8 + 2 * tig, sb2 = sa + 1;  // D: sequences of this thread
+  const bool xv = sx < P.nseq, v0 = sa < P.nseq, v1 = sb2 < P.nseq;
+  const uint8_t *imx = P.img + (size_t)(xv ? sx : 0) * P.istride;
+  const uint8_t *im0 = P.img + (size_t)(v0 ? sa : 0) * P.istride;
+  const uint8_t *im1 = P.img + (size_t)(v1 ? sb2 : 0) * P.istride;
+  Q4Chain ch;
+  // x of the first block; then always one block ahead (units run in the
+  // order tile, chunk, so the block after a unit's last is the next chunk's
+  // first: block ((c + 1) % nch) * nbc)
+  Q4X xc;
+  q4x_load<FMT == Q4K>(imx, xv, im0, v0, im1, v1, xc);
+  for (int u = 0; u < nunits; u++) {
+    const int st = u % S, c = u % P.nch;
+    if (!mbar_wait_bounded(&full[st], (u / S) & 1, P.err)) break;
+    if (active) {
+      if (c == 0) {
 #pragma unroll
-          for (int i = 0; i < 4; i++) {
-            ch.m[i] = 0.0f;
+        for (int i = 0; i < 4; i++) {
+          ch.m[i] = 0.0f;
 #pragma unroll
-            for (int k = 0; k < 8; k++) ch.s[k][i] = 0.0f;
-          }
-        }
-        const uint8_t *tile = stages + (size_t)st * P.stage_bytes;
-        const uint8_t *row0 = tile + (16 * g + gid) * P.ps, *row1 = row0 + 8 * P.ps;
-#pragma unroll 1
-        for (int b = 0; b < nbc; b++) {
-          // the next block's x (block 0 again after the last: the next tile's first)
-          const size_t xo = (size_t)(b + 1 < nbc ? b + 1 : 0) * kImgQ8K4;
-          Q4X xn;
-          q4x_load(imx + xo, xv, im0 + xo, v0, im1 + xo, v1, xn);
-          q4k_batch_block(row0, row1, nbc, b, xc, ch);
-          xc = xn;
-        }
-        if (c == P.nch - 1) {
-          const int r0 = rb + (u / P.nch) * T + 16 * g + gid;
-#pragma unroll
-          for (int i = 0; i < 4; i++) {
-            const int row = r0 + 8 * (i >> 1), seq = (i & 1) ? sb2 : sa;
-            float acc = ch.m[i];
-#pragma unroll
-            for (int k = 0; k < 8; k++) acc = __fadd_rn(acc, ch.s[k][i]);
-            if (row < re && seq < P.nseq) batch_emit(P, row, seq, acc, best);
-          }
+          for (int k = 0; k < 8; k++) ch.s[k][i] = 0.0f;
         }
       }
-      __syncwarp();
-      if (lane == 0) mbar_arrive(&empty[st]);
-    }
-  } else {
-    float ch[SB][4];
-    for (int u = 0; u < nunits; u++) {
-      const int st = u % S, c = u % P.nch;
-      if (!mbar_wait_bounded(&full[st], (u / S) & 1, P.err)) break;
-      if (active) {
-        if (c == 0) {
-#pragma unroll
-          for (int q = 0; q < SB; q++)
-#pragma unroll
-            for (int i = 0; i < 4; i++) ch[q][i] = 0.0f;
-        }
-        const uint8_t *tile = stages + (size_t)st * P.stage_bytes;
-        const uint8_t *row0 = tile + (16 * g + gid) * P.ps, *row1 = row0 + 8 * P.ps;
-        // sequence q's x of block b, loaded one (block, sequence) step ahead
-        const int nvq = min(SB, P.nseq - sg * SB);  // this group's sequences (warp-uniform)
-        auto xim = [&](int b, int q) {
-          return P.img + (size_t)(sg * SB + q) * P.istride + (size_t)(c * nbc + b) * kImgQ8K6;
-        };
-        XBlock6 xc;
-        load_xblock6(xim(0, 0), xc);
+      const uint8_t *tile = stages + (size_t)st * P.stage_bytes;
+      const uint8_t *row0 = tile + (16 * g + gid) * P.ps, *row1 = row0 + 8 * P.ps;
+      const int nxt = ((c + 1) % P.nch) * nbc;
 #pragma unroll 1
-        for (int b = 0; b < nbc; b++) {
-          Q6Frag f;
-          q6k_batch_frag(row0, row1, nbc, b, f);
+      for (int b = 0; b < nbc; b++) {
+        const size_t xo = (size_t)(b + 1 < nbc ? c * nbc + b + 1 : nxt) * kImgQ8K4;
+        Q4X xn;
+        q4x_load<FMT == Q4K>(imx + xo, xv, im0 + xo, v0, im1 + xo, v1, xn);
+        if constexpr (FMT == Q4K) q4k_batch_block(row0, row1, nbc, b, xc, ch);
+        else q6d_batch_block(row0, row1, b, xc, ch);
+        xc = xn;
+      }
+      if (c == P.nch - 1) {
+        const int r0 = rb + (u / P.nch) * T + 16 * g + gid;
 #pragma unroll
-          for (int q = 0; q < SB; q++) {
-            if (q < nvq) {
-              const bool lastq = q + 1 >= nvq;
-              const int bn = lastq ? b + 1 : b, qn = lastq ? 0 : q + 1;
-              XBlock6 xn = xc;
-              if (bn < nbc) load_xblock6(xim(bn, qn), xn);
-              q6k_batch_seq(f, xc, ch[q]);
-              xc = xn;
-            }
-          }
-        }
-        if (c == P.nch - 1) {
-          // s = 0 + sums[0] + ... + sums[7]: the row's classes 2 t, 2 t + 1
-          // are held by the lane with tig = t of its row quad
-          const int r0 = rb + (u / P.nch) * T + 16 * g + gid;
+        for (int i = 0; i < 4; i++) {
+          const int row = r0 + 8 * (i >> 1), seq = (i & 1) ? sb2 : sa;
+          // s = sumf + sums[0] + ... + sums[7] (Q6_K: sumf = 0)
+          float acc = ch.m[i];
 #pragma unroll
-          for (int q = 0; q < SB; q++) {
-            const int seq = sg * SB + q;
-#pragma unroll
-            for (int half = 0; half < 2; half++) {
-              float acc = 0.0f;
-#pragma unroll
-              for (int t = 0; t < 4; t++) {
-                const float a = __shfl_sync(0xffffffffu, ch[q][2 * half], (lane & ~3) + t);
-                const float b2 = __shfl_sync(0xffffffffu, ch[q][2 * half + 1], (lane & ~3) + t);
-                acc = __fadd_rn(acc, a);
-                acc = __fadd_rn(acc, b2);
-              }
-              const int row = r0 + 8 * half;
-              if (tig == 0 && row < re && seq < P.nseq) batch_emit(P, row, seq, acc, best);
-            }
-          }
+          for (int k = 0; k < 8; k++) acc = __fadd_rn(acc, ch.s[k][i]);
+          if (row < re && seq < P.nseq) batch_emit(P, row, seq, acc, best);
         }
       }
-      __syncwarp();
-      if (lane == 0) mbar_arrive(&empty[st]);
     }
+    __syncwarp();
+    if (lane == 0) mbar_arrive(&empty[st]);
   }
 
   if (P.key) {
@@ -405,18 +357,17 @@ __global__ void __launch_bounds__(kBatchThreads, 1) gemv_batch_kernel(BParams P)
   }
 }
 
-// Batched x images: quantize_q8_k of every span of every sequence (grid: spans x sequences).
-template <int FMT>
-__global__ void __launch_bounds__(256) prep_q8k_batch(const float *__restrict__ x, size_t dim_in,
-                                                      size_t xstride, uint8_t *__restrict__ img, size_t istride) {
+// Batched x images: quantize_q8_k of every span of every sequence (grid:
+// spans x sequences), in the class-major layout of the Q4_K image, which the
+// batched kernel reads for both formats.
+__global__ void __launch_bounds__(256) prep_q8k_batch(const float *__restrict__ x, size_t dim_in, size_t xstride,
+                                                      uint8_t *__restrict__ img, size_t istride) {
   pdl_trigger();
   __shared__ Q8KSpanSmem sm;
   const size_t span = blockIdx.x, s = blockIdx.y;
   const size_t e = span * kQK + threadIdx.x;
   const float v = e < dim_in ? x[s * xstride + e] : 0.0f;
-  uint8_t *im = img + s * istride;
-  if constexpr (FMT == Q4K) q8k_span_write(v, im + span * kImgQ8K4, nullptr, sm);
-  else q8k_span_write(v, nullptr, im + span * kImgQ8K6, sm);
+  q8k_span_write(v, img + s * istride + span * kImgQ8K4, nullptr, sm);
 }
 
 using BatchFn = void (*)(BParams);
@@ -447,28 +398,62 @@ cudaError_t ensure_batch_attr(int device, BatchFn fn, int smem) {
   return e;
 }
 
+// Q4_K: a unit is 32 rows x the whole row. Q6_K (digit planes): 32 rows x
+// nbc consecutive blocks, nbc the largest divisor of the block count up to 4
+// (the planes of consecutive blocks are contiguous). Rows are padded to 64
+// bytes past a multiple of 128 in shared memory, so the eight rows x four
+// lanes of a 128-bit load hit distinct banks.
 BatchPlan batch_plan(int device, const unltd_weight_s &w) {
   BatchPlan p;
   const bool q4 = w.dtype == Q4K;
-  p.T = q4 ? 32 : 16;
-  const bool chunked = !q4 && q6_chunked(w.nb) && w.row_stride == w.row_bytes;
-  p.nch = chunked ? (int)(w.nb / kQ6Chunk) : 1;
-  p.nbc = chunked ? kQ6Chunk : (int)w.nb;
-  p.unit_bytes = chunked ? kQ6Chunk * kQ6Bytes : (int)w.row_stride;
-  p.ps = (int)round_up((size_t)p.unit_bytes, 128) + (q4 ? 32 : 16);
+  p.T = 32;
+  if (q4) {
+    p.nch = 1;
+    p.nbc = (int)w.nb;
+    p.unit_bytes = (int)w.row_stride;
+  } else {
+    int nbc = 1;
+    for (int c = 4; c >= 1; c--)
+      if (w.nb % c == 0) {
+        nbc = c;
+        break;
+      }
+    p.nbc = nbc;
+    p.nch = (int)(w.nb / nbc);
+    p.unit_bytes = nbc * kBatch6Block;
+  }
+  p.ps = (int)round_up((size_t)p.unit_bytes, 128) + (q4 ? 32 : 64);
   p.stage_bytes = (int)round_up((size_t)p.T * p.ps, 128);
   const int smem_max = max_smem_optin_b(device) - 1024;
   p.S = std::min(kBatchStages, (smem_max - kBatchHdr) / p.stage_bytes);
   if (p.S < 2) return p;
   p.smem = kBatchHdr + p.S * p.stage_bytes;
-  p.fn = q4 ? gemv_batch_kernel<Q4K, 32, 8> : gemv_batch_kernel<Q6K, 16, 4>;
+  p.fn = q4 ? gemv_batch_kernel<Q4K, 32, 8> : gemv_batch_kernel<Q6K, 32, 8>;
   return p;
 }
 
 }  // namespace
 
-size_t gemv_batch_img_bytes(const unltd_weight_s &w) {
-  return round_up(w.nb * (size_t)(w.dtype == Q4K ? kImgQ8K4 : kImgQ8K6), 256);
+size_t gemv_batch_img_bytes(const unltd_weight_s &w) { return round_up(w.nb * (size_t)kImgQ8K4, 256); }
+
+int32_t gemv_batch_prepare(unltd_ctx ctx, unltd_weight_s *w) {
+  if (w->dtype != Q6K || w->dev_b || w->dim_out == 0) return UNLTD_OK;
+  const size_t pitch = w->nb * kBatch6Block;
+  uint8_t *out = nullptr;
+  cudaError_t e = cudaMalloc(&out, w->dim_out * pitch);
+  if (e != cudaSuccess) return cuda_error(e, "gemv_batch: Q6_K digit planes");
+  const size_t n = w->dim_out * w->nb * kQK;
+  batch6_convert<<<(unsigned)((n + 255) / 256), 256, 0, ctx->stream>>>(w->dev, w->row_stride, w->dim_out, w->nb, out,
+                                                                        pitch);
+  e = cudaGetLastError();
+  if (e == cudaSuccess) e = cudaStreamSynchronize(ctx->stream);
+  if (e != cudaSuccess) {
+    cudaFree(out);
+    return cuda_error(e, "gemv_batch: Q6_K digit planes");
+  }
+  w->dev_b = out;
+  w->b_pitch = pitch;
+  return UNLTD_OK;
 }
 
 int32_t gemv_batch_launch(unltd_ctx ctx, const BatchGemvArgs &a) {
@@ -480,6 +465,7 @@ int32_t gemv_batch_launch(unltd_ctx ctx, const BatchGemvArgs &a) {
   if (w.dim_out > (size_t)INT32_MAX) return set_error(UNLTD_ERR_UNSUPPORTED, "gemv_batch: too many rows");
   const BatchPlan pl = batch_plan(ctx->device, w);
   if (!pl.fn) return set_error(UNLTD_ERR_UNSUPPORTED, "gemv_batch: rows too long for a shared-memory tile");
+  if (w.dtype == Q6K && !w.dev_b) return set_error(UNLTD_ERR_INVALID_ARG, "gemv_batch: Q6_K weight not prepared");
   cudaStream_t st = ctx->stream;
   const size_t istride = gemv_batch_img_bytes(w);
   const uint8_t *img = a.img;
@@ -488,8 +474,7 @@ int32_t gemv_batch_launch(unltd_ctx ctx, const BatchGemvArgs &a) {
     if (ctx->scratch_bytes < istride * a.nseq)
       return set_error(UNLTD_ERR_INVALID_ARG, "gemv_batch: scratch not reserved");
     const dim3 grid((unsigned)w.nb, (unsigned)a.nseq);
-    if (w.dtype == Q4K) prep_q8k_batch<Q4K><<<grid, 256, 0, st>>>(a.x, w.dim_in, a.xstride, ctx->scratch, istride);
-    else prep_q8k_batch<Q6K><<<grid, 256, 0, st>>>(a.x, w.dim_in, a.xstride, ctx->scratch, istride);
+    prep_q8k_batch<<<grid, 256, 0, st>>>(a.x, w.dim_in, a.xstride, ctx->scratch, istride);
     cudaError_t e = cudaGetLastError();
     if (e != cudaSuccess) return cuda_error(e, "gemv_batch prep");
     ctx->launches += 1;
@@ -498,8 +483,8 @@ int32_t gemv_batch_launch(unltd_ctx ctx, const BatchGemvArgs &a) {
   if (cudaError_t e = ensure_batch_attr(ctx->device, pl.fn, max_smem_optin_b(ctx->device) - 1024); e != cudaSuccess)
     return cuda_error(e, "gemv_batch attribute");
   BParams P;
-  P.W = w.dev;
-  P.pitch = w.row_stride;
+  P.W = w.dtype == Q6K ? w.dev_b : w.dev;
+  P.pitch = w.dtype == Q6K ? w.b_pitch : w.row_stride;
   P.rows = (int)w.dim_out;
   P.nbc = pl.nbc;
   P.nch = pl.nch;
@@ -539,7 +524,7 @@ int32_t gemv_batch_launch(unltd_ctx ctx, const BatchGemvArgs &a) {
 cudaError_t gemv_batch_prewarm(int device) {
   const int m = max_smem_optin_b(device) - 1024;
   cudaError_t e = ensure_batch_attr(device, gemv_batch_kernel<Q4K, 32, 8>, m);
-  if (e == cudaSuccess) e = ensure_batch_attr(device, gemv_batch_kernel<Q6K, 16, 4>, m);
+  if (e == cudaSuccess) e = ensure_batch_attr(device, gemv_batch_kernel<Q6K, 32, 8>, m);
   return e;
 }
 

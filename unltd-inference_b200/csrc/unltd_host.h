@@ -70,6 +70,12 @@ struct unltd_weight_s {
   size_t row_bytes = 0;   // GGUF bytes per row
   size_t row_stride = 0;  // device bytes per row (row_bytes rounded up to 16)
   uint8_t *dev = nullptr;
+  // Q6_K for the batched GEMV (made on first batched use): per block, the
+  // scaled quants v = sc * (q - 32) as two int8 digit planes (v = 128 w1 + w0)
+  // in the MMA's operand order, then the block's f16 d; kBatch6Block bytes
+  // per block, b_pitch per row.
+  uint8_t *dev_b = nullptr;
+  size_t b_pitch = 0;
 };
 
 namespace unltd {
@@ -160,6 +166,10 @@ int32_t gemv_batch_launch(unltd_ctx ctx, const BatchGemvArgs &a);
 size_t gemv_batch_img_bytes(const unltd_weight_s &w);
 bool gemv_batch_supported(int device, const unltd_weight_s &w);
 cudaError_t gemv_batch_prewarm(int device);
+// Makes w's batched-GEMV operands (Q6_K digit planes) if w needs them and
+// they do not exist yet; allocates and synchronizes, so never inside a
+// stream capture.
+int32_t gemv_batch_prepare(unltd_ctx ctx, unltd_weight_s *w);
 // True when gemv_launch can fuse an RMSNorm of length w.dim_in into w's GEMV.
 bool gemv_norm_fusable(unltd_ctx ctx, const unltd_weight_s &w, int mode);
 // True when w's GEMV runs on the tensor-core kernel (peer row-split sums).
