@@ -271,7 +271,7 @@ def decode_bytes_per_token(cfg, position, n_seq=1):
     return total
 
 
-def decode_batch_bench(m, cfg, st, pos0, n_seq, n_steps):
+def decode_batch_bench(m, cfg, st, pos0, n_seq, n_steps, profile_region=False):
     """BASELINE config 4 at batch n_seq on one GPU: n_seq sequences from the
     2048-position state (each its own first token) decoded together through
     unltd_qwen35_batch_decode; every weight matrix is read once per step for
@@ -286,12 +286,16 @@ def decode_batch_bench(m, cfg, st, pos0, n_seq, n_steps):
     ext = torch.cuda.ExternalStream(b.info()["stream"])
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     torch.cuda.synchronize()
+    if profile_region:
+        torch.cuda.profiler.start()
     t0 = time.perf_counter()
     e0.record(ext)
     toks = b.decode(warm[:, -1], n_steps)
     e1.record(ext)
     torch.cuda.synchronize()
     wall = time.perf_counter() - t0
+    if profile_region:
+        torch.cuda.profiler.stop()
     ms_step = e0.elapsed_time(e1) / n_steps
     bps = decode_bytes_per_token(cfg, pos0 + 4 + n_steps // 2, n_seq)
     peak, peak_kind = _peaks()
@@ -308,7 +312,7 @@ def decode_batch_bench(m, cfg, st, pos0, n_seq, n_steps):
     return out
 
 
-def decode_bench(n_tokens, with_cpu, rank=0, world=1, dist=None, profile_region=False, batch=32):
+def decode_bench(n_tokens, with_cpu, rank=0, world=1, dist=None, profile_region=False, batch=32, profile_batch=False):
     """BASELINE configs 3 and 4: greedy decode of the synthetic 9B-class hybrid
     model from a 2048-position context through unltd_qwen35_decode, on one GPU
     or tensor-parallel over `world` GPUs (one process each). Device-timed on
@@ -374,7 +378,7 @@ def decode_bench(n_tokens, with_cpu, rank=0, world=1, dist=None, profile_region=
     s.close()
     if world == 1 and batch > 1:
         out["batch"] = 1
-        out["batch%d" % batch] = decode_batch_bench(m, cfg, st, pos0, batch, max(4, n_tokens // 4))
+        out["batch%d" % batch] = decode_batch_bench(m, cfg, st, pos0, batch, max(4, n_tokens // 4), profile_batch)
     m.close()
     ctx.close()
     if with_cpu and rank == 0:
@@ -491,6 +495,8 @@ def main():
     ap.add_argument("--gemm-only", action="store_true", help="measure only the config-2 GEMM (profiling)")
     ap.add_argument("--profile-region", action="store_true",
                     help="bracket the timed decode with cudaProfilerStart/Stop (ncu --profile-from-start off)")
+    ap.add_argument("--profile-batch", action="store_true",
+                    help="bracket the timed batch decode instead (ncu --profile-from-start off)")
     args = ap.parse_args()
     if args.impl == "reference":
         return run_reference(args)
@@ -525,6 +531,7 @@ def main():
 
     if args.decode_only:
         d = decode_bench(args.decode_tokens, with_cpu=False, rank=rank, world=world, dist=dist, batch=args.decode_batch,
+                         profile_batch=args.profile_batch,
                          profile_region=args.profile_region)
         if rank == 0:
             os.write(out_fd, (json.dumps({"metric": "decode tok/s", "decode": d}) + "\n").encode())

@@ -314,7 +314,7 @@ static int32_t check_batch(unltd_ctx c, unltd_weight w, int32_t n_seq, int32_t m
 
 // Grows the context scratch to n_seq batched x images of w.
 static int32_t reserve_batch(unltd_ctx c, unltd_weight w, int32_t n_seq) {
-  const size_t need = gemv_batch_img_bytes(*w) * (size_t)n_seq;
+  const size_t need = gemv_batch_img_bytes(*w, n_seq);
   if (c->scratch_bytes >= need) return UNLTD_OK;
   if (c->scratch_fixed) return set_error(UNLTD_ERR_UNSUPPORTED, "gemv_batch: x images larger than the fixed scratch");
   cudaError_t e = cudaStreamSynchronize(c->stream);

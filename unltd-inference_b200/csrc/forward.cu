@@ -54,6 +54,13 @@ __device__ __forceinline__ T *seq_ptr(T *p, size_t off) {
   return p ? reinterpret_cast<T *>(reinterpret_cast<uintptr_t>(p) + off) : p;
 }
 __device__ __forceinline__ size_t seq_off(size_t ss) { return (size_t)blockIdx.z * ss; }
+// A batch session's producers write the batched x images (shared by the
+// sequences, kBImgBlock per span and group of 8 sequences): the block of
+// this CTA's sequence for `span`, or null without a batched image.
+__device__ __forceinline__ uint8_t *seq_bimg(uint8_t *bimg, int nsg, int span) {
+  return bimg ? bimg + bimg_block((size_t)span, (int)(blockIdx.z >> 3), nsg) : nullptr;
+}
+__device__ __forceinline__ int seq_sl() { return (int)(blockIdx.z & 7); }
 
 // ---- reductions -----------------------------------------------------------
 // Sum of a and b over the block; every thread receives the same values.
@@ -113,6 +120,8 @@ struct NormArgs {
   unsigned long long *key;  // non-null: reset the LM-head argmax state
   unsigned *done;
   size_t ss = 0;            // bytes between the sequences' arenas (a, b, r_out, images)
+  uint8_t *bimg = nullptr;  // batch session: the batched x images (then img4 = img6 = null)
+  int nsg = 0;
 };
 
 __global__ void __launch_bounds__(256) norm_quant_kernel(NormArgs p) {
@@ -169,7 +178,7 @@ __global__ void __launch_bounds__(256) norm_quant_kernel(NormArgs p) {
   if (p.r_out) p.r_out[e] = r;
   const float xn = __fmul_rn(__fmul_rn(r, scale), p.w[e]);
   q8k_span_write(xn, p.img4 ? p.img4 + (size_t)span * kImgQ8K4 : nullptr,
-                 p.img6 ? p.img6 + (size_t)span * kImgQ8K6 : nullptr, sm);
+                 p.img6 ? p.img6 + (size_t)span * kImgQ8K6 : nullptr, sm, seq_bimg(p.bimg, p.nsg, span), seq_sl());
   if (p.key && span == 0 && t == 0) {
     *p.key = 0ull;
     *p.done = 0u;
@@ -195,7 +204,7 @@ __global__ void embed_q4k_kernel(const uint8_t *table, size_t stride, size_t nb,
 
 // ---- SwiGLU (kernels.rs:174-182) fused with the Q8_K image of its output ---
 __global__ void __launch_bounds__(256) swiglu_quant_kernel(const float *g, const float *u, uint8_t *img4,
-                                                           uint8_t *img6, size_t ss) {
+                                                           uint8_t *img6, size_t ss, uint8_t *bimg, int nsg) {
   pdl_trigger();
   __shared__ Q8KSpanSmem sm;
   pdl_wait();
@@ -207,7 +216,7 @@ __global__ void __launch_bounds__(256) swiglu_quant_kernel(const float *g, const
   const float t = g[e];
   const float s = __fdiv_rn(t, __fadd_rn(1.0f, exp_cr(-t)));
   q8k_span_write(__fmul_rn(s, u[e]), img4 ? img4 + (size_t)span * kImgQ8K4 : nullptr,
-                 img6 ? img6 + (size_t)span * kImgQ8K6 : nullptr, sm);
+                 img6 ? img6 + (size_t)span * kImgQ8K6 : nullptr, sm, seq_bimg(bimg, nsg, span), seq_sl());
 }
 
 // ---- recurrent layer between the projections (qwen35_forward.rs:390-508) --
@@ -226,6 +235,8 @@ struct RecrArgs {
   unsigned *span_ctr;
   uint8_t *img4, *img6;
   size_t ss = 0;  // bytes between the sequences' arenas
+  uint8_t *bimg = nullptr;  // batch session: the batched x images (then img4 = img6 = null)
+  int nsg = 0;
 };
 
 // One CTA per (v-head h, quarter of its columns), one thread per channel of
@@ -291,7 +302,7 @@ __device__ __forceinline__ float gdn_dot(const float (&st)[RW], const float *xw,
 // (quantize_q8_k) by warp 0. Thread j takes column j of both heads.
 template <int HD>
 __device__ __noinline__ void gated_norm_span(const float *y, const float *z, const float *ssm_norm, float eps,
-                                             uint8_t *img4, uint8_t *img6, int span) {
+                                             uint8_t *img4, uint8_t *img6, int span, uint8_t *imb) {
   static_assert(HD == 128, "a span holds two heads of 128");
   __shared__ double red2[2][HD / 32];
   __shared__ float so[256];
@@ -345,7 +356,7 @@ __device__ __noinline__ void gated_norm_span(const float *y, const float *z, con
 #pragma unroll
     for (int k = 0; k < 8; k++) v[k] = so[8 * lane + k];
     q8k_span_write_warp(v, lane, img4 ? img4 + (size_t)span * kImgQ8K4 : nullptr,
-                        img6 ? img6 + (size_t)span * kImgQ8K6 : nullptr);
+                        img6 ? img6 + (size_t)span * kImgQ8K6 : nullptr, imb, seq_sl());
   }
 }
 
@@ -513,7 +524,7 @@ __global__ void __launch_bounds__(HD) recr_mid_kernel(RecrArgs a) {
   __syncthreads();
   if (s_last) {
     __threadfence();
-    gated_norm_span<HD>(a.y, a.proj + a.z_off, a.ssm_norm, a.eps, a.img4, a.img6, span);
+    gated_norm_span<HD>(a.y, a.proj + a.z_off, a.ssm_norm, a.eps, a.img4, a.img6, span, seq_bimg(a.bimg, a.nsg, span));
   }
 }
 
@@ -535,6 +546,8 @@ struct AttnArgs {
   int nh, nkv, n_rot, nrp, ctx, nsplit;
   float eps, kq_scale;
   size_t ss = 0;  // bytes between the sequences' arenas
+  uint8_t *bimg = nullptr;  // batch session: the batched x images (then img4 = img6 = null)
+  int nsg = 0;
 };
 
 // This CTA's sequence's copies of the per-sequence buffers.
@@ -898,7 +911,7 @@ __global__ void __launch_bounds__(256) attn_combine_quant_kernel(AttnArgs a) {
   }
   const float gate = a.qk[(size_t)h * 2 * HDV + HDV + c];
   q8k_span_write(__fmul_rn(attn, sigmoid_f(gate)), a.img4 ? a.img4 + (size_t)span * kImgQ8K4 : nullptr,
-                 a.img6 ? a.img6 + (size_t)span * kImgQ8K6 : nullptr, sm);
+                 a.img6 ? a.img6 + (size_t)span * kImgQ8K6 : nullptr, sm, seq_bimg(a.bimg, a.nsg, span), seq_sl());
 }
 
 // greedy token from the cross-GPU maximum of the argmax keys
@@ -1004,6 +1017,8 @@ struct unltd_qwen35_session_s {
   int nseq = 1;
   size_t ss = 0;
   uint8_t *arena = nullptr;
+  uint8_t *bimg = nullptr;  // the batched x images (n_seq > 1)
+  int nsg = 0;
   std::vector<int> seq_pos;
   // activations
   float *X = nullptr, *R = nullptr, *T = nullptr, *F = nullptr;
@@ -1337,8 +1352,8 @@ int32_t dalloc(std::vector<void *> &bufs, T **p, size_t n, const char *what) {
 int64_t launch_gemv_img(unltd_qwen35_session s, const unltd_weight_s *w, float *y, int32_t *rc, bool send = false) {
   if (s->nseq > 1) {  // every sequence's GEMV in one pass over w
     BatchGemvArgs b{w};
-    b.img = s->img4;  // the batched GEMV reads the class-major (Q4_K) image for both formats
-    b.istride = s->ss;
+    b.img = s->bimg;
+    b.nsg = s->nsg;
     b.y = y;
     b.ystride = s->ss / 4;
     b.nseq = s->nseq;
@@ -1400,13 +1415,15 @@ int32_t enqueue_step(unltd_qwen35_session s) {
   const bool batch = s->nseq > 1;
   const unsigned nz = (unsigned)s->nseq;
   // the images a producer writes for its consumers: in a batch session the
-  // class-major (Q4_K) image only, which the batched GEMV reads for Q6_K too
-  auto im4 = [&](bool q4) { return batch || q4 ? s->img4 : nullptr; };
+  // batched image only (the batched GEMV reads it for both formats)
+  auto im4 = [&](bool q4) { return !batch && q4 ? s->img4 : nullptr; };
   auto im6 = [&](bool q6) { return !batch && q6 ? s->img6 : nullptr; };
   auto norm = [&](const float *a, const float *b, float *r_out, const float *w, bool q4, bool q6, bool argmax) {
     NormArgs p{a, b, r_out, w, d.n, d.eps, im4(q4), im6(q6),
                argmax && !batch ? s->ctx->argmax_key : nullptr, argmax && !batch ? s->ctx->argmax_done : nullptr};
     p.ss = s->ss;
+    p.bimg = s->bimg;
+    p.nsg = s->nsg;
     chk(launch_pdl(norm_quant_kernel, dim3(d.n / 256, 1, nz), dim3(256), 0, st, p), "norm");
   };
   // RMSNorm of a (+ b) feeding projection p (outputs at out + p.off[i]): fused
@@ -1485,6 +1502,8 @@ int32_t enqueue_step(unltd_qwen35_session s) {
       a.img4 = im4(L.out->dtype == Q4K);
       a.img6 = im6(L.out->dtype == Q6K);
       a.ss = s->ss;
+      a.bimg = s->bimg;
+      a.nsg = s->nsg;
       const dim3 rg(d.nvl, 128 / kGdnCols, nz);
       if (d.K == 4) chk(launch_pdl(recr_mid_kernel<128, 4>, rg, dim3(128), 0, st, a), "recr_mid");
       else chk(launch_pdl(recr_mid_kernel<128, 0>, rg, dim3(128), 0, st, a), "recr_mid");
@@ -1514,6 +1533,8 @@ int32_t enqueue_step(unltd_qwen35_session s) {
       a.eps = d.eps;
       a.kq_scale = d.kq_scale;
       a.ss = s->ss;
+      a.bimg = s->bimg;
+      a.nsg = s->nsg;
       const dim3 sg(d.nkvl, (s->ctx_len + 31) / 32, nz), vg(d.nkvl, s->nsplit, nz);
       const size_t q_smem = (size_t)(d.nhl / d.nkvl) * d.hdv * 8, v_smem = (size_t)kChunk * d.hdv * 4;
       const size_t sm_smem = softmax_smem(s->ctx_len);
@@ -1537,7 +1558,8 @@ int32_t enqueue_step(unltd_qwen35_session s) {
     // residual = x_in + attn_out; rmsnorm(residual, post_attention_norm) -> gate|up image
     norm_proj(s->X, s->T, s->R, L.post_norm, L.gate_up, s->FF, out_send);
     chk(launch_pdl(swiglu_quant_kernel, dim3(d.nffl / 256, 1, nz), dim3(256), 0, st, (const float *)s->FF,
-                   (const float *)(s->FF + d.nffl), im4(L.down->dtype == Q4K), im6(L.down->dtype == Q6K), s->ss),
+                   (const float *)(s->FF + d.nffl), im4(L.down->dtype == Q4K), im6(L.down->dtype == Q6K), s->ss,
+                   s->bimg, s->nsg),
         "swiglu");
     nl += launch_gemv_img(s, L.down, s->F, &rc, down_send);
     if (!down_send) allreduce(s->F, d.n);
@@ -1547,8 +1569,8 @@ int32_t enqueue_step(unltd_qwen35_session s) {
   norm(s->R, s->F, s->X, m->out_norm, m->output->dtype == Q4K, m->output->dtype == Q6K, true);
   if (batch) {
     BatchGemvArgs b{m->output};
-    b.img = s->img4;
-    b.istride = s->ss;
+    b.img = s->bimg;
+    b.nsg = s->nsg;
     b.y = s->logits;
     b.ystride = s->ss / 4;
     b.nseq = s->nseq;
@@ -1908,6 +1930,10 @@ int32_t unltd_qwen35_session_create_batch(unltd_qwen35 m, int32_t ctx_len, int32
   if (!rc)
     for (auto &sl : A.slots) *sl.first = s->arena + sl.second;
   if (!rc) rc = dalloc(B, &s->rope, (size_t)ctx_len * std::max(d.nrp, 1), "session");
+  if (!rc && n_seq > 1) {
+    s->nsg = (n_seq + 7) / 8;
+    rc = dalloc(B, &s->bimg, spans * s->nsg * kBImgBlock, "session batched images");
+  }
   // IMROPE angles (kernels.rs:381-400): angle = pos * theta^ic by repeated
   // multiplication; (cos, sin) of the rotated pairs ic % 3 == 0, from libm.
   if (!rc && d.nrp > 0) {

@@ -46,8 +46,8 @@ struct BParams {
   int rows, nbc, nch;  // rows; blocks per unit; units per row
   int unit_bytes;      // bytes of one row's unit (a 16-block chunk or the whole row)
   int ps, stage_bytes, S;
-  const uint8_t *img;  // x images: sequence s at img + s * istride
-  size_t istride;
+  const uint8_t *img;  // batched x images: (block b, sequence group sg) at img + bimg_block(b, sg, nsg)
+  int nsg;
   float *y;            // y of sequence s at y + s * ystride (may be null with argmax)
   size_t ystride;
   int nseq;
@@ -73,9 +73,12 @@ struct Q4Chain {
   float m[4];     // sumf (min term), same order
 };
 
-// This lane's x operands of one block (from global memory): the B words of
-// sequence gid for the eight classes, its min-term words, and the d of the
-// two sequences of its D columns. Loaded one block ahead of their use.
+// This lane's x operands of one block, from the batched image of its
+// sequence group (one coalesced 8-byte load each): the B words of sequence
+// gid for the eight classes, its min-term words, and the d of the two
+// sequences of its D columns. Loaded one block ahead of their use. Slots of
+// sequences past the batch are never written; they feed only D columns that
+// are never emitted (and the min-term rows with tig >= 2 are zero in A).
 struct Q4X {
   uint2 bx[8];
   uint32_t bml, bmh;
@@ -83,17 +86,16 @@ struct Q4X {
 };
 
 template <bool MIN>
-__device__ __forceinline__ void q4x_load(const uint8_t *xg, bool xv, const uint8_t *xs0, bool v0, const uint8_t *xs1,
-                                         bool v1, Q4X &x) {
-  const int tig = threadIdx.x & 3;
-  const uint8_t *xw = xg + 128 * (tig >> 1) + 8 * (tig & 1);
+__device__ __forceinline__ void q4x_load(const uint8_t *blk, Q4X &x) {
+  const int lane = threadIdx.x & 31, tig = lane & 3;
 #pragma unroll
-  for (int k = 0; k < 8; k++) x.bx[k] = xv ? ldg64(xw + 16 * k) : make_uint2(0u, 0u);
-  const bool bmv = MIN && xv && tig < 2;
-  x.bml = bmv ? ldg32(xg + kImgQ8K4_BM + 4 * tig) : 0u;
-  x.bmh = bmv ? ldg32(xg + kImgQ8K4_BM + 4 * (2 + tig)) : 0u;
-  x.xd0 = v0 ? ldgf(xs0 + kImgQ8K4_D) : 0.0f;
-  x.xd1 = v1 ? ldgf(xs1 + kImgQ8K4_D) : 0.0f;
+  for (int k = 0; k < 8; k++) x.bx[k] = ldg64(blk + 256 * k + 8 * lane);
+  const uint2 bm = MIN && tig < 2 ? ldg64(blk + 2048 + 8 * lane) : make_uint2(0u, 0u);
+  x.bml = bm.x;
+  x.bmh = bm.y;
+  const float2 xd = __ldg(reinterpret_cast<const float2 *>(blk + 2304 + 8 * tig));
+  x.xd0 = xd.x;
+  x.xd1 = xd.y;
 }
 
 __device__ __forceinline__ void q4k_batch_block(const uint8_t *row0, const uint8_t *row1, int nbc, int b,
@@ -279,18 +281,15 @@ __global__ void __launch_bounds__(kBatchThreads, 1) gemv_batch_kernel(BParams P)
   const bool active = sg < nsg;
   const int nbc = P.nbc;
   static_assert(SB == 8, "the 8 sequences of a group are the MMA's N");
-  const int sx = sg * 8 + gid;                   // B: sequence of column gid
   const int sa = sg * 8 + 2 * tig, sb2 = sa + 1;  // D: sequences of this thread
-  const bool xv = sx < P.nseq, v0 = sa < P.nseq, v1 = sb2 < P.nseq;
-  const uint8_t *imx = P.img + (size_t)(xv ? sx : 0) * P.istride;
-  const uint8_t *im0 = P.img + (size_t)(v0 ? sa : 0) * P.istride;
-  const uint8_t *im1 = P.img + (size_t)(v1 ? sb2 : 0) * P.istride;
+  const uint8_t *img = P.img + (size_t)(active ? sg : 0) * kBImgBlock;  // block b at + b * nsg * kBImgBlock
+  const size_t bstride = (size_t)P.nsg * kBImgBlock;
   Q4Chain ch;
   // x of the first block; then always one block ahead (units run in the
   // order tile, chunk, so the block after a unit's last is the next chunk's
   // first: block ((c + 1) % nch) * nbc)
   Q4X xc;
-  q4x_load<FMT == Q4K>(imx, xv, im0, v0, im1, v1, xc);
+  if (active) q4x_load<FMT == Q4K>(img, xc);
   for (int u = 0; u < nunits; u++) {
     const int st = u % S, c = u % P.nch;
     if (!mbar_wait_bounded(&full[st], (u / S) & 1, P.err)) break;
@@ -308,9 +307,9 @@ __global__ void __launch_bounds__(kBatchThreads, 1) gemv_batch_kernel(BParams P)
       const int nxt = ((c + 1) % P.nch) * nbc;
 #pragma unroll 1
       for (int b = 0; b < nbc; b++) {
-        const size_t xo = (size_t)(b + 1 < nbc ? c * nbc + b + 1 : nxt) * kImgQ8K4;
+        const size_t xo = (size_t)(b + 1 < nbc ? c * nbc + b + 1 : nxt) * bstride;
         Q4X xn;
-        q4x_load<FMT == Q4K>(imx + xo, xv, im0 + xo, v0, im1 + xo, v1, xn);
+        q4x_load<FMT == Q4K>(img + xo, xn);
         if constexpr (FMT == Q4K) q4k_batch_block(row0, row1, nbc, b, xc, ch);
         else q6d_batch_block(row0, row1, b, xc, ch);
         xc = xn;
@@ -361,13 +360,13 @@ __global__ void __launch_bounds__(kBatchThreads, 1) gemv_batch_kernel(BParams P)
 // spans x sequences), in the class-major layout of the Q4_K image, which the
 // batched kernel reads for both formats.
 __global__ void __launch_bounds__(256) prep_q8k_batch(const float *__restrict__ x, size_t dim_in, size_t xstride,
-                                                      uint8_t *__restrict__ img, size_t istride) {
+                                                      uint8_t *__restrict__ img, int nsg) {
   pdl_trigger();
   __shared__ Q8KSpanSmem sm;
   const size_t span = blockIdx.x, s = blockIdx.y;
   const size_t e = span * kQK + threadIdx.x;
   const float v = e < dim_in ? x[s * xstride + e] : 0.0f;
-  q8k_span_write(v, img + s * istride + span * kImgQ8K4, nullptr, sm);
+  q8k_span_write(v, nullptr, nullptr, sm, img + bimg_block(span, (int)(s >> 3), nsg), (int)(s & 7));
 }
 
 using BatchFn = void (*)(BParams);
@@ -400,9 +399,11 @@ cudaError_t ensure_batch_attr(int device, BatchFn fn, int smem) {
 
 // Q4_K: a unit is 32 rows x the whole row. Q6_K (digit planes): 32 rows x
 // nbc consecutive blocks, nbc the largest divisor of the block count up to 4
-// (the planes of consecutive blocks are contiguous). Rows are padded to 64
-// bytes past a multiple of 128 in shared memory, so the eight rows x four
-// lanes of a 128-bit load hit distinct banks.
+// (the planes of consecutive blocks are contiguous). Shared-memory rows are
+// padded past a multiple of 128 bytes so a warp's 128-bit loads (eight rows
+// x four lanes) take the minimum four wavefronts: by 16 bytes for Q4_K
+// (lanes read 16 bytes at 32 tig of their row), by 64 for the Q6_K planes
+// (lanes read 16 bytes at 16 tig).
 BatchPlan batch_plan(int device, const unltd_weight_s &w) {
   BatchPlan p;
   const bool q4 = w.dtype == Q4K;
@@ -422,7 +423,7 @@ BatchPlan batch_plan(int device, const unltd_weight_s &w) {
     p.nch = (int)(w.nb / nbc);
     p.unit_bytes = nbc * kBatch6Block;
   }
-  p.ps = (int)round_up((size_t)p.unit_bytes, 128) + (q4 ? 32 : 64);
+  p.ps = (int)round_up((size_t)p.unit_bytes, 128) + (q4 ? 16 : 64);
   p.stage_bytes = (int)round_up((size_t)p.T * p.ps, 128);
   const int smem_max = max_smem_optin_b(device) - 1024;
   p.S = std::min(kBatchStages, (smem_max - kBatchHdr) / p.stage_bytes);
@@ -434,7 +435,9 @@ BatchPlan batch_plan(int device, const unltd_weight_s &w) {
 
 }  // namespace
 
-size_t gemv_batch_img_bytes(const unltd_weight_s &w) { return round_up(w.nb * (size_t)kImgQ8K4, 256); }
+size_t gemv_batch_img_bytes(const unltd_weight_s &w, int nseq) {
+  return w.nb * (size_t)((nseq + 7) / 8) * kBImgBlock;
+}
 
 int32_t gemv_batch_prepare(unltd_ctx ctx, unltd_weight_s *w) {
   if (w->dtype != Q6K || w->dev_b || w->dim_out == 0) return UNLTD_OK;
@@ -467,14 +470,14 @@ int32_t gemv_batch_launch(unltd_ctx ctx, const BatchGemvArgs &a) {
   if (!pl.fn) return set_error(UNLTD_ERR_UNSUPPORTED, "gemv_batch: rows too long for a shared-memory tile");
   if (w.dtype == Q6K && !w.dev_b) return set_error(UNLTD_ERR_INVALID_ARG, "gemv_batch: Q6_K weight not prepared");
   cudaStream_t st = ctx->stream;
-  const size_t istride = gemv_batch_img_bytes(w);
+  const int nsg = (a.nseq + 7) / 8;
   const uint8_t *img = a.img;
   if (!img) {
     if (!a.x) return set_error(UNLTD_ERR_INVALID_ARG, "gemv_batch: no x and no image");
-    if (ctx->scratch_bytes < istride * a.nseq)
+    if (ctx->scratch_bytes < gemv_batch_img_bytes(w, a.nseq))
       return set_error(UNLTD_ERR_INVALID_ARG, "gemv_batch: scratch not reserved");
     const dim3 grid((unsigned)w.nb, (unsigned)a.nseq);
-    prep_q8k_batch<<<grid, 256, 0, st>>>(a.x, w.dim_in, a.xstride, ctx->scratch, istride);
+    prep_q8k_batch<<<grid, 256, 0, st>>>(a.x, w.dim_in, a.xstride, ctx->scratch, nsg);
     cudaError_t e = cudaGetLastError();
     if (e != cudaSuccess) return cuda_error(e, "gemv_batch prep");
     ctx->launches += 1;
@@ -493,7 +496,7 @@ int32_t gemv_batch_launch(unltd_ctx ctx, const BatchGemvArgs &a) {
   P.stage_bytes = pl.stage_bytes;
   P.S = pl.S;
   P.img = img;
-  P.istride = a.img ? a.istride : istride;
+  P.nsg = a.img ? a.nsg : nsg;
   P.y = a.y;
   P.ystride = a.ystride;
   P.nseq = a.nseq;

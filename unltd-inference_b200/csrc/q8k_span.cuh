@@ -16,8 +16,11 @@ struct Q8KSpanSmem {
 };
 
 // v = element t (threadIdx.x) of the span. im4 / im6 (either may be null):
-// this span's Q4_K / Q6_K image. All 256 threads must call.
-__device__ __forceinline__ void q8k_span_write(float v, uint8_t *im4, uint8_t *im6, Q8KSpanSmem &s) {
+// this span's Q4_K / Q6_K image; imb (may be null): the span's batched image
+// (kBImgBlock, unltd_internal.cuh) of this sequence's group, sl = the
+// sequence's index in it. All 256 threads must call.
+__device__ __forceinline__ void q8k_span_write(float v, uint8_t *im4, uint8_t *im6, Q8KSpanSmem &s,
+                                               uint8_t *imb = nullptr, int sl = 0) {
   const int t = threadIdx.x;
   if (t < 16) s.hsum[t] = 0;
   // first strict argmax of |x|; NaN never wins (the reference's `ax > amax`)
@@ -61,11 +64,9 @@ __device__ __forceinline__ void q8k_span_write(float v, uint8_t *im4, uint8_t *i
     q = ni < 127 ? ni : 127;
     d = __fdiv_rn(1.0f, iscale);
   }
-  if (im4) {
-    // class-major (q4k_q8k_xpos); hsum[g] = sum of group g's q8 values
-    im4[q4k_q8k_xpos(t)] = (uint8_t)(int8_t)q;
-    atomicAdd(&s.hsum[t >> 5], q);
-  }
+  if (im4) im4[q4k_q8k_xpos(t)] = (uint8_t)(int8_t)q;  // class-major (q4k_q8k_xpos)
+  if (imb) imb[bimg_q8(t, sl)] = (uint8_t)(int8_t)q;
+  if (im4 || imb) atomicAdd(&s.hsum[t >> 5], q);      // hsum[g] = sum of group g's q8 values
   if (im6) {
     // element -> (lane j, half hh, run position ipos); word w = (ipos%8)/2 holds
     // run positions (2w, 2w+8 | 2w+1, 2w+9); masked copies A (bytes 0,1) and
@@ -81,9 +82,10 @@ __device__ __forceinline__ void q8k_span_write(float v, uint8_t *im4, uint8_t *i
     if (t == 0) *reinterpret_cast<float *>(im6 + kImgQ8K6_D) = d;
   }
   __syncthreads();
-  if (im4) {
-    if (t == 0) *reinterpret_cast<float *>(im4 + kImgQ8K4_D) = d;
-    if (t < 16) reinterpret_cast<int *>(im4 + kImgQ8K4_BS)[t] = s.hsum[t];
+  if (im4 || imb) {
+    if (t == 0 && im4) *reinterpret_cast<float *>(im4 + kImgQ8K4_D) = d;
+    if (t == 0 && imb) *reinterpret_cast<float *>(imb + bimg_d(sl)) = d;
+    if (t < 16 && im4) reinterpret_cast<int *>(im4 + kImgQ8K4_BS)[t] = s.hsum[t];
     if (t < 4) {  // the min term's B operand words (kImgQ8K4_BM)
       const int c = t >> 1, tg = t & 1;
       uint32_t bm = 0u;
@@ -93,15 +95,17 @@ __device__ __forceinline__ void q8k_span_write(float v, uint8_t *im4, uint8_t *i
         const int lo = ((g + 128) & 255) - 128, hi = (g - lo) >> 8;
         bm |= (uint32_t)((c == 0 ? lo : hi) & 0xFF) << (8 * i);
       }
-      reinterpret_cast<uint32_t *>(im4 + kImgQ8K4_BM)[t] = bm;
+      if (im4) reinterpret_cast<uint32_t *>(im4 + kImgQ8K4_BM)[t] = bm;
+      if (imb) *reinterpret_cast<uint32_t *>(imb + bimg_bm(sl, tg, c)) = bm;
     }
   }
 }
 
 // The same quantize_q8_k of one span held by ONE warp: lane l holds elements
 // 8l .. 8l+7 in v[0..7]. Warp shuffles only, no block barrier, so the warps
-// of a CTA quantize their spans concurrently.
-__device__ __forceinline__ void q8k_span_write_warp(const float (&v)[8], int lane, uint8_t *im4, uint8_t *im6) {
+// of a CTA quantize their spans concurrently. imb / sl as q8k_span_write.
+__device__ __forceinline__ void q8k_span_write_warp(const float (&v)[8], int lane, uint8_t *im4, uint8_t *im6,
+                                                    uint8_t *imb = nullptr, int sl = 0) {
   // first strict argmax of |x| (ties: lowest index); NaN never wins
   float a = -1.0f, val = 0.0f;
   int idx = 8 * lane;
@@ -141,22 +145,26 @@ __device__ __forceinline__ void q8k_span_write_warp(const float (&v)[8], int lan
 #pragma unroll
     for (int k = 0; k < 8; k++) q[k] = 0;
   }
-  if (im4) {
+  if (im4 || imb) {
     // class-major (q4k_q8k_xpos of e = 8 lane + k); group g = lane / 4
     const int g = lane >> 2;
     const int base = 128 * (g >> 2) + 4 * (g & 3) + (lane & 3);
     int hs = 0;
 #pragma unroll
     for (int k = 0; k < 8; k++) {
-      im4[base + 16 * k] = (uint8_t)(int8_t)q[k];
+      if (im4) im4[base + 16 * k] = (uint8_t)(int8_t)q[k];
+      if (imb) imb[bimg_q8(8 * lane + k, sl)] = (uint8_t)(int8_t)q[k];
       hs += q[k];
     }
     hs += __shfl_xor_sync(0xffffffffu, hs, 1);
     hs += __shfl_xor_sync(0xffffffffu, hs, 2);
-    int *bs = reinterpret_cast<int *>(im4 + kImgQ8K4_BS);
-    if ((lane & 3) == 0) bs[g] = hs;
-    if (lane < 8) bs[8 + lane] = 0;
-    if (lane == 0) *reinterpret_cast<float *>(im4 + kImgQ8K4_D) = d;
+    if (im4) {
+      int *bs = reinterpret_cast<int *>(im4 + kImgQ8K4_BS);
+      if ((lane & 3) == 0) bs[g] = hs;
+      if (lane < 8) bs[8 + lane] = 0;
+      if (lane == 0) *reinterpret_cast<float *>(im4 + kImgQ8K4_D) = d;
+    }
+    if (imb && lane == 0) *reinterpret_cast<float *>(imb + bimg_d(sl)) = d;
     // the min term's B operand words (kImgQ8K4_BM): lane 2c + t packs the
     // low (c = 0) or high (c = 1) bytes of group sums 4t .. 4t + 3
     uint32_t bm = 0u;
@@ -166,7 +174,8 @@ __device__ __forceinline__ void q8k_span_write_warp(const float (&v)[8], int lan
       const int lo = ((gs + 128) & 255) - 128, hi = (gs - lo) >> 8;
       bm |= (uint32_t)(((lane >> 1) & 1 ? hi : lo) & 0xFF) << (8 * i);
     }
-    if (lane < 4) reinterpret_cast<uint32_t *>(im4 + kImgQ8K4_BM)[lane] = bm;
+    if (lane < 4 && im4) reinterpret_cast<uint32_t *>(im4 + kImgQ8K4_BM)[lane] = bm;
+    if (lane < 4 && imb) *reinterpret_cast<uint32_t *>(imb + bimg_bm(sl, lane & 1, (lane >> 1) & 1)) = bm;
   }
   if (im6) {
 #pragma unroll

@@ -151,8 +151,8 @@ struct BatchGemvArgs {
   const unltd_weight_s *w;
   const float *x = nullptr;     // [nseq][xstride] f32 (null: img is given)
   size_t xstride = 0;
-  const uint8_t *img = nullptr;  // non-null: the x images, sequence s at img + s * istride
-  size_t istride = 0;
+  const uint8_t *img = nullptr;  // non-null: the batched x images (kBImgBlock per span and sequence group)
+  int nsg = 0;                   // sequence groups the images hold (their stride)
   float *y = nullptr;           // [nseq][ystride] (may be null with argmax)
   size_t ystride = 0;
   int nseq = 1;
@@ -162,8 +162,8 @@ struct BatchGemvArgs {
   size_t tstride = 1;                 // token of sequence s at token[s * tstride]
 };
 int32_t gemv_batch_launch(unltd_ctx ctx, const BatchGemvArgs &a);
-// Bytes of one sequence's x image for w (the stride of the batched images).
-size_t gemv_batch_img_bytes(const unltd_weight_s &w);
+// Bytes of the batched x images of nseq sequences for w.
+size_t gemv_batch_img_bytes(const unltd_weight_s &w, int nseq);
 bool gemv_batch_supported(int device, const unltd_weight_s &w);
 cudaError_t gemv_batch_prewarm(int device);
 // Makes w's batched-GEMV operands (Q6_K digit planes) if w needs them and

@@ -105,6 +105,25 @@ __host__ __device__ inline int q6_q8k_byte(int j, int hh, int w, int ab, int bpo
   return 128 * (2 * hh + (w >> 1)) + 16 * j + 4 * (2 * (w & 1) + ab) + bpos;
 }
 
+// Batched x images (batch decode): one image per (span, group of 8
+// sequences), kBImgBlock bytes, the Q8_K values laid out as the batched
+// GEMV's MMA B fragments so a lane's operand is one coalesced 8-byte load:
+//   [0, 2048)    class k at 256 k; lane (sl, t) = 4 sl + t at 8 lane: the
+//                q8 words of groups 2t and 2t + 1 (byte i: element 32 g +
+//                8 i + k) of sequence sl of the group;
+//   [2048, 2304) lane 4 sl + t (t < 2): the balanced low / high bytes of the
+//                group sums 4t .. 4t + 3 of sequence sl (the Q4_K min term);
+//   [2304, 2336) the eight sequences' d.
+constexpr int kBImgBlock = 2368;
+__host__ __device__ inline size_t bimg_block(size_t span, int sg, int nsg) {
+  return (span * (size_t)nsg + (size_t)sg) * kBImgBlock;
+}
+__host__ __device__ inline int bimg_q8(int e, int sl) {
+  return (e & 7) * 256 + (sl * 4 + (e >> 6)) * 8 + ((e >> 5) & 1) * 4 + ((e >> 3) & 3);
+}
+__host__ __device__ inline int bimg_bm(int sl, int t, int c) { return 2048 + (sl * 4 + t) * 8 + c * 4; }
+__host__ __device__ inline int bimg_d(int sl) { return 2304 + 4 * sl; }
+
 // Q6_K rows of more than 16 blocks (a multiple of 16) are stored as chunks of
 // 16 blocks, each laid out like a 16-block row ([ql][qh][scales][d]), so a
 // 16-block slice of a long row is one contiguous 3360-byte range (the
