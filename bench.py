@@ -312,7 +312,36 @@ def decode_batch_bench(m, cfg, st, pos0, n_seq, n_steps, profile_region=False):
     return out
 
 
-def decode_bench(n_tokens, with_cpu, rank=0, world=1, dist=None, profile_region=False, batch=32, profile_batch=False):
+def prefill_bench(m, cfg, st, pos0, n):
+    """A prompt of n seeded tokens after the 2048-position state through
+    unltd_qwen35_prefill (32-token chunks, each weight read once per chunk;
+    the same bits as the token-by-token unltd_qwen35_feed). Device-timed on
+    the session stream."""
+    import torch
+
+    s = m.session(pos0 + n + 40)
+    s.set_state(pos0, st["conv"], st["gdn"], st["k"], st["v"])
+    prompt = [int(t) for t in np.random.default_rng(7).integers(0, cfg["vocab"], n + 32)]
+    s.prefill(prompt[:32])  # warm-up: workspace, batched operands
+    ext = torch.cuda.ExternalStream(s.info()["stream"])
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    torch.cuda.synchronize()
+    t0 = time.perf_counter()
+    e0.record(ext)
+    s.prefill(prompt[32:])
+    e1.record(ext)
+    torch.cuda.synchronize()
+    wall = time.perf_counter() - t0
+    ms = e0.elapsed_time(e1)
+    s.close()
+    return {"workload": f"qwen35_9b_synthetic_prefill_{n}_tokens_after_ctx2048", "tokens": n,
+            "tok_s": round(n / (ms * 1e-3), 1), "ms": round(ms, 3), "e2e_tok_s": round(n / wall, 1),
+            "arithmetic": "Q8K_EXACT projections batched over 32-token chunks; state and next token bit-identical "
+                          "to the token-by-token prompt"}
+
+
+def decode_bench(n_tokens, with_cpu, rank=0, world=1, dist=None, profile_region=False, batch=32, profile_batch=False,
+                 prefill=256):
     """BASELINE configs 3 and 4: greedy decode of the synthetic 9B-class hybrid
     model from a 2048-position context through unltd_qwen35_decode, on one GPU
     or tensor-parallel over `world` GPUs (one process each). Device-timed on
@@ -376,6 +405,8 @@ def decode_bench(n_tokens, with_cpu, rank=0, world=1, dist=None, profile_region=
         "distinct_tokens": len(set(int(t) for t in toks)),
     }
     s.close()
+    if world == 1 and prefill > 0:
+        out["prefill"] = prefill_bench(m, cfg, st, pos0, prefill)
     if world == 1 and batch > 1:
         out["batch"] = 1
         out["batch%d" % batch] = decode_batch_bench(m, cfg, st, pos0, batch, max(4, n_tokens // 4), profile_batch)

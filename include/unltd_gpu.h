@@ -300,6 +300,14 @@ int32_t unltd_qwen35_session_get_state(unltd_qwen35_session s, float *const *con
 /* Teacher-forced steps over a prompt; *next_token (nullable) = the greedy
  * token after the last one. */
 int32_t unltd_qwen35_feed(unltd_qwen35_session s, const uint32_t *tokens, int32_t n, uint32_t *next_token);
+/* The same prompt as a batched prefill (one GPU, one-sequence session): the
+ * prompt in chunks of up to 32 tokens, every projection one batched GEMV per
+ * chunk (each weight read once per chunk), attention batched over the chunk's
+ * tokens, the recurrence token by token. The state, the last token's logits
+ * and hidden state, and *next_token are the bits unltd_qwen35_feed gives
+ * (the reference prefills token by token, qwen35_forward.rs:8-12,
+ * greedy.rs:55-65). */
+int32_t unltd_qwen35_prefill(unltd_qwen35_session s, const uint32_t *tokens, int32_t n, uint32_t *next_token);
 /* Greedy decode of n_steps tokens: step 0 consumes `token`, step i consumes
  * tokens_out[i-1]; tokens_out[i] = argmax of step i's logits. */
 int32_t unltd_qwen35_decode(unltd_qwen35_session s, uint32_t token, int32_t n_steps, uint32_t *tokens_out);

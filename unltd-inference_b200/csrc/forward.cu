@@ -56,11 +56,13 @@ __device__ __forceinline__ T *seq_ptr(T *p, size_t off) {
 __device__ __forceinline__ size_t seq_off(size_t ss) { return (size_t)blockIdx.z * ss; }
 // A batch session's producers write the batched x images (shared by the
 // sequences, kBImgBlock per span and group of 8 sequences): the block of
-// this CTA's sequence for `span`, or null without a batched image.
-__device__ __forceinline__ uint8_t *seq_bimg(uint8_t *bimg, int nsg, int span) {
-  return bimg ? bimg + bimg_block((size_t)span, (int)(blockIdx.z >> 3), nsg) : nullptr;
+// this CTA's sequence (seq0 + blockIdx.z; a prefill launches the per-token
+// kernels one token at a time with seq0 = the token) for `span`, or null
+// without a batched image.
+__device__ __forceinline__ uint8_t *seq_bimg(uint8_t *bimg, int nsg, int seq0, int span) {
+  return bimg ? bimg + bimg_block((size_t)span, (int)((seq0 + blockIdx.z) >> 3), nsg) : nullptr;
 }
-__device__ __forceinline__ int seq_sl() { return (int)(blockIdx.z & 7); }
+__device__ __forceinline__ int seq_sl(int seq0) { return (int)((seq0 + blockIdx.z) & 7); }
 
 // ---- reductions -----------------------------------------------------------
 // Sum of a and b over the block; every thread receives the same values.
@@ -178,7 +180,7 @@ __global__ void __launch_bounds__(256) norm_quant_kernel(NormArgs p) {
   if (p.r_out) p.r_out[e] = r;
   const float xn = __fmul_rn(__fmul_rn(r, scale), p.w[e]);
   q8k_span_write(xn, p.img4 ? p.img4 + (size_t)span * kImgQ8K4 : nullptr,
-                 p.img6 ? p.img6 + (size_t)span * kImgQ8K6 : nullptr, sm, seq_bimg(p.bimg, p.nsg, span), seq_sl());
+                 p.img6 ? p.img6 + (size_t)span * kImgQ8K6 : nullptr, sm, seq_bimg(p.bimg, p.nsg, 0, span), seq_sl(0));
   if (p.key && span == 0 && t == 0) {
     *p.key = 0ull;
     *p.done = 0u;
@@ -187,10 +189,10 @@ __global__ void __launch_bounds__(256) norm_quant_kernel(NormArgs p) {
 
 // ---- token embedding: one Q4_K row, dequantized (min_forward.rs:160-184) --
 __global__ void embed_q4k_kernel(const uint8_t *table, size_t stride, size_t nb, const uint32_t *token,
-                                 uint32_t vocab, float *x, int n, int *err, size_t ss) {
+                                 uint32_t vocab, float *x, int n, int *err, size_t ss, size_t tss) {
   pdl_trigger();
   pdl_wait();
-  token = seq_ptr(token, seq_off(ss));
+  token = seq_ptr(token, seq_off(tss));
   x = seq_ptr(x, seq_off(ss));
   uint32_t t = *token;
   if (t >= vocab) {
@@ -216,7 +218,7 @@ __global__ void __launch_bounds__(256) swiglu_quant_kernel(const float *g, const
   const float t = g[e];
   const float s = __fdiv_rn(t, __fadd_rn(1.0f, exp_cr(-t)));
   q8k_span_write(__fmul_rn(s, u[e]), img4 ? img4 + (size_t)span * kImgQ8K4 : nullptr,
-                 img6 ? img6 + (size_t)span * kImgQ8K6 : nullptr, sm, seq_bimg(bimg, nsg, span), seq_sl());
+                 img6 ? img6 + (size_t)span * kImgQ8K6 : nullptr, sm, seq_bimg(bimg, nsg, 0, span), seq_sl(0));
 }
 
 // ---- recurrent layer between the projections (qwen35_forward.rs:390-508) --
@@ -236,7 +238,7 @@ struct RecrArgs {
   uint8_t *img4, *img6;
   size_t ss = 0;  // bytes between the sequences' arenas
   uint8_t *bimg = nullptr;  // batch session: the batched x images (then img4 = img6 = null)
-  int nsg = 0;
+  int nsg = 0, seq0 = 0;    // the image slot of this launch's sequence z is seq0 + z
 };
 
 // One CTA per (v-head h, quarter of its columns), one thread per channel of
@@ -302,7 +304,7 @@ __device__ __forceinline__ float gdn_dot(const float (&st)[RW], const float *xw,
 // (quantize_q8_k) by warp 0. Thread j takes column j of both heads.
 template <int HD>
 __device__ __noinline__ void gated_norm_span(const float *y, const float *z, const float *ssm_norm, float eps,
-                                             uint8_t *img4, uint8_t *img6, int span, uint8_t *imb) {
+                                             uint8_t *img4, uint8_t *img6, int span, uint8_t *imb, int sl) {
   static_assert(HD == 128, "a span holds two heads of 128");
   __shared__ double red2[2][HD / 32];
   __shared__ float so[256];
@@ -356,7 +358,7 @@ __device__ __noinline__ void gated_norm_span(const float *y, const float *z, con
 #pragma unroll
     for (int k = 0; k < 8; k++) v[k] = so[8 * lane + k];
     q8k_span_write_warp(v, lane, img4 ? img4 + (size_t)span * kImgQ8K4 : nullptr,
-                        img6 ? img6 + (size_t)span * kImgQ8K6 : nullptr, imb, seq_sl());
+                        img6 ? img6 + (size_t)span * kImgQ8K6 : nullptr, imb, sl);
   }
 }
 
@@ -524,8 +526,151 @@ __global__ void __launch_bounds__(HD) recr_mid_kernel(RecrArgs a) {
   __syncthreads();
   if (s_last) {
     __threadfence();
-    gated_norm_span<HD>(a.y, a.proj + a.z_off, a.ssm_norm, a.eps, a.img4, a.img6, span, seq_bimg(a.bimg, a.nsg, span));
+    gated_norm_span<HD>(a.y, a.proj + a.z_off, a.ssm_norm, a.eps, a.img4, a.img6, span,
+                        seq_bimg(a.bimg, a.nsg, a.seq0, span), seq_sl(a.seq0));
   }
+}
+
+// The recurrent layer for a prefill chunk of T tokens in one launch: each
+// CTA (v-head h, quarter of its columns) keeps its state slice in registers
+// and runs recr_mid_kernel's step for tokens 0 .. T-1 in order. The conv
+// window of token t (position pos + t) takes the rows of earlier chunk tokens
+// from their projections (pss bytes apart) and older rows from the ring,
+// which this kernel does not write (CTAs of other heads read the same q/k
+// channels; prefill_ring_kernel updates it after the launch). The gated norm of
+// token t's span runs in the span's last CTA for that token (a counter per
+// token and span). The same operations per token as recr_mid_kernel.
+struct RecrChunkArgs {
+  RecrArgs r;   // r.proj / r.y: token 0's; r.pos: the session's position (the chunk's first)
+  size_t pss;   // bytes between consecutive tokens' activations
+  int T;
+  int nspan;    // spans of y: the counters of token t at r.span_ctr + t * nspan
+};
+
+template <int HD>
+__global__ void __launch_bounds__(HD) recr_chunk_kernel(RecrChunkArgs c) {
+  pdl_trigger();
+  __shared__ float qs[HD], ks[HD];
+  __shared__ float gdn_fb[kGdnCols * HD];
+  __shared__ double red[2 * HD / 32];
+  __shared__ float s_f[2];
+  __shared__ float vs[kGdnCols];
+  __shared__ unsigned s_last;
+  pdl_wait();
+  const RecrArgs &a = c.r;
+  const int h = blockIdx.x, quarter = blockIdx.y, j = threadIdx.x;
+  const int qk = h % a.nqk;
+  const int pos0 = *a.pos, K = a.K;
+  const int c0 = quarter * kGdnCols;
+  const int chq = qk * HD + j, chk = a.nqk * HD + qk * HD + j;
+  const int chv = 2 * a.nqk * HD + h * HD + c0 + (j & (kGdnCols - 1));
+  const int jc = j >> 2, w = j & 3;
+  constexpr int RW = HD / 4;
+  float *S = a.state + (size_t)h * HD * HD + c0 + jc;
+  float st[RW];
+#pragma unroll
+  for (int ii = 0; ii < RW; ii++) st[ii] = S[(size_t)(RW * w + ii) * HD];
+  const float dtb = a.dt_bias[h], ssa = a.ssm_a[h];
+  auto proj_of = [&](int t) { return reinterpret_cast<const float *>(reinterpret_cast<const uint8_t *>(a.proj) + (size_t)t * c.pss); };
+  const int span = (h * HD) >> 8;
+#pragma unroll 1
+  for (int t = 0; t < c.T; t++) {
+    const float *pr = proj_of(t);
+    const int pos = pos0 + t;
+    const float beta_raw = pr[a.beta_off + h], alpha = pr[a.alpha_off + h];
+    // depthwise conv over [window rows, current qkv] (kernels.rs:265-310), silu
+    auto conv = [&](int ch) {
+      float sacc = 0.0f;
+      for (int tau = 0; tau < K; tau++) {
+        float xv;
+        if (tau == K - 1) {
+          xv = pr[ch];
+        } else {
+          const int qp = pos - (K - 1) + tau;  // the row's position
+          xv = qp >= pos0 ? proj_of(qp - pos0)[ch] : a.ring[(size_t)((pos + tau) % K) * a.dconv + ch];
+        }
+        sacc = __fadd_rn(sacc, __fmul_rn(xv, a.convw[(size_t)ch * K + tau]));
+      }
+      return sacc;
+    };
+    float q = silu_f(conv(chq)), k = silu_f(conv(chk)), v = 0.0f;
+    if (j < kGdnCols) v = silu_f(conv(chv));
+    // l2_norm_rows of q and k (kernels.rs:236-252)
+    qs[j] = q;
+    ks[j] = k;
+    double Sq = (double)__fmul_rn(q, q), Sk = (double)__fmul_rn(k, k);
+    block_sum2<HD>(Sq, Sk, red);
+    float fq, fk;
+    const bool okq = resolve_sum(Sq, Sq, HD, ToF32{}, &fq);
+    const bool okk = resolve_sum(Sk, Sk, HD, ToF32{}, &fk);
+    if (!okq || !okk) {
+      __syncthreads();
+      if (j < 2 && !(j == 0 ? okq : okk)) {
+        const float *src = j == 0 ? qs : ks;
+        double s2 = 0.0;
+#pragma unroll 1
+        for (int i = 0; i < HD; i++) s2 = __dadd_rn(s2, (double)__fmul_rn(src[i], src[i]));
+        s_f[j] = (float)s2;
+      }
+      __syncthreads();
+      if (!okq) fq = s_f[0];
+      if (!okk) fk = s_f[1];
+    }
+    q = __fmul_rn(q, __fdiv_rn(1.0f, fmaxf(__fsqrt_rn(fq), a.eps)));
+    k = __fmul_rn(k, __fdiv_rn(1.0f, fmaxf(__fsqrt_rn(fk), a.eps)));
+    __syncthreads();
+    qs[j] = q;
+    ks[j] = k;
+    const float beta = sigmoid_f(beta_raw);
+    const float gate = __fmul_rn(softplus_f(__fadd_rn(alpha, dtb)), ssa);
+    const float g = exp_cr(gate);
+    if (j < kGdnCols) vs[j] = v;
+    __syncthreads();
+    // gdn_fused_step (as recr_mid_kernel)
+#pragma unroll
+    for (int ii = 0; ii < RW; ii++) st[ii] = __fmul_rn(st[ii], g);
+    const float dk = gdn_dot<RW>(st, ks + RW * w, ks, gdn_fb + jc * HD, w);
+    const float d = __fmul_rn(__fsub_rn(vs[jc], dk), beta);
+#pragma unroll
+    for (int ii = 0; ii < RW; ii++) st[ii] = __fadd_rn(st[ii], __fmul_rn(ks[RW * w + ii], d));
+    const float dq = gdn_dot<RW>(st, qs + RW * w, qs, gdn_fb + jc * HD, w);
+    float *yt = reinterpret_cast<float *>(reinterpret_cast<uint8_t *>(a.y) + (size_t)t * c.pss);
+    if (w == 0) yt[h * HD + c0 + jc] = __fmul_rn(dq, __fdiv_rn(1.0f, __fsqrt_rn((float)HD)));
+    // the span's last CTA for this token runs its gated norm
+    unsigned *ctr = a.span_ctr + (size_t)t * c.nspan;
+    __threadfence();
+    __syncthreads();
+    if (j == 0) {
+      const unsigned n = (256 / HD) * gridDim.y;
+      const unsigned prev = atomicAdd(ctr + span, 1u);
+      s_last = prev == n - 1;
+      if (prev == n - 1) ctr[span] = 0u;
+    }
+    __syncthreads();
+    if (s_last) {
+      __threadfence();
+      gated_norm_span<HD>(yt, pr + a.z_off, a.ssm_norm, a.eps, nullptr, nullptr, span,
+                          seq_bimg(a.bimg, a.nsg, t, span), t & 7);
+    }
+    __syncthreads();
+  }
+#pragma unroll
+  for (int ii = 0; ii < RW; ii++) S[(size_t)(RW * w + ii) * HD] = st[ii];
+}
+
+// The conv windows after a prefill chunk: the chunk's last K positions'
+// qkv rows, each in its ring slot (pos + K - 1) % K, as the one-token steps
+// leave them. One thread per (position, channel).
+__global__ void prefill_ring_kernel(const float *proj, size_t pss, int T, float *ring, int dconv, int K,
+                                    const int *pos) {
+  pdl_trigger();
+  pdl_wait();
+  const int t0 = max(0, T - K), nrow = T - t0;
+  const int i = blockIdx.x * blockDim.x + threadIdx.x;
+  if (i >= nrow * dconv) return;
+  const int t = t0 + i / dconv, ch = i % dconv;
+  const float *pr = reinterpret_cast<const float *>(reinterpret_cast<const uint8_t *>(proj) + (size_t)t * pss);
+  ring[(size_t)((*pos + t + K - 1) % K) * dconv + ch] = pr[ch];
 }
 
 // ---- full-attention layer (qwen35_forward.rs:584-686) ----------------------
@@ -545,9 +690,10 @@ struct AttnArgs {
   const int *pos;
   int nh, nkv, n_rot, nrp, ctx, nsplit;
   float eps, kq_scale;
-  size_t ss = 0;  // bytes between the sequences' arenas
+  size_t ss = 0;     // bytes between the sequences' arenas
+  size_t kv_ss = 0;  // the same for the caches (0: a prefill chunk's tokens share one cache)
   uint8_t *bimg = nullptr;  // batch session: the batched x images (then img4 = img6 = null)
-  int nsg = 0;
+  int nsg = 0, seq0 = 0;    // the image slot of this launch's sequence z is seq0 + z
 };
 
 // This CTA's sequence's copies of the per-sequence buffers.
@@ -556,8 +702,8 @@ __device__ __forceinline__ void attn_at_seq(AttnArgs &a) {
   a.qk = seq_ptr(a.qk, so);
   a.v = seq_ptr(a.v, so);
   a.q = seq_ptr(a.q, so);
-  a.kcache = seq_ptr(a.kcache, so);
-  a.vcache = seq_ptr(a.vcache, so);
+  a.kcache = seq_ptr(a.kcache, seq_off(a.kv_ss));
+  a.vcache = seq_ptr(a.vcache, seq_off(a.kv_ss));
   a.scores = seq_ptr(a.scores, so);
   a.part = seq_ptr(a.part, so);
   a.img4 = seq_ptr(a.img4, so);
@@ -911,7 +1057,8 @@ __global__ void __launch_bounds__(256) attn_combine_quant_kernel(AttnArgs a) {
   }
   const float gate = a.qk[(size_t)h * 2 * HDV + HDV + c];
   q8k_span_write(__fmul_rn(attn, sigmoid_f(gate)), a.img4 ? a.img4 + (size_t)span * kImgQ8K4 : nullptr,
-                 a.img6 ? a.img6 + (size_t)span * kImgQ8K6 : nullptr, sm, seq_bimg(a.bimg, a.nsg, span), seq_sl());
+                 a.img6 ? a.img6 + (size_t)span * kImgQ8K6 : nullptr, sm, seq_bimg(a.bimg, a.nsg, a.seq0, span),
+                 seq_sl(a.seq0));
 }
 
 // greedy token from the cross-GPU maximum of the argmax keys
@@ -920,6 +1067,23 @@ __global__ void key_to_token_kernel(const unsigned long long *key, uint32_t *tok
   pdl_trigger();
   pdl_wait();
   *token = 0xffffffffu - (uint32_t)(*key & 0xffffffffull);
+}
+
+// A prefill chunk of T tokens: token t of the chunk sits at position
+// *pos + t (the session's position before the chunk).
+__global__ void prefill_begin_kernel(const int *pos, int *lane_pos, size_t lane_ss, int T) {
+  pdl_trigger();
+  pdl_wait();
+  const int t = threadIdx.x;
+  if (t < T) *reinterpret_cast<int *>(reinterpret_cast<uint8_t *>(lane_pos) + (size_t)t * lane_ss) = *pos + t;
+}
+// ... and after it: the session's position advances by T; with the LM head,
+// its current token becomes the greedy token after the chunk's last token.
+__global__ void prefill_end_kernel(int *pos, int T, uint32_t *cur_token, const uint32_t *last) {
+  pdl_trigger();
+  pdl_wait();
+  *pos += T;
+  if (last) *cur_token = *last;
 }
 
 // token bookkeeping at the end of a step
@@ -1019,6 +1183,20 @@ struct unltd_qwen35_session_s {
   uint8_t *arena = nullptr;
   uint8_t *bimg = nullptr;  // the batched x images (n_seq > 1)
   int nsg = 0;
+  // prefill (unltd_qwen35_prefill): kPrefillLanes activation lanes (a
+  // chunk's tokens), made on first use; the state stays the session's
+  struct Prefill {
+    size_t ss = 0;
+    uint8_t *arena = nullptr;
+    float *X = nullptr, *R = nullptr, *T = nullptr, *F = nullptr, *proj = nullptr, *Y = nullptr, *FF = nullptr;
+    float *q = nullptr, *scores = nullptr, *logits = nullptr;
+    double2 *part = nullptr;
+    int *pos = nullptr;
+    uint32_t *tok = nullptr;  // the chunk's tokens, contiguous; then the LM head's
+    uint8_t *bimg = nullptr;
+    unsigned *span_ctr = nullptr;  // the recurrent chunk kernel's counters: token t at + t * nspan
+    int nspan = 0;
+  } pf;
   std::vector<int> seq_pos;
   // activations
   float *X = nullptr, *R = nullptr, *T = nullptr, *F = nullptr;
@@ -1468,7 +1646,7 @@ int32_t enqueue_step(unltd_qwen35_session s) {
   };
   chk(launch_pdl(embed_q4k_kernel, dim3(d.n / 256, 1, nz), dim3(256), 0, st, (const uint8_t *)m->embd->dev,
                  m->embd->row_stride, m->embd->nb, (const uint32_t *)s->cur_token, (uint32_t)d.vocab, s->X, d.n,
-                 s->ctx->err, s->ss),
+                 s->ctx->err, s->ss, s->ss),
       "embed");
   bool down_sent = false;  // the previous layer's down GEMV sent its rows to the peers
   for (int il = 0; il < d.n_layer; il++) {
@@ -1533,6 +1711,7 @@ int32_t enqueue_step(unltd_qwen35_session s) {
       a.eps = d.eps;
       a.kq_scale = d.kq_scale;
       a.ss = s->ss;
+      a.kv_ss = s->ss;
       a.bimg = s->bimg;
       a.nsg = s->nsg;
       const dim3 sg(d.nkvl, (s->ctx_len + 31) / 32, nz), vg(d.nkvl, s->nsplit, nz);
@@ -1628,6 +1807,235 @@ int32_t run_step(unltd_qwen35_session s) {
     return cuda_error(cudaGraphLaunch(s->graph, s->ctx->stream), "qwen35: graph launch");
   }
   return enqueue_step(s);
+}
+
+constexpr int kPrefillLanes = 32;
+constexpr int kPrefillNsg = kPrefillLanes / 8;
+
+// The prefill workspace: the activation buffers of kPrefillLanes tokens.
+int32_t prefill_alloc(unltd_qwen35_session s) {
+  if (s->pf.arena) return UNLTD_OK;
+  unltd_qwen35 m = s->m;
+  const Derived &d = m->d;
+  auto &P = s->pf;
+  struct Slot {
+    void **p;
+    size_t bytes, off;
+  };
+  std::vector<Slot> sl;
+  size_t off = 0;
+  auto add = [&](void **p, size_t bytes) {
+    off = round_up(off, 256);
+    sl.push_back({p, bytes, off});
+    off += std::max<size_t>(bytes, 16);
+  };
+  const size_t n = (size_t)d.n * 4;
+  add((void **)&P.X, n);
+  add((void **)&P.R, n);
+  add((void **)&P.T, n);
+  add((void **)&P.F, n);
+  add((void **)&P.proj, m->proj_rows * 4);
+  add((void **)&P.Y, n);
+  add((void **)&P.FF, 2 * (size_t)d.nffl * 4);
+  add((void **)&P.q, (size_t)d.nhl * d.hdv * 4);
+  add((void **)&P.scores, (size_t)d.nhl * s->ctx_len * 4);
+  add((void **)&P.part, (size_t)d.nhl * s->nsplit * d.hdv * sizeof(double2));
+  add((void **)&P.logits, (size_t)(d.v1 - d.v0) * 4);
+  add((void **)&P.pos, 4);
+  P.ss = round_up(off, 4096);
+  const size_t spans = (size_t)std::max(d.n, d.nff) / 256;
+  P.nspan = d.nvl * d.hd / 256 + 1;
+  const size_t img_bytes = spans * kPrefillNsg * kBImgBlock, ctr_bytes = (size_t)kPrefillLanes * P.nspan * 4;
+  const size_t extra = kPrefillLanes * 4 + img_bytes + ctr_bytes;
+  cudaError_t e = cudaMalloc(&P.arena, P.ss * kPrefillLanes + extra);
+  if (e == cudaSuccess) e = cudaMemset(P.arena, 0, P.ss * kPrefillLanes + extra);
+  if (e != cudaSuccess) {
+    if (P.arena) cudaFree(P.arena);
+    P.arena = nullptr;
+    return cuda_error(e, "qwen35_prefill: workspace");
+  }
+  for (auto &x : sl) *x.p = P.arena + x.off;
+  P.tok = reinterpret_cast<uint32_t *>(P.arena + P.ss * kPrefillLanes);
+  P.bimg = P.arena + P.ss * kPrefillLanes + kPrefillLanes * 4;
+  P.span_ctr = reinterpret_cast<unsigned *>(P.bimg + img_bytes);
+  s->bufs.push_back(P.arena);
+  // the batched GEMV's operands of the Q6_K projections, its kernels' attributes
+  std::vector<unltd_weight_s *> ws{m->output};
+  for (const Layer &L : m->layers) {
+    ws.insert(ws.end(), L.in.w.begin(), L.in.w.end());
+    ws.insert(ws.end(), L.gate_up.w.begin(), L.gate_up.w.end());
+    ws.push_back(L.out);
+    ws.push_back(L.down);
+  }
+  int32_t rc = cuda_error(gemv_batch_prewarm(m->ctx->device), "batched GEMV attributes");
+  for (auto *w : ws)
+    if (!rc) rc = gemv_batch_prepare(m->ctx, w);
+  return rc;
+}
+
+// Enqueue one prefill chunk of T tokens (already in pf.tok): the tokens'
+// projections as batched GEMVs (one pass over every weight for the chunk),
+// the norms, SwiGLU and attention batched over the tokens (attention shares
+// the session's cache: token t attends to positions <= its own, whose K/V
+// rows the chunk's attn_pre wrote first), the recurrent kernel token by token
+// on the session's state. Every token's arithmetic is that of a decode step,
+// so the state after the chunk, and with `head` the greedy token after it,
+// are the bits the one-token steps give. Without `head` the LM head is
+// skipped (a prompt's earlier chunks need no logits).
+int32_t enqueue_prefill(unltd_qwen35_session s, int T, bool head) {
+  unltd_qwen35 m = s->m;
+  const Derived &d = m->d;
+  auto &P = s->pf;
+  cudaStream_t st = s->ctx->stream;
+  int32_t rc = UNLTD_OK;
+  const unsigned nz = (unsigned)T;
+  const size_t pss = P.ss;
+  auto chk = [&](cudaError_t e, const char *what) {
+    if (!rc) rc = cuda_error(e, what);
+  };
+  auto lane = [&](auto *p, int t) {
+    return reinterpret_cast<decltype(p)>(reinterpret_cast<uint8_t *>(p) + (size_t)t * pss);
+  };
+  auto norm = [&](const float *a, const float *b, float *r_out, const float *w) {
+    NormArgs p{a, b, r_out, w, d.n, d.eps, nullptr, nullptr, nullptr, nullptr};
+    p.ss = pss;
+    p.bimg = P.bimg;
+    p.nsg = kPrefillNsg;
+    chk(launch_pdl(norm_quant_kernel, dim3(d.n / 256, 1, nz), dim3(256), 0, st, p), "prefill norm");
+  };
+  auto gemv = [&](const unltd_weight_s *w, float *y) {
+    BatchGemvArgs b{w};
+    b.img = P.bimg;
+    b.nsg = kPrefillNsg;
+    b.y = y;
+    b.ystride = pss / 4;
+    b.nseq = T;
+    if (!rc) rc = gemv_batch_launch(s->ctx, b);
+  };
+  auto norm_proj = [&](const float *a, const float *b, float *r_out, const float *w, const Proj &p, float *out) {
+    norm(a, b, r_out, w);
+    for (size_t i = 0; i < p.w.size(); i++) gemv(p.w[i], out + p.off[i]);
+  };
+  chk(launch_pdl(prefill_begin_kernel, dim3(1), dim3(32), 0, st, (const int *)s->pos, P.pos, pss, T), "prefill");
+  chk(launch_pdl(embed_q4k_kernel, dim3(d.n / 256, 1, nz), dim3(256), 0, st, (const uint8_t *)m->embd->dev,
+                 m->embd->row_stride, m->embd->nb, (const uint32_t *)P.tok, (uint32_t)d.vocab, P.X, d.n,
+                 s->ctx->err, pss, (size_t)4),
+      "prefill embed");
+  for (int il = 0; il < d.n_layer; il++) {
+    const Layer &L = m->layers[il];
+    if (il == 0) norm_proj(P.X, nullptr, nullptr, L.attn_norm, L.in, P.proj);
+    else norm_proj(P.R, P.F, P.X, L.attn_norm, L.in, P.proj);
+    if (!L.attn) {
+      // the recurrence: the chunk's tokens in order inside one launch, on the session's state
+      RecrChunkArgs c;
+      RecrArgs &a = c.r;
+      a.proj = P.proj;
+      a.ring = s->ring[L.slot];
+      a.convw = L.convw;
+      a.dt_bias = L.dt_bias;
+      a.ssm_a = L.ssm_a;
+      a.ssm_norm = L.ssm_norm;
+      a.state = s->state[L.slot];
+      a.y = P.Y;
+      a.pos = s->pos;
+      a.K = d.K;
+      a.nqk = d.nqkl;
+      a.nv = d.nvl;
+      a.dconv = d.dconvl;
+      a.z_off = d.dconvl;
+      a.beta_off = d.dconvl + d.nvl * d.hd;
+      a.alpha_off = a.beta_off + d.nvl;
+      a.eps = d.eps;
+      a.span_ctr = P.span_ctr;
+      a.img4 = nullptr;
+      a.img6 = nullptr;
+      a.ss = 0;
+      a.bimg = P.bimg;
+      a.nsg = kPrefillNsg;
+      c.pss = pss;
+      c.T = T;
+      c.nspan = P.nspan;
+      chk(launch_pdl(recr_chunk_kernel<128>, dim3(d.nvl, 128 / kGdnCols), dim3(128), 0, st, c), "prefill recurrence");
+      const int nring = std::min(T, d.K) * d.dconvl;
+      chk(launch_pdl(prefill_ring_kernel, dim3((nring + 255) / 256), dim3(256), 0, st, (const float *)P.proj, pss, T,
+                     s->ring[L.slot], d.dconvl, d.K, (const int *)s->pos),
+          "prefill ring");
+    } else {
+      AttnArgs a;
+      a.qk = P.proj;
+      a.v = P.proj + 2 * d.nhl * d.hdv + d.kvlenl;
+      a.q_norm = L.q_norm;
+      a.k_norm = L.k_norm;
+      a.rope = s->rope;
+      a.q = P.q;
+      a.kcache = s->kc[L.slot];
+      a.vcache = s->vc[L.slot];
+      a.scores = P.scores;
+      a.part = P.part;
+      a.img4 = nullptr;
+      a.img6 = nullptr;
+      a.pos = P.pos;
+      a.nh = d.nhl;
+      a.nkv = d.nkvl;
+      a.n_rot = d.n_rot;
+      a.nrp = d.nrp;
+      a.ctx = s->ctx_len;
+      a.nsplit = s->nsplit;
+      a.eps = d.eps;
+      a.kq_scale = d.kq_scale;
+      a.ss = pss;
+      a.kv_ss = 0;  // one cache for the chunk's tokens
+      a.bimg = P.bimg;
+      a.nsg = kPrefillNsg;
+      const dim3 sg(d.nkvl, (s->ctx_len + 31) / 32, nz), vg(d.nkvl, s->nsplit, nz);
+      const size_t q_smem = (size_t)(d.nhl / d.nkvl) * d.hdv * 8, v_smem = (size_t)kChunk * d.hdv * 4;
+      const size_t sm_smem = softmax_smem(s->ctx_len);
+      const dim3 cg(d.nhl * d.hdv / 256, 1, nz), pg(d.nhl + d.nkvl, 1, nz), smg(d.nhl, 1, nz);
+      if (d.hdv == 256) {
+        chk(launch_pdl(attn_pre_kernel<256>, pg, dim3(256), 0, st, a), "attn_pre");
+        chk(launch_pdl(attn_scores_kernel<256>, sg, dim3(256), q_smem, st, a), "attn_scores");
+        chk(launch_pdl(attn_softmax_kernel, smg, dim3(256), sm_smem, st, a), "attn_softmax");
+        chk(launch_pdl(attn_values_kernel<256>, vg, dim3(256), v_smem, st, a), "attn_values");
+        chk(launch_pdl(attn_combine_quant_kernel<256>, cg, dim3(256), 0, st, a), "attn_combine");
+      } else {
+        chk(launch_pdl(attn_pre_kernel<128>, pg, dim3(128), 0, st, a), "attn_pre");
+        chk(launch_pdl(attn_scores_kernel<128>, sg, dim3(256), q_smem, st, a), "attn_scores");
+        chk(launch_pdl(attn_softmax_kernel, smg, dim3(256), sm_smem, st, a), "attn_softmax");
+        chk(launch_pdl(attn_values_kernel<128>, vg, dim3(128), v_smem, st, a), "attn_values");
+        chk(launch_pdl(attn_combine_quant_kernel<128>, cg, dim3(256), 0, st, a), "attn_combine");
+      }
+    }
+    gemv(L.out, P.T);
+    norm_proj(P.X, P.T, P.R, L.post_norm, L.gate_up, P.FF);
+    chk(launch_pdl(swiglu_quant_kernel, dim3(d.nffl / 256, 1, nz), dim3(256), 0, st, (const float *)P.FF,
+                   (const float *)(P.FF + d.nffl), (uint8_t *)nullptr, (uint8_t *)nullptr, pss, P.bimg,
+                   kPrefillNsg),
+        "prefill swiglu");
+    gemv(L.down, P.F);
+  }
+  const uint32_t *last = nullptr;
+  if (head) {
+    // l_out -> output norm -> LM head + greedy argmax of every token (the last one's is kept)
+    norm(P.R, P.F, P.X, m->out_norm);
+    BatchGemvArgs b{m->output};
+    b.img = P.bimg;
+    b.nsg = kPrefillNsg;
+    b.y = P.logits;
+    b.ystride = pss / 4;
+    b.nseq = T;
+    b.key = s->ctx->bkey;
+    b.done = s->ctx->bdone;
+    b.token = P.tok;
+    b.tstride = 1;
+    if (!rc) rc = gemv_batch_launch(s->ctx, b);
+    last = P.tok + (T - 1);
+    // the last token's hidden state and logits where session_read finds them
+    chk(cudaMemcpyAsync(s->X, lane(P.X, T - 1), (size_t)d.n * 4, cudaMemcpyDeviceToDevice, st), "prefill");
+    chk(cudaMemcpyAsync(s->logits, lane(P.logits, T - 1), (size_t)(d.v1 - d.v0) * 4, cudaMemcpyDeviceToDevice, st),
+        "prefill");
+  }
+  chk(launch_pdl(prefill_end_kernel, dim3(1), dim3(1), 0, st, s->pos, T, s->cur_token, last), "prefill end");
+  return rc;
 }
 
 }  // namespace
@@ -2145,6 +2553,39 @@ int32_t unltd_qwen35_feed(unltd_qwen35_session s, const uint32_t *tokens, int32_
   }
   if (!rc && next_token && n > 0) rc = cuda_error(cudaMemcpyAsync(next_token, s->cur_token, 4, cudaMemcpyDeviceToHost, st), "qwen35_feed");
   if (!rc) rc = sync_and_check(s->ctx, st, "qwen35_feed");
+  if (!rc) {
+    s->host_pos += n;
+    s->seq_pos[0] = s->host_pos;
+  }
+  return rc;
+}
+
+// A prompt in chunks of up to 32 tokens (enqueue_prefill): the same state,
+// logits, hidden state and next token as unltd_qwen35_feed, with every weight
+// read once per chunk.
+int32_t unltd_qwen35_prefill(unltd_qwen35_session s, const uint32_t *tokens, int32_t n, uint32_t *next_token) {
+  if (!s || (!tokens && n > 0)) return set_error(UNLTD_ERR_INVALID_ARG, "qwen35_prefill: NULL argument");
+  if (s->nseq != 1) return set_error(UNLTD_ERR_INVALID_ARG, "qwen35_prefill: a batch session");
+  if (s->m->d.world != 1) return set_error(UNLTD_ERR_UNSUPPORTED, "qwen35_prefill: one GPU (use qwen35_feed)");
+  if (n < 0 || n > s->ctx_len - s->host_pos)
+    return set_error(UNLTD_ERR_LENGTH, "qwen35_prefill: context full (" + std::to_string(s->host_pos) + " of " +
+                                           std::to_string(s->ctx_len) + " positions used)");
+  for (int i = 0; i < n; i++)
+    if (tokens[i] >= (uint32_t)s->m->d.vocab)
+      return set_error(UNLTD_ERR_INVALID_ARG, "qwen35_prefill: token " + std::to_string(tokens[i]) + " outside the vocab");
+  if (n == 0) return UNLTD_OK;
+  CtxGuard g(s->m->ctx->device);
+  int32_t rc = prefill_alloc(s);
+  cudaStream_t st = s->ctx->stream;
+  for (int i0 = 0; !rc && i0 < n; i0 += kPrefillLanes) {
+    const int T = std::min(kPrefillLanes, n - i0);
+    rc = cuda_error(cudaMemcpyAsync(s->pf.tok, tokens + i0, (size_t)T * 4, cudaMemcpyHostToDevice, st),
+                    "qwen35_prefill");
+    if (!rc) rc = enqueue_prefill(s, T, i0 + T == n);  // the next chunk's copy is ordered after it
+  }
+  if (!rc && next_token) rc = cuda_error(cudaMemcpyAsync(next_token, s->cur_token, 4, cudaMemcpyDeviceToHost, st),
+                                         "qwen35_prefill");
+  if (!rc) rc = sync_and_check(s->ctx, st, "qwen35_prefill");
   if (!rc) {
     s->host_pos += n;
     s->seq_pos[0] = s->host_pos;

@@ -90,6 +90,7 @@ SIGNATURES = [
     ("unltd_qwen35_session_set_state", _I, [_P, _I, _P, _P, _P, _P]),
     ("unltd_qwen35_session_get_state", _I, [_P, _P, _P, _P, _P]),
     ("unltd_qwen35_feed", _I, [_P, _P, _I, _P]),
+    ("unltd_qwen35_prefill", _I, [_P, _P, _I, _P]),
     ("unltd_qwen35_decode", _I, [_P, ctypes.c_uint32, _I, _P]),
     ("unltd_qwen35_session_info", _I, [_P, ctypes.POINTER(_I), ctypes.POINTER(_P), ctypes.POINTER(_I64)]),
     ("unltd_qwen35_session_read", _I, [_P, _P, _P]),
@@ -561,6 +562,13 @@ class Qwen35Session:
         t = np.ascontiguousarray(tokens, dtype=np.uint32)
         nxt = np.zeros(1, np.uint32)
         _check(lib().unltd_qwen35_feed(self.h, t.ctypes.data, t.size, nxt.ctypes.data))
+        return int(nxt[0])
+
+    def prefill(self, tokens) -> int:
+        """The prompt through unltd_qwen35_prefill (batched; same bits as feed)."""
+        t = np.ascontiguousarray(tokens, dtype=np.uint32)
+        nxt = np.zeros(1, np.uint32)
+        _check(lib().unltd_qwen35_prefill(self.h, t.ctypes.data, t.size, nxt.ctypes.data))
         return int(nxt[0])
 
     def decode(self, token: int, n_steps: int, out: np.ndarray | None = None) -> np.ndarray:
