@@ -175,6 +175,37 @@ static void gemv(float *out, const float *x, const uint8_t *w, int dtype, int di
         ora_gemv_quant_q8k(out, x, w, rb(dtype, din) * (size_t)dout, (size_t)din, (size_t)dout, dtype, nthreads);
 }
 
+/* Tensor parallelism over `g_split` ranks (test infrastructure): the
+ * projections split by input columns (ffn_down, ssm_out, attn_output) as the
+ * ranks compute them: rank r takes columns [r din / W, (r + 1) din / W) of
+ * x and of every row (its own gemv_quant_q8k over that slice, the chain over
+ * its blocks only), and the partial outputs are summed in rank order in f32,
+ * y = ((p0 + p1) + p2) + ... Every other part of the step is the same on one
+ * GPU and on W (heads, rows and vocab rows split whole). 1: one device. */
+static int g_split = 1;
+
+void ora_forward_row_split(int world) { g_split = world < 1 ? 1 : world; }
+
+static void gemv_rowsplit(float *out, const float *x, const uint8_t *w, int dtype, int din, int dout, int nthreads) {
+    if (g_split == 1 || g_exact_gemv) {
+        gemv(out, x, w, dtype, din, dout, nthreads);
+        return;
+    }
+    const int cols = din / g_split;
+    const size_t rbf = rb(dtype, din), rbs = rb(dtype, cols);
+    uint8_t *ws = (uint8_t *)malloc(rbs * (size_t)dout);
+    float *part = (float *)malloc(sizeof(float) * dout);
+    for (int r = 0; r < g_split; r++) {
+        const size_t off = rb(dtype, cols * r);  /* the slice's first byte in a row */
+        for (int row = 0; row < dout; row++) memcpy(ws + rbs * row, w + rbf * row + off, rbs);
+        ora_gemv_quant_q8k(part, x + (size_t)cols * r, ws, rbs * (size_t)dout, (size_t)cols, (size_t)dout, dtype,
+                           nthreads);
+        for (int i = 0; i < dout; i++) out[i] = r == 0 ? part[i] : out[i] + part[i];
+    }
+    free(ws);
+    free(part);
+}
+
 #define T(L, f) (tensors[ORA_T_GLOBALS + (L) * ORA_T_PER_LAYER + (f)])
 #define D(L, f) (dtypes[ORA_T_GLOBALS + (L) * ORA_T_PER_LAYER + (f)])
 
@@ -189,7 +220,7 @@ static void ffn(const ora_model_cfg *c, void **tensors, const int *dtypes, int i
     gemv(g, p, (const uint8_t *)T(il, ORA_FFN_GATE), D(il, ORA_FFN_GATE), n, nff, nthreads);
     gemv(u, p, (const uint8_t *)T(il, ORA_FFN_UP), D(il, ORA_FFN_UP), n, nff, nthreads);
     ora_swiglu(g, g, u, nff);
-    gemv(f, g, (const uint8_t *)T(il, ORA_FFN_DOWN), D(il, ORA_FFN_DOWN), nff, n, nthreads);
+    gemv_rowsplit(f, g, (const uint8_t *)T(il, ORA_FFN_DOWN), D(il, ORA_FFN_DOWN), nff, n, nthreads);
     free(p);
     free(g);
     free(u);
@@ -249,7 +280,7 @@ static void recr_layer(const ora_model_cfg *c, void **tensors, const int *dtypes
     for (int h = 0; h < nv; h++) ora_rmsnorm(y + (size_t)h * hd, gdn_out + (size_t)h * hd, ssmn, hd, eps);
     for (int i = 0; i < n; i++) y[i] = y[i] * silu1(z[i]);
     float *attn_out = (float *)malloc(sizeof(float) * n);
-    gemv(attn_out, y, (const uint8_t *)T(il, ORA_SSM_OUT), D(il, ORA_SSM_OUT), n, n, nthreads);
+    gemv_rowsplit(attn_out, y, (const uint8_t *)T(il, ORA_SSM_OUT), D(il, ORA_SSM_OUT), n, n, nthreads);
     float *residual = (float *)malloc(sizeof(float) * n);
     for (int i = 0; i < n; i++) residual[i] = x_in[i] + attn_out[i];
     float *f = (float *)malloc(sizeof(float) * n);
@@ -306,7 +337,7 @@ static void attn_layer(const ora_model_cfg *c, void **tensors, const int *dtypes
     float *gated = (float *)malloc(sizeof(float) * n);
     for (int i = 0; i < n; i++) gated[i] = attn[i] * sigmoid1(gt[i]);
     float *attn_out = (float *)malloc(sizeof(float) * n);
-    gemv(attn_out, gated, (const uint8_t *)T(il, ORA_ATTN_OUT), D(il, ORA_ATTN_OUT), n, n, nthreads);
+    gemv_rowsplit(attn_out, gated, (const uint8_t *)T(il, ORA_ATTN_OUT), D(il, ORA_ATTN_OUT), n, n, nthreads);
     float *residual = (float *)malloc(sizeof(float) * n);
     for (int i = 0; i < n; i++) residual[i] = x_in[i] + attn_out[i];
     float *f = (float *)malloc(sizeof(float) * n);

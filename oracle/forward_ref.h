@@ -78,6 +78,11 @@ void ora_ssm_conv(float *out, const float *x, int ncs, const float *kernel, int 
 /* Projections through gemv_quant (on = 1) instead of gemv_quant_q8k (0, the
  * default and the reference's choice); process-wide. */
 void ora_forward_exact_gemv(int on);
+/* The projections split by input columns (ffn_down, ssm_out, attn_output)
+ * as `world` tensor-parallel ranks compute them: per-rank partial
+ * gemv_quant_q8k over equal column slices, summed in rank order in f32
+ * (1, the default: one device); process-wide. */
+void ora_forward_row_split(int world);
 
 int ora_decode_token(const ora_model_cfg *c, void **tensors, const int *dtypes, float **conv, float **gdn,
                      float **kcache, float **vcache, int position, uint32_t token, float *logits, float *hidden_out,

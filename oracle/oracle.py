@@ -292,6 +292,13 @@ class Qwen35Oracle:
         instead of gemv_quant_q8k; measures the reference's own Q8_K error."""
         lib().ora_forward_exact_gemv(1 if on else 0)
 
+    @staticmethod
+    def row_split(world: int):
+        """Process-wide: the input-split projections (ffn_down, ssm_out,
+        attn_output) as `world` tensor-parallel ranks compute them (per-rank
+        partial gemv_quant_q8k, summed in rank order); 1 = one device."""
+        lib().ora_forward_row_split(int(world))
+
     def greedy(self, token: int, n_steps: int, nthreads: int = 8):
         """greedy.rs: step, argmax (first index of the max), feed back."""
         out, logits, hidden = [], None, None

@@ -168,3 +168,46 @@ def test_decode_step_is_deterministic_and_stateful():
     la2, _ = a.step(7)
     assert not np.array_equal(la2, la)
     assert a.position == 12
+
+
+def test_row_split_restates_rank_order_sums():
+    """Qwen35Oracle.row_split(world): the input-split projections as
+    per-rank partial gemv_quant_q8k over equal column slices, summed in rank
+    order. One projection restated in numpy from the one-device
+    gemv_quant_q8k of each slice gives the same bits as a decode step built
+    on it predicts: world 1 is the one-device step again, world 2 moves the
+    hidden state by rounding only (same greedy token, close values)."""
+    import synth
+
+    # one GEMV: rank partials summed in rank order (f32)
+    for dtype, din in ((synth.Q4K, 1024), (synth.Q6K, 2048)):
+        dout = 37
+        wb = synth.quant_weights(dtype, din, dout, seed=din)
+        x = synth.activations(din, seed=din + 1)
+        rbf = oracle.row_bytes(dtype, din)
+        W = np.frombuffer(bytes(wb), np.uint8).reshape(dout, rbf)
+        for world in (2, 4):
+            cols = din // world
+            rbs = oracle.row_bytes(dtype, cols)
+            y = None
+            for r in range(world):
+                ws = np.ascontiguousarray(W[:, r * rbs:(r + 1) * rbs])
+                p = oracle.gemv_quant_q8k(x[r * cols:(r + 1) * cols], ws, cols, dout, dtype)
+                y = p if y is None else (y + p).astype(np.float32)
+            full = oracle.gemv_quant_q8k(x, wb, din, dout, dtype)
+            assert np.max(np.abs(y - full)) <= 1e-4 * np.max(np.abs(full))
+    # the forward
+    cfg = synth.QWEN35_TINY
+    t = synth.qwen35_model(cfg, 3)
+    st = synth.qwen35_state(cfg, 10, 4)
+    l1, h1 = oracle.Qwen35Oracle(cfg, t, 32, st, 10).step(7)
+    oracle.Qwen35Oracle.row_split(2)
+    try:
+        l2, h2 = oracle.Qwen35Oracle(cfg, t, 32, st, 10).step(7)
+    finally:
+        oracle.Qwen35Oracle.row_split(1)
+    l3, h3 = oracle.Qwen35Oracle(cfg, t, 32, st, 10).step(7)
+    assert (bits(l3) == bits(l1)).all() and (bits(h3) == bits(h1)).all()
+    assert not np.array_equal(bits(h2), bits(h1))
+    assert oracle.argmax(l2) == oracle.argmax(l1)
+    assert np.max(np.abs(h2 - h1)) <= 1e-3 * np.max(np.abs(h1))

@@ -6,10 +6,11 @@ oracle; run with torchrun (one process per GPU), e.g.
 
 Every rank holds its shard (unltd_qwen35_create_tp); rank 0 compares the
 greedy stream, the full logits (gathered from the vocab shards) and the
-hidden state with the oracle and prints one JSON line. The row-split
-projections sum their partial outputs across GPUs, so logits and hidden
-states match the oracle within a tolerance rather than bit for bit; the
-token stream must be identical.
+hidden state with the oracle and prints one JSON line: bit for bit against
+the oracle of the sharded arithmetic (Qwen35Oracle.row_split(world): the
+input-split projections as per-rank partial gemv_quant_q8k summed in rank
+order), and as a drift against the one-device oracle (the rank-order sums
+round differently from the reference's single chain).
 """
 import argparse
 import datetime
@@ -128,6 +129,20 @@ def main():
                                         nthreads=os.cpu_count() or 8)
             out["logits_bit_identical_given_hidden"] = bool(np.array_equal(own.view(np.uint32),
                                                                            logits.view(np.uint32)))
+            # the oracle of the sharded arithmetic: the same steps bit for bit
+            oracle.Qwen35Oracle.row_split(world)
+            try:
+                so = oracle.Qwen35Oracle(cfg, tensors, pos0 + n + 10, st, pos0)
+                stoks, sl, sh, tok = [], None, None, start
+                for _ in range(n + 2):
+                    sl, sh = so.step(tok, nthreads=os.cpu_count() or 8)
+                    tok = oracle.argmax(sl)
+                    stoks.append(tok)
+            finally:
+                oracle.Qwen35Oracle.row_split(1)
+            out["stream_matches_split_oracle"] = stoks == toks.tolist()
+            out["logits_bit_identical_to_split_oracle"] = bool(np.array_equal(sl.view(np.uint32), logits.view(np.uint32)))
+            out["hidden_bit_identical_to_split_oracle"] = bool(np.array_equal(sh.view(np.uint32), hd.view(np.uint32)))
         print(json.dumps(out), flush=True)
     s.close()
     m.close()
