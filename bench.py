@@ -271,11 +271,13 @@ def decode_bytes_per_token(cfg, position, n_seq=1):
     return total
 
 
-def decode_batch_bench(m, cfg, st, pos0, n_seq, n_steps, profile_region=False):
-    """BASELINE config 4 at batch n_seq on one GPU: n_seq sequences from the
+def decode_batch_bench(m, cfg, st, pos0, n_seq, n_steps, profile_region=False, world=1, dist=None):
+    """BASELINE config 4 at batch n_seq: n_seq sequences from the
     2048-position state (each its own first token) decoded together through
-    unltd_qwen35_batch_decode; every weight matrix is read once per step for
-    all sequences. Device-timed on the session stream."""
+    unltd_qwen35_batch_decode, on one GPU or tensor-parallel over `world`
+    (every rank holds its shard of the weights and of every sequence's
+    state); every weight matrix is read once per step for all sequences.
+    Device-timed on each rank's session stream, the max over ranks."""
     import torch
 
     b = m.batch_session(pos0 + n_steps + 16, n_seq)
@@ -286,6 +288,8 @@ def decode_batch_bench(m, cfg, st, pos0, n_seq, n_steps, profile_region=False):
     ext = torch.cuda.ExternalStream(b.info()["stream"])
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     torch.cuda.synchronize()
+    if dist:
+        dist.barrier()
     if profile_region:
         torch.cuda.profiler.start()
     t0 = time.perf_counter()
@@ -297,13 +301,19 @@ def decode_batch_bench(m, cfg, st, pos0, n_seq, n_steps, profile_region=False):
     if profile_region:
         torch.cuda.profiler.stop()
     ms_step = e0.elapsed_time(e1) / n_steps
+    if dist:
+        tt = torch.tensor([ms_step, wall], device="cuda", dtype=torch.float64)
+        dist.all_reduce(tt, op=dist.ReduceOp.MAX)
+        ms_step, wall = float(tt[0]), float(tt[1])
     bps = decode_bytes_per_token(cfg, pos0 + 4 + n_steps // 2, n_seq)
     peak, peak_kind = _peaks()
     gbs = bps / (ms_step * 1e-3) / 1e9
-    out = {"workload": f"config4_qwen35_9b_synthetic_greedy_decode_ctx2048_batch{n_seq}", "n_seq": n_seq,
-           "steps": n_steps, "n_gpus": 1, "tok_s": round(n_seq * 1e3 / ms_step, 1), "ms_per_step": round(ms_step, 4),
-           "e2e_tok_s": round(n_seq * n_steps / wall, 1), "bytes_per_step": bps, "hbm_gbs": round(gbs, 1),
-           "roofline_frac": round(gbs / peak, 4), "peak": peak, "peak_kind": peak_kind,
+    out = {"workload": f"config4_qwen35_9b_synthetic_greedy_decode_ctx2048_batch{n_seq}" +
+                       (f"_tp{world}" if world > 1 else ""), "n_seq": n_seq,
+           "steps": n_steps, "n_gpus": world, "tok_s": round(n_seq * 1e3 / ms_step, 1),
+           "ms_per_step": round(ms_step, 4), "e2e_tok_s": round(n_seq * n_steps / wall, 1), "bytes_per_step": bps,
+           "hbm_gbs": round(gbs, 1), "hbm_gbs_per_gpu": round(gbs / world, 1),
+           "roofline_frac": round(gbs / world / peak, 4), "peak": peak, "peak_kind": peak_kind,
            "launches_per_step": b.info()["launches_per_step"],
            "arithmetic": "Q8K_EXACT projections (one weight pass for all sequences); every sequence bit-identical "
                          "to a one-sequence session",
@@ -407,9 +417,10 @@ def decode_bench(n_tokens, with_cpu, rank=0, world=1, dist=None, profile_region=
     s.close()
     if world == 1 and prefill > 0:
         out["prefill"] = prefill_bench(m, cfg, st, pos0, prefill)
-    if world == 1 and batch > 1:
+    if batch > 1:
         out["batch"] = 1
-        out["batch%d" % batch] = decode_batch_bench(m, cfg, st, pos0, batch, max(4, n_tokens // 4), profile_batch)
+        out["batch%d" % batch] = decode_batch_bench(m, cfg, st, pos0, batch, max(4, n_tokens // 4), profile_batch,
+                                                    world, dist)
     m.close()
     ctx.close()
     if with_cpu and rank == 0:

@@ -146,3 +146,25 @@ def test_tp_shard_forms_at_world(world):
     assert out["same_token_on_all_ranks"] and out["token_matches_oracle"] and out["logits_bit_identical"], out
     assert out["colsplit_maxrel"] <= 1e-4, out
     assert out["colsplit_same_on_all_ranks"], out
+
+
+@pytest.mark.parametrize("model,world,batch", [("tiny", 2, 5), ("9b", 2, 32), ("9b", 4, 32), ("9b", 8, 32)])
+def test_tp_batch_decode_matches_split_oracle(model, world, batch):
+    """Batch decode across GPUs (batch 32): every rank
+    holds its shard of the model and every sequence's state; the row-split
+    outputs of all sequences go through one rank-order peer all-reduce, the
+    vocab-split LM head through a MAX of every sequence's key. Sequences 0
+    and B-1 bit-identical to the oracle of the sharded arithmetic (stream,
+    gathered logits, hidden state)."""
+    if not torch.cuda.is_available() or torch.cuda.device_count() < world:
+        pytest.skip(f"needs {world} GPUs")
+    from __graft_entry__ import build
+
+    build()
+    args = ["--model", model, "--steps", "4", "--allreduce", "peer", "--batch", str(batch)]
+    if model == "9b":
+        args += ["--position", "40"]
+    out = _run_torchrun(world, "tp_decode_check.py", *args)
+    assert out["same_streams_on_all_ranks"], out
+    assert out["streams_match_split_oracle"], out
+    assert out["logits_bit_identical_to_split_oracle"] and out["hidden_bit_identical_to_split_oracle"], out

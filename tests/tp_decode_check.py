@@ -58,6 +58,8 @@ def main():
     ap.add_argument("--position", type=int, default=40)
     ap.add_argument("--first-token", type=int, default=None, help="first token (default: 5 tiny, 7 for the 9B model)")
     ap.add_argument("--no-oracle", action="store_true")
+    ap.add_argument("--batch", type=int, default=1,
+                    help="sequences of a batch session (first tokens first-token + 37 z); sequences 0 and B-1 checked")
     ap.add_argument("--allreduce", default="peer", choices=["peer", "nccl"],
                     help="peer: one kernel over NVLink peer memory; nccl: ncclAllReduce")
     args = ap.parse_args()
@@ -75,6 +77,8 @@ def main():
         ctx.peer_init()
     m = ug.Qwen35Model(ctx, cfg, rank, world)
     m.load(tensors)
+    if args.batch > 1:
+        return batch_main(args, cfg, tensors, st, ctx, m, rank, world, pos0, n)
     s = m.session(pos0 + n + 10)
     s.set_state(pos0, st["conv"], st["gdn"], st["k"], st["v"])
     start = args.first_token if args.first_token is not None else (5 if args.model == "tiny" else 7)
@@ -145,6 +149,67 @@ def main():
             out["hidden_bit_identical_to_split_oracle"] = bool(np.array_equal(sh.view(np.uint32), hd.view(np.uint32)))
         print(json.dumps(out), flush=True)
     s.close()
+    m.close()
+    ctx.close()
+    dist.barrier()
+    dist.destroy_process_group()
+
+
+def batch_main(args, cfg, tensors, st, ctx, m, rank, world, pos0, n):
+    """A batch session on every rank: each sequence from the same state with
+    its own first token; sequences 0 and B-1 against the oracle of the
+    sharded arithmetic, bit for bit."""
+    B = args.batch
+    start = args.first_token if args.first_token is not None else (5 if args.model == "tiny" else 7)
+    first = [(start + 37 * z) % cfg["vocab"] for z in range(B)]
+    b = m.batch_session(pos0 + n + 10, B)
+    for z in range(B):
+        b.set_state(z, pos0, st["conv"], st["gdn"], st["k"], st["v"])
+    warm = b.decode(first, 2)
+    dist.barrier()
+    torch.cuda.synchronize()
+    t0 = time.perf_counter()
+    toks = b.decode(warm[:, -1], n)
+    dt = time.perf_counter() - t0
+    toks = np.concatenate([warm, toks], axis=1)
+    v0, v1 = b.shape()["vocab"]
+    check = sorted({0, B - 1})
+    reads = {z: b.read(z) for z in check}
+    parts = [None] * world
+    dist.all_gather_object(parts, (v0, v1, {z: reads[z][0] for z in check}))
+    streams = [None] * world
+    dist.all_gather_object(streams, toks.tolist())
+    out = {"model": args.model, "world": world, "batch": B, "steps": n, "position": pos0,
+           "same_streams_on_all_ranks": all(x == streams[0] for x in streams),
+           "tok_s": round(B * n / dt, 1)}
+    if rank == 0 and not args.no_oracle:
+        import oracle
+
+        ok_tok, ok_lg, ok_hd = True, True, True
+        oracle.Qwen35Oracle.row_split(world)
+        try:
+            for z in check:
+                logits = np.zeros(cfg["vocab"], np.float32)
+                for a, c, lgs in parts:
+                    logits[a:c] = lgs[z]
+                so = oracle.Qwen35Oracle(cfg, tensors, pos0 + n + 10, st, pos0)
+                tok, stoks = first[z], []
+                for _ in range(n + 2):
+                    sl, sh = so.step(tok, nthreads=os.cpu_count() or 8)
+                    tok = oracle.argmax(sl)
+                    stoks.append(tok)
+                ok_tok &= stoks == toks[z].tolist()
+                ok_lg &= bool(np.array_equal(sl.view(np.uint32), logits.view(np.uint32)))
+                ok_hd &= bool(np.array_equal(sh.view(np.uint32), reads[z][1].view(np.uint32)))
+        finally:
+            oracle.Qwen35Oracle.row_split(1)
+        out["checked_sequences"] = check
+        out["streams_match_split_oracle"] = ok_tok
+        out["logits_bit_identical_to_split_oracle"] = ok_lg
+        out["hidden_bit_identical_to_split_oracle"] = ok_hd
+    if rank == 0:
+        print(json.dumps(out), flush=True)
+    b.close()
     m.close()
     ctx.close()
     dist.barrier()

@@ -3,6 +3,7 @@
 // so the library binds to the libnccl.so.2 the host process already loaded
 // (e.g. PyTorch's) instead of linking a second copy.
 #include <dlfcn.h>
+#include <algorithm>
 #include <nccl.h>
 
 #include <mutex>
@@ -59,6 +60,7 @@ int32_t nccl_error(ncclResult_t r, const char *what) {
 struct PeerArgs {
   uint8_t *map[kPeerMaxRanks];  // every rank's area as mapped here
   unsigned *ctr;                // all-reduces issued so far (this device)
+  unsigned *done;               // [2]: CTAs that finished writing / summing (reset by the last)
   int rank, world;
   int *err;
 };
@@ -77,16 +79,19 @@ __device__ __forceinline__ uint64_t peer_ns() {
   return t;
 }
 
-// One CTA: (1) this rank's buf into slot [parity][rank] of every rank's area
-// (peer stores over NVLink), (2) after a system fence, its flag in every
-// area, (3) wait (bounded, ~2 s) for every rank's flag here, (4) the sum (or
-// max) of the slots in rank order 0, 1, ..., so every rank computes the same
-// bits. Parities alternate: a rank can only reuse a parity after all ranks
-// flagged the following all-reduce, i.e. finished reading this one.
+// Grid of G CTAs, CTA b on elements [b count / G, (b + 1) count / G): (1)
+// this rank's buf into slot [parity][rank] of every rank's area (peer stores
+// over NVLink), (2) after a system fence, the last CTA to finish writing
+// raises this rank's flag in every area, (3) every CTA waits (bounded, ~2 s)
+// for every rank's flag here, (4) the sum (or max) of its elements of the
+// slots in rank order 0, 1, ..., so every rank computes the same bits; the
+// last CTA to finish advances the counter. Parities alternate: a rank can
+// only reuse a parity after all ranks flagged the following all-reduce, i.e.
+// finished reading this one.
 template <typename T, bool MAXOP>
 __global__ void __launch_bounds__(1024) peer_allreduce_kernel(T *buf, int count, PeerArgs a) {
   __shared__ unsigned s_ep;
-  __shared__ int s_ok;
+  __shared__ int s_ok, s_last;
   asm volatile("griddepcontrol.wait;" ::: "memory");
   if (threadIdx.x == 0) {
     s_ep = *a.ctr + 1u;
@@ -94,15 +99,23 @@ __global__ void __launch_bounds__(1024) peer_allreduce_kernel(T *buf, int count,
   }
   __syncthreads();
   const unsigned ep = s_ep;
+  const int G = gridDim.x;
+  const int i0 = (int)((long long)count * blockIdx.x / G), i1 = (int)((long long)count * (blockIdx.x + 1) / G);
   const size_t slot0 = kPeerFlagBytes + (size_t)(ep & 1u) * kPeerMaxRanks * kPeerSlotBytes;
   for (int r = 0; r < a.world; r++) {
     T *dst = reinterpret_cast<T *>(a.map[r] + slot0 + (size_t)a.rank * kPeerSlotBytes);
-    for (int i = threadIdx.x; i < count; i += blockDim.x) dst[i] = buf[i];
+    for (int i = i0 + threadIdx.x; i < i1; i += blockDim.x) dst[i] = buf[i];
   }
   __threadfence_system();
   __syncthreads();
-  if (threadIdx.x < a.world)
-    st_release_sys(reinterpret_cast<unsigned *>(a.map[threadIdx.x]) + a.rank, ep);
+  if (threadIdx.x == 0) s_last = atomicAdd(&a.done[0], 1u) == (unsigned)G - 1;
+  __syncthreads();
+  if (s_last) {  // every CTA's stores are visible: raise the flags
+    __threadfence_system();
+    if (threadIdx.x < a.world)
+      st_release_sys(reinterpret_cast<unsigned *>(a.map[threadIdx.x]) + a.rank, ep);
+    if (threadIdx.x == 0) a.done[0] = 0u;
+  }
   if (threadIdx.x < a.world) {
     const unsigned *flag = reinterpret_cast<const unsigned *>(a.map[a.rank]) + threadIdx.x;
     if (ld_acquire_sys(flag) - ep > 0x7fffffffu) {  // flag < ep (wrap-safe)
@@ -120,7 +133,7 @@ __global__ void __launch_bounds__(1024) peer_allreduce_kernel(T *buf, int count,
   __syncthreads();
   if (s_ok) {
     const uint8_t *mine = a.map[a.rank] + slot0;
-    for (int i = threadIdx.x; i < count; i += blockDim.x) {
+    for (int i = i0 + threadIdx.x; i < i1; i += blockDim.x) {
       T v = __ldcv(reinterpret_cast<const T *>(mine) + i);
       for (int r = 1; r < a.world; r++) {
         const T o = __ldcv(reinterpret_cast<const T *>(mine + (size_t)r * kPeerSlotBytes) + i);
@@ -130,18 +143,24 @@ __global__ void __launch_bounds__(1024) peer_allreduce_kernel(T *buf, int count,
       buf[i] = v;
     }
   }
-  if (threadIdx.x == 0) *a.ctr = ep;
+  __syncthreads();
+  if (threadIdx.x == 0 && atomicAdd(&a.done[1], 1u) == (unsigned)G - 1) {  // every CTA has read ep
+    a.done[1] = 0u;
+    *a.ctr = ep;
+  }
 }
 
 int32_t peer_allreduce(unltd_ctx c, cudaStream_t st, void *buf, size_t count, bool max_u64) {
   PeerArgs a;
   for (int r = 0; r < kPeerMaxRanks; r++) a.map[r] = static_cast<uint8_t *>(c->peer_map[r]);
   a.ctr = c->peer_ctr;
+  a.done = c->peer_ctr + 2;
   a.rank = c->rank;
   a.world = c->world;
   a.err = c->err;
   cudaLaunchConfig_t cfg = {};
-  cfg.gridDim = dim3(1);
+  // one CTA for a decode step's vector (latency), more for a batch's
+  cfg.gridDim = dim3((unsigned)std::min<size_t>(64, std::max<size_t>(1, count / 4096)));
   cfg.blockDim = dim3(1024);
   cfg.stream = st;
   cudaLaunchAttribute at[1];
@@ -229,8 +248,10 @@ int32_t unltd_peer_export(unltd_ctx c, void *handle_out, size_t handle_bytes) {
   if (!c->peer_area) {
     cudaError_t e = cudaMalloc(&c->peer_area, kPeerAreaBytes);
     if (e == cudaSuccess) e = cudaMemset(c->peer_area, 0, kPeerAreaBytes);
-    if (e == cudaSuccess) e = cudaMalloc(&c->peer_ctr, 2 * sizeof(unsigned));
-    if (e == cudaSuccess) e = cudaMemset(c->peer_ctr, 0, 2 * sizeof(unsigned));
+    // [0] all-reduces issued, [1] the fused GEMV send path's CTA count, [2..3]
+    // the all-reduce kernel's CTA counts
+    if (e == cudaSuccess) e = cudaMalloc(&c->peer_ctr, 4 * sizeof(unsigned));
+    if (e == cudaSuccess) e = cudaMemset(c->peer_ctr, 0, 4 * sizeof(unsigned));
     c->peer_done = c->peer_ctr + 1;
     if (e != cudaSuccess) {
       peer_close(c);

@@ -122,6 +122,7 @@ struct NormArgs {
   unsigned long long *key;  // non-null: reset the LM-head argmax state
   unsigned *done;
   size_t ss = 0;            // bytes between the sequences' arenas (a, b, r_out, images)
+  size_t bss = 0;           // b's own stride when it is not in the arenas (0: ss)
   uint8_t *bimg = nullptr;  // batch session: the batched x images (then img4 = img6 = null)
   int nsg = 0;
 };
@@ -135,7 +136,7 @@ __global__ void __launch_bounds__(256) norm_quant_kernel(NormArgs p) {
   {
     const size_t so = seq_off(p.ss);
     p.a = seq_ptr(p.a, so);
-    p.b = seq_ptr(p.b, so);
+    p.b = seq_ptr(p.b, p.bss ? seq_off(p.bss) : so);
     p.r_out = seq_ptr(p.r_out, so);
     p.img4 = seq_ptr(p.img4, so);
     p.img6 = seq_ptr(p.img6, so);
@@ -1063,9 +1064,11 @@ __global__ void __launch_bounds__(256) attn_combine_quant_kernel(AttnArgs a) {
 
 // greedy token from the cross-GPU maximum of the argmax keys
 // (orderable(logit) << 32 | ~global_row): the first index of the maximum
-__global__ void key_to_token_kernel(const unsigned long long *key, uint32_t *token) {
+__global__ void key_to_token_kernel(const unsigned long long *key, uint32_t *token, size_t tss) {
   pdl_trigger();
   pdl_wait();
+  key += blockIdx.z;  // a batch: one key per sequence, its token in its arena
+  token = seq_ptr(token, seq_off(tss));
   *token = 0xffffffffu - (uint32_t)(*key & 0xffffffffull);
 }
 
@@ -1183,6 +1186,11 @@ struct unltd_qwen35_session_s {
   uint8_t *arena = nullptr;
   uint8_t *bimg = nullptr;  // the batched x images (n_seq > 1)
   int nsg = 0;
+  // tensor-parallel batch: the row-split projections' outputs of every
+  // sequence, contiguous ([n_seq][n_embd]) for one all-reduce, and the
+  // sequences' LM-head argmax keys
+  float *tpbuf = nullptr;
+  unsigned long long *tpkeys = nullptr;
   // prefill (unltd_qwen35_prefill): kPrefillLanes activation lanes (a
   // chunk's tokens), made on first use; the state stays the session's
   struct Prefill {
@@ -1533,7 +1541,7 @@ int64_t launch_gemv_img(unltd_qwen35_session s, const unltd_weight_s *w, float *
     b.img = s->bimg;
     b.nsg = s->nsg;
     b.y = y;
-    b.ystride = s->ss / 4;
+    b.ystride = s->tpbuf && y == s->tpbuf ? (size_t)s->m->d.n : s->ss / 4;  // tpbuf: contiguous rows
     b.nseq = s->nseq;
     if (!*rc) *rc = gemv_batch_launch(s->ctx, b);
     return 1;
@@ -1592,6 +1600,10 @@ int32_t enqueue_step(unltd_qwen35_session s) {
   };
   const bool batch = s->nseq > 1;
   const unsigned nz = (unsigned)s->nseq;
+  // a tensor-parallel batch: the row-split outputs go to tpbuf, one
+  // all-reduce for all sequences, and the consuming norm reads them there
+  const bool tpb = batch && d.world > 1;
+  const size_t tpss = (size_t)d.n * 4;
   // the images a producer writes for its consumers: in a batch session the
   // batched image only (the batched GEMV reads it for both formats)
   auto im4 = [&](bool q4) { return !batch && q4 ? s->img4 : nullptr; };
@@ -1600,6 +1612,7 @@ int32_t enqueue_step(unltd_qwen35_session s) {
     NormArgs p{a, b, r_out, w, d.n, d.eps, im4(q4), im6(q6),
                argmax && !batch ? s->ctx->argmax_key : nullptr, argmax && !batch ? s->ctx->argmax_done : nullptr};
     p.ss = s->ss;
+    if (tpb && b == s->tpbuf) p.bss = tpss;
     p.bimg = s->bimg;
     p.nsg = s->nsg;
     chk(launch_pdl(norm_quant_kernel, dim3(d.n / 256, 1, nz), dim3(256), 0, st, p), "norm");
@@ -1656,7 +1669,7 @@ int32_t enqueue_step(unltd_qwen35_session s) {
                            gemv_tc_eligible(s->ctx, *L.down, MODE_Q8K);
     // layer input = l_out of the previous layer (residual + ffn), fused into the norm
     if (il == 0) norm_proj(s->X, nullptr, nullptr, L.attn_norm, L.in, s->proj);
-    else norm_proj(s->R, s->F, s->X, L.attn_norm, L.in, s->proj, down_sent);
+    else norm_proj(s->R, tpb ? s->tpbuf : s->F, s->X, L.attn_norm, L.in, s->proj, down_sent);
     if (!L.attn) {
       RecrArgs a;
       a.proj = s->proj;
@@ -1685,8 +1698,9 @@ int32_t enqueue_step(unltd_qwen35_session s) {
       const dim3 rg(d.nvl, 128 / kGdnCols, nz);
       if (d.K == 4) chk(launch_pdl(recr_mid_kernel<128, 4>, rg, dim3(128), 0, st, a), "recr_mid");
       else chk(launch_pdl(recr_mid_kernel<128, 0>, rg, dim3(128), 0, st, a), "recr_mid");
-      nl += launch_gemv_img(s, L.out, s->T, &rc, out_send);
-      if (!out_send) allreduce(s->T, d.n);
+      nl += launch_gemv_img(s, L.out, tpb ? s->tpbuf : s->T, &rc, out_send);
+      if (tpb) allreduce(s->tpbuf, (int)(nz * d.n));
+      else if (!out_send) allreduce(s->T, d.n);
     } else {
       AttnArgs a;
       a.qk = s->proj;
@@ -1731,21 +1745,23 @@ int32_t enqueue_step(unltd_qwen35_session s) {
         chk(launch_pdl(attn_values_kernel<128>, vg, dim3(128), v_smem, st, a), "attn_values");
         chk(launch_pdl(attn_combine_quant_kernel<128>, cg, dim3(256), 0, st, a), "attn_combine");
       }
-      nl += launch_gemv_img(s, L.out, s->T, &rc, out_send);
-      if (!out_send) allreduce(s->T, d.n);
+      nl += launch_gemv_img(s, L.out, tpb ? s->tpbuf : s->T, &rc, out_send);
+      if (tpb) allreduce(s->tpbuf, (int)(nz * d.n));
+      else if (!out_send) allreduce(s->T, d.n);
     }
     // residual = x_in + attn_out; rmsnorm(residual, post_attention_norm) -> gate|up image
-    norm_proj(s->X, s->T, s->R, L.post_norm, L.gate_up, s->FF, out_send);
+    norm_proj(s->X, tpb ? s->tpbuf : s->T, s->R, L.post_norm, L.gate_up, s->FF, out_send);
     chk(launch_pdl(swiglu_quant_kernel, dim3(d.nffl / 256, 1, nz), dim3(256), 0, st, (const float *)s->FF,
                    (const float *)(s->FF + d.nffl), im4(L.down->dtype == Q4K), im6(L.down->dtype == Q6K), s->ss,
                    s->bimg, s->nsg),
         "swiglu");
-    nl += launch_gemv_img(s, L.down, s->F, &rc, down_send);
-    if (!down_send) allreduce(s->F, d.n);
+    nl += launch_gemv_img(s, L.down, tpb ? s->tpbuf : s->F, &rc, down_send);
+    if (tpb) allreduce(s->tpbuf, (int)(nz * d.n));
+    else if (!down_send) allreduce(s->F, d.n);
     down_sent = down_send;
   }
   // l_out of the last layer -> output norm -> LM head + greedy argmax
-  norm(s->R, s->F, s->X, m->out_norm, m->output->dtype == Q4K, m->output->dtype == Q6K, true);
+  norm(s->R, tpb ? s->tpbuf : s->F, s->X, m->out_norm, m->output->dtype == Q4K, m->output->dtype == Q6K, true);
   if (batch) {
     BatchGemvArgs b{m->output};
     b.img = s->bimg;
@@ -1757,8 +1773,19 @@ int32_t enqueue_step(unltd_qwen35_session s) {
     b.done = s->ctx->bdone;
     b.token = s->cur_token;
     b.tstride = s->ss / 4;
+    if (tpb) {  // vocab shards: every sequence's key, MAX across the ranks, then its token
+      b.row0 = d.v0;
+      b.key_out = s->tpkeys;
+    }
     if (!rc) rc = gemv_batch_launch(s->ctx, b);
     nl += 1;
+    if (tpb) {
+      if (!rc) rc = comm_allreduce(m->ctx, st, s->tpkeys, nz, true);
+      nl += 1;
+      chk(launch_pdl(key_to_token_kernel, dim3(1, 1, nz), dim3(1), 0, st, (const unsigned long long *)s->tpkeys,
+                     s->cur_token, s->ss),
+          "key_to_token");
+    }
   } else {
     GemvArgs g{m->output, nullptr, s->logits, MODE_Q8K, s->ctx->argmax_key, s->ctx->argmax_done, s->cur_token};
     g.img = m->output->dtype == Q4K ? s->img4 : s->img6;
@@ -1770,7 +1797,7 @@ int32_t enqueue_step(unltd_qwen35_session s) {
       if (!rc) rc = comm_allreduce(m->ctx, st, s->tpkey, 1, true);
       nl += 1;
       chk(launch_pdl(key_to_token_kernel, dim3(1), dim3(1), 0, st, (const unsigned long long *)s->tpkey,
-                     s->cur_token),
+                     s->cur_token, (size_t)0),
           "key_to_token");
     }
   }
@@ -2270,8 +2297,8 @@ int32_t unltd_qwen35_session_create_batch(unltd_qwen35 m, int32_t ctx_len, int32
   if (n_seq < 1 || n_seq > kMaxBatch)
     return set_error(UNLTD_ERR_INVALID_ARG, "qwen35_session_create: n_seq must be in [1, 32]");
   const Derived &d = m->d;
-  if (n_seq > 1 && d.world > 1)
-    return set_error(UNLTD_ERR_UNSUPPORTED, "qwen35_session_create: batch decode runs on one GPU");
+  if (n_seq > 1 && d.world > 1 && (size_t)n_seq * d.n > kPeerMaxCount)
+    return set_error(UNLTD_ERR_UNSUPPORTED, "qwen35_session_create: batch too large for the tensor-parallel sum");
   if (n_seq > 1) {  // every projection must have a batched GEMV
     auto ok = [&](const unltd_weight_s *w) { return gemv_batch_supported(m->ctx->device, *w); };
     bool all = ok(m->output);
@@ -2342,6 +2369,11 @@ int32_t unltd_qwen35_session_create_batch(unltd_qwen35 m, int32_t ctx_len, int32
     s->nsg = (n_seq + 7) / 8;
     rc = dalloc(B, &s->bimg, spans * s->nsg * kBImgBlock, "session batched images");
   }
+  if (!rc && n_seq > 1 && d.world > 1) {
+    rc = dalloc(B, &s->tpbuf, (size_t)n_seq * d.n, "session tensor-parallel sums");
+    if (!rc) rc = dalloc(B, &s->tpkeys, (size_t)n_seq, "session tensor-parallel keys");
+    if (!rc) rc = cuda_error(cudaMemset(s->tpbuf, 0, (size_t)n_seq * d.n * 4), "session init");
+  }
   // IMROPE angles (kernels.rs:381-400): angle = pos * theta^ic by repeated
   // multiplication; (cos, sin) of the rotated pairs ic % 3 == 0, from libm.
   if (!rc && d.nrp > 0) {
@@ -2386,6 +2418,11 @@ int32_t unltd_qwen35_session_create_batch(unltd_qwen35 m, int32_t ctx_len, int32
     if (!rc) rc = cuda_error(cudaMemset(s->tpkey, 0, 8), "session init");
     if (!rc) rc = comm_allreduce(m->ctx, s->ctx->stream, s->T, (size_t)d.n, false);
     if (!rc) rc = comm_allreduce(m->ctx, s->ctx->stream, s->tpkey, 1, true);
+    if (!rc && n_seq > 1) {  // a batch's collectives too
+      rc = comm_allreduce(m->ctx, s->ctx->stream, s->tpbuf, (size_t)n_seq * d.n, false);
+      if (!rc) rc = cuda_error(cudaMemset(s->tpkeys, 0, (size_t)n_seq * 8), "session init");
+      if (!rc) rc = comm_allreduce(m->ctx, s->ctx->stream, s->tpkeys, (size_t)n_seq, true);
+    }
     if (!rc) rc = cuda_error(cudaStreamSynchronize(s->ctx->stream), "session init");
   }
   if (rc) {

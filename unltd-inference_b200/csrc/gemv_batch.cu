@@ -55,6 +55,8 @@ struct BParams {
   unsigned *done;
   uint32_t *token;     // token of sequence s at token[s * tstride]
   size_t tstride;
+  int row0;                         // global index of row 0 (a vocab shard)
+  unsigned long long *key_out;      // non-null: the final keys here instead of tokens
   int *err;
 };
 
@@ -220,7 +222,7 @@ __global__ void batch6_convert(const uint8_t *__restrict__ dev, size_t stride, s
 __device__ __forceinline__ void batch_emit(const BParams &P, int row, int seq, float acc,
                                            unsigned long long *best) {
   if (P.y) P.y[(size_t)seq * P.ystride + row] = acc;
-  if (P.key) atomicMax(best + seq, argmax_key(acc, row));
+  if (P.key) atomicMax(best + seq, argmax_key(acc, P.row0 + row));
 }
 
 // T rows per tile (16 x the row groups); SB sequences per warp task. Warp w
@@ -346,7 +348,8 @@ __global__ void __launch_bounds__(kBatchThreads, 1) gemv_batch_kernel(BParams P)
         __threadfence();
         if (s < P.nseq) {
           const unsigned long long kf = atomicAdd(P.key + s, 0ull);
-          P.token[(size_t)s * P.tstride] = 0xffffffffu - (uint32_t)(kf & 0xffffffffull);
+          if (P.key_out) P.key_out[s] = kf;
+          else P.token[(size_t)s * P.tstride] = 0xffffffffu - (uint32_t)(kf & 0xffffffffull);
           P.key[s] = 0ull;
         }
         __syncwarp();
@@ -504,6 +507,8 @@ int32_t gemv_batch_launch(unltd_ctx ctx, const BatchGemvArgs &a) {
   P.done = a.done;
   P.token = a.token;
   P.tstride = a.tstride;
+  P.row0 = a.row0;
+  P.key_out = a.key_out;
   P.err = ctx->err;
   const int grid = std::max(1, std::min(ctx->num_sms, (P.rows + pl.T - 1) / pl.T));
   cudaLaunchConfig_t cfg = {};

@@ -55,7 +55,7 @@ namespace unltd {
 // all-reduce number rank src completed writing here), then two parities x
 // kPeerMaxRanks source slots of kPeerMaxCount 8-byte words.
 constexpr int kPeerMaxRanks = 8;
-constexpr size_t kPeerMaxCount = 16384;  // floats (or u64) per all-reduce
+constexpr size_t kPeerMaxCount = 131072;  // floats (or u64) per all-reduce: 32 sequences x 4096
 constexpr size_t kPeerFlagBytes = 256;
 constexpr size_t kPeerSlotBytes = kPeerMaxCount * 8;
 constexpr size_t kPeerAreaBytes = kPeerFlagBytes + 2 * kPeerMaxRanks * kPeerSlotBytes;
@@ -160,6 +160,10 @@ struct BatchGemvArgs {
   unsigned *done = nullptr;
   uint32_t *token = nullptr;
   size_t tstride = 1;                 // token of sequence s at token[s * tstride]
+  // a vocab shard: the global index of row 0; non-null key_out: every
+  // sequence's final argmax key there instead of its token
+  int row0 = 0;
+  unsigned long long *key_out = nullptr;
 };
 int32_t gemv_batch_launch(unltd_ctx ctx, const BatchGemvArgs &a);
 // Bytes of the batched x images of nseq sequences for w.
