@@ -408,9 +408,9 @@ def decode_bench(n_tokens, with_cpu, rank=0, world=1, dist=None, profile_region=
         "launches_per_step": info["launches_per_step"], "graph": "one CUDA graph per token",
         "arithmetic": ("Q8K_EXACT projections; f32/f64 ops in the reference's order (hidden states bit-identical to "
                        "the oracle)" if world == 1 else
-                       "Q8K_EXACT projections; row-split partial outputs summed in rank order over NVLink peer "
-                       "memory, fused into the GEMVs (same greedy stream as the oracle; hidden state within 1e-3 "
-                       "max-rel of it, logits bit-identical given that hidden state)"),
+                       "Q8K_EXACT projections; row-split partial outputs summed in rank order by the NVLink peer "
+                       "all-reduce kernel (bit-identical to the oracle of the sharded arithmetic; same greedy stream "
+                       "as the one-device oracle)"),
         "tokens_tail": [int(t) for t in toks[-4:]],
         "distinct_tokens": len(set(int(t) for t in toks)),
     }
