@@ -351,7 +351,7 @@ def prefill_bench(m, cfg, st, pos0, n):
 
 
 def decode_bench(n_tokens, with_cpu, rank=0, world=1, dist=None, profile_region=False, batch=32, profile_batch=False,
-                 prefill=256):
+                 prefill=256, layers=0):
     """BASELINE configs 3 and 4: greedy decode of the synthetic 9B-class hybrid
     model from a 2048-position context through unltd_qwen35_decode, on one GPU
     or tensor-parallel over `world` GPUs (one process each). Device-timed on
@@ -360,7 +360,9 @@ def decode_bench(n_tokens, with_cpu, rank=0, world=1, dist=None, profile_region=
 
     import unltd_gpu as ug
 
-    cfg = synth.QWEN35_9B
+    cfg = dict(synth.QWEN35_9B)
+    if layers:  # profiling: the same attention and recurrent layers, fewer of them, small FFN and vocab
+        cfg.update(n_layer=layers, n_ff=1024, vocab=1000)
     pos0 = 2048
     tensors = synth.qwen35_model(cfg, 2026)
     st = synth.qwen35_state(cfg, pos0, 2027)
@@ -539,6 +541,10 @@ def main():
                     help="bracket the timed decode with cudaProfilerStart/Stop (ncu --profile-from-start off)")
     ap.add_argument("--profile-batch", action="store_true",
                     help="bracket the timed batch decode instead (ncu --profile-from-start off)")
+    ap.add_argument("--decode-layers", type=int, default=0,
+                    help="profiling: a model with this many layers of the 9B shapes (small FFN and vocab)")
+    ap.add_argument("--batch-gemv", default=None, metavar="DTYPE:DIM_IN:DIM_OUT:N_SEQ",
+                    help="profiling: four unltd_gemv_batch calls on seeded weights (e.g. q4k:4096:12288:32)")
     args = ap.parse_args()
     if args.impl == "reference":
         return run_reference(args)
@@ -564,6 +570,20 @@ def main():
     stream = torch.cuda.current_stream()
     ctx = ug.Context(local, stream=stream.cuda_stream)
 
+    if args.batch_gemv:
+        dt, di, do, ns = args.batch_gemv.split(":")
+        dtype = {"q4k": ug.Q4K, "q6k": ug.Q6K}[dt]
+        di, do, ns = int(di), int(do), int(ns)
+        w = ctx.upload(synth.quant_weights(dtype, di, do, seed=3), dtype, di, do)
+        X = torch.randn(ns, di, device="cuda")
+        Y = torch.empty(ns, do, device="cuda")
+        for _ in range(4):
+            ctx.gemv_batch(w, X, Y, ns)
+        torch.cuda.synchronize()
+        w.free()
+        ctx.close()
+        return
+
     if args.gemm_only:
         if rank == 0:
             os.write(out_fd, (json.dumps({"metric": "config-2 GEMM", "gemm_prefill": gemm_bench(ctx, stream, args.steps)})
@@ -573,7 +593,8 @@ def main():
 
     if args.decode_only:
         d = decode_bench(args.decode_tokens, with_cpu=False, rank=rank, world=world, dist=dist, batch=args.decode_batch,
-                         profile_batch=args.profile_batch,
+                         profile_batch=args.profile_batch, layers=args.decode_layers,
+                         prefill=0 if args.decode_layers else 256,
                          profile_region=args.profile_region)
         if rank == 0:
             os.write(out_fd, (json.dumps({"metric": "decode tok/s", "decode": d}) + "\n").encode())
