@@ -362,7 +362,7 @@ def decode_bench(n_tokens, with_cpu, rank=0, world=1, dist=None, profile_region=
 
     cfg = dict(synth.QWEN35_9B)
     if layers:  # profiling: the same attention and recurrent layers, fewer of them, small FFN and vocab
-        cfg.update(n_layer=layers, n_ff=1024, vocab=1000)
+        cfg.update(n_layer=layers, n_ff=1024, vocab=4096)
     pos0 = 2048
     tensors = synth.qwen35_model(cfg, 2026)
     st = synth.qwen35_state(cfg, pos0, 2027)
