@@ -812,23 +812,33 @@ template <int HDV, int GN>
 __device__ __forceinline__ void score_pass(const double *qsm, const float (&kv)[4][HDV / 32], const AttnArgs &a,
                                            int kvh, int G, int g0, int gn, int p0, int n_ctx, int warp, int lane) {
   constexpr int E = HDV / 32, L = 4 * GN;
+  static_assert(E % 2 == 0, "tree level 1 pairs elements");
   double v[16];
 #pragma unroll
   for (int i = 0; i < 16; i++) v[i] = 0.0;
+  // head-major: a head's q slice is read from shared memory once for the
+  // warp's four positions (each k element converted per use)
 #pragma unroll
-  for (int r = 0; r < 4; r++) {
-    double kd[E];  // position r's k row, converted once for all heads
+  for (int gi = 0; gi < GN; gi++) {
+    if (gi < gn) {
+      const double2 *qg2 = reinterpret_cast<const double2 *>(qsm + (g0 + gi) * HDV + lane * E);
+      double qd[E];
 #pragma unroll
-    for (int t = 0; t < E; t++) kd[t] = (double)kv[r][t];
+      for (int t = 0; t < E; t += 2) {
+        const double2 q2 = qg2[t / 2];
+        qd[t] = q2.x;
+        qd[t + 1] = q2.y;
+      }
 #pragma unroll
-    for (int gi = 0; gi < GN; gi++) {
-      if (gi < gn) {
-        const double *qg = qsm + (g0 + gi) * HDV + lane * E;
+      for (int r = 0; r < 4; r++) {
+        // tree level 1 as fma: q k of two f32 values is exact in f64, so
+        // fma(q_t, k_t, q_t+1 k_t+1) rounds exactly as the pair's add does
         double pr[E];
 #pragma unroll
-        for (int t = 0; t < E; t++) pr[t] = __dmul_rn(qg[t], kd[t]);
+        for (int t = 0; t < E; t += 2)
+          pr[t] = __fma_rn(qd[t], (double)kv[r][t], __dmul_rn(qd[t + 1], (double)kv[r][t + 1]));
 #pragma unroll
-        for (int w = 1; w < E; w <<= 1)
+        for (int w = 2; w < E; w <<= 1)
 #pragma unroll
           for (int t = 0; t < E; t += 2 * w) pr[t] = __dadd_rn(pr[t], pr[t + w]);
         v[r * GN + gi] = pr[0];
@@ -965,12 +975,14 @@ __global__ void __launch_bounds__(HDV) attn_values_kernel(AttnArgs a) {
   double S[kMaxGroup], Q[kMaxGroup];
 #pragma unroll
   for (int g = 0; g < kMaxGroup; g++) S[g] = Q[g] = 0.0;
+  // soft[p] * v[p] of two f32 values is exact in f64, so one fma rounds
+  // exactly as the reference's add of the product does
   for (int p = 0; p < len; p++) {
     const double v = (double)vsm[p * HDV + c];
 #pragma unroll
     for (int g = 0; g < kMaxGroup; g++) {
       if (g < G) {
-        S[g] = __dadd_rn(S[g], __dmul_rn(ssoft[g][p], v));
+        S[g] = __fma_rn(ssoft[g][p], v, S[g]);
         Q[g] = __dadd_rn(Q[g], fabs(S[g]));
       }
     }
