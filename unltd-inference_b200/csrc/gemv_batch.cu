@@ -8,21 +8,22 @@
 //
 // The weights stream through shared memory once for all sequences (bulk
 // copies by a producer warp, as in the single-sequence kernels); each compute
-// warp owns 16 rows x a group of sequences for the whole row and keeps the
+// warp owns 16 rows x a group of 8 sequences for the whole row and keeps the
 // f32 chains of its (row, class, sequence) triples in registers, so no chain
-// buffer or chain warp is needed. The x images (one per sequence, the Q8_K
-// layouts of unltd_internal.cuh) are read from global memory (L2).
+// buffer or chain warp is needed. x comes from the batched images
+// (unltd_internal.cuh, bimg_*): per span and group of 8 sequences, laid out
+// as this kernel's B fragments, read from global memory (L2) one block ahead.
 //
-//  * Q4_K: the sequences are the MMA's N dimension. For class k the K
-//    dimension is the class's 32 elements of the block (4 per scale group);
-//    each 4-element word of a group shares the group's 6-bit scale, so the
-//    scale is folded into A as two digits, sc = sc_lo + 8 sc_hi (0..7 each):
-//    A_lo = q * sc_lo, A_hi = q * sc_hi (<= 105, one 32-bit multiply per
-//    packed word, no carries), and sumi[k] = D_lo + 8 D_hi exactly. The min
-//    term is an m16n8k16 MMA of the mins against the balanced low / high
+// The sequences are the MMA's N dimension. For class k the K dimension is
+// the class's 32 elements of the block (4 per scale group):
+//  * Q4_K: each 4-element word of a group shares the group's 6-bit scale, so
+//    the scale is folded into A as two digits, sc = sc_lo + 8 sc_hi (0..7
+//    each): A_lo = q * sc_lo, A_hi = q * sc_hi (<= 105, one 32-bit multiply
+//    per packed word, no carries), and sumi[k] = D_lo + 8 D_hi exactly. The
+//    min term is an m16n8k16 MMA of the mins against the balanced low / high
 //    bytes of the sequences' group sums.
-//  * Q6_K: per sequence, the class-masked MMAs of the single-sequence kernel
-//    (A operands and scales built once per block and reused).
+//  * Q6_K: A comes from digit planes made once per weight (batch6_convert):
+//    v = sc * (q - 32) = 128 w1 + w0, so sumi[k] = D0 + 128 D1 exactly.
 #include <algorithm>
 #include <mutex>
 #include <vector>
