@@ -532,54 +532,63 @@ __global__ void __launch_bounds__(HD) recr_mid_kernel(RecrArgs a) {
   }
 }
 
-// The recurrent layer for a prefill chunk of T tokens in one launch: each
-// CTA (v-head h, quarter of its columns) keeps its state slice in registers
-// and runs recr_mid_kernel's step for tokens 0 .. T-1 in order. The conv
-// window of token t (position pos + t) takes the rows of earlier chunk tokens
-// from their projections (pss bytes apart) and older rows from the ring,
-// which this kernel does not write (CTAs of other heads read the same q/k
-// channels; prefill_ring_kernel updates it after the launch). The gated norm of
-// token t's span runs in the span's last CTA for that token (a counter per
-// token and span). The same operations per token as recr_mid_kernel.
+// The recurrent layer for a prefill chunk of T tokens in one launch, with
+// the operations of recr_mid_kernel per token. Each CTA (v-head h, quarter of
+// its columns) works in two phases:
+//  A. what does not depend on the GDN state, for every token at once (warp
+//     w takes tokens w, w + 4, ...): the conv (the window rows of earlier
+//     chunk tokens from their projections, pss bytes apart, older rows from
+//     the ring, which this kernel does not write), silu, the l2 norms of q
+//     and k (warp sums resolved exactly as in block_sum2 + resolve_sum),
+//     beta and the gate, into shared memory;
+//  B. the state recurrence token by token: each warp owns eight columns of
+//     the state slice (registers), so the loop needs no block barrier;
+//     y of token t goes to its activations.
+// The gated norm of every (span, token) runs afterwards (prefill_gnorm_kernel)
+// and the ring is updated after that (prefill_ring_kernel).
 struct RecrChunkArgs {
   RecrArgs r;   // r.proj / r.y: token 0's; r.pos: the session's position (the chunk's first)
   size_t pss;   // bytes between consecutive tokens' activations
   int T;
-  int nspan;    // spans of y: the counters of token t at r.span_ctr + t * nspan
+};
+
+constexpr int kChunkTok = 32;  // tokens of a prefill chunk (kPrefillLanes)
+
+template <int HD>
+struct RecrChunkSmem {
+  float q[kChunkTok][HD], k[kChunkTok][HD], v[kChunkTok][kGdnCols];
+  float beta[kChunkTok], g[kChunkTok];
 };
 
 template <int HD>
 __global__ void __launch_bounds__(HD) recr_chunk_kernel(RecrChunkArgs c) {
+  static_assert(HD == 128, "four warps, four channels per lane");
   pdl_trigger();
-  __shared__ float qs[HD], ks[HD];
+  extern __shared__ __align__(16) uint8_t csm[];
+  RecrChunkSmem<HD> &sm = *reinterpret_cast<RecrChunkSmem<HD> *>(csm);
   __shared__ float gdn_fb[kGdnCols * HD];
-  __shared__ double red[2 * HD / 32];
-  __shared__ float s_f[2];
-  __shared__ float vs[kGdnCols];
-  __shared__ unsigned s_last;
   pdl_wait();
   const RecrArgs &a = c.r;
   const int h = blockIdx.x, quarter = blockIdx.y, j = threadIdx.x;
+  const int warp = j >> 5, lane = j & 31;
   const int qk = h % a.nqk;
   const int pos0 = *a.pos, K = a.K;
   const int c0 = quarter * kGdnCols;
-  const int chq = qk * HD + j, chk = a.nqk * HD + qk * HD + j;
-  const int chv = 2 * a.nqk * HD + h * HD + c0 + (j & (kGdnCols - 1));
-  const int jc = j >> 2, w = j & 3;
   constexpr int RW = HD / 4;
+  const int jc = j >> 2, w = j & 3;
   float *S = a.state + (size_t)h * HD * HD + c0 + jc;
   float st[RW];
 #pragma unroll
   for (int ii = 0; ii < RW; ii++) st[ii] = S[(size_t)(RW * w + ii) * HD];
   const float dtb = a.dt_bias[h], ssa = a.ssm_a[h];
-  auto proj_of = [&](int t) { return reinterpret_cast<const float *>(reinterpret_cast<const uint8_t *>(a.proj) + (size_t)t * c.pss); };
-  const int span = (h * HD) >> 8;
-#pragma unroll 1
-  for (int t = 0; t < c.T; t++) {
+  auto proj_of = [&](int t) {
+    return reinterpret_cast<const float *>(reinterpret_cast<const uint8_t *>(a.proj) + (size_t)t * c.pss);
+  };
+
+  // ---- A: conv, silu, l2 norms, beta, gate of every token ----
+  for (int t = warp; t < c.T; t += 4) {
     const float *pr = proj_of(t);
     const int pos = pos0 + t;
-    const float beta_raw = pr[a.beta_off + h], alpha = pr[a.alpha_off + h];
-    // depthwise conv over [window rows, current qkv] (kernels.rs:265-310), silu
     auto conv = [&](int ch) {
       float sacc = 0.0f;
       for (int tau = 0; tau < K; tau++) {
@@ -594,69 +603,92 @@ __global__ void __launch_bounds__(HD) recr_chunk_kernel(RecrChunkArgs c) {
       }
       return sacc;
     };
-    float q = silu_f(conv(chq)), k = silu_f(conv(chk)), v = 0.0f;
-    if (j < kGdnCols) v = silu_f(conv(chv));
-    // l2_norm_rows of q and k (kernels.rs:236-252)
-    qs[j] = q;
-    ks[j] = k;
-    double Sq = (double)__fmul_rn(q, q), Sk = (double)__fmul_rn(k, k);
-    block_sum2<HD>(Sq, Sk, red);
+    float q[4], k[4];
+    double Sq = 0.0, Sk = 0.0;
+#pragma unroll
+    for (int m = 0; m < 4; m++) {
+      const int jj = lane + 32 * m;
+      q[m] = silu_f(conv(qk * HD + jj));
+      k[m] = silu_f(conv(a.nqk * HD + qk * HD + jj));
+      sm.q[t][jj] = q[m];
+      sm.k[t][jj] = k[m];
+      Sq += (double)__fmul_rn(q[m], q[m]);
+      Sk += (double)__fmul_rn(k[m], k[m]);
+    }
+    sm.v[t][lane] = silu_f(conv(2 * a.nqk * HD + h * HD + c0 + lane));
+#pragma unroll
+    for (int o = 16; o; o >>= 1) {
+      Sq += __shfl_xor_sync(~0u, Sq, o);
+      Sk += __shfl_xor_sync(~0u, Sk, o);
+    }
+    // l2_norm_rows (kernels.rs:236-252): the sum of squares resolved exactly;
+    // rare ambiguity: lane 0 sums the squares left to right
     float fq, fk;
     const bool okq = resolve_sum(Sq, Sq, HD, ToF32{}, &fq);
     const bool okk = resolve_sum(Sk, Sk, HD, ToF32{}, &fk);
+    __syncwarp();
     if (!okq || !okk) {
-      __syncthreads();
-      if (j < 2 && !(j == 0 ? okq : okk)) {
-        const float *src = j == 0 ? qs : ks;
-        double s2 = 0.0;
+      float f2[2] = {fq, fk};
+      if (lane == 0) {
+        for (int which = 0; which < 2; which++) {
+          if (which == 0 ? okq : okk) continue;
+          const float *src = which == 0 ? sm.q[t] : sm.k[t];
+          double s2 = 0.0;
 #pragma unroll 1
-        for (int i = 0; i < HD; i++) s2 = __dadd_rn(s2, (double)__fmul_rn(src[i], src[i]));
-        s_f[j] = (float)s2;
+          for (int i = 0; i < HD; i++) s2 = __dadd_rn(s2, (double)__fmul_rn(src[i], src[i]));
+          f2[which] = (float)s2;
+        }
       }
-      __syncthreads();
-      if (!okq) fq = s_f[0];
-      if (!okk) fk = s_f[1];
+      fq = __shfl_sync(~0u, f2[0], 0);
+      fk = __shfl_sync(~0u, f2[1], 0);
     }
-    q = __fmul_rn(q, __fdiv_rn(1.0f, fmaxf(__fsqrt_rn(fq), a.eps)));
-    k = __fmul_rn(k, __fdiv_rn(1.0f, fmaxf(__fsqrt_rn(fk), a.eps)));
-    __syncthreads();
-    qs[j] = q;
-    ks[j] = k;
-    const float beta = sigmoid_f(beta_raw);
-    const float gate = __fmul_rn(softplus_f(__fadd_rn(alpha, dtb)), ssa);
-    const float g = exp_cr(gate);
-    if (j < kGdnCols) vs[j] = v;
-    __syncthreads();
-    // gdn_fused_step (as recr_mid_kernel)
+    const float iq = __fdiv_rn(1.0f, fmaxf(__fsqrt_rn(fq), a.eps));
+    const float ik = __fdiv_rn(1.0f, fmaxf(__fsqrt_rn(fk), a.eps));
+    __syncwarp();
+#pragma unroll
+    for (int m = 0; m < 4; m++) {
+      sm.q[t][lane + 32 * m] = __fmul_rn(q[m], iq);
+      sm.k[t][lane + 32 * m] = __fmul_rn(k[m], ik);
+    }
+    if (lane == 0) {
+      const float beta_raw = pr[a.beta_off + h], alpha = pr[a.alpha_off + h];
+      sm.beta[t] = sigmoid_f(beta_raw);
+      sm.g[t] = exp_cr(__fmul_rn(softplus_f(__fadd_rn(alpha, dtb)), ssa));
+    }
+  }
+  __syncthreads();
+
+  // ---- B: gdn_fused_step token by token (as recr_mid_kernel) ----
+#pragma unroll 1
+  for (int t = 0; t < c.T; t++) {
+    const float g = sm.g[t], beta = sm.beta[t];
+    const float *ks = sm.k[t], *qs = sm.q[t];
 #pragma unroll
     for (int ii = 0; ii < RW; ii++) st[ii] = __fmul_rn(st[ii], g);
     const float dk = gdn_dot<RW>(st, ks + RW * w, ks, gdn_fb + jc * HD, w);
-    const float d = __fmul_rn(__fsub_rn(vs[jc], dk), beta);
+    const float d = __fmul_rn(__fsub_rn(sm.v[t][jc], dk), beta);
 #pragma unroll
     for (int ii = 0; ii < RW; ii++) st[ii] = __fadd_rn(st[ii], __fmul_rn(ks[RW * w + ii], d));
     const float dq = gdn_dot<RW>(st, qs + RW * w, qs, gdn_fb + jc * HD, w);
     float *yt = reinterpret_cast<float *>(reinterpret_cast<uint8_t *>(a.y) + (size_t)t * c.pss);
     if (w == 0) yt[h * HD + c0 + jc] = __fmul_rn(dq, __fdiv_rn(1.0f, __fsqrt_rn((float)HD)));
-    // the span's last CTA for this token runs its gated norm
-    unsigned *ctr = a.span_ctr + (size_t)t * c.nspan;
-    __threadfence();
-    __syncthreads();
-    if (j == 0) {
-      const unsigned n = (256 / HD) * gridDim.y;
-      const unsigned prev = atomicAdd(ctr + span, 1u);
-      s_last = prev == n - 1;
-      if (prev == n - 1) ctr[span] = 0u;
-    }
-    __syncthreads();
-    if (s_last) {
-      __threadfence();
-      gated_norm_span<HD>(yt, pr + a.z_off, a.ssm_norm, a.eps, nullptr, nullptr, span,
-                          seq_bimg(a.bimg, a.nsg, t, span), t & 7);
-    }
-    __syncthreads();
   }
 #pragma unroll
   for (int ii = 0; ii < RW; ii++) S[(size_t)(RW * w + ii) * HD] = st[ii];
+}
+
+// The gated norm of the recurrent output and its Q8_K image, for every
+// (span, token) of a prefill chunk (grid spans x T; gated_norm_span).
+template <int HD>
+__global__ void __launch_bounds__(HD) prefill_gnorm_kernel(const float *y, const float *proj, size_t pss, int z_off,
+                                                           const float *ssm_norm, float eps, uint8_t *bimg, int nsg) {
+  pdl_trigger();
+  pdl_wait();
+  const int span = blockIdx.x, t = blockIdx.y;
+  const float *yt = reinterpret_cast<const float *>(reinterpret_cast<const uint8_t *>(y) + (size_t)t * pss);
+  const float *pr = reinterpret_cast<const float *>(reinterpret_cast<const uint8_t *>(proj) + (size_t)t * pss);
+  gated_norm_span<HD>(yt, pr + z_off, ssm_norm, eps, nullptr, nullptr, span,
+                      bimg + bimg_block((size_t)span, t >> 3, nsg), t & 7);
 }
 
 // The conv windows after a prefill chunk: the chunk's last K positions'
@@ -1214,8 +1246,6 @@ struct unltd_qwen35_session_s {
     int *pos = nullptr;
     uint32_t *tok = nullptr;  // the chunk's tokens, contiguous; then the LM head's
     uint8_t *bimg = nullptr;
-    unsigned *span_ctr = nullptr;  // the recurrent chunk kernel's counters: token t at + t * nspan
-    int nspan = 0;
   } pf;
   std::vector<int> seq_pos;
   // activations
@@ -1849,6 +1879,7 @@ int32_t run_step(unltd_qwen35_session s) {
 }
 
 constexpr int kPrefillLanes = 32;
+static_assert(kPrefillLanes == kChunkTok, "the recurrent chunk kernel holds a chunk's tokens");
 constexpr int kPrefillNsg = kPrefillLanes / 8;
 
 // The prefill workspace: the activation buffers of kPrefillLanes tokens.
@@ -1883,9 +1914,8 @@ int32_t prefill_alloc(unltd_qwen35_session s) {
   add((void **)&P.pos, 4);
   P.ss = round_up(off, 4096);
   const size_t spans = (size_t)std::max(d.n, d.nff) / 256;
-  P.nspan = d.nvl * d.hd / 256 + 1;
-  const size_t img_bytes = spans * kPrefillNsg * kBImgBlock, ctr_bytes = (size_t)kPrefillLanes * P.nspan * 4;
-  const size_t extra = kPrefillLanes * 4 + img_bytes + ctr_bytes;
+  const size_t img_bytes = spans * kPrefillNsg * kBImgBlock;
+  const size_t extra = kPrefillLanes * 4 + img_bytes;
   cudaError_t e = cudaMalloc(&P.arena, P.ss * kPrefillLanes + extra);
   if (e == cudaSuccess) e = cudaMemset(P.arena, 0, P.ss * kPrefillLanes + extra);
   if (e != cudaSuccess) {
@@ -1896,7 +1926,6 @@ int32_t prefill_alloc(unltd_qwen35_session s) {
   for (auto &x : sl) *x.p = P.arena + x.off;
   P.tok = reinterpret_cast<uint32_t *>(P.arena + P.ss * kPrefillLanes);
   P.bimg = P.arena + P.ss * kPrefillLanes + kPrefillLanes * 4;
-  P.span_ctr = reinterpret_cast<unsigned *>(P.bimg + img_bytes);
   s->bufs.push_back(P.arena);
   // the batched GEMV's operands of the Q6_K projections, its kernels' attributes
   std::vector<unltd_weight_s *> ws{m->output};
@@ -1907,6 +1936,10 @@ int32_t prefill_alloc(unltd_qwen35_session s) {
     ws.push_back(L.down);
   }
   int32_t rc = cuda_error(gemv_batch_prewarm(m->ctx->device), "batched GEMV attributes");
+  if (!rc)
+    rc = cuda_error(cudaFuncSetAttribute(recr_chunk_kernel<128>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         (int)sizeof(RecrChunkSmem<128>)),
+                    "prefill recurrence attributes");
   for (auto *w : ws)
     if (!rc) rc = gemv_batch_prepare(m->ctx, w);
   return rc;
@@ -1985,7 +2018,7 @@ int32_t enqueue_prefill(unltd_qwen35_session s, int T, bool head) {
       a.beta_off = d.dconvl + d.nvl * d.hd;
       a.alpha_off = a.beta_off + d.nvl;
       a.eps = d.eps;
-      a.span_ctr = P.span_ctr;
+      a.span_ctr = nullptr;
       a.img4 = nullptr;
       a.img6 = nullptr;
       a.ss = 0;
@@ -1993,8 +2026,12 @@ int32_t enqueue_prefill(unltd_qwen35_session s, int T, bool head) {
       a.nsg = kPrefillNsg;
       c.pss = pss;
       c.T = T;
-      c.nspan = P.nspan;
-      chk(launch_pdl(recr_chunk_kernel<128>, dim3(d.nvl, 128 / kGdnCols), dim3(128), 0, st, c), "prefill recurrence");
+      chk(launch_pdl(recr_chunk_kernel<128>, dim3(d.nvl, 128 / kGdnCols), dim3(128), sizeof(RecrChunkSmem<128>), st,
+                     c),
+          "prefill recurrence");
+      chk(launch_pdl(prefill_gnorm_kernel<128>, dim3(d.nvl * d.hd / 256, T), dim3(128), 0, st, (const float *)P.Y,
+                     (const float *)P.proj, pss, d.dconvl, (const float *)L.ssm_norm, d.eps, P.bimg, kPrefillNsg),
+          "prefill gated norm");
       const int nring = std::min(T, d.K) * d.dconvl;
       chk(launch_pdl(prefill_ring_kernel, dim3((nring + 255) / 256), dim3(256), 0, st, (const float *)P.proj, pss, T,
                      s->ring[L.slot], d.dconvl, d.K, (const int *)s->pos),
