@@ -322,7 +322,7 @@ def decode_batch_bench(m, cfg, st, pos0, n_seq, n_steps, profile_region=False, w
     return out
 
 
-def prefill_bench(m, cfg, st, pos0, n):
+def prefill_bench(m, cfg, st, pos0, n, profile_region=False):
     """A prompt of n seeded tokens after the 2048-position state through
     unltd_qwen35_prefill (32-token chunks, each weight read once per chunk;
     the same bits as the token-by-token unltd_qwen35_feed). Device-timed on
@@ -336,12 +336,16 @@ def prefill_bench(m, cfg, st, pos0, n):
     ext = torch.cuda.ExternalStream(s.info()["stream"])
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     torch.cuda.synchronize()
+    if profile_region:
+        torch.cuda.profiler.start()
     t0 = time.perf_counter()
     e0.record(ext)
     s.prefill(prompt[32:])
     e1.record(ext)
     torch.cuda.synchronize()
     wall = time.perf_counter() - t0
+    if profile_region:
+        torch.cuda.profiler.stop()
     ms = e0.elapsed_time(e1)
     s.close()
     return {"workload": f"qwen35_9b_synthetic_prefill_{n}_tokens_after_ctx2048", "tokens": n,
@@ -351,7 +355,7 @@ def prefill_bench(m, cfg, st, pos0, n):
 
 
 def decode_bench(n_tokens, with_cpu, rank=0, world=1, dist=None, profile_region=False, batch=32, profile_batch=False,
-                 prefill=256, layers=0):
+                 prefill=256, layers=0, profile_prefill=False):
     """BASELINE configs 3 and 4: greedy decode of the synthetic 9B-class hybrid
     model from a 2048-position context through unltd_qwen35_decode, on one GPU
     or tensor-parallel over `world` GPUs (one process each). Device-timed on
@@ -418,7 +422,7 @@ def decode_bench(n_tokens, with_cpu, rank=0, world=1, dist=None, profile_region=
     }
     s.close()
     if world == 1 and prefill > 0:
-        out["prefill"] = prefill_bench(m, cfg, st, pos0, prefill)
+        out["prefill"] = prefill_bench(m, cfg, st, pos0, prefill, profile_prefill)
     if batch > 1:
         out["batch"] = 1
         out["batch%d" % batch] = decode_batch_bench(m, cfg, st, pos0, batch, max(4, n_tokens // 4), profile_batch,
@@ -541,6 +545,8 @@ def main():
                     help="bracket the timed decode with cudaProfilerStart/Stop (ncu --profile-from-start off)")
     ap.add_argument("--profile-batch", action="store_true",
                     help="bracket the timed batch decode instead (ncu --profile-from-start off)")
+    ap.add_argument("--profile-prefill", action="store_true",
+                    help="bracket the timed prefill instead (ncu --profile-from-start off)")
     ap.add_argument("--decode-layers", type=int, default=0,
                     help="profiling: a model with this many layers of the 9B shapes (small FFN and vocab)")
     ap.add_argument("--batch-gemv", default=None, metavar="DTYPE:DIM_IN:DIM_OUT:N_SEQ",
@@ -595,7 +601,7 @@ def main():
         d = decode_bench(args.decode_tokens, with_cpu=False, rank=rank, world=world, dist=dist, batch=args.decode_batch,
                          profile_batch=args.profile_batch, layers=args.decode_layers,
                          prefill=0 if args.decode_layers else 256,
-                         profile_region=args.profile_region)
+                         profile_region=args.profile_region, profile_prefill=args.profile_prefill)
         if rank == 0:
             os.write(out_fd, (json.dumps({"metric": "decode tok/s", "decode": d}) + "\n").encode())
         ctx.close()

@@ -21,6 +21,7 @@
 // left-to-right.
 #include <cmath>
 #include <cstring>
+#include <type_traits>
 #include <map>
 #include <string>
 #include <vector>
@@ -258,7 +259,7 @@ constexpr int kGdnCols = 32;
 // with the running-error bound (see attn_combine_quant_kernel); when the
 // bound cannot decide, the column's terms go through shared memory and lane
 // w == 0 sums all of them left to right.
-template <int RW>
+template <int RW, int XP = 0>  // XP: x holds its four chunks RW + XP floats apart
 __device__ __forceinline__ float gdn_dot(const float (&st)[RW], const float *xw, const float *x, float *fb, int w) {
   double Sw = 0.0, Qw = 0.0;
 #pragma unroll
@@ -288,7 +289,7 @@ __device__ __forceinline__ float gdn_dot(const float (&st)[RW], const float *xw,
     if (amb && w == 0) {
       double s = 0.0;
 #pragma unroll 1
-      for (int i = 0; i < 4 * RW; i++) s = __dadd_rn(s, (double)__fmul_rn(fb[i], x[i]));
+      for (int i = 0; i < 4 * RW; i++) s = __dadd_rn(s, (double)__fmul_rn(fb[i], x[i + (i / RW) * XP]));
       fb[0] = (float)s;
     }
     __syncwarp();
@@ -554,13 +555,19 @@ struct RecrChunkArgs {
 
 constexpr int kChunkTok = 32;  // tokens of a prefill chunk (kPrefillLanes)
 
+// q and k rows of a token hold their four quarter chunks (HD / 4 channels each)
+// kChunkPad floats apart, so the four lanes of a column (one chunk each) read
+// different banks
+constexpr int kChunkPad = 8;
 template <int HD>
 struct RecrChunkSmem {
-  float q[kChunkTok][HD], k[kChunkTok][HD], v[kChunkTok][kGdnCols];
+  static constexpr int kRow = HD + 4 * kChunkPad;
+  static __device__ __forceinline__ int at(int i) { return i + (i / (HD / 4)) * kChunkPad; }
+  float q[kChunkTok][kRow], k[kChunkTok][kRow], v[kChunkTok][kGdnCols];
   float beta[kChunkTok], g[kChunkTok];
 };
 
-template <int HD>
+template <int HD, int KT>  // KT: conv_kernel known at compile time (0: c.r.K at run time)
 __global__ void __launch_bounds__(HD) recr_chunk_kernel(RecrChunkArgs c) {
   static_assert(HD == 128, "four warps, four channels per lane");
   pdl_trigger();
@@ -572,7 +579,7 @@ __global__ void __launch_bounds__(HD) recr_chunk_kernel(RecrChunkArgs c) {
   const int h = blockIdx.x, quarter = blockIdx.y, j = threadIdx.x;
   const int warp = j >> 5, lane = j & 31;
   const int qk = h % a.nqk;
-  const int pos0 = *a.pos, K = a.K;
+  const int pos0 = *a.pos, K = KT > 0 ? KT : a.K;
   const int c0 = quarter * kGdnCols;
   constexpr int RW = HD / 4;
   const int jc = j >> 2, w = j & 3;
@@ -585,48 +592,111 @@ __global__ void __launch_bounds__(HD) recr_chunk_kernel(RecrChunkArgs c) {
     return reinterpret_cast<const float *>(reinterpret_cast<const uint8_t *>(a.proj) + (size_t)t * c.pss);
   };
 
-  // ---- A: conv, silu, l2 norms, beta, gate of every token ----
-  for (int t = warp; t < c.T; t += 4) {
+  // ---- A0: the chunk's q, k, v channels of this CTA into shared memory
+  // (independent loads, column j by thread j); beta and the gate of token
+  // t by thread t ----
+  const int chq0 = qk * HD, chk0 = a.nqk * HD + qk * HD, chv0 = 2 * a.nqk * HD + h * HD + c0;
+  using Sm = RecrChunkSmem<HD>;
+  const int jp = Sm::at(j);
+#pragma unroll 4
+  for (int t = 0; t < c.T; t++) {
     const float *pr = proj_of(t);
-    const int pos = pos0 + t;
-    auto conv = [&](int ch) {
-      float sacc = 0.0f;
-      for (int tau = 0; tau < K; tau++) {
-        float xv;
-        if (tau == K - 1) {
-          xv = pr[ch];
-        } else {
-          const int qp = pos - (K - 1) + tau;  // the row's position
-          xv = qp >= pos0 ? proj_of(qp - pos0)[ch] : a.ring[(size_t)((pos + tau) % K) * a.dconv + ch];
-        }
-        sacc = __fadd_rn(sacc, __fmul_rn(xv, a.convw[(size_t)ch * K + tau]));
+    sm.q[t][jp] = pr[chq0 + j];
+    sm.k[t][jp] = pr[chk0 + j];
+    if (j < kGdnCols) sm.v[t][j] = pr[chv0 + j];
+  }
+  if (j < c.T) {
+    const float *pr = proj_of(j);
+    const float beta_raw = pr[a.beta_off + h], alpha = pr[a.alpha_off + h];
+    sm.beta[j] = sigmoid_f(beta_raw);
+    sm.g[j] = exp_cr(__fmul_rn(softplus_f(__fadd_rn(alpha, dtb)), ssa));
+  }
+  // ---- A1: depthwise conv over [window rows, current qkv] (kernels.rs:265-310)
+  // and silu, in place: thread j owns column j, tokens in descending order, so
+  // the rows token t reads (its own and the K-1 before it, or the ring's for
+  // positions before the chunk) are still the raw projections ----
+  {
+    // NC columns of one stride at once, four tokens per pass: the loads of a
+    // pass precede its stores, and its 4 x NC silu are independent
+    auto conv_cols = [&](auto ncs, float *const *col, int stride, const int *ch) {
+      constexpr int NC = decltype(ncs)::value;
+      float wr[NC][KT > 0 ? KT : 1];
+      if constexpr (KT > 0) {
+#pragma unroll
+        for (int n = 0; n < NC; n++)
+#pragma unroll
+          for (int tau = 0; tau < KT; tau++) wr[n][tau] = a.convw[(size_t)ch[n] * KT + tau];
       }
-      return sacc;
+#pragma unroll 1
+      for (int t0 = c.T - 1; t0 >= 0; t0 -= 4) {
+        float r[4][NC];
+#pragma unroll
+        for (int u = 0; u < 4; u++) {
+          const int t = t0 - u, pos = pos0 + t;
+#pragma unroll
+          for (int n = 0; n < NC; n++) {
+            float sacc = 0.0f;
+            if (t >= 0) {
+              if constexpr (KT > 0) {
+#pragma unroll
+                for (int tau = 0; tau < KT; tau++) {
+                  const int qp = pos - (KT - 1) + tau;  // the row's position
+                  const float xv = qp >= pos0 ? col[n][(qp - pos0) * stride]
+                                              : a.ring[(size_t)((pos + tau) % KT) * a.dconv + ch[n]];
+                  sacc = __fadd_rn(sacc, __fmul_rn(xv, wr[n][tau]));
+                }
+              } else {
+                for (int tau = 0; tau < K; tau++) {
+                  const int qp = pos - (K - 1) + tau;
+                  const float xv = qp >= pos0 ? col[n][(qp - pos0) * stride]
+                                              : a.ring[(size_t)((pos + tau) % K) * a.dconv + ch[n]];
+                  sacc = __fadd_rn(sacc, __fmul_rn(xv, a.convw[(size_t)ch[n] * K + tau]));
+                }
+              }
+            }
+            r[u][n] = sacc;
+          }
+        }
+#pragma unroll
+        for (int u = 0; u < 4; u++)
+#pragma unroll
+          for (int n = 0; n < NC; n++)
+            if (t0 - u >= 0) col[n][(t0 - u) * stride] = silu_f(r[u][n]);
+      }
     };
+    {
+      float *const cols[2] = {&sm.q[0][jp], &sm.k[0][jp]};
+      const int chs[2] = {chq0 + j, chk0 + j};
+      conv_cols(std::integral_constant<int, 2>{}, cols, Sm::kRow, chs);
+    }
+    if (j < kGdnCols) {
+      float *const cols[1] = {&sm.v[0][j]};
+      const int chs[1] = {chv0 + j};
+      conv_cols(std::integral_constant<int, 1>{}, cols, kGdnCols, chs);
+    }
+  }
+  __syncthreads();
+  // ---- A2: l2_norm_rows of q and k (kernels.rs:236-252): warp w takes tokens
+  // w, w + 4, ...; the sums of squares resolved exactly; rare ambiguity: lane 0
+  // sums the squares left to right ----
+  for (int t = warp; t < c.T; t += 4) {
     float q[4], k[4];
     double Sq = 0.0, Sk = 0.0;
 #pragma unroll
     for (int m = 0; m < 4; m++) {
-      const int jj = lane + 32 * m;
-      q[m] = silu_f(conv(qk * HD + jj));
-      k[m] = silu_f(conv(a.nqk * HD + qk * HD + jj));
-      sm.q[t][jj] = q[m];
-      sm.k[t][jj] = k[m];
+      q[m] = sm.q[t][Sm::at(lane + 32 * m)];
+      k[m] = sm.k[t][Sm::at(lane + 32 * m)];
       Sq += (double)__fmul_rn(q[m], q[m]);
       Sk += (double)__fmul_rn(k[m], k[m]);
     }
-    sm.v[t][lane] = silu_f(conv(2 * a.nqk * HD + h * HD + c0 + lane));
 #pragma unroll
     for (int o = 16; o; o >>= 1) {
       Sq += __shfl_xor_sync(~0u, Sq, o);
       Sk += __shfl_xor_sync(~0u, Sk, o);
     }
-    // l2_norm_rows (kernels.rs:236-252): the sum of squares resolved exactly;
-    // rare ambiguity: lane 0 sums the squares left to right
     float fq, fk;
     const bool okq = resolve_sum(Sq, Sq, HD, ToF32{}, &fq);
     const bool okk = resolve_sum(Sk, Sk, HD, ToF32{}, &fk);
-    __syncwarp();
     if (!okq || !okk) {
       float f2[2] = {fq, fk};
       if (lane == 0) {
@@ -635,7 +705,7 @@ __global__ void __launch_bounds__(HD) recr_chunk_kernel(RecrChunkArgs c) {
           const float *src = which == 0 ? sm.q[t] : sm.k[t];
           double s2 = 0.0;
 #pragma unroll 1
-          for (int i = 0; i < HD; i++) s2 = __dadd_rn(s2, (double)__fmul_rn(src[i], src[i]));
+          for (int i = 0; i < HD; i++) s2 = __dadd_rn(s2, (double)__fmul_rn(src[Sm::at(i)], src[Sm::at(i)]));
           f2[which] = (float)s2;
         }
       }
@@ -647,13 +717,8 @@ __global__ void __launch_bounds__(HD) recr_chunk_kernel(RecrChunkArgs c) {
     __syncwarp();
 #pragma unroll
     for (int m = 0; m < 4; m++) {
-      sm.q[t][lane + 32 * m] = __fmul_rn(q[m], iq);
-      sm.k[t][lane + 32 * m] = __fmul_rn(k[m], ik);
-    }
-    if (lane == 0) {
-      const float beta_raw = pr[a.beta_off + h], alpha = pr[a.alpha_off + h];
-      sm.beta[t] = sigmoid_f(beta_raw);
-      sm.g[t] = exp_cr(__fmul_rn(softplus_f(__fadd_rn(alpha, dtb)), ssa));
+      sm.q[t][Sm::at(lane + 32 * m)] = __fmul_rn(q[m], iq);
+      sm.k[t][Sm::at(lane + 32 * m)] = __fmul_rn(k[m], ik);
     }
   }
   __syncthreads();
@@ -663,13 +728,19 @@ __global__ void __launch_bounds__(HD) recr_chunk_kernel(RecrChunkArgs c) {
   for (int t = 0; t < c.T; t++) {
     const float g = sm.g[t], beta = sm.beta[t];
     const float *ks = sm.k[t], *qs = sm.q[t];
+    float kx[RW], qx[RW];  // this lane's chunk of k and q (128-bit loads)
+#pragma unroll
+    for (int ii = 0; ii < RW; ii += 4) {
+      *reinterpret_cast<float4 *>(&kx[ii]) = *reinterpret_cast<const float4 *>(ks + Sm::at(RW * w) + ii);
+      *reinterpret_cast<float4 *>(&qx[ii]) = *reinterpret_cast<const float4 *>(qs + Sm::at(RW * w) + ii);
+    }
 #pragma unroll
     for (int ii = 0; ii < RW; ii++) st[ii] = __fmul_rn(st[ii], g);
-    const float dk = gdn_dot<RW>(st, ks + RW * w, ks, gdn_fb + jc * HD, w);
+    const float dk = gdn_dot<RW, kChunkPad>(st, kx, ks, gdn_fb + jc * HD, w);
     const float d = __fmul_rn(__fsub_rn(sm.v[t][jc], dk), beta);
 #pragma unroll
-    for (int ii = 0; ii < RW; ii++) st[ii] = __fadd_rn(st[ii], __fmul_rn(ks[RW * w + ii], d));
-    const float dq = gdn_dot<RW>(st, qs + RW * w, qs, gdn_fb + jc * HD, w);
+    for (int ii = 0; ii < RW; ii++) st[ii] = __fadd_rn(st[ii], __fmul_rn(kx[ii], d));
+    const float dq = gdn_dot<RW, kChunkPad>(st, qx, qs, gdn_fb + jc * HD, w);
     float *yt = reinterpret_cast<float *>(reinterpret_cast<uint8_t *>(a.y) + (size_t)t * c.pss);
     if (w == 0) yt[h * HD + c0 + jc] = __fmul_rn(dq, __fdiv_rn(1.0f, __fsqrt_rn((float)HD)));
   }
@@ -1043,7 +1114,6 @@ __global__ void __launch_bounds__(256) attn_combine_quant_kernel(AttnArgs a) {
   attn_at_seq(a);
   const int span = blockIdx.x, t = threadIdx.x;
   const int e = span * 256 + t, h = e / HDV, c = e % HDV;
-  const int kvh = h / (a.nh / a.nkv);
   const int n = *a.pos + 1;
   const int nw = (n + kChunk - 1) / kChunk;
   const double2 *pp = a.part + (size_t)h * a.nsplit * HDV + c;
@@ -1937,9 +2007,11 @@ int32_t prefill_alloc(unltd_qwen35_session s) {
   }
   int32_t rc = cuda_error(gemv_batch_prewarm(m->ctx->device), "batched GEMV attributes");
   if (!rc)
-    rc = cuda_error(cudaFuncSetAttribute(recr_chunk_kernel<128>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                         (int)sizeof(RecrChunkSmem<128>)),
-                    "prefill recurrence attributes");
+    for (auto fn : {recr_chunk_kernel<128, 4>, recr_chunk_kernel<128, 0>})
+      if (!rc)
+        rc = cuda_error(cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                             (int)sizeof(RecrChunkSmem<128>)),
+                        "prefill recurrence attributes");
   for (auto *w : ws)
     if (!rc) rc = gemv_batch_prepare(m->ctx, w);
   return rc;
@@ -2026,8 +2098,8 @@ int32_t enqueue_prefill(unltd_qwen35_session s, int T, bool head) {
       a.nsg = kPrefillNsg;
       c.pss = pss;
       c.T = T;
-      chk(launch_pdl(recr_chunk_kernel<128>, dim3(d.nvl, 128 / kGdnCols), dim3(128), sizeof(RecrChunkSmem<128>), st,
-                     c),
+      chk(launch_pdl(d.K == 4 ? recr_chunk_kernel<128, 4> : recr_chunk_kernel<128, 0>, dim3(d.nvl, 128 / kGdnCols),
+                     dim3(128), sizeof(RecrChunkSmem<128>), st, c),
           "prefill recurrence");
       chk(launch_pdl(prefill_gnorm_kernel<128>, dim3(d.nvl * d.hd / 256, T), dim3(128), 0, st, (const float *)P.Y,
                      (const float *)P.proj, pss, d.dconvl, (const float *)L.ssm_norm, d.eps, P.bimg, kPrefillNsg),
