@@ -259,6 +259,15 @@ constexpr int kGdnCols = 32;
 // with the running-error bound (see attn_combine_quant_kernel); when the
 // bound cannot decide, the column's terms go through shared memory and lane
 // w == 0 sums all of them left to right.
+// q and k of a head in shared memory hold their four quarter chunks (HD / 4
+// channels each) kChunkPad floats apart, so the four lanes of a state column
+// (one chunk each) read different banks, with 128-bit loads
+constexpr int kChunkPad = 8;
+template <int HD>
+__device__ __forceinline__ int chunk_at(int i) {
+  return i + (i / (HD / 4)) * kChunkPad;
+}
+
 template <int RW, int XP = 0>  // XP: x holds its four chunks RW + XP floats apart
 __device__ __forceinline__ float gdn_dot(const float (&st)[RW], const float *xw, const float *x, float *fb, int w) {
   double Sw = 0.0, Qw = 0.0;
@@ -367,7 +376,7 @@ __device__ __noinline__ void gated_norm_span(const float *y, const float *z, con
 template <int HD, int KT>  // KT: conv_kernel known at compile time (0: a.K at run time)
 __global__ void __launch_bounds__(HD) recr_mid_kernel(RecrArgs a) {
   pdl_trigger();
-  __shared__ float qs[HD], ks[HD];
+  __shared__ __align__(16) float qs[HD + 4 * kChunkPad], ks[HD + 4 * kChunkPad];  // chunk_at layout
   __shared__ float gdn_fb[kGdnCols * HD];  // fallback of gdn_dot: one column's terms
   __shared__ double red[2 * HD / 32];
   __shared__ float s_f[2];
@@ -462,8 +471,9 @@ __global__ void __launch_bounds__(HD) recr_mid_kernel(RecrArgs a) {
   }
 
   // l2_norm_rows of q and k (kernels.rs:236-252)
-  qs[j] = q;
-  ks[j] = k;
+  const int jp = chunk_at<HD>(j);
+  qs[jp] = q;
+  ks[jp] = k;
   double Sq = (double)__fmul_rn(q, q), Sk = (double)__fmul_rn(k, k);
   block_sum2<HD>(Sq, Sk, red);
   float fq, fk;
@@ -475,7 +485,10 @@ __global__ void __launch_bounds__(HD) recr_mid_kernel(RecrArgs a) {
       const float *src = j == 0 ? qs : ks;
       double s = 0.0;
 #pragma unroll 1
-      for (int i = 0; i < HD; i++) s = __dadd_rn(s, (double)__fmul_rn(src[i], src[i]));
+      for (int i = 0; i < HD; i++) {
+        const float xi = src[chunk_at<HD>(i)];
+        s = __dadd_rn(s, (double)__fmul_rn(xi, xi));
+      }
       s_f[j] = (float)s;
     }
     __syncthreads();
@@ -485,8 +498,8 @@ __global__ void __launch_bounds__(HD) recr_mid_kernel(RecrArgs a) {
   q = __fmul_rn(q, __fdiv_rn(1.0f, fmaxf(__fsqrt_rn(fq), a.eps)));
   k = __fmul_rn(k, __fdiv_rn(1.0f, fmaxf(__fsqrt_rn(fk), a.eps)));
   __syncthreads();
-  qs[j] = q;
-  ks[j] = k;
+  qs[jp] = q;
+  ks[jp] = k;
 
   // beta = sigmoid(beta_raw); gate = softplus(alpha + dt_bias) * ssm_a
   const float beta = sigmoid_f(beta_raw);
@@ -501,13 +514,20 @@ __global__ void __launch_bounds__(HD) recr_mid_kernel(RecrArgs a) {
   // w = j % 4. Each dot over i is evaluated as four in-order chunk sums whose
   // combination is resolved exactly (gdn_dot); the four lanes of a column
   // hold the same results.
+  float kx[RW], qx[RW];  // this lane's chunk of k, then of q (128-bit loads)
+#pragma unroll
+  for (int ii = 0; ii < RW; ii += 4)
+    *reinterpret_cast<float4 *>(&kx[ii]) = *reinterpret_cast<const float4 *>(ks + chunk_at<HD>(RW * w) + ii);
 #pragma unroll
   for (int ii = 0; ii < RW; ii++) st[ii] = __fmul_rn(st[ii], g);
-  const float dk = gdn_dot<RW>(st, ks + RW * w, ks, gdn_fb + jc * HD, w);
+  const float dk = gdn_dot<RW, kChunkPad>(st, kx, ks, gdn_fb + jc * HD, w);
   const float d = __fmul_rn(__fsub_rn(vs[jc], dk), beta);
 #pragma unroll
-  for (int ii = 0; ii < RW; ii++) st[ii] = __fadd_rn(st[ii], __fmul_rn(ks[RW * w + ii], d));
-  const float dq = gdn_dot<RW>(st, qs + RW * w, qs, gdn_fb + jc * HD, w);
+  for (int ii = 0; ii < RW; ii++) st[ii] = __fadd_rn(st[ii], __fmul_rn(kx[ii], d));
+#pragma unroll
+  for (int ii = 0; ii < RW; ii += 4)
+    *reinterpret_cast<float4 *>(&qx[ii]) = *reinterpret_cast<const float4 *>(qs + chunk_at<HD>(RW * w) + ii);
+  const float dq = gdn_dot<RW, kChunkPad>(st, qx, qs, gdn_fb + jc * HD, w);
   if (w == 0) a.y[h * HD + c0 + jc] = __fmul_rn(dq, __fdiv_rn(1.0f, __fsqrt_rn((float)HD)));
 #pragma unroll
   for (int ii = 0; ii < RW; ii++) S[(size_t)(RW * w + ii) * HD] = st[ii];
@@ -555,14 +575,10 @@ struct RecrChunkArgs {
 
 constexpr int kChunkTok = 32;  // tokens of a prefill chunk (kPrefillLanes)
 
-// q and k rows of a token hold their four quarter chunks (HD / 4 channels each)
-// kChunkPad floats apart, so the four lanes of a column (one chunk each) read
-// different banks
-constexpr int kChunkPad = 8;
 template <int HD>
 struct RecrChunkSmem {
   static constexpr int kRow = HD + 4 * kChunkPad;
-  static __device__ __forceinline__ int at(int i) { return i + (i / (HD / 4)) * kChunkPad; }
+  static __device__ __forceinline__ int at(int i) { return chunk_at<HD>(i); }
   float q[kChunkTok][kRow], k[kChunkTok][kRow], v[kChunkTok][kGdnCols];
   float beta[kChunkTok], g[kChunkTok];
 };
@@ -728,18 +744,19 @@ __global__ void __launch_bounds__(HD) recr_chunk_kernel(RecrChunkArgs c) {
   for (int t = 0; t < c.T; t++) {
     const float g = sm.g[t], beta = sm.beta[t];
     const float *ks = sm.k[t], *qs = sm.q[t];
-    float kx[RW], qx[RW];  // this lane's chunk of k and q (128-bit loads)
+    float kx[RW], qx[RW];  // this lane's chunk of k, then of q (128-bit loads)
 #pragma unroll
-    for (int ii = 0; ii < RW; ii += 4) {
+    for (int ii = 0; ii < RW; ii += 4)
       *reinterpret_cast<float4 *>(&kx[ii]) = *reinterpret_cast<const float4 *>(ks + Sm::at(RW * w) + ii);
-      *reinterpret_cast<float4 *>(&qx[ii]) = *reinterpret_cast<const float4 *>(qs + Sm::at(RW * w) + ii);
-    }
 #pragma unroll
     for (int ii = 0; ii < RW; ii++) st[ii] = __fmul_rn(st[ii], g);
     const float dk = gdn_dot<RW, kChunkPad>(st, kx, ks, gdn_fb + jc * HD, w);
     const float d = __fmul_rn(__fsub_rn(sm.v[t][jc], dk), beta);
 #pragma unroll
     for (int ii = 0; ii < RW; ii++) st[ii] = __fadd_rn(st[ii], __fmul_rn(kx[ii], d));
+#pragma unroll
+    for (int ii = 0; ii < RW; ii += 4)
+      *reinterpret_cast<float4 *>(&qx[ii]) = *reinterpret_cast<const float4 *>(qs + Sm::at(RW * w) + ii);
     const float dq = gdn_dot<RW, kChunkPad>(st, qx, qs, gdn_fb + jc * HD, w);
     float *yt = reinterpret_cast<float *>(reinterpret_cast<uint8_t *>(a.y) + (size_t)t * c.pss);
     if (w == 0) yt[h * HD + c0 + jc] = __fmul_rn(dq, __fdiv_rn(1.0f, __fsqrt_rn((float)HD)));
