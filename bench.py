@@ -600,7 +600,7 @@ def main():
     if args.decode_only:
         d = decode_bench(args.decode_tokens, with_cpu=False, rank=rank, world=world, dist=dist, batch=args.decode_batch,
                          profile_batch=args.profile_batch, layers=args.decode_layers,
-                         prefill=0 if args.decode_layers else 256,
+                         prefill=0 if args.decode_layers and not args.profile_prefill else 256,
                          profile_region=args.profile_region, profile_prefill=args.profile_prefill)
         if rank == 0:
             os.write(out_fd, (json.dumps({"metric": "decode tok/s", "decode": d}) + "\n").encode())
