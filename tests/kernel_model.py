@@ -3,7 +3,9 @@
 Restates, element by element, what gemv.cu / weights.cu do with the device
 row layout: the within-block permutations of the repack, the x-image
 positions, the words each lane loads, the DP4A products and the lane
-reductions. Tests compare this model with the oracle on CPU, so a wrong
+reductions; and the integer decompositions of the batched GEMV
+(gemv_batch.cu): Q4_K's scale split into two 3-bit digits folded into A,
+Q6_K's digit planes w = 128 w1 + w0. Tests compare this model with the oracle on CPU, so a wrong
 permutation or lane mapping is caught before anything runs on a GPU.
 """
 from __future__ import annotations
