@@ -636,7 +636,7 @@ __global__ void __launch_bounds__(HD) recr_chunk_kernel(RecrChunkArgs c) {
     // pass precede its stores, and its 4 x NC silu are independent
     auto conv_cols = [&](auto ncs, float *const *col, int stride, const int *ch) {
       constexpr int NC = decltype(ncs)::value;
-      float wr[NC][KT > 0 ? KT : 1];
+      [[maybe_unused]] float wr[NC][KT > 0 ? KT : 1];  // KT == 0: the weights are read per tap
       if constexpr (KT > 0) {
 #pragma unroll
         for (int n = 0; n < NC; n++)
